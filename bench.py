@@ -1,0 +1,318 @@
+#!/usr/bin/env python
+"""Batched encoder throughput of the SparseLattice integer forward path on B200.
+
+Workload: the batched-encoder configuration -- the nomic-bert encoder architecture (12 layers,
+d_model 768, 12 heads, SiLU-gated FFN 3072, vocab 30522) with Q4_0 weights (seeded synthetic
+GGUF), sequences of 512 token ids drawn uniformly from the vocabulary. One step is one forward of
+a batch of B sequences per GPU, pooled to Q30 int64 embeddings, bit-identical to the reference's
+integer path. Sequences are independent: N GPUs each run their own batch (weak scaling), no
+collective on the data path; torch.distributed only provides the barrier and the max-over-ranks
+timing reduction.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SEQ = 512
+ARCH = dict(layers=12, embd=768, heads=12, ff=3072, vocab=30522, ctx=512)
+METRIC = "encoder embeddings/s"
+UNIT = "embeddings/s"
+
+
+def workload_name(batch: int) -> str:
+    return (f"batched encoder: nomic-bert {ARCH['layers']}L d{ARCH['embd']} H{ARCH['heads']} "
+            f"SiLU-FFN {ARCH['ff']} V{ARCH['vocab']}, Q4_0 weights, {SEQ} tokens/seq, {batch} seqs/GPU/step")
+
+
+def model_path() -> str:
+    from spatialdb_b200 import synth
+
+    shape = synth.EncoderShape(**ARCH)
+    return synth.cached("encoder_nomic_L12_d768_q4_0_seed3.gguf",
+                        lambda p: synth.write_encoder(p, shape, synth.Q4_0, seed=3))
+
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def recorded_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if one exists."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    return json.load(open(p)).get(kernel, {}).get("bytes_per_launch")
+
+
+class Clocks:
+    """nvidia-smi samples of one GPU's clocks during the timed region."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict | None:
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(path: str, sample_seqs: int, seed: int = 99) -> dict:
+    """The oracle (C++ restatement of the reference CPU path, OpenMP over output columns as the
+    reference's Parallel.For) on a bounded sample of the workload, all host threads."""
+    import numpy as np
+    import oracle
+
+    cores = oracle.set_threads(os.cpu_count() or 1)
+    enc = oracle.Encoder(path)
+    ids = np.random.default_rng(seed).integers(0, ARCH["vocab"], (sample_seqs, SEQ)).astype(np.int32)
+    t0 = time.perf_counter()
+    enc.forward(ids)
+    dt = time.perf_counter() - t0
+    return {"value": sample_seqs / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{sample_seqs} sequence(s) x {SEQ} tokens of the same workload, {dt:.1f} s"}
+
+
+def run_reference(args) -> None:
+    """Reference arm: the reference's CPU algorithm (the oracle port; the C# reference needs a .NET
+    runtime that this image lacks) on the host cores, one bounded sample per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    import oracle
+
+    path = model_path()
+    cores = oracle.set_threads(os.cpu_count() or 1)
+    enc = oracle.Encoder(path)
+    rng = np.random.default_rng(7)
+    per_step = 1
+    for _ in range(args.warmup):
+        enc.forward(rng.integers(0, ARCH["vocab"], (per_step, SEQ)).astype(np.int32))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        enc.forward(rng.integers(0, ARCH["vocab"], (per_step, SEQ)).astype(np.int32))
+    dt = time.perf_counter() - t0
+    value = per_step * args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+        "config": {"workload": workload_name(per_step), "seq_len": SEQ, "batch_per_step": per_step},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{per_step} sequence x {SEQ} tokens per step"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+
+    import spatialdb_b200 as slx
+    from spatialdb_b200._lib import KernelStat
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    if rank == 0:
+        path = model_path()
+    if dist:
+        dist.barrier()
+    path = model_path()
+
+    B, K, W = args.batch, args.steps, args.warmup
+    ctx = slx.Context(local)
+    model = slx.IntegerTransformerSource.load(path, ctx=ctx)
+    lib = ctx._lib
+    stream = torch.cuda.current_stream()
+    rng = np.random.default_rng(1000 + rank)
+    ids_host = rng.integers(0, ARCH["vocab"], (W + K, B, SEQ)).astype(np.int32)
+    ids_dev = torch.from_numpy(ids_host).cuda()
+    pooled = torch.empty((B, ARCH["embd"]), dtype=torch.int64, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
+
+    def step(i):
+        model.encode_device(ids_dev[i].data_ptr(), B, SEQ, pooled.data_ptr(), stream.cuda_stream)
+
+    for i in range(W):
+        flush.zero_()
+        step(i)
+    torch.cuda.synchronize()
+
+    launches0 = ctypes_i64()
+    lib.slx_launch_count(ctx._h, launches0)
+    lib.slx_profile_begin(ctx._h)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local) if rank == 0 else None
+    for i in range(K):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step(W + i)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    stats = (KernelStat * 16)()
+    nstat = ctypes_int()
+    lib.slx_profile_end(ctx._h, stats, 16, nstat)
+    launches1 = ctypes_i64()
+    lib.slx_launch_count(ctx._h, launches1)
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    value = world * B * K / (max_ms / 1000.0)
+
+    # end to end through the public host-buffer API (pinned host ids in, pooled int64 out)
+    ids_pinned = torch.from_numpy(ids_host).pin_memory().numpy()
+    out_host = np.empty((B, ARCH["embd"]), np.int64)
+    model.forward(ids_pinned[0])
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(K):
+        out_host[:] = model.forward(ids_pinned[W + i])
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * B * K / float(te.item())
+
+    # parity spot check of the timed outputs against the host path (same library)
+    last = pooled.cpu().numpy()
+    chk = model.forward(ids_host[W + K - 1])
+    parity_ok = bool((last == chk).all())
+
+    if rank == 0:
+        peaks = measured_peaks()
+        cls = {s.name.decode(): s for s in stats[: nstat.value]}
+        top = max(cls.values(), key=lambda s: s.ms) if cls else None
+        int8_peak = 2.0 * peaks["bf16_tflops"]
+        roof = None
+        if top is not None and top.ms > 0:
+            achieved = 2.0 * top.macs / (top.ms / 1000.0) / 1e12
+            roof = {"bound": "tensor", "kernel": top.name.decode(), "achieved": achieved, "peak": int8_peak,
+                    "unit": "TOPS", "frac": achieved / int8_peak,
+                    "peak_source": f"2 x {peaks['source']} bf16 dense ({peaks['bf16_tflops']} TF/s): B200 int8:bf16 dense rate",
+                    "ops": "algorithmic: 2 x int64 multiply-accumulates of the Q30 product",
+                    "launches": int(top.launches), "avg_launch_ms": top.ms / max(1, top.launches),
+                    "traffic": recorded_traffic(top.name.decode())}
+        breakdown = {s.name.decode(): {"ms_per_step": s.ms / K, "launches_per_step": s.launches / K}
+                     for s in stats[: nstat.value]}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": max_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int64", "data": "synthetic",
+            "config": {"workload": workload_name(B), "seq_len": SEQ, "batch_per_gpu": B, "weights": "Q4_0",
+                       "parallelism": f"dp{world} (independent sequences)",
+                       "l2": "flushed (256 MiB write) before every timed step, outside the step's events"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(B * SEQ * 4),
+                    "d2h_bytes_per_step": int(B * ARCH["embd"] * 8)},
+            "gpu_launches": int(launches1.value - launches0.value),
+            "roofline": roof,
+            "kernels": breakdown,
+            "parity_spot_check": parity_ok,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(path, args.cpu_sample)
+        print(json.dumps(line), flush=True)
+    del model, ctx
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def ctypes_i64():
+    import ctypes
+    return ctypes.c_int64(0)
+
+
+def ctypes_int():
+    import ctypes
+    return ctypes.c_int(0)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=16, help="sequences per GPU per step")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-sample", type=int, default=2, help="sequences in the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

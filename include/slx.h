@@ -1,0 +1,134 @@
+/* slx.h -- C ABI of libslx, the sm_100a implementation of SparseLattice's quantized integer
+ * transformer forward path (GGUF dequantization fused into the Q30 matrix products of the
+ * nomic-bert encoder and the Gemma causal LM, with the integer attention, norms and FFN).
+ *
+ * Plain C types only; no CUDA or framework types in the signatures. Every entry point returns an
+ * slx_status; a message for the last failure on a context is available from slx_last_error().
+ * Host-buffer entry points copy in and out and return when the result is on the host. Device
+ * entry points (suffix _device) take device pointers and a stream handle (cudaStream_t passed as
+ * void*, NULL = the context's stream) and return once the work is queued.
+ *
+ * Citations are to the reference project damiant3/SpatialDb, directory SparseLattice/.
+ */
+#ifndef SLX_H
+#define SLX_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The C# shim maps them back to the reference's exception types. */
+typedef int slx_status;
+#define SLX_OK 0
+#define SLX_EINVAL 1        /* ArgumentException: bad shape, null pointer, bad kind */
+#define SLX_EFORMAT 2       /* InvalidDataException: bad magic / version / value type */
+#define SLX_ENOTFOUND 3     /* FileNotFoundException / KeyNotFoundException */
+#define SLX_EUNSUPPORTED 4  /* NotSupportedException: dtype or architecture */
+#define SLX_EEOF 5          /* EndOfStreamException: truncated tensor data */
+#define SLX_ERANGE 6        /* IndexOutOfRangeException: MXFP4 nibble 15, RoPE row past its table */
+#define SLX_EOOM 7          /* device allocation failed */
+#define SLX_ECUDA 8         /* CUDA runtime error */
+#define SLX_ETIMEOUT 9      /* a bounded device wait gave up */
+
+/* Model kinds for slx_model_load_gguf. */
+#define SLX_MODEL_ENCODER 0       /* IntegerTransformerSource (nomic-bert / bert) */
+#define SLX_MODEL_CAUSAL 1        /* IntegerCausalSource (gemma*) */
+#define SLX_MODEL_GEMMA_ENCODER 2 /* IntegerGemmaSource (gemma*, non-causal, mean pooled) */
+
+typedef struct slx_ctx slx_ctx;
+typedef struct slx_model slx_model;
+
+/* ---- context ------------------------------------------------------------------------------ */
+/* Binds a CUDA device and creates the context's stream. No reference counterpart: the C# host
+ * creates one context per thread or serialises calls on one. */
+slx_status slx_init(int device, slx_ctx** out);
+slx_status slx_destroy(slx_ctx* ctx);
+/* Message of the last failure on ctx (valid until the next call on ctx). */
+const char* slx_last_error(slx_ctx* ctx);
+/* Library version string. */
+const char* slx_version(void);
+
+/* ---- GGUF ---------------------------------------------------------------------------------- */
+/* GgufReader.ReadTensorF32 (Gguf/GgufReader.cs:141-145, 172-201) for one tensor of a file:
+ * dequantizes on the device with GgufDequantizer's formulas and element orders
+ * (Gguf/GgufDequantizer.cs:7-325) and copies `n` floats to host `out` (n = element count). */
+slx_status slx_gguf_read_f32(slx_ctx* ctx, const char* path, const char* tensor, float* out, int64_t n);
+
+/* GgufDequantizer.Dequantize* over raw block bytes already in host memory
+ * (Gguf/GgufDequantizer.cs:19-325; dtype ids from Gguf/GgufTypes.cs:21-38). */
+slx_status slx_dequantize(slx_ctx* ctx, int dtype, const uint8_t* raw, int64_t nbytes, float* out, int64_t n);
+
+/* ---- models -------------------------------------------------------------------------------- */
+/* IntegerTransformerSource.Load (Gguf/IntegerTransformerSource.Loading.cs:47-58),
+ * IntegerCausalSource.Load (Gguf/IntegerCausalSource.Loading.cs:41-52) and
+ * IntegerGemmaSource.Load (Gguf/IntegerGemmaSource.Loading.cs:57-69): parses the GGUF file and
+ * uploads the packed weight blocks to device memory. scale_bits is the Q scale (30). */
+slx_status slx_model_load_gguf(slx_ctx* ctx, const char* path, int kind, int scale_bits, slx_model** out);
+slx_status slx_model_free(slx_model* model);
+/* info[0..11]: kind, embd, heads, kv_heads, head_dim, ff, layers, vocab, eos, unk, q_dim, kv_dim. */
+slx_status slx_model_info(slx_model* model, int32_t* info, int n);
+
+/* ---- encoder (IEmbeddingSource, Embedding/IEmbeddingSource.cs:13-33) ----------------------- */
+/* IntegerTransformerSource.Forward on token ids (Gguf/IntegerTransformerSource.cs:65-78) for B
+ * sequences of T tokens each (EmbedBatchAsync's loop, :40-47, done as one batch): writes the
+ * mean-pooled Q30 vectors pooled_q30[B][embd]. If l2 is not NULL it also receives ForwardFloat's
+ * L2-normalised float vectors (:52-62, .Forward.cs:89-99). Also serves SLX_MODEL_GEMMA_ENCODER
+ * (IntegerGemmaSource.Forward, Gguf/IntegerGemmaSource.cs:66-80). */
+slx_status slx_encode(slx_model* model, const int32_t* ids, int B, int T, int64_t* pooled_q30, float* l2);
+/* Same on device buffers: d_ids[B*T] int32, d_pooled[B*embd] int64, queued on `stream`. */
+slx_status slx_encode_device(slx_model* model, const int32_t* d_ids, int B, int T, int64_t* d_pooled, void* stream);
+
+/* Hidden states after the first n_layers blocks (n_layers < 0: all), x_q30[T][embd], for one
+ * sequence: the state ForwardCausalWithTrace samples (Gguf/IntegerCausalSource.Forward.cs:154-176)
+ * and the encoder equivalent; used to bisect parity by layer. final_norm applies the causal
+ * model's output RmsNorm after the last block. */
+slx_status slx_trace_hidden(slx_model* model, const int32_t* ids, int T, int n_layers, int final_norm, int64_t* x_q30);
+
+/* ---- causal LM (IntegerCausalSource, Gguf/IntegerCausalSource.cs:86-200) ------------------- */
+/* ForwardCausal (:128-147): last position's hidden state after the output norm, Q30. */
+slx_status slx_causal_forward_last(slx_model* model, const int32_t* ids, int T, int64_t* last_q30);
+/* ForwardCausalFloat + PredictNextToken without lattice (:114-122, :149-161): greedy next id
+ * from VocabLattice.ArgmaxBruteForce (Lattice/VocabLattice.cs:103-126), for B sequences of T. */
+slx_status slx_causal_next_token(slx_model* model, const int32_t* ids, int B, int T, int32_t* next);
+/* Generate on token ids (:86-108): full re-forward per step, greedy, stops at EOS (not
+ * emitted). B independent prompts of T tokens; out[B][max_new] receives the new ids and
+ * n_out[B] their counts. */
+slx_status slx_causal_generate(slx_model* model, const int32_t* ids, int B, int T, int max_new, int32_t* out,
+                               int32_t* n_out);
+
+/* ---- kernel-level ---------------------------------------------------------------------------- */
+/* IntegerMatMul.MatMul with GGUF weights (Math/IntegerMatMul.cs:37-76 for the long composite,
+ * :166-205 for the Half composite): c[M][N] = (long)((sum_k a[M][K] * w[n][k]) >> shift), where
+ * w is the Q30 composite of the GGUF tensor `w_raw` (dtype, N rows of K, flat block order) formed
+ * as IntegerTransformerSource (half_composite = 0) or IntegerCausalSource (half_composite = 1)
+ * forms it. Host buffers. */
+slx_status slx_matmul_q30(slx_ctx* ctx, const int64_t* a, int M, int K, int dtype, const uint8_t* w_raw,
+                          int64_t w_bytes, int N, int half_composite, int scale_bits, int shift, int64_t* c);
+/* Same on device buffers (a, w_raw, c device pointers), queued on `stream`. */
+slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K, int dtype, const uint8_t* d_w,
+                                 int64_t w_bytes, int N, int half_composite, int scale_bits, int shift, int64_t* d_c,
+                                 void* stream);
+
+/* ---- measurement ---------------------------------------------------------------------------- */
+/* No reference counterpart (the reference times with Stopwatch, SparseLattice.Perf/Program.cs:817-830).
+ * Per kernel class, the library's launches on ctx between begin and end, their device time from
+ * CUDA events recorded on the launch stream, and the algorithmic multiply-accumulates they
+ * performed. Classes: gemm, attention, norm, rope, ffn_gate, embed, pool, add, argmax. */
+typedef struct slx_kernel_stat {
+    char name[24];
+    int64_t launches;
+    double ms;
+    double macs;
+    double bytes;
+} slx_kernel_stat;
+slx_status slx_profile_begin(slx_ctx* ctx);
+slx_status slx_profile_end(slx_ctx* ctx, slx_kernel_stat* stats, int cap, int* n);
+/* Running count of kernels the library has queued on ctx. */
+slx_status slx_launch_count(slx_ctx* ctx, int64_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SLX_H */

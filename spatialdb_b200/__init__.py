@@ -1,0 +1,244 @@
+"""spatialdb_b200 -- SparseLattice's quantized integer transformer forward path on B200 (sm_100a).
+
+Host-side mirror of the reference's model sources over the libslx C ABI (include/slx.h):
+
+* IntegerTransformerSource  (SparseLattice/Gguf/IntegerTransformerSource*.cs) -- nomic-bert / bert
+  encoder; forward(ids) -> pooled Q30 long, forward_float(ids) -> L2-normalised float.
+* IntegerGemmaSource        (SparseLattice/Gguf/IntegerGemmaSource*.cs) -- Gemma encoder.
+* IntegerCausalSource       (SparseLattice/Gguf/IntegerCausalSource*.cs) -- Gemma causal LM;
+  forward_causal, next_token, generate (greedy, full re-forward per token).
+* dequantize / read_tensor_f32  (SparseLattice/Gguf/GgufDequantizer.cs, GgufReader.cs).
+* matmul_q30                (SparseLattice/Math/IntegerMatMul.cs) with GGUF-packed weights.
+
+Tokenizers stay with the caller (the C# host keeps them); these entry points take token ids.
+All work runs in the CUDA library; nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import I32P, I64P, F32P, U8P, VP
+
+SLX_OK, SLX_EINVAL, SLX_EFORMAT, SLX_ENOTFOUND, SLX_EUNSUPPORTED, SLX_EEOF, SLX_ERANGE, SLX_EOOM, SLX_ECUDA, SLX_ETIMEOUT = range(10)
+MODEL_ENCODER, MODEL_CAUSAL, MODEL_GEMMA_ENCODER = 0, 1, 2
+
+
+class SlxError(RuntimeError):
+    """Raised for a non-zero slx_status; `status` holds the code."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"[{status}] {message}")
+        self.status = status
+
+
+class InvalidDataError(SlxError):      # InvalidDataException
+    pass
+
+
+class NotSupportedError(SlxError):     # NotSupportedException
+    pass
+
+
+class NotFoundError(SlxError):         # FileNotFoundException / KeyNotFoundException
+    pass
+
+
+class EndOfStreamError(SlxError):      # EndOfStreamException
+    pass
+
+
+class IndexOutOfRangeError(SlxError):  # IndexOutOfRangeException
+    pass
+
+
+_EXC = {SLX_EFORMAT: InvalidDataError, SLX_EUNSUPPORTED: NotSupportedError, SLX_ENOTFOUND: NotFoundError,
+        SLX_EEOF: EndOfStreamError, SLX_ERANGE: IndexOutOfRangeError}
+
+
+def _p(a: np.ndarray, t):
+    return a.ctypes.data_as(t)
+
+
+class Context:
+    """One CUDA device and stream (slx_init)."""
+
+    _default: "Context | None" = None
+
+    def __init__(self, device: int = 0):
+        self._lib = _lib.lib()
+        h = VP()
+        st = self._lib.slx_init(device, ctypes.byref(h))
+        if st:
+            raise SlxError(st, f"slx_init(device={device}) failed")
+        self._h = h
+        self.device = device
+
+    @classmethod
+    def default(cls) -> "Context":
+        if cls._default is None:
+            cls._default = Context(0)
+        return cls._default
+
+    def check(self, st: int):
+        if st:
+            msg = self._lib.slx_last_error(self._h).decode(errors="replace")
+            raise _EXC.get(st, SlxError)(st, msg)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.slx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def dequantize(dtype: int, raw, n: int, ctx: Context | None = None) -> np.ndarray:
+    """GgufDequantizer for one raw tensor (n output floats)."""
+    ctx = ctx or Context.default()
+    buf = np.frombuffer(bytes(raw), np.uint8).copy() if not isinstance(raw, np.ndarray) else np.ascontiguousarray(raw, np.uint8)
+    out = np.zeros(n, np.float32)
+    ctx.check(ctx._lib.slx_dequantize(ctx._h, int(dtype), _p(buf, U8P), buf.size, _p(out, F32P), int(n)))
+    return out
+
+
+def read_tensor_f32(path: str, name: str, n: int, ctx: Context | None = None) -> np.ndarray:
+    """GgufReader.ReadTensorF32 (n must be the tensor's element count)."""
+    ctx = ctx or Context.default()
+    out = np.zeros(n, np.float32)
+    ctx.check(ctx._lib.slx_gguf_read_f32(ctx._h, path.encode(), name.encode(), _p(out, F32P), int(n)))
+    return out
+
+
+def matmul_q30(a: np.ndarray, dtype: int, w_raw, N: int, half_composite: bool = False, scale_bits: int = 30,
+               shift: int = 30, ctx: Context | None = None) -> np.ndarray:
+    """IntegerMatMul.MatMul of int64 a[M][K] with a GGUF weight of N rows of K (flat block order)."""
+    ctx = ctx or Context.default()
+    a = np.ascontiguousarray(np.atleast_2d(a), np.int64)
+    M, K = a.shape
+    w = np.frombuffer(bytes(w_raw), np.uint8).copy() if not isinstance(w_raw, np.ndarray) else np.ascontiguousarray(w_raw, np.uint8)
+    c = np.empty((M, N), np.int64)
+    ctx.check(ctx._lib.slx_matmul_q30(ctx._h, _p(a, I64P), M, K, int(dtype), _p(w, U8P), w.size, N, int(half_composite),
+                                      scale_bits, shift, _p(c, I64P)))
+    return c
+
+
+class _Model:
+    kind = -1
+
+    def __init__(self, path: str, scale_bits: int = 30, ctx: Context | None = None):
+        self.ctx = ctx or Context.default()
+        h = VP()
+        self.ctx.check(self.ctx._lib.slx_model_load_gguf(self.ctx._h, path.encode(), self.kind, scale_bits, ctypes.byref(h)))
+        self._h = h
+        info = np.zeros(12, np.int32)
+        self.ctx._lib.slx_model_info(self._h, _p(info, I32P), 12)
+        (_, self.embd, self.heads, self.kv_heads, self.head_dim, self.ff, self.layers, self.vocab, self.eos, self.unk,
+         self.q_dim, self.kv_dim) = [int(v) for v in info]
+        self.scale_bits = scale_bits
+        self.path = path
+
+    @classmethod
+    def load(cls, path: str, scale_bits: int = 30, ctx: Context | None = None):
+        return cls(path, scale_bits, ctx)
+
+    @property
+    def dimensions(self) -> int:
+        return self.embd
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.ctx._lib.slx_model_free(self._h)
+            self._h = None
+
+    def dispose(self):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def trace_hidden(self, ids, n_layers: int = -1, final_norm: bool = False) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int32).reshape(-1)
+        x = np.empty((ids.size, self.embd), np.int64)
+        self.ctx.check(self.ctx._lib.slx_trace_hidden(self._h, _p(ids, I32P), ids.size, n_layers, int(final_norm), _p(x, I64P)))
+        return x
+
+
+class _Encoder(_Model):
+    def forward(self, ids) -> np.ndarray:
+        """Forward on token ids [B, T] (or [T]) -> pooled Q30 long [B, embd]."""
+        ids = np.ascontiguousarray(np.atleast_2d(ids), np.int32)
+        B, T = ids.shape
+        out = np.empty((B, self.embd), np.int64)
+        self.ctx.check(self.ctx._lib.slx_encode(self._h, _p(ids, I32P), B, T, _p(out, I64P), None))
+        return out
+
+    def forward_float(self, ids) -> np.ndarray:
+        """ForwardFloat: pooled vectors dequantized and L2-normalised (float32)."""
+        ids = np.ascontiguousarray(np.atleast_2d(ids), np.int32)
+        B, T = ids.shape
+        out = np.empty((B, self.embd), np.int64)
+        l2 = np.empty((B, self.embd), np.float32)
+        self.ctx.check(self.ctx._lib.slx_encode(self._h, _p(ids, I32P), B, T, _p(out, I64P), _p(l2, F32P)))
+        return l2
+
+    def embed_batch(self, batch_ids) -> np.ndarray:
+        """EmbedBatchAsync on equal-length id sequences, as one device batch."""
+        return self.forward_float(batch_ids)
+
+    def encode_device(self, d_ids_ptr: int, B: int, T: int, d_pooled_ptr: int, stream: int = 0):
+        """Queue a forward on device buffers (raw device pointers, cudaStream_t as int)."""
+        self.ctx.check(self.ctx._lib.slx_encode_device(self._h, VP(d_ids_ptr), B, T, VP(d_pooled_ptr), VP(stream or None)))
+
+
+class IntegerTransformerSource(_Encoder):
+    """nomic-bert / bert integer encoder (IntegerTransformerSource)."""
+    kind = MODEL_ENCODER
+
+
+class IntegerGemmaSource(_Encoder):
+    """Gemma integer encoder, non-causal GQA, mean pooled (IntegerGemmaSource)."""
+    kind = MODEL_GEMMA_ENCODER
+
+
+class IntegerCausalSource(_Model):
+    """Gemma causal LM in Q30 integer arithmetic (IntegerCausalSource)."""
+    kind = MODEL_CAUSAL
+
+    def forward_causal(self, ids) -> np.ndarray:
+        """ForwardCausal: last position's hidden state after the output norm (Q30 long [embd])."""
+        ids = np.ascontiguousarray(ids, np.int32).reshape(-1)
+        out = np.empty(self.embd, np.int64)
+        self.ctx.check(self.ctx._lib.slx_causal_forward_last(self._h, _p(ids, I32P), ids.size, _p(out, I64P)))
+        return out
+
+    def forward_causal_float(self, ids) -> np.ndarray:
+        """ForwardCausalFloat: (float)(v * 2^-scale_bits) of forward_causal."""
+        v = self.forward_causal(ids)
+        return (v.astype(np.float64) * 2.0 ** -self.scale_bits).astype(np.float32)
+
+    def next_token(self, ids) -> np.ndarray:
+        """Greedy next id for each of B sequences [B, T] (ArgmaxBruteForce head)."""
+        ids = np.ascontiguousarray(np.atleast_2d(ids), np.int32)
+        B, T = ids.shape
+        out = np.empty(B, np.int32)
+        self.ctx.check(self.ctx._lib.slx_causal_next_token(self._h, _p(ids, I32P), B, T, _p(out, I32P)))
+        return out
+
+    def generate(self, ids, max_new_tokens: int = 64) -> list[np.ndarray]:
+        """Generate on token ids [B, T]: greedy, full re-forward per token, stop at EOS."""
+        ids = np.ascontiguousarray(np.atleast_2d(ids), np.int32)
+        B, T = ids.shape
+        out = np.zeros((B, max(max_new_tokens, 1)), np.int32)
+        n = np.zeros(B, np.int32)
+        self.ctx.check(self.ctx._lib.slx_causal_generate(self._h, _p(ids, I32P), B, T, max_new_tokens, _p(out, I32P), _p(n, I32P)))
+        return [out[b, : n[b]].copy() for b in range(B)]

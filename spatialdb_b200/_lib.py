@@ -1,0 +1,76 @@
+"""ctypes binding of libslx.so (include/slx.h).
+
+The library is built in-tree on first use (nvcc for sm_100a). There is no fallback: if the CUDA
+library cannot be built or loaded, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import threading
+
+from . import build as _build
+
+_lock = threading.Lock()
+_lib = None
+
+I64P = ctypes.POINTER(ctypes.c_int64)
+I32P = ctypes.POINTER(ctypes.c_int32)
+U8P = ctypes.POINTER(ctypes.c_uint8)
+F32P = ctypes.POINTER(ctypes.c_float)
+VP = ctypes.c_void_p
+i, i64 = ctypes.c_int, ctypes.c_int64
+
+# name -> (restype, argtypes); kept in the order of include/slx.h
+SIGNATURES = {
+    "slx_init": (i, [i, ctypes.POINTER(VP)]),
+    "slx_destroy": (i, [VP]),
+    "slx_last_error": (ctypes.c_char_p, [VP]),
+    "slx_version": (ctypes.c_char_p, []),
+    "slx_gguf_read_f32": (i, [VP, ctypes.c_char_p, ctypes.c_char_p, F32P, i64]),
+    "slx_dequantize": (i, [VP, i, U8P, i64, F32P, i64]),
+    "slx_model_load_gguf": (i, [VP, ctypes.c_char_p, i, i, ctypes.POINTER(VP)]),
+    "slx_model_free": (i, [VP]),
+    "slx_model_info": (i, [VP, I32P, i]),
+    "slx_encode": (i, [VP, I32P, i, i, I64P, F32P]),
+    "slx_encode_device": (i, [VP, VP, i, i, VP, VP]),
+    "slx_trace_hidden": (i, [VP, I32P, i, i, i, I64P]),
+    "slx_causal_forward_last": (i, [VP, I32P, i, I64P]),
+    "slx_causal_next_token": (i, [VP, I32P, i, i, I32P]),
+    "slx_causal_generate": (i, [VP, I32P, i, i, i, I32P, I32P]),
+    "slx_matmul_q30": (i, [VP, I64P, i, i, i, U8P, i64, i, i, i, i, I64P]),
+    "slx_matmul_q30_device": (i, [VP, VP, i, i, i, VP, i64, i, i, i, i, VP, VP]),
+    "slx_profile_begin": (i, [VP]),
+    "slx_profile_end": (i, [VP, VP, i, ctypes.POINTER(i)]),
+    "slx_launch_count": (i, [VP, I64P]),
+}
+
+
+class KernelStat(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 24), ("launches", ctypes.c_int64), ("ms", ctypes.c_double),
+                ("macs", ctypes.c_double), ("bytes", ctypes.c_double)]
+
+
+def header_symbols() -> list[str]:
+    """Function names declared in include/slx.h."""
+    src = open(os.path.join(_build.INCLUDE, "slx.h")).read()
+    return re.findall(r"^\s*(?:slx_status|const char\*)\s+(slx_\w+)\s*\(", src, re.M)
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    with _lock:
+        if _lib is None:
+            path = _build.build()
+            cdll = ctypes.CDLL(path)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(cdll, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = cdll
+    return _lib
+
+
+def library_path() -> str:
+    return _build.LIB

@@ -1,0 +1,603 @@
+// k_core.cu -- exact integer kernels of the SparseLattice forward path on CUDA cores.
+//
+// Every kernel reproduces the reference's integer results bit for bit (C# unchecked long /
+// Int128 arithmetic, truncating division, flooring shifts). The tensor-core GEMM in k_gemm_tc.cu
+// replaces gemm_exact on the hot path; this file keeps the exact general path that any
+// activation range falls back to.
+#include <cstdio>
+
+#include "slx_device.cuh"
+#include "slx_kernels.h"
+
+namespace slx {
+
+// ------------------------------------------------------------------------------------------
+// GEMM: c = (a . w^T) >> shift (+ r)    IntegerMatMul.MatMul + DotInt128 (IntegerMatMul.cs:37-76,
+// 209-229) with the weight's Q30 composite formed in-kernel from the packed GGUF blocks.
+// 64x64 output tile, K in steps of one 32-element quant block, 4x4 Int128 accumulators per thread.
+// ------------------------------------------------------------------------------------------
+namespace {
+constexpr int GBM = 64, GBN = 64, GBK = 32;
+
+__global__ __launch_bounds__(256) void k_gemm_exact(const int64_t* __restrict__ A, int64_t lda, int M, int K,
+                                                    WDesc W, int64_t* __restrict__ C, int64_t ldc, int shift,
+                                                    const int64_t* __restrict__ R, int64_t ldr) {
+    __shared__ int64_t As[GBK][GBM + 1];
+    __shared__ int64_t Ws[GBK][GBN + 1];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * GBM, n0 = blockIdx.x * GBN;
+    const int N = (int)W.N;
+    u128 acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0;
+
+    for (int k0 = 0; k0 < K; k0 += GBK) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            int idx = tid + 256 * i, r = idx >> 5, c = idx & 31;
+            int gm = m0 + r, gk = k0 + c;
+            As[c][r] = (gm < M && gk < K) ? A[(int64_t)gm * lda + gk] : 0;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            int idx = tid + 256 * i, r = idx >> 5, c = idx & 31;
+            int gn = n0 + r, gk = k0 + c;
+            int64_t w = 0;
+            if (gn < N && gk < K)
+                w = composite(dequant_elem(W.dtype, W.data, (int64_t)gn * K + gk, W.nblocks), W.mode, W.scale);
+            Ws[c][r] = w;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int kk = 0; kk < GBK; kk++) {
+            int64_t a[4], w[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) a[i] = As[kk][ty + 16 * i];
+#pragma unroll
+            for (int j = 0; j < 4; j++) w[j] = Ws[kk][tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] += (u128)((i128)a[i] * (i128)w[j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int m = m0 + ty + 16 * i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int n = n0 + tx + 16 * j;
+            if (n >= N) continue;
+            int64_t v = shift > 0 ? lo64(sar128((i128)acc[i][j], shift)) : lo64((i128)acc[i][j]);
+            if (R) v = wadd(v, R[(int64_t)m * ldr + n]);
+            C[(int64_t)m * ldc + n] = v;
+        }
+    }
+}
+
+__global__ void k_weight_q30(WDesc W, int64_t n, int64_t* out) {
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i < n) out[i] = composite(dequant_elem(W.dtype, W.data, i, W.nblocks), W.mode, W.scale);
+}
+}  // namespace
+
+int gemm_exact(const int64_t* a, int64_t lda, int M, int K, const WDesc& w, int64_t* c, int64_t ldc, int shift,
+                const int64_t* r, int64_t ldr, cudaStream_t st) {
+    if (M <= 0 || w.N <= 0) return 0;
+    dim3 grid((unsigned)((w.N + GBN - 1) / GBN), (unsigned)((M + GBM - 1) / GBM));
+    k_gemm_exact<<<grid, 256, 0, st>>>(a, lda, M, K, w, c, ldc, shift, r, ldr);
+    return 1;
+}
+
+int weight_to_q30(const WDesc& w, int64_t n, int64_t* out, cudaStream_t st) {
+    if (n <= 0) return 0;
+    k_weight_q30<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, n, out);
+    return 1;
+}
+
+// ------------------------------------------------------------------------------------------
+// GgufDequantizer formulas for every decodable dtype (GgufDequantizer.cs:7-325), one element per
+// thread, float arithmetic in the reference's order without contraction.
+// ------------------------------------------------------------------------------------------
+namespace {
+__device__ __constant__ float c_mxfp4[15] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
+                                             -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -10.0f};
+
+SLX_DEV void q4k_scale(const uint8_t* raw, int j, int& sc, int& m) {  // UnpackQ4KScales (:345-357)
+    if (j < 4) {
+        sc = raw[j] & 63;
+        m = raw[j + 4] & 63;
+    } else {
+        sc = (raw[j + 4] & 0x0F) | ((raw[j - 4] >> 6) << 4);
+        m = (raw[j + 4] >> 4) | ((raw[j] >> 6) << 4);
+    }
+}
+
+__global__ void k_dequant_f32(int dtype, const uint8_t* __restrict__ raw, int64_t n, float* __restrict__ out,
+                              int* flag) {
+    int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (e >= n) return;
+    float v = 0.0f;
+    switch (dtype) {
+        case 0: v = ((const float*)raw)[e]; break;
+        case 1: v = h2f(((const uint16_t*)raw)[e]); break;
+        case 30: v = __uint_as_float((uint32_t)((const uint16_t*)raw)[e] << 16); break;
+        case 8: case 2: v = dequant_elem(dtype, raw, e, n / 32); break;
+        case 39: {  // DequantizeMXFP4 (:97-123)
+            int64_t b = e >> 5;
+            if (b >= n / 32) break;
+            const uint8_t* blk = raw + b * 17;
+            int j = (int)(e & 31);
+            uint8_t byte = blk[1 + (j >> 1)];
+            // The reference decodes lo then hi of each byte; an out-of-range nibble throws.
+            int nib = (j & 1) ? ((byte >> 4) & 0x0F) : (byte & 0x0F);
+            uint8_t e8 = blk[0];
+            float shared = e8 == 0 ? 0.0f : ldexpf(1.0f, (int)e8 - 127);
+            if (nib >= 15) { atomicOr(flag, KERR_RANGE); break; }
+            v = __fmul_rn(c_mxfp4[nib], shared);
+            break;
+        }
+        case 10: {  // DequantizeQ2K (:125-156)
+            int64_t sb = e >> 8;
+            if (sb >= n / 256) break;
+            const uint8_t* s = raw + sb * 84;
+            int j = (int)(e & 255);
+            float d = h2f(ld_u16(s)), dmin = h2f(ld_u16(s + 2));
+            uint8_t scb = s[4 + j / 16];
+            int q = (s[20 + j / 4] >> ((j % 4) * 2)) & 3;
+            v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)(scb & 0x0F)), (float)q), __fmul_rn(dmin, (float)(scb >> 4)));
+            break;
+        }
+        case 11: {  // DequantizeQ3K (:158-199)
+            int64_t sb = e >> 8;
+            if (sb >= n / 256) break;
+            const uint8_t* s = raw + sb * 110;
+            int j = (int)(e & 255), g = j / 16;
+            const uint8_t* sc = s + 96;
+            int low4 = (g < 8) ? (sc[g] & 0x0F) : (sc[g - 8] >> 4);
+            int high2 = (sc[8 + g / 4] >> (2 * (g % 4))) & 3;
+            int scale = (low4 | (high2 << 4)) - 32;
+            int q = ((s[32 + j / 4] >> ((j % 4) * 2)) & 3) | (((s[j / 8] >> (j % 8)) & 1) << 2);
+            float d = h2f(ld_u16(s + 108));
+            v = __fmul_rn(__fmul_rn(d, (float)scale), (float)(q - 4));
+            break;
+        }
+        case 12: case 13: {  // DequantizeQ4K (:201-232), DequantizeQ5K (:234-268)
+            bool q5 = dtype == 13;
+            int64_t sb = e >> 8;
+            if (sb >= n / 256) break;
+            const uint8_t* s = raw + sb * (q5 ? 176 : 144);
+            int j = (int)(e & 255), sub = j / 32;
+            int sc, m;
+            q4k_scale(s + 4, sub, sc, m);
+            int qb = s[(q5 ? 48 : 16) + j / 2];
+            int q = (j % 2 == 0) ? (qb & 0x0F) : (qb >> 4);
+            if (q5) q |= ((s[16 + j / 8] >> (j % 8)) & 1) << 4;
+            float d = h2f(ld_u16(s)), dmin = h2f(ld_u16(s + 2));
+            v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
+            break;
+        }
+        case 14: {  // DequantizeQ6K (:270-303)
+            int64_t sb = e >> 8;
+            if (sb >= n / 256) break;
+            const uint8_t* s = raw + sb * 210;
+            int j = (int)(e & 255);
+            int8_t sc = (int8_t)s[192 + j / 16];
+            int qb = s[j / 2];
+            int q = ((j % 2 == 0) ? (qb & 0x0F) : (qb >> 4)) | (((s[128 + j / 4] >> ((j % 4) * 2)) & 3) << 4);
+            float d = h2f(ld_u16(s + 208));
+            v = __fmul_rn(__fmul_rn(d, (float)sc), (float)(q - 32));
+            break;
+        }
+        case 15: {  // DequantizeQ8K (:305-325)
+            int64_t sb = e >> 8;
+            if (sb >= n / 256) break;
+            const uint8_t* s = raw + sb * 292;
+            float d;
+            memcpy(&d, s, 4);
+            v = __fmul_rn(d, (float)(int8_t)s[4 + (e & 255)]);
+            break;
+        }
+    }
+    out[e] = v;
+}
+}  // namespace
+
+int dequant_f32(int dtype, const uint8_t* raw, int64_t n, float* out, int* flag, cudaStream_t st) {
+    if (n <= 0) return 0;
+    k_dequant_f32<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(dtype, raw, n, out, flag);
+    return 1;
+}
+
+// ------------------------------------------------------------------------------------------
+// Embeddings
+// ------------------------------------------------------------------------------------------
+namespace {
+// IntegerTransformerSource.BuildEmbeddings (IntegerTransformerSource.Forward.cs:7-26)
+__global__ void k_embed_encoder(const int32_t* __restrict__ ids, int T, WDesc tok, const int64_t* __restrict__ tt,
+                                int unk, int64_t* __restrict__ x, int* flag) {
+    int row = blockIdx.x;
+    int d = (int)tok.K;
+    int id = ids[row];
+    int64_t src = (int64_t)id * d;
+    if (id < 0 || src + d > tok.elements) src = (int64_t)unk * d;
+    bool bad = unk < 0 || src + d > tok.elements;
+    if (bad && threadIdx.x == 0) atomicOr(flag, KERR_RANGE);
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        int64_t e = bad ? 0 : composite(dequant_elem(tok.dtype, tok.data, src + j, tok.nblocks), tok.mode, tok.scale);
+        x[(int64_t)row * d + j] = wadd(e, tt[j]);
+    }
+}
+
+// IntegerCausalSource.BuildEmbeddings (IntegerCausalSource.Forward.cs:7-31) with a Half composite;
+// IntegerGemmaSource.BuildEmbeddings (IntegerGemmaSource.Forward.cs:7-30) with a long composite.
+__global__ void k_embed_scaled(const int32_t* __restrict__ ids, WDesc tok, int unk, int64_t sqrt_d,
+                               int64_t* __restrict__ x, int* flag) {
+    int row = blockIdx.x;
+    int d = (int)tok.K;
+    int id = ids[row];
+    int64_t src = (int64_t)id * d;
+    if (id < 0 || src + d > tok.elements) src = (int64_t)unk * d;
+    bool bad = unk < 0 || src + d > tok.elements;
+    if (bad && threadIdx.x == 0) atomicOr(flag, KERR_RANGE);
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        int64_t e = bad ? 0 : composite(dequant_elem(tok.dtype, tok.data, src + j, tok.nblocks), tok.mode, tok.scale);
+        x[(int64_t)row * d + j] = lo64((i128)e * sqrt_d);
+    }
+}
+}  // namespace
+
+int embed_encoder(const int32_t* ids, int B, int T, const WDesc& tok, const int64_t* tt, int unk, int64_t* x,
+                   int* flag, cudaStream_t st) {
+    if (B * T <= 0) return 0;
+    k_embed_encoder<<<B * T, 256, 0, st>>>(ids, T, tok, tt, unk, x, flag);
+    return 1;
+}
+
+int embed_scaled(const int32_t* ids, int B, int T, const WDesc& tok, int unk, int64_t sqrt_d, int64_t* x, int* flag,
+                  cudaStream_t st) {
+    if (B * T <= 0) return 0;
+    k_embed_scaled<<<B * T, 256, 0, st>>>(ids, tok, unk, sqrt_d, x, flag);
+    return 1;
+}
+
+// ------------------------------------------------------------------------------------------
+// Norms (IntegerLayerNorm.cs)
+// ------------------------------------------------------------------------------------------
+namespace {
+constexpr int NT = 256;
+
+SLX_DEV u128 block_sum_u128(u128 v, u128* sh) {
+    v = warp_sum_u128(v);
+    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) sh[w] = v;
+    __syncthreads();
+    u128 t = 0;
+    if (threadIdx.x < 32) {
+        t = (threadIdx.x < (blockDim.x >> 5)) ? sh[threadIdx.x] : 0;
+        t = warp_sum_u128(t);
+        if (threadIdx.x == 0) sh[0] = t;
+    }
+    __syncthreads();
+    t = sh[0];
+    __syncthreads();
+    return t;
+}
+
+// NormalizeRow (IntegerLayerNorm.cs:21-57)
+__global__ __launch_bounds__(NT) void k_layernorm(int64_t* __restrict__ X, int64_t ld, int n,
+                                                  const int64_t* __restrict__ w, const int64_t* __restrict__ b) {
+    __shared__ u128 sh[NT / 32];
+    __shared__ int64_t s_isq;
+    __shared__ int s_zero;
+    int64_t* x = X + (int64_t)blockIdx.x * ld;
+    u128 s = 0;
+    for (int j = threadIdx.x; j < n; j += NT) s += (u128)(i128)x[j];
+    s = block_sum_u128(s, sh);
+    int64_t mean = lo64((i128)s / (i128)n);
+    u128 ss = 0;
+    for (int j = threadIdx.x; j < n; j += NT) {
+        int64_t dl = wsub(x[j], mean);
+        ss += (u128)((i128)dl * dl);
+    }
+    ss = block_sum_u128(ss, sh);
+    if (threadIdx.x == 0) {
+        i128 var = (i128)ss / (i128)n;
+        s_zero = var <= 0;
+        int64_t isq = var > 0 ? isqrt_u128((u128)var) : 0;
+        s_isq = isq == 0 ? 1 : isq;
+    }
+    __syncthreads();
+    if (s_zero) {
+        for (int j = threadIdx.x; j < n; j += NT) x[j] = b[j];
+        return;
+    }
+    int64_t isq = s_isq;
+    for (int j = threadIdx.x; j < n; j += NT) {
+        int64_t dl = wsub(x[j], mean);
+        x[j] = wadd(lo64(((i128)dl * w[j]) / (i128)isq), b[j]);
+    }
+}
+
+// RmsNormRow (IntegerLayerNorm.cs:71-93); row r = segment (r % per) of line (r / per).
+__global__ __launch_bounds__(NT) void k_rmsnorm(int64_t* __restrict__ X, int64_t ld, int per, int n,
+                                                const int64_t* __restrict__ w) {
+    __shared__ u128 sh[NT / 32];
+    __shared__ int64_t s_rms;
+    __shared__ int s_skip;
+    int r = blockIdx.x;
+    int64_t* x = X + (int64_t)(r / per) * ld + (int64_t)(r % per) * n;
+    u128 ss = 0;
+    for (int j = threadIdx.x; j < n; j += NT) ss += (u128)((i128)x[j] * x[j]);
+    ss = block_sum_u128(ss, sh);
+    if (threadIdx.x == 0) {
+        i128 ms = (i128)ss / (i128)n;
+        s_skip = ms <= 0;
+        int64_t rms = ms > 0 ? isqrt_u128((u128)ms) : 0;
+        s_rms = rms == 0 ? 1 : rms;
+    }
+    __syncthreads();
+    if (s_skip) return;
+    int64_t rms = s_rms;
+    for (int j = threadIdx.x; j < n; j += NT) x[j] = lo64(((i128)x[j] * w[j]) / (i128)rms);
+}
+}  // namespace
+
+int layernorm_rows(int64_t* x, int64_t ld, int rows, int n, const int64_t* w, const int64_t* b, cudaStream_t st) {
+    if (rows <= 0) return 0;
+    k_layernorm<<<rows, NT, 0, st>>>(x, ld, n, w, b);
+    return 1;
+}
+
+int rmsnorm_rows(int64_t* x, int64_t ld, int rows, int per, int n, const int64_t* w, cudaStream_t st) {
+    if (rows <= 0) return 0;
+    k_rmsnorm<<<rows, NT, 0, st>>>(x, ld, per, n, w);
+    return 1;
+}
+
+// ------------------------------------------------------------------------------------------
+// RoPE (IntegerAttention.ApplyRoPE, IntegerAttention.cs:35-58)
+// ------------------------------------------------------------------------------------------
+namespace {
+__global__ void k_rope(int64_t* __restrict__ X, int64_t ld, int T, int nh, int hd, const int64_t* __restrict__ cs,
+                       const int64_t* __restrict__ sn, int64_t total) {
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    int half = hd / 2;
+    int p = (int)(i % half);
+    int64_t mh = i / half;
+    int h = (int)(mh % nh);
+    int64_t m = mh / nh;
+    int t = (int)(m % T);
+    int64_t* hb = X + m * ld + (int64_t)h * hd;
+    int64_t c = cs[(int64_t)t * half + p], s = sn[(int64_t)t * half + p];
+    int64_t x0 = hb[p], x1 = hb[p + half];
+    hb[p] = lo64(sar128((i128)((u128)((i128)x0 * c) - (u128)((i128)x1 * s)), 30));
+    hb[p + half] = lo64(sar128((i128)((u128)((i128)x0 * s) + (u128)((i128)x1 * c)), 30));
+}
+}  // namespace
+
+int rope_rows(int64_t* x, int64_t ld, int B, int T, int nh, int hd, const int64_t* cos, const int64_t* sin,
+               cudaStream_t st) {
+    int64_t total = (int64_t)B * T * nh * (hd / 2);
+    if (total <= 0) return 0;
+    k_rope<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(x, ld, T, nh, hd, cos, sin, total);
+    return 1;
+}
+
+// ------------------------------------------------------------------------------------------
+// Attention, one warp per query row (IntegerAttention.cs:60-109, 165-202, 246-289, 333-377):
+// scores (long)(dot >> shift) / ISqrt64(hd) with masked slots set to -2^29, FixedSoftmax over the
+// whole row, then out[d] += (long)((Int128)w * v[s][d] >> 30) term by term.
+// ------------------------------------------------------------------------------------------
+namespace {
+constexpr int AW = 4;  // warps (query rows) per block
+
+__global__ __launch_bounds__(AW * 32) void k_attention(const int64_t* __restrict__ Q, int64_t ldq,
+                                                       const int64_t* __restrict__ Kp, int64_t ldk,
+                                                       const int64_t* __restrict__ V, int64_t ldv,
+                                                       int64_t* __restrict__ O, int64_t ldo, int T, int nh, int nkv,
+                                                       int hd, int score_shift, int64_t sqrt_hd, int mode,
+                                                       int window) {
+    extern __shared__ int64_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * AW + warp;
+    const int h = blockIdx.y, b = blockIdx.z;
+    int64_t* sc = smem + (size_t)warp * (T + hd);
+    int64_t* qrow = sc + T;
+    if (t >= T) return;
+    const int kvh = h / (nh / nkv);
+    const int64_t rowq = (int64_t)b * T + t;
+    for (int d = lane; d < hd; d += 32) qrow[d] = Q[rowq * ldq + (int64_t)h * hd + d];
+    __syncwarp();
+    const int64_t mask = -(1LL << 29);
+    const int ws = t - window + 1 > 0 ? t - window + 1 : 0;
+    int64_t mx = INT64_MIN;
+    for (int s = lane; s < T; s += 32) {
+        int64_t v;
+        if ((mode >= 1 && s > t) || (mode == 2 && s < ws)) {
+            v = mask;
+        } else {
+            const int64_t* kr = Kp + ((int64_t)b * T + s) * ldk + (int64_t)kvh * hd;
+            u128 acc = 0;
+            for (int d = 0; d < hd; d++) acc += (u128)((i128)qrow[d] * kr[d]);
+            v = cs_div64(lo64(sar128((i128)acc, score_shift)), sqrt_hd);
+        }
+        sc[s] = v;
+        mx = v > mx ? v : mx;
+    }
+    mx = warp_max_i64(mx);
+    u128 sum = 0;
+    for (int s = lane; s < T; s += 32) {
+        int64_t e = fixed_exp30(wsub(sc[s], mx));
+        sc[s] = e;
+        sum += (u128)(i128)e;
+    }
+    sum = warp_sum_u128(sum);
+    const i128 ssum = (i128)sum;
+    const bool fast = ssum > 0 && (sum >> 64) == 0;
+    for (int s = lane; s < T; s += 32) {
+        int64_t e = sc[s];
+        int64_t p;
+        if (ssum == 0)
+            p = (1LL << 30) / T;
+        else if (fast && e >= 0 && e <= (1LL << 33))
+            p = (int64_t)(((uint64_t)e << 30) / (uint64_t)sum);
+        else
+            p = lo64(((i128)e * (1LL << 30)) / ssum);
+        sc[s] = p;
+    }
+    __syncwarp();
+    int64_t* orow = O + rowq * ldo + (int64_t)h * hd;
+    const int64_t* vb = V + (int64_t)b * T * ldv + (int64_t)kvh * hd;
+    for (int d = lane; d < hd; d += 32) {
+        int64_t acc = 0;
+        for (int s = 0; s < T; s++) acc = wadd(acc, lo64(sar128((i128)sc[s] * vb[(int64_t)s * ldv + d], 30)));
+        orow[d] = acc;
+    }
+}
+}  // namespace
+
+int attention(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
+               int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int score_shift, int64_t sqrt_hd,
+               int mode, int window, cudaStream_t st) {
+    if (B * T <= 0) return 0;
+    size_t smem = (size_t)AW * (T + hd) * sizeof(int64_t);
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        configured = smem;
+    }
+    dim3 grid((unsigned)((T + AW - 1) / AW), (unsigned)nh, (unsigned)B);
+    k_attention<<<grid, AW * 32, smem, st>>>(q, ldq, k, ldk, v, ldv, out, ldo, T, nh, nkv, hd, score_shift, sqrt_hd,
+                                             mode, window);
+    return 1;
+}
+
+// ------------------------------------------------------------------------------------------
+// FFN gate, residual adds, pooling
+// ------------------------------------------------------------------------------------------
+namespace {
+// IntegerFFN.Apply: up[i] = (long)((Int128)FixedSiLU(gate[i]) * up[i] >> 30) (IntegerFFN.cs:84-89)
+__global__ void k_silu_gate(const int64_t* __restrict__ G, int64_t ldg, int64_t* __restrict__ U, int64_t ldu, int F,
+                            int64_t total) {
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    int64_t m = i / F, f = i % F;
+    int64_t g = G[m * ldg + f];
+    int64_t* u = U + m * ldu + f;
+    *u = lo64(sar128((i128)fixed_silu30(g) * *u, 30));
+}
+
+__global__ void k_add(int64_t* __restrict__ D, int64_t ldd, const int64_t* __restrict__ S, int64_t lds, int n,
+                      int64_t total) {
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    int64_t m = i / n, j = i % n;
+    D[m * ldd + j] = wadd(D[m * ldd + j], S[m * lds + j]);
+}
+
+// MeanPool (IntegerTransformerSource.Forward.cs:69-87)
+__global__ void k_mean_pool(const int64_t* __restrict__ X, int64_t ld, int T, int d, int64_t* __restrict__ P) {
+    int j = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+    if (j >= d) return;
+    u128 s = 0;
+    for (int t = 0; t < T; t++) s += (u128)(i128)X[((int64_t)b * T + t) * ld + j];
+    P[(int64_t)b * d + j] = T > 0 ? lo64((i128)s / (i128)T) : 0;
+}
+
+__global__ void k_gather_last(const int64_t* __restrict__ X, int64_t ld, int T, int d, int64_t* __restrict__ D) {
+    int j = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+    if (j < d) D[(int64_t)b * d + j] = X[((int64_t)b * T + T - 1) * ld + j];
+}
+
+// VocabLattice.ArgmaxBruteForce (Lattice/VocabLattice.cs:103-126): h[j] = (float)(last[j] * 2^-s)
+// (IntegerCausalSource.ForwardCausalFloat :114-122), dot accumulated in order j = 0..d-1 with
+// separate fp32 multiply and add, strict '>' (first maximum wins, NaN never selected).
+// Candidates are combined through a 64-bit key: ordered score bits, then the inverted row id.
+constexpr int AMT = 128;
+SLX_DEV uint32_t ordered(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__global__ __launch_bounds__(AMT) void k_argmax(const int64_t* __restrict__ last, int d, WDesc tok, int vocab,
+                                                double scale, unsigned long long* keys) {
+    extern __shared__ float hs[];
+    int b = blockIdx.y;
+    for (int j = threadIdx.x; j < d; j += AMT) hs[j] = __double2float_rn((double)last[(int64_t)b * d + j] * scale);
+    __syncthreads();
+    int v = blockIdx.x * AMT + threadIdx.x;
+    unsigned long long key = 0;
+    if (v < vocab) {
+        float dot = 0.0f;
+        int64_t base = (int64_t)v * d;
+        for (int j = 0; j < d; j++) {
+            float e = h2f(f2h(dequant_elem(tok.dtype, tok.data, base + j, tok.nblocks)));
+            dot = __fadd_rn(dot, __fmul_rn(hs[j], e));
+        }
+        if (dot > -INFINITY) key = ((unsigned long long)ordered(dot) << 32) | (0xFFFFFFFFu - (uint32_t)v);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+        key = k2 > key ? k2 : key;
+    }
+    if ((threadIdx.x & 31) == 0 && key) atomicMax(keys + b, key);
+}
+
+__global__ void k_keys_to_ids(const unsigned long long* keys, int B, int32_t* ids) {
+    int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) ids[b] = keys[b] ? (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[b] & 0xFFFFFFFFu)) : 0;
+}
+}  // namespace
+
+int silu_gate(const int64_t* gate, int64_t ldg, int64_t* up, int64_t ldu, int M, int F, cudaStream_t st) {
+    int64_t total = (int64_t)M * F;
+    if (total <= 0) return 0;
+    k_silu_gate<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(gate, ldg, up, ldu, F, total);
+    return 1;
+}
+
+int add_rows(int64_t* dst, int64_t ldd, const int64_t* src, int64_t lds, int M, int n, cudaStream_t st) {
+    int64_t total = (int64_t)M * n;
+    if (total <= 0) return 0;
+    k_add<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(dst, ldd, src, lds, n, total);
+    return 1;
+}
+
+int mean_pool(const int64_t* x, int64_t ld, int B, int T, int d, int64_t* pooled, cudaStream_t st) {
+    if (B <= 0) return 0;
+    k_mean_pool<<<dim3((unsigned)((d + 127) / 128), (unsigned)B), 128, 0, st>>>(x, ld, T, d, pooled);
+    return 1;
+}
+
+int gather_last_rows(const int64_t* x, int64_t ld, int B, int T, int d, int64_t* dst, cudaStream_t st) {
+    if (B <= 0) return 0;
+    k_gather_last<<<dim3((unsigned)((d + 127) / 128), (unsigned)B), 128, 0, st>>>(x, ld, T, d, dst);
+    return 1;
+}
+
+int argmax_vocab(const int64_t* last, int B, int d, const WDesc& tok, int vocab, int scale_bits,
+                  unsigned long long* keys, int32_t* ids, cudaStream_t st) {
+    if (B <= 0) return 0;
+    int64_t rows = tok.elements / d;
+    if (vocab > rows) vocab = (int)rows;
+    cudaMemsetAsync(keys, 0, sizeof(unsigned long long) * B, st);
+    size_t smem = (size_t)d * sizeof(float);
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        cudaFuncSetAttribute(k_argmax, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        configured = smem;
+    }
+    if (vocab > 0) {
+        dim3 grid((unsigned)((vocab + AMT - 1) / AMT), (unsigned)B);
+        k_argmax<<<grid, AMT, smem, st>>>(last, d, tok, vocab, ldexp(1.0, -scale_bits), keys);
+    }
+    k_keys_to_ids<<<(B + 127) / 128, 128, 0, st>>>(keys, B, ids);
+    return 1 + (vocab > 0 ? 1 : 0);
+}
+
+}  // namespace slx

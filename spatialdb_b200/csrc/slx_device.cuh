@@ -1,0 +1,147 @@
+// slx_device.cuh -- device-side integer helpers shared by the slx kernels.
+//
+// The arithmetic follows C# semantics of SparseLattice's integer path:
+//   * long / Int128 arithmetic wraps (unchecked), so sums are carried in unsigned __int128;
+//   * `/` truncates toward zero, `>>` on signed values floors;
+//   * (long)double truncates, NaN / out of range gives long.MinValue (x64 .NET 8 conversion);
+//   * (Half)float rounds to nearest even (__float2half_rn).
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+
+typedef __int128 i128;
+typedef unsigned __int128 u128;
+
+#define SLX_DEV __device__ __forceinline__
+
+SLX_DEV int64_t lo64(i128 v) { return (int64_t)(uint64_t)(u128)v; }
+SLX_DEV i128 sar128(i128 v, int n) { return v >> (n & 127); }
+SLX_DEV int64_t wadd(int64_t a, int64_t b) { return (int64_t)((uint64_t)a + (uint64_t)b); }
+SLX_DEV int64_t wsub(int64_t a, int64_t b) { return (int64_t)((uint64_t)a - (uint64_t)b); }
+SLX_DEV int64_t wmul(int64_t a, int64_t b) { return (int64_t)((uint64_t)a * (uint64_t)b); }
+SLX_DEV int64_t cs_div64(int64_t a, int64_t b) { return b == -1 ? wsub(0, a) : a / b; }
+
+SLX_DEV int64_t cs_d2l(double v) {
+    if (v >= -9223372036854775808.0 && v < 9223372036854775808.0) return __double2ll_rz(v);
+    return INT64_MIN;
+}
+
+SLX_DEV float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+SLX_DEV uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+SLX_DEV uint16_t ld_u16(const uint8_t* p) { return *(const uint16_t*)p; }
+
+// GGUF dtype ids (GgufTypes.cs:21-38).
+enum : int { DT_F32 = 0, DT_F16 = 1, DT_Q4_0 = 2, DT_Q8_0 = 8, DT_BF16 = 30 };
+
+// One element of a flat GGUF tensor, decoded the way GgufDequantizer decodes it
+// (Q8_0: GgufDequantizer.cs:31-49, Q4_0: :51-76 with element 2j in the low nibble, F16: :19-29,
+// BF16: :78-89, F32: :7-17). `nblocks` bounds the 32-element blocks (ComputeByteCount truncates).
+SLX_DEV float dequant_elem(int dtype, const uint8_t* base, int64_t e, int64_t nblocks) {
+    switch (dtype) {
+        case DT_Q8_0: {
+            int64_t b = e >> 5;
+            if (b >= nblocks) return 0.0f;
+            const uint8_t* blk = base + b * 34;
+            return __fmul_rn(h2f(ld_u16(blk)), (float)(int8_t)blk[2 + (e & 31)]);
+        }
+        case DT_Q4_0: {
+            int64_t b = e >> 5;
+            if (b >= nblocks) return 0.0f;
+            const uint8_t* blk = base + b * 18;
+            int j = (int)(e & 31);
+            uint8_t raw = blk[2 + (j >> 1)];
+            int q = ((j & 1) ? (raw >> 4) : (raw & 0x0F)) - 8;
+            return __fmul_rn(h2f(ld_u16(blk)), (float)q);
+        }
+        case DT_F16: return h2f(((const uint16_t*)base)[e]);
+        case DT_BF16: return __uint_as_float((uint32_t)((const uint16_t*)base)[e] << 16);
+        default: return ((const float*)base)[e];
+    }
+}
+
+// Composite Q30 weight as the reference forms it from a dequantized float:
+//   mode 0 (IntegerTransformerSource.Q, IntegerMatMul.QuantizeFromFloat :297-304): (long)(f * 2^s)
+//   mode 1 (IntegerCausalSource.ReadAsHalf + DotInt128Mixed(Half) :255-275): (long)((float)(Half)f * 2^s)
+SLX_DEV int64_t composite(float f, int mode, double scale) {
+    if (mode == 1) f = h2f(f2h(f));
+    return cs_d2l((double)f * scale);
+}
+
+// Exact floor square root of a non-negative 128-bit value (ISqrt64 / ISqrt128,
+// IntegerLayerNorm.cs:99-149). Returned as the low 64 bits, like the reference's (long)x.
+SLX_DEV int64_t isqrt_u128(u128 v) {
+    if (v == 0) return 0;
+    u128 x = (u128)sqrt((double)v);
+    if (x == 0) x = 1;
+    if ((v >> 104) != 0) {  // double seed is short of bits: Newton steps
+        for (int it = 0; it < 4; it++) {
+            u128 nx = (x + v / x) >> 1;
+            if (nx == x) break;
+            x = nx;
+        }
+    }
+    while (x * x > v) x--;
+    while ((x + 1) * (x + 1) <= v) x++;
+    return (int64_t)(uint64_t)x;
+}
+
+// FixedExp (IntegerTranscendentals.cs:13-47), fracBits = 30. The Taylor term update
+// (long)((Int128)term * r / (n << 30)) equals ((term * r) >> 30) / n whenever term, r >= 0 and
+// term * r < 2^64 (floor of floor); that fast path covers every input after range reduction,
+// the general Int128 form stays for anything else.
+SLX_DEV int64_t fixed_exp30(int64_t x) {
+    const int64_t ln2 = 744261117;  // (long)(0.6931471805599453 * 2^30)
+    int64_t k = x >= 0 ? x / ln2 : wsub(0, cs_div64(wsub(wadd(wsub(0, x), ln2), 1), ln2));
+    int64_t r = wsub(x, wmul(k, ln2));
+    if (k > 62) return INT64_MAX;
+    if (k < -40) return 0;
+    const int64_t one = 1LL << 30;
+    int64_t term = one, sum = one;
+#pragma unroll
+    for (int n = 1; n <= 14; n++) {
+        if (term >= 0 && r >= 0 && __umul64hi((uint64_t)term, (uint64_t)r) == 0) {
+            uint64_t p = (uint64_t)term * (uint64_t)r;
+            term = (int64_t)((p >> 30) / (uint64_t)n);
+        } else {
+            term = lo64(((i128)term * r) / ((i128)n << 30));
+        }
+        sum = wadd(sum, term);
+        if (term == 0 && n > 4) break;
+    }
+    if (k >= 0) {
+        if (k >= 63 || sum > (INT64_MAX >> k)) return INT64_MAX;
+        return (int64_t)((uint64_t)sum << k);
+    }
+    int sh = (int)(-k);
+    if (sh >= 63) return 0;
+    return sum >> sh;
+}
+
+// FixedSigmoid / FixedSiLU (IntegerTranscendentals.cs:49-69), fracBits = 30.
+SLX_DEV int64_t fixed_sigmoid30(int64_t x) {
+    const int64_t one = 1LL << 30, thr = 20LL << 30;
+    if (x > thr) return one;
+    if (x < -thr) return 0;
+    int64_t den = wadd(one, fixed_exp30(wsub(0, x)));
+    if (den == 0) return one;
+    if (den > 0) return (int64_t)((1ULL << 60) / (uint64_t)den);
+    return lo64((i128)(1LL << 60) / (i128)den);
+}
+SLX_DEV int64_t fixed_silu30(int64_t x) { return lo64(sar128((i128)x * fixed_sigmoid30(x), 30)); }
+
+// 128-bit warp reductions (wrap-around sums).
+SLX_DEV u128 warp_sum_u128(u128 v) {
+    for (int o = 16; o > 0; o >>= 1) {
+        uint64_t lo = __shfl_xor_sync(0xffffffffu, (unsigned long long)(uint64_t)v, o);
+        uint64_t hi = __shfl_xor_sync(0xffffffffu, (unsigned long long)(uint64_t)(v >> 64), o);
+        v += ((u128)hi << 64) | lo;
+    }
+    return v;
+}
+SLX_DEV int64_t warp_max_i64(int64_t v) {
+    for (int o = 16; o > 0; o >>= 1) {
+        int64_t w = (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, o);
+        v = w > v ? w : v;
+    }
+    return v;
+}

@@ -1,0 +1,855 @@
+// slx_model.cu -- model loading, forward orchestration and the extern "C" entry points of libslx.
+//
+// The forward passes restate, stage by stage, the reference sources:
+//   encoder:  IntegerTransformerSource.Forward (Gguf/IntegerTransformerSource.cs:65-78) and
+//             ApplyTransformerBlock (Gguf/IntegerTransformerSource.Forward.cs:28-67);
+//   causal:   IntegerCausalSource.ForwardCausal (Gguf/IntegerCausalSource.cs:128-147) and
+//             ApplyCausalBlock (Gguf/IntegerCausalSource.Forward.cs:45-114);
+//   gemma encoder: IntegerGemmaSource.Forward (Gguf/IntegerGemmaSource.cs:66-80) and
+//             ApplyGemmaBlock (Gguf/IntegerGemmaSource.Forward.cs:32-75).
+// B independent sequences of T tokens run as one batch: every projection is one GEMM over B*T
+// rows, attention and pooling stay per sequence.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "gguf.hpp"
+#include "slx.h"
+#include "slx_kernels.h"
+#include "slx_gemm.h"
+
+using namespace slx;
+
+// Kernel classes reported by slx_profile_end.
+enum KClass { KC_GEMM, KC_ATTENTION, KC_NORM, KC_ROPE, KC_FFN_GATE, KC_EMBED, KC_POOL, KC_ADD, KC_ARGMAX, KC_COUNT };
+static const char* kKClassName[KC_COUNT] = {"gemm", "attention", "norm", "rope", "ffn_gate", "embed", "pool", "add", "argmax"};
+
+struct ProfRecord {
+    int cls;
+    int launches;
+    cudaEvent_t a, b;
+    double macs, bytes;
+};
+
+struct slx_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    int* d_flag = nullptr;
+    int64_t launches = 0;            // kernels queued by the library on this context
+    bool prof = false;
+    std::vector<ProfRecord> records;
+    std::vector<cudaEvent_t> event_pool;
+    cudaEvent_t event() {
+        if (!event_pool.empty()) { cudaEvent_t e = event_pool.back(); event_pool.pop_back(); return e; }
+        cudaEvent_t e = nullptr;
+        cudaEventCreate(&e);
+        return e;
+    }
+};
+
+// Runs one launcher (which returns how many kernels it queued), counting launches and, when
+// profiling, bracketing it with events on the launch stream.
+template <class F>
+static inline void run_k(slx_ctx* c, int cls, double macs, double bytes, cudaStream_t st, F&& f) {
+    if (!c->prof) {
+        c->launches += f();
+        return;
+    }
+    ProfRecord r{cls, 0, c->event(), c->event(), macs, bytes};
+    cudaEventRecord(r.a, st);
+    r.launches = f();
+    cudaEventRecord(r.b, st);
+    c->launches += r.launches;
+    c->records.push_back(r);
+}
+
+namespace {
+
+int set_err(slx_ctx* c, int code, const char* fmt, ...) {
+    if (!c) return code;
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    c->err = buf;
+    return code;
+}
+
+#define CK(call)                                                                                 \
+    do {                                                                                         \
+        cudaError_t e_ = (call);                                                                 \
+        if (e_ != cudaSuccess)                                                                   \
+            return set_err(ctx, e_ == cudaErrorMemoryAllocation ? SLX_EOOM : SLX_ECUDA, "%s: %s", \
+                           #call, cudaGetErrorString(e_));                                      \
+    } while (0)
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+};
+
+// Exact floor sqrt of a non-negative long (ISqrt64, Math/IntegerLayerNorm.cs:130-149).
+int64_t isqrt64_host(int64_t v) {
+    if (v <= 0) return 0;
+    int64_t x = (int64_t)std::sqrt((double)v);
+    if (x <= 0) x = 1;
+    while (x > 0 && (__int128)x * x > v) x--;
+    while ((__int128)(x + 1) * (x + 1) <= v) x++;
+    return x;
+}
+
+// IntegerRoPECache (Math/IntegerAttention.cs:14-32): built on the host in double precision with
+// the C library's pow/cos/sin, truncated to Q30.
+void rope_table(int rows, int hd, float base, std::vector<int64_t>& cs, std::vector<int64_t>& sn) {
+    int half = hd / 2;
+    cs.assign((size_t)rows * half, 0);
+    sn.assign((size_t)rows * half, 0);
+    auto q30 = [](double v) -> int64_t {
+        double s = v * (double)(1LL << 30);
+        if (s >= -9223372036854775808.0 && s < 9223372036854775808.0) return (int64_t)s;
+        return INT64_MIN;
+    };
+    for (int t = 0; t < rows; t++)
+        for (int i = 0; i < half; i++) {
+            double theta = std::pow((double)base, -2.0 * i / hd);
+            double angle = t * theta;
+            cs[(size_t)t * half + i] = q30(std::cos(angle));
+            sn[(size_t)t * half + i] = q30(std::sin(angle));
+        }
+}
+
+}  // namespace
+
+struct slx_model {
+    slx_ctx* ctx = nullptr;
+    int kind = 0, scale_bits = 30;
+    int embd = 0, heads = 0, kv_heads = 0, head_dim = 0, q_dim = 0, kv_dim = 0, ff = 0, layers = 0;
+    int vocab = 0, unk = 0, eos = 0, sliding = 0, global_interval = 0, rope_rows = 0;
+    float rope_base = 10000.0f, rope_base_global = 10000.0f;
+    std::vector<void*> allocs;
+    WDesc tok;
+    int64_t *tt = nullptr, *enw = nullptr, *enb = nullptr, *out_norm = nullptr;
+    struct Layer {
+        WDesc qkv, o, gate, up, down, q, k, v;
+        GemmPlan p_qkv, p_o, p_gate, p_up, p_down, p_q, p_k, p_v;
+        int64_t *anw = nullptr, *anb = nullptr, *lnw = nullptr, *lnb = nullptr;
+        int64_t *attn_norm = nullptr, *qn = nullptr, *kn = nullptr, *post_attn = nullptr, *ffn_norm = nullptr,
+                *post_ffw = nullptr;
+    };
+    std::vector<Layer> L;
+    int64_t *cos_l = nullptr, *sin_l = nullptr, *cos_g = nullptr, *sin_g = nullptr;
+    std::map<std::string, DevBuf> ws;
+    GemmWorkspace gws;
+
+    ~slx_model() {
+        for (auto& kv : ws) cudaFree(kv.second.p);
+        for (void* p : allocs) cudaFree(p);
+        gemm_workspace_free(gws);
+    }
+
+    template <class T>
+    T* buf(const char* name, size_t count) {
+        DevBuf& b = ws[name];
+        size_t need = count * sizeof(T);
+        if (need > b.bytes) {
+            if (b.p) cudaFree(b.p);
+            b.p = nullptr;
+            b.bytes = 0;
+            if (cudaMalloc(&b.p, need) != cudaSuccess) return nullptr;
+            b.bytes = need;
+        }
+        return (T*)b.p;
+    }
+};
+
+namespace {
+
+struct Loader {
+    slx_ctx* ctx;
+    slx_model* m;
+    GgufFile& g;
+
+    int upload(const void* src, size_t bytes, void** dst) {
+        CK(cudaMalloc(dst, bytes ? bytes : 1));
+        m->allocs.push_back(*dst);
+        if (bytes) CK(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
+        return SLX_OK;
+    }
+
+    // A tensor as a weight descriptor; natively decoded dtypes stay packed, the rest are
+    // dequantized once on the device to F32 (the float the reference itself would produce).
+    int weight(const std::string& name, int64_t K, int64_t N, int mode, WDesc& w, bool need_shape = true) {
+        const GgufTensor* t = g.tensor(name);
+        if (!t) return set_err(ctx, SLX_ENOTFOUND, "Tensor '%s' not found in GGUF file", name.c_str());
+        std::vector<uint8_t> raw;
+        std::string err;
+        int st = g.read_raw(*t, raw, err);
+        if (st) return set_err(ctx, st, "%s", err.c_str());
+        if (need_shape && t->elements < K * N)
+            return set_err(ctx, SLX_ERANGE, "tensor '%s' has %lld elements, the forward indexes %lld", name.c_str(),
+                           (long long)t->elements, (long long)(K * N));
+        void* d = nullptr;
+        if ((st = upload(raw.data(), raw.size(), &d))) return st;
+        w = WDesc();
+        w.K = K;
+        w.N = N;
+        w.elements = t->elements;
+        w.mode = mode;
+        w.scale = std::ldexp(1.0, m->scale_bits);
+        switch (t->dtype) {
+            case GG_F32: case GG_F16: case GG_BF16: case GG_Q8_0: case GG_Q4_0:
+                w.dtype = (int)t->dtype;
+                w.data = (const uint8_t*)d;
+                w.nblocks = t->elements / 32;
+                return SLX_OK;
+            default: {
+                float* f = nullptr;
+                CK(cudaMalloc(&f, sizeof(float) * std::max<int64_t>(t->elements, 1)));
+                m->allocs.push_back(f);
+                CK(cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), ctx->stream));
+                dequant_f32((int)t->dtype, (const uint8_t*)d, t->elements, f, ctx->d_flag, ctx->stream);
+                int flag = 0;
+                CK(cudaMemcpyAsync(&flag, ctx->d_flag, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+                CK(cudaStreamSynchronize(ctx->stream));
+                if (flag) return set_err(ctx, SLX_ERANGE, "MXFP4 nibble 15 in '%s' (index outside the 15-entry table)", name.c_str());
+                w.dtype = GG_F32;
+                w.data = (const uint8_t*)f;
+                w.nblocks = 0;
+                return SLX_OK;
+            }
+        }
+    }
+
+    // A vector tensor's first n elements as Q30 long (IntegerMatMul.QuantizeFromFloat).
+    int vec_q30(const std::string& name, int64_t n, int64_t** out) {
+        WDesc w;
+        int st = weight(name, n, 1, 0, w);
+        if (st) return st;
+        CK(cudaMalloc((void**)out, sizeof(int64_t) * std::max<int64_t>(n, 1)));
+        m->allocs.push_back(*out);
+        weight_to_q30(w, n, *out, ctx->stream);
+        return SLX_OK;
+    }
+
+    int ones(int64_t n, int64_t** out) {  // MakeOnesWeight (IntegerCausalSource.Loading.cs:227-233)
+        std::vector<int64_t> h((size_t)n, 1LL << m->scale_bits);
+        return upload(h.data(), h.size() * sizeof(int64_t), (void**)out);
+    }
+
+    int vec_or_ones(const std::string& name, int64_t n, int64_t** out) {
+        return g.tensor(name) ? vec_q30(name, n, out) : ones(n, out);
+    }
+
+    int rope(int rows, int hd, float base, int64_t** cs, int64_t** sn) {
+        std::vector<int64_t> c, s;
+        rope_table(rows, hd, base, c, s);
+        int st = upload(c.data(), c.size() * 8, (void**)cs);
+        if (st) return st;
+        return upload(s.data(), s.size() * 8, (void**)sn);
+    }
+};
+
+int lower_eq(const std::string& a, const char* b) {
+    std::string x = a;
+    std::transform(x.begin(), x.end(), x.begin(), ::tolower);
+    return x == b;
+}
+
+// IntegerTransformerSource.LoadFromReader (Gguf/IntegerTransformerSource.Loading.cs:72-151)
+int load_encoder(slx_ctx* ctx, slx_model* m, GgufFile& g) {
+    if (!lower_eq(g.arch, "nomic-bert") && !lower_eq(g.arch, "bert"))
+        return set_err(ctx, SLX_EUNSUPPORTED, "Architecture '%s' is not supported. Only 'nomic-bert' and 'bert' are implemented.", g.arch.c_str());
+    m->embd = g.embd; m->heads = g.heads; m->kv_heads = g.heads; m->layers = g.layers; m->ff = g.ff;
+    if (m->embd <= 0 || m->heads <= 0 || m->embd % m->heads) return set_err(ctx, SLX_EINVAL, "bad encoder dimensions");
+    m->head_dim = m->embd / m->heads; m->q_dim = m->embd; m->kv_dim = m->embd;
+    m->rope_base = g.get_float(g.arch + ".rope.freq_base", 10000.0f);
+    Loader ld{ctx, m, g};
+    int d = m->embd, F = m->ff, st;
+    const GgufTensor* te = g.tensor("token_embd.weight");
+    if (!te) return set_err(ctx, SLX_ENOTFOUND, "Tensor 'token_embd.weight' not found in GGUF file");
+    if ((st = ld.weight("token_embd.weight", d, te->elements / d, 0, m->tok))) return st;
+    if ((st = ld.vec_q30("token_types.weight", d, &m->tt))) return st;
+    if ((st = ld.vec_q30("token_embd_norm.weight", d, &m->enw))) return st;
+    if ((st = ld.vec_q30("token_embd_norm.bias", d, &m->enb))) return st;
+    m->L.resize(m->layers);
+    for (int i = 0; i < m->layers; i++) {
+        std::string p = "blk." + std::to_string(i);
+        auto& l = m->L[i];
+        if ((st = ld.weight(p + ".attn_qkv.weight", d, 3 * d, 0, l.qkv))) return st;
+        if ((st = ld.weight(p + ".attn_output.weight", d, d, 0, l.o))) return st;
+        if ((st = ld.vec_q30(p + ".attn_output_norm.weight", d, &l.anw))) return st;
+        if ((st = ld.vec_q30(p + ".attn_output_norm.bias", d, &l.anb))) return st;
+        if ((st = ld.weight(p + ".ffn_up.weight", d, F, 0, l.up))) return st;
+        if ((st = ld.weight(p + ".ffn_gate.weight", d, F, 0, l.gate))) return st;
+        if ((st = ld.weight(p + ".ffn_down.weight", F, d, 0, l.down))) return st;
+        if ((st = ld.vec_q30(p + ".layer_output_norm.weight", d, &l.lnw))) return st;
+        if ((st = ld.vec_q30(p + ".layer_output_norm.bias", d, &l.lnb))) return st;
+    }
+    // WordPieceTokenizer.FromGguf (Gguf/WordPieceTokenizer.cs:23-30) rejects an empty vocabulary.
+    if (g.n_tokens == 0) return set_err(ctx, SLX_EINVAL, "GGUF file contains no tokenizer vocabulary");
+    m->unk = g.unk; m->eos = g.eos; m->vocab = g.n_tokens;
+    m->rope_rows = 512;  // s_ropeMaxSeqLen (IntegerTransformerSource.cs:27)
+    return ld.rope(m->rope_rows, m->head_dim, m->rope_base, &m->cos_g, &m->sin_g);
+}
+
+// IntegerCausalSource.LoadFromReader (Gguf/IntegerCausalSource.Loading.cs:74-195); with
+// gemma_encoder, IntegerGemmaSource.LoadFromReader (Gguf/IntegerGemmaSource.Loading.cs:80-157).
+int load_causal(slx_ctx* ctx, slx_model* m, GgufFile& g, bool gemma_encoder) {
+    std::string a = g.arch, al = a;
+    std::transform(al.begin(), al.end(), al.begin(), ::tolower);
+    if (al.rfind("gemma", 0) != 0) return set_err(ctx, SLX_EUNSUPPORTED, "Architecture '%s' is not supported.", a.c_str());
+    m->embd = g.embd; m->heads = g.heads; m->layers = g.layers; m->ff = g.ff;
+    if (m->embd <= 0 || m->heads <= 0) return set_err(ctx, SLX_EINVAL, "bad model dimensions");
+    m->kv_heads = g.get_int_i32(a + ".attention.head_count_kv", m->heads);
+    m->head_dim = g.get_int_i32(a + ".attention.key_length", m->embd / m->heads);
+    m->rope_base = g.get_float(a + ".rope.freq_base", 10000.0f);
+    m->vocab = g.n_tokens;
+    if (!gemma_encoder) {
+        m->sliding = g.get_int_i32(a + ".attention.sliding_window", 0);
+        m->global_interval = m->sliding > 0 ? 6 : 0;
+        m->rope_base_global = m->sliding > 0 ? 1000000.0f : m->rope_base;
+    } else {
+        m->rope_base_global = m->rope_base;
+    }
+    if (m->kv_heads <= 0 || m->heads % m->kv_heads || m->head_dim <= 0 || m->head_dim % 2)
+        return set_err(ctx, SLX_EINVAL, "bad attention dimensions");
+    m->q_dim = m->heads * m->head_dim;
+    m->kv_dim = m->kv_heads * m->head_dim;
+    Loader ld{ctx, m, g};
+    int d = m->embd, F = m->ff, hd = m->head_dim, st;
+    const GgufTensor* te = g.tensor("token_embd.weight");
+    if (!te) return set_err(ctx, SLX_ENOTFOUND, "Tensor 'token_embd.weight' not found in GGUF file");
+    if ((st = ld.weight("token_embd.weight", d, te->elements / d, gemma_encoder ? 0 : 1, m->tok))) return st;
+    if ((st = ld.vec_q30("output_norm.weight", d, &m->out_norm))) return st;
+    m->L.resize(m->layers);
+    for (int i = 0; i < m->layers; i++) {
+        std::string p = "blk." + std::to_string(i);
+        auto& l = m->L[i];
+        if ((st = ld.vec_q30(p + ".attn_norm.weight", d, &l.attn_norm))) return st;
+        if ((st = ld.weight(p + ".attn_q.weight", d, m->q_dim, 1, l.q))) return st;
+        if ((st = ld.weight(p + ".attn_k.weight", d, m->kv_dim, 1, l.k))) return st;
+        if ((st = ld.weight(p + ".attn_v.weight", d, m->kv_dim, 1, l.v))) return st;
+        if (gemma_encoder) {
+            if ((st = ld.vec_q30(p + ".attn_q_norm.weight", hd, &l.qn))) return st;
+            if ((st = ld.vec_q30(p + ".attn_k_norm.weight", hd, &l.kn))) return st;
+        } else {
+            if ((st = ld.vec_or_ones(p + ".attn_q_norm.weight", hd, &l.qn))) return st;
+            if ((st = ld.vec_or_ones(p + ".attn_k_norm.weight", hd, &l.kn))) return st;
+        }
+        if ((st = ld.weight(p + ".attn_output.weight", m->q_dim, d, 1, l.o))) return st;
+        if (gemma_encoder) {
+            if ((st = ld.vec_q30(p + ".post_attention_norm.weight", d, &l.post_attn))) return st;
+        } else if ((st = ld.vec_or_ones(p + ".post_attention_norm.weight", d, &l.post_attn))) {
+            return st;
+        }
+        if ((st = ld.vec_q30(p + ".ffn_norm.weight", d, &l.ffn_norm))) return st;
+        if ((st = ld.weight(p + ".ffn_gate.weight", d, F, 1, l.gate))) return st;
+        if ((st = ld.weight(p + ".ffn_up.weight", d, F, 1, l.up))) return st;
+        if ((st = ld.weight(p + ".ffn_down.weight", F, d, 1, l.down))) return st;
+        if (gemma_encoder) {
+            if ((st = ld.vec_q30(p + ".post_ffw_norm.weight", d, &l.post_ffw))) return st;
+        } else if ((st = ld.vec_or_ones(p + ".post_ffw_norm.weight", d, &l.post_ffw))) {
+            return st;
+        }
+    }
+    m->unk = g.unk; m->eos = g.eos;
+    m->rope_rows = 2048;  // RopeMaxSeqLen (IntegerCausalSource.cs:38, IntegerGemmaSource.cs:30)
+    if ((st = ld.rope(m->rope_rows, hd, m->rope_base, &m->cos_l, &m->sin_l))) return st;
+    return ld.rope(m->rope_rows, hd, m->rope_base_global, &m->cos_g, &m->sin_g);
+}
+
+int prepare_gemms(slx_ctx* ctx, slx_model* m) {
+    for (auto& l : m->L) {
+        WDesc* ws[8] = {&l.qkv, &l.o, &l.gate, &l.up, &l.down, &l.q, &l.k, &l.v};
+        GemmPlan* ps[8] = {&l.p_qkv, &l.p_o, &l.p_gate, &l.p_up, &l.p_down, &l.p_q, &l.p_k, &l.p_v};
+        for (int i = 0; i < 8; i++) {
+            if (!ws[i]->data) continue;
+            int st = gemm_prepare(*ws[i], *ps[i], ctx->stream, ctx->err);
+            if (st) return st;
+            if (ps[i]->limb_bytes) m->allocs.push_back(ps[i]->limbs);
+        }
+    }
+    return SLX_OK;
+}
+
+// One projection: c = (a . w^T) >> shift (+ r).
+inline void project(slx_model* m, const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPlan& p, int64_t* c,
+                    int64_t ldc, const int64_t* r, int64_t ldr, cudaStream_t st) {
+    double macs = (double)M * (double)w.N * (double)w.K;
+    run_k(m->ctx, KC_GEMM, macs, 0, st, [&] { return gemm_run(a, lda, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st); });
+}
+#define RUN(cls, macs, bytes, call) run_k(ctx, cls, macs, bytes, st, [&] { return call; })
+
+// Encoder forward to the last block's output, x[B*T][d] (layer limit for tracing).
+int encoder_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, int64_t*& x_out, cudaStream_t st) {
+    slx_ctx* ctx = m->ctx;
+    if (T > m->rope_rows) return set_err(ctx, SLX_ERANGE, "sequence length %d exceeds the RoPE table (%d rows)", T, m->rope_rows);
+    const int d = m->embd, F = m->ff, M = B * T, hd = m->head_dim;
+    int64_t* x = m->buf<int64_t>("x", (size_t)M * d);
+    int64_t* qkv = m->buf<int64_t>("qkv", (size_t)M * 3 * d);
+    int64_t* att = m->buf<int64_t>("att", (size_t)M * d);
+    int64_t* h = m->buf<int64_t>("h", (size_t)M * d);
+    int64_t* gate = m->buf<int64_t>("gate", (size_t)M * F);
+    int64_t* up = m->buf<int64_t>("up", (size_t)M * F);
+    if (!x || !qkv || !att || !h || !gate || !up) return set_err(ctx, SLX_EOOM, "workspace allocation failed (M=%d)", M);
+    RUN(KC_EMBED, 0, 0, embed_encoder(ids, B, T, m->tok, m->tt, m->unk, x, ctx->d_flag, st));
+    RUN(KC_NORM, 0, 0, layernorm_rows(x, d, M, d, m->enw, m->enb, st));
+    const int sshift = 2 * m->scale_bits - 30;
+    const int64_t sq = std::max<int64_t>(1, isqrt64_host(hd));
+    int nl = n_layers < 0 ? m->layers : std::min(n_layers, m->layers);
+    for (int i = 0; i < nl; i++) {
+        auto& l = m->L[i];
+        project(m, x, d, M, l.qkv, l.p_qkv, qkv, 3 * d, nullptr, 0, st);
+        RUN(KC_ROPE, 0, 0, rope_rows(qkv, 3 * d, B, T, m->heads, hd, m->cos_g, m->sin_g, st));
+        RUN(KC_ROPE, 0, 0, rope_rows(qkv + d, 3 * d, B, T, m->heads, hd, m->cos_g, m->sin_g, st));
+        RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0, attention(qkv, 3 * d, qkv + d, 3 * d, qkv + 2 * d, 3 * d, att, d, B, T, m->heads, m->heads, hd, sshift, sq, 0, 0, st));
+        project(m, att, d, M, l.o, l.p_o, h, d, x, d, st);  // O-projection + residual (AddInPlace)
+        RUN(KC_NORM, 0, 0, layernorm_rows(h, d, M, d, l.anw, l.anb, st));
+        project(m, h, d, M, l.gate, l.p_gate, gate, F, nullptr, 0, st);
+        project(m, h, d, M, l.up, l.p_up, up, F, nullptr, 0, st);
+        RUN(KC_FFN_GATE, 0, 0, silu_gate(gate, F, up, F, M, F, st));
+        project(m, up, F, M, l.down, l.p_down, x, d, h, d, st);  // down-projection + residual
+        RUN(KC_NORM, 0, 0, layernorm_rows(x, d, M, d, l.lnw, l.lnb, st));
+    }
+    x_out = x;
+    return SLX_OK;
+}
+
+// Causal / Gemma-encoder forward to the last block's output x[B*T][d].
+int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, int64_t*& x_out, cudaStream_t st) {
+    slx_ctx* ctx = m->ctx;
+    if (T > m->rope_rows) return set_err(ctx, SLX_ERANGE, "sequence length %d exceeds the RoPE table (%d rows)", T, m->rope_rows);
+    const int d = m->embd, F = m->ff, M = B * T, hd = m->head_dim, qd = m->q_dim, kvd = m->kv_dim;
+    int64_t* x = m->buf<int64_t>("x", (size_t)M * d);
+    int64_t* xn = m->buf<int64_t>("xn", (size_t)M * d);
+    int64_t* p = m->buf<int64_t>("p", (size_t)M * d);
+    int64_t* q = m->buf<int64_t>("q", (size_t)M * qd);
+    int64_t* k = m->buf<int64_t>("k", (size_t)M * kvd);
+    int64_t* v = m->buf<int64_t>("v", (size_t)M * kvd);
+    int64_t* att = m->buf<int64_t>("att", (size_t)M * qd);
+    int64_t* gate = m->buf<int64_t>("gate", (size_t)M * F);
+    int64_t* up = m->buf<int64_t>("up", (size_t)M * F);
+    if (!x || !xn || !p || !q || !k || !v || !att || !gate || !up)
+        return set_err(ctx, SLX_EOOM, "workspace allocation failed (M=%d)", M);
+    const bool causal = m->kind == SLX_MODEL_CAUSAL;
+    RUN(KC_EMBED, 0, 0, embed_scaled(ids, B, T, m->tok, m->unk, isqrt64_host(d), x, ctx->d_flag, st));
+    const int sshift = 2 * m->scale_bits - 30;
+    const int64_t sq = std::max<int64_t>(1, isqrt64_host(hd));
+    int nl = n_layers < 0 ? m->layers : std::min(n_layers, m->layers);
+    for (int i = 0; i < nl; i++) {
+        auto& l = m->L[i];
+        bool global = !causal || m->global_interval <= 0 || ((i + 1) % m->global_interval) == 0;  // IsGlobalLayer
+        cudaMemcpyAsync(xn, x, sizeof(int64_t) * M * d, cudaMemcpyDeviceToDevice, st);
+        RUN(KC_NORM, 0, 0, rmsnorm_rows(xn, d, M, 1, d, l.attn_norm, st));
+        project(m, xn, d, M, l.q, l.p_q, q, qd, nullptr, 0, st);
+        project(m, xn, d, M, l.k, l.p_k, k, kvd, nullptr, 0, st);
+        project(m, xn, d, M, l.v, l.p_v, v, kvd, nullptr, 0, st);
+        RUN(KC_NORM, 0, 0, rmsnorm_rows(q, qd, M * m->heads, m->heads, hd, l.qn, st));
+        RUN(KC_NORM, 0, 0, rmsnorm_rows(k, kvd, M * m->kv_heads, m->kv_heads, hd, l.kn, st));
+        const int64_t* cs = global ? m->cos_g : m->cos_l;
+        const int64_t* sn = global ? m->sin_g : m->sin_l;
+        RUN(KC_ROPE, 0, 0, rope_rows(q, qd, B, T, m->heads, hd, cs, sn, st));
+        RUN(KC_ROPE, 0, 0, rope_rows(k, kvd, B, T, m->kv_heads, hd, cs, sn, st));
+        int mode = !causal ? 0 : ((global || m->sliding <= 0) ? 1 : 2);
+        RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0, attention(q, qd, k, kvd, v, kvd, att, qd, B, T, m->heads, m->kv_heads, hd, sshift, sq, mode, m->sliding, st));
+        project(m, att, qd, M, l.o, l.p_o, p, d, nullptr, 0, st);
+        RUN(KC_NORM, 0, 0, rmsnorm_rows(p, d, M, 1, d, l.post_attn, st));
+        RUN(KC_ADD, 0, 0, add_rows(p, d, x, d, M, d, st));  // projected += residual; p is the FFN residual
+        cudaMemcpyAsync(xn, p, sizeof(int64_t) * M * d, cudaMemcpyDeviceToDevice, st);
+        RUN(KC_NORM, 0, 0, rmsnorm_rows(xn, d, M, 1, d, l.ffn_norm, st));
+        project(m, xn, d, M, l.gate, l.p_gate, gate, F, nullptr, 0, st);
+        project(m, xn, d, M, l.up, l.p_up, up, F, nullptr, 0, st);
+        RUN(KC_FFN_GATE, 0, 0, silu_gate(gate, F, up, F, M, F, st));
+        project(m, up, F, M, l.down, l.p_down, x, d, nullptr, 0, st);
+        RUN(KC_NORM, 0, 0, rmsnorm_rows(x, d, M, 1, d, l.post_ffw, st));
+        RUN(KC_ADD, 0, 0, add_rows(x, d, p, d, M, d, st));
+    }
+    x_out = x;
+    return SLX_OK;
+}
+
+int check_flag(slx_ctx* ctx, cudaStream_t st) {
+    int flag = 0;
+    CK(cudaMemcpyAsync(&flag, ctx->d_flag, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (flag & KERR_RANGE) return set_err(ctx, SLX_ERANGE, "index out of range (token id and UNK row outside the table)");
+    return SLX_OK;
+}
+
+cudaStream_t pick(slx_ctx* ctx, void* s) { return s ? (cudaStream_t)s : ctx->stream; }
+
+int encode_device(slx_model* m, const int32_t* d_ids, int B, int T, int64_t* d_pooled, cudaStream_t st) {
+    slx_ctx* ctx = m->ctx;
+    if (B < 0 || T < 0) return set_err(ctx, SLX_EINVAL, "bad batch shape B=%d T=%d", B, T);
+    if (B == 0) return SLX_OK;
+    if (T == 0) {  // MeanPool of an empty sequence returns zeros (IntegerTransformerSource.Forward.cs:73)
+        CK(cudaMemsetAsync(d_pooled, 0, sizeof(int64_t) * B * m->embd, st));
+        return SLX_OK;
+    }
+    int64_t* x = nullptr;
+    int rc;
+    if (m->kind == SLX_MODEL_ENCODER) {
+        rc = encoder_hidden(m, d_ids, B, T, -1, x, st);
+        if (rc) return rc;
+    } else {
+        rc = causal_hidden(m, d_ids, B, T, -1, x, st);
+        if (rc) return rc;
+        RUN(KC_NORM, 0, 0, rmsnorm_rows(x, m->embd, B * T, 1, m->embd, m->out_norm, st));  // final RmsNorm (IntegerGemmaSource.cs:77)
+    }
+    RUN(KC_POOL, 0, 0, mean_pool(x, m->embd, B, T, m->embd, d_pooled, st));
+    CK(cudaGetLastError());
+    return SLX_OK;
+}
+
+// Last position after the output norm for each of B sequences: last[B][d].
+int causal_last(slx_model* m, const int32_t* d_ids, int B, int T, int64_t* d_last, cudaStream_t st) {
+    slx_ctx* ctx = m->ctx;
+    int64_t* x = nullptr;
+    int rc = causal_hidden(m, d_ids, B, T, -1, x, st);
+    if (rc) return rc;
+    RUN(KC_POOL, 0, 0, gather_last_rows(x, m->embd, B, T, m->embd, d_last, st));
+    RUN(KC_NORM, 0, 0, rmsnorm_rows(d_last, m->embd, B, 1, m->embd, m->out_norm, st));
+    CK(cudaGetLastError());
+    return SLX_OK;
+}
+
+// ForwardFloat + L2Normalize on the host (IntegerTransformerSource.cs:52-62, .Forward.cs:89-99):
+// sequential fp32 without contraction (the host compiler runs with -ffp-contract=off).
+void to_float_l2(const int64_t* v, int d, int sb, float* out) {
+    double scale = std::pow(2.0, -sb);
+    for (int j = 0; j < d; j++) out[j] = (float)((double)v[j] * scale);
+    float norm = 0.0f;
+    for (int j = 0; j < d; j++) norm += out[j] * out[j];
+    norm = std::sqrt(norm);
+    if (norm < 1e-10f) return;
+    float inv = 1.0f / norm;
+    for (int j = 0; j < d; j++) out[j] *= inv;
+}
+
+}  // namespace
+
+// ==============================================================================================
+// extern "C" ABI
+// ==============================================================================================
+extern "C" {
+
+const char* slx_version(void) { return "slx 0.1 (sm_100a)"; }
+
+slx_status slx_init(int device, slx_ctx** out) {
+    if (!out) return SLX_EINVAL;
+    *out = nullptr;
+    std::unique_ptr<slx_ctx> c(new slx_ctx());
+    slx_ctx* ctx = c.get();
+    c->device = device;
+    CK(cudaSetDevice(device));
+    CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    CK(cudaMalloc(&c->d_flag, sizeof(int)));
+    CK(cudaMemset(c->d_flag, 0, sizeof(int)));
+    *out = c.release();
+    return SLX_OK;
+}
+
+slx_status slx_destroy(slx_ctx* ctx) {
+    if (!ctx) return SLX_EINVAL;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->d_flag);
+    for (auto& r : ctx->records) { cudaEventDestroy(r.a); cudaEventDestroy(r.b); }
+    for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return SLX_OK;
+}
+
+const char* slx_last_error(slx_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+slx_status slx_model_load_gguf(slx_ctx* ctx, const char* path, int kind, int scale_bits, slx_model** out) {
+    if (!ctx || !path || !out) return set_err(ctx, SLX_EINVAL, "null argument");
+    *out = nullptr;
+    if (scale_bits < 1 || scale_bits > 62) return set_err(ctx, SLX_EINVAL, "scale_bits %d out of range", scale_bits);
+    CK(cudaSetDevice(ctx->device));
+    GgufFile g;
+    std::string err;
+    int st = g.open(path, err);
+    if (st) return set_err(ctx, st, "%s", err.c_str());
+    std::unique_ptr<slx_model> m(new slx_model());
+    m->ctx = ctx;
+    m->kind = kind;
+    m->scale_bits = scale_bits;
+    if (kind == SLX_MODEL_ENCODER)
+        st = load_encoder(ctx, m.get(), g);
+    else if (kind == SLX_MODEL_CAUSAL || kind == SLX_MODEL_GEMMA_ENCODER)
+        st = load_causal(ctx, m.get(), g, kind == SLX_MODEL_GEMMA_ENCODER);
+    else
+        return set_err(ctx, SLX_EINVAL, "unknown model kind %d", kind);
+    if (st) return st;
+    if ((st = prepare_gemms(ctx, m.get()))) return st;
+    CK(cudaStreamSynchronize(ctx->stream));
+    CK(cudaGetLastError());
+    *out = m.release();
+    return SLX_OK;
+}
+
+slx_status slx_model_free(slx_model* m) {
+    if (!m) return SLX_EINVAL;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    delete m;
+    return SLX_OK;
+}
+
+slx_status slx_model_info(slx_model* m, int32_t* info, int n) {
+    if (!m || !info) return SLX_EINVAL;
+    int32_t v[12] = {m->kind, m->embd, m->heads, m->kv_heads, m->head_dim, m->ff, m->layers, m->vocab, m->eos, m->unk,
+                     m->q_dim, m->kv_dim};
+    for (int i = 0; i < n && i < 12; i++) info[i] = v[i];
+    return SLX_OK;
+}
+
+slx_status slx_encode_device(slx_model* m, const int32_t* d_ids, int B, int T, int64_t* d_pooled, void* stream) {
+    if (!m || (B > 0 && T > 0 && (!d_ids || !d_pooled))) return m ? set_err(m->ctx, SLX_EINVAL, "null argument") : SLX_EINVAL;
+    if (m->kind == SLX_MODEL_CAUSAL) return set_err(m->ctx, SLX_EINVAL, "slx_encode on a causal model");
+    return encode_device(m, d_ids, B, T, d_pooled, pick(m->ctx, stream));
+}
+
+slx_status slx_encode(slx_model* m, const int32_t* ids, int B, int T, int64_t* pooled, float* l2) {
+    if (!m) return SLX_EINVAL;
+    slx_ctx* ctx = m->ctx;
+    if (B < 0 || T < 0 || (B > 0 && T > 0 && !ids) || (B > 0 && !pooled)) return set_err(ctx, SLX_EINVAL, "bad arguments");
+    if (m->kind == SLX_MODEL_CAUSAL) return set_err(ctx, SLX_EINVAL, "slx_encode on a causal model");
+    if (B == 0) return SLX_OK;
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    int32_t* d_ids = m->buf<int32_t>("ids", (size_t)std::max(1, B * T));
+    int64_t* d_pooled = m->buf<int64_t>("pooled", (size_t)B * m->embd);
+    if (!d_ids || !d_pooled) return set_err(ctx, SLX_EOOM, "workspace allocation failed");
+    CK(cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), st));
+    if (B * T > 0) CK(cudaMemcpyAsync(d_ids, ids, sizeof(int32_t) * B * T, cudaMemcpyHostToDevice, st));
+    int rc = encode_device(m, d_ids, B, T, d_pooled, st);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(pooled, d_pooled, sizeof(int64_t) * B * m->embd, cudaMemcpyDeviceToHost, st));
+    if ((rc = check_flag(ctx, st))) return rc;
+    if (l2)
+        for (int b = 0; b < B; b++) to_float_l2(pooled + (int64_t)b * m->embd, m->embd, m->scale_bits, l2 + (int64_t)b * m->embd);
+    return SLX_OK;
+}
+
+slx_status slx_trace_hidden(slx_model* m, const int32_t* ids, int T, int n_layers, int final_norm, int64_t* x_q30) {
+    if (!m || !ids || !x_q30 || T <= 0) return m ? set_err(m->ctx, SLX_EINVAL, "bad arguments") : SLX_EINVAL;
+    slx_ctx* ctx = m->ctx;
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    int32_t* d_ids = m->buf<int32_t>("ids", (size_t)T);
+    if (!d_ids) return set_err(ctx, SLX_EOOM, "workspace allocation failed");
+    CK(cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), st));
+    CK(cudaMemcpyAsync(d_ids, ids, sizeof(int32_t) * T, cudaMemcpyHostToDevice, st));
+    int64_t* x = nullptr;
+    int rc = m->kind == SLX_MODEL_ENCODER ? encoder_hidden(m, d_ids, 1, T, n_layers, x, st)
+                                          : causal_hidden(m, d_ids, 1, T, n_layers, x, st);
+    if (rc) return rc;
+    if (final_norm && m->kind != SLX_MODEL_ENCODER) rmsnorm_rows(x, m->embd, T, 1, m->embd, m->out_norm, st);
+    CK(cudaMemcpyAsync(x_q30, x, sizeof(int64_t) * T * m->embd, cudaMemcpyDeviceToHost, st));
+    return check_flag(ctx, st);
+}
+
+slx_status slx_causal_forward_last(slx_model* m, const int32_t* ids, int T, int64_t* last) {
+    if (!m || !ids || !last || T <= 0) return m ? set_err(m->ctx, SLX_EINVAL, "bad arguments") : SLX_EINVAL;
+    slx_ctx* ctx = m->ctx;
+    if (m->kind != SLX_MODEL_CAUSAL) return set_err(ctx, SLX_EINVAL, "not a causal model");
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    int32_t* d_ids = m->buf<int32_t>("ids", (size_t)T);
+    int64_t* d_last = m->buf<int64_t>("last", (size_t)m->embd);
+    if (!d_ids || !d_last) return set_err(ctx, SLX_EOOM, "workspace allocation failed");
+    CK(cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), st));
+    CK(cudaMemcpyAsync(d_ids, ids, sizeof(int32_t) * T, cudaMemcpyHostToDevice, st));
+    int rc = causal_last(m, d_ids, 1, T, d_last, st);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(last, d_last, sizeof(int64_t) * m->embd, cudaMemcpyDeviceToHost, st));
+    return check_flag(ctx, st);
+}
+
+slx_status slx_causal_next_token(slx_model* m, const int32_t* ids, int B, int T, int32_t* next) {
+    if (!m || !ids || !next || B <= 0 || T <= 0) return m ? set_err(m->ctx, SLX_EINVAL, "bad arguments") : SLX_EINVAL;
+    slx_ctx* ctx = m->ctx;
+    if (m->kind != SLX_MODEL_CAUSAL) return set_err(ctx, SLX_EINVAL, "not a causal model");
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    int32_t* d_ids = m->buf<int32_t>("ids", (size_t)B * T);
+    int64_t* d_last = m->buf<int64_t>("last", (size_t)B * m->embd);
+    unsigned long long* keys = m->buf<unsigned long long>("keys", (size_t)B);
+    int32_t* d_next = m->buf<int32_t>("next", (size_t)B);
+    if (!d_ids || !d_last || !keys || !d_next) return set_err(ctx, SLX_EOOM, "workspace allocation failed");
+    CK(cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), st));
+    CK(cudaMemcpyAsync(d_ids, ids, sizeof(int32_t) * B * T, cudaMemcpyHostToDevice, st));
+    int rc = causal_last(m, d_ids, B, T, d_last, st);
+    if (rc) return rc;
+    RUN(KC_ARGMAX, 0, 0, argmax_vocab(d_last, B, m->embd, m->tok, m->vocab, m->scale_bits, keys, d_next, st));
+    CK(cudaMemcpyAsync(next, d_next, sizeof(int32_t) * B, cudaMemcpyDeviceToHost, st));
+    return check_flag(ctx, st);
+}
+
+slx_status slx_causal_generate(slx_model* m, const int32_t* ids, int B, int T, int max_new, int32_t* out,
+                               int32_t* n_out) {
+    if (!m || !ids || !out || !n_out || B <= 0 || T <= 0 || max_new < 0)
+        return m ? set_err(m->ctx, SLX_EINVAL, "bad arguments") : SLX_EINVAL;
+    slx_ctx* ctx = m->ctx;
+    if (m->kind != SLX_MODEL_CAUSAL) return set_err(ctx, SLX_EINVAL, "not a causal model");
+    std::vector<int32_t> seq((size_t)B * T);
+    std::memcpy(seq.data(), ids, sizeof(int32_t) * B * T);
+    std::vector<int> done((size_t)B, 0);
+    for (int b = 0; b < B; b++) n_out[b] = 0;
+    std::vector<int32_t> next((size_t)B);
+    int cur = T;
+    for (int step = 0; step < max_new; step++) {
+        int alive = 0;
+        for (int b = 0; b < B; b++) alive += !done[b];
+        if (!alive) break;
+        int rc = slx_causal_next_token(m, seq.data(), B, cur, next.data());
+        if (rc) return rc;
+        std::vector<int32_t> grown((size_t)B * (cur + 1));
+        for (int b = 0; b < B; b++) {
+            std::memcpy(&grown[(size_t)b * (cur + 1)], &seq[(size_t)b * cur], sizeof(int32_t) * cur);
+            int32_t nx = next[b];
+            if (!done[b] && nx == m->eos) done[b] = 1;  // Generate stops before appending EOS
+            if (!done[b]) out[(size_t)b * max_new + n_out[b]++] = nx;
+            grown[(size_t)b * (cur + 1) + cur] = done[b] ? m->eos : nx;
+        }
+        seq.swap(grown);
+        cur++;
+    }
+    return SLX_OK;
+}
+
+slx_status slx_dequantize(slx_ctx* ctx, int dtype, const uint8_t* raw, int64_t nbytes, float* out, int64_t n) {
+    if (!ctx || (n > 0 && (!raw || !out)) || n < 0 || nbytes < 0) return set_err(ctx, SLX_EINVAL, "bad arguments");
+    int64_t need = gguf_decode_bytes((uint32_t)dtype, n);
+    if (need < 0) return set_err(ctx, SLX_EUNSUPPORTED, "Dequantization of dtype %d is not yet implemented", dtype);
+    if (nbytes < need) return set_err(ctx, SLX_EEOF, "Unexpected end of GGUF stream: expected %lld bytes, got %lld", (long long)need, (long long)nbytes);
+    if (n == 0) return SLX_OK;
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    uint8_t* d_raw = nullptr;
+    float* d_out = nullptr;
+    CK(cudaMalloc(&d_raw, std::max<int64_t>(need, 1)));
+    if (cudaMalloc(&d_out, sizeof(float) * n) != cudaSuccess) {
+        cudaFree(d_raw);
+        return set_err(ctx, SLX_EOOM, "device allocation failed");
+    }
+    cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), st);
+    cudaMemcpyAsync(d_raw, raw, need, cudaMemcpyHostToDevice, st);
+    dequant_f32(dtype, d_raw, n, d_out, ctx->d_flag, st);
+    cudaMemcpyAsync(out, d_out, sizeof(float) * n, cudaMemcpyDeviceToHost, st);
+    int rc = check_flag(ctx, st);
+    cudaFree(d_raw);
+    cudaFree(d_out);
+    return rc;
+}
+
+slx_status slx_gguf_read_f32(slx_ctx* ctx, const char* path, const char* tensor, float* out, int64_t n) {
+    if (!ctx || !path || !tensor) return set_err(ctx, SLX_EINVAL, "null argument");
+    GgufFile g;
+    std::string err;
+    int st = g.open(path, err);
+    if (st) return set_err(ctx, st, "%s", err.c_str());
+    const GgufTensor* t = g.tensor(tensor);
+    if (!t) return set_err(ctx, SLX_ENOTFOUND, "Tensor '%s' not found in GGUF file", tensor);
+    if (n != t->elements) return set_err(ctx, SLX_EINVAL, "output holds %lld floats, tensor has %lld", (long long)n, (long long)t->elements);
+    std::vector<uint8_t> raw;
+    if ((st = g.read_raw(*t, raw, err))) return set_err(ctx, st, "%s", err.c_str());
+    return slx_dequantize(ctx, (int)t->dtype, raw.data(), (int64_t)raw.size(), out, n);
+}
+
+slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K, int dtype, const uint8_t* d_w,
+                                 int64_t w_bytes, int N, int half_composite, int scale_bits, int shift, int64_t* d_c,
+                                 void* stream) {
+    if (!ctx || M < 0 || K <= 0 || N <= 0 || !d_w || (M > 0 && (!d_a || !d_c))) return set_err(ctx, SLX_EINVAL, "bad arguments");
+    if (dtype != GG_F32 && dtype != GG_F16 && dtype != GG_BF16 && dtype != GG_Q8_0 && dtype != GG_Q4_0)
+        return set_err(ctx, SLX_EUNSUPPORTED, "matmul weight dtype %d (expand other formats with slx_dequantize)", dtype);
+    int64_t elems = (int64_t)N * K;
+    if (w_bytes < gguf_byte_count((uint32_t)dtype, elems)) return set_err(ctx, SLX_EEOF, "weight buffer too small");
+    WDesc w;
+    w.dtype = dtype; w.data = d_w; w.nblocks = elems / 32; w.elements = elems; w.N = N; w.K = K;
+    w.mode = half_composite ? 1 : 0;
+    w.scale = std::ldexp(1.0, scale_bits);
+    cudaStream_t st = pick(ctx, stream);
+    RUN(KC_GEMM, (double)M * N * K, 0, gemm_exact(d_a, K, M, K, w, d_c, N, shift, nullptr, 0, st));
+    CK(cudaGetLastError());
+    return SLX_OK;
+}
+
+slx_status slx_matmul_q30(slx_ctx* ctx, const int64_t* a, int M, int K, int dtype, const uint8_t* w_raw, int64_t w_bytes,
+                          int N, int half_composite, int scale_bits, int shift, int64_t* c) {
+    if (!ctx || M <= 0 || K <= 0 || N <= 0 || !a || !w_raw || !c) return set_err(ctx, SLX_EINVAL, "bad arguments");
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    int64_t need = gguf_byte_count((uint32_t)dtype, (int64_t)N * K);
+    if (w_bytes < need) return set_err(ctx, SLX_EEOF, "weight buffer too small");
+    int64_t *da = nullptr, *dc = nullptr;
+    uint8_t* dw = nullptr;
+    CK(cudaMalloc(&da, sizeof(int64_t) * M * K));
+    CK(cudaMalloc(&dc, sizeof(int64_t) * M * N));
+    CK(cudaMalloc(&dw, need));
+    cudaMemcpyAsync(da, a, sizeof(int64_t) * M * K, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(dw, w_raw, need, cudaMemcpyHostToDevice, st);
+    int rc = slx_matmul_q30_device(ctx, da, M, K, dtype, dw, need, N, half_composite, scale_bits, shift, dc, st);
+    if (!rc) {
+        cudaMemcpyAsync(c, dc, sizeof(int64_t) * M * N, cudaMemcpyDeviceToHost, st);
+        cudaError_t e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) rc = set_err(ctx, SLX_ECUDA, "%s", cudaGetErrorString(e));
+    }
+    cudaFree(da);
+    cudaFree(dc);
+    cudaFree(dw);
+    return rc;
+}
+
+slx_status slx_profile_begin(slx_ctx* ctx) {
+    if (!ctx) return SLX_EINVAL;
+    for (auto& r : ctx->records) { ctx->event_pool.push_back(r.a); ctx->event_pool.push_back(r.b); }
+    ctx->records.clear();
+    ctx->prof = true;
+    return SLX_OK;
+}
+
+slx_status slx_profile_end(slx_ctx* ctx, slx_kernel_stat* stats, int cap, int* n) {
+    if (!ctx || !n) return SLX_EINVAL;
+    ctx->prof = false;
+    slx_kernel_stat acc[KC_COUNT];
+    std::memset(acc, 0, sizeof acc);
+    for (int c = 0; c < KC_COUNT; c++) snprintf(acc[c].name, sizeof acc[c].name, "%s", kKClassName[c]);
+    for (auto& r : ctx->records) {
+        CK(cudaEventSynchronize(r.b));
+        float ms = 0;
+        CK(cudaEventElapsedTime(&ms, r.a, r.b));
+        acc[r.cls].launches += r.launches;
+        acc[r.cls].ms += ms;
+        acc[r.cls].macs += r.macs;
+        acc[r.cls].bytes += r.bytes;
+        ctx->event_pool.push_back(r.a);
+        ctx->event_pool.push_back(r.b);
+    }
+    ctx->records.clear();
+    int k = 0;
+    for (int c = 0; c < KC_COUNT; c++)
+        if (acc[c].launches && k < cap && stats) stats[k++] = acc[c];
+    *n = k;
+    return SLX_OK;
+}
+
+slx_status slx_launch_count(slx_ctx* ctx, int64_t* launches) {
+    if (!ctx || !launches) return SLX_EINVAL;
+    *launches = ctx->launches;
+    return SLX_OK;
+}
+
+}  // extern "C"
