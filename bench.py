@@ -181,7 +181,10 @@ def run_ours(args) -> None:
     ctx = slx.Context(local)
     model = slx.IntegerTransformerSource.load(path, ctx=ctx)
     lib = ctx._lib
-    stream = torch.cuda.current_stream()
+    # A stream of our own: torch's default stream has handle 0, which the library reads as "use the
+    # context's stream"; events and launches must share one stream.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     rng = np.random.default_rng(1000 + rank)
     ids_host = rng.integers(0, ARCH["vocab"], (W + K, B, SEQ)).astype(np.int32)
     ids_dev = torch.from_numpy(ids_host).cuda()

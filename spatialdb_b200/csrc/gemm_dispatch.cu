@@ -1,23 +1,80 @@
 // gemm_dispatch.cu -- chooses the kernel for each projection (see slx_gemm.h).
+//
+// Tensor-core path (k_gemm_tc.cu) when the weight's Q30 composites fit 4 balanced int8 digits and
+// K < 32768; per call the activations are split into 5 digit planes, and if any activation needs
+// more digits the exact CUDA-core kernel (launched right behind, gated on the same device flag)
+// computes the result instead. Either way the output equals IntegerMatMul.MatMul bit for bit.
+#include <cstdlib>
+
 #include "slx_gemm.h"
+#include "slx_status.h"
 
 namespace slx {
 
+namespace {
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+}  // namespace
+
+bool tc_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("SLX_DISABLE_TC");
+        on = (e && e[0] == '1') ? 0 : 1;
+    }
+    return on == 1;
+}
+
 int gemm_prepare(const WDesc& w, GemmPlan& plan, cudaStream_t st, std::string& err) {
-    (void)w; (void)st; (void)err;
     plan = GemmPlan();
-    return 0;
+    if (!tc_enabled() || w.K >= 32768 || w.N <= 0 || w.K <= 0) return SLX_OK;
+    int maxd = tc::weight_digits(w, st, err);
+    if (maxd < 0) return SLX_ECUDA;
+    if (maxd > 4) return SLX_OK;  // composites too wide for the digit path: exact kernel
+    plan.wlimbs = maxd < 1 ? 1 : maxd;
+    plan.n_pad = round_up(w.N, tc::BN);
+    plan.k_pad = round_up(w.K, tc::BK);
+    plan.limb_bytes = (size_t)plan.wlimbs * plan.n_pad * plan.k_pad;
+    if (cudaMalloc(&plan.limbs, plan.limb_bytes) != cudaSuccess) { err = "device allocation failed"; return SLX_EOOM; }
+    tc::split_w(w, plan.wlimbs, plan.n_pad, plan.k_pad, (int8_t*)plan.limbs, st);
+    if (!tc::encode_planes(plan.tmap_w, plan.limbs, plan.k_pad, plan.n_pad, plan.wlimbs, tc::BN)) {
+        cudaFree(plan.limbs);
+        plan = GemmPlan();
+        return SLX_OK;  // no tensor-map encoder available: exact kernel
+    }
+    plan.use_tc = 1;
+    return SLX_OK;
 }
 
 int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPlan& plan, int64_t* c, int64_t ldc,
-              int shift, const int64_t* r, int64_t ldr, GemmWorkspace& ws, cudaStream_t st) {
-    (void)plan; (void)ws;
-    return gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st);
+             int shift, const int64_t* r, int64_t ldr, GemmWorkspace& ws, cudaStream_t st) {
+    if (M <= 0) return 0;
+    if (!plan.use_tc) return gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st);
+    const int64_t mpad = round_up(M, tc::BM);
+    const size_t need = (size_t)tc::LA * mpad * plan.k_pad + 256;
+    if (need > ws.bytes) {
+        if (ws.p) cudaFree(ws.p);
+        ws.p = nullptr;
+        ws.bytes = 0;
+        if (cudaMalloc(&ws.p, need) != cudaSuccess) return gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st);
+        ws.bytes = need;
+    }
+    int* flag = (int*)ws.p;
+    int8_t* planes = (int8_t*)ws.p + 256;
+    alignas(64) unsigned char tmap_a[128];
+    if (!tc::encode_planes(tmap_a, planes, plan.k_pad, mpad, tc::LA, tc::BM))
+        return gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st);
+    cudaMemsetAsync(flag, 0, sizeof(int), st);
+    tc::split_a(a, lda, M, (int)w.K, mpad, plan.k_pad, planes, flag, st);
+    tc::launch(tmap_a, plan.tmap_w, plan.wlimbs, M, (int)w.N, (int)w.K, mpad, plan.n_pad, plan.k_pad, shift, c, ldc, r,
+               ldr, flag, ws.err, st);
+    gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st, flag);  // runs only if the split overflowed
+    return 3;
 }
 
 void gemm_workspace_free(GemmWorkspace& ws) {
     if (ws.p) cudaFree(ws.p);
-    ws = GemmWorkspace();
+    ws.p = nullptr;
+    ws.bytes = 0;
 }
 
 }  // namespace slx

@@ -21,7 +21,9 @@ constexpr int GBM = 64, GBN = 64, GBK = 32;
 
 __global__ __launch_bounds__(256) void k_gemm_exact(const int64_t* __restrict__ A, int64_t lda, int M, int K,
                                                     WDesc W, int64_t* __restrict__ C, int64_t ldc, int shift,
-                                                    const int64_t* __restrict__ R, int64_t ldr) {
+                                                    const int64_t* __restrict__ R, int64_t ldr,
+                                                    const int* __restrict__ only_if) {
+    if (only_if && *only_if == 0) return;
     __shared__ int64_t As[GBK][GBM + 1];
     __shared__ int64_t Ws[GBK][GBN + 1];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -86,10 +88,10 @@ __global__ void k_weight_q30(WDesc W, int64_t n, int64_t* out) {
 }  // namespace
 
 int gemm_exact(const int64_t* a, int64_t lda, int M, int K, const WDesc& w, int64_t* c, int64_t ldc, int shift,
-                const int64_t* r, int64_t ldr, cudaStream_t st) {
+                const int64_t* r, int64_t ldr, cudaStream_t st, const int* only_if) {
     if (M <= 0 || w.N <= 0) return 0;
     dim3 grid((unsigned)((w.N + GBN - 1) / GBN), (unsigned)((M + GBM - 1) / GBM));
-    k_gemm_exact<<<grid, 256, 0, st>>>(a, lda, M, K, w, c, ldc, shift, r, ldr);
+    k_gemm_exact<<<grid, 256, 0, st>>>(a, lda, M, K, w, c, ldc, shift, r, ldr, only_if);
     return 1;
 }
 

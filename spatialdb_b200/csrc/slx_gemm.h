@@ -17,13 +17,28 @@ struct GemmPlan {
     uint8_t* limbs = nullptr;  // device: limb planes [wlimbs][N_pad][K_pad]
     size_t limb_bytes = 0;
     int64_t n_pad = 0, k_pad = 0;
+    alignas(64) unsigned char tmap_w[128];  // CUtensorMap of the weight digit planes
 };
 
 // Per-model scratch shared by the projections.
 struct GemmWorkspace {
     void* p = nullptr;
     size_t bytes = 0;
+    int* err = nullptr;  // device error word (bounded-wait timeouts)
 };
+
+// Tensor-core kernel launchers (k_gemm_tc.cu).
+namespace tc {
+constexpr int BM = 128, BN = 64, BK = 128, LA = 5;
+// Encodes a TMA map over int8 digit planes [planes][rows][kpad] with a (128 B, box_rows, planes) box.
+bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows);
+int weight_digits(const WDesc& w, cudaStream_t st, std::string& err);      // digits of the widest composite
+void split_w(const WDesc& w, int lw, int64_t npad, int64_t kpad, int8_t* planes, cudaStream_t st);
+void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t kpad, int8_t* planes, int* overflow,
+             cudaStream_t st);
+void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K, int64_t mpad, int64_t npad, int64_t kpad,
+            int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st);
+}  // namespace tc
 
 int gemm_prepare(const WDesc& w, GemmPlan& plan, cudaStream_t st, std::string& err);
 int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPlan& plan, int64_t* c, int64_t ldc,

@@ -20,11 +20,12 @@ struct WDesc {
 };
 
 // Device-side error flags set by kernels instead of trapping (read back by the host).
-enum : int { KERR_NONE = 0, KERR_RANGE = 1 };
+enum : int { KERR_NONE = 0, KERR_RANGE = 1, KERR_TIMEOUT = 2 };
 
 // c[M][N] = lo64((sum_k a[m][k] * w[n][k]) >> shift) (+ r[m][n] if r), exact Int128 accumulation.
+// With only_if, the kernel does nothing unless *only_if is nonzero (device-side gate).
 int gemm_exact(const int64_t* a, int64_t lda, int M, int K, const WDesc& w, int64_t* c, int64_t ldc, int shift,
-                const int64_t* r, int64_t ldr, cudaStream_t st);
+                const int64_t* r, int64_t ldr, cudaStream_t st, const int* only_if = nullptr);
 
 // Q30 composite of elements [0, n) of a weight into out (norm vectors, token-type rows).
 int weight_to_q30(const WDesc& w, int64_t n, int64_t* out, cudaStream_t st);

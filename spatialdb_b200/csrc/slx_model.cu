@@ -482,6 +482,7 @@ int check_flag(slx_ctx* ctx, cudaStream_t st) {
     CK(cudaMemcpyAsync(&flag, ctx->d_flag, sizeof(int), cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
     if (flag & KERR_RANGE) return set_err(ctx, SLX_ERANGE, "index out of range (token id and UNK row outside the table)");
+    if (flag & KERR_TIMEOUT) return set_err(ctx, SLX_ETIMEOUT, "a tensor-core GEMM gave up on a bounded wait");
     return SLX_OK;
 }
 
@@ -592,6 +593,7 @@ slx_status slx_model_load_gguf(slx_ctx* ctx, const char* path, int kind, int sca
     else
         return set_err(ctx, SLX_EINVAL, "unknown model kind %d", kind);
     if (st) return st;
+    m->gws.err = ctx->d_flag;
     if ((st = prepare_gemms(ctx, m.get()))) return st;
     CK(cudaStreamSynchronize(ctx->stream));
     CK(cudaGetLastError());
@@ -782,7 +784,18 @@ slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K,
     w.mode = half_composite ? 1 : 0;
     w.scale = std::ldexp(1.0, scale_bits);
     cudaStream_t st = pick(ctx, stream);
-    RUN(KC_GEMM, (double)M * N * K, 0, gemm_exact(d_a, K, M, K, w, d_c, N, shift, nullptr, 0, st));
+    // One-off plan: the weight's digit planes are built for this call and released with it.
+    GemmPlan plan;
+    std::string err;
+    int rc = gemm_prepare(w, plan, st, err);
+    if (rc) return set_err(ctx, rc, "%s", err.c_str());
+    GemmWorkspace ws;
+    ws.err = ctx->d_flag;
+    RUN(KC_GEMM, (double)M * N * K, 0, gemm_run(d_a, K, M, w, plan, d_c, N, shift, nullptr, 0, ws, st));
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (plan.limbs) cudaFree(plan.limbs);
+    gemm_workspace_free(ws);
+    if (e != cudaSuccess) return set_err(ctx, SLX_ECUDA, "%s", cudaGetErrorString(e));
     CK(cudaGetLastError());
     return SLX_OK;
 }
@@ -799,13 +812,13 @@ slx_status slx_matmul_q30(slx_ctx* ctx, const int64_t* a, int M, int K, int dtyp
     CK(cudaMalloc(&da, sizeof(int64_t) * M * K));
     CK(cudaMalloc(&dc, sizeof(int64_t) * M * N));
     CK(cudaMalloc(&dw, need));
+    cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), st);
     cudaMemcpyAsync(da, a, sizeof(int64_t) * M * K, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(dw, w_raw, need, cudaMemcpyHostToDevice, st);
     int rc = slx_matmul_q30_device(ctx, da, M, K, dtype, dw, need, N, half_composite, scale_bits, shift, dc, st);
     if (!rc) {
         cudaMemcpyAsync(c, dc, sizeof(int64_t) * M * N, cudaMemcpyDeviceToHost, st);
-        cudaError_t e = cudaStreamSynchronize(st);
-        if (e != cudaSuccess) rc = set_err(ctx, SLX_ECUDA, "%s", cudaGetErrorString(e));
+        rc = check_flag(ctx, st);
     }
     cudaFree(da);
     cudaFree(dc);

@@ -1,0 +1,80 @@
+"""Parity of the tensor-core projection GEMM (balanced int8 digits on tcgen05) with the oracle.
+
+Activations are drawn inside the 5-digit range (|a| < 2^38) so the tensor-core path produces the
+result; the overflow cases push one activation outside it, which must route that call to the
+exact CUDA-core kernel with the same bit-exact answer.
+"""
+import numpy as np
+import pytest
+
+import spatialdb_b200 as slx
+from spatialdb_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    return slx.Context(0)
+
+
+def _raw(dtype, rng, n):
+    if dtype == synth.Q8_0:
+        return synth.random_q8_0(rng, n)
+    if dtype == synth.Q4_0:
+        return synth.random_q4_0(rng, n)
+    return synth.encode(dtype, rng.standard_normal(n).astype(np.float32) * 0.05)
+
+
+def _ref(oracle, a, dtype, raw, N, half, shift):
+    M, K = a.shape
+    f = oracle.dequantize(dtype, raw, N * K)
+    if half:
+        return oracle.matmul_half(a, M, K, oracle.float_to_half(f), N, 30, shift).reshape(M, N)
+    return oracle.matmul_long(a, M, K, oracle.quantize_from_float(f), N, shift).reshape(M, N)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 128, 64), (128, 128, 64), (200, 384, 130), (256, 768, 2304), (300, 3072, 768),
+                                   (129, 96, 70)])
+@pytest.mark.parametrize("dtype,half", [(synth.Q8_0, False), (synth.Q4_0, False), (synth.Q4_0, True), (synth.F16, False)])
+def test_tc_matches_oracle(ctx, oracle, M, K, N, dtype, half):
+    rng = np.random.default_rng(M + 7 * K + 13 * N + dtype)
+    raw = _raw(dtype, rng, N * K)
+    a = rng.integers(-(1 << 37), 1 << 37, (M, K), dtype=np.int64)
+    for shift in (30, 0):
+        got = slx.matmul_q30(a, dtype, raw, N, half_composite=half, shift=shift, ctx=ctx)
+        np.testing.assert_array_equal(got, _ref(oracle, a, dtype, raw, N, half, shift), err_msg=f"shift {shift}")
+
+
+def test_tc_digit_edges(ctx, oracle):
+    """Activations at the digit boundaries (+-128, +-2^31, the 5-digit limits) and all-zero rows."""
+    rng = np.random.default_rng(3)
+    M, K, N = 160, 256, 96
+    raw = _raw(synth.Q8_0, rng, N * K)
+    edges = np.array([127, 128, -128, -129, 255, 256, -256, 1 << 31, -(1 << 31), (1 << 38) + 12345,
+                      -(1 << 38) - 999, 0, 1, -1], np.int64)
+    a = rng.choice(edges, size=(M, K))
+    a[5] = 0
+    got = slx.matmul_q30(a, synth.Q8_0, raw, N, ctx=ctx)
+    np.testing.assert_array_equal(got, _ref(oracle, a, synth.Q8_0, raw, N, False, 30))
+
+
+@pytest.mark.parametrize("big", [1 << 45, np.iinfo(np.int64).min, np.iinfo(np.int64).max])
+def test_tc_overflow_falls_back_exactly(ctx, oracle, big):
+    rng = np.random.default_rng(4)
+    M, K, N = 130, 256, 64
+    raw = _raw(synth.Q4_0, rng, N * K)
+    a = rng.integers(-(1 << 30), 1 << 30, (M, K), dtype=np.int64)
+    a[77, 13] = big
+    got = slx.matmul_q30(a, synth.Q4_0, raw, N, ctx=ctx)
+    np.testing.assert_array_equal(got, _ref(oracle, a, synth.Q4_0, raw, N, False, 30))
+
+
+def test_tc_exact_integer_weights(ctx):
+    """F32 weights v * 2^-30 have composite exactly v, so c = a . w^T in plain integers (shift 0)."""
+    M, K, N = 128, 128, 64
+    a = np.eye(M, K, dtype=np.int64)
+    w = np.array([[n * 1000 + k for k in range(K)] for n in range(N)], np.int64)
+    raw = (w.astype(np.float64) * 2.0 ** -30).astype(np.float32).reshape(-1).view(np.uint8)
+    got = slx.matmul_q30(a, synth.F32, raw, N, shift=0, ctx=ctx)
+    np.testing.assert_array_equal(got, a @ w.T)
