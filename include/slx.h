@@ -111,6 +111,14 @@ slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K,
                                  int64_t w_bytes, int N, int half_composite, int scale_bits, int shift, int64_t* d_c,
                                  void* stream);
 
+/* IntegerAttention on Q30 host arrays for one sequence (Math/IntegerAttention.cs):
+ * mode 0 MultiHeadAttention / GroupedQueryAttention (:60-109, :125-202), mode 1
+ * CausalGroupedQueryAttention (:205-289, leaky -2^29 mask), mode 2 SlidingWindowCausalGQA
+ * (:293-377). q[seq][q_embd], k and v [seq][kv_dim], out[seq][q_embd]; scale_exp as the
+ * reference's scaleExponent (score shift 2|scale_exp| - 30). */
+slx_status slx_attention(slx_ctx* ctx, const int64_t* q, const int64_t* k, const int64_t* v, int seq, int q_embd,
+                         int kv_dim, int n_heads, int n_kv_heads, int scale_exp, int mode, int window, int64_t* out);
+
 /* ---- measurement ---------------------------------------------------------------------------- */
 /* No reference counterpart (the reference times with Stopwatch, SparseLattice.Perf/Program.cs:817-830).
  * Per kernel class, the library's launches on ctx between begin and end, their device time from

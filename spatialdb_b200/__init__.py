@@ -129,6 +129,19 @@ def matmul_q30(a: np.ndarray, dtype: int, w_raw, N: int, half_composite: bool = 
     return c
 
 
+def attention(q, k, v, seq: int, n_heads: int, n_kv_heads: int, scale_exp: int = -30, mode: int = 0,
+              window: int = 0, ctx: Context | None = None) -> np.ndarray:
+    """IntegerAttention on Q30 arrays of one sequence: mode 0 (grouped) multi-head, 1 causal, 2 sliding window."""
+    ctx = ctx or Context.default()
+    q = np.ascontiguousarray(q, np.int64).reshape(seq, -1)
+    k = np.ascontiguousarray(k, np.int64).reshape(seq, -1)
+    v = np.ascontiguousarray(v, np.int64).reshape(seq, -1)
+    out = np.empty_like(q)
+    ctx.check(ctx._lib.slx_attention(ctx._h, _p(q, I64P), _p(k, I64P), _p(v, I64P), seq, q.shape[1], k.shape[1], n_heads,
+                                     n_kv_heads, scale_exp, mode, window, _p(out, I64P)))
+    return out
+
+
 class _Model:
     kind = -1
 

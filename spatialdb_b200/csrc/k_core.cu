@@ -404,7 +404,8 @@ __global__ __launch_bounds__(AW * 32) void k_attention(const int64_t* __restrict
                                                        const int64_t* __restrict__ V, int64_t ldv,
                                                        int64_t* __restrict__ O, int64_t ldo, int T, int nh, int nkv,
                                                        int hd, int score_shift, int64_t sqrt_hd, int mode,
-                                                       int window) {
+                                                       int window, const int* __restrict__ only_if) {
+    if (only_if && *only_if == 0) return;
     extern __shared__ int64_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * AW + warp;
@@ -466,7 +467,7 @@ __global__ __launch_bounds__(AW * 32) void k_attention(const int64_t* __restrict
 
 int attention(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
                int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int score_shift, int64_t sqrt_hd,
-               int mode, int window, cudaStream_t st) {
+               int mode, int window, cudaStream_t st, const int* only_if) {
     if (B * T <= 0) return 0;
     size_t smem = (size_t)AW * (T + hd) * sizeof(int64_t);
     static size_t configured = 0;
@@ -476,7 +477,7 @@ int attention(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, cons
     }
     dim3 grid((unsigned)((T + AW - 1) / AW), (unsigned)nh, (unsigned)B);
     k_attention<<<grid, AW * 32, smem, st>>>(q, ldq, k, ldk, v, ldv, out, ldo, T, nh, nkv, hd, score_shift, sqrt_hd,
-                                             mode, window);
+                                             mode, window, only_if);
     return 1;
 }
 

@@ -18,6 +18,8 @@
 // (bounded) for its outstanding copies, frees TMEM and returns.
 #include <cuda.h>
 
+#include <cstring>
+
 #include "slx_device.cuh"
 #include "slx_gemm.h"
 #include "slx_kernels.h"
@@ -32,11 +34,17 @@ constexpr int THREADS = 192;
 struct Params {
     int M, N, K, nkb, lw, shift, nstages;
     int64_t* C;
-    int64_t ldc;
+    int64_t ldc, c_zstride;
     const int64_t* R;
     int64_t ldr;
-    const int* skip;  // nonzero: the activation did not fit LA digits, the exact kernel runs instead
+    const int* skip;  // nonzero: an operand did not fit its digits, the exact kernel runs instead
     int* err;         // set on a bounded-wait timeout
+    // batch z = blockIdx.z: A operand batch z, B operand batch (z / zh) * zkv + (z % zh) / zgroup
+    int zh, zgroup, zkv;
+    // epilogue: mode 0 projection (shift, residual); mode 1 attention scores
+    // ((long)(acc >> shift) / div, masked slots -2^29 for mask_mode 1 causal / 2 sliding window)
+    int mode, mask_mode, window;
+    int64_t div;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -69,10 +77,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return true;
 }
 
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
     asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-        ::"r"(dst), "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        ::"r"(dst), "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
         : "memory");
 }
 
@@ -121,10 +130,12 @@ __device__ __forceinline__ void tmem_st16_zero(uint32_t taddr) {
         ::"r"(taddr), "r"(z) : "memory");
 }
 
-template <int LW>
+template <int LW, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, Params p) {
     constexpr int S = LA + LW - 1;
+    static_assert(S * BN <= 512, "TMEM holds 512 columns");
+    static_assert((BN * LW) % 16 == 0 && BN * LW <= 256, "M=128 MMA needs N a multiple of 16, at most 256");
     constexpr int A_STAGE = BM * BK * LA;
     constexpr int W_STAGE = BN * BK * LW;
     constexpr int STAGE = A_STAGE + W_STAGE;
@@ -171,6 +182,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     fence_after();
 
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int z = blockIdx.z;
+    const int zb = (z / p.zh) * p.zkv + (z % p.zh) / p.zgroup;
     const uint32_t sbase = smem_u32(smem);
 
     if (warp == 0) {
@@ -182,8 +195,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                 if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) { s_fail = 1; break; }
                 if (*(volatile int*)&s_fail) break;
                 mbar_expect_tx(full0 + 8 * s, STAGE);
-                tma_load_3d(sbase + s * STAGE, &tmA, kb * BK, m0, 0, full0 + 8 * s);
-                tma_load_3d(sbase + s * STAGE + A_STAGE, &tmW, kb * BK, n0, 0, full0 + 8 * s);
+                tma_load_4d(sbase + s * STAGE, &tmA, kb * BK, m0, 0, z, full0 + 8 * s);
+                tma_load_4d(sbase + s * STAGE + A_STAGE, &tmW, kb * BK, n0, 0, zb, full0 + 8 * s);
                 issued = kb + 1;
             }
             if (*(volatile int*)&s_fail) {  // let copies still in flight land before the CTA exits
@@ -225,6 +238,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                 for (int s = 0; s < S; s++) tmem_ld16(taddr + s * BN + c * 16, v[s]);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 if (row < p.M) {
+                    int64_t* crow = p.C + (int64_t)z * p.c_zstride + (int64_t)row * p.ldc;
+                    const int ws = row - p.window + 1;
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         const int n = n0 + c * 16 + j;
@@ -233,8 +248,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
 #pragma unroll
                         for (int s = S - 2; s >= 0; s--) acc = (acc << 8) + (i128)(int32_t)v[s][j];
                         int64_t out = p.shift > 0 ? lo64(sar128(acc, p.shift)) : lo64(acc);
-                        if (p.R) out = wadd(out, p.R[(int64_t)row * p.ldr + n]);
-                        p.C[(int64_t)row * p.ldc + n] = out;
+                        if (p.mode == 0) {
+                            if (p.R) out = wadd(out, p.R[(int64_t)row * p.ldr + n]);
+                        } else if ((p.mask_mode >= 1 && n > row) || (p.mask_mode == 2 && n < ws)) {
+                            out = -(1LL << 29);  // maskValue (IntegerAttention.cs:222)
+                        } else {
+                            out = cs_div64(out, p.div);
+                        }
+                        crow[n] = out;
                     }
                 }
             }
@@ -278,6 +299,43 @@ __global__ void k_split_a(const int64_t* __restrict__ A, int64_t lda, int M, int
 #pragma unroll
     for (int i = 0; i < LA; i++)
         *(uint4*)(planes + ((int64_t)i * Mpad + row) * Kpad + k0) = make_uint4(pk[i][0], pk[i][1], pk[i][2], pk[i][3]);
+}
+
+// Balanced digits of per-head rows: X row (b*T + t), head h, hd values at X + (b*T+t)*ld + h*hd
+// -> planes[(b*nh + h)][i][t][k] (t < tpad, k < kpad, zero padded). Sets *overflow when a value
+// needs more than LA digits.
+__global__ void k_split_heads(const int64_t* __restrict__ X, int64_t ld, int T, int nh, int hd, int tpad, int kpad,
+                              int8_t* __restrict__ planes, int* overflow, int64_t total) {
+    const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (idx >= total) return;
+    const int chunks = kpad / 16;
+    const int k0 = (int)(idx % chunks) * 16;
+    const int64_t r = idx / chunks;  // over (b*nh + h) * tpad + t
+    const int t = (int)(r % tpad);
+    const int64_t bh = r / tpad;
+    const int h = (int)(bh % nh);
+    const int64_t b = bh / nh;
+    uint32_t pk[LA][4];
+#pragma unroll
+    for (int i = 0; i < LA; i++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) pk[i][q] = 0;
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        int64_t x = (t < T && k0 + j < hd) ? X[(b * T + t) * ld + (int64_t)h * hd + k0 + j] : 0;
+#pragma unroll
+        for (int i = 0; i < LA; i++) {
+            int d = (int)(((uint64_t)x + 128u) & 255u) - 128;
+            x = (x - d) >> 8;
+            pk[i][j >> 2] |= (uint32_t)(uint8_t)(int8_t)d << (8 * (j & 3));
+        }
+        bad |= x != 0;
+    }
+    if (bad) atomicOr(overflow, 1);
+#pragma unroll
+    for (int i = 0; i < LA; i++)
+        *(uint4*)(planes + ((bh * LA + i) * tpad + t) * kpad + k0) = make_uint4(pk[i][0], pk[i][1], pk[i][2], pk[i][3]);
 }
 
 // Number of balanced base-256 digits the largest composite weight needs.
@@ -331,36 +389,44 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int LW>
-constexpr size_t stage_bytes() { return (size_t)BM * BK * LA + (size_t)BN * BK * LW; }
+template <int LW, int BNT>
+constexpr size_t stage_bytes() { return (size_t)BM * BK * LA + (size_t)BNT * BK * LW; }
 
-template <int LW>
+template <int LW, int BNT>
 int stages() {
-    int n = (int)((227 * 1024 - 1024 - 256) / stage_bytes<LW>());
+    int n = (int)((227 * 1024 - 1024 - 256) / stage_bytes<LW, BNT>());
     return n > 4 ? 4 : n;
 }
 
-template <int LW>
+template <int LW, int BNT>
 void launch_lw(const CUtensorMap& ta, const CUtensorMap& tw, Params p, dim3 grid, cudaStream_t st) {
-    p.nstages = stages<LW>();
-    const size_t smem = p.nstages * stage_bytes<LW>() + 1024 + (2 * p.nstages + 2) * 8;
+    p.nstages = stages<LW, BNT>();
+    const size_t smem = p.nstages * stage_bytes<LW, BNT>() + 1024 + (2 * p.nstages + 2) * 8;
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(k_gemm_tc<LW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_gemm_tc<LW, BNT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         configured = true;
     }
-    k_gemm_tc<LW><<<grid, THREADS, smem, st>>>(ta, tw, p);
+    k_gemm_tc<LW, BNT><<<grid, THREADS, smem, st>>>(ta, tw, p);
+}
+
+Params base_params() {
+    Params p;
+    memset(&p, 0, sizeof p);
+    p.zh = 1; p.zgroup = 1; p.zkv = 1; p.div = 1;
+    return p;
 }
 }  // namespace
 
-bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows) {
+bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows, int64_t batch) {
     EncodeTiledFn fn = encode_fn();
-    if (!fn || kpad % BK || planes < 1 || planes > 255 || box_rows < 1 || box_rows > 256) return false;
-    cuuint64_t dims[3] = {(cuuint64_t)kpad, (cuuint64_t)rows, (cuuint64_t)planes};
-    cuuint64_t strides[2] = {(cuuint64_t)kpad, (cuuint64_t)(kpad * rows)};
-    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, (cuuint32_t)planes};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn((CUtensorMap*)map128, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, estr,
+    if (!fn || kpad % BK || planes < 1 || planes > 255 || box_rows < 1 || box_rows > 256 || batch < 1) return false;
+    if (((uintptr_t)base & 15) != 0) return false;
+    cuuint64_t dims[4] = {(cuuint64_t)kpad, (cuuint64_t)rows, (cuuint64_t)planes, (cuuint64_t)batch};
+    cuuint64_t strides[3] = {(cuuint64_t)kpad, (cuuint64_t)(kpad * rows), (cuuint64_t)(kpad * rows * planes)};
+    cuuint32_t box[4] = {(cuuint32_t)BK, (cuuint32_t)box_rows, (cuuint32_t)planes, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn((CUtensorMap*)map128, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, base, dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
@@ -393,18 +459,39 @@ void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t 
 
 void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K, int64_t mpad, int64_t npad, int64_t kpad,
             int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st) {
-    Params p;
+    Params p = base_params();
     p.M = M; p.N = N; p.K = K; p.nkb = (int)(kpad / BK); p.lw = lw; p.shift = shift; p.nstages = 2;
     p.C = c; p.ldc = ldc; p.R = r; p.ldr = ldr; p.skip = skip; p.err = err;
     dim3 grid((unsigned)(npad / BN), (unsigned)(mpad / BM));
     const CUtensorMap& ta = *(const CUtensorMap*)tmap_a;
     const CUtensorMap& tw = *(const CUtensorMap*)tmap_w;
     switch (lw) {
-        case 1: launch_lw<1>(ta, tw, p, grid, st); break;
-        case 2: launch_lw<2>(ta, tw, p, grid, st); break;
-        case 3: launch_lw<3>(ta, tw, p, grid, st); break;
-        default: launch_lw<4>(ta, tw, p, grid, st); break;
+        case 1: launch_lw<1, BN>(ta, tw, p, grid, st); break;
+        case 2: launch_lw<2, BN>(ta, tw, p, grid, st); break;
+        case 3: launch_lw<3, BN>(ta, tw, p, grid, st); break;
+        default: launch_lw<4, BN>(ta, tw, p, grid, st); break;
     }
+}
+
+void split_heads(const int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad, int8_t* planes,
+                 int* overflow, cudaStream_t st) {
+    const int64_t total = (int64_t)B * nh * tpad * (kpad / 16);
+    if (total <= 0) return;
+    k_split_heads<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(x, ld, T, nh, hd, (int)tpad, (int)kpad, planes, overflow,
+                                                                  total);
+}
+
+void launch_scores(const void* tmap_q, const void* tmap_k, int B, int T, int nh, int nkv, int64_t tpad_k, int64_t kpad,
+                   int shift, int64_t div, int mask_mode, int window, int64_t* scores, const int* skip, int* err,
+                   cudaStream_t st) {
+    Params p = base_params();
+    p.M = T; p.N = T; p.K = (int)kpad; p.nkb = (int)(kpad / BK); p.lw = LA; p.shift = shift;
+    p.C = scores; p.ldc = T; p.c_zstride = (int64_t)T * T;
+    p.skip = skip; p.err = err;
+    p.zh = nh; p.zgroup = nh / nkv; p.zkv = nkv;
+    p.mode = 1; p.mask_mode = mask_mode; p.window = window; p.div = div;
+    dim3 grid((unsigned)(tpad_k / SBN), (unsigned)((T + BM - 1) / BM), (unsigned)(B * nh));
+    launch_lw<LA, SBN>(*(const CUtensorMap*)tmap_q, *(const CUtensorMap*)tmap_k, p, grid, st);
 }
 
 }  // namespace tc

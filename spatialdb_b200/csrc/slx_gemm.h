@@ -30,16 +30,26 @@ struct GemmWorkspace {
 // Tensor-core kernel launchers (k_gemm_tc.cu).
 namespace tc {
 constexpr int BM = 128, BN = 64, BK = 128, LA = 5;
-// Encodes a TMA map over int8 digit planes [planes][rows][kpad] with a (128 B, box_rows, planes) box.
-bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows);
+constexpr int SBN = 48;  // key columns per CTA in the attention-score GEMM (5 x 5 digits)
+// Encodes a TMA map over int8 digit planes [batch][planes][rows][kpad] with a
+// (128 B, box_rows, planes, 1) box.
+bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows, int64_t batch = 1);
 int weight_digits(const WDesc& w, cudaStream_t st, std::string& err);      // digits of the widest composite
 void split_w(const WDesc& w, int lw, int64_t npad, int64_t kpad, int8_t* planes, cudaStream_t st);
 void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t kpad, int8_t* planes, int* overflow,
              cudaStream_t st);
 void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K, int64_t mpad, int64_t npad, int64_t kpad,
             int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st);
+// Per-head digit planes of rows at x + (b*T+t)*ld + h*hd -> [(b*nh+h)][LA][tpad][kpad].
+void split_heads(const int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad, int8_t* planes,
+                 int* overflow, cudaStream_t st);
+// scores[(b*nh+h)][t][s] = (long)(q.k >> shift) / div with the reference's causal / window mask.
+void launch_scores(const void* tmap_q, const void* tmap_k, int B, int T, int nh, int nkv, int64_t tpad_k, int64_t kpad,
+                   int shift, int64_t div, int mask_mode, int window, int64_t* scores, const int* skip, int* err,
+                   cudaStream_t st);
 }  // namespace tc
 
+bool tc_enabled();
 int gemm_prepare(const WDesc& w, GemmPlan& plan, cudaStream_t st, std::string& err);
 int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPlan& plan, int64_t* c, int64_t ldc,
               int shift, const int64_t* r, int64_t ldr, GemmWorkspace& ws, cudaStream_t st);

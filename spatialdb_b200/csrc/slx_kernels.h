@@ -53,9 +53,20 @@ int rope_rows(int64_t* x, int64_t ld, int B, int T, int nh, int hd, const int64_
 
 // Attention for B sequences of T: q (ldq, nh heads of hd), k/v (ldk/ldv, nkv heads), out (ldo).
 // mode 0 non-causal, 1 causal with the -2^(frac-1) mask, 2 sliding window.
+// With only_if, the kernel does nothing unless *only_if is nonzero.
 int attention(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
                int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int score_shift, int64_t sqrt_hd,
-               int mode, int window, cudaStream_t st);
+               int mode, int window, cudaStream_t st, const int* only_if = nullptr);
+
+// Same attention with tensor-core scores (k_attn.cu): digit split of q/k, tcgen05 score GEMM,
+// CUDA-core softmax and per-term PV, and the exact kernel gated behind them for out-of-range
+// inputs. ws must hold attention_tc_workspace() bytes. Returns the kernels queued, -1 if the
+// tensor maps could not be encoded (nothing queued).
+size_t attention_tc_workspace(int B, int T, int nh, int nkv, int hd);
+bool attention_tc_supported(int T, int nh, int nkv, int hd);
+int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
+                 int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int score_shift, int64_t sqrt_hd,
+                 int mode, int window, void* ws, int* err, cudaStream_t st);
 
 // up[i] = (FixedSiLU(gate[i]) * up[i]) >> 30 over M rows of F (IntegerFFN)
 int silu_gate(const int64_t* gate, int64_t ldg, int64_t* up, int64_t ldu, int M, int F, cudaStream_t st);

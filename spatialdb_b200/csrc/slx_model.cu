@@ -381,6 +381,22 @@ int prepare_gemms(slx_ctx* ctx, slx_model* m) {
     return SLX_OK;
 }
 
+// Attention for one layer: tensor-core scores when the shape allows (exact kernel gated behind).
+int attend(slx_model* m, const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
+           int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int sshift, int64_t sq, int mode, int window,
+           cudaStream_t st) {
+    if (tc_enabled() && attention_tc_supported(T, nh, nkv, hd)) {
+        size_t need = attention_tc_workspace(B, T, nh, nkv, hd);
+        void* ws = m->buf<uint8_t>("attn_ws", need);
+        if (ws) {
+            int n = attention_tc(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, sshift, sq, mode, window, ws,
+                                 m->ctx->d_flag, st);
+            if (n >= 0) return n;
+        }
+    }
+    return attention(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, sshift, sq, mode, window, st);
+}
+
 // One projection: c = (a . w^T) >> shift (+ r).
 inline void project(slx_model* m, const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPlan& p, int64_t* c,
                     int64_t ldc, const int64_t* r, int64_t ldr, cudaStream_t st) {
@@ -411,7 +427,7 @@ int encoder_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers,
         project(m, x, d, M, l.qkv, l.p_qkv, qkv, 3 * d, nullptr, 0, st);
         RUN(KC_ROPE, 0, 0, rope_rows(qkv, 3 * d, B, T, m->heads, hd, m->cos_g, m->sin_g, st));
         RUN(KC_ROPE, 0, 0, rope_rows(qkv + d, 3 * d, B, T, m->heads, hd, m->cos_g, m->sin_g, st));
-        RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0, attention(qkv, 3 * d, qkv + d, 3 * d, qkv + 2 * d, 3 * d, att, d, B, T, m->heads, m->heads, hd, sshift, sq, 0, 0, st));
+        RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0, attend(m, qkv, 3 * d, qkv + d, 3 * d, qkv + 2 * d, 3 * d, att, d, B, T, m->heads, m->heads, hd, sshift, sq, 0, 0, st));
         project(m, att, d, M, l.o, l.p_o, h, d, x, d, st);  // O-projection + residual (AddInPlace)
         RUN(KC_NORM, 0, 0, layernorm_rows(h, d, M, d, l.anw, l.anb, st));
         project(m, h, d, M, l.gate, l.p_gate, gate, F, nullptr, 0, st);
@@ -460,7 +476,7 @@ int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, 
         RUN(KC_ROPE, 0, 0, rope_rows(q, qd, B, T, m->heads, hd, cs, sn, st));
         RUN(KC_ROPE, 0, 0, rope_rows(k, kvd, B, T, m->kv_heads, hd, cs, sn, st));
         int mode = !causal ? 0 : ((global || m->sliding <= 0) ? 1 : 2);
-        RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0, attention(q, qd, k, kvd, v, kvd, att, qd, B, T, m->heads, m->kv_heads, hd, sshift, sq, mode, m->sliding, st));
+        RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0, attend(m, q, qd, k, kvd, v, kvd, att, qd, B, T, m->heads, m->kv_heads, hd, sshift, sq, mode, m->sliding, st));
         project(m, att, qd, M, l.o, l.p_o, p, d, nullptr, 0, st);
         RUN(KC_NORM, 0, 0, rmsnorm_rows(p, d, M, 1, d, l.post_attn, st));
         RUN(KC_ADD, 0, 0, add_rows(p, d, x, d, M, d, st));  // projected += residual; p is the FFN residual
@@ -823,6 +839,48 @@ slx_status slx_matmul_q30(slx_ctx* ctx, const int64_t* a, int M, int K, int dtyp
     cudaFree(da);
     cudaFree(dc);
     cudaFree(dw);
+    return rc;
+}
+
+slx_status slx_attention(slx_ctx* ctx, const int64_t* q, const int64_t* k, const int64_t* v, int seq, int q_embd,
+                         int kv_dim, int nh, int nkv, int scale_exp, int mode, int window, int64_t* out) {
+    if (!ctx || !q || !k || !v || !out || seq <= 0 || nh <= 0 || nkv <= 0 || nh % nkv || q_embd % nh || kv_dim % nkv ||
+        mode < 0 || mode > 2)
+        return set_err(ctx, SLX_EINVAL, "bad arguments");
+    const int hd = q_embd / nh;
+    if (kv_dim / nkv != hd) return set_err(ctx, SLX_EINVAL, "q and kv head sizes differ");
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    const size_t nq = (size_t)seq * q_embd, nk = (size_t)seq * kv_dim;
+    int64_t *dq = nullptr, *dk = nullptr, *dv = nullptr, *dout = nullptr;
+    void* ws = nullptr;
+    const int abs_scale = scale_exp < 0 ? -scale_exp : scale_exp;
+    const int sshift = 2 * abs_scale - 30;
+    int64_t sq = isqrt64_host(hd);
+    if (sq == 0) sq = 1;
+    const bool tc = tc_enabled() && attention_tc_supported(seq, nh, nkv, hd);
+    const size_t wsb = tc ? attention_tc_workspace(1, seq, nh, nkv, hd) : 0;
+    int rc = SLX_OK;
+    if (cudaMalloc(&dq, nq * 8) != cudaSuccess || cudaMalloc(&dk, nk * 8) != cudaSuccess ||
+        cudaMalloc(&dv, nk * 8) != cudaSuccess || cudaMalloc(&dout, nq * 8) != cudaSuccess ||
+        (wsb && cudaMalloc(&ws, wsb) != cudaSuccess)) {
+        rc = set_err(ctx, SLX_EOOM, "device allocation failed");
+    } else {
+        cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), st);
+        cudaMemcpyAsync(dq, q, nq * 8, cudaMemcpyHostToDevice, st);
+        cudaMemcpyAsync(dk, k, nk * 8, cudaMemcpyHostToDevice, st);
+        cudaMemcpyAsync(dv, v, nk * 8, cudaMemcpyHostToDevice, st);
+        int n = -1;
+        if (tc) n = attention_tc(dq, q_embd, dk, kv_dim, dv, kv_dim, dout, q_embd, 1, seq, nh, nkv, hd, sshift, sq, mode,
+                                 window, ws, ctx->d_flag, st);
+        if (n < 0) n = attention(dq, q_embd, dk, kv_dim, dv, kv_dim, dout, q_embd, 1, seq, nh, nkv, hd, sshift, sq, mode,
+                                 window, st);
+        ctx->launches += n;
+        cudaMemcpyAsync(out, dout, nq * 8, cudaMemcpyDeviceToHost, st);
+        rc = check_flag(ctx, st);
+    }
+    cudaFree(dq); cudaFree(dk); cudaFree(dv); cudaFree(dout);
+    if (ws) cudaFree(ws);
     return rc;
 }
 
