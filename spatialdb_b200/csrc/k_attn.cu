@@ -180,7 +180,7 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     tc::launch_scores(mq, mk, B, T, nh, nkv, tk, kpad, score_shift, sqrt_hd, mode, window, scores, flag, err, st);
     const size_t smem = (size_t)PR * T * 4 + (size_t)VT * hd * 8;
     static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
+    if (smem > 32 * 1024 && smem > configured) {  // opt in well before 48 KB (static smem adds to it)
         cudaFuncSetAttribute(k_softmax_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         configured = smem;
     }
