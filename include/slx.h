@@ -63,7 +63,7 @@ slx_status slx_dequantize(slx_ctx* ctx, int dtype, const uint8_t* raw, int64_t n
 /* ---- models -------------------------------------------------------------------------------- */
 /* IntegerTransformerSource.Load (Gguf/IntegerTransformerSource.Loading.cs:47-58),
  * IntegerCausalSource.Load (Gguf/IntegerCausalSource.Loading.cs:41-52) and
- * IntegerGemmaSource.Load (Gguf/IntegerGemmaSource.Loading.cs:57-69): parses the GGUF file and
+ * IntegerGemmaSource.Load (Gguf/IntegerGemmaSource.Loading.cs:58-69): parses the GGUF file and
  * uploads the packed weight blocks to device memory. scale_bits is the Q scale (30). */
 slx_status slx_model_load_gguf(slx_ctx* ctx, const char* path, int kind, int scale_bits, slx_model** out);
 slx_status slx_model_free(slx_model* model);
