@@ -31,6 +31,7 @@ typedef int slx_status;
 #define SLX_EOOM 7          /* device allocation failed */
 #define SLX_ECUDA 8         /* CUDA runtime error */
 #define SLX_ETIMEOUT 9      /* a bounded device wait gave up */
+#define SLX_ESCRATCH 10     /* the request is larger than slx_matmul_q30_noalloc's fixed scratch */
 
 /* Model kinds for slx_model_load_gguf. */
 #define SLX_MODEL_ENCODER 0       /* IntegerTransformerSource (nomic-bert / bert) */
@@ -110,6 +111,22 @@ slx_status slx_matmul_q30(slx_ctx* ctx, const int64_t* a, int M, int K, int dtyp
 slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K, int dtype, const uint8_t* d_w,
                                  int64_t w_bytes, int N, int half_composite, int scale_bits, int shift, int64_t* d_c,
                                  void* stream);
+
+/* No counterpart in the reference: slx_matmul_q30_device for callers that must not allocate device
+ * memory -- services whose GPU memory is owned by another allocator (a framework's caching
+ * allocator or a pre-sized arena), where a cudaMalloc inside a request fails or breaks the budget,
+ * and latency-bound request paths that cannot pay for cudaMalloc and its implicit device
+ * synchronisation. Same arguments and bit-exact result as slx_matmul_q30_device (ldc = N), on the
+ * current CUDA device, but every intermediate lives in a fixed scratch array compiled into the
+ * library (SLX_NOALLOC_SCRATCH_BYTES on every device that loads it, held until exit).
+ * Limit: 256 + 5*ceil(M/128)*128*ceil(K/128)*128 + 4*ceil(N/64)*64*ceil(K/128)*128 bytes must fit
+ * the scratch and K < 32768, else SLX_ESCRATCH. The first call on a device looks up the scratch
+ * address there (cudaGetSymbolAddress); make that first call before any stream capture. The call
+ * returns after its work on `stream` has finished. All calls share the scratch: calls whose GPU
+ * work overlaps (other streams or threads on the same device) race and must be serialised. */
+#define SLX_NOALLOC_SCRATCH_BYTES (32u << 20)
+slx_status slx_matmul_q30_noalloc(const int64_t* d_a, int M, int K, int dtype, const uint8_t* d_w, int64_t w_bytes,
+                                  int N, int half_composite, int scale_bits, int shift, int64_t* d_c, void* stream);
 
 /* IntegerAttention on Q30 host arrays for one sequence (Math/IntegerAttention.cs):
  * mode 0 MultiHeadAttention / GroupedQueryAttention (:60-109, :125-202), mode 1

@@ -22,7 +22,8 @@ import numpy as np
 from . import _lib
 from ._lib import I32P, I64P, F32P, U8P, VP
 
-SLX_OK, SLX_EINVAL, SLX_EFORMAT, SLX_ENOTFOUND, SLX_EUNSUPPORTED, SLX_EEOF, SLX_ERANGE, SLX_EOOM, SLX_ECUDA, SLX_ETIMEOUT = range(10)
+(SLX_OK, SLX_EINVAL, SLX_EFORMAT, SLX_ENOTFOUND, SLX_EUNSUPPORTED, SLX_EEOF, SLX_ERANGE, SLX_EOOM, SLX_ECUDA, SLX_ETIMEOUT,
+ SLX_ESCRATCH) = range(11)
 MODEL_ENCODER, MODEL_CAUSAL, MODEL_GEMMA_ENCODER = 0, 1, 2
 
 

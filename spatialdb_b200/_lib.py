@@ -41,6 +41,7 @@ SIGNATURES = {
     "slx_causal_generate": (i, [VP, I32P, i, i, i, I32P, I32P]),
     "slx_matmul_q30": (i, [VP, I64P, i, i, i, U8P, i64, i, i, i, i, I64P]),
     "slx_matmul_q30_device": (i, [VP, VP, i, i, i, VP, i64, i, i, i, i, VP, VP]),
+    "slx_matmul_q30_noalloc": (i, [VP, i, i, i, VP, i64, i, i, i, i, VP, VP]),
     "slx_attention": (i, [VP, I64P, I64P, I64P, i, i, i, i, i, i, i, i, I64P]),
     "slx_profile_begin": (i, [VP]),
     "slx_profile_end": (i, [VP, VP, i, ctypes.POINTER(i)]),
