@@ -31,14 +31,69 @@ SLX_DEV uint64_t udiv_inv(uint64_t n, uint64_t d, uint64_t inv) {
     return q;
 }
 
+// out[t][d] = sum_s floor(p[t][s] * v[s][d] / 2^30) for the block's rows, wrapping sums.
+// p * v = p * v_hi * 2^30 + p * v_lo, so each term is p*v_hi + umulhi(p, 4*v_lo) exactly.
+template <int RPT, int HD>
+__device__ __forceinline__ void pv_rows(const uint32_t* __restrict__ P, int Tp, const int64_t* __restrict__ vb, int64_t ldv,
+                                        uint32_t* Vlo4, int32_t* Vhi, int T, int t0, int64_t* __restrict__ O, int64_t ldo,
+                                        int b, int h, int* s_bad) {
+    constexpr int G = PT / HD;  // row groups
+    static_assert(G * RPT == PR, "rows per block");
+    const int d = threadIdx.x % HD, g = threadIdx.x / HD;
+    uint64_t acc[RPT];
+#pragma unroll
+    for (int j = 0; j < RPT; j++) acc[j] = 0;
+    for (int s0 = 0; s0 < Tp; s0 += VT) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < VT * HD; i += PT) {
+            const int s = s0 + i / HD, dd = i % HD;
+            int64_t v = s < T ? vb[(int64_t)s * ldv + dd] : 0;
+            const int64_t hi = v >> 30;
+            if (hi < INT32_MIN || hi > INT32_MAX) *s_bad = 1;
+            Vhi[i] = (int32_t)hi;
+            Vlo4[i] = (uint32_t)(v & ((1LL << 30) - 1)) << 2;
+        }
+        __syncthreads();
+        if (*s_bad) return;
+        const int nk = min(VT, Tp - s0);
+        for (int s = 0; s < nk; s += 4) {
+            uint32_t lo[4];
+            int32_t hi[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                lo[u] = Vlo4[(s + u) * HD + d];
+                hi[u] = Vhi[(s + u) * HD + d];
+            }
+#pragma unroll
+            for (int j = 0; j < RPT; j++) {
+                const uint4 p4 = *(const uint4*)(P + (size_t)(g + G * j) * Tp + s0 + s);
+                const uint32_t pw[4] = {p4.x, p4.y, p4.z, p4.w};
+                uint64_t a = acc[j];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    a += (uint64_t)((int64_t)(int32_t)pw[u] * (int64_t)hi[u]);
+                    a += __umulhi(pw[u], lo[u]);
+                }
+                acc[j] = a;
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < RPT; j++) {
+        const int t = t0 + g + G * j;
+        if (t < T) O[((int64_t)b * T + t) * ldo + (int64_t)h * HD + d] = (int64_t)acc[j];
+    }
+}
+
 __global__ __launch_bounds__(PT) void k_softmax_pv(const int64_t* __restrict__ S, const int64_t* __restrict__ V,
                                                    int64_t ldv, int64_t* __restrict__ O, int64_t ldo, int T, int nh,
                                                    int nkv, int hd, const int* __restrict__ skip, int* flag) {
     if (*skip) return;
     extern __shared__ uint8_t sm[];
-    uint32_t* P = (uint32_t*)sm;                                   // [PR][T]
-    uint32_t* Vlo = P + (size_t)PR * T;                            // [VT][hd]
-    int32_t* Vhi = (int32_t*)(Vlo + (size_t)VT * hd);              // [VT][hd]
+    const int Tp = (T + 3) & ~3;                                   // P rows padded to 4 keys (16 B)
+    uint32_t* P = (uint32_t*)sm;                                   // [PR][Tp], p in [0, 2^30]
+    uint32_t* Vlo4 = P + (size_t)PR * Tp;                          // [VT][hd], 4 * (v mod 2^30)
+    int32_t* Vhi = (int32_t*)(Vlo4 + (size_t)VT * hd);             // [VT][hd], v >> 30
     __shared__ int s_bad;
     const int h = blockIdx.y, b = blockIdx.z, t0 = blockIdx.x * PR;
     const int kvh = h / (nh / nkv);
@@ -49,7 +104,8 @@ __global__ __launch_bounds__(PT) void k_softmax_pv(const int64_t* __restrict__ S
     // ---- softmax rows (FixedSoftmax), two rows per warp
     for (int r = warp; r < PR; r += PT / 32) {
         const int t = t0 + r;
-        uint32_t* prow = P + (size_t)r * T;
+        uint32_t* prow = P + (size_t)r * Tp;
+        for (int s = T + lane; s < Tp; s += 32) prow[s] = 0;
         if (t >= T) {
             for (int s = lane; s < T; s += 32) prow[s] = 0;
             continue;
@@ -85,61 +141,18 @@ __global__ __launch_bounds__(PT) void k_softmax_pv(const int64_t* __restrict__ S
         if (threadIdx.x == 0) atomicOr(flag, 1);
         return;
     }
-
-    // ---- PV: thread owns outputs (r, d) with d = tid % hd-chunk
+    // ---- PV. Thread (g, d): d = tid % hd, rows g, g+G, ... (G = PT/hd row groups). Each key's
+    // (v_hi, 4*v_lo) is read once per thread and used for all its rows; p comes four keys at a time.
     const int64_t* vb = V + (int64_t)b * T * ldv + (int64_t)kvh * hd;
-    const int outs = PR * hd;
-    const int per = (outs + PT - 1) / PT;  // outputs per thread (4 for hd 64, 16 for hd 256)
-    uint64_t acc_hi[16];  // wrapping sums (the reference adds longs unchecked)
-    uint64_t acc_lo[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) { acc_hi[i] = 0; acc_lo[i] = 0; }
-    for (int s0 = 0; s0 < T; s0 += VT) {
-        const int nk = min(VT, T - s0);
-        __syncthreads();
-        for (int i = threadIdx.x; i < nk * hd; i += PT) {
-            const int s = i / hd, d = i % hd;
-            const int64_t v = vb[(int64_t)(s0 + s) * ldv + d];
-            const int64_t hi = v >> 30;
-            if (hi < INT32_MIN || hi > INT32_MAX) s_bad = 1;
-            Vhi[i] = (int32_t)hi;
-            Vlo[i] = (uint32_t)(v & ((1LL << 30) - 1));
-        }
-        __syncthreads();
-        if (s_bad) break;
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-            if (j >= per) break;
-            const int o = threadIdx.x + j * PT;
-            if (o >= outs) break;
-            const int r = o / hd, d = o % hd;
-            const uint32_t* prow = P + (size_t)r * T + s0;
-            uint64_t ah = acc_hi[j];
-            uint64_t al = acc_lo[j];
-            for (int s = 0; s < nk; s++) {
-                const uint32_t pw = prow[s];
-                const uint32_t lo = Vlo[s * hd + d];
-                ah += (uint64_t)((int64_t)(int32_t)pw * (int64_t)Vhi[s * hd + d]);
-                al += __umulhi(pw << 2, lo) + ((pw >> 30) ? lo : 0u);
-            }
-            acc_hi[j] = ah;
-            acc_lo[j] = al;
-        }
+    switch (hd) {
+        case 16: pv_rows<1, 16>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad); break;
+        case 32: pv_rows<2, 32>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad); break;
+        case 64: pv_rows<4, 64>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad); break;
+        case 128: pv_rows<8, 128>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad); break;
+        default: pv_rows<16, 256>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad); break;
     }
     __syncthreads();
-    if (s_bad) {
-        if (threadIdx.x == 0) atomicOr(flag, 1);
-        return;
-    }
-#pragma unroll
-    for (int j = 0; j < 16; j++) {
-        if (j >= per) break;
-        const int o = threadIdx.x + j * PT;
-        if (o >= outs) break;
-        const int r = o / hd, d = o % hd;
-        const int t = t0 + r;
-        if (t < T) O[((int64_t)b * T + t) * ldo + (int64_t)h * hd + d] = (int64_t)(acc_hi[j] + acc_lo[j]);
-    }
+    if (s_bad && threadIdx.x == 0) atomicOr(flag, 1);
 }
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
@@ -153,9 +166,11 @@ size_t attention_tc_workspace(int B, int T, int nh, int nkv, int hd) {
     return (size_t)(256 + round_up(qbytes, 256) + round_up(kbytes, 256) + sbytes);
 }
 
+size_t softmax_pv_smem(int T, int hd) { return (size_t)PR * ((T + 3) & ~3) * 4 + (size_t)VT * hd * 8; }
+
 bool attention_tc_supported(int T, int nh, int nkv, int hd) {
-    const size_t smem = (size_t)PR * T * 4 + (size_t)VT * hd * 8;
-    return hd % 16 == 0 && hd <= 256 && PR * hd <= 16 * PT && nkv > 0 && nh % nkv == 0 && smem <= 200 * 1024;
+    const bool hd_ok = hd == 16 || hd == 32 || hd == 64 || hd == 128 || hd == 256;
+    return hd_ok && nkv > 0 && nh % nkv == 0 && softmax_pv_smem(T, hd) <= 200 * 1024;
 }
 
 int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
@@ -178,7 +193,7 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     tc::split_heads(q, ldq, B, T, nh, hd, tq, kpad, qp, flag, st);
     tc::split_heads(k, ldk, B, T, nkv, hd, tk, kpad, kp, flag, st);
     tc::launch_scores(mq, mk, B, T, nh, nkv, tk, kpad, score_shift, sqrt_hd, mode, window, scores, flag, err, st);
-    const size_t smem = (size_t)PR * T * 4 + (size_t)VT * hd * 8;
+    const size_t smem = softmax_pv_smem(T, hd);
     static size_t configured = 0;
     if (smem > 32 * 1024 && smem > configured) {  // opt in well before 48 KB (static smem adds to it)
         cudaFuncSetAttribute(k_softmax_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

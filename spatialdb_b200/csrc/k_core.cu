@@ -318,10 +318,11 @@ __global__ __launch_bounds__(NT) void k_layernorm(int64_t* __restrict__ X, int64
         for (int j = threadIdx.x; j < n; j += NT) x[j] = b[j];
         return;
     }
-    int64_t isq = s_isq;
+    const int64_t isq = s_isq;
+    const double rd = 1.0 / (double)isq;
     for (int j = threadIdx.x; j < n; j += NT) {
         int64_t dl = wsub(x[j], mean);
-        x[j] = wadd(lo64(((i128)dl * w[j]) / (i128)isq), b[j]);
+        x[j] = wadd(div_trunc((i128)dl * w[j], isq, rd), b[j]);
     }
 }
 
@@ -344,8 +345,9 @@ __global__ __launch_bounds__(NT) void k_rmsnorm(int64_t* __restrict__ X, int64_t
     }
     __syncthreads();
     if (s_skip) return;
-    int64_t rms = s_rms;
-    for (int j = threadIdx.x; j < n; j += NT) x[j] = lo64(((i128)x[j] * w[j]) / (i128)rms);
+    const int64_t rms = s_rms;
+    const double rd = 1.0 / (double)rms;
+    for (int j = threadIdx.x; j < n; j += NT) x[j] = div_trunc((i128)x[j] * w[j], rms, rd);
 }
 }  // namespace
 

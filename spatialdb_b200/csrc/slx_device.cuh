@@ -117,6 +117,28 @@ SLX_DEV int64_t fixed_exp30(int64_t x) {
     return sum >> sh;
 }
 
+// Truncating num / d for d >= 1 with rd = 1.0 / d: a double estimate corrected to the exact
+// quotient by its integer remainder. Used when |num| < 2^62 and the quotient is below 2^50, where
+// the estimate is within one of the quotient; any other case divides in Int128.
+SLX_DEV int64_t div_trunc(i128 num, int64_t d, double rd) {
+    const i128 lim = (i128)1 << 62;
+    if (num > -lim && num < lim) {
+        const int64_t n = (int64_t)num;
+        const uint64_t an = n < 0 ? (uint64_t)(-n) : (uint64_t)n;
+        if ((an >> 50) < (uint64_t)d || d >= (1LL << 12)) {
+            const double qd = (double)an * rd;
+            if (qd < 1125899906842624.0) {  // 2^50
+                int64_t q = (int64_t)qd;
+                int64_t r = (int64_t)an - q * d;
+                while (r < 0) { q--; r += d; }
+                while (r >= d) { q++; r -= d; }
+                return n < 0 ? -q : q;
+            }
+        }
+    }
+    return lo64(num / (i128)d);
+}
+
 // FixedSigmoid / FixedSiLU (IntegerTranscendentals.cs:49-69), fracBits = 30.
 SLX_DEV int64_t fixed_sigmoid30(int64_t x) {
     const int64_t one = 1LL << 30, thr = 20LL << 30;
@@ -124,7 +146,13 @@ SLX_DEV int64_t fixed_sigmoid30(int64_t x) {
     if (x < -thr) return 0;
     int64_t den = wadd(one, fixed_exp30(wsub(0, x)));
     if (den == 0) return one;
-    if (den > 0) return (int64_t)((1ULL << 60) / (uint64_t)den);
+    if (den > 0) {  // 2^60 / den, den in [2^30, 2^59): estimate within one, then exact correction
+        int64_t q = (int64_t)(1152921504606846976.0 * __drcp_rn((double)den));
+        int64_t r = (int64_t)((1ULL << 60) - (uint64_t)q * (uint64_t)den);
+        while (r < 0) { q--; r += den; }
+        while (r >= den) { q++; r -= den; }
+        return q;
+    }
     return lo64((i128)(1LL << 60) / (i128)den);
 }
 SLX_DEV int64_t fixed_silu30(int64_t x) { return lo64(sar128((i128)x * fixed_sigmoid30(x), 30)); }
