@@ -240,6 +240,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                 if (row < p.M) {
                     int64_t* crow = p.C + (int64_t)z * p.c_zstride + (int64_t)row * p.ldc;
                     const int ws = row - p.window + 1;
+                    const double rdiv = 1.0 / (double)p.div;
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         const int n = n0 + c * 16 + j;
@@ -253,7 +254,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                         } else if ((p.mask_mode >= 1 && n > row) || (p.mask_mode == 2 && n < ws)) {
                             out = -(1LL << 29);  // maskValue (IntegerAttention.cs:222)
                         } else {
-                            out = cs_div64(out, p.div);
+                            out = div_small(out, p.div, rdiv);
                         }
                         crow[n] = out;
                     }

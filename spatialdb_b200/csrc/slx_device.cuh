@@ -88,7 +88,9 @@ SLX_DEV int64_t isqrt_u128(u128 v) {
 // FixedExp (IntegerTranscendentals.cs:13-47), fracBits = 30. The Taylor term update
 // (long)((Int128)term * r / (n << 30)) equals ((term * r) >> 30) / n whenever term, r >= 0 and
 // term * r < 2^64 (floor of floor); that fast path covers every input after range reduction,
-// the general Int128 form stays for anything else.
+// the general Int128 form stays for anything else. The reference stops once a term is 0 past
+// n = 4; a zero term stays zero and adds nothing, so all 14 steps run here, fully unrolled, which
+// turns every division by n into a multiply by a constant.
 SLX_DEV int64_t fixed_exp30(int64_t x) {
     const int64_t ln2 = 744261117;  // (long)(0.6931471805599453 * 2^30)
     int64_t k = x >= 0 ? x / ln2 : wsub(0, cs_div64(wsub(wadd(wsub(0, x), ln2), 1), ln2));
@@ -106,7 +108,6 @@ SLX_DEV int64_t fixed_exp30(int64_t x) {
             term = lo64(((i128)term * r) / ((i128)n << 30));
         }
         sum = wadd(sum, term);
-        if (term == 0 && n > 4) break;
     }
     if (k >= 0) {
         if (k >= 63 || sum > (INT64_MAX >> k)) return INT64_MAX;
@@ -137,6 +138,20 @@ SLX_DEV int64_t div_trunc(i128 num, int64_t d, double rd) {
         }
     }
     return lo64(num / (i128)d);
+}
+
+// C# long / long for a positive divisor d with rd = 1.0 / d: exact (double estimate corrected by
+// the integer remainder) when |x| < 2^52, cs_div64 otherwise.
+SLX_DEV int64_t div_small(int64_t x, int64_t d, double rd) {
+    const uint64_t ax = x < 0 ? (uint64_t)0 - (uint64_t)x : (uint64_t)x;
+    if (ax < (1ULL << 52)) {
+        int64_t q = (int64_t)((double)ax * rd);
+        int64_t r = (int64_t)ax - q * d;
+        while (r < 0) { q--; r += d; }
+        while (r >= d) { q++; r -= d; }
+        return x < 0 ? -q : q;
+    }
+    return cs_div64(x, d);
 }
 
 // FixedSigmoid / FixedSiLU (IntegerTranscendentals.cs:49-69), fracBits = 30.
