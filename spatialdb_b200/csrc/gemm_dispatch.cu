@@ -27,17 +27,26 @@ bool tc_enabled() {
 int gemm_prepare(const WDesc& w, GemmPlan& plan, cudaStream_t st, std::string& err) {
     plan = GemmPlan();
     if (!tc_enabled() || w.K >= 32768 || w.N <= 0 || w.K <= 0) return SLX_OK;
-    int maxd = tc::weight_digits(w, st, err);
+    // Factor each row's common trailing zero bits out of its composites (restored exactly in the
+    // epilogue's Int128 sum), so the digit planes hold fewer significant bits.
+    if (cudaMalloc(&plan.row_shift, (size_t)w.N) != cudaSuccess) { err = "device allocation failed"; return SLX_EOOM; }
+    tc::weight_tz(w, plan.row_shift, st);
+    int maxd = tc::weight_digits(w, st, err, plan.row_shift);
     if (maxd < 0) return SLX_ECUDA;
-    if (maxd > 4) return SLX_OK;  // composites too wide for the digit path: exact kernel
+    if (maxd > 4) {  // composites too wide for the digit path: exact kernel
+        cudaFree(plan.row_shift);
+        plan.row_shift = nullptr;
+        return SLX_OK;
+    }
     plan.wlimbs = maxd < 1 ? 1 : maxd;
     plan.n_pad = round_up(w.N, tc::BN);
     plan.k_pad = round_up(w.K, tc::BK);
     plan.limb_bytes = (size_t)plan.wlimbs * plan.n_pad * plan.k_pad;
     if (cudaMalloc(&plan.limbs, plan.limb_bytes) != cudaSuccess) { err = "device allocation failed"; return SLX_EOOM; }
-    tc::split_w(w, plan.wlimbs, plan.n_pad, plan.k_pad, (int8_t*)plan.limbs, st);
+    tc::split_w(w, plan.wlimbs, plan.n_pad, plan.k_pad, (int8_t*)plan.limbs, st, plan.row_shift);
     if (!tc::encode_planes(plan.tmap_w, plan.limbs, plan.k_pad, plan.n_pad, plan.wlimbs, tc::BN)) {
         cudaFree(plan.limbs);
+        cudaFree(plan.row_shift);
         plan = GemmPlan();
         return SLX_OK;  // no tensor-map encoder available: exact kernel
     }
@@ -66,7 +75,7 @@ int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPla
     cudaMemsetAsync(flag, 0, sizeof(int), st);
     tc::split_a(a, lda, M, (int)w.K, mpad, plan.k_pad, planes, flag, st);
     tc::launch(tmap_a, plan.tmap_w, plan.wlimbs, M, (int)w.N, (int)w.K, mpad, plan.n_pad, plan.k_pad, shift, c, ldc, r,
-               ldr, flag, ws.err, st);
+               ldr, flag, ws.err, st, plan.row_shift);
     gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st, flag);  // runs only if the split overflowed
     return 3;
 }

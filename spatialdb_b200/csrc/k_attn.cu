@@ -40,9 +40,10 @@ __device__ __forceinline__ void pv_rows(const uint32_t* __restrict__ P, int Tp, 
     constexpr int G = PT / HD;  // row groups
     static_assert(G * RPT == PR, "rows per block");
     const int d = threadIdx.x % HD, g = threadIdx.x / HD;
-    uint64_t acc[RPT];
+    int64_t acc_hi[RPT];   // sum of p * v_hi (two's-complement wrap, as the reference's long adds)
+    uint64_t acc_lo[RPT];  // sum of floor(p * v_lo / 2^30)
 #pragma unroll
-    for (int j = 0; j < RPT; j++) acc[j] = 0;
+    for (int j = 0; j < RPT; j++) { acc_hi[j] = 0; acc_lo[j] = 0; }
     for (int s0 = 0; s0 < Tp; s0 += VT) {
         __syncthreads();
         for (int i = threadIdx.x; i < VT * HD; i += PT) {
@@ -67,21 +68,24 @@ __device__ __forceinline__ void pv_rows(const uint32_t* __restrict__ P, int Tp, 
 #pragma unroll
             for (int j = 0; j < RPT; j++) {
                 const uint4 p4 = *(const uint4*)(P + (size_t)(g + G * j) * Tp + s0 + s);
-                const uint32_t pw[4] = {p4.x, p4.y, p4.z, p4.w};
-                uint64_t a = acc[j];
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    a += (uint64_t)((int64_t)(int32_t)pw[u] * (int64_t)hi[u]);
-                    a += __umulhi(pw[u], lo[u]);
-                }
-                acc[j] = a;
+                int64_t ah = acc_hi[j];
+                // p <= 2^30 fits s32: one mad.wide.s32 per term (64-bit wrap-around sum)
+                asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(ah) : "r"((int32_t)p4.x), "r"(hi[0]));
+                asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(ah) : "r"((int32_t)p4.y), "r"(hi[1]));
+                asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(ah) : "r"((int32_t)p4.z), "r"(hi[2]));
+                asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(ah) : "r"((int32_t)p4.w), "r"(hi[3]));
+                acc_hi[j] = ah;
+                // each floor(p * 4 v_lo / 2^32) < 2^30, so four of them sum below 2^32
+                const uint32_t q = __umulhi(p4.x, lo[0]) + __umulhi(p4.y, lo[1]) + __umulhi(p4.z, lo[2]) +
+                                   __umulhi(p4.w, lo[3]);
+                acc_lo[j] += q;
             }
         }
     }
 #pragma unroll
     for (int j = 0; j < RPT; j++) {
         const int t = t0 + g + G * j;
-        if (t < T) O[((int64_t)b * T + t) * ldo + (int64_t)h * HD + d] = (int64_t)acc[j];
+        if (t < T) O[((int64_t)b * T + t) * ldo + (int64_t)h * HD + d] = (int64_t)((uint64_t)acc_hi[j] + acc_lo[j]);
     }
 }
 

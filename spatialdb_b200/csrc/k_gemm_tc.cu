@@ -45,6 +45,8 @@ struct Params {
     // ((long)(acc >> shift) / div, masked slots -2^29 for mask_mode 1 causal / 2 sliding window)
     int mode, mask_mode, window;
     int64_t div;
+    // projections: the weight row n was stored as w >> row_shift[n] (its common trailing zeros)
+    const int8_t* row_shift;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -248,6 +250,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                         i128 acc = (i128)(int32_t)v[S - 1][j];
 #pragma unroll
                         for (int s = S - 2; s >= 0; s--) acc = (acc << 8) + (i128)(int32_t)v[s][j];
+                        if (p.row_shift) acc <<= p.row_shift[n];
                         int64_t out = p.shift > 0 ? lo64(sar128(acc, p.shift)) : lo64(acc);
                         if (p.mode == 0) {
                             if (p.R) out = wadd(out, p.R[(int64_t)row * p.ldr + n]);
@@ -339,12 +342,34 @@ __global__ void k_split_heads(const int64_t* __restrict__ X, int64_t ld, int T, 
         *(uint4*)(planes + ((bh * LA + i) * tpad + t) * kpad + k0) = make_uint4(pk[i][0], pk[i][1], pk[i][2], pk[i][3]);
 }
 
-// Number of balanced base-256 digits the largest composite weight needs.
-__global__ void k_weight_digits(WDesc W, int* maxd) {
+// Common trailing zero bits of each weight row's Q30 composites (0 for an all-zero row).
+// Q4_0 / Q8_0 composites are d_int * q with d_int an f16 mantissa times a power of two, so a row
+// typically shares ten or more low zero bits; storing w >> tz[n] saves one or two digits.
+__global__ void k_weight_tz(WDesc W, int8_t* tz) {
+    const int n = blockIdx.x;
+    int m = 64;
+    for (int64_t k = threadIdx.x; k < W.K; k += blockDim.x) {
+        int64_t x = composite(dequant_elem(W.dtype, W.data, (int64_t)n * W.K + k, W.nblocks), W.mode, W.scale);
+        if (x != 0) m = min(m, __ffsll(x) - 1);
+    }
+    for (int o = 16; o > 0; o >>= 1) m = min(m, __shfl_xor_sync(0xffffffffu, m, o));
+    __shared__ int sm[32];
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int i = 1; i < (int)(blockDim.x >> 5); i++) m = min(m, sm[i]);
+        m = min(m, sm[0]);
+        tz[n] = (int8_t)(m >= 63 ? 0 : m);
+    }
+}
+
+// Number of balanced base-256 digits the largest (row-shifted) composite weight needs.
+__global__ void k_weight_digits(WDesc W, int* maxd, const int8_t* tz) {
     int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     int nd = 0;
     if (e < W.N * W.K) {
         int64_t x = composite(dequant_elem(W.dtype, W.data, e, W.nblocks), W.mode, W.scale);
+        if (tz) x >>= tz[e / W.K];
         while (x != 0 && nd < 9) {
             int d = (int)(((uint64_t)x + 128u) & 255u) - 128;
             x = (x - d) >> 8;
@@ -355,12 +380,14 @@ __global__ void k_weight_digits(WDesc W, int* maxd) {
     if ((threadIdx.x & 31) == 0 && nd) atomicMax(maxd, nd);
 }
 
-// Weight digit planes[j][n][k] (n < Npad, k < Kpad, zero padded) of the Q30 composite.
-__global__ void k_split_w(WDesc W, int lw, int Npad, int Kpad, int8_t* __restrict__ planes) {
+// Weight digit planes[j][n][k] (n < Npad, k < Kpad, zero padded) of the Q30 composite, shifted
+// right by the row's common trailing zeros when tz is given.
+__global__ void k_split_w(WDesc W, int lw, int Npad, int Kpad, int8_t* __restrict__ planes, const int8_t* tz) {
     const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (idx >= (int64_t)Npad * Kpad) return;
     const int n = (int)(idx / Kpad), k = (int)(idx % Kpad);
     int64_t x = (n < W.N && k < W.K) ? composite(dequant_elem(W.dtype, W.data, (int64_t)n * W.K + k, W.nblocks), W.mode, W.scale) : 0;
+    if (tz && n < W.N) x >>= tz[n];
     for (int j = 0; j < lw; j++) {
         int d = (int)(((uint64_t)x + 128u) & 255u) - 128;
         x = (x - d) >> 8;
@@ -433,12 +460,16 @@ bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int pla
     return r == CUDA_SUCCESS;
 }
 
-int weight_digits(const WDesc& w, cudaStream_t st, std::string& err) {
+void weight_tz(const WDesc& w, int8_t* tz, cudaStream_t st) {
+    k_weight_tz<<<(unsigned)w.N, 256, 0, st>>>(w, tz);
+}
+
+int weight_digits(const WDesc& w, cudaStream_t st, std::string& err, const int8_t* tz) {
     int* d_max = nullptr;
     if (cudaMalloc(&d_max, sizeof(int)) != cudaSuccess) { err = "device allocation failed"; return -1; }
     cudaMemsetAsync(d_max, 0, sizeof(int), st);
     const int64_t n = w.N * w.K;
-    k_weight_digits<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, d_max);
+    k_weight_digits<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, d_max, tz);
     int maxd = 0;
     cudaMemcpyAsync(&maxd, d_max, sizeof(int), cudaMemcpyDeviceToHost, st);
     cudaError_t e = cudaStreamSynchronize(st);
@@ -447,9 +478,9 @@ int weight_digits(const WDesc& w, cudaStream_t st, std::string& err) {
     return maxd;
 }
 
-void split_w(const WDesc& w, int lw, int64_t npad, int64_t kpad, int8_t* planes, cudaStream_t st) {
+void split_w(const WDesc& w, int lw, int64_t npad, int64_t kpad, int8_t* planes, cudaStream_t st, const int8_t* tz) {
     const int64_t tot = npad * kpad;
-    k_split_w<<<(unsigned)((tot + 255) / 256), 256, 0, st>>>(w, lw, (int)npad, (int)kpad, planes);
+    k_split_w<<<(unsigned)((tot + 255) / 256), 256, 0, st>>>(w, lw, (int)npad, (int)kpad, planes, tz);
 }
 
 void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t kpad, int8_t* planes, int* overflow,
@@ -459,10 +490,11 @@ void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t 
 }
 
 void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K, int64_t mpad, int64_t npad, int64_t kpad,
-            int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st) {
+            int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st,
+            const int8_t* row_shift) {
     Params p = base_params();
     p.M = M; p.N = N; p.K = K; p.nkb = (int)(kpad / BK); p.lw = lw; p.shift = shift; p.nstages = 2;
-    p.C = c; p.ldc = ldc; p.R = r; p.ldr = ldr; p.skip = skip; p.err = err;
+    p.C = c; p.ldc = ldc; p.R = r; p.ldr = ldr; p.skip = skip; p.err = err; p.row_shift = row_shift;
     dim3 grid((unsigned)(npad / BN), (unsigned)(mpad / BM));
     const CUtensorMap& ta = *(const CUtensorMap*)tmap_a;
     const CUtensorMap& tw = *(const CUtensorMap*)tmap_w;

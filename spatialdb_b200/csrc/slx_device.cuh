@@ -88,9 +88,8 @@ SLX_DEV int64_t isqrt_u128(u128 v) {
 // FixedExp (IntegerTranscendentals.cs:13-47), fracBits = 30. The Taylor term update
 // (long)((Int128)term * r / (n << 30)) equals ((term * r) >> 30) / n whenever term, r >= 0 and
 // term * r < 2^64 (floor of floor); that fast path covers every input after range reduction,
-// the general Int128 form stays for anything else. The reference stops once a term is 0 past
-// n = 4; a zero term stays zero and adds nothing, so all 14 steps run here, fully unrolled, which
-// turns every division by n into a multiply by a constant.
+// the general Int128 form stays for anything else. The loop is unrolled, so each division by n
+// is a multiply by a constant; it stops, as the reference does, once a term is 0 past n = 4.
 SLX_DEV int64_t fixed_exp30(int64_t x) {
     const int64_t ln2 = 744261117;  // (long)(0.6931471805599453 * 2^30)
     int64_t k = x >= 0 ? x / ln2 : wsub(0, cs_div64(wsub(wadd(wsub(0, x), ln2), 1), ln2));
@@ -108,6 +107,7 @@ SLX_DEV int64_t fixed_exp30(int64_t x) {
             term = lo64(((i128)term * r) / ((i128)n << 30));
         }
         sum = wadd(sum, term);
+        if (term == 0 && n > 4) break;
     }
     if (k >= 0) {
         if (k >= 63 || sum > (INT64_MAX >> k)) return INT64_MAX;

@@ -18,6 +18,7 @@ struct GemmPlan {
     size_t limb_bytes = 0;
     int64_t n_pad = 0, k_pad = 0;
     alignas(64) unsigned char tmap_w[128];  // CUtensorMap of the weight digit planes
+    int8_t* row_shift = nullptr;              // device [N]: trailing zeros factored out of each row
 };
 
 // Per-model scratch shared by the projections.
@@ -34,12 +35,17 @@ constexpr int SBN = 48;  // key columns per CTA in the attention-score GEMM (5 x
 // Encodes a TMA map over int8 digit planes [batch][planes][rows][kpad] with a
 // (128 B, box_rows, planes, 1) box.
 bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows, int64_t batch = 1);
-int weight_digits(const WDesc& w, cudaStream_t st, std::string& err);      // digits of the widest composite
-void split_w(const WDesc& w, int lw, int64_t npad, int64_t kpad, int8_t* planes, cudaStream_t st);
+// Per-row common trailing zeros of the Q30 composites -> tz[N].
+void weight_tz(const WDesc& w, int8_t* tz, cudaStream_t st);
+// Digits of the widest composite (after the optional per-row shift tz).
+int weight_digits(const WDesc& w, cudaStream_t st, std::string& err, const int8_t* tz = nullptr);
+void split_w(const WDesc& w, int lw, int64_t npad, int64_t kpad, int8_t* planes, cudaStream_t st,
+             const int8_t* tz = nullptr);
 void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t kpad, int8_t* planes, int* overflow,
              cudaStream_t st);
 void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K, int64_t mpad, int64_t npad, int64_t kpad,
-            int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st);
+            int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st,
+            const int8_t* row_shift = nullptr);
 // Per-head digit planes of rows at x + (b*T+t)*ld + h*hd -> [(b*nh+h)][LA][tpad][kpad].
 void split_heads(const int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad, int8_t* planes,
                  int* overflow, cudaStream_t st);

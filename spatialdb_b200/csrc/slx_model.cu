@@ -376,6 +376,7 @@ int prepare_gemms(slx_ctx* ctx, slx_model* m) {
             int st = gemm_prepare(*ws[i], *ps[i], ctx->stream, ctx->err);
             if (st) return st;
             if (ps[i]->limb_bytes) m->allocs.push_back(ps[i]->limbs);
+            if (ps[i]->row_shift) m->allocs.push_back(ps[i]->row_shift);
         }
     }
     return SLX_OK;
@@ -810,6 +811,7 @@ slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K,
     RUN(KC_GEMM, (double)M * N * K, 0, gemm_run(d_a, K, M, w, plan, d_c, N, shift, nullptr, 0, ws, st));
     cudaError_t e = cudaStreamSynchronize(st);
     if (plan.limbs) cudaFree(plan.limbs);
+    if (plan.row_shift) cudaFree(plan.row_shift);
     gemm_workspace_free(ws);
     if (e != cudaSuccess) return set_err(ctx, SLX_ECUDA, "%s", cudaGetErrorString(e));
     CK(cudaGetLastError());
