@@ -89,9 +89,11 @@ __device__ __forceinline__ void pv_rows(const uint32_t* __restrict__ P, int Tp, 
     }
 }
 
+template <int HD>
 __global__ __launch_bounds__(PT) void k_softmax_pv(const int64_t* __restrict__ S, const int64_t* __restrict__ V,
                                                    int64_t ldv, int64_t* __restrict__ O, int64_t ldo, int T, int nh,
-                                                   int nkv, int hd, const int* __restrict__ skip, int* flag) {
+                                                   int nkv, const int* __restrict__ skip, int* flag) {
+    constexpr int hd = HD;
     if (*skip) return;
     extern __shared__ uint8_t sm[];
     const int Tp = (T + 3) & ~3;                                   // P rows padded to 4 keys (16 B)
@@ -148,18 +150,23 @@ __global__ __launch_bounds__(PT) void k_softmax_pv(const int64_t* __restrict__ S
     // ---- PV. Thread (g, d): d = tid % hd, rows g, g+G, ... (G = PT/hd row groups). Each key's
     // (v_hi, 4*v_lo) is read once per thread and used for all its rows; p comes four keys at a time.
     const int64_t* vb = V + (int64_t)b * T * ldv + (int64_t)kvh * hd;
-    switch (hd) {
-        case 16: pv_rows<1, 16>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad); break;
-        case 32: pv_rows<2, 32>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad); break;
-        case 64: pv_rows<4, 64>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad); break;
-        case 128: pv_rows<8, 128>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad); break;
-        default: pv_rows<16, 256>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad); break;
-    }
+    pv_rows<PR * HD / PT, HD>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad);
     __syncthreads();
     if (s_bad && threadIdx.x == 0) atomicOr(flag, 1);
 }
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+template <int HD>
+void launch_pv(dim3 grid, size_t smem, const int64_t* scores, const int64_t* v, int64_t ldv, int64_t* out, int64_t ldo,
+               int T, int nh, int nkv, int* flag, cudaStream_t st) {
+    static size_t configured = 0;
+    if (smem > 32 * 1024 && smem > configured) {  // opt in well before 48 KB (static smem adds to it)
+        cudaFuncSetAttribute(k_softmax_pv<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        configured = smem;
+    }
+    k_softmax_pv<HD><<<grid, PT, smem, st>>>(scores, v, ldv, out, ldo, T, nh, nkv, flag, flag);
+}
 }  // namespace
 
 size_t attention_tc_workspace(int B, int T, int nh, int nkv, int hd) {
@@ -198,13 +205,14 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     tc::split_heads(k, ldk, B, T, nkv, hd, tk, kpad, kp, flag, st);
     tc::launch_scores(mq, mk, B, T, nh, nkv, tk, kpad, score_shift, sqrt_hd, mode, window, scores, flag, err, st);
     const size_t smem = softmax_pv_smem(T, hd);
-    static size_t configured = 0;
-    if (smem > 32 * 1024 && smem > configured) {  // opt in well before 48 KB (static smem adds to it)
-        cudaFuncSetAttribute(k_softmax_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured = smem;
-    }
     dim3 grid((unsigned)((T + PR - 1) / PR), (unsigned)nh, (unsigned)B);
-    k_softmax_pv<<<grid, PT, smem, st>>>(scores, v, ldv, out, ldo, T, nh, nkv, hd, flag, flag);
+    switch (hd) {
+        case 16: launch_pv<16>(grid, smem, scores, v, ldv, out, ldo, T, nh, nkv, flag, st); break;
+        case 32: launch_pv<32>(grid, smem, scores, v, ldv, out, ldo, T, nh, nkv, flag, st); break;
+        case 64: launch_pv<64>(grid, smem, scores, v, ldv, out, ldo, T, nh, nkv, flag, st); break;
+        case 128: launch_pv<128>(grid, smem, scores, v, ldv, out, ldo, T, nh, nkv, flag, st); break;
+        default: launch_pv<256>(grid, smem, scores, v, ldv, out, ldo, T, nh, nkv, flag, st); break;
+    }
     // the exact kernel redoes the whole call when anything fell outside the fast ranges
     attention(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, score_shift, sqrt_hd, mode, window, st, flag);
     return 6;

@@ -97,17 +97,33 @@ SLX_DEV int64_t fixed_exp30(int64_t x) {
     if (k > 62) return INT64_MAX;
     if (k < -40) return 0;
     const int64_t one = 1LL << 30;
-    int64_t term = one, sum = one;
+    int64_t sum = one;
+    if (r >= 0 && r < ln2) {
+        // After range reduction 0 <= r < ln2 < 2^30 and every term stays <= 2^30, so term * r fits
+        // 60 bits and ((term * r) >> 30) / n is the exact quotient in 32-bit arithmetic.
+        uint32_t term = (uint32_t)one;
+        const uint32_t rr = (uint32_t)r;
+        uint32_t s32 = (uint32_t)one;  // e^r * 2^30 < 2^31
 #pragma unroll
-    for (int n = 1; n <= 14; n++) {
-        if (term >= 0 && r >= 0 && __umul64hi((uint64_t)term, (uint64_t)r) == 0) {
-            uint64_t p = (uint64_t)term * (uint64_t)r;
-            term = (int64_t)((p >> 30) / (uint64_t)n);
-        } else {
-            term = lo64(((i128)term * r) / ((i128)n << 30));
+        for (int n = 1; n <= 14; n++) {
+            term = (uint32_t)(((uint64_t)term * rr) >> 30) / (uint32_t)n;
+            s32 += term;
+            if (term == 0 && n > 4) break;
         }
-        sum = wadd(sum, term);
-        if (term == 0 && n > 4) break;
+        sum = (int64_t)s32;
+    } else {
+        int64_t term = one;
+#pragma unroll
+        for (int n = 1; n <= 14; n++) {
+            if (term >= 0 && r >= 0 && __umul64hi((uint64_t)term, (uint64_t)r) == 0) {
+                uint64_t p = (uint64_t)term * (uint64_t)r;
+                term = (int64_t)((p >> 30) / (uint64_t)n);
+            } else {
+                term = lo64(((i128)term * r) / ((i128)n << 30));
+            }
+            sum = wadd(sum, term);
+            if (term == 0 && n > 4) break;
+        }
     }
     if (k >= 0) {
         if (k >= 63 || sum > (INT64_MAX >> k)) return INT64_MAX;
@@ -116,28 +132,6 @@ SLX_DEV int64_t fixed_exp30(int64_t x) {
     int sh = (int)(-k);
     if (sh >= 63) return 0;
     return sum >> sh;
-}
-
-// Truncating num / d for d >= 1 with rd = 1.0 / d: a double estimate corrected to the exact
-// quotient by its integer remainder. Used when |num| < 2^62 and the quotient is below 2^50, where
-// the estimate is within one of the quotient; any other case divides in Int128.
-SLX_DEV int64_t div_trunc(i128 num, int64_t d, double rd) {
-    const i128 lim = (i128)1 << 62;
-    if (num > -lim && num < lim) {
-        const int64_t n = (int64_t)num;
-        const uint64_t an = n < 0 ? (uint64_t)(-n) : (uint64_t)n;
-        if ((an >> 50) < (uint64_t)d || d >= (1LL << 12)) {
-            const double qd = (double)an * rd;
-            if (qd < 1125899906842624.0) {  // 2^50
-                int64_t q = (int64_t)qd;
-                int64_t r = (int64_t)an - q * d;
-                while (r < 0) { q--; r += d; }
-                while (r >= d) { q++; r -= d; }
-                return n < 0 ? -q : q;
-            }
-        }
-    }
-    return lo64(num / (i128)d);
 }
 
 // C# long / long for a positive divisor d with rd = 1.0 / d: exact (double estimate corrected by
