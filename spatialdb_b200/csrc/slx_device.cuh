@@ -134,6 +134,28 @@ SLX_DEV int64_t fixed_exp30(int64_t x) {
     return sum >> sh;
 }
 
+// Truncating num / d for d >= 1 with rd = 1.0 / d: a double estimate corrected to the exact
+// quotient by its integer remainder. Used when |num| < 2^62 and the quotient is below 2^50, where
+// the estimate is within one of the quotient; any other case divides in Int128.
+SLX_DEV int64_t div_trunc(i128 num, int64_t d, double rd) {
+    const i128 lim = (i128)1 << 62;
+    if (num > -lim && num < lim) {
+        const int64_t n = (int64_t)num;
+        const uint64_t an = n < 0 ? (uint64_t)(-n) : (uint64_t)n;
+        if ((an >> 50) < (uint64_t)d) {
+            const double qd = (double)an * rd;
+            if (qd < 1125899906842624.0) {  // 2^50
+                int64_t q = (int64_t)qd;
+                int64_t r = (int64_t)an - q * d;
+                while (r < 0) { q--; r += d; }
+                while (r >= d) { q++; r -= d; }
+                return n < 0 ? -q : q;
+            }
+        }
+    }
+    return lo64(num / (i128)d);
+}
+
 // C# long / long for a positive divisor d with rd = 1.0 / d: exact (double estimate corrected by
 // the integer remainder) when |x| < 2^52, cs_div64 otherwise.
 SLX_DEV int64_t div_small(int64_t x, int64_t d, double rd) {
