@@ -1,0 +1,203 @@
+// k_gemv.cu -- exact decode-shaped GEMV (M <= 8 rows) straight from packed Q4_0 / Q8_0 blocks.
+//
+// IntegerMatMul.MatMul with the encoder's composite weights (Math/IntegerMatMul.cs:37-76,
+// IntegerTransformerSource.Q): w = (long)(d * q * 2^30). For a finite f16 scale d the product
+// d*q*2^30 is an integer, so w = D * q with D = (long)(d * 2^30), and a block's contribution is
+//     sum_{k in block} a_k * w_k = D * sum_k a_k q_k.
+// The inner sum runs on dp4a over the 5 balanced base-256 digits of the activations
+// (a = sum_i a_i 256^i, |a_i q| <= 2^14, 32 terms per block: exact int32), combined into an
+// int64 per block and multiplied by D into the Int128 accumulator. A non-finite scale makes every
+// composite of its block long.MinValue, handled as D = long.MinValue with q = 1 for each element.
+// Weights are read once from HBM: the lanes of a warp take consecutive 18- or 34-byte blocks
+// (2-byte aligned, read as 16-bit words) of NC output columns, so a warp streams contiguous bytes;
+// the activation digits (a few KB) stay in L1/L2 and each block's digits serve all NC columns.
+// Rows whose activations need a sixth digit raise the overflow word, and the exact kernel (gated
+// on it) computes the call instead.
+#include "slx_device.cuh"
+#include "slx_kernels.h"
+
+namespace slx {
+namespace {
+
+constexpr int GV_THREADS = 256;
+constexpr int ND = 5;  // activation digits
+
+// Activation digits for the GEMV: dig[m][i][k] (int8) in the element order a block's 32-bit
+// words present: for Q4_0 word j of a block carries elements (8j, 8j+2, 8j+4, 8j+6) in its low
+// nibbles and (8j+1, ..., 8j+7) in its high nibbles; Q8_0 words carry elements in order.
+// Also bsum[m][i][blk] = sum of digit i over the block (for the Q4_0 offset of 8).
+__global__ void k_gemv_prep(const int64_t* __restrict__ A, int64_t lda, int M, int K, int q4, int8_t* __restrict__ dig,
+                            int* __restrict__ bsum, int* overflow) {
+    const int nb = K / 32;
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;  // over M * nb blocks
+    if (idx >= M * nb) return;
+    const int m = idx / nb, blk = idx % nb;
+    int8_t d[ND][32];
+    int sum[ND] = {0, 0, 0, 0, 0};
+    bool bad = false;
+    for (int e = 0; e < 32; e++) {
+        int64_t x = A[(int64_t)m * lda + (int64_t)blk * 32 + e];
+        // position of element e inside the block's byte stream
+        int pos;
+        if (q4) {
+            const int j = e >> 3, r = e & 7;          // word j, r-th element of the word
+            pos = j * 8 + ((r & 1) ? 4 : 0) + (r >> 1);  // even elements first (low nibbles), then odd
+        } else {
+            pos = e;
+        }
+#pragma unroll
+        for (int i = 0; i < ND; i++) {
+            int dd = (int)(((uint64_t)x + 128u) & 255u) - 128;
+            x = (x - dd) >> 8;
+            d[i][pos] = (int8_t)dd;
+            sum[i] += dd;
+        }
+        bad |= x != 0;
+    }
+    if (bad) atomicOr(overflow, 1);
+    for (int i = 0; i < ND; i++) {
+        int8_t* dst = dig + ((int64_t)m * ND + i) * K + (int64_t)blk * 32;
+        for (int e = 0; e < 32; e++) dst[e] = d[i][e];
+        bsum[((int64_t)m * ND + i) * nb + blk] = sum[i];
+    }
+}
+
+SLX_DEV int dp4a_su(int a_signed, unsigned b_unsigned, int c) {
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a_signed), "r"(b_unsigned), "r"(c));
+    return d;
+}
+
+// One block's 8 words of 4 bytes: Q4_0 nibbles unpacked to (low nibbles, high nibbles) of 4 words,
+// Q8_0 signed bytes as they are. Returns the block's scale bits.
+template <bool Q4>
+SLX_DEV uint16_t load_block(const uint8_t* __restrict__ blk, uint32_t (&w)[8]) {
+    const uint16_t* h = (const uint16_t*)blk;
+    const uint16_t scale = h[0];
+    if (Q4) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t x = (uint32_t)h[1 + 2 * j] | ((uint32_t)h[2 + 2 * j] << 16);
+            w[2 * j] = x & 0x0F0F0F0Fu;             // elements 8j, 8j+2, 8j+4, 8j+6 (nibble values 0..15)
+            w[2 * j + 1] = (x >> 4) & 0x0F0F0F0Fu;  // elements 8j+1, ..., 8j+7
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) w[j] = (uint32_t)h[1 + 2 * j] | ((uint32_t)h[2 + 2 * j] << 16);
+    }
+    return scale;
+}
+
+// Warp = NC output columns; lanes take blocks blk = lane, lane+32, ... of those columns, so each
+// block's activation digits are loaded once and used for all NC columns.
+template <bool Q4, int MM, int NC>
+__global__ __launch_bounds__(GV_THREADS) void k_gemv(const uint8_t* __restrict__ W, int N, int K, const int8_t* __restrict__ dig,
+                                                     const int* __restrict__ bsum, int64_t* __restrict__ C, int64_t ldc,
+                                                     int shift, const int* __restrict__ skip) {
+    if (*skip) return;
+    constexpr int BB = Q4 ? 18 : 34;
+    const int nb = K / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = (blockIdx.x * (GV_THREADS / 32) + warp) * NC;
+    if (n0 >= N) return;
+    u128 acc[MM][NC];
+#pragma unroll
+    for (int m = 0; m < MM; m++)
+#pragma unroll
+        for (int c = 0; c < NC; c++) acc[m][c] = 0;
+    for (int blk = lane; blk < nb; blk += 32) {
+        uint32_t w[NC][8];
+        int64_t D[NC];
+        bool fin[NC];
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            const int n = min(n0 + c, N - 1);
+            const uint16_t sbits = load_block<Q4>(W + ((int64_t)n * nb + blk) * BB, w[c]);
+            const float d = h2f(sbits);
+            fin[c] = isfinite(d);
+            D[c] = fin[c] ? (int64_t)((double)d * 1073741824.0) : INT64_MIN;
+        }
+#pragma unroll
+        for (int m = 0; m < MM; m++) {
+            int64_t S[NC];
+#pragma unroll
+            for (int c = 0; c < NC; c++) S[c] = 0;
+#pragma unroll
+            for (int i = ND - 1; i >= 0; i--) {
+                const int8_t* dg = dig + ((int64_t)m * ND + i) * K + (int64_t)blk * 32;
+                const int4 a0 = __ldg((const int4*)dg), a1 = __ldg((const int4*)(dg + 16));
+                const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const int bs = __ldg(bsum + ((int64_t)m * ND + i) * nb + blk);
+#pragma unroll
+                for (int c = 0; c < NC; c++) {
+                    int p = 0;
+#pragma unroll
+                    for (int j = 0; j < 8; j++) p = Q4 ? dp4a_su(av[j], w[c][j], p) : __dp4a(av[j], (int)w[c][j], p);
+                    if (Q4) p -= 8 * bs;
+                    if (!fin[c]) p = bs;  // every composite of the block is long.MinValue
+                    S[c] = S[c] * 256 + p;  // digits combined high to low: |S| < 2^59
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < NC; c++) acc[m][c] += (u128)((i128)S[c] * D[c]);
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MM; m++)
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            const u128 v = warp_sum_u128(acc[m][c]);
+            if (lane == 0 && n0 + c < N)
+                C[(int64_t)m * ldc + n0 + c] = shift > 0 ? lo64(sar128((i128)v, shift)) : lo64((i128)v);
+        }
+}
+
+template <bool Q4, int MM, int NC>
+void launch_one(const uint8_t* w, int N, int K, const int8_t* dig, const int* bsum, int64_t* c, int64_t ldc, int shift,
+                const int* skip, cudaStream_t st) {
+    const int cols_per_block = (GV_THREADS / 32) * NC;
+    dim3 grid((unsigned)((N + cols_per_block - 1) / cols_per_block));
+    k_gemv<Q4, MM, NC><<<grid, GV_THREADS, 0, st>>>(w, N, K, dig, bsum, c, ldc, shift, skip);
+}
+
+template <bool Q4>
+void launch_gemv_m(int M, const uint8_t* w, int N, int K, const int8_t* dig, const int* bsum, int64_t* c, int64_t ldc,
+                   int shift, const int* skip, cudaStream_t st) {
+    switch (M) {
+        case 1: launch_one<Q4, 1, 4>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
+        case 2: launch_one<Q4, 2, 4>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
+        case 3: launch_one<Q4, 3, 2>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
+        case 4: launch_one<Q4, 4, 2>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
+        case 5: launch_one<Q4, 5, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
+        case 6: launch_one<Q4, 6, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
+        case 7: launch_one<Q4, 7, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
+        default: launch_one<Q4, 8, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
+    }
+}
+
+}  // namespace
+
+bool gemv_supported(const WDesc& w, int M) {
+    return M >= 1 && M <= 8 && w.mode == 0 && (w.dtype == DT_Q4_0 || w.dtype == DT_Q8_0) && w.K % 32 == 0 &&
+           w.nblocks * 32 >= w.N * w.K;
+}
+
+size_t gemv_workspace(int M, int K) { return 256 + (size_t)M * ND * K + (size_t)M * ND * (K / 32) * 4 + 256; }
+
+int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws,
+               cudaStream_t st) {
+    const int K = (int)w.K, N = (int)w.N, nb = K / 32;
+    int* flag = (int*)ws;
+    int8_t* dig = (int8_t*)ws + 256;
+    int* bsum = (int*)(dig + (((size_t)M * ND * K + 255) & ~(size_t)255));
+    cudaMemsetAsync(flag, 0, sizeof(int), st);
+    k_gemv_prep<<<(M * nb + 127) / 128, 128, 0, st>>>(a, lda, M, K, w.dtype == DT_Q4_0, dig, bsum, flag);
+    if (w.dtype == DT_Q4_0)
+        launch_gemv_m<true>(M, w.data, N, K, dig, bsum, c, ldc, shift, flag, st);
+    else
+        launch_gemv_m<false>(M, w.data, N, K, dig, bsum, c, ldc, shift, flag, st);
+    gemm_exact(a, lda, M, K, w, c, ldc, shift, nullptr, 0, st, flag);
+    return 3;
+}
+
+}  // namespace slx

@@ -78,3 +78,29 @@ def test_tc_exact_integer_weights(ctx):
     raw = (w.astype(np.float64) * 2.0 ** -30).astype(np.float32).reshape(-1).view(np.uint8)
     got = slx.matmul_q30(a, synth.F32, raw, N, shift=0, ctx=ctx)
     np.testing.assert_array_equal(got, a @ w.T)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8])
+@pytest.mark.parametrize("dtype", [synth.Q4_0, synth.Q8_0])
+@pytest.mark.parametrize("K,N", [(64, 37), (4096, 300), (1024, 1030)])
+def test_gemv_matches_oracle(ctx, oracle, M, dtype, K, N):
+    """Decode-shaped calls (M <= 8, long composite) take the packed-block GEMV."""
+    rng = np.random.default_rng(M * 131 + K + N + dtype)
+    raw = _raw(dtype, rng, N * K)
+    a = rng.integers(-(1 << 37), 1 << 37, (M, K), dtype=np.int64)
+    got = slx.matmul_q30(a, dtype, raw, N, shift=30, ctx=ctx)
+    np.testing.assert_array_equal(got, _ref(oracle, a, dtype, raw, N, False, 30))
+
+
+def test_gemv_non_finite_scales_and_overflow(ctx, oracle):
+    rng = np.random.default_rng(77)
+    M, K, N = 2, 256, 40
+    raw = synth.random_q4_0(rng, N * K).reshape(-1, 18)
+    raw[3, 0:2] = np.frombuffer(np.float16(np.inf).tobytes(), np.uint8)
+    raw[9, 0:2] = np.frombuffer(np.float16(np.nan).tobytes(), np.uint8)
+    raw[11, 0:2] = np.frombuffer(np.float16(-np.inf).tobytes(), np.uint8)
+    raw = raw.reshape(-1)
+    a = rng.integers(-(1 << 30), 1 << 30, (M, K), dtype=np.int64)
+    np.testing.assert_array_equal(slx.matmul_q30(a, synth.Q4_0, raw, N, ctx=ctx), _ref(oracle, a, synth.Q4_0, raw, N, False, 30))
+    a[1, 5] = 1 << 44  # beyond 5 digits: exact fallback
+    np.testing.assert_array_equal(slx.matmul_q30(a, synth.Q4_0, raw, N, ctx=ctx), _ref(oracle, a, synth.Q4_0, raw, N, False, 30))
