@@ -104,6 +104,98 @@ class Clocks:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def gemv_bench(ctx, torch, stream, iters: int = 200) -> dict:
+    """Decode-shaped dequant+matmul microbench: exact GEMV on packed Q4_0 / Q8_0 blocks, K 4096 x
+    N 11008, M = 1 and 8 rows of Q30 activations (fp32 N(0,1) quantized as QuantizeFromFloat).
+    Distinct weight copies are rotated so their total exceeds L2 and every call streams from HBM.
+    Time per launch of the GEMV kernel from the library's CUDA events on the launch stream."""
+    import ctypes
+
+    import numpy as np
+
+    from spatialdb_b200 import synth
+    from spatialdb_b200._lib import KernelStat
+
+    lib = ctx._lib
+    hbm = measured_peaks()["hbm_gbs"]
+    K, N = 4096, 11008
+    out = {"shape": f"K {K} x N {N}", "l2": "weight copies rotated, total > 300 MB"}
+    rng = np.random.default_rng(11)
+    for name, dtype in (("q4_0", synth.Q4_0), ("q8_0", synth.Q8_0)):
+        raw = synth.random_q4_0(rng, N * K) if dtype == synth.Q4_0 else synth.random_q8_0(rng, N * K)
+        wb = raw.size
+        copies = max(2, -(-300_000_000 // wb))
+        dev = [torch.from_numpy(raw).cuda() for _ in range(copies)]
+        for M in (1, 8):
+            x = torch.randn(M, K, dtype=torch.float32, generator=torch.Generator().manual_seed(M))
+            a = torch.trunc(x.double() * 2.0 ** 30).long().cuda()
+            c = torch.empty((M, N), dtype=torch.int64, device="cuda")
+
+            def call(i):
+                st_ = lib.slx_matmul_q30_device(ctx._h, ctypes.c_void_p(a.data_ptr()), M, K, dtype,
+                                                ctypes.c_void_p(dev[i % copies].data_ptr()), wb, N, 0, 30, 30,
+                                                ctypes.c_void_p(c.data_ptr()), ctypes.c_void_p(stream.cuda_stream))
+                if st_:
+                    raise RuntimeError(lib.slx_last_error(ctx._h))
+
+            for i in range(10):
+                call(i)
+            torch.cuda.synchronize()
+            lib.slx_profile_begin(ctx._h)
+            for i in range(iters):
+                call(i)
+            torch.cuda.synchronize()
+            stats = (KernelStat * 16)()
+            n = ctypes.c_int(0)
+            lib.slx_profile_end(ctx._h, stats, 16, ctypes.byref(n))
+            cls = {s_.name.decode(): s_ for s_ in stats[: n.value]}
+            g = cls["gemv"]
+            per_ms = g.ms / g.launches
+            moved = wb + M * K * 8 + M * N * 8
+            gbs = moved / (per_ms / 1000.0) / 1e9
+            call_ms = sum(s_.ms for s_ in cls.values()) / iters
+            out[f"{name}_m{M}"] = {"us_per_launch": 1000 * per_ms, "gbs": gbs, "frac_of_measured_hbm": gbs / hbm,
+                                   "bytes_per_launch": moved, "us_per_call_all_kernels": 1000 * call_ms}
+        del dev
+    return out
+
+
+def gemma_bench(ctx, decode_b1: int = 128, decode_b16: int = 8) -> dict:
+    """Gemma-2B-shaped causal LM (18 layers, d 2048, 8 query / 1 KV head of 256, GeGLU-width
+    SiLU FFN 16384, vocab 256000, Q4_0 projections and embeddings, F16 norms): a 512-token prompt,
+    then greedy tokens with a full re-forward per token exactly as the reference's Generate does
+    (its leaky causal mask rules out a KV cache)."""
+    import numpy as np
+
+    import spatialdb_b200 as slx
+    from spatialdb_b200 import synth
+
+    shape = synth.CausalShape()
+    path = synth.cached("gemma2b_shape_q4_0_f16norm_seed5.gguf",
+                        lambda p: synth.write_causal(p, shape, synth.Q4_0, synth.F16, seed=5, eos=shape.vocab - 1))
+    t0 = time.perf_counter()
+    m = slx.IntegerCausalSource.load(path, ctx=ctx)
+    load_s = time.perf_counter() - t0
+    rng = np.random.default_rng(21)
+    res = {"model": "gemma 18L d2048 8q/1kv hd256 F16384 V256000 Q4_0", "prompt": 512, "load_s": load_s}
+    p1 = rng.integers(0, shape.vocab - 1, (1, 512)).astype(np.int32)
+    m.generate(p1, 1)  # warm-up: workspaces at full size
+    t0 = time.perf_counter()
+    g = m.generate(p1, decode_b1)
+    dt = time.perf_counter() - t0
+    res["batch1"] = {"new_tokens": int(len(g[0])), "s": dt, "tok_per_s": len(g[0]) / dt}
+    p16 = rng.integers(0, shape.vocab - 1, (16, 512)).astype(np.int32)
+    m.generate(p16, 1)
+    t0 = time.perf_counter()
+    g = m.generate(p16, decode_b16)
+    dt = time.perf_counter() - t0
+    n16 = sum(len(x) for x in g)
+    res["batch16"] = {"new_tokens": int(n16), "steps": decode_b16, "s": dt, "tok_per_s": n16 / dt,
+                      "note": f"first {decode_b16} of the configuration's 128 steps (context 512..{511 + decode_b16})"}
+    m.close()
+    return res
+
+
 def cpu_baseline(path: str, sample_seqs: int, seed: int = 99) -> dict:
     """The oracle (C++ restatement of the reference CPU path, OpenMP over output columns as the
     reference's Parallel.For) on a bounded sample of the workload, all host threads."""
@@ -282,6 +374,17 @@ def run_ours(args) -> None:
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(path, args.cpu_sample)
+        if world == 1 and not args.skip_secondary:
+            sec = {}
+            try:
+                sec["gemv"] = gemv_bench(ctx, torch, stream)
+            except Exception as e:  # reported, never silently dropped
+                sec["gemv"] = {"error": repr(e)}
+            try:
+                sec["gemma_decode"] = gemma_bench(ctx)
+            except Exception as e:
+                sec["gemma_decode"] = {"error": repr(e)}
+            line["secondary"] = sec
         print(json.dumps(line), flush=True)
     del model, ctx
     if dist:
@@ -308,6 +411,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-sample", type=int, default=2, help="sequences in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-secondary", action="store_true", help="skip the GEMV and Gemma decode measurements")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

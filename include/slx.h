@@ -107,7 +107,10 @@ slx_status slx_causal_generate(slx_model* model, const int32_t* ids, int B, int 
  * forms it. Host buffers. */
 slx_status slx_matmul_q30(slx_ctx* ctx, const int64_t* a, int M, int K, int dtype, const uint8_t* w_raw,
                           int64_t w_bytes, int N, int half_composite, int scale_bits, int shift, int64_t* c);
-/* Same on device buffers (a, w_raw, c device pointers), queued on `stream`. */
+/* Same on device buffers (a, w_raw, c device pointers), queued on `stream`. Decode-shaped calls
+ * (M <= 8, Q4_0 / Q8_0, long composite, K a multiple of 32) stream the packed blocks and return
+ * once queued; other shapes build the weight's tensor-core digit planes for the call and return
+ * after the stream has finished with them. */
 slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K, int dtype, const uint8_t* d_w,
                                  int64_t w_bytes, int N, int half_composite, int scale_bits, int shift, int64_t* d_c,
                                  void* stream);
@@ -140,7 +143,7 @@ slx_status slx_attention(slx_ctx* ctx, const int64_t* q, const int64_t* k, const
 /* No reference counterpart (the reference times with Stopwatch, SparseLattice.Perf/Program.cs:817-830).
  * Per kernel class, the library's launches on ctx between begin and end, their device time from
  * CUDA events recorded on the launch stream, and the algorithmic multiply-accumulates they
- * performed. Classes: gemm, attention, norm, rope, ffn_gate, embed, pool, add, argmax. */
+ * performed. Classes: gemm, attention, norm, rope, ffn_gate, embed, pool, add, argmax, gemv, split, fallback. */
 typedef struct slx_kernel_stat {
     char name[24];
     int64_t launches;

@@ -4,6 +4,7 @@
 // Int128 arithmetic, truncating division, flooring shifts). The tensor-core GEMM in k_gemm_tc.cu
 // replaces gemm_exact on the hot path; this file keeps the exact general path that any
 // activation range falls back to.
+#include <algorithm>
 #include <cstdio>
 
 #include "slx_device.cuh"
@@ -27,8 +28,10 @@ __global__ __launch_bounds__(256) void k_gemm_exact(const int64_t* __restrict__ 
     __shared__ int64_t As[GBK][GBM + 1];
     __shared__ int64_t Ws[GBK][GBN + 1];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const int m0 = blockIdx.y * GBM, n0 = blockIdx.x * GBN;
     const int N = (int)W.N;
+    const int ntn = (N + GBN - 1) / GBN, ntiles = ntn * ((M + GBM - 1) / GBM);
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int m0 = (tile / ntn) * GBM, n0 = (tile % ntn) * GBN;
     u128 acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; i++)
@@ -79,6 +82,8 @@ __global__ __launch_bounds__(256) void k_gemm_exact(const int64_t* __restrict__ 
             C[(int64_t)m * ldc + n] = v;
         }
     }
+    __syncthreads();  // the next tile reuses As / Ws
+    }
 }
 
 __global__ void k_weight_q30(WDesc W, int64_t n, int64_t* out) {
@@ -90,8 +95,10 @@ __global__ void k_weight_q30(WDesc W, int64_t n, int64_t* out) {
 int gemm_exact(const int64_t* a, int64_t lda, int M, int K, const WDesc& w, int64_t* c, int64_t ldc, int shift,
                 const int64_t* r, int64_t ldr, cudaStream_t st, const int* only_if) {
     if (M <= 0 || w.N <= 0) return 0;
-    dim3 grid((unsigned)((w.N + GBN - 1) / GBN), (unsigned)((M + GBM - 1) / GBM));
-    k_gemm_exact<<<grid, 256, 0, st>>>(a, lda, M, K, w, c, ldc, shift, r, ldr, only_if);
+    const int64_t ntiles = ((w.N + GBN - 1) / GBN) * (int64_t)((M + GBM - 1) / GBM);
+    // Gated behind a faster path it usually does nothing, so a small grid walks the tiles.
+    const int64_t grid = only_if ? std::min<int64_t>(ntiles, 2 * 148) : ntiles;
+    k_gemm_exact<<<(unsigned)grid, 256, 0, st>>>(a, lda, M, K, w, c, ldc, shift, r, ldr, only_if);
     return 1;
 }
 
@@ -406,15 +413,18 @@ __global__ __launch_bounds__(AW * 32) void k_attention(const int64_t* __restrict
                                                        const int64_t* __restrict__ V, int64_t ldv,
                                                        int64_t* __restrict__ O, int64_t ldo, int T, int nh, int nkv,
                                                        int hd, int score_shift, int64_t sqrt_hd, int mode,
-                                                       int window, const int* __restrict__ only_if) {
+                                                       int window, int B, const int* __restrict__ only_if) {
     if (only_if && *only_if == 0) return;
     extern __shared__ int64_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * AW + warp;
-    const int h = blockIdx.y, b = blockIdx.z;
+    const int nxb = (T + AW - 1) / AW;
+    const int64_t nblocks = (int64_t)nxb * nh * B;
+    for (int64_t blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
+    const int t = (int)(blk % nxb) * AW + warp;
+    const int h = (int)((blk / nxb) % nh), b = (int)(blk / ((int64_t)nxb * nh));
     int64_t* sc = smem + (size_t)warp * (T + hd);
     int64_t* qrow = sc + T;
-    if (t >= T) return;
+    if (t >= T) continue;
     const int kvh = h / (nh / nkv);
     const int64_t rowq = (int64_t)b * T + t;
     for (int d = lane; d < hd; d += 32) qrow[d] = Q[rowq * ldq + (int64_t)h * hd + d];
@@ -464,6 +474,8 @@ __global__ __launch_bounds__(AW * 32) void k_attention(const int64_t* __restrict
         for (int s = 0; s < T; s++) acc = wadd(acc, lo64(sar128((i128)sc[s] * vb[(int64_t)s * ldv + d], 30)));
         orow[d] = acc;
     }
+    __syncwarp();  // the next query row reuses this warp's scores
+    }
 }
 }  // namespace
 
@@ -477,9 +489,10 @@ int attention(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, cons
         cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         configured = smem;
     }
-    dim3 grid((unsigned)((T + AW - 1) / AW), (unsigned)nh, (unsigned)B);
-    k_attention<<<grid, AW * 32, smem, st>>>(q, ldq, k, ldk, v, ldv, out, ldo, T, nh, nkv, hd, score_shift, sqrt_hd,
-                                             mode, window, only_if);
+    const int64_t nblocks = (int64_t)((T + AW - 1) / AW) * nh * B;
+    const int64_t grid = only_if ? std::min<int64_t>(nblocks, 4 * 148) : nblocks;
+    k_attention<<<(unsigned)grid, AW * 32, smem, st>>>(q, ldq, k, ldk, v, ldv, out, ldo, T, nh, nkv, hd, score_shift,
+                                                      sqrt_hd, mode, window, B, only_if);
     return 1;
 }
 

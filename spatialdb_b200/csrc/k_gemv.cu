@@ -184,20 +184,47 @@ bool gemv_supported(const WDesc& w, int M) {
 
 size_t gemv_workspace(int M, int K) { return 256 + (size_t)M * ND * K + (size_t)M * ND * (K / 32) * 4 + 256; }
 
+namespace {
+struct GemvWs {
+    int* flag;
+    int8_t* dig;
+    int* bsum;
+};
+GemvWs gemv_ws(void* ws, int M, int K) {
+    GemvWs g;
+    g.flag = (int*)ws;
+    g.dig = (int8_t*)ws + 256;
+    g.bsum = (int*)(g.dig + (((size_t)M * ND * K + 255) & ~(size_t)255));
+    return g;
+}
+}  // namespace
+
+int gemv_prep(const int64_t* a, int64_t lda, int M, const WDesc& w, void* ws, cudaStream_t st) {
+    const int K = (int)w.K, nb = K / 32;
+    GemvWs g = gemv_ws(ws, M, K);
+    cudaMemsetAsync(g.flag, 0, sizeof(int), st);
+    k_gemv_prep<<<(M * nb + 127) / 128, 128, 0, st>>>(a, lda, M, K, w.dtype == DT_Q4_0, g.dig, g.bsum, g.flag);
+    return 1;
+}
+
+int gemv_main(int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws, cudaStream_t st) {
+    const int K = (int)w.K, N = (int)w.N;
+    GemvWs g = gemv_ws(ws, M, K);
+    if (w.dtype == DT_Q4_0)
+        launch_gemv_m<true>(M, w.data, N, K, g.dig, g.bsum, c, ldc, shift, g.flag, st);
+    else
+        launch_gemv_m<false>(M, w.data, N, K, g.dig, g.bsum, c, ldc, shift, g.flag, st);
+    return 1;
+}
+
 int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws,
                cudaStream_t st) {
-    const int K = (int)w.K, N = (int)w.N, nb = K / 32;
-    int* flag = (int*)ws;
-    int8_t* dig = (int8_t*)ws + 256;
-    int* bsum = (int*)(dig + (((size_t)M * ND * K + 255) & ~(size_t)255));
-    cudaMemsetAsync(flag, 0, sizeof(int), st);
-    k_gemv_prep<<<(M * nb + 127) / 128, 128, 0, st>>>(a, lda, M, K, w.dtype == DT_Q4_0, dig, bsum, flag);
-    if (w.dtype == DT_Q4_0)
-        launch_gemv_m<true>(M, w.data, N, K, dig, bsum, c, ldc, shift, flag, st);
-    else
-        launch_gemv_m<false>(M, w.data, N, K, dig, bsum, c, ldc, shift, flag, st);
-    gemm_exact(a, lda, M, K, w, c, ldc, shift, nullptr, 0, st, flag);
-    return 3;
+    int n = gemv_prep(a, lda, M, w, ws, st);
+    n += gemv_main(M, w, c, ldc, shift, ws, st);
+    n += gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, nullptr, 0, st, gemv_ws(ws, M, (int)w.K).flag);
+    return n;
 }
+
+const int* gemv_flag(void* ws) { return (const int*)ws; }
 
 }  // namespace slx

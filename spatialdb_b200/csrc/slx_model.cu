@@ -28,8 +28,10 @@
 using namespace slx;
 
 // Kernel classes reported by slx_profile_end.
-enum KClass { KC_GEMM, KC_ATTENTION, KC_NORM, KC_ROPE, KC_FFN_GATE, KC_EMBED, KC_POOL, KC_ADD, KC_ARGMAX, KC_COUNT };
-static const char* kKClassName[KC_COUNT] = {"gemm", "attention", "norm", "rope", "ffn_gate", "embed", "pool", "add", "argmax"};
+enum KClass { KC_GEMM, KC_ATTENTION, KC_NORM, KC_ROPE, KC_FFN_GATE, KC_EMBED, KC_POOL, KC_ADD, KC_ARGMAX, KC_GEMV,
+              KC_SPLIT, KC_FALLBACK, KC_COUNT };
+static const char* kKClassName[KC_COUNT] = {"gemm", "attention", "norm", "rope", "ffn_gate", "embed", "pool", "add",
+                                            "argmax", "gemv", "split", "fallback"};
 
 struct ProfRecord {
     int cls;
@@ -46,6 +48,7 @@ struct slx_ctx {
     int64_t launches = 0;            // kernels queued by the library on this context
     bool prof = false;
     std::vector<ProfRecord> records;
+    GemmWorkspace kws;               // scratch of the kernel-level matmul entry points
     std::vector<cudaEvent_t> event_pool;
     cudaEvent_t event() {
         if (!event_pool.empty()) { cudaEvent_t e = event_pool.back(); event_pool.pop_back(); return e; }
@@ -583,6 +586,7 @@ slx_status slx_destroy(slx_ctx* ctx) {
     cudaFree(ctx->d_flag);
     for (auto& r : ctx->records) { cudaEventDestroy(r.a); cudaEventDestroy(r.b); }
     for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
+    gemm_workspace_free(ctx->kws);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
     return SLX_OK;
@@ -801,6 +805,20 @@ slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K,
     w.mode = half_composite ? 1 : 0;
     w.scale = std::ldexp(1.0, scale_bits);
     cudaStream_t st = pick(ctx, stream);
+    if (gemv_supported(w, M)) {  // decode-shaped: packed-block GEMV, queued without a host sync
+        const size_t need = gemv_workspace(M, K);
+        if (need > ctx->kws.bytes) {
+            gemm_workspace_free(ctx->kws);
+            CK(cudaMalloc(&ctx->kws.p, need));
+            ctx->kws.bytes = need;
+        }
+        RUN(KC_SPLIT, 0, (double)M * K * 8, gemv_prep(d_a, K, M, w, ctx->kws.p, st));
+        RUN(KC_GEMV, (double)M * N * K, (double)gguf_byte_count((uint32_t)dtype, elems) + (double)M * (K + N) * 8,
+            gemv_main(M, w, d_c, N, shift, ctx->kws.p, st));
+        RUN(KC_FALLBACK, 0, 0, gemm_exact(d_a, K, M, K, w, d_c, N, shift, nullptr, 0, st, gemv_flag(ctx->kws.p)));
+        CK(cudaGetLastError());
+        return SLX_OK;
+    }
     // One-off plan: the weight's digit planes are built for this call and released with it.
     GemmPlan plan;
     std::string err;
@@ -898,6 +916,7 @@ slx_status slx_profile_end(slx_ctx* ctx, slx_kernel_stat* stats, int cap, int* n
     if (!ctx || !n) return SLX_EINVAL;
     ctx->prof = false;
     slx_kernel_stat acc[KC_COUNT];
+    static_assert(sizeof(kKClassName) / sizeof(kKClassName[0]) == KC_COUNT, "kernel class names");
     std::memset(acc, 0, sizeof acc);
     for (int c = 0; c < KC_COUNT; c++) snprintf(acc[c].name, sizeof acc[c].name, "%s", kKClassName[c]);
     for (auto& r : ctx->records) {
