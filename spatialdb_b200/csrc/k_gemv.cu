@@ -8,9 +8,9 @@
 // (a = sum_i a_i 256^i, |a_i q| <= 2^14, 32 terms per block: exact int32), combined into an
 // int64 per block and multiplied by D into the Int128 accumulator. A non-finite scale makes every
 // composite of its block long.MinValue, handled as D = long.MinValue with q = 1 for each element.
-// Weights are read once from HBM: the lanes of a warp take consecutive 18- or 34-byte blocks
-// (2-byte aligned, read as 16-bit words) of NC output columns, so a warp streams contiguous bytes;
-// the activation digits (a few KB) stay in L1/L2 and each block's digits serve all NC columns.
+// Weights are read once from HBM with 16-byte copies into shared memory (each warp streams NC
+// output columns' contiguous blocks); the activation digits (a few KB) stay in L1/L2 and each
+// block's digits serve all NC columns.
 // Rows whose activations need a sixth digit raise the overflow word, and the exact kernel (gated
 // on it) computes the call instead.
 #include "slx_device.cuh"
@@ -88,59 +88,106 @@ SLX_DEV uint16_t load_block(const uint8_t* __restrict__ blk, uint32_t (&w)[8]) {
     return scale;
 }
 
-// Warp = NC output columns; lanes take blocks blk = lane, lane+32, ... of those columns, so each
-// block's activation digits are loaded once and used for all NC columns.
+// Warp = NC output columns. The warp streams its columns' packed blocks through shared memory in
+// chunks of 64 blocks with 16-byte cp.async copies (double buffered, so the next chunk is in flight
+// while this one is decoded); lane l decodes blocks l and l+32 of each chunk. Row starts and chunk
+// starts are 16-byte aligned when K is a multiple of 256 (checked by the launcher).
+constexpr int GV_CHUNK = 64;  // blocks per chunk
+
+SLX_DEV void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+                 : "memory");
+}
+SLX_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+SLX_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 template <bool Q4, int MM, int NC>
 __global__ __launch_bounds__(GV_THREADS) void k_gemv(const uint8_t* __restrict__ W, int N, int K, const int8_t* __restrict__ dig,
                                                      const int* __restrict__ bsum, int64_t* __restrict__ C, int64_t ldc,
                                                      int shift, const int* __restrict__ skip) {
     if (*skip) return;
     constexpr int BB = Q4 ? 18 : 34;
+    constexpr int CHB = GV_CHUNK * BB;       // bytes per column chunk (multiple of 16)
+    constexpr int VEC = CHB / 16;            // 16-byte copies per column chunk
+    extern __shared__ __align__(16) uint8_t gv_smem[];
     const int nb = K / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = (blockIdx.x * (GV_THREADS / 32) + warp) * NC;
     if (n0 >= N) return;
+    uint8_t* buf = gv_smem + (size_t)warp * 2 * NC * CHB;  // [2][NC][CHB]
+    const int nchunks = (nb + GV_CHUNK - 1) / GV_CHUNK;
+
+    auto issue = [&](int ch) {
+        uint8_t* dst = buf + (ch & 1) * NC * CHB;
+        const int blocks = min(GV_CHUNK, nb - ch * GV_CHUNK);
+        const int vecs = (blocks * BB + 15) / 16;
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            const int n = min(n0 + c, N - 1);
+            const uint8_t* src = W + ((int64_t)n * nb + (int64_t)ch * GV_CHUNK) * BB;
+            for (int v = lane; v < vecs; v += 32) cp_async16(dst + c * CHB + v * 16, src + v * 16);
+        }
+        cp_async_commit();
+    };
+
     u128 acc[MM][NC];
 #pragma unroll
     for (int m = 0; m < MM; m++)
 #pragma unroll
         for (int c = 0; c < NC; c++) acc[m][c] = 0;
-    for (int blk = lane; blk < nb; blk += 32) {
-        uint32_t w[NC][8];
-        int64_t D[NC];
-        bool fin[NC];
-#pragma unroll
-        for (int c = 0; c < NC; c++) {
-            const int n = min(n0 + c, N - 1);
-            const uint16_t sbits = load_block<Q4>(W + ((int64_t)n * nb + blk) * BB, w[c]);
-            const float d = h2f(sbits);
-            fin[c] = isfinite(d);
-            D[c] = fin[c] ? (int64_t)((double)d * 1073741824.0) : INT64_MIN;
+    issue(0);
+    for (int ch = 0; ch < nchunks; ch++) {
+        if (ch + 1 < nchunks) {
+            issue(ch + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
+        __syncwarp();
+        const uint8_t* cur = buf + (ch & 1) * NC * CHB;
+        const int blocks = min(GV_CHUNK, nb - ch * GV_CHUNK);
 #pragma unroll
-        for (int m = 0; m < MM; m++) {
-            int64_t S[NC];
+        for (int half = 0; half < 2; half++) {
+            const int lb = lane + 32 * half;
+            if (lb >= blocks) break;
+            const int blk = ch * GV_CHUNK + lb;
+            uint32_t w[NC][8];
+            int64_t D[NC];
+            bool fin[NC];
 #pragma unroll
-            for (int c = 0; c < NC; c++) S[c] = 0;
-#pragma unroll
-            for (int i = ND - 1; i >= 0; i--) {
-                const int8_t* dg = dig + ((int64_t)m * ND + i) * K + (int64_t)blk * 32;
-                const int4 a0 = __ldg((const int4*)dg), a1 = __ldg((const int4*)(dg + 16));
-                const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                const int bs = __ldg(bsum + ((int64_t)m * ND + i) * nb + blk);
-#pragma unroll
-                for (int c = 0; c < NC; c++) {
-                    int p = 0;
-#pragma unroll
-                    for (int j = 0; j < 8; j++) p = Q4 ? dp4a_su(av[j], w[c][j], p) : __dp4a(av[j], (int)w[c][j], p);
-                    if (Q4) p -= 8 * bs;
-                    if (!fin[c]) p = bs;  // every composite of the block is long.MinValue
-                    S[c] = S[c] * 256 + p;  // digits combined high to low: |S| < 2^59
-                }
+            for (int c = 0; c < NC; c++) {
+                const uint16_t sbits = load_block<Q4>(cur + c * CHB + lb * BB, w[c]);
+                const float d = h2f(sbits);
+                fin[c] = isfinite(d);
+                D[c] = fin[c] ? (int64_t)((double)d * 1073741824.0) : INT64_MIN;
             }
 #pragma unroll
-            for (int c = 0; c < NC; c++) acc[m][c] += (u128)((i128)S[c] * D[c]);
+            for (int m = 0; m < MM; m++) {
+                int64_t S[NC];
+#pragma unroll
+                for (int c = 0; c < NC; c++) S[c] = 0;
+#pragma unroll
+                for (int i = ND - 1; i >= 0; i--) {
+                    const int8_t* dg = dig + ((int64_t)m * ND + i) * K + (int64_t)blk * 32;
+                    const int4 a0 = __ldg((const int4*)dg), a1 = __ldg((const int4*)(dg + 16));
+                    const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                    const int bs = __ldg(bsum + ((int64_t)m * ND + i) * nb + blk);
+#pragma unroll
+                    for (int c = 0; c < NC; c++) {
+                        int p = 0;
+#pragma unroll
+                        for (int j = 0; j < 8; j++) p = Q4 ? dp4a_su(av[j], w[c][j], p) : __dp4a(av[j], (int)w[c][j], p);
+                        if (Q4) p -= 8 * bs;
+                        if (!fin[c]) p = bs;  // every composite of the block is long.MinValue
+                        S[c] = S[c] * 256 + p;  // digits combined high to low: |S| < 2^59
+                    }
+                }
+#pragma unroll
+                for (int c = 0; c < NC; c++) acc[m][c] += (u128)((i128)S[c] * D[c]);
+            }
         }
+        __syncwarp();  // this buffer is refilled two chunks later
     }
 #pragma unroll
     for (int m = 0; m < MM; m++)
@@ -157,7 +204,13 @@ void launch_one(const uint8_t* w, int N, int K, const int8_t* dig, const int* bs
                 const int* skip, cudaStream_t st) {
     const int cols_per_block = (GV_THREADS / 32) * NC;
     dim3 grid((unsigned)((N + cols_per_block - 1) / cols_per_block));
-    k_gemv<Q4, MM, NC><<<grid, GV_THREADS, 0, st>>>(w, N, K, dig, bsum, c, ldc, shift, skip);
+    const size_t smem = (size_t)(GV_THREADS / 32) * 2 * NC * GV_CHUNK * (Q4 ? 18 : 34);
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(k_gemv<Q4, MM, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        configured = true;
+    }
+    k_gemv<Q4, MM, NC><<<grid, GV_THREADS, smem, st>>>(w, N, K, dig, bsum, c, ldc, shift, skip);
 }
 
 template <bool Q4>
@@ -178,8 +231,8 @@ void launch_gemv_m(int M, const uint8_t* w, int N, int K, const int8_t* dig, con
 }  // namespace
 
 bool gemv_supported(const WDesc& w, int M) {
-    return M >= 1 && M <= 8 && w.mode == 0 && (w.dtype == DT_Q4_0 || w.dtype == DT_Q8_0) && w.K % 32 == 0 &&
-           w.nblocks * 32 >= w.N * w.K;
+    return M >= 1 && M <= 8 && w.mode == 0 && (w.dtype == DT_Q4_0 || w.dtype == DT_Q8_0) && w.K % 256 == 0 &&
+           w.nblocks * 32 >= w.N * w.K && ((uintptr_t)w.data & 15) == 0;
 }
 
 size_t gemv_workspace(int M, int K) { return 256 + (size_t)M * ND * K + (size_t)M * ND * (K / 32) * 4 + 256; }
