@@ -1,8 +1,8 @@
 // k_gemv.cu -- exact decode-shaped GEMV (M <= 8 rows) straight from packed Q4_0 / Q8_0 blocks.
 //
 // IntegerMatMul.MatMul with the encoder's composite weights (Math/IntegerMatMul.cs:37-76,
-// IntegerTransformerSource.Q): w = (long)(d * q * 2^30). For a finite f16 scale d the product
-// d*q*2^30 is an integer, so w = D * q with D = (long)(d * 2^30), and a block's contribution is
+// IntegerTransformerSource.Q): w = (long)(d * q * 2^s). For a finite f16 scale d and s >= 24 the
+// product d*q*2^s is an integer, so w = D * q with D = (long)(d * 2^s), and a block's contribution is
 //     sum_{k in block} a_k * w_k = D * sum_k a_k q_k.
 // The inner sum runs on dp4a over the 5 balanced base-256 digits of the activations
 // (a = sum_i a_i 256^i, |a_i q| <= 2^14, 32 terms per block: exact int32), combined into an
@@ -11,8 +11,8 @@
 // Weights are read once from HBM with 16-byte copies into shared memory (each warp streams NC
 // output columns' contiguous blocks); the activation digits (a few KB) stay in L1/L2 and each
 // block's digits serve all NC columns.
-// Rows whose activations need a sixth digit raise the overflow word, and the exact kernel (gated
-// on it) computes the call instead.
+// If any activation needs a sixth digit, the prep kernel raises the overflow word and every warp
+// takes the Int128 multiply-accumulate path over the composites instead.
 #include "slx_device.cuh"
 #include "slx_kernels.h"
 
@@ -105,10 +105,28 @@ SLX_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) :
 template <bool Q4, int MM, int NC>
 __global__ __launch_bounds__(GV_THREADS) void k_gemv(const uint8_t* __restrict__ W, int N, int K, const int8_t* __restrict__ dig,
                                                      const int* __restrict__ bsum, int64_t* __restrict__ C, int64_t ldc,
-                                                     int shift, const int* __restrict__ skip) {
-    if (*skip) return;
+                                                     int shift, const int* __restrict__ skip,
+                                                     const int64_t* __restrict__ A, int64_t lda, double scale) {
     constexpr int BB = Q4 ? 18 : 34;
     constexpr int CHB = GV_CHUNK * BB;       // bytes per column chunk (multiple of 16)
+    if (*skip) {  // an activation needs a sixth digit: Int128 multiply-accumulate of the composites
+        const int warp_ = threadIdx.x >> 5, lane_ = threadIdx.x & 31;
+        const int nb0 = (blockIdx.x * (GV_THREADS / 32) + warp_) * NC;
+        const int64_t nblk = K / 32;
+        for (int c = 0; c < NC && nb0 + c < N; c++) {
+            for (int m = 0; m < MM; m++) {
+                u128 a128 = 0;
+                for (int k = lane_; k < K; k += 32) {
+                    const int64_t e = (int64_t)(nb0 + c) * K + k;
+                    const int64_t wq = composite(dequant_elem(Q4 ? DT_Q4_0 : DT_Q8_0, W, e, nblk * N), 0, scale);
+                    a128 += (u128)((i128)A[(int64_t)m * lda + k] * wq);
+                }
+                a128 = warp_sum_u128(a128);
+                if (lane_ == 0) C[(int64_t)m * ldc + nb0 + c] = shift > 0 ? lo64(sar128((i128)a128, shift)) : lo64((i128)a128);
+            }
+        }
+        return;
+    }
     constexpr int VEC = CHB / 16;            // 16-byte copies per column chunk
     extern __shared__ __align__(16) uint8_t gv_smem[];
     const int nb = K / 32;
@@ -160,7 +178,7 @@ __global__ __launch_bounds__(GV_THREADS) void k_gemv(const uint8_t* __restrict__
                 const uint16_t sbits = load_block<Q4>(cur + c * CHB + lb * BB, w[c]);
                 const float d = h2f(sbits);
                 fin[c] = isfinite(d);
-                D[c] = fin[c] ? (int64_t)((double)d * 1073741824.0) : INT64_MIN;
+                D[c] = fin[c] ? (int64_t)((double)d * scale) : INT64_MIN;
             }
 #pragma unroll
             for (int m = 0; m < MM; m++) {
@@ -201,7 +219,7 @@ __global__ __launch_bounds__(GV_THREADS) void k_gemv(const uint8_t* __restrict__
 
 template <bool Q4, int MM, int NC>
 void launch_one(const uint8_t* w, int N, int K, const int8_t* dig, const int* bsum, int64_t* c, int64_t ldc, int shift,
-                const int* skip, cudaStream_t st) {
+                const int* skip, const int64_t* a, int64_t lda, double scale, cudaStream_t st) {
     const int cols_per_block = (GV_THREADS / 32) * NC;
     dim3 grid((unsigned)((N + cols_per_block - 1) / cols_per_block));
     const size_t smem = (size_t)(GV_THREADS / 32) * 2 * NC * GV_CHUNK * (Q4 ? 18 : 34);
@@ -210,28 +228,30 @@ void launch_one(const uint8_t* w, int N, int K, const int8_t* dig, const int* bs
         cudaFuncSetAttribute(k_gemv<Q4, MM, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         configured = true;
     }
-    k_gemv<Q4, MM, NC><<<grid, GV_THREADS, smem, st>>>(w, N, K, dig, bsum, c, ldc, shift, skip);
+    k_gemv<Q4, MM, NC><<<grid, GV_THREADS, smem, st>>>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale);
 }
 
 template <bool Q4>
 void launch_gemv_m(int M, const uint8_t* w, int N, int K, const int8_t* dig, const int* bsum, int64_t* c, int64_t ldc,
-                   int shift, const int* skip, cudaStream_t st) {
+                   int shift, const int* skip, const int64_t* a, int64_t lda, double scale, cudaStream_t st) {
     switch (M) {
-        case 1: launch_one<Q4, 1, 4>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
-        case 2: launch_one<Q4, 2, 4>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
-        case 3: launch_one<Q4, 3, 2>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
-        case 4: launch_one<Q4, 4, 2>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
-        case 5: launch_one<Q4, 5, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
-        case 6: launch_one<Q4, 6, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
-        case 7: launch_one<Q4, 7, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
-        default: launch_one<Q4, 8, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, st); break;
+        case 1: launch_one<Q4, 1, 4>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
+        case 2: launch_one<Q4, 2, 4>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
+        case 3: launch_one<Q4, 3, 2>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
+        case 4: launch_one<Q4, 4, 2>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
+        case 5: launch_one<Q4, 5, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
+        case 6: launch_one<Q4, 6, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
+        case 7: launch_one<Q4, 7, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
+        default: launch_one<Q4, 8, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
     }
 }
 
 }  // namespace
 
 bool gemv_supported(const WDesc& w, int M) {
+    // d * 2^s is an integer for every f16 d only when s >= 24 (the smallest subnormal is 2^-24)
     return M >= 1 && M <= 8 && w.mode == 0 && (w.dtype == DT_Q4_0 || w.dtype == DT_Q8_0) && w.K % 256 == 0 &&
+           w.scale >= 16777216.0 &&
            w.nblocks * 32 >= w.N * w.K && ((uintptr_t)w.data & 15) == 0;
 }
 
@@ -260,24 +280,20 @@ int gemv_prep(const int64_t* a, int64_t lda, int M, const WDesc& w, void* ws, cu
     return 1;
 }
 
-int gemv_main(int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws, cudaStream_t st) {
+int gemv_main(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws,
+              cudaStream_t st) {
     const int K = (int)w.K, N = (int)w.N;
     GemvWs g = gemv_ws(ws, M, K);
     if (w.dtype == DT_Q4_0)
-        launch_gemv_m<true>(M, w.data, N, K, g.dig, g.bsum, c, ldc, shift, g.flag, st);
+        launch_gemv_m<true>(M, w.data, N, K, g.dig, g.bsum, c, ldc, shift, g.flag, a, lda, w.scale, st);
     else
-        launch_gemv_m<false>(M, w.data, N, K, g.dig, g.bsum, c, ldc, shift, g.flag, st);
+        launch_gemv_m<false>(M, w.data, N, K, g.dig, g.bsum, c, ldc, shift, g.flag, a, lda, w.scale, st);
     return 1;
 }
 
 int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws,
                cudaStream_t st) {
-    int n = gemv_prep(a, lda, M, w, ws, st);
-    n += gemv_main(M, w, c, ldc, shift, ws, st);
-    n += gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, nullptr, 0, st, gemv_ws(ws, M, (int)w.K).flag);
-    return n;
+    return gemv_prep(a, lda, M, w, ws, st) + gemv_main(a, lda, M, w, c, ldc, shift, ws, st);
 }
-
-const int* gemv_flag(void* ws) { return (const int*)ws; }
 
 }  // namespace slx

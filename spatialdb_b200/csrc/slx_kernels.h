@@ -64,11 +64,10 @@ bool gemv_supported(const WDesc& w, int M);
 size_t gemv_workspace(int M, int K);
 int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws,
                cudaStream_t st);
-// The same in its three parts: activation digits, the GEMV proper, then gemm_exact gated on
-// gemv_flag(ws).
+// The same in its two parts: activation digits, then the GEMV proper (exact for any activations).
 int gemv_prep(const int64_t* a, int64_t lda, int M, const WDesc& w, void* ws, cudaStream_t st);
-int gemv_main(int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws, cudaStream_t st);
-const int* gemv_flag(void* ws);
+int gemv_main(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws,
+              cudaStream_t st);
 
 // Same attention with tensor-core scores (k_attn.cu): digit split of q/k, tcgen05 score GEMM,
 // CUDA-core softmax and per-term PV, and the exact kernel gated behind them for out-of-range

@@ -814,8 +814,7 @@ slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K,
         }
         RUN(KC_SPLIT, 0, (double)M * K * 8, gemv_prep(d_a, K, M, w, ctx->kws.p, st));
         RUN(KC_GEMV, (double)M * N * K, (double)gguf_byte_count((uint32_t)dtype, elems) + (double)M * (K + N) * 8,
-            gemv_main(M, w, d_c, N, shift, ctx->kws.p, st));
-        RUN(KC_FALLBACK, 0, 0, gemm_exact(d_a, K, M, K, w, d_c, N, shift, nullptr, 0, st, gemv_flag(ctx->kws.p)));
+            gemv_main(d_a, K, M, w, d_c, N, shift, ctx->kws.p, st));
         CK(cudaGetLastError());
         return SLX_OK;
     }
