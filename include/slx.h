@@ -139,11 +139,44 @@ slx_status slx_matmul_q30_noalloc(const int64_t* d_a, int M, int K, int dtype, c
 slx_status slx_attention(slx_ctx* ctx, const int64_t* q, const int64_t* k, const int64_t* v, int seq, int q_embd,
                          int kv_dim, int n_heads, int n_kv_heads, int scale_exp, int mode, int window, int64_t* out);
 
+/* ---- lattice k-NN search ------------------------------------------------------------------------ */
+/* The embed+search path: EmbeddingLattice<TPayload>(occupants) + QueryKNearestL2(center, k)
+ * (Lattice/EmbeddingLattice.cs:70-77) over vectors quantized by EmbeddingAdapter.Quantize
+ * (Math/EmbeddingAdapter.cs:15-41), as VocabLattice builds and queries it (Lattice/VocabLattice.cs:15-58):
+ * rows are float embeddings, quantized with (zero_threshold, global_scale) -- VocabLattice uses
+ * 0.001 and 1e9 -- and every query is quantized with the lattice's options. The answer is exact:
+ * the k smallest SparseVector.DistanceSquaredL2Fast distances (Math/SparseVector.cs:138-169),
+ * ascending; equal distances are ordered by id (the reference leaves them to an unstable sort).
+ * ids are id_base + row (so shards of one database can carry global ids); entries past the
+ * database are id -1 with distance UINT64_MAX (the reference returns a shorter list). A quantized
+ * component outside int32 is SLX_ERANGE; dim <= 16384; 0 <= k <= 16. */
+typedef struct slx_lattice slx_lattice;
+#define SLX_KNN_EXACT 1 /* query flag: skip the tensor-core bound, scan every row exactly */
+slx_status slx_lattice_build(slx_ctx* ctx, const float* vectors, int64_t n, int dim, float zero_threshold,
+                             int64_t global_scale, int64_t id_base, slx_lattice** out);
+slx_status slx_lattice_build_device(slx_ctx* ctx, const float* d_vectors, int64_t n, int dim, float zero_threshold,
+                                    int64_t global_scale, int64_t id_base, void* stream, slx_lattice** out);
+slx_status slx_lattice_free(slx_lattice* lat);
+/* info: n rows, dim, id_base */
+slx_status slx_lattice_info(slx_lattice* lat, int64_t* info, int n);
+/* ids [nq][k], dist [nq][k]; n_exact (nullable) = queries the bound could not decide, answered by an
+ * exact scan. The device variant synchronizes its stream once (to size that scan). */
+slx_status slx_lattice_query_knn_l2(slx_lattice* lat, const float* queries, int nq, int k, int flags, int64_t* ids,
+                                    uint64_t* dist, int* n_exact);
+slx_status slx_lattice_query_knn_l2_device(slx_lattice* lat, const float* d_queries, int nq, int k, int flags,
+                                           int64_t* d_ids, uint64_t* d_dist, int* n_exact, void* stream);
+/* k-way merge of per-shard answers: d_ids/d_dist [parts][nq][k] (each list ascending, as returned
+ * above) -> [nq][k]; parts <= 64. No reference counterpart: the sharded database's top-k merge after
+ * an all-gather of the shards' answers. */
+slx_status slx_knn_merge_device(slx_ctx* ctx, const int64_t* d_ids, const uint64_t* d_dist, int parts, int nq, int k,
+                                int64_t* d_out_ids, uint64_t* d_out_dist, void* stream);
+
 /* ---- measurement ---------------------------------------------------------------------------- */
 /* No reference counterpart (the reference times with Stopwatch, SparseLattice.Perf/Program.cs:817-830).
  * Per kernel class, the library's launches on ctx between begin and end, their device time from
  * CUDA events recorded on the launch stream, and the algorithmic multiply-accumulates they
- * performed. Classes: gemm, attention, norm, rope, ffn_gate, embed, pool, add, argmax, gemv, split, fallback. */
+ * performed. Classes: gemm, attention, norm, rope, ffn_gate, embed, pool, add, argmax, gemv, split, fallback,
+ * search. */
 typedef struct slx_kernel_stat {
     char name[24];
     int64_t launches;

@@ -23,6 +23,7 @@ I32P = ctypes.POINTER(ctypes.c_int32)
 U16P = ctypes.POINTER(ctypes.c_uint16)
 U8P = ctypes.POINTER(ctypes.c_uint8)
 F32P = ctypes.POINTER(ctypes.c_float)
+U64P = ctypes.POINTER(ctypes.c_uint64)
 VP = ctypes.c_void_p
 
 
@@ -93,6 +94,9 @@ def _sig(lib):
     f("slxo_causal_next_token", i, VP, I32P, i, I32P)
     f("slxo_causal_generate", i, VP, I32P, i, i, I32P, ctypes.POINTER(i))
     f("slxo_gemma_encoder_forward", i, VP, I32P, i, i, I64P)
+    f("slxo_quantize_dense", None, F32P, i64, f32, i64, I64P)
+    f("slxo_distance_sq_l2_fast", ctypes.c_uint64, I64P, I64P, i)
+    f("slxo_knn_l2", None, I64P, i64, i, I64P, i, i, i64, I64P, U64P)
 
 
 def lib():
@@ -290,6 +294,31 @@ def argmax_half(h, E_half, vocab: int, dims: int) -> int:
     h = np.ascontiguousarray(h, np.float32)
     E = np.ascontiguousarray(E_half, np.uint16)
     return lib().slxo_argmax_half(_p(h, F32P), _p(E, U16P), E.size, vocab, dims)
+
+
+def quantize_dense(e, zero_threshold: float = 0.001, global_scale: int = 1_000_000_000) -> np.ndarray:
+    """EmbeddingAdapter.QuantizeDense / Quantize (no sparsity budget) of float embeddings, any shape."""
+    e = np.ascontiguousarray(e, dtype=np.float32)
+    out = np.empty(e.shape, np.int64)
+    lib().slxo_quantize_dense(_p(e, F32P), e.size, zero_threshold, int(global_scale), _p(out, I64P))
+    return out
+
+
+def distance_sq_l2_fast(a, b) -> int:
+    a, b = _i64(a), _i64(b)
+    return int(lib().slxo_distance_sq_l2_fast(_p(a, I64P), _p(b, I64P), a.size))
+
+
+def knn_l2(db, queries, k: int, id_base: int = 0):
+    """Exact k nearest rows of db ([n, dim] int64) for each query row, ascending (distance, id).
+    Returns (ids [nq, k] int64, dist [nq, k] uint64); missing entries (k > n) are -1 / UINT64_MAX."""
+    db, q = _i64(db), _i64(queries)
+    n, dim = db.shape
+    nq = q.shape[0]
+    ids = np.empty((nq, k), np.int64)
+    dist = np.empty((nq, k), np.uint64)
+    lib().slxo_knn_l2(_p(db, I64P), n, dim, _p(q, I64P), nq, k, id_base, _p(ids, I64P), _p(dist, U64P))
+    return ids, dist
 
 
 class Gguf:

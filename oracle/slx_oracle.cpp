@@ -8,7 +8,9 @@
 //   Gguf/GgufReader.cs, Gguf/GgufDequantizer.cs, Gguf/GgufTensorInfo.cs, Gguf/GgufTypes.cs,
 //   Math/IntegerMatMul.cs, Math/IntegerTranscendentals.cs, Math/IntegerLayerNorm.cs,
 //   Math/IntegerAttention.cs, Math/IntegerFFN.cs, Gguf/IntegerTransformerSource*.cs,
-//   Gguf/IntegerCausalSource*.cs, Gguf/IntegerGemmaSource*.cs, Lattice/VocabLattice.cs.
+//   Gguf/IntegerCausalSource*.cs, Gguf/IntegerGemmaSource*.cs, Lattice/VocabLattice.cs,
+//   and for the lattice k-NN search Math/EmbeddingAdapter.cs, Math/SparseVector.cs,
+//   Lattice/EmbeddingLattice.cs (KnnHeap), Lattice/RecallEvaluator.cs.
 // Each function names the file:line it follows. C# semantics reproduced here:
 //   * Int128 and long arithmetic is unchecked (wraps); accumulation is done in unsigned __int128
 //     so wrap-around is defined in C++ too.
@@ -1214,6 +1216,63 @@ static int causal_next(const Causal& c, const int32_t* ids, int T, int32_t* next
 // ==========================================================================================
 // C ABI for the Python test harness (ctypes)
 // ==========================================================================================
+
+// ------------------------------------------------------------------------------------------
+// Lattice k-NN search (embed + search)
+// ------------------------------------------------------------------------------------------
+// EmbeddingAdapter.QuantizeDense (Math/EmbeddingAdapter.cs:43-54): per component,
+// |e| < ZeroThreshold (float compare) -> 0, else (long)(e * (double)GlobalScale). Entry for entry this
+// is the dense form of EmbeddingAdapter.Quantize (:15-41) without a sparsity budget: Quantize drops
+// exactly the components that are 0 here.
+static void quantize_dense(const float* e, int64_t n, float zero_threshold, int64_t global_scale, int64_t* out) {
+    const double scale = (double)global_scale;
+    for (int64_t i = 0; i < n; i++) out[i] = std::fabs(e[i]) < zero_threshold ? 0 : cs_d2l((double)e[i] * scale);
+}
+
+// SparseVector.DistanceSquaredL2Fast (Math/SparseVector.cs:138-169) on dense vectors: the sparse
+// merge adds (a-b)^2 where both are present and v^2 where one is, which is the dense sum over
+// all dimensions; every square is (ulong)(diff * diff) with long wrap-around, summed in ulong.
+static inline uint64_t distance_sq_l2_fast(const int64_t* a, const int64_t* b, int dim) {
+    uint64_t sum = 0;
+    for (int d = 0; d < dim; d++) {
+        const int64_t diff = wrap_sub(a[d], b[d]);
+        sum += (uint64_t)wrap_mul(diff, diff);
+    }
+    return sum;
+}
+
+// Exact k nearest database rows by DistanceSquaredL2Fast, ascending. RecallEvaluator.
+// BruteForceKNearestL2 (Lattice/RecallEvaluator.cs:148-163) sorts all distances, and EmbeddingLattice.
+// QueryKNearestL2 (Lattice/EmbeddingLattice.cs:70-77, KnnHeap :321-387) keeps the k smallest; both
+// leave the order of equal distances to an unstable sort, so equal distances are ordered here by
+// ascending row id. Rows past n (k > n) are reported as id -1, distance UINT64_MAX.
+static void knn_l2(const int64_t* db, int64_t n, int dim, const int64_t* q, int nq, int k, int64_t id_base,
+                   int64_t* ids, uint64_t* dist) {
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int qi = 0; qi < nq; qi++) {
+        std::vector<std::pair<uint64_t, int64_t>> best;  // max-heap of the k smallest (distance, id)
+        best.reserve((size_t)k + 1);
+        const int64_t* qv = q + (int64_t)qi * dim;
+        for (int64_t r = 0; r < n; r++) {
+            const std::pair<uint64_t, int64_t> e(distance_sq_l2_fast(qv, db + r * dim, dim), r + id_base);
+            if ((int)best.size() < k) {
+                best.push_back(e);
+                std::push_heap(best.begin(), best.end());
+            } else if (k > 0 && e < best.front()) {
+                std::pop_heap(best.begin(), best.end());
+                best.back() = e;
+                std::push_heap(best.begin(), best.end());
+            }
+        }
+        std::sort(best.begin(), best.end());
+        for (int j = 0; j < k; j++) {
+            const bool ok = j < (int)best.size();
+            ids[(int64_t)qi * k + j] = ok ? best[j].second : -1;
+            dist[(int64_t)qi * k + j] = ok ? best[j].first : UINT64_MAX;
+        }
+    }
+}
+
 extern "C" {
 
 int slxo_set_threads(int n) {
@@ -1408,6 +1467,16 @@ int slxo_gemma_encoder_forward(void* cp, const int32_t* ids, int B, int T, int64
         mean_pool(x.data(), T, c->embd, pooled + (int64_t)b * c->embd);
     }
     return SLXO_OK;
+}
+
+// ---- lattice k-NN ----
+void slxo_quantize_dense(const float* e, int64_t n, float zero_threshold, int64_t global_scale, int64_t* out) {
+    quantize_dense(e, n, zero_threshold, global_scale, out);
+}
+uint64_t slxo_distance_sq_l2_fast(const int64_t* a, const int64_t* b, int dim) { return distance_sq_l2_fast(a, b, dim); }
+void slxo_knn_l2(const int64_t* db, int64_t n, int dim, const int64_t* q, int nq, int k, int64_t id_base, int64_t* ids,
+                 uint64_t* dist) {
+    knn_l2(db, n, dim, q, nq, k, id_base, ids, dist);
 }
 
 }  // extern "C"

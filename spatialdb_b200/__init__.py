@@ -20,7 +20,7 @@ import ctypes
 import numpy as np
 
 from . import _lib
-from ._lib import I32P, I64P, F32P, U8P, VP
+from ._lib import I32P, I64P, F32P, U8P, U64P, VP
 
 (SLX_OK, SLX_EINVAL, SLX_EFORMAT, SLX_ENOTFOUND, SLX_EUNSUPPORTED, SLX_EEOF, SLX_ERANGE, SLX_EOOM, SLX_ECUDA, SLX_ETIMEOUT,
  SLX_ESCRATCH) = range(11)
@@ -256,3 +256,101 @@ class IntegerCausalSource(_Model):
         n = np.zeros(B, np.int32)
         self.ctx.check(self.ctx._lib.slx_causal_generate(self._h, _p(ids, I32P), B, T, max_new_tokens, _p(out, I32P), _p(n, I32P)))
         return [out[b, : n[b]].copy() for b in range(B)]
+
+
+# ---- lattice k-NN search --------------------------------------------------------------------------
+
+KNN_EXACT = 1  # query flag: scan every row exactly instead of bounding with the tensor cores
+
+
+class QuantizationOptions:
+    """QuantizationOptions (Math/EmbeddingAdapter.cs:4-11). The class defaults are the reference's
+    (ZeroThreshold 0.01, GlobalScale long.MaxValue); VocabLattice uses (0.001, 1e9), which is
+    VOCAB_LATTICE_OPTIONS and the default of EmbeddingLattice here. No sparsity budget."""
+
+    def __init__(self, zero_threshold: float = 0.01, global_scale: int = (1 << 63) - 1):
+        self.zero_threshold = float(zero_threshold)
+        self.global_scale = int(global_scale)
+
+
+VOCAB_LATTICE_OPTIONS = QuantizationOptions(0.001, 1_000_000_000)
+
+
+class EmbeddingLattice:
+    """Exact k-nearest-neighbour search over float embeddings on the device: the rows are quantized
+    with EmbeddingAdapter.Quantize (options as above) and query_k_nearest_l2 returns
+    EmbeddingLattice.QueryKNearestL2's answer (Lattice/EmbeddingLattice.cs:70-77): the k smallest
+    DistanceSquaredL2Fast distances, ascending, equal distances by id. ids are id_base + row."""
+
+    def __init__(self, vectors, options: QuantizationOptions = VOCAB_LATTICE_OPTIONS, id_base: int = 0,
+                 ctx: Context | None = None):
+        self._ctx = ctx or Context.default()
+        self.options = options
+        v = np.ascontiguousarray(vectors, np.float32)
+        if v.ndim != 2:
+            raise ValueError("vectors must be [n, dim]")
+        h = VP()
+        self._ctx.check(self._ctx._lib.slx_lattice_build(self._ctx._h, _p(v, F32P), v.shape[0], v.shape[1],
+                                                         options.zero_threshold, options.global_scale, int(id_base),
+                                                         ctypes.byref(h)))
+        self._h = h
+        self.n, self.dim, self.id_base = v.shape[0], v.shape[1], int(id_base)
+        self.last_exact = 0
+
+    @classmethod
+    def from_device(cls, d_vectors_ptr: int, n: int, dim: int, options: QuantizationOptions = VOCAB_LATTICE_OPTIONS,
+                    id_base: int = 0, stream: int = 0, ctx: Context | None = None) -> "EmbeddingLattice":
+        self = cls.__new__(cls)
+        self._ctx = ctx or Context.default()
+        self.options = options
+        h = VP()
+        self._ctx.check(self._ctx._lib.slx_lattice_build_device(self._ctx._h, VP(d_vectors_ptr), int(n), int(dim),
+                                                                options.zero_threshold, options.global_scale,
+                                                                int(id_base), VP(stream), ctypes.byref(h)))
+        self._h = h
+        self.n, self.dim, self.id_base = int(n), int(dim), int(id_base)
+        self.last_exact = 0
+        return self
+
+    def query_k_nearest_l2(self, queries, k: int, exact: bool = False):
+        """(ids [nq, k] int64, distances [nq, k] uint64); -1 / UINT64_MAX past the database."""
+        q = np.ascontiguousarray(np.atleast_2d(queries), np.float32)
+        nq = q.shape[0]
+        ids = np.empty((nq, k), np.int64)
+        dist = np.empty((nq, k), np.uint64)
+        ne = ctypes.c_int(0)
+        self._ctx.check(self._ctx._lib.slx_lattice_query_knn_l2(self._h, _p(q, F32P), nq, int(k),
+                                                                KNN_EXACT if exact else 0, _p(ids, I64P),
+                                                                _p(dist, U64P), ctypes.byref(ne)))
+        self.last_exact = ne.value
+        return ids, dist
+
+    def query_device(self, d_queries_ptr: int, nq: int, k: int, d_ids_ptr: int, d_dist_ptr: int, exact: bool = False,
+                     stream: int = 0) -> int:
+        """Device buffers: queries [nq, dim] float32, ids [nq, k] int64, dist [nq, k] uint64. Returns the
+        number of queries answered by an exact scan."""
+        ne = ctypes.c_int(0)
+        self._ctx.check(self._ctx._lib.slx_lattice_query_knn_l2_device(
+            self._h, VP(d_queries_ptr), int(nq), int(k), KNN_EXACT if exact else 0, VP(d_ids_ptr), VP(d_dist_ptr),
+            ctypes.byref(ne), VP(stream)))
+        self.last_exact = ne.value
+        return ne.value
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._ctx._lib.slx_lattice_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def knn_merge_device(d_ids_ptr: int, d_dist_ptr: int, parts: int, nq: int, k: int, d_out_ids_ptr: int,
+                     d_out_dist_ptr: int, stream: int = 0, ctx: Context | None = None):
+    """k-way merge of per-shard answers [parts][nq][k] into [nq][k] on the device."""
+    ctx = ctx or Context.default()
+    ctx.check(ctx._lib.slx_knn_merge_device(ctx._h, VP(d_ids_ptr), VP(d_dist_ptr), int(parts), int(nq), int(k),
+                                            VP(d_out_ids_ptr), VP(d_out_dist_ptr), VP(stream)))

@@ -19,8 +19,9 @@ I64P = ctypes.POINTER(ctypes.c_int64)
 I32P = ctypes.POINTER(ctypes.c_int32)
 U8P = ctypes.POINTER(ctypes.c_uint8)
 F32P = ctypes.POINTER(ctypes.c_float)
+U64P = ctypes.POINTER(ctypes.c_uint64)
 VP = ctypes.c_void_p
-i, i64 = ctypes.c_int, ctypes.c_int64
+i, i64, f32 = ctypes.c_int, ctypes.c_int64, ctypes.c_float
 
 # name -> (restype, argtypes); kept in the order of include/slx.h
 SIGNATURES = {
@@ -43,6 +44,13 @@ SIGNATURES = {
     "slx_matmul_q30_device": (i, [VP, VP, i, i, i, VP, i64, i, i, i, i, VP, VP]),
     "slx_matmul_q30_noalloc": (i, [VP, i, i, i, VP, i64, i, i, i, i, VP, VP]),
     "slx_attention": (i, [VP, I64P, I64P, I64P, i, i, i, i, i, i, i, i, I64P]),
+    "slx_lattice_build": (i, [VP, F32P, i64, i, f32, i64, i64, ctypes.POINTER(VP)]),
+    "slx_lattice_build_device": (i, [VP, VP, i64, i, f32, i64, i64, VP, ctypes.POINTER(VP)]),
+    "slx_lattice_free": (i, [VP]),
+    "slx_lattice_info": (i, [VP, I64P, i]),
+    "slx_lattice_query_knn_l2": (i, [VP, F32P, i, i, i, I64P, U64P, ctypes.POINTER(i)]),
+    "slx_lattice_query_knn_l2_device": (i, [VP, VP, i, i, i, VP, VP, ctypes.POINTER(i), VP]),
+    "slx_knn_merge_device": (i, [VP, VP, VP, i, i, i, VP, VP, VP]),
     "slx_profile_begin": (i, [VP]),
     "slx_profile_end": (i, [VP, VP, i, ctypes.POINTER(i)]),
     "slx_launch_count": (i, [VP, I64P]),

@@ -11,9 +11,10 @@
 // Weights are read once from HBM with 16-byte copies into shared memory (each warp streams NC
 // output columns' contiguous blocks); the activation digits (a few KB) stay in L1/L2 and each
 // block's digits serve all NC columns.
-// If any activation needs a sixth digit, the prep kernel raises the overflow word and every warp
-// takes the Int128 multiply-accumulate path over the composites instead.
+// If any activation needs a sixth digit, the prep kernel stores its call's tag in the overflow word
+// and every warp takes the Int128 multiply-accumulate path over the composites instead.
 #include "slx_device.cuh"
+#include "slx_gemm.h"
 #include "slx_kernels.h"
 
 namespace slx {
@@ -21,45 +22,57 @@ namespace {
 
 constexpr int GV_THREADS = 256;
 constexpr int ND = 5;  // activation digits
+constexpr int FLAG_WORD = 16;  // int index of the GEMV overflow word in the workspace
 
-// Activation digits for the GEMV: dig[m][i][k] (int8) in the element order a block's 32-bit
-// words present: for Q4_0 word j of a block carries elements (8j, 8j+2, 8j+4, 8j+6) in its low
-// nibbles and (8j+1, ..., 8j+7) in its high nibbles; Q8_0 words carry elements in order.
-// Also bsum[m][i][blk] = sum of digit i over the block (for the Q4_0 offset of 8).
+// Activation digits for the GEMV, dig[m][blk][i][32] (int8, 160 contiguous bytes per row and
+// block), in the element order a block's 32-bit words present: for Q4_0 word j of a block carries
+// elements (8j, 8j+2, 8j+4, 8j+6) in its low nibbles and (8j+1, ..., 8j+7) in its high nibbles;
+// Q8_0 words carry elements in order. asum[m][blk] = sum of the block's activations (wrapping),
+// used for the Q4_0 offset of 8 and for non-finite scales. Four threads per (row, block), each
+// splitting 8 consecutive activations. An activation that needs a sixth digit stores `tag` in the
+// overflow word.
 __global__ void k_gemv_prep(const int64_t* __restrict__ A, int64_t lda, int M, int K, int q4, int8_t* __restrict__ dig,
-                            int* __restrict__ bsum, int* overflow) {
+                            int64_t* __restrict__ asum, int* overflow, int tag) {
     const int nb = K / 32;
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;  // over M * nb blocks
-    if (idx >= M * nb) return;
-    const int m = idx / nb, blk = idx % nb;
-    int8_t d[ND][32];
-    int sum[ND] = {0, 0, 0, 0, 0};
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const int pair = t >> 2, j = t & 3;  // pair = m * nb + blk; blocks of 4 threads stay inside one warp
+    const bool live = pair < M * nb;
+    const int m = live ? pair / nb : 0, blk = live ? pair % nb : 0;
+    int64_t x[8];
+    int64_t sum = 0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        x[e] = live ? A[(int64_t)m * lda + (int64_t)blk * 32 + 8 * j + e] : 0;
+        sum = wadd(sum, x[e]);
+    }
+    uint32_t lo[ND], hi[ND];
+#pragma unroll
+    for (int i = 0; i < ND; i++) lo[i] = hi[i] = 0;
     bool bad = false;
-    for (int e = 0; e < 32; e++) {
-        int64_t x = A[(int64_t)m * lda + (int64_t)blk * 32 + e];
-        // position of element e inside the block's byte stream
-        int pos;
-        if (q4) {
-            const int j = e >> 3, r = e & 7;          // word j, r-th element of the word
-            pos = j * 8 + ((r & 1) ? 4 : 0) + (r >> 1);  // even elements first (low nibbles), then odd
-        } else {
-            pos = e;
-        }
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        int64_t v = x[e];
+        // Q4_0: even elements go to the low-nibble word, odd ones to the high-nibble word;
+        // Q8_0: elements 0..3 to the first word, 4..7 to the second.
+        const int word = q4 ? (e & 1) : (e >> 2);
+        const int byte = q4 ? (e >> 1) : (e & 3);
 #pragma unroll
         for (int i = 0; i < ND; i++) {
-            int dd = (int)(((uint64_t)x + 128u) & 255u) - 128;
-            x = (x - dd) >> 8;
-            d[i][pos] = (int8_t)dd;
-            sum[i] += dd;
+            const int d = (int)(((uint64_t)v + 128u) & 255u) - 128;
+            v = (v - d) >> 8;
+            const uint32_t b = (uint32_t)(uint8_t)(int8_t)d << (8 * byte);
+            if (word) hi[i] |= b; else lo[i] |= b;
         }
-        bad |= x != 0;
+        bad |= v != 0;
     }
-    if (bad) atomicOr(overflow, 1);
-    for (int i = 0; i < ND; i++) {
-        int8_t* dst = dig + ((int64_t)m * ND + i) * K + (int64_t)blk * 32;
-        for (int e = 0; e < 32; e++) dst[e] = d[i][e];
-        bsum[((int64_t)m * ND + i) * nb + blk] = sum[i];
-    }
+    sum = wadd(sum, (int64_t)__shfl_xor_sync(0xffffffffu, (long long)sum, 1));
+    sum = wadd(sum, (int64_t)__shfl_xor_sync(0xffffffffu, (long long)sum, 2));
+    if (!live) return;
+    if (bad) atomicExch(overflow, tag);
+    int8_t* dst = dig + (int64_t)pair * (ND * 32) + 8 * j;
+#pragma unroll
+    for (int i = 0; i < ND; i++) *(uint2*)(dst + i * 32) = make_uint2(lo[i], hi[i]);
+    if (j == 0) asum[pair] = sum;
 }
 
 SLX_DEV int dp4a_su(int a_signed, unsigned b_unsigned, int c) {
@@ -68,24 +81,38 @@ SLX_DEV int dp4a_su(int a_signed, unsigned b_unsigned, int c) {
     return d;
 }
 
-// One block's 8 words of 4 bytes: Q4_0 nibbles unpacked to (low nibbles, high nibbles) of 4 words,
-// Q8_0 signed bytes as they are. Returns the block's scale bits.
+// One block's 8 words of 4 bytes from shared memory: Q4_0 nibbles unpacked to (low nibbles, high
+// nibbles) of 4 words, Q8_0 signed bytes as they are. Returns the block's scale bits. Blocks are 18 or
+// 34 bytes, so a block starts on a 4-byte boundary or 2 bytes past one: the words are read aligned
+// and funnel-shifted by 16 bits (or taken as they are, a clamped shift of 32).
 template <bool Q4>
 SLX_DEV uint16_t load_block(const uint8_t* __restrict__ blk, uint32_t (&w)[8]) {
-    const uint16_t* h = (const uint16_t*)blk;
-    const uint16_t scale = h[0];
+    constexpr int NW = Q4 ? 5 : 9;
+    const uint32_t* p = (const uint32_t*)((uintptr_t)blk & ~(uintptr_t)3);
+    const uint32_t s = ((uintptr_t)blk & 2) ? 32u : 16u;
+    uint32_t r[NW];
+#pragma unroll
+    for (int i = 0; i < NW; i++) r[i] = p[i];
+    const uint16_t scale = (uint16_t)(r[0] >> (s - 16));
     if (Q4) {
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            const uint32_t x = (uint32_t)h[1 + 2 * j] | ((uint32_t)h[2 + 2 * j] << 16);
+            const uint32_t x = __funnelshift_rc(r[j], r[j + 1], s);
             w[2 * j] = x & 0x0F0F0F0Fu;             // elements 8j, 8j+2, 8j+4, 8j+6 (nibble values 0..15)
             w[2 * j + 1] = (x >> 4) & 0x0F0F0F0Fu;  // elements 8j+1, ..., 8j+7
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < 8; j++) w[j] = (uint32_t)h[1 + 2 * j] | ((uint32_t)h[2 + 2 * j] << 16);
+        for (int j = 0; j < 8; j++) w[j] = __funnelshift_rc(r[j], r[j + 1], s);
     }
     return scale;
+}
+
+// acc += (Int128)s * d
+SLX_DEV void mac128(u128& acc, int64_t s, int64_t d) {
+    const uint64_t lo = (uint64_t)s * (uint64_t)d;
+    const int64_t hi = __mul64hi(s, d);
+    acc += ((u128)(uint64_t)hi << 64) | lo;
 }
 
 // Warp = NC output columns. The warp streams its columns' packed blocks through shared memory in
@@ -104,12 +131,12 @@ SLX_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) :
 
 template <bool Q4, int MM, int NC>
 __global__ __launch_bounds__(GV_THREADS) void k_gemv(const uint8_t* __restrict__ W, int N, int K, const int8_t* __restrict__ dig,
-                                                     const int* __restrict__ bsum, int64_t* __restrict__ C, int64_t ldc,
-                                                     int shift, const int* __restrict__ skip,
+                                                     const int64_t* __restrict__ asum, int64_t* __restrict__ C, int64_t ldc,
+                                                     int shift, const int* __restrict__ skip, int tag,
                                                      const int64_t* __restrict__ A, int64_t lda, double scale) {
     constexpr int BB = Q4 ? 18 : 34;
     constexpr int CHB = GV_CHUNK * BB;       // bytes per column chunk (multiple of 16)
-    if (*skip) {  // an activation needs a sixth digit: Int128 multiply-accumulate of the composites
+    if (*skip == tag) {  // an activation needs a sixth digit: Int128 multiply-accumulate of the composites
         const int warp_ = threadIdx.x >> 5, lane_ = threadIdx.x & 31;
         const int nb0 = (blockIdx.x * (GV_THREADS / 32) + warp_) * NC;
         const int64_t nblk = K / 32;
@@ -182,27 +209,34 @@ __global__ __launch_bounds__(GV_THREADS) void k_gemv(const uint8_t* __restrict__
             }
 #pragma unroll
             for (int m = 0; m < MM; m++) {
-                int64_t S[NC];
+                const int8_t* dg = dig + ((int64_t)m * nb + blk) * (ND * 32);
+                int4 dv[ND][2];
 #pragma unroll
-                for (int c = 0; c < NC; c++) S[c] = 0;
+                for (int i = 0; i < ND; i++) {
+                    dv[i][0] = __ldg((const int4*)(dg + 32 * i));
+                    dv[i][1] = __ldg((const int4*)(dg + 32 * i + 16));
+                }
+                const int64_t as = __ldg(asum + (int64_t)m * nb + blk);
 #pragma unroll
-                for (int i = ND - 1; i >= 0; i--) {
-                    const int8_t* dg = dig + ((int64_t)m * ND + i) * K + (int64_t)blk * 32;
-                    const int4 a0 = __ldg((const int4*)dg), a1 = __ldg((const int4*)(dg + 16));
-                    const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                    const int bs = __ldg(bsum + ((int64_t)m * ND + i) * nb + blk);
+                for (int c = 0; c < NC; c++) {
+                    int P[ND];
 #pragma unroll
-                    for (int c = 0; c < NC; c++) {
+                    for (int i = 0; i < ND; i++) {
+                        const int av[8] = {dv[i][0].x, dv[i][0].y, dv[i][0].z, dv[i][0].w,
+                                           dv[i][1].x, dv[i][1].y, dv[i][1].z, dv[i][1].w};
                         int p = 0;
 #pragma unroll
-                        for (int j = 0; j < 8; j++) p = Q4 ? dp4a_su(av[j], w[c][j], p) : __dp4a(av[j], (int)w[c][j], p);
-                        if (Q4) p -= 8 * bs;
-                        if (!fin[c]) p = bs;  // every composite of the block is long.MinValue
-                        S[c] = S[c] * 256 + p;  // digits combined high to low: |S| < 2^59
+                        for (int jj = 0; jj < 8; jj++)
+                            p = Q4 ? dp4a_su(av[jj], w[c][jj], p) : __dp4a(av[jj], (int)w[c][jj], p);
+                        P[i] = p;
                     }
+                    // sum_i 256^i P_i: |P_i| < 2^17, so the two low pairs combine in 32 bits
+                    const int t01 = P[1] * 256 + P[0], t23 = P[3] * 256 + P[2];
+                    int64_t S = (int64_t)t01 + (int64_t)t23 * 65536 + ((int64_t)P[4] << 32);
+                    if (Q4) S -= 8 * as;    // nibble q - 8
+                    if (!fin[c]) S = as;    // every composite of the block is long.MinValue
+                    mac128(acc[m][c], S, D[c]);
                 }
-#pragma unroll
-                for (int c = 0; c < NC; c++) acc[m][c] += (u128)((i128)S[c] * D[c]);
             }
         }
         __syncwarp();  // this buffer is refilled two chunks later
@@ -218,8 +252,8 @@ __global__ __launch_bounds__(GV_THREADS) void k_gemv(const uint8_t* __restrict__
 }
 
 template <bool Q4, int MM, int NC>
-void launch_one(const uint8_t* w, int N, int K, const int8_t* dig, const int* bsum, int64_t* c, int64_t ldc, int shift,
-                const int* skip, const int64_t* a, int64_t lda, double scale, cudaStream_t st) {
+void launch_one(const uint8_t* w, int N, int K, const int8_t* dig, const int64_t* asum, int64_t* c, int64_t ldc, int shift,
+                const int* skip, int tag, const int64_t* a, int64_t lda, double scale, cudaStream_t st) {
     const int cols_per_block = (GV_THREADS / 32) * NC;
     dim3 grid((unsigned)((N + cols_per_block - 1) / cols_per_block));
     const size_t smem = (size_t)(GV_THREADS / 32) * 2 * NC * GV_CHUNK * (Q4 ? 18 : 34);
@@ -228,23 +262,42 @@ void launch_one(const uint8_t* w, int N, int K, const int8_t* dig, const int* bs
         cudaFuncSetAttribute(k_gemv<Q4, MM, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         configured = true;
     }
-    k_gemv<Q4, MM, NC><<<grid, GV_THREADS, smem, st>>>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale);
+    k_gemv<Q4, MM, NC><<<grid, GV_THREADS, smem, st>>>(w, N, K, dig, asum, c, ldc, shift, skip, tag, a, lda, scale);
 }
 
 template <bool Q4>
-void launch_gemv_m(int M, const uint8_t* w, int N, int K, const int8_t* dig, const int* bsum, int64_t* c, int64_t ldc,
-                   int shift, const int* skip, const int64_t* a, int64_t lda, double scale, cudaStream_t st) {
+void launch_gemv_m(int M, const uint8_t* w, int N, int K, const int8_t* dig, const int64_t* asum, int64_t* c,
+                   int64_t ldc, int shift, const int* skip, int tag, const int64_t* a, int64_t lda, double scale,
+                   cudaStream_t st) {
+#define SLX_GV(MM, NC) launch_one<Q4, MM, NC>(w, N, K, dig, asum, c, ldc, shift, skip, tag, a, lda, scale, st)
     switch (M) {
-        case 1: launch_one<Q4, 1, 4>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
-        case 2: launch_one<Q4, 2, 4>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
-        case 3: launch_one<Q4, 3, 2>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
-        case 4: launch_one<Q4, 4, 2>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
-        case 5: launch_one<Q4, 5, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
-        case 6: launch_one<Q4, 6, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
-        case 7: launch_one<Q4, 7, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
-        default: launch_one<Q4, 8, 1>(w, N, K, dig, bsum, c, ldc, shift, skip, a, lda, scale, st); break;
+        case 1: SLX_GV(1, 4); break;
+        case 2: SLX_GV(2, 4); break;
+        case 3: SLX_GV(3, 2); break;
+        case 4: SLX_GV(4, 2); break;
+        case 5: SLX_GV(5, 1); break;
+        case 6: SLX_GV(6, 1); break;
+        case 7: SLX_GV(7, 1); break;
+        default: SLX_GV(8, 1); break;
     }
+#undef SLX_GV
 }
+
+// Workspace: [0, 256) flags (the GEMV overflow word at int index FLAG_WORD), then the digits
+// (M * K * 5 bytes), then the per-block activation sums (M * K / 32 int64).
+struct GemvWs {
+    int* flag;
+    int8_t* dig;
+    int64_t* asum;
+};
+GemvWs gemv_ws(void* ws, int M, int K) {
+    GemvWs g;
+    g.flag = (int*)ws + FLAG_WORD;
+    g.dig = (int8_t*)ws + 256;
+    g.asum = (int64_t*)(g.dig + (((size_t)M * ND * K + 255) & ~(size_t)255));
+    return g;
+}
+size_t gemv_workspace(int M, int K) { return 256 + (((size_t)M * ND * K + 255) & ~(size_t)255) + (size_t)M * (K / 32) * 8; }
 
 }  // namespace
 
@@ -255,44 +308,42 @@ bool gemv_supported(const WDesc& w, int M) {
            w.nblocks * 32 >= w.N * w.K && ((uintptr_t)w.data & 15) == 0;
 }
 
-size_t gemv_workspace(int M, int K) { return 256 + (size_t)M * ND * K + (size_t)M * ND * (K / 32) * 4 + 256; }
-
-namespace {
-struct GemvWs {
-    int* flag;
-    int8_t* dig;
-    int* bsum;
-};
-GemvWs gemv_ws(void* ws, int M, int K) {
-    GemvWs g;
-    g.flag = (int*)ws;
-    g.dig = (int8_t*)ws + 256;
-    g.bsum = (int*)(g.dig + (((size_t)M * ND * K + 255) & ~(size_t)255));
-    return g;
+bool gemv_reserve(GemmWorkspace& ws, int M, int K, cudaStream_t st) {
+    const size_t need = gemv_workspace(M, K);
+    if (need <= ws.bytes) return true;
+    if (ws.p) cudaFree(ws.p);
+    ws.p = nullptr;
+    ws.bytes = 0;
+    ws.tag = 0;
+    if (cudaMalloc(&ws.p, need) != cudaSuccess) return false;
+    ws.bytes = need;
+    cudaMemsetAsync(ws.p, 0, 256, st);  // overflow words start below every tag
+    return true;
 }
-}  // namespace
 
-int gemv_prep(const int64_t* a, int64_t lda, int M, const WDesc& w, void* ws, cudaStream_t st) {
+int gemv_prep(const int64_t* a, int64_t lda, int M, const WDesc& w, GemmWorkspace& ws, cudaStream_t st) {
     const int K = (int)w.K, nb = K / 32;
-    GemvWs g = gemv_ws(ws, M, K);
-    cudaMemsetAsync(g.flag, 0, sizeof(int), st);
-    k_gemv_prep<<<(M * nb + 127) / 128, 128, 0, st>>>(a, lda, M, K, w.dtype == DT_Q4_0, g.dig, g.bsum, g.flag);
+    GemvWs g = gemv_ws(ws.p, M, K);
+    ws.tag = ws.tag >= 0x3fffffff ? 1 : ws.tag + 1;  // never 0, the cleared value
+    const int threads = M * nb * 4;
+    k_gemv_prep<<<(threads + 127) / 128, 128, 0, st>>>(a, lda, M, K, w.dtype == DT_Q4_0, g.dig, g.asum, g.flag,
+                                                       (int)ws.tag);
     return 1;
 }
 
-int gemv_main(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws,
-              cudaStream_t st) {
+int gemv_main(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift,
+              const GemmWorkspace& ws, cudaStream_t st) {
     const int K = (int)w.K, N = (int)w.N;
-    GemvWs g = gemv_ws(ws, M, K);
+    GemvWs g = gemv_ws(ws.p, M, K);
     if (w.dtype == DT_Q4_0)
-        launch_gemv_m<true>(M, w.data, N, K, g.dig, g.bsum, c, ldc, shift, g.flag, a, lda, w.scale, st);
+        launch_gemv_m<true>(M, w.data, N, K, g.dig, g.asum, c, ldc, shift, g.flag, (int)ws.tag, a, lda, w.scale, st);
     else
-        launch_gemv_m<false>(M, w.data, N, K, g.dig, g.bsum, c, ldc, shift, g.flag, a, lda, w.scale, st);
+        launch_gemv_m<false>(M, w.data, N, K, g.dig, g.asum, c, ldc, shift, g.flag, (int)ws.tag, a, lda, w.scale, st);
     return 1;
 }
 
-int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws,
-               cudaStream_t st) {
+int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift,
+               GemmWorkspace& ws, cudaStream_t st) {
     return gemv_prep(a, lda, M, w, ws, st) + gemv_main(a, lda, M, w, c, ldc, shift, ws, st);
 }
 

@@ -26,6 +26,7 @@ struct GemmWorkspace {
     void* p = nullptr;
     size_t bytes = 0;
     int* err = nullptr;  // device error word (bounded-wait timeouts)
+    unsigned tag = 0;    // last GEMV call tag (k_gemv.cu)
 };
 
 // Tensor-core kernel launchers (k_gemm_tc.cu).
@@ -60,5 +61,18 @@ int gemm_prepare(const WDesc& w, GemmPlan& plan, cudaStream_t st, std::string& e
 int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPlan& plan, int64_t* c, int64_t ldc,
               int shift, const int64_t* r, int64_t ldr, GemmWorkspace& ws, cudaStream_t st);
 void gemm_workspace_free(GemmWorkspace& ws);
+
+// Decode-shaped exact GEMV (M <= 8) straight from packed Q4_0 / Q8_0 blocks with the long
+// composite (k_gemv.cu).
+bool gemv_supported(const WDesc& w, int M);
+// Grows ws for an M x K GEMV (clearing its overflow word when it allocates); false when out of memory.
+bool gemv_reserve(GemmWorkspace& ws, int M, int K, cudaStream_t st);
+// Activation digits, then the GEMV proper (exact for any activations). Every prep call takes a new
+// tag that the GEMV compares with the overflow word, so the word never needs clearing.
+int gemv_prep(const int64_t* a, int64_t lda, int M, const WDesc& w, GemmWorkspace& ws, cudaStream_t st);
+int gemv_main(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift,
+              const GemmWorkspace& ws, cudaStream_t st);
+int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift,
+               GemmWorkspace& ws, cudaStream_t st);
 
 }  // namespace slx

@@ -58,16 +58,7 @@ int attention(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, cons
                int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int score_shift, int64_t sqrt_hd,
                int mode, int window, cudaStream_t st, const int* only_if = nullptr);
 
-// Decode-shaped exact GEMV (M <= 8) straight from packed Q4_0 / Q8_0 blocks with the long
-// composite (k_gemv.cu); the exact kernel is gated behind it. ws: gemv_workspace() bytes.
-bool gemv_supported(const WDesc& w, int M);
-size_t gemv_workspace(int M, int K);
-int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws,
-               cudaStream_t st);
-// The same in its two parts: activation digits, then the GEMV proper (exact for any activations).
-int gemv_prep(const int64_t* a, int64_t lda, int M, const WDesc& w, void* ws, cudaStream_t st);
-int gemv_main(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift, void* ws,
-              cudaStream_t st);
+
 
 // Same attention with tensor-core scores (k_attn.cu): digit split of q/k, tcgen05 score GEMM,
 // CUDA-core softmax and per-term PV, and the exact kernel gated behind them for out-of-range

@@ -24,14 +24,15 @@
 #include "slx.h"
 #include "slx_kernels.h"
 #include "slx_gemm.h"
+#include "slx_search.h"
 
 using namespace slx;
 
 // Kernel classes reported by slx_profile_end.
 enum KClass { KC_GEMM, KC_ATTENTION, KC_NORM, KC_ROPE, KC_FFN_GATE, KC_EMBED, KC_POOL, KC_ADD, KC_ARGMAX, KC_GEMV,
-              KC_SPLIT, KC_FALLBACK, KC_COUNT };
+              KC_SPLIT, KC_FALLBACK, KC_SEARCH, KC_COUNT };
 static const char* kKClassName[KC_COUNT] = {"gemm", "attention", "norm", "rope", "ffn_gate", "embed", "pool", "add",
-                                            "argmax", "gemv", "split", "fallback"};
+                                            "argmax", "gemv", "split", "fallback", "search"};
 
 struct ProfRecord {
     int cls;
@@ -806,15 +807,10 @@ slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K,
     w.scale = std::ldexp(1.0, scale_bits);
     cudaStream_t st = pick(ctx, stream);
     if (gemv_supported(w, M)) {  // decode-shaped: packed-block GEMV, queued without a host sync
-        const size_t need = gemv_workspace(M, K);
-        if (need > ctx->kws.bytes) {
-            gemm_workspace_free(ctx->kws);
-            CK(cudaMalloc(&ctx->kws.p, need));
-            ctx->kws.bytes = need;
-        }
-        RUN(KC_SPLIT, 0, (double)M * K * 8, gemv_prep(d_a, K, M, w, ctx->kws.p, st));
+        if (!gemv_reserve(ctx->kws, M, K, st)) return set_err(ctx, SLX_EOOM, "GEMV workspace");
+        RUN(KC_SPLIT, 0, (double)M * K * 8, gemv_prep(d_a, K, M, w, ctx->kws, st));
         RUN(KC_GEMV, (double)M * N * K, (double)gguf_byte_count((uint32_t)dtype, elems) + (double)M * (K + N) * 8,
-            gemv_main(d_a, K, M, w, d_c, N, shift, ctx->kws.p, st));
+            gemv_main(d_a, K, M, w, d_c, N, shift, ctx->kws, st));
         CK(cudaGetLastError());
         return SLX_OK;
     }
@@ -940,6 +936,131 @@ slx_status slx_profile_end(slx_ctx* ctx, slx_kernel_stat* stats, int cap, int* n
 slx_status slx_launch_count(slx_ctx* ctx, int64_t* launches) {
     if (!ctx || !launches) return SLX_EINVAL;
     *launches = ctx->launches;
+    return SLX_OK;
+}
+
+// ---- lattice k-NN search ----------------------------------------------------------------------
+
+struct slx_lattice {
+    slx_ctx* ctx = nullptr;
+    search::Lattice L;
+    float zero_threshold = 0.001f;
+    int64_t global_scale = 1000000000;
+};
+
+slx_status slx_lattice_build_device(slx_ctx* ctx, const float* d_vectors, int64_t n, int dim, float zero_threshold,
+                                    int64_t global_scale, int64_t id_base, void* stream, slx_lattice** out) {
+    if (!ctx || !out) return set_err(ctx, SLX_EINVAL, "null argument");
+    *out = nullptr;
+    CK(cudaSetDevice(ctx->device));
+    std::unique_ptr<slx_lattice> lat(new slx_lattice());
+    lat->ctx = ctx;
+    lat->zero_threshold = zero_threshold;
+    lat->global_scale = global_scale;
+    std::string err;
+    cudaStream_t st = pick(ctx, stream);
+    int rc = search::build(d_vectors, n, dim, zero_threshold, global_scale, id_base, lat->L, st, err);
+    if (n > 0) ctx->launches += 2;
+    if (rc) {
+        search::release(lat->L);
+        return set_err(ctx, rc, "%s", err.c_str());
+    }
+    *out = lat.release();
+    return SLX_OK;
+}
+
+slx_status slx_lattice_build(slx_ctx* ctx, const float* vectors, int64_t n, int dim, float zero_threshold,
+                             int64_t global_scale, int64_t id_base, slx_lattice** out) {
+    if (!ctx || !out || (n > 0 && !vectors) || n < 0 || dim < 1) return set_err(ctx, SLX_EINVAL, "bad arguments");
+    CK(cudaSetDevice(ctx->device));
+    float* d = nullptr;
+    const size_t bytes = (size_t)n * dim * sizeof(float);
+    if (bytes) {
+        if (cudaMalloc(&d, bytes) != cudaSuccess) { cudaGetLastError(); return set_err(ctx, SLX_EOOM, "lattice input"); }
+        cudaError_t e = cudaMemcpyAsync(d, vectors, bytes, cudaMemcpyHostToDevice, ctx->stream);
+        if (e != cudaSuccess) { cudaFree(d); return set_err(ctx, SLX_ECUDA, "%s", cudaGetErrorString(e)); }
+    }
+    slx_status rc = slx_lattice_build_device(ctx, d, n, dim, zero_threshold, global_scale, id_base, nullptr, out);
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(d);
+    return rc;
+}
+
+slx_status slx_lattice_free(slx_lattice* lat) {
+    if (!lat) return SLX_EINVAL;
+    cudaSetDevice(lat->ctx->device);
+    cudaStreamSynchronize(lat->ctx->stream);
+    search::release(lat->L);
+    delete lat;
+    return SLX_OK;
+}
+
+slx_status slx_lattice_info(slx_lattice* lat, int64_t* info, int n) {
+    if (!lat || !info || n < 0) return SLX_EINVAL;
+    const int64_t v[3] = {lat->L.n, lat->L.dim, lat->L.id_base};
+    for (int i = 0; i < n && i < 3; i++) info[i] = v[i];
+    return SLX_OK;
+}
+
+slx_status slx_lattice_query_knn_l2_device(slx_lattice* lat, const float* d_queries, int nq, int k, int flags,
+                                           int64_t* d_ids, uint64_t* d_dist, int* n_exact, void* stream) {
+    if (!lat) return SLX_EINVAL;
+    slx_ctx* ctx = lat->ctx;
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = pick(ctx, stream);
+    std::string err;
+    int rc = 0;
+    run_k(ctx, KC_SEARCH, 2.0 * nq * (double)lat->L.n * lat->L.dim, 0, st, [&] {
+        int64_t nl = 0;
+        rc = search::query(lat->L, d_queries, nq, k, lat->zero_threshold, lat->global_scale,
+                           (flags & SLX_KNN_EXACT) != 0, d_ids, d_dist, n_exact, st, err, &nl);
+        return (int)nl;
+    });
+    if (rc) return set_err(ctx, rc, "%s", err.c_str());
+    return SLX_OK;
+}
+
+slx_status slx_lattice_query_knn_l2(slx_lattice* lat, const float* queries, int nq, int k, int flags, int64_t* ids,
+                                    uint64_t* dist, int* n_exact) {
+    if (!lat) return SLX_EINVAL;
+    slx_ctx* ctx = lat->ctx;
+    if (nq < 0 || k < 0 || (nq > 0 && k > 0 && (!queries || !ids || !dist)))
+        return set_err(ctx, SLX_EINVAL, "bad arguments");
+    if (n_exact) *n_exact = 0;
+    if (nq == 0 || k == 0) return SLX_OK;
+    CK(cudaSetDevice(ctx->device));
+    const size_t qb = (size_t)nq * lat->L.dim * sizeof(float), ob = (size_t)nq * k * 8;
+    void* buf = nullptr;
+    if (cudaMalloc(&buf, qb + 2 * ob + 512) != cudaSuccess) { cudaGetLastError(); return set_err(ctx, SLX_EOOM, "query buffers"); }
+    float* dq = (float*)buf;
+    int64_t* di = (int64_t*)((char*)buf + ((qb + 255) & ~(size_t)255));
+    uint64_t* dd = (uint64_t*)((char*)di + ((ob + 255) & ~(size_t)255));
+    cudaMemcpyAsync(dq, queries, qb, cudaMemcpyHostToDevice, ctx->stream);
+    slx_status rc = slx_lattice_query_knn_l2_device(lat, dq, nq, k, flags, di, dd, n_exact, nullptr);
+    if (rc == SLX_OK) {
+        cudaMemcpyAsync(ids, di, ob, cudaMemcpyDeviceToHost, ctx->stream);
+        cudaMemcpyAsync(dist, dd, ob, cudaMemcpyDeviceToHost, ctx->stream);
+        cudaError_t e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) rc = set_err(ctx, SLX_ECUDA, "%s", cudaGetErrorString(e));
+    } else {
+        cudaStreamSynchronize(ctx->stream);
+    }
+    cudaFree(buf);
+    return rc;
+}
+
+slx_status slx_knn_merge_device(slx_ctx* ctx, const int64_t* d_ids, const uint64_t* d_dist, int parts, int nq, int k,
+                                int64_t* d_out_ids, uint64_t* d_out_dist, void* stream) {
+    if (!ctx || parts < 1 || parts > 64 || nq < 0 || k < 0) return set_err(ctx, SLX_EINVAL, "bad arguments");
+    if (nq == 0 || k == 0) return SLX_OK;
+    if (!d_ids || !d_dist || !d_out_ids || !d_out_dist) return set_err(ctx, SLX_EINVAL, "null buffer");
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = pick(ctx, stream);
+    run_k(ctx, KC_SEARCH, 0, 0, st, [&] {
+        search::merge_parts(d_ids, d_dist, parts, nq, k, d_out_ids, d_out_dist, st);
+        return 1;
+    });
+    CK(cudaGetLastError());
     return SLX_OK;
 }
 

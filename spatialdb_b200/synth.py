@@ -351,3 +351,21 @@ def cached(name: str, make) -> str:
     if not os.path.exists(path):
         make(path)
     return path
+
+
+def gaussian_mixture(rng: np.random.Generator, n: int, dim: int = 768, centres: int = 1024, sigma: float = 0.1,
+                     centre_vectors: np.ndarray | None = None) -> np.ndarray:
+    """Embed+search inputs: centres c ~ N(0, I) L2-normalized, points c + sigma N(0, I) L2-normalized
+    (float32 [n, dim]). Pass centre_vectors to draw queries from the same mixture as a database."""
+    c = centre_vectors
+    if c is None:
+        c = rng.standard_normal((centres, dim))
+        c /= np.linalg.norm(c, axis=1, keepdims=True)
+    x = c[rng.integers(0, c.shape[0], n)] + sigma * rng.standard_normal((n, dim))
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    return x.astype(np.float32)
+
+
+def mixture_centres(rng: np.random.Generator, dim: int = 768, centres: int = 1024) -> np.ndarray:
+    c = rng.standard_normal((centres, dim))
+    return c / np.linalg.norm(c, axis=1, keepdims=True)

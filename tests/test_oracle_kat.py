@@ -404,3 +404,68 @@ def test_causal_mask_is_leaky(oracle):
     q, k, v = (rng.integers(-(1 << 30), 1 << 30, 8) for _ in range(3))
     c = oracle.attention(q, k, v, 2, 4, 4, 1, 1, -30, mode=1)
     assert (c[:4] != v[:4]).any()
+
+
+# ---- lattice k-NN search ----
+
+def test_quantize_kills_noise_under_threshold(oracle):  # EmbeddingAdapterTests.cs:8-22
+    q = oracle.quantize_dense(np.array([0.0, 0.005, -0.005, 0.5, -0.8, 0.001], np.float32), 0.01, (1 << 63) - 1)
+    assert (q != 0).sum() == 2 and q[3] != 0 and q[4] != 0
+
+
+def test_quantize_defaults_sign_and_zeros(oracle):  # EmbeddingAdapterTests.cs:24-50
+    big = (1 << 63) - 1
+    assert (oracle.quantize_dense(np.array([0.0, 0.005, -0.005], np.float32), 0.01, big) == 0).all()
+    q = oracle.quantize_dense(np.array([0.0, 0.5, -0.5], np.float32), 0.01, big)
+    assert q[0] == 0 and q[1] > 0 and q[2] < 0
+
+
+def test_quantize_truncates_double_product(oracle):
+    """(long)(e * (double)GlobalScale): the float widens to double, the product rounds once, the cast
+    truncates toward zero; NaN and out-of-range give long.MinValue."""
+    e = np.array([0.1, -0.1, 0.3333333, 1e-3, 0.0009999, 2.5, np.nan], np.float32)
+    q = oracle.quantize_dense(e, 0.001, 1_000_000_000)
+    expect = [int(np.float64(np.float32(x)) * 1e9) if np.isfinite(x) and abs(x) >= np.float32(0.001) else 0 for x in e[:-1]]
+    assert list(q[:-1]) == expect
+    assert q[-1] == np.iinfo(np.int64).min
+    assert oracle.quantize_dense(np.array([1.0], np.float32), 0.0, (1 << 63) - 1)[0] == np.iinfo(np.int64).min
+
+
+def test_distance_squared_l2_known(oracle):  # SparseVectorTests.cs:103-116, 118-136
+    a = np.array([10, 0, 30, 0, 0], np.int64)
+    b = np.array([7, 20, 25, 0, 0], np.int64)
+    assert oracle.distance_sq_l2_fast(a, b) == 434
+    a = np.array([10, 0, 30, 0, 5], np.int64)
+    assert oracle.distance_sq_l2_fast(a, b) == sum((int(x) - int(y)) ** 2 for x, y in zip(a, b))
+    assert oracle.distance_sq_l2_fast(a, a) == 0  # SparseVectorTests.cs:207-214
+
+
+def test_distance_fast_wraps_in_ulong(oracle):
+    """DistanceSquaredL2Fast sums (ulong)(diff * diff) with long wrap-around (SparseVector.cs:138-169)."""
+    a = np.array([3_000_000_000, 3_000_000_000], np.int64)
+    b = np.array([0, -3_000_000_000], np.int64)
+    exact = 3_000_000_000 ** 2 + 6_000_000_000 ** 2
+    assert oracle.distance_sq_l2_fast(a, b) == exact % (1 << 64)
+
+
+def test_knn_linear_items(oracle):  # KnnQueryTests.cs:14-22, 92-102 (BuildLinearItems :277-286)
+    db = np.zeros((5, 5), np.int64)
+    db[:, 0] = (np.arange(5) + 1) * 100
+    center = np.array([[300, 0, 0, 0, 0]], np.int64)
+    ids, dist = oracle.knn_l2(db, center, 100)
+    assert (ids[0, :5] >= 0).all() and (ids[0, 5:] == -1).all()  # k > corpus: all 5 rows, then padding
+    assert list(ids[0, :5]) == [2, 1, 3, 0, 4]  # equal distances (1 and 3) ordered by id
+    assert list(dist[0, :5]) == [0, 10000, 10000, 40000, 40000]
+    ids0, _ = oracle.knn_l2(db, center, 0)
+    assert ids0.shape == (1, 0)
+
+
+def test_knn_matches_sorted_brute_force(oracle):  # KnnQueryTests.cs:75-90 (RecallEvaluator.BruteForceKNearestL2)
+    rng = np.random.default_rng(7)
+    db = np.zeros((60, 8), np.int64)
+    db[:, :2] = rng.integers(100, 1000, (60, 2))
+    center = np.zeros((1, 8), np.int64)
+    center[0, 0], center[0, 2] = 400, 600
+    ids, dist = oracle.knn_l2(db, center, 5)
+    full = sorted((oracle.distance_sq_l2_fast(center[0], db[r]), r) for r in range(60))
+    assert [r for _, r in full[:5]] == list(ids[0]) and [d for d, _ in full[:5]] == list(dist[0])
