@@ -202,6 +202,176 @@ def gemma_bench(ctx, decode_b1: int = 128, decode_b16: int = 8) -> dict:
     return res
 
 
+SEARCH = dict(rows=10_000_000, dim=768, queries=10_000, k=10, centres=1024, sigma=0.1)
+CHUNK_ROWS = 1 << 20
+
+
+def _mixture_rows(torch, centres, lo: int, hi: int, sigma: float, seed: int):
+    """Rows [lo, hi) of the seeded device mixture: chunk c of CHUNK_ROWS rows draws from generator
+    seed + c, so a shard's rows equal the same rows of the whole database."""
+    dim = centres.shape[1]
+    out = torch.empty((hi - lo, dim), dtype=torch.float32, device="cuda")
+    g = torch.Generator(device="cuda")
+    for c in range(lo // CHUNK_ROWS, (hi + CHUNK_ROWS - 1) // CHUNK_ROWS):
+        c0, c1 = c * CHUNK_ROWS, (c + 1) * CHUNK_ROWS
+        g.manual_seed(seed + c)
+        idx = torch.randint(0, centres.shape[0], (CHUNK_ROWS,), generator=g, device="cuda")
+        x = centres[idx] + sigma * torch.randn((CHUNK_ROWS, dim), generator=g, device="cuda")
+        x /= x.norm(dim=1, keepdim=True)
+        a, b = max(lo, c0), min(hi, c1)
+        out[a - lo:b - lo] = x[a - c0:b - c0]
+        del x, idx
+    return out
+
+
+def search_bench(ctx, torch, stream, world: int, rank: int, dist, steps: int = 3, warmup: int = 1,
+                 cpu: bool = True) -> dict:
+    """Embed+search: 10M rows x 768 from a 1024-centre Gaussian mixture (sigma 0.1, L2-normalized),
+    quantized with VocabLattice's options (zero threshold 0.001, global scale 1e9); 10K queries from
+    the same mixture, top-10 by exact DistanceSquaredL2Fast. Rows shard contiguously over the ranks;
+    each rank answers every query on its shard, and the answers are all-gathered (NCCL) and merged
+    on the device. One step = the 10K-query batch. Device time from CUDA events on the launch
+    stream, max over ranks."""
+    import numpy as np
+
+    import spatialdb_b200 as slx
+    from spatialdb_b200.sharded import device_merge, gather_merge, shard_bounds
+
+    n, dim, nq, k = SEARCH["rows"], SEARCH["dim"], SEARCH["queries"], SEARCH["k"]
+    lo, hi = shard_bounds(n, world, rank)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(4242)
+    centres = torch.randn((SEARCH["centres"], dim), generator=g, device="cuda")
+    centres /= centres.norm(dim=1, keepdim=True)
+    rows = _mixture_rows(torch, centres, lo, hi, SEARCH["sigma"], 10_000)
+    gq = torch.Generator(device="cuda")
+    gq.manual_seed(7777)
+    qidx = torch.randint(0, SEARCH["centres"], (nq,), generator=gq, device="cuda")
+    queries = centres[qidx] + SEARCH["sigma"] * torch.randn((nq, dim), generator=gq, device="cuda")
+    queries /= queries.norm(dim=1, keepdim=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    lat = slx.EmbeddingLattice.from_device(rows.data_ptr(), hi - lo, dim, id_base=lo, stream=stream.cuda_stream, ctx=ctx)
+    build_s = time.perf_counter() - t0
+    ids = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+    dd = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+    merge = device_merge(ctx, stream.cuda_stream)
+
+    def step():
+        ne = lat.query_device(queries.data_ptr(), nq, k, ids.data_ptr(), dd.data_ptr(), stream=stream.cuda_stream)
+        if dist:
+            mi, md = gather_merge(ids, dd, merge)
+            return ne, mi, md
+        return ne, ids, dd
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    n_exact = []
+    for i in range(steps):
+        ev[i][0].record(stream)
+        ne, mi, md = step()
+        ev[i][1].record(stream)
+        n_exact.append(ne)
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+
+    # end to end: host float queries in (pinned), ids and distances out
+    q_host = queries.cpu().pin_memory()
+    ids_h = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+    dd_h = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+    q_dev = torch.empty_like(queries)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        q_dev.copy_(q_host, non_blocking=True)
+        lat.query_device(q_dev.data_ptr(), nq, k, ids.data_ptr(), dd.data_ptr(), stream=stream.cuda_stream)
+        if dist:
+            mi, md = gather_merge(ids, dd, merge)
+        else:
+            mi, md = ids, dd
+        ids_h.copy_(mi, non_blocking=True)
+        dd_h.copy_(md, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+
+    # checks: the local answer against the library's exact scan for 8 queries, and the distances of
+    # the returned rows against the oracle's DistanceSquaredL2Fast on the oracle-quantized rows
+    checks = {}
+    if rank == 0:
+        import oracle
+
+        ids_l, dd_l = lat.query_k_nearest_l2(queries[:8].cpu().numpy(), k)
+        ex_i, ex_d = lat.query_k_nearest_l2(queries[:8].cpu().numpy(), k, exact=True)
+        checks["bound_equals_exact_scan"] = bool((ids_l == ex_i).all() and (dd_l == ex_d).all())
+        ok = True
+        for qi in range(4):
+            r = ids_l[qi] - lo
+            rv = rows[torch.from_numpy(r).cuda()].cpu().numpy()
+            qv = oracle.quantize_dense(queries[qi].cpu().numpy(), 0.001, 1_000_000_000)
+            rq = oracle.quantize_dense(rv, 0.001, 1_000_000_000)
+            ok &= all(oracle.distance_sq_l2_fast(qv, rq[j]) == int(dd_l[qi, j]) for j in range(k))
+        checks["oracle_distances_of_returned_rows"] = bool(ok)
+    del rows
+    lat.close()
+    torch.cuda.empty_cache()
+    res = None
+    if rank == 0:
+        peaks = measured_peaks()
+        int8_peak = 2.0 * peaks["bf16_tflops"]
+        ops = 2.0 * nq * n * dim
+        achieved = ops * steps / (max_ms / 1000.0) / 1e12
+        res = {
+            "workload": f"embed+search: {n} rows x {dim} (mixture of {SEARCH['centres']}, sigma {SEARCH['sigma']}), "
+                        f"{nq} queries, top-{k}, exact DistanceSquaredL2Fast",
+            "gpus": world, "shard_rows": hi - lo, "build_s": build_s,
+            "queries_per_s": nq * steps / (max_ms / 1000.0), "ms_per_batch": max_ms / steps,
+            "e2e_queries_per_s": nq * steps / float(te.item()),
+            "exact_scan_queries_per_batch": n_exact,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
+                         "frac": achieved / int8_peak,
+                         "ops": "algorithmic: 2 x queries x rows x dim (one multiply-add per component pair)",
+                         "peak_source": f"2 x {peaks['source']} bf16 dense"},
+            "checks": checks,
+            "scaling": "strong (fixed database, rows sharded over the GPUs)",
+        }
+        if cpu and world == 1:
+            res["cpu_baseline"] = search_cpu_baseline()
+    return res
+
+
+def search_cpu_baseline(sample_rows: int = 200_000, sample_queries: int = 4) -> dict:
+    """The oracle's exact brute force (all host threads) on a bounded sample: `sample_queries` queries
+    over `sample_rows` rows of the same distribution, scaled to the full database."""
+    import numpy as np
+    import oracle
+    from spatialdb_b200 import synth
+
+    cores = oracle.set_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(31)
+    c = synth.mixture_centres(rng, SEARCH["dim"], SEARCH["centres"])
+    db = oracle.quantize_dense(synth.gaussian_mixture(rng, sample_rows, SEARCH["dim"], centre_vectors=c), 0.001, 1_000_000_000)
+    q = oracle.quantize_dense(synth.gaussian_mixture(rng, sample_queries, SEARCH["dim"], centre_vectors=c), 0.001, 1_000_000_000)
+    t0 = time.perf_counter()
+    oracle.knn_l2(db, q, SEARCH["k"])
+    dt = time.perf_counter() - t0
+    per_query_full = dt / sample_queries * (SEARCH["rows"] / sample_rows)
+    return {"value": 1.0 / per_query_full, "unit": "queries/s", "cores": cores, "kind": "port",
+            "sample": f"{sample_queries} queries x {sample_rows} rows ({dt:.1f} s), scaled to {SEARCH['rows']} rows"}
+
+
 def cpu_baseline(path: str, sample_seqs: int, seed: int = 99) -> dict:
     """The oracle (C++ restatement of the reference CPU path, OpenMP over output columns as the
     reference's Parallel.For) on a bounded sample of the workload, all host threads."""
@@ -347,6 +517,13 @@ def run_ours(args) -> None:
     chk = model.forward(ids_host[W + K - 1])
     parity_ok = bool((last == chk).all())
 
+    search_res = None
+    if not args.skip_secondary and not args.skip_search:
+        try:
+            search_res = search_bench(ctx, torch, stream, world, rank, dist, cpu=not args.no_cpu_baseline)
+        except Exception as e:  # reported, never silently dropped
+            search_res = {"error": repr(e)}
+
     if rank == 0:
         peaks = measured_peaks()
         cls = {s.name.decode(): s for s in stats[: nstat.value]}
@@ -381,7 +558,7 @@ def run_ours(args) -> None:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(path, args.cpu_sample)
         if world == 1 and not args.skip_secondary:
-            sec = {}
+            sec = line.setdefault("secondary", {})
             try:
                 sec["gemv"] = gemv_bench(ctx, torch, stream)
             except Exception as e:  # reported, never silently dropped
@@ -390,7 +567,8 @@ def run_ours(args) -> None:
                 sec["gemma_decode"] = gemma_bench(ctx)
             except Exception as e:
                 sec["gemma_decode"] = {"error": repr(e)}
-            line["secondary"] = sec
+        if search_res is not None:
+            line.setdefault("secondary", {})["search"] = search_res
         print(json.dumps(line), flush=True)
     del model, ctx
     if dist:
@@ -417,7 +595,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-sample", type=int, default=2, help="sequences in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--skip-secondary", action="store_true", help="skip the GEMV and Gemma decode measurements")
+    ap.add_argument("--skip-secondary", action="store_true",
+                    help="skip the GEMV, Gemma decode and embed+search measurements")
+    ap.add_argument("--skip-search", action="store_true", help="skip the embed+search measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -321,6 +321,21 @@ def knn_l2(db, queries, k: int, id_base: int = 0):
     return ids, dist
 
 
+def merge_topk(ids, dist):
+    """Merge per-shard answers [parts][nq][k] (ascending, id -1 = empty) into [nq][k] by
+    (distance, id); the k-way merge a sharded database needs after gathering its shards' answers."""
+    ids = np.asarray(ids, np.int64)
+    dist = np.asarray(dist, np.uint64)
+    parts, nq, k = ids.shape
+    out_i = np.full((nq, k), -1, np.int64)
+    out_d = np.full((nq, k), np.iinfo(np.uint64).max, np.uint64)
+    for q in range(nq):
+        cand = sorted((int(dist[p, q, j]), int(ids[p, q, j])) for p in range(parts) for j in range(k) if ids[p, q, j] >= 0)
+        for j, (d, i) in enumerate(cand[:k]):
+            out_i[q, j], out_d[q, j] = i, d
+    return out_i, out_d
+
+
 class Gguf:
     """GgufReader restatement (GgufReader.cs:54-130) over a file."""
 

@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 k_search_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmD, TcParams p) {
     constexpr uint32_t IDESC = idesc_i8(2 * DBN);
     if (!bound_ok(p.qs, p.ds)) return;  // the merge sends every query to the exact scan
-    if ((int)blockIdx.x * p.tiles_per_chunk >= p.ntiles) return;
+    if ((int)blockIdx.y * p.tiles_per_chunk >= p.ntiles) return;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -177,6 +177,7 @@ k_search_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * STAGES, tfull = empty0 + 8 * STAGES, tempty = tfull + 8;
     uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 2);
     __shared__ int s_fail;
+    __shared__ int64_t s_keys[8][THREADS];  // epilogue: keys that passed, read back by the insertion loop
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -207,8 +208,10 @@ k_search_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     __syncthreads();
     fence_after();
 
-    const int m0 = blockIdx.y * QBM;
-    const int t0 = blockIdx.x * p.tiles_per_chunk;
+    // blockIdx.x = query tile (fastest), blockIdx.y = database chunk: the CTAs resident together are
+    // the query tiles of one or two chunks, which then read the same database tiles through L2.
+    const int m0 = blockIdx.x * QBM;
+    const int t0 = blockIdx.y * p.tiles_per_chunk;
     const int ntl = min(p.tiles_per_chunk, p.ntiles - t0);
     const uint32_t sbase = smem_u32(smem);
 
@@ -284,14 +287,27 @@ k_search_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                 tmem_ld8(taddr + DBN + col, g1);
                 tmem_ld8(taddr + 2 * DBN + col, g2);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                // Fast path: keys against the current threshold only. Keys that pass go through
+                // shared memory to one insertion loop (a single copy of the list code).
+                unsigned pass = 0;
+                int64_t keys[8];
 #pragma unroll
                 for (int jj = 0; jj < 8; jj++) {
                     const int64_t n = nbase + 8 * c + jj;
-                    if (n < p.n) {
-                        const int64_t h = (int64_t)(int32_t)g0[jj] + (int64_t)(int32_t)g1[jj] * 256 +
-                                          (int64_t)(int32_t)g2[jj] * 65536;
-                        const int64_t key = wsub((int64_t)__ldg(p.dn + n), (int64_t)((uint64_t)h << sh));
-                        if (less_pair(key, (int32_t)n, wk, wi)) list_put(lk, li, wk, wi, wp, key, (int32_t)n);
+                    const int64_t h = (int64_t)(int32_t)g0[jj] + (int64_t)(int32_t)g1[jj] * 256 +
+                                      (int64_t)(int32_t)g2[jj] * 65536;
+                    keys[jj] = wsub((int64_t)__ldg(p.dn + min(n, p.n - 1)), (int64_t)((uint64_t)h << sh));
+                    if (n < p.n && less_pair(keys[jj], (int32_t)n, wk, wi)) pass |= 1u << jj;
+                }
+                if (pass) {
+#pragma unroll
+                    for (int jj = 0; jj < 8; jj++) s_keys[jj][threadIdx.x] = keys[jj];
+                    while (pass) {
+                        const int jj = __ffs(pass) - 1;
+                        pass &= pass - 1;
+                        const int64_t key = s_keys[jj][threadIdx.x];
+                        const int32_t id = (int32_t)(nbase + 8 * c + jj);
+                        if (less_pair(key, id, wk, wi)) list_put(lk, li, wk, wi, wp, key, id);
                     }
                 }
             }
@@ -303,7 +319,7 @@ k_search_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             if (lane == 0) mbar_arrive(tempty);
         }
         if (ok && row < p.nq) {
-            const size_t base = ((size_t)row * p.nslots + (size_t)blockIdx.x * 2 + half) * T;
+            const size_t base = ((size_t)row * p.nslots + (size_t)blockIdx.y * 2 + half) * T;
 #pragma unroll
             for (int j = 0; j < T; j++) { p.ckey[base + j] = lk[j]; p.cid[base + j] = li[j]; }
         }
@@ -567,11 +583,14 @@ unsigned grid_for(int64_t total, int threads) {
     return (unsigned)std::max<int64_t>(1, std::min<int64_t>(b, 148 * 16));
 }
 
-// Chunks per query tile minimizing (waves of 148 CTAs) x (tiles per CTA).
+// Chunks per query tile minimizing (waves of 148 CTAs) x (tiles per CTA), with chunks of at least
+// MIN_CHUNK tiles when the database has them: a slot's first candidates all enter its list, so short
+// chunks pay that start-up on every CTA.
+constexpr int MIN_CHUNK = 256;
 int pick_chunks(int qtiles, int ntiles) {
     int best = 1;
     double best_cost = 1e300;
-    const int maxc = std::min(ntiles, 4096);
+    const int maxc = std::max(1, std::min(ntiles / MIN_CHUNK, 4096));
     for (int c = 1; c <= maxc; c++) {
         const int per = (ntiles + c - 1) / c;
         const int chunks = (ntiles + per - 1) / per;
@@ -691,7 +710,7 @@ int query(Lattice& L, const float* d_q, int nq, int k, float zero_threshold, int
         CUtensorMap mq, md;
         memcpy(&mq, tmq, sizeof(mq));
         memcpy(&md, L.tmap, sizeof(md));
-        k_search_tc<<<dim3((unsigned)nchunks, (unsigned)qtiles), THREADS, SMEM, st>>>(mq, md, tp);
+        k_search_tc<<<dim3((unsigned)qtiles, (unsigned)nchunks), THREADS, SMEM, st>>>(mq, md, tp);
         MergeParams mp{};
         mp.nslots = nslots; mp.k = k; mp.mode = 0; mp.ckey = ckey; mp.cid = cid; mp.qlist = nullptr;
         mp.qvals = qvals; mp.dvals = L.vals; mp.dim = dim; mp.qn2 = qn2; mp.qh2 = qh2; mp.ql2 = ql2;
