@@ -43,14 +43,22 @@ namespace {
 using namespace tc;
 
 constexpr int QBM = 128;   // queries per tile (TMEM lanes)
-constexpr int DBN = 128;   // database rows per tile
+constexpr int DBN = 80;    // database rows per tile: 3 column blocks of 80 per accumulator, two accumulators
 constexpr int BKB = 128;   // K bytes per ring stage (one 128-byte swizzle row)
 constexpr int STAGES = 3;
 constexpr int THREADS = 320;  // warp 0 TMA, warp 1 TMEM + MMA, warps 2..9 epilogue
+constexpr int EPI = 256;      // epilogue threads
 constexpr int A_STAGE = 2 * QBM * BKB;
 constexpr int B_STAGE = 2 * DBN * BKB;
 constexpr int STAGE = A_STAGE + B_STAGE;
-constexpr size_t SMEM = (size_t)STAGES * STAGE + 1024 + 256;
+constexpr int ACC_COLS = 256;  // TMEM column stride of the two accumulators
+constexpr int HALF = DBN / 2;  // database columns per epilogue warp
+constexpr int CAP = 16;        // pending candidates per epilogue thread
+constexpr size_t BUF_BYTES = (size_t)CAP * EPI * 12;
+constexpr size_t SMEM = (size_t)STAGES * STAGE + BUF_BYTES + 1024 + 256;
+static_assert(STAGE % 1024 == 0 && A_STAGE % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+static_assert(3 * DBN <= ACC_COLS && ACC_COLS + 3 * DBN <= 512, "two accumulators in 512 TMEM columns");
+static_assert(HALF % 8 == 0, "epilogue chunks of 8 columns");
 constexpr int EXACT_THREADS = 256;
 
 SLX_DEV int pick_shift(unsigned long long max_abs) {
@@ -159,12 +167,15 @@ struct TcParams {
     int* err;
 };
 
-// CTA = 128 queries x one chunk of database tiles (128 rows each). Per tile, for every 32-byte K step,
-// two MMAs (M=128, N=256, K=32): query digit i times the database's two digit planes stacked along N,
-// written at TMEM column 128*i, so products of digit sum i+j accumulate in column block i+j. The first
-// MMA of a tile overwrites blocks 0 and 1; block 2 is cleared by the epilogue after it reads a tile.
-// Epilogue warps: lane quadrant warp%4, column half (warp-2)/4; each thread keeps its query's T
-// smallest keys over the chunk.
+// CTA = 128 queries x one chunk of database tiles (80 rows each). Per tile, for every 32-byte K step,
+// two MMAs (M=128, N=160, K=32): query digit i times the database's two digit planes stacked along N,
+// written at TMEM column 80*i of the tile's accumulator, so products of digit sum i+j accumulate in
+// column block i+j. Tiles alternate between two accumulators (columns 0 and 256), so the epilogue
+// of one tile overlaps the MMAs of the next. The first MMA of a tile overwrites blocks 0 and 1;
+// block 2 is cleared by the epilogue after it reads the tile.
+// Epilogue warps: lane quadrant warp%4, column half (warp-2)/4. Each thread keeps its query's T
+// smallest keys over the chunk; keys under the thread's threshold queue in shared memory and the
+// warp merges the queues together, so one pass over the list code serves many lanes.
 __global__ void __launch_bounds__(THREADS, 1)
 k_search_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmD, TcParams p) {
     constexpr uint32_t IDESC = idesc_i8(2 * DBN);
@@ -173,11 +184,13 @@ k_search_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = (uint64_t*)(smem + (size_t)STAGES * STAGE);
-    const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * STAGES, tfull = empty0 + 8 * STAGES, tempty = tfull + 8;
-    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 2);
+    int64_t* q_key = (int64_t*)(smem + (size_t)STAGES * STAGE);  // [CAP][EPI]
+    int32_t* q_id = (int32_t*)(q_key + CAP * EPI);                // [CAP][EPI]
+    uint64_t* bars = (uint64_t*)(smem + (size_t)STAGES * STAGE + BUF_BYTES);
+    const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * STAGES;
+    const uint32_t tfull0 = empty0 + 8 * STAGES, tempty0 = tfull0 + 16;  // two each
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 4);
     __shared__ int s_fail;
-    __shared__ int64_t s_keys[8][THREADS];  // epilogue: keys that passed, read back by the insertion loop
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -186,8 +199,10 @@ k_search_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             mbar_init(full0 + 8 * i, 1);
             mbar_init(empty0 + 8 * i, 1);
         }
-        mbar_init(tfull, 1);
-        mbar_init(tempty, 8);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(tfull0 + 8 * b, 1);
+            mbar_init(tempty0 + 8 * b, 8);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -198,10 +213,13 @@ k_search_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (warp >= 2 && warp < 6) {  // column block 2 starts at zero
+    if (warp >= 2 && warp < 6) {  // column block 2 of both accumulators starts at zero
         const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
 #pragma unroll
-        for (int c = 0; c < DBN; c += 16) tmem_st16_zero(tmem + lane_base + 2 * DBN + c);
+        for (int b = 0; b < 2; b++) {
+#pragma unroll
+            for (int c = 0; c < DBN; c += 16) tmem_st16_zero(tmem + lane_base + b * ACC_COLS + 2 * DBN + c);
+        }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
     fence_before();
@@ -239,30 +257,33 @@ k_search_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         if (lane == 0) {  // MMA issuer
             int it = 0;
             for (int j = 0; j < ntl; j++) {
-                if (!mbar_wait(tempty, (uint32_t)(j & 1) ^ 1u)) { s_fail = 1; break; }
+                const int b = j & 1;
+                if (!mbar_wait(tempty0 + 8 * b, (uint32_t)((j >> 1) & 1) ^ 1u)) { s_fail = 1; break; }
                 fence_after();
+                const uint32_t acc = tmem + b * ACC_COLS;
                 bool fail = false;
                 for (int kb = 0; kb < p.nkb; kb++, it++) {
                     const int s = it % STAGES;
                     if (!mbar_wait(full0 + 8 * s, (uint32_t)(it / STAGES) & 1u)) { fail = true; break; }
                     fence_after();
-                    const uint32_t a = sbase + s * STAGE, b = a + A_STAGE;
+                    const uint32_t a = sbase + s * STAGE, bb = a + A_STAGE;
 #pragma unroll
                     for (int kk = 0; kk < BKB / 32; kk++) {
-                        const uint64_t bdesc = sw128_desc(b + kk * 32);
+                        const uint64_t bdesc = sw128_desc(bb + kk * 32);
 #pragma unroll
                         for (int i = 0; i < 2; i++)
-                            umma_i8(tmem + i * DBN, sw128_desc(a + i * (QBM * BKB) + kk * 32), bdesc, IDESC,
+                            umma_i8(acc + i * DBN, sw128_desc(a + i * (QBM * BKB) + kk * 32), bdesc, IDESC,
                                     (kb | kk | i) ? 1u : 0u);
                     }
                     umma_commit(empty0 + 8 * s);
                 }
                 if (fail) { s_fail = 1; break; }
-                umma_commit(tfull);
+                umma_commit(tfull0 + 8 * b);
             }
         }
     } else {  // epilogue
         const int quad = warp & 3, half = (warp - 2) >> 2;
+        const int et = threadIdx.x - 64;  // epilogue thread index
         const int row = m0 + 32 * quad + lane;
         const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16);
         const int sh = pick_shift(p.qs->max_abs) + pick_shift(p.ds->max_abs) + 1;
@@ -272,52 +293,60 @@ k_search_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         for (int j = 0; j < T; j++) { lk[j] = INT64_MAX; li[j] = INT32_MAX; }
         int64_t wk = INT64_MAX;
         int32_t wi = INT32_MAX;
-        int wp = 0;
-        bool ok = true;
-        for (int j = 0; j < ntl; j++) {
-            ok = __all_sync(0xffffffffu, mbar_wait(tfull, (uint32_t)j & 1u));  // tcgen05.ld is warp-collective
-            if (!ok) { s_fail = 1; break; }
-            fence_after();
-            const int64_t nbase = (int64_t)(t0 + j) * DBN + 64 * half;
-#pragma unroll 1
-            for (int c = 0; c < 8; c++) {
-                uint32_t g0[8], g1[8], g2[8];
-                const uint32_t col = 64 * half + 8 * c;
-                tmem_ld8(taddr + col, g0);
-                tmem_ld8(taddr + DBN + col, g1);
-                tmem_ld8(taddr + 2 * DBN + col, g2);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                // Fast path: keys against the current threshold only. Keys that pass go through
-                // shared memory to one insertion loop (a single copy of the list code).
-                unsigned pass = 0;
-                int64_t keys[8];
-#pragma unroll
-                for (int jj = 0; jj < 8; jj++) {
-                    const int64_t n = nbase + 8 * c + jj;
-                    const int64_t h = (int64_t)(int32_t)g0[jj] + (int64_t)(int32_t)g1[jj] * 256 +
-                                      (int64_t)(int32_t)g2[jj] * 65536;
-                    keys[jj] = wsub((int64_t)__ldg(p.dn + min(n, p.n - 1)), (int64_t)((uint64_t)h << sh));
-                    if (n < p.n && less_pair(keys[jj], (int32_t)n, wk, wi)) pass |= 1u << jj;
-                }
-                if (pass) {
-#pragma unroll
-                    for (int jj = 0; jj < 8; jj++) s_keys[jj][threadIdx.x] = keys[jj];
-                    while (pass) {
-                        const int jj = __ffs(pass) - 1;
-                        pass &= pass - 1;
-                        const int64_t key = s_keys[jj][threadIdx.x];
-                        const int32_t id = (int32_t)(nbase + 8 * c + jj);
-                        if (less_pair(key, id, wk, wi)) list_put(lk, li, wk, wi, wp, key, id);
-                    }
+        int wp = 0, cnt = 0;
+        auto flush = [&]() {
+            const int mx = __reduce_max_sync(0xffffffffu, cnt);
+            for (int i = 0; i < mx; i++) {
+                if (i < cnt) {
+                    const int64_t key = q_key[i * EPI + et];
+                    const int32_t id = q_id[i * EPI + et];
+                    if (less_pair(key, id, wk, wi)) list_put(lk, li, wk, wi, wp, key, id);
                 }
             }
+            cnt = 0;
+        };
+        bool ok = true;
+        for (int j = 0; j < ntl; j++) {
+            const int b = j & 1;
+            const int64_t nbase = (int64_t)(t0 + j) * DBN + HALF * half;
+            // this tile's squared norms, fetched before the wait: lane l holds columns l and 32 + l
+            const int64_t dn0 = (int64_t)__ldg(p.dn + min(nbase + lane, p.n - 1));
+            const int64_t dn1 = lane + 32 < HALF ? (int64_t)__ldg(p.dn + min(nbase + 32 + lane, p.n - 1)) : 0;
+            ok = __all_sync(0xffffffffu, mbar_wait(tfull0 + 8 * b, (uint32_t)(j >> 1) & 1u));  // tcgen05.ld is warp-collective
+            if (!ok) { s_fail = 1; break; }
+            fence_after();
+            const uint32_t acc = taddr + b * ACC_COLS + HALF * half;
+#pragma unroll 1
+            for (int c = 0; c < HALF / 8; c++) {
+                uint32_t g0[8], g1[8], g2[8];
+                tmem_ld8(acc + 8 * c, g0);
+                tmem_ld8(acc + DBN + 8 * c, g1);
+                tmem_ld8(acc + 2 * DBN + 8 * c, g2);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-            for (int c = 0; c < 4; c++) tmem_st16_zero(taddr + 2 * DBN + 64 * half + 16 * c);
+                for (int jj = 0; jj < 8; jj++) {
+                    const int col = 8 * c + jj;
+                    const int64_t dnc = (int64_t)__shfl_sync(0xffffffffu, (long long)(col < 32 ? dn0 : dn1), col & 31);
+                    const int64_t n = nbase + col;
+                    const int64_t h = (int64_t)(int32_t)g0[jj] + (int64_t)(int32_t)g1[jj] * 256 +
+                                      (int64_t)(int32_t)g2[jj] * 65536;
+                    const int64_t key = wsub(dnc, (int64_t)((uint64_t)h << sh));
+                    if (n < p.n && less_pair(key, (int32_t)n, wk, wi)) {
+                        q_key[cnt * EPI + et] = key;
+                        q_id[cnt * EPI + et] = (int32_t)n;
+                        cnt++;
+                    }
+                }
+                if (__any_sync(0xffffffffu, cnt > CAP - 8)) flush();
+            }
+#pragma unroll
+            for (int c = 0; c < HALF; c += 8) tmem_st8_zero(taddr + b * ACC_COLS + 2 * DBN + HALF * half + c);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty);
+            if (lane == 0) mbar_arrive(tempty0 + 8 * b);
         }
+        flush();
         if (ok && row < p.nq) {
             const size_t base = ((size_t)row * p.nslots + (size_t)blockIdx.y * 2 + half) * T;
 #pragma unroll
