@@ -57,7 +57,7 @@ int gemm_prepare(const WDesc& w, GemmPlan& plan, cudaStream_t st, std::string& e
 int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPlan& plan, int64_t* c, int64_t ldc,
              int shift, const int64_t* r, int64_t ldr, GemmWorkspace& ws, cudaStream_t st) {
     if (M <= 0) return 0;
-    if (!r && gemv_supported(w, M) && gemv_reserve(ws, M, (int)w.K, st))  // decode-shaped: stream the packed blocks once
+    if (!r && gemv_supported(w, M) && gemv_reserve(ws, M, (int)w.N, (int)w.K, st))  // decode-shaped: stream the packed blocks once
         return gemv_exact(a, lda, M, w, c, ldc, shift, ws, st);
     if (!plan.use_tc) return gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st);
     const int64_t mpad = round_up(M, tc::BM);
@@ -68,8 +68,7 @@ int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPla
         ws.bytes = 0;
         if (cudaMalloc(&ws.p, need) != cudaSuccess) return gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st);
         ws.bytes = need;
-        ws.tag = 0;
-        cudaMemsetAsync(ws.p, 0, 256, st);  // flag words (the GEMV's overflow word starts below every tag)
+        cudaMemsetAsync(ws.p, 0, need, st);  // flag words, and the GEMV's row-tile counters start at zero
     }
     int* flag = (int*)ws.p;
     int8_t* planes = (int8_t*)ws.p + 256;
@@ -88,7 +87,6 @@ void gemm_workspace_free(GemmWorkspace& ws) {
     if (ws.p) cudaFree(ws.p);
     ws.p = nullptr;
     ws.bytes = 0;
-    ws.tag = 0;
 }
 
 }  // namespace slx

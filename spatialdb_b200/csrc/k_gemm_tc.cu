@@ -378,6 +378,20 @@ bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int pla
     return r == CUDA_SUCCESS;
 }
 
+bool encode_rows_u16(void* map128, const void* base, int64_t row_u16, int64_t rows, int box_x, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || box_x < 8 || box_x > 256 || (box_x * 2) % 16 || box_rows < 1 || box_rows > 256) return false;
+    if (((uintptr_t)base & 15) != 0 || (row_u16 * 2) % 16 != 0) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)row_u16, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(row_u16 * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn((CUtensorMap*)map128, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box,
+                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 void weight_tz(const WDesc& w, int8_t* tz, cudaStream_t st) {
     k_weight_tz<<<(unsigned)w.N, 256, 0, st>>>(w, tz);
 }

@@ -26,7 +26,7 @@ struct GemmWorkspace {
     void* p = nullptr;
     size_t bytes = 0;
     int* err = nullptr;  // device error word (bounded-wait timeouts)
-    unsigned tag = 0;    // last GEMV call tag (k_gemv.cu)
+    unsigned tag = 0;    // last GEMV call's tag (the GEMV's overflow word is compared with it)
 };
 
 // Tensor-core kernel launchers (k_gemm_tc.cu).
@@ -36,6 +36,8 @@ constexpr int SBN = 48;  // key columns per CTA in the attention-score GEMM (5 x
 // Encodes a TMA map over int8 digit planes [batch][planes][rows][kpad] with a
 // (128 B, box_rows, planes, 1) box.
 bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows, int64_t batch = 1);
+// Encodes a TMA map over `rows` rows of row_u16 16-bit elements (no swizzle), box (box_x, box_rows).
+bool encode_rows_u16(void* map128, const void* base, int64_t row_u16, int64_t rows, int box_x, int box_rows);
 // Per-row common trailing zeros of the Q30 composites -> tz[N].
 void weight_tz(const WDesc& w, int8_t* tz, cudaStream_t st);
 // Digits of the widest composite (after the optional per-row shift tz).
@@ -63,15 +65,12 @@ int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPla
 void gemm_workspace_free(GemmWorkspace& ws);
 
 // Decode-shaped exact GEMV (M <= 8) straight from packed Q4_0 / Q8_0 blocks with the long
-// composite (k_gemv.cu).
+// composite, digit products on the tensor cores (k_gemv_tc.cu).
 bool gemv_supported(const WDesc& w, int M);
-// Grows ws for an M x K GEMV (clearing its overflow word when it allocates); false when out of memory.
-bool gemv_reserve(GemmWorkspace& ws, int M, int K, cudaStream_t st);
-// Activation digits, then the GEMV proper (exact for any activations). Every prep call takes a new
-// tag that the GEMV compares with the overflow word, so the word never needs clearing.
-int gemv_prep(const int64_t* a, int64_t lda, int M, const WDesc& w, GemmWorkspace& ws, cudaStream_t st);
-int gemv_main(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift,
-              const GemmWorkspace& ws, cudaStream_t st);
+size_t gemv_workspace(int M, int N, int K);
+// Grows ws for an M x N x K GEMV (zeroing it when it allocates); false when out of memory.
+bool gemv_reserve(GemmWorkspace& ws, int M, int N, int K, cudaStream_t st);
+// One launch; bounded-wait timeouts set KERR_TIMEOUT in *ws.err when it is set.
 int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift,
                GemmWorkspace& ws, cudaStream_t st);
 

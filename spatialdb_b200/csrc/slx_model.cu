@@ -807,10 +807,10 @@ slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K,
     w.scale = std::ldexp(1.0, scale_bits);
     cudaStream_t st = pick(ctx, stream);
     if (gemv_supported(w, M)) {  // decode-shaped: packed-block GEMV, queued without a host sync
-        if (!gemv_reserve(ctx->kws, M, K, st)) return set_err(ctx, SLX_EOOM, "GEMV workspace");
-        RUN(KC_SPLIT, 0, (double)M * K * 8, gemv_prep(d_a, K, M, w, ctx->kws, st));
+        if (!gemv_reserve(ctx->kws, M, N, K, st)) return set_err(ctx, SLX_EOOM, "GEMV workspace");
+        ctx->kws.err = ctx->d_flag;
         RUN(KC_GEMV, (double)M * N * K, (double)gguf_byte_count((uint32_t)dtype, elems) + (double)M * (K + N) * 8,
-            gemv_main(d_a, K, M, w, d_c, N, shift, ctx->kws, st));
+            gemv_exact(d_a, K, M, w, d_c, N, shift, ctx->kws, st));
         CK(cudaGetLastError());
         return SLX_OK;
     }

@@ -104,3 +104,32 @@ def test_gemv_non_finite_scales_and_overflow(ctx, oracle):
     np.testing.assert_array_equal(slx.matmul_q30(a, synth.Q4_0, raw, N, ctx=ctx), _ref(oracle, a, synth.Q4_0, raw, N, False, 30))
     a[1, 5] = 1 << 44  # beyond 5 digits: exact fallback
     np.testing.assert_array_equal(slx.matmul_q30(a, synth.Q4_0, raw, N, ctx=ctx), _ref(oracle, a, synth.Q4_0, raw, N, False, 30))
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("dtype", [synth.Q4_0, synth.Q8_0])
+def test_gemv_split_k_uneven(ctx, oracle, M, dtype):
+    """K = 11008 (43 chunks of 256, split unevenly over the CTAs along K) and N with a ragged last
+    row tile: the Int128 partials of every row tile add up exactly."""
+    K, N = 11008, 200
+    rng = np.random.default_rng(M * 17 + dtype)
+    raw = _raw(dtype, rng, N * K)
+    a = rng.integers(-(1 << 38), 1 << 38, (M, K), dtype=np.int64)
+    for shift in (30, 0):
+        got = slx.matmul_q30(a, dtype, raw, N, shift=shift, ctx=ctx)
+        np.testing.assert_array_equal(got, _ref(oracle, a, dtype, raw, N, False, shift))
+
+
+def test_gemv_large_scale_bits_take_general_path(ctx, oracle):
+    """scale_bits beyond 39 can push d * q * 2^s past 2^63 (long.MinValue composites): the general
+    path handles them; the result still matches the reference's composites."""
+    rng = np.random.default_rng(12)
+    K, N = 512, 64
+    raw = synth.random_q8_0(rng, N * K)
+    a = rng.integers(-(1 << 20), 1 << 20, (2, K), dtype=np.int64)
+    f = oracle.dequantize(synth.Q8_0, raw, N * K)
+    w = np.array([int(x) for x in (f.astype(np.float64) * 2.0 ** 45)], dtype=object)
+    w = np.array([v if -(1 << 63) <= v < (1 << 63) else -(1 << 63) for v in w], np.int64)
+    want = oracle.matmul_long(a, 2, K, w, N, 30).reshape(2, N)
+    got = slx.matmul_q30(a, synth.Q8_0, raw, N, scale_bits=45, shift=30, ctx=ctx)
+    np.testing.assert_array_equal(got, want)
