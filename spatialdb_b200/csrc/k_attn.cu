@@ -1,136 +1,393 @@
-// k_attn.cu -- exact integer attention with tensor-core scores.
+// k_attn.cu -- exact integer attention: tcgen05 scores, fixed-point softmax and per-term P.V.
 //
 // Reference semantics (Math/IntegerAttention.cs:60-109, 165-202, 246-289, 333-377), per head:
-//   score[t][s] = (long)((sum_d q[t][d]*k[s][d]) >> 30) / ISqrt64(hd)   (masked slots: -2^29)
-//   p[t][s]     = FixedSoftmax(score[t][:])                              (IntegerTranscendentals.cs:71-97)
-//   out[t][d]   = sum_s (long)(((Int128)p[t][s] * v[s][d]) >> 30)       (floor per term, wrapping sum)
-// Scores come from the tcgen05 digit GEMM (k_gemm_tc.cu, 5 x 5 balanced digits of q and k). The
-// softmax and the per-term floor run here on CUDA cores: with v = v_hi*2^30 + v_lo
-// (v_lo in [0, 2^30)) and 0 <= p <= 2^30,
-//   floor(p*v / 2^30) = p*v_hi + floor(p*v_lo / 2^30),
-// and floor(p*v_lo / 2^30) = umulhi(4p, v_lo) (+ v_lo when p == 2^30), two 32-bit multiplies a term.
-// Any row outside that fast range (q/k wider than 5 digits, an exp above 2^30 after a long
-// wrap-around, |v_hi| >= 2^31) raises the call's flag, and the exact kernel redoes the call.
+//   score[t][s] = (long)((sum_d q[t][d]*k[s][d]) >> shift) / ISqrt64(hd)   (masked slots: -2^29)
+//   p[t][s]     = FixedSoftmax(score[t][:])                                 (IntegerTranscendentals.cs:71-97)
+//   out[t][d]   = sum_s (long)(((Int128)p[t][s] * v[s][d]) >> 30)          (floor per term, long sum)
+//
+// k_scores: q and k of a head are split into 5 balanced base-256 digits (k_split_heads). One CTA
+// keeps its 128-query tile's digit planes in shared memory and streams 16-key tiles of k by TMA;
+// per 32-wide K step one tcgen05.mma per query digit i multiplies against all five key digits
+// stacked along N, so digit pair (i, j) lands in TMEM column block i+j (9 blocks of 16 columns,
+// each an exact int32 sum). Three TMEM accumulators rotate so the epilogue of one tile overlaps
+// the MMAs of the next. With P_s the block sums (|P_s| < 2^25 for hd <= 256),
+//   L = P_0 + 2^8 P_1 + 2^16 P_2 + 2^24 P_3,   H = P_4 + ... + 2^32 P_8,   sum = 2^32 H + L,
+// and for 0 <= shift <= 32, floor(sum / 2^shift) = 2^(32-shift) H + (L >> shift) in wrapping
+// 64-bit arithmetic -- the reference's (long)(Int128 >> shift) without 128-bit work. The epilogue
+// also keeps each row's maximum for the softmax.
+//
+// k_softmax_pv: e = FixedExp(score - max) (the reference's Taylor recurrence, ten terms suffice
+// for 0 <= r < ln 2), p = (e << 30) / sum. With v = v_hi 2^30 + v_lo (0 <= v_lo < 2^30) and
+// 0 <= p <= 2^30,
+//   floor(p v / 2^30) = p v_hi + floor(p v_lo / 2^30),
+// the first part summed in fp64 (exact: sum_s p_s <= 2^30 and |v_hi| < 2^22 keep every partial
+// sum an integer below 2^52) and the second as one mad.hi.u32 per term (the sum stays below
+// sum_s p_s <= 2^30, so 32 bits hold it). Any row outside these fast ranges (q/k wider than five
+// digits, a score difference that wraps, |v_hi| >= 2^22) raises the call's flag, and the exact
+// kernel redoes the call.
+#include <cuda.h>
+
 #include "slx_device.cuh"
 #include "slx_gemm.h"
 #include "slx_kernels.h"
+#include "tc_ptx.cuh"
 
 namespace slx {
 namespace {
 
-constexpr int PR = 16;   // query rows per block
-constexpr int PT = 256;  // threads per block
-constexpr int VT = 32;   // keys per V tile
+using namespace tc;
 
-// Division of n < 2^63 by an invariant d in [1, 2^63): floor via a 64-bit reciprocal estimate and
-// a bounded correction (the estimate is at most 2 below the quotient).
-SLX_DEV uint64_t udiv_inv(uint64_t n, uint64_t d, uint64_t inv) {
-    uint64_t q = __umul64hi(n, inv);
-    uint64_t r = n - q * d;
-    while (r >= d) { q++; r -= d; }
-    return q;
+// ---------------------------------------------------------------------------------------------
+// scores
+// ---------------------------------------------------------------------------------------------
+constexpr int QM = 128;                 // query rows per CTA (TMEM lanes)
+constexpr int NK = 16;                  // keys per tile
+constexpr int NSH = 2 * LA - 1;         // shift blocks of 16 columns
+constexpr int NBUF = 3;                 // TMEM accumulators
+constexpr int BUF_COLS = NSH * NK;      // 144
+constexpr int EPI = 8;                  // epilogue warps (two per TMEM lane quarter)
+constexpr int S_THREADS = 32 * (2 + EPI);
+constexpr uint32_t QPLANE = QM * BK;    // one query digit plane, one 128-byte K block
+constexpr uint32_t KPLANE = NK * BK;
+constexpr uint32_t IDESC_S = idesc_i8(LA * NK);
+static_assert(NBUF * BUF_COLS <= 512, "TMEM holds 512 columns");
+
+struct ScoreParams {
+    int T, SR, nh, zgroup, nkv, ksteps, shift, mask_mode, window, ntiles, stages;  // SR: score row stride (even)
+    int64_t div;
+    int dshift;  // log2(div) when div is a power of two, else -1
+    int64_t* S;
+    int64_t* rmax;
+    const int* skip;
+    int* err;
+};
+
+template <int KB>
+__global__ void __launch_bounds__(S_THREADS, 1)
+k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, ScoreParams p) {
+    constexpr uint32_t QBYTES = KB * LA * QPLANE;
+    constexpr uint32_t KSTAGE = KB * LA * KPLANE;
+    if (*p.skip) return;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const int nst = p.stages;
+    uint64_t* bars = (uint64_t*)(smem + QBYTES + (size_t)nst * KSTAGE);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + nst), qfull = smem_u32(bars + 2 * nst);
+    const uint32_t done0 = smem_u32(bars + 2 * nst + 1), tfree0 = smem_u32(bars + 2 * nst + 1 + NBUF);
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * nst + 1 + 2 * NBUF);
+    __shared__ int s_fail;
+    __shared__ int64_t s_max[QM];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        for (int i = 0; i < nst; i++) {
+            mbar_init(full0 + 8 * i, 1);
+            mbar_init(empty0 + 8 * i, 1);
+        }
+        mbar_init(qfull, 1);
+        for (int b = 0; b < NBUF; b++) {
+            mbar_init(done0 + 8 * b, 1);
+            mbar_init(tfree0 + 8 * b, EPI);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int q4 = warp & 3, half = (warp - 2) >> 2;           // epilogue: lane quarter, column half
+    const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
+    if (warp >= 2) {  // every MMA accumulates: start from zero
+#pragma unroll 1
+        for (int b = 0; b < NBUF; b++)
+#pragma unroll
+            for (int s = 0; s < NSH; s++) tmem_st8_zero(tmem + lane_base + b * BUF_COLS + s * NK + 8 * half);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+
+    const int m0 = blockIdx.x * QM, z = blockIdx.y;
+    const int zb = (z / p.nh) * p.nkv + (z % p.nh) / p.zgroup;
+    const uint32_t sq = smem_u32(smem), sk = sq + QBYTES;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer: the query tile once, then the key tiles through the ring
+            mbar_expect_tx(qfull, QBYTES);
+#pragma unroll
+            for (int kb = 0; kb < KB; kb++) tma_load_4d(sq + kb * LA * QPLANE, &tmQ, kb * BK, m0, 0, z, qfull);
+            int issued = 0;
+            for (int t = 0; t < p.ntiles; t++) {
+                const int s = t % nst;
+                if (!mbar_wait(empty0 + 8 * s, ((uint32_t)(t / nst) & 1u) ^ 1u)) { s_fail = 1; break; }
+                if (*(volatile int*)&s_fail) break;
+                mbar_expect_tx(full0 + 8 * s, KSTAGE);
+#pragma unroll
+                for (int kb = 0; kb < KB; kb++)
+                    tma_load_4d(sk + s * KSTAGE + kb * LA * KPLANE, &tmK, kb * BK, t * NK, 0, zb, full0 + 8 * s);
+                issued = t + 1;
+            }
+            if (*(volatile int*)&s_fail) {  // let copies still in flight land before the CTA exits
+                mbar_wait(qfull, 0);
+                for (int t = issued - nst < 0 ? 0 : issued - nst; t < issued; t++)
+                    mbar_wait(full0 + 8 * (t % nst), (uint32_t)(t / nst) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            bool ok = mbar_wait(qfull, 0);
+            for (int t = 0; ok && t < p.ntiles; t++) {
+                const int s = t % nst, b = t % NBUF;
+                if (!mbar_wait(full0 + 8 * s, (uint32_t)(t / nst) & 1u) ||
+                    !mbar_wait(tfree0 + 8 * b, ((uint32_t)(t / NBUF) & 1u) ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                fence_after();
+                const uint32_t kst = sk + s * KSTAGE, d = tmem + b * BUF_COLS;
+                for (int kk = 0; kk < p.ksteps; kk++) {
+                    const uint32_t koff = (kk >> 2) * (LA * KPLANE) + (kk & 3) * 32;
+                    const uint32_t qoff = (kk >> 2) * (LA * QPLANE) + (kk & 3) * 32;
+                    const uint64_t bdesc = sw128_desc(kst + koff);
+#pragma unroll
+                    for (int i = 0; i < LA; i++) umma_i8(d + i * NK, sw128_desc(sq + qoff + i * QPLANE), bdesc, IDESC_S, 1u);
+                }
+                umma_commit(empty0 + 8 * s);
+                umma_commit(done0 + 8 * b);
+            }
+            if (!ok) s_fail = 1;
+        }
+    } else {  // epilogue: row = TMEM lane, 8 of each tile's 16 keys
+        const int row = m0 + 32 * q4 + lane;
+        const bool row_ok = row < p.T;
+        int64_t* srow = p.S + ((int64_t)z * p.T + (row_ok ? row : 0)) * p.SR;
+        const int ws = row - p.window + 1;
+        const double rdiv = 1.0 / (double)p.div;
+        int64_t mx = INT64_MIN;
+#pragma unroll 1
+        for (int t = 0; t < p.ntiles; t++) {
+            const int b = t % NBUF;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(done0 + 8 * b, (uint32_t)(t / NBUF) & 1u));
+            if (!ok) { s_fail = 1; break; }
+            fence_after();
+            uint32_t v[NSH][8];
+            const uint32_t ta = tmem + lane_base + b * BUF_COLS + 8 * half;
+#pragma unroll
+            for (int s = 0; s < NSH; s++) tmem_ld8(ta + s * NK, v[s]);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int s = 0; s < NSH; s++) tmem_st8_zero(ta + s * NK);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tfree0 + 8 * b);
+            const int n0 = t * NK + 8 * half;
+            int64_t o[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint64_t L = (uint64_t)(int64_t)(int32_t)v[0][j] + ((uint64_t)(int64_t)(int32_t)v[1][j] << 8) +
+                                   ((uint64_t)(int64_t)(int32_t)v[2][j] << 16) + ((uint64_t)(int64_t)(int32_t)v[3][j] << 24);
+                const uint64_t H = (uint64_t)(int64_t)(int32_t)v[4][j] + ((uint64_t)(int64_t)(int32_t)v[5][j] << 8) +
+                                   ((uint64_t)(int64_t)(int32_t)v[6][j] << 16) + ((uint64_t)(int64_t)(int32_t)v[7][j] << 24) +
+                                   ((uint64_t)(int64_t)(int32_t)v[8][j] << 32);
+                int64_t x = (int64_t)((H << (32 - p.shift)) + (uint64_t)((int64_t)L >> p.shift));
+                const int n = n0 + j;
+                if ((p.mask_mode >= 1 && n > row) || (p.mask_mode == 2 && n < ws)) {
+                    x = -(1LL << 29);  // maskValue (IntegerAttention.cs:222)
+                } else if (p.dshift >= 0) {  // C# long division truncates toward zero
+                    x = (int64_t)((uint64_t)x + ((uint64_t)(x >> 63) & (uint64_t)(p.div - 1))) >> p.dshift;
+                } else {
+                    x = div_small(x, p.div, rdiv);
+                }
+                o[j] = x;
+                if (n < p.T) mx = max(mx, x);
+            }
+            if (row_ok) {
+                if (n0 + 8 <= p.T) {
+#pragma unroll
+                    for (int j = 0; j < 8; j += 2) *(longlong2*)(srow + n0 + j) = make_longlong2(o[j], o[j + 1]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        if (n0 + j < p.T) srow[n0 + j] = o[j];
+                }
+            }
+        }
+        // row maximum over both column halves
+        if (half == 1) s_max[32 * q4 + lane] = mx;
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI) : "memory");
+        if (half == 0 && row_ok) p.rmax[(int64_t)z * p.T + row] = max(mx, s_max[32 * q4 + lane]);
+    }
+    fence_before();
+    __syncthreads();
+    if (s_fail && threadIdx.x == 0 && p.err) atomicOr(p.err, KERR_TIMEOUT);
+    if (warp == 1) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    }
 }
 
-// out[t][d] = sum_s floor(p[t][s] * v[s][d] / 2^30) for the block's rows, wrapping sums.
-// p * v = p * v_hi * 2^30 + p * v_lo, so each term is p*v_hi + umulhi(p, 4*v_lo) exactly.
-template <int RPT, int HD>
-__device__ __forceinline__ void pv_rows(const uint32_t* __restrict__ P, int Tp, const int64_t* __restrict__ vb, int64_t ldv,
-                                        uint32_t* Vlo4, int32_t* Vhi, int T, int t0, int64_t* __restrict__ O, int64_t ldo,
-                                        int b, int h, int* s_bad) {
-    constexpr int G = PT / HD;  // row groups
-    static_assert(G * RPT == PR, "rows per block");
-    const int d = threadIdx.x % HD, g = threadIdx.x / HD;
-    int64_t acc_hi[RPT];   // sum of p * v_hi (two's-complement wrap, as the reference's long adds)
-    uint64_t acc_lo[RPT];  // sum of floor(p * v_lo / 2^30)
-#pragma unroll
-    for (int j = 0; j < RPT; j++) { acc_hi[j] = 0; acc_lo[j] = 0; }
-    for (int s0 = 0; s0 < Tp; s0 += VT) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < VT * HD; i += PT) {
-            const int s = s0 + i / HD, dd = i % HD;
-            int64_t v = s < T ? vb[(int64_t)s * ldv + dd] : 0;
-            const int64_t hi = v >> 30;
-            if (hi < INT32_MIN || hi > INT32_MAX) *s_bad = 1;
-            Vhi[i] = (int32_t)hi;
-            Vlo4[i] = (uint32_t)(v & ((1LL << 30) - 1)) << 2;
-        }
-        __syncthreads();
-        if (*s_bad) return;
-        const int nk = min(VT, Tp - s0);
-        for (int s = 0; s < nk; s += 4) {
-            uint32_t lo[4];
-            int32_t hi[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                lo[u] = Vlo4[(s + u) * HD + d];
-                hi[u] = Vhi[(s + u) * HD + d];
-            }
-#pragma unroll
-            for (int j = 0; j < RPT; j++) {
-                const uint4 p4 = *(const uint4*)(P + (size_t)(g + G * j) * Tp + s0 + s);
-                int64_t ah = acc_hi[j];
-                // p <= 2^30 fits s32: one mad.wide.s32 per term (64-bit wrap-around sum)
-                asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(ah) : "r"((int32_t)p4.x), "r"(hi[0]));
-                asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(ah) : "r"((int32_t)p4.y), "r"(hi[1]));
-                asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(ah) : "r"((int32_t)p4.z), "r"(hi[2]));
-                asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(ah) : "r"((int32_t)p4.w), "r"(hi[3]));
-                acc_hi[j] = ah;
-                // each floor(p * 4 v_lo / 2^32) < 2^30, so four of them sum below 2^32
-                const uint32_t q = __umulhi(p4.x, lo[0]) + __umulhi(p4.y, lo[1]) + __umulhi(p4.z, lo[2]) +
-                                   __umulhi(p4.w, lo[3]);
-                acc_lo[j] += q;
-            }
-        }
-    }
-#pragma unroll
-    for (int j = 0; j < RPT; j++) {
-        const int t = t0 + g + G * j;
-        if (t < T) O[((int64_t)b * T + t) * ldo + (int64_t)h * HD + d] = (int64_t)((uint64_t)acc_hi[j] + acc_lo[j]);
-    }
+template <int KB>
+constexpr int score_stages() { return KB == 1 ? 6 : 2; }
+
+template <int KB>
+constexpr size_t score_smem() {
+    return (size_t)KB * LA * QPLANE + (size_t)score_stages<KB>() * KB * LA * KPLANE + 1024 +
+           (2 * score_stages<KB>() + 1 + 2 * NBUF + 1) * 8;
 }
+
+template <int KB>
+void launch_scores_kb(const CUtensorMap& tq, const CUtensorMap& tk, ScoreParams p, dim3 grid, cudaStream_t st) {
+    p.stages = score_stages<KB>();
+    constexpr size_t smem = score_smem<KB>();
+    static_assert(smem <= 227 * 1024, "score kernel shared memory");
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(k_scores<KB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        configured = true;
+    }
+    k_scores<KB><<<grid, S_THREADS, smem, st>>>(tq, tk, p);
+}
+
+// ---------------------------------------------------------------------------------------------
+// softmax + P.V
+// ---------------------------------------------------------------------------------------------
+constexpr int PR = 32;  // query rows per block
 
 template <int HD>
-__global__ __launch_bounds__(PT) void k_softmax_pv(const int64_t* __restrict__ S, const int64_t* __restrict__ V,
-                                                   int64_t ldv, int64_t* __restrict__ O, int64_t ldo, int T, int nh,
-                                                   int nkv, const int* __restrict__ skip, int* flag) {
-    constexpr int hd = HD;
+struct Pv {
+    static constexpr int CPT = 4;                      // columns per thread: 2c, 2c+1, HD/2+2c, HD/2+2c+1
+    static constexpr int RPT = HD >= 64 ? 4 : HD / 16; // rows per thread
+    static constexpr int CG = HD / CPT, RG = PR / RPT;
+    static constexpr int THREADS = CG * RG;            // 128 (hd <= 64), 256 (128), 512 (256)
+    static constexpr int VT = HD >= 256 ? 8 : 16;      // keys per chunk
+    static constexpr int PUS = VT + 4;                 // p row strides (4-word bank offset per row)
+    static constexpr int PDS = VT + 2;
+    static constexpr int MINB = THREADS <= 128 ? 4 : 1;
+    // one staging buffer: v >> 30 (fp64), 4 (v mod 2^30) (uint32), p (uint32)
+    static constexpr int VH_BYTES = VT * HD * 8, VL_BYTES = VT * HD * 4, PU_BYTES = PR * PUS * 4;
+    static constexpr int BUF = VH_BYTES + VL_BYTES + PU_BYTES;
+    static constexpr size_t SMEM = 2 * (size_t)BUF + (size_t)PR * PDS * 8;
+};
+
+// V -> v >> 30 as fp64 and 4 * (v mod 2^30) as uint32, per (sequence, kv head) [T][HD]; the uint32
+// plane stores each P.V thread's four columns (2g, 2g+1, HD/2+2g, HD/2+2g+1) adjacent. |v >> 30|
+// >= 2^22 sets the flag (the fp64 sums would no longer be exact).
+template <int HD>
+__global__ void k_split_v(const int64_t* __restrict__ V, int64_t ldv, int T, int nkv, double* __restrict__ Vh,
+                          uint32_t* __restrict__ Vl, const int* __restrict__ skip, int* flag) {
     if (*skip) return;
-    extern __shared__ uint8_t sm[];
-    const int Tp = (T + 3) & ~3;                                   // P rows padded to 4 keys (16 B)
-    uint32_t* P = (uint32_t*)sm;                                   // [PR][Tp], p in [0, 2^30]
-    uint32_t* Vlo4 = P + (size_t)PR * Tp;                          // [VT][hd], 4 * (v mod 2^30)
-    int32_t* Vhi = (int32_t*)(Vlo4 + (size_t)VT * hd);             // [VT][hd], v >> 30
+    const int zk = blockIdx.y, b = zk / nkv, kvh = zk % nkv;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= T * HD) return;
+    const int s = i / HD, d = i % HD;
+    const int64_t v = V[((int64_t)b * T + s) * ldv + (int64_t)kvh * HD + d];
+    const int64_t hi = v >> 30;
+    if (hi < -(1LL << 22) || hi >= (1LL << 22)) atomicOr(flag, 1);
+    const int64_t base = (int64_t)zk * T * HD;
+    Vh[base + i] = (double)hi;
+    const int g = d < HD / 2 ? d >> 1 : (d - HD / 2) >> 1, j = d < HD / 2 ? (d & 1) : 2 + (d & 1);
+    Vl[base + (int64_t)s * HD + 4 * g + j] = (uint32_t)(v & ((1LL << 30) - 1)) << 2;
+}
+
+// FixedExp(x) for the softmax's x = score - max (IntegerTranscendentals.cs FixedExp): k = -ceil(-x / ln2),
+// r = x - k ln2 in [0, ln2), e^r by the truncating Taylor recurrence term = (term * r >> 30) / n, then
+// e^r >> -k. Every term past the tenth is zero for r < ln2, and (term * r) >> 30 = umulhi(term, 4r).
+// x > 0 (a wrapped difference) and x near long.MinValue (where the reference's own range reduction
+// wraps) set bad.
+SLX_DEV uint32_t exp_nonpos30(int64_t x, bool& bad) {
+    constexpr int64_t LN2 = 744261117;  // (long)(0.6931471805599453 * 2^30)
+    if (x > 0 || x < -(1LL << 62)) { bad = true; return 0; }
+    if (x < -30 * LN2) return 0;  // a shift of 31 or more clears e^r < 2^31
+    const int64_t nx = -x;        // < 2^35, exact in double
+    int64_t c = (int64_t)((double)nx * (1.0 / (double)LN2));
+    int64_t r = c * LN2 - nx;     // c = ceil(nx / ln2) <=> 0 <= r < ln2
+    if (r < 0) { c++; r += LN2; }
+    else if (r >= LN2) { c--; r -= LN2; }
+    const uint32_t r4 = (uint32_t)r << 2;
+    uint32_t term = 1u << 30, sum = 1u << 30;
+#pragma unroll
+    for (int n = 1; n <= 10; n++) {
+        term = __umulhi(term, r4) / (uint32_t)n;
+        sum += term;
+    }
+    return sum >> c;  // c <= 30
+}
+
+// floor(e * 2^30 / sum) for e <= 2^30 and sum in [1, 2^41): an fp64 estimate (within one) corrected
+// by the exact remainder.
+SLX_DEV uint32_t p_div(uint32_t e, uint64_t sum, double inv30) {
+    int64_t q = (int64_t)((double)e * inv30);
+    int64_t r = (int64_t)(((uint64_t)e << 30) - (uint64_t)q * sum);
+    if (r < 0) q--;
+    else if (r >= (int64_t)sum) q++;
+    return (uint32_t)q;
+}
+
+SLX_DEV void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+SLX_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+SLX_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// One block: PR query rows of one head.
+//  1. softmax, warp per row, in place over the row's score storage (row stride SR int64): pass one
+//     writes e = FixedExp(score - max) as uint32 over the first half (each 128-key chunk is read
+//     completely before its e values are written), pass two rewrites them as p = (e << 30) / sum
+//     and zeroes p up to the next multiple of four keys;
+//  2. P.V over chunks of VT keys: p, v >> 30 and 4 (v mod 2^30) arrive by cp.async into one of two
+//     buffers while the other chunk computes; p is widened to fp64 once per chunk. Thread (rg, cg)
+//     owns rows rg*RPT .. and columns 2cg, 2cg+1, HD/2+2cg, HD/2+2cg+1.
+template <int HD>
+__global__ __launch_bounds__(Pv<HD>::THREADS, Pv<HD>::MINB) void k_softmax_pv(
+    int64_t* S, int SR, const int64_t* __restrict__ rmax, const double* __restrict__ Vh, const uint32_t* __restrict__ Vl,
+    int64_t* __restrict__ O, int64_t ldo, int T, int nh, int nkv, const int* __restrict__ skip, int* flag) {
+    using C = Pv<HD>;
+    constexpr int TH = C::THREADS, VT = C::VT, RPT = C::RPT, CG = C::CG, PUS = C::PUS, PDS = C::PDS;
+    constexpr int SU = 4;  // keys per lane per softmax chunk (loads batched, exps interleaved)
+    if (*skip) return;
+    extern __shared__ __align__(16) uint8_t sm[];
+    double* Pd = (double*)(sm + 2 * C::BUF);  // [PR][PDS]
     __shared__ int s_bad;
     const int h = blockIdx.y, b = blockIdx.z, t0 = blockIdx.x * PR;
-    const int kvh = h / (nh / nkv);
+    const int z = b * nh + h, zk = b * nkv + h / (nh / nkv);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int T4 = (T + 3) & ~3;
     if (threadIdx.x == 0) s_bad = 0;
     __syncthreads();
 
-    // ---- softmax rows (FixedSoftmax), two rows per warp
-    for (int r = warp; r < PR; r += PT / 32) {
+    // ---- 1. softmax rows
+    for (int r = warp; r < PR; r += TH / 32) {
         const int t = t0 + r;
-        uint32_t* prow = P + (size_t)r * Tp;
-        for (int s = T + lane; s < Tp; s += 32) prow[s] = 0;
-        if (t >= T) {
-            for (int s = lane; s < T; s += 32) prow[s] = 0;
-            continue;
-        }
-        const int64_t* srow = S + (((int64_t)b * nh + h) * T + t) * T;
-        int64_t mx = INT64_MIN;
-        for (int s = lane; s < T; s += 32) mx = max(mx, srow[s]);
-        mx = warp_max_i64(mx);
+        if (t >= T) continue;
+        const int64_t* srow = S + ((int64_t)z * T + t) * SR;
+        uint32_t* prow = (uint32_t*)(S + ((int64_t)z * T + t) * SR);
+        const int64_t mx = rmax[(int64_t)z * T + t];
         uint64_t sum = 0;
         bool bad = false;
-        for (int s = lane; s < T; s += 32) {
-            int64_t e = fixed_exp30(wsub(srow[s], mx));
-            bad |= e < 0 || e > (1LL << 30);
-            prow[s] = (uint32_t)e;
-            sum += (uint64_t)e;
+        for (int s0 = 0; s0 < T; s0 += 32 * SU) {
+            int64_t x[SU];
+#pragma unroll
+            for (int u = 0; u < SU; u++) {
+                const int sk = s0 + 32 * u + lane;
+                x[u] = sk < T ? srow[sk] : mx;
+            }
+            __syncwarp();  // this chunk is read before its e values overwrite the first half of it
+#pragma unroll
+            for (int u = 0; u < SU; u++) {
+                const int sk = s0 + 32 * u + lane;
+                const uint32_t e = exp_nonpos30(wsub(x[u], mx), bad);
+                if (sk < T) { prow[sk] = e; sum += e; }
+            }
         }
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, (unsigned long long)sum, o);
-        bad = __any_sync(0xffffffffu, bad);
-        if (bad) {
+        if (__any_sync(0xffffffffu, bad)) {
             if (lane == 0) s_bad = 1;
             continue;
         }
@@ -138,80 +395,191 @@ __global__ __launch_bounds__(PT) void k_softmax_pv(const int64_t* __restrict__ S
         if (sum == 0) {  // uniform = one / len
             for (int s = lane; s < T; s += 32) prow[s] = (uint32_t)((1LL << 30) / T);
         } else {
-            const uint64_t inv = ~0ULL / sum;
-            for (int s = lane; s < T; s += 32) prow[s] = (uint32_t)udiv_inv((uint64_t)prow[s] << 30, sum, inv);
+            const double inv30 = 1073741824.0 / (double)sum;
+            for (int s = lane; s < T; s += 32) prow[s] = p_div(prow[s], sum, inv30);
         }
+        if (lane < T4 - T) prow[T + lane] = 0;
     }
     __syncthreads();
     if (s_bad) {
         if (threadIdx.x == 0) atomicOr(flag, 1);
         return;
     }
-    // ---- PV. Thread (g, d): d = tid % hd, rows g, g+G, ... (G = PT/hd row groups). Each key's
-    // (v_hi, 4*v_lo) is read once per thread and used for all its rows; p comes four keys at a time.
-    const int64_t* vb = V + (int64_t)b * T * ldv + (int64_t)kvh * hd;
-    pv_rows<PR * HD / PT, HD>(P, Tp, vb, ldv, Vlo4, Vhi, T, t0, O, ldo, b, h, &s_bad);
-    __syncthreads();
-    if (s_bad && threadIdx.x == 0) atomicOr(flag, 1);
+
+    // ---- 2. P.V
+    const int cg = threadIdx.x % CG, rg = threadIdx.x / CG;
+    const int c0 = 2 * cg, c1 = HD / 2 + 2 * cg;
+    const double* vh0 = Vh + (int64_t)zk * T * HD;
+    const uint32_t* vl0 = Vl + (int64_t)zk * T * HD;
+    const uint32_t sbase = tc::smem_u32(sm);
+    auto issue = [&](int k0, int buf) {
+        const uint32_t dst = sbase + buf * C::BUF;
+        const int keys = min(VT, T - k0);
+        for (int g = threadIdx.x; g < C::VH_BYTES / 16; g += TH) {  // v >> 30: HD/2 granules a key
+            const int s = g / (HD / 2);
+            cp_async16(dst + g * 16, s < keys ? vh0 + (int64_t)k0 * HD + g * 2 : vh0, s < keys ? 16u : 0u);
+        }
+        for (int g = threadIdx.x; g < C::VL_BYTES / 16; g += TH) {  // 4 (v mod 2^30): HD/4 granules a key
+            const int s = g / (HD / 4);
+            cp_async16(dst + C::VH_BYTES + g * 16, s < keys ? vl0 + (int64_t)k0 * HD + g * 4 : vl0, s < keys ? 16u : 0u);
+        }
+        for (int g = threadIdx.x; g < PR * (VT / 4); g += TH) {  // p: VT/4 granules a row
+            const int r = g / (VT / 4), s = k0 + 4 * (g % (VT / 4));
+            const int t = t0 + r;
+            const bool ok = t < T && s < T4;
+            const uint32_t* src = ok ? (const uint32_t*)(S + ((int64_t)z * T + t) * SR) + s : (const uint32_t*)S;
+            cp_async16(dst + C::VH_BYTES + C::VL_BYTES + (r * PUS + 4 * (g % (VT / 4))) * 4, src, ok ? 16u : 0u);
+        }
+        cp_async_commit();
+    };
+    double ah[RPT][4];
+    uint32_t al[RPT][4];
+#pragma unroll
+    for (int r = 0; r < RPT; r++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) { ah[r][c] = 0.0; al[r][c] = 0; }
+    issue(0, 0);
+    for (int k0 = 0, buf = 0; k0 < T; k0 += VT, buf ^= 1) {
+        cp_async_wait_all();
+        __syncthreads();  // chunk k0 is in for every thread; the other buffer and Pd are free
+        if (k0 + VT < T) issue(k0 + VT, buf ^ 1);
+        const double* Vhs = (const double*)(sm + buf * C::BUF);
+        const uint32_t* Vls = (const uint32_t*)(sm + buf * C::BUF + C::VH_BYTES);
+        const uint32_t* Pu = (const uint32_t*)(sm + buf * C::BUF + C::VH_BYTES + C::VL_BYTES);
+        for (int i = threadIdx.x; i < PR * VT; i += TH) {
+            const int r = i / VT, s = i % VT;
+            Pd[r * PDS + s] = (double)Pu[r * PUS + s];
+        }
+        __syncthreads();
+#pragma unroll 2
+        for (int s = 0; s < VT; s += 4) {
+            uint4 pu[RPT];
+#pragma unroll
+            for (int r = 0; r < RPT; r++) pu[r] = *(const uint4*)(Pu + (rg * RPT + r) * PUS + s);
+#pragma unroll
+            for (int u = 0; u < 4; u += 2) {
+                const double2 ha0 = *(const double2*)(Vhs + (s + u) * HD + c0);
+                const double2 ha1 = *(const double2*)(Vhs + (s + u) * HD + c1);
+                const double2 hb0 = *(const double2*)(Vhs + (s + u + 1) * HD + c0);
+                const double2 hb1 = *(const double2*)(Vhs + (s + u + 1) * HD + c1);
+                const uint4 la = *(const uint4*)(Vls + (s + u) * HD + 4 * cg);
+                const uint4 lb = *(const uint4*)(Vls + (s + u + 1) * HD + 4 * cg);
+#pragma unroll
+                for (int r = 0; r < RPT; r++) {
+                    const double2 pd = *(const double2*)(Pd + (rg * RPT + r) * PDS + s + u);
+                    const uint32_t pa = u == 0 ? pu[r].x : pu[r].z, pb = u == 0 ? pu[r].y : pu[r].w;
+                    ah[r][0] = fma(pd.y, hb0.x, fma(pd.x, ha0.x, ah[r][0]));
+                    ah[r][1] = fma(pd.y, hb0.y, fma(pd.x, ha0.y, ah[r][1]));
+                    ah[r][2] = fma(pd.y, hb1.x, fma(pd.x, ha1.x, ah[r][2]));
+                    ah[r][3] = fma(pd.y, hb1.y, fma(pd.x, ha1.y, ah[r][3]));
+                    al[r][0] += __umulhi(pa, la.x) + __umulhi(pb, lb.x);
+                    al[r][1] += __umulhi(pa, la.y) + __umulhi(pb, lb.y);
+                    al[r][2] += __umulhi(pa, la.z) + __umulhi(pb, lb.z);
+                    al[r][3] += __umulhi(pa, la.w) + __umulhi(pb, lb.w);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RPT; r++) {
+        const int t = t0 + rg * RPT + r;
+        if (t >= T) continue;
+        int64_t* orow = O + ((int64_t)b * T + t) * ldo + (int64_t)h * HD;
+        orow[c0] = __double2ll_rz(ah[r][0]) + (int64_t)al[r][0];
+        orow[c0 + 1] = __double2ll_rz(ah[r][1]) + (int64_t)al[r][1];
+        orow[c1] = __double2ll_rz(ah[r][2]) + (int64_t)al[r][2];
+        orow[c1 + 1] = __double2ll_rz(ah[r][3]) + (int64_t)al[r][3];
+    }
 }
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 template <int HD>
-void launch_pv(dim3 grid, size_t smem, const int64_t* scores, const int64_t* v, int64_t ldv, int64_t* out, int64_t ldo,
-               int T, int nh, int nkv, int* flag, cudaStream_t st) {
-    static size_t configured = 0;
-    if (smem > 32 * 1024 && smem > configured) {  // opt in well before 48 KB (static smem adds to it)
+void launch_pv(int B, int T, int nh, int nkv, int64_t* scores, int sr, const int64_t* rmax, const int64_t* v, int64_t ldv,
+               double* vh, uint32_t* vl, int64_t* out, int64_t ldo, int* flag, cudaStream_t st) {
+    const dim3 vgrid((unsigned)((T * HD + 255) / 256), (unsigned)(B * nkv));
+    k_split_v<HD><<<vgrid, 256, 0, st>>>(v, ldv, T, nkv, vh, vl, flag, flag);
+    constexpr size_t smem = Pv<HD>::SMEM;
+    static_assert(smem <= 200 * 1024, "softmax/PV shared memory");
+    static bool configured = false;
+    if (!configured) {
         cudaFuncSetAttribute(k_softmax_pv<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured = smem;
+        configured = true;
     }
-    k_softmax_pv<HD><<<grid, PT, smem, st>>>(scores, v, ldv, out, ldo, T, nh, nkv, flag, flag);
+    dim3 grid((unsigned)((T + PR - 1) / PR), (unsigned)nh, (unsigned)B);
+    k_softmax_pv<HD><<<grid, Pv<HD>::THREADS, smem, st>>>(scores, sr, rmax, vh, vl, out, ldo, T, nh, nkv, flag, flag);
+}
+
+struct Layout {
+    int64_t kpad, tq, tk, sr, qbytes, kbytes, sbytes, mbytes, vhbytes, vlbytes;
+};
+
+Layout layout(int B, int T, int nh, int nkv, int hd) {
+    Layout l;
+    l.kpad = round_up(hd, BK);
+    l.tq = round_up(T, QM);
+    l.tk = round_up(T, NK);
+    l.qbytes = round_up((int64_t)B * nh * LA * l.tq * l.kpad, 256);
+    l.kbytes = round_up((int64_t)B * nkv * LA * l.tk * l.kpad, 256);
+    l.sr = round_up(T, 2);
+    l.sbytes = round_up((int64_t)B * nh * T * l.sr * 8, 256);
+    l.mbytes = round_up((int64_t)B * nh * T * 8, 256);
+    l.vhbytes = round_up((int64_t)B * nkv * T * hd * 8, 256);
+    l.vlbytes = (int64_t)B * nkv * T * hd * 4;
+    return l;
 }
 }  // namespace
 
 size_t attention_tc_workspace(int B, int T, int nh, int nkv, int hd) {
-    const int64_t kpad = round_up(hd, tc::BK);
-    const int64_t qbytes = (int64_t)B * nh * tc::LA * round_up(T, tc::BM) * kpad;
-    const int64_t kbytes = (int64_t)B * nkv * tc::LA * round_up(T, tc::SBN) * kpad;
-    const int64_t sbytes = (int64_t)B * nh * T * T * 8;
-    return (size_t)(256 + round_up(qbytes, 256) + round_up(kbytes, 256) + sbytes);
+    const Layout l = layout(B, T, nh, nkv, hd);
+    return (size_t)(256 + l.qbytes + l.kbytes + l.sbytes + l.mbytes + l.vhbytes + l.vlbytes);
 }
-
-size_t softmax_pv_smem(int T, int hd) { return (size_t)PR * ((T + 3) & ~3) * 4 + (size_t)VT * hd * 8; }
 
 bool attention_tc_supported(int T, int nh, int nkv, int hd) {
     const bool hd_ok = hd == 16 || hd == 32 || hd == 64 || hd == 128 || hd == 256;
-    return hd_ok && nkv > 0 && nh % nkv == 0 && softmax_pv_smem(T, hd) <= 200 * 1024;
+    return hd_ok && T > 0 && nkv > 0 && nh % nkv == 0;
 }
 
 int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
                  int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int score_shift, int64_t sqrt_hd,
                  int mode, int window, void* ws, int* err, cudaStream_t st) {
-    const int64_t kpad = round_up(hd, tc::BK);
-    const int64_t tq = round_up(T, tc::BM), tk = round_up(T, tc::SBN);
+    if (score_shift < 0 || score_shift > 32 || sqrt_hd < 1) return -1;
+    const Layout l = layout(B, T, nh, nkv, hd);
     uint8_t* base = (uint8_t*)ws;
     int* flag = (int*)base;
     int8_t* qp = (int8_t*)(base + 256);
-    const int64_t qbytes = round_up((int64_t)B * nh * tc::LA * tq * kpad, 256);
-    int8_t* kp = qp + qbytes;
-    const int64_t kbytes = round_up((int64_t)B * nkv * tc::LA * tk * kpad, 256);
-    int64_t* scores = (int64_t*)(kp + kbytes);
+    int8_t* kp = qp + l.qbytes;
+    int64_t* scores = (int64_t*)(kp + l.kbytes);
+    int64_t* rmax = (int64_t*)((uint8_t*)scores + l.sbytes);
+    double* vh = (double*)((uint8_t*)rmax + l.mbytes);
+    uint32_t* vl = (uint32_t*)((uint8_t*)vh + l.vhbytes);
     alignas(64) unsigned char mq[128], mk[128];
-    if (!tc::encode_planes(mq, qp, kpad, tq, tc::LA, tc::BM, (int64_t)B * nh) ||
-        !tc::encode_planes(mk, kp, kpad, tk, tc::LA, tc::SBN, (int64_t)B * nkv))
+    if (!encode_planes(mq, qp, l.kpad, l.tq, LA, QM, (int64_t)B * nh) ||
+        !encode_planes(mk, kp, l.kpad, l.tk, LA, NK, (int64_t)B * nkv))
         return -1;
     cudaMemsetAsync(flag, 0, sizeof(int), st);
-    tc::split_heads(q, ldq, B, T, nh, hd, tq, kpad, qp, flag, st);
-    tc::split_heads(k, ldk, B, T, nkv, hd, tk, kpad, kp, flag, st);
-    tc::launch_scores(mq, mk, B, T, nh, nkv, tk, kpad, score_shift, sqrt_hd, mode, window, scores, flag, err, st);
-    const size_t smem = softmax_pv_smem(T, hd);
-    dim3 grid((unsigned)((T + PR - 1) / PR), (unsigned)nh, (unsigned)B);
+    split_heads(q, ldq, B, T, nh, hd, l.tq, l.kpad, qp, flag, st);
+    split_heads(k, ldk, B, T, nkv, hd, l.tk, l.kpad, kp, flag, st);
+
+    ScoreParams sp;
+    sp.T = T; sp.SR = (int)l.sr; sp.nh = nh; sp.zgroup = nh / nkv; sp.nkv = nkv;
+    sp.ksteps = (hd + 31) / 32;
+    sp.shift = score_shift; sp.mask_mode = mode; sp.window = window;
+    sp.ntiles = (int)(l.tk / NK);
+    sp.stages = 0;
+    sp.div = sqrt_hd;
+    sp.dshift = (sqrt_hd & (sqrt_hd - 1)) == 0 ? __builtin_ctzll((unsigned long long)sqrt_hd) : -1;
+    sp.S = scores; sp.rmax = rmax; sp.skip = flag; sp.err = err;
+    const dim3 sgrid((unsigned)(l.tq / QM), (unsigned)(B * nh));
+    if (l.kpad == BK) launch_scores_kb<1>(*(const CUtensorMap*)mq, *(const CUtensorMap*)mk, sp, sgrid, st);
+    else launch_scores_kb<2>(*(const CUtensorMap*)mq, *(const CUtensorMap*)mk, sp, sgrid, st);
+
     switch (hd) {
-        case 16: launch_pv<16>(grid, smem, scores, v, ldv, out, ldo, T, nh, nkv, flag, st); break;
-        case 32: launch_pv<32>(grid, smem, scores, v, ldv, out, ldo, T, nh, nkv, flag, st); break;
-        case 64: launch_pv<64>(grid, smem, scores, v, ldv, out, ldo, T, nh, nkv, flag, st); break;
-        case 128: launch_pv<128>(grid, smem, scores, v, ldv, out, ldo, T, nh, nkv, flag, st); break;
-        default: launch_pv<256>(grid, smem, scores, v, ldv, out, ldo, T, nh, nkv, flag, st); break;
+        case 16: launch_pv<16>(B, T, nh, nkv, scores, (int)l.sr, rmax, v, ldv, vh, vl, out, ldo, flag, st); break;
+        case 32: launch_pv<32>(B, T, nh, nkv, scores, (int)l.sr, rmax, v, ldv, vh, vl, out, ldo, flag, st); break;
+        case 64: launch_pv<64>(B, T, nh, nkv, scores, (int)l.sr, rmax, v, ldv, vh, vl, out, ldo, flag, st); break;
+        case 128: launch_pv<128>(B, T, nh, nkv, scores, (int)l.sr, rmax, v, ldv, vh, vl, out, ldo, flag, st); break;
+        default: launch_pv<256>(B, T, nh, nkv, scores, (int)l.sr, rmax, v, ldv, vh, vl, out, ldo, flag, st); break;
     }
     // the exact kernel redoes the whole call when anything fell outside the fast ranges
     attention(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, score_shift, sqrt_hd, mode, window, st, flag);

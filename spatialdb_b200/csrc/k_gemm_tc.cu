@@ -35,18 +35,12 @@ constexpr int THREADS = 192;
 struct Params {
     int M, N, K, nkb, lw, shift, nstages;
     int64_t* C;
-    int64_t ldc, c_zstride;
+    int64_t ldc;
     const int64_t* R;
     int64_t ldr;
     const int* skip;  // nonzero: an operand did not fit its digits, the exact kernel runs instead
     int* err;         // set on a bounded-wait timeout
-    // batch z = blockIdx.z: A operand batch z, B operand batch (z / zh) * zkv + (z % zh) / zgroup
-    int zh, zgroup, zkv;
-    // epilogue: mode 0 projection (shift, residual); mode 1 attention scores
-    // ((long)(acc >> shift) / div, masked slots -2^29 for mask_mode 1 causal / 2 sliding window)
-    int mode, mask_mode, window;
-    int64_t div;
-    // projections: the weight row n was stored as w >> row_shift[n] (its common trailing zeros)
+    // the weight row n was stored as w >> row_shift[n] (its common trailing zeros)
     const int8_t* row_shift;
 };
 
@@ -102,8 +96,6 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     fence_after();
 
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-    const int z = blockIdx.z;
-    const int zb = (z / p.zh) * p.zkv + (z % p.zh) / p.zgroup;
     const uint32_t sbase = smem_u32(smem);
 
     if (warp == 0) {
@@ -115,8 +107,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                 if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) { s_fail = 1; break; }
                 if (*(volatile int*)&s_fail) break;
                 mbar_expect_tx(full0 + 8 * s, STAGE);
-                tma_load_4d(sbase + s * STAGE, &tmA, kb * BK, m0, 0, z, full0 + 8 * s);
-                tma_load_4d(sbase + s * STAGE + A_STAGE, &tmW, kb * BK, n0, 0, zb, full0 + 8 * s);
+                tma_load_4d(sbase + s * STAGE, &tmA, kb * BK, m0, 0, 0, full0 + 8 * s);
+                tma_load_4d(sbase + s * STAGE + A_STAGE, &tmW, kb * BK, n0, 0, 0, full0 + 8 * s);
                 issued = kb + 1;
             }
             if (*(volatile int*)&s_fail) {  // let copies still in flight land before the CTA exits
@@ -158,9 +150,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                 for (int s = 0; s < S; s++) tmem_ld16(taddr + s * BN + c * 16, v[s]);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 if (row < p.M) {
-                    int64_t* crow = p.C + (int64_t)z * p.c_zstride + (int64_t)row * p.ldc;
-                    const int ws = row - p.window + 1;
-                    const double rdiv = 1.0 / (double)p.div;
+                    int64_t* crow = p.C + (int64_t)row * p.ldc;
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         const int n = n0 + c * 16 + j;
@@ -170,13 +160,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                         for (int s = S - 2; s >= 0; s--) acc = (acc << 8) + (i128)(int32_t)v[s][j];
                         if (p.row_shift) acc <<= p.row_shift[n];
                         int64_t out = p.shift > 0 ? lo64(sar128(acc, p.shift)) : lo64(acc);
-                        if (p.mode == 0) {
-                            if (p.R) out = wadd(out, p.R[(int64_t)row * p.ldr + n]);
-                        } else if ((p.mask_mode >= 1 && n > row) || (p.mask_mode == 2 && n < ws)) {
-                            out = -(1LL << 29);  // maskValue (IntegerAttention.cs:222)
-                        } else {
-                            out = div_small(out, p.div, rdiv);
-                        }
+                        if (p.R) out = wadd(out, p.R[(int64_t)row * p.ldr + n]);
                         crow[n] = out;
                     }
                 }
@@ -359,7 +343,6 @@ void launch_lw(const CUtensorMap& ta, const CUtensorMap& tw, Params p, dim3 grid
 Params base_params() {
     Params p;
     memset(&p, 0, sizeof p);
-    p.zh = 1; p.zgroup = 1; p.zkv = 1; p.div = 1;
     return p;
 }
 }  // namespace
@@ -446,18 +429,6 @@ void split_heads(const int64_t* x, int64_t ld, int B, int T, int nh, int hd, int
                                                                   total);
 }
 
-void launch_scores(const void* tmap_q, const void* tmap_k, int B, int T, int nh, int nkv, int64_t tpad_k, int64_t kpad,
-                   int shift, int64_t div, int mask_mode, int window, int64_t* scores, const int* skip, int* err,
-                   cudaStream_t st) {
-    Params p = base_params();
-    p.M = T; p.N = T; p.K = (int)kpad; p.nkb = (int)(kpad / BK); p.lw = LA; p.shift = shift;
-    p.C = scores; p.ldc = T; p.c_zstride = (int64_t)T * T;
-    p.skip = skip; p.err = err;
-    p.zh = nh; p.zgroup = nh / nkv; p.zkv = nkv;
-    p.mode = 1; p.mask_mode = mask_mode; p.window = window; p.div = div;
-    dim3 grid((unsigned)(tpad_k / SBN), (unsigned)((T + BM - 1) / BM), (unsigned)(B * nh));
-    launch_lw<LA, SBN>(*(const CUtensorMap*)tmap_q, *(const CUtensorMap*)tmap_k, p, grid, st);
-}
 
 }  // namespace tc
 }  // namespace slx

@@ -32,7 +32,6 @@ struct GemmWorkspace {
 // Tensor-core kernel launchers (k_gemm_tc.cu).
 namespace tc {
 constexpr int BM = 128, BN = 64, BK = 128, LA = 5;
-constexpr int SBN = 48;  // key columns per CTA in the attention-score GEMM (5 x 5 digits)
 // Encodes a TMA map over int8 digit planes [batch][planes][rows][kpad] with a
 // (128 B, box_rows, planes, 1) box.
 bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows, int64_t batch = 1);
@@ -52,10 +51,6 @@ void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K,
 // Per-head digit planes of rows at x + (b*T+t)*ld + h*hd -> [(b*nh+h)][LA][tpad][kpad].
 void split_heads(const int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad, int8_t* planes,
                  int* overflow, cudaStream_t st);
-// scores[(b*nh+h)][t][s] = (long)(q.k >> shift) / div with the reference's causal / window mask.
-void launch_scores(const void* tmap_q, const void* tmap_k, int B, int T, int nh, int nkv, int64_t tpad_k, int64_t kpad,
-                   int shift, int64_t div, int mask_mode, int window, int64_t* scores, const int* skip, int* err,
-                   cudaStream_t st);
 }  // namespace tc
 
 bool tc_enabled();
