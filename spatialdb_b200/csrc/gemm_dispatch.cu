@@ -28,7 +28,7 @@ int gemm_prepare(const WDesc& w, GemmPlan& plan, cudaStream_t st, std::string& e
     plan = GemmPlan();
     if (!tc_enabled() || w.K >= 32768 || w.N <= 0 || w.K <= 0) return SLX_OK;
     // Factor each row's common trailing zero bits out of its composites (restored exactly in the
-    // epilogue's Int128 sum), so the digit planes hold fewer significant bits.
+    // epilogue), so the digit planes hold fewer significant bits.
     if (cudaMalloc(&plan.row_shift, (size_t)w.N) != cudaSuccess) { err = "device allocation failed"; return SLX_EOOM; }
     tc::weight_tz(w, plan.row_shift, st);
     int maxd = tc::weight_digits(w, st, err, plan.row_shift);
@@ -44,7 +44,7 @@ int gemm_prepare(const WDesc& w, GemmPlan& plan, cudaStream_t st, std::string& e
     plan.limb_bytes = (size_t)plan.wlimbs * plan.n_pad * plan.k_pad;
     if (cudaMalloc(&plan.limbs, plan.limb_bytes) != cudaSuccess) { err = "device allocation failed"; return SLX_EOOM; }
     tc::split_w(w, plan.wlimbs, plan.n_pad, plan.k_pad, (int8_t*)plan.limbs, st, plan.row_shift);
-    if (!tc::encode_planes(plan.tmap_w, plan.limbs, plan.k_pad, plan.n_pad, plan.wlimbs, tc::BN)) {
+    if (!tc::encode_planes(plan.tmap_w, plan.limbs, plan.k_pad, plan.n_pad, plan.wlimbs, tc::GN, 1, tc::GK)) {
         cudaFree(plan.limbs);
         cudaFree(plan.row_shift);
         plan = GemmPlan();
@@ -73,7 +73,7 @@ int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPla
     int* flag = (int*)ws.p;
     int8_t* planes = (int8_t*)ws.p + 256;
     alignas(64) unsigned char tmap_a[128];
-    if (!tc::encode_planes(tmap_a, planes, plan.k_pad, mpad, tc::LA, tc::BM))
+    if (!tc::encode_planes(tmap_a, planes, plan.k_pad, mpad, tc::LA, tc::GM, 1, tc::GK))
         return gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st);
     cudaMemsetAsync(flag, 0, sizeof(int), st);
     tc::split_a(a, lda, M, (int)w.K, mpad, plan.k_pad, planes, flag, st);

@@ -111,8 +111,8 @@ extern "C" slx_status slx_matmul_q30_noalloc(const int64_t* d_a, int M, int K, i
     w.scale = ldexp(1.0, scale_bits);
 
     alignas(64) unsigned char map_a[128], map_w[128];
-    if (!tc::encode_planes(map_a, a_planes, kpad, mpad, tc::LA, tc::BM) ||
-        !tc::encode_planes(map_w, w_dig, kpad, npad, kWeightDigits, tc::BN))
+    if (!tc::encode_planes(map_a, a_planes, kpad, mpad, tc::LA, tc::GM, 1, tc::GK) ||
+        !tc::encode_planes(map_w, w_dig, kpad, npad, kWeightDigits, tc::GN, 1, tc::GK))
         return SLX_ECUDA;
     if (cudaMemsetAsync(scratch, 0, 256, st) != cudaSuccess) return SLX_ECUDA;  // overflow and error words
     const int64_t tot = npad * kpad;

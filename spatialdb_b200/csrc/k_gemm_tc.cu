@@ -5,17 +5,21 @@
 //     a = sum_i a_i 256^i  (LA = 5 digits: |a| < ~2^39),   w = sum_j w_j 256^j  (LW <= 4 digits),
 // so  sum_k a w = sum_s 256^s P_s  with  P_s = sum_{i+j=s} sum_k a_ik w_jk.
 // Each P_s is an exact int32 (|a_i w_j| <= 2^14, at most 4 pairs per s, K < 32768) and
-// accumulates in TMEM. One tcgen05.mma.kind::i8 per activation digit i and 32-wide K step uses the
-// weight digit planes stacked along N (LW x 64 rows) as the B operand and writes its accumulator at
-// TMEM column offset 64*i: the product a_i*w_j lands in column block i+j, so all pairs of equal
-// shift s sum in the same TMEM columns (S = LA+LW-1 blocks of 64 columns, <= 512).
-// The epilogue combines the S int32 partials per output into Int128, applies the shift (floor) and
-// the optional residual, and stores int64 -- bit-identical to the reference.
+// accumulates in TMEM.
 //
-// Operands arrive by TMA (cp.async.bulk.tensor, 128-byte swizzle, no multicast) into a 2-stage
-// smem ring; one thread issues the MMAs; tcgen05.commit releases ring stages and signals the
-// epilogue. Every mbarrier wait is bounded: on timeout the kernel records an error, waits
-// (bounded) for its outstanding copies, frees TMEM and returns.
+// Tiles are weight-stationary: a tile is GN = 128 weight rows (the MMA's M, one per TMEM lane) by
+// GM = 32 activation rows. One tcgen05.mma.kind::i8 per weight digit j and 32-byte K step takes
+// the five activation digit planes stacked along N (5 x 32 rows) as the B operand and writes at
+// TMEM column offset 32*j, so digit pair (i, j) lands in column block i+j: S = LA+LW-1 blocks of
+// 32 columns (<= 256), two accumulators in the 512 TMEM columns. The kernel is persistent: one CTA
+// per SM walks the tiles; operands stream by TMA (GK-byte K stages with the matching swizzle, no
+// multicast) through a ring of stages while one thread issues the MMAs; the epilogue of one tile (eight warps)
+// overlaps the MMAs of the next. In the epilogue each thread owns one weight row n, so a warp's
+// stores of an output row are 32 consecutive int64 (coalesced, residual loads likewise).
+// The S partials combine in 64-bit arithmetic (sum = 2^32 H + L, H and L below 2^56) into
+// lo64(floor(sum * 2^row_shift / 2^shift)) -- bit-identical to the reference's Int128 result.
+// Every mbarrier wait is bounded: on timeout the kernel records an error, waits (bounded) for its
+// outstanding copies, frees TMEM and returns.
 #include <cuda.h>
 
 #include <cstring>
@@ -28,12 +32,12 @@
 namespace slx {
 namespace tc {
 
-// BM = 128 output rows per CTA (TMEM lanes), BN = 64 output columns, BK = 128 K bytes per ring
-// stage (one 128-byte swizzle row), LA = 5 activation digits (slx_gemm.h).
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, each half of the tile's activation rows
+constexpr int THREADS = 32 * (2 + EPI_WARPS);
+constexpr int NACC = 2;       // TMEM accumulators (tile parity picks one)
 
 struct Params {
-    int M, N, K, nkb, lw, shift, nstages;
+    int M, N, nkb, shift, tiles_m, tiles;
     int64_t* C;
     int64_t ldc;
     const int64_t* R;
@@ -44,24 +48,57 @@ struct Params {
     const int8_t* row_shift;
 };
 
-template <int LW, int BN>
+// K-major operand, 64-byte swizzle: rows of 64 bytes, 8-row groups 512 bytes apart.
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(512 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)4 << 61;
+    return d;
+}
+
+// Bounded spin on an mbarrier phase without suspending (the MMA issuer's waits are short and on the
+// critical path): about two seconds of SM clock, then false.
+__device__ __forceinline__ bool mbar_spin(uint32_t bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 64; i++)
+            if (mbar_try(bar, parity)) return true;
+        if (clock64() - t0 > 4000000000LL) return false;
+    }
+}
+
+template <int LW>
+__host__ __device__ constexpr int gemm_stages() {
+    return (int)((227 * 1024 - 2048) / ((size_t)LW * GN * GK + (size_t)LA * GM * GK)) > 6
+               ? 6
+               : (int)((227 * 1024 - 2048) / ((size_t)LW * GN * GK + (size_t)LA * GM * GK));
+}
+
+// Descriptor of a K-major operand staged with the swizzle that matches GK-byte rows.
+__device__ __forceinline__ uint64_t kdesc(uint32_t addr) { return GK == 128 ? sw128_desc(addr) : sw64_desc(addr); }
+
+template <int LW>
 __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, Params p) {
     constexpr int S = LA + LW - 1;
-    static_assert(S * BN <= 512, "TMEM holds 512 columns");
-    static_assert((BN * LW) % 16 == 0 && BN * LW <= 256, "M=128 MMA needs N a multiple of 16, at most 256");
-    constexpr int A_STAGE = BM * BK * LA;
-    constexpr int W_STAGE = BN * BK * LW;
-    constexpr int STAGE = A_STAGE + W_STAGE;
-    constexpr uint32_t IDESC = idesc_i8(BN * LW);
+    constexpr int ACC = S * GM;  // columns per accumulator
+    static_assert(NACC * ACC <= 512 && S <= 8, "TMEM holds 512 columns; the epilogue combines at most 8 blocks");
+    constexpr int W_ST = LW * GN * GK, A_ST = LA * GM * GK, STAGE = W_ST + A_ST;
+    constexpr int nst = gemm_stages<LW>();
+    constexpr uint32_t IDESC = idesc_i8(LA * GM);
     if (p.skip && *p.skip) return;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    const int nst = p.nstages;
     uint64_t* bars = (uint64_t*)(smem + (size_t)nst * STAGE);
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + nst), done = smem_u32(bars + 2 * nst);
-    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * nst + 1);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + nst);
+    const uint32_t tfull0 = smem_u32(bars + 2 * nst), tfree0 = smem_u32(bars + 2 * nst + NACC);
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * nst + 2 * NACC);
     __shared__ int s_fail;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -71,7 +108,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             mbar_init(full0 + 8 * i, 1);
             mbar_init(empty0 + 8 * i, 1);
         }
-        mbar_init(done, 1);
+        for (int b = 0; b < NACC; b++) {
+            mbar_init(tfull0 + 8 * b, 1);
+            mbar_init(tfree0 + 8 * b, EPI_WARPS);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -82,89 +122,122 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
-
-    // Zero the accumulators: digit products of different i overlap in their column blocks, so every
-    // MMA accumulates.
+    const int q4 = warp & 3, half = (warp - 2) >> 2;  // epilogue: TMEM lane quarter, half of the GM rows
+    const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
+    // Every MMA accumulates (digit pairs of different j share column blocks): start from zero.
     if (warp >= 2) {
-        const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
 #pragma unroll
-        for (int c = 0; c < S * BN; c += 16) tmem_st16_zero(tmem + lane_base + c);
+        for (int b = 0; b < NACC; b++)
+#pragma unroll
+            for (int s = 0; s < S; s++) tmem_st16_zero(tmem + lane_base + b * ACC + s * GM + 16 * half);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
     fence_before();
     __syncthreads();
     fence_after();
-
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     const uint32_t sbase = smem_u32(smem);
 
     if (warp == 0) {
-        if (lane == 0) {  // TMA producer
-            int issued = 0;
-            for (int kb = 0; kb < p.nkb; kb++) {
-                const int s = kb % nst;
-                const uint32_t ph = (uint32_t)(kb / nst) & 1u;
-                if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) { s_fail = 1; break; }
-                if (*(volatile int*)&s_fail) break;
-                mbar_expect_tx(full0 + 8 * s, STAGE);
-                tma_load_4d(sbase + s * STAGE, &tmA, kb * BK, m0, 0, 0, full0 + 8 * s);
-                tma_load_4d(sbase + s * STAGE + A_STAGE, &tmW, kb * BK, n0, 0, 0, full0 + 8 * s);
-                issued = kb + 1;
+        if (lane == 0) {  // TMA producer, running ahead across tiles
+            int g = 0, s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
+                const int m0 = (t % p.tiles_m) * GM, n0 = (t / p.tiles_m) * GN;
+                for (int kb = 0; kb < p.nkb; kb++, g++) {
+                    if (!mbar_wait(empty0 + 8 * s, ph ^ 1u) || *(volatile int*)&s_fail) {
+                        s_fail = 1;
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(full0 + 8 * s, STAGE);
+                    tma_load_4d(sbase + s * STAGE, &tmW, kb * GK, n0, 0, 0, full0 + 8 * s);
+                    tma_load_4d(sbase + s * STAGE + W_ST, &tmA, kb * GK, m0, 0, 0, full0 + 8 * s);
+                    if (++s == nst) { s = 0; ph ^= 1u; }
+                }
             }
-            if (*(volatile int*)&s_fail) {  // let copies still in flight land before the CTA exits
-                for (int kb = issued - nst < 0 ? 0 : issued - nst; kb < issued; kb++)
-                    mbar_wait(full0 + 8 * (kb % nst), (uint32_t)(kb / nst) & 1u);
-            }
+            if (!ok)  // let copies still in flight land before the CTA exits
+                for (int j = g - nst < 0 ? 0 : g - nst; j < g; j++) mbar_wait(full0 + 8 * (j % nst), (uint32_t)(j / nst) & 1u);
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
-            for (int kb = 0; kb < p.nkb; kb++) {
-                const int s = kb % nst;
-                const uint32_t ph = (uint32_t)(kb / nst) & 1u;
-                if (!mbar_wait(full0 + 8 * s, ph)) { s_fail = 1; break; }
+            int lt = 0, s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, lt++) {
+                const int b = lt & 1;
+                if (!mbar_spin(tfree0 + 8 * b, ((uint32_t)(lt >> 1) & 1u) ^ 1u)) { ok = false; break; }
                 fence_after();
-                const uint32_t a = sbase + s * STAGE, w = a + A_STAGE;
+                const uint32_t d = tmem + b * ACC;
+                for (int kb = 0; kb < p.nkb; kb++) {
+                    if (!mbar_spin(full0 + 8 * s, ph)) { ok = false; break; }
+                    fence_after();
+                    const uint32_t w = sbase + s * STAGE, a = w + W_ST;
 #pragma unroll
-                for (int kk = 0; kk < BK / 32; kk++) {
-                    const uint64_t bdesc = sw128_desc(w + kk * 32);
+                    for (int kk = 0; kk < GK / 32; kk++) {
+                        const uint64_t bdesc = kdesc(a + kk * 32);
 #pragma unroll
-                    for (int i = 0; i < LA; i++)
-                        umma_i8(tmem + i * BN, sw128_desc(a + i * (BM * BK) + kk * 32), bdesc, IDESC, 1u);
+                        for (int j = 0; j < LW; j++) umma_i8(d + j * GM, kdesc(w + j * (GN * GK) + kk * 32), bdesc, IDESC, 1u);
+                    }
+                    umma_commit(empty0 + 8 * s);
+                    if (++s == nst) { s = 0; ph ^= 1u; }
                 }
-                umma_commit(empty0 + 8 * s);
+                if (!ok) break;
+                umma_commit(tfull0 + 8 * b);
             }
-            umma_commit(done);
+            if (!ok) s_fail = 1;
         }
-    } else {  // epilogue: warps 2..5, TMEM lanes 32*(warp%4) ..
-        const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0));  // tcgen05.ld below is warp-collective
-        if (!ok) s_fail = 1;
-        fence_after();
-        const int lb = 32 * (warp & 3);
-        const int row = m0 + lb + lane;
-        const uint32_t taddr = tmem + ((uint32_t)lb << 16);
-        if (ok) {
+    } else {  // epilogue: thread = weight row n (TMEM lane), half of the tile's activation rows
+        int lt = 0;
+        for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, lt++) {
+            const int b = lt & 1;
+            const int m0 = (t % p.tiles_m) * GM, n0 = (t / p.tiles_m) * GN;
+            const int n = n0 + 32 * q4 + lane;
+            const bool n_ok = n < p.N;
+            // out = lo64(floor(sum * 2^rs / 2^shift)), sum = 2^32 H + L, e = shift - rs:
+            //   e <= 0: (H << 32-e) + (L << -e);  0 < e <= 32: (H << 32-e) + (L >> e);
+            //   e > 32: (H + (L >> 32)) >> (e - 32).
+            const int e = p.shift - ((p.row_shift && n_ok) ? p.row_shift[n] : 0);
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull0 + 8 * b, (uint32_t)(lt >> 1) & 1u));
+            if (!ok) { s_fail = 1; break; }
+            fence_after();
+            const uint32_t ta = tmem + lane_base + b * ACC + 16 * half;
 #pragma unroll 1
-            for (int c = 0; c < BN / 16; c++) {
-                uint32_t v[S][16];
+            for (int c = 0; c < 16; c += 8) {
+                uint32_t v[S][8];
 #pragma unroll
-                for (int s = 0; s < S; s++) tmem_ld16(taddr + s * BN + c * 16, v[s]);
+                for (int s = 0; s < S; s++) tmem_ld8(ta + s * GM + c, v[s]);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (row < p.M) {
-                    int64_t* crow = p.C + (int64_t)row * p.ldc;
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const int n = n0 + c * 16 + j;
-                        if (n >= p.N) break;
-                        i128 acc = (i128)(int32_t)v[S - 1][j];
+                for (int s = 0; s < S; s++) tmem_st8_zero(ta + s * GM + c);
 #pragma unroll
-                        for (int s = S - 2; s >= 0; s--) acc = (acc << 8) + (i128)(int32_t)v[s][j];
-                        if (p.row_shift) acc <<= p.row_shift[n];
-                        int64_t out = p.shift > 0 ? lo64(sar128(acc, p.shift)) : lo64(acc);
-                        if (p.R) out = wadd(out, p.R[(int64_t)row * p.ldr + n]);
-                        crow[n] = out;
+                for (int j = 0; j < 8; j++) {
+                    const int m = m0 + 16 * half + c + j;
+                    uint64_t L = 0, H = 0;
+#pragma unroll
+                    for (int s = 0; s < S && s < 4; s++) L += (uint64_t)(int64_t)(int32_t)v[s][j] << (8 * s);
+#pragma unroll
+                    for (int s = 4; s < S; s++) H += (uint64_t)(int64_t)(int32_t)v[s][j] << (8 * (s - 4));
+                    uint64_t out;
+                    if (e <= 0) {
+                        out = (-e >= 64 ? 0 : L << -e) + (32 - e >= 64 ? 0 : H << (32 - e));
+                    } else if (e <= 32) {
+                        out = (H << (32 - e)) + (uint64_t)((int64_t)L >> e);
+                    } else {
+                        const int64_t q = (int64_t)H + ((int64_t)L >> 32);
+                        out = (uint64_t)(e - 32 >= 64 ? (q >> 63) : q >> (e - 32));
+                    }
+                    if (n_ok && m < p.M) {
+                        int64_t o = (int64_t)out;
+                        if (p.R) o = wadd(o, p.R[(int64_t)m * p.ldr + n]);
+                        p.C[(int64_t)m * p.ldc + n] = o;
                     }
                 }
             }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tfree0 + 8 * b);
         }
     }
     fence_before();
@@ -319,25 +392,32 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int LW, int BNT>
-constexpr size_t stage_bytes() { return (size_t)BM * BK * LA + (size_t)BNT * BK * LW; }
+template <int LW>
+constexpr size_t stage_bytes() { return (size_t)LW * GN * GK + (size_t)LA * GM * GK; }
 
-template <int LW, int BNT>
-int stages() {
-    int n = (int)((227 * 1024 - 1024 - 256) / stage_bytes<LW, BNT>());
-    return n > 4 ? 4 : n;
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
 }
 
-template <int LW, int BNT>
-void launch_lw(const CUtensorMap& ta, const CUtensorMap& tw, Params p, dim3 grid, cudaStream_t st) {
-    p.nstages = stages<LW, BNT>();
-    const size_t smem = p.nstages * stage_bytes<LW, BNT>() + 1024 + (2 * p.nstages + 2) * 8;
+template <int LW>
+void launch_lw(const CUtensorMap& ta, const CUtensorMap& tw, Params p, cudaStream_t st) {
+    constexpr int nst = gemm_stages<LW>();
+    const size_t smem = nst * stage_bytes<LW>() + 1024 + (2 * nst + 2 * NACC + 1) * 8;
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(k_gemm_tc<LW, BNT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_gemm_tc<LW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         configured = true;
     }
-    k_gemm_tc<LW, BNT><<<grid, THREADS, smem, st>>>(ta, tw, p);
+    const int grid = p.tiles < sm_count() ? p.tiles : sm_count();
+    k_gemm_tc<LW><<<grid, THREADS, smem, st>>>(ta, tw, p);
 }
 
 Params base_params() {
@@ -347,16 +427,19 @@ Params base_params() {
 }
 }  // namespace
 
-bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows, int64_t batch) {
+bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows, int64_t batch, int box_k) {
     EncodeTiledFn fn = encode_fn();
-    if (!fn || kpad % BK || planes < 1 || planes > 255 || box_rows < 1 || box_rows > 256 || batch < 1) return false;
+    if (!fn || (box_k != 128 && box_k != 64) || kpad % box_k || planes < 1 || planes > 255 || box_rows < 1 ||
+        box_rows > 256 || batch < 1)
+        return false;
     if (((uintptr_t)base & 15) != 0) return false;
     cuuint64_t dims[4] = {(cuuint64_t)kpad, (cuuint64_t)rows, (cuuint64_t)planes, (cuuint64_t)batch};
     cuuint64_t strides[3] = {(cuuint64_t)kpad, (cuuint64_t)(kpad * rows), (cuuint64_t)(kpad * rows * planes)};
-    cuuint32_t box[4] = {(cuuint32_t)BK, (cuuint32_t)box_rows, (cuuint32_t)planes, 1};
+    cuuint32_t box[4] = {(cuuint32_t)box_k, (cuuint32_t)box_rows, (cuuint32_t)planes, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = fn((CUtensorMap*)map128, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, base, dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, box_k == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -407,17 +490,19 @@ void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t 
 void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K, int64_t mpad, int64_t npad, int64_t kpad,
             int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st,
             const int8_t* row_shift) {
+    (void)K;
     Params p = base_params();
-    p.M = M; p.N = N; p.K = K; p.nkb = (int)(kpad / BK); p.lw = lw; p.shift = shift; p.nstages = 2;
+    p.M = M; p.N = N; p.nkb = (int)(kpad / GK); p.shift = shift;
+    p.tiles_m = (int)(mpad / GM);
+    p.tiles = p.tiles_m * (int)((npad + GN - 1) / GN);
     p.C = c; p.ldc = ldc; p.R = r; p.ldr = ldr; p.skip = skip; p.err = err; p.row_shift = row_shift;
-    dim3 grid((unsigned)(npad / BN), (unsigned)(mpad / BM));
     const CUtensorMap& ta = *(const CUtensorMap*)tmap_a;
     const CUtensorMap& tw = *(const CUtensorMap*)tmap_w;
     switch (lw) {
-        case 1: launch_lw<1, BN>(ta, tw, p, grid, st); break;
-        case 2: launch_lw<2, BN>(ta, tw, p, grid, st); break;
-        case 3: launch_lw<3, BN>(ta, tw, p, grid, st); break;
-        default: launch_lw<4, BN>(ta, tw, p, grid, st); break;
+        case 1: launch_lw<1>(ta, tw, p, st); break;
+        case 2: launch_lw<2>(ta, tw, p, st); break;
+        case 3: launch_lw<3>(ta, tw, p, st); break;
+        default: launch_lw<4>(ta, tw, p, st); break;
     }
 }
 

@@ -31,10 +31,12 @@ struct GemmWorkspace {
 
 // Tensor-core kernel launchers (k_gemm_tc.cu).
 namespace tc {
-constexpr int BM = 128, BN = 64, BK = 128, LA = 5;
+constexpr int BM = 128, BN = 64, BK = 128, LA = 5;  // padding of the digit planes (rows, weight rows, K bytes)
+constexpr int GM = 32, GN = 128, GK = 128;        // projection tile: activation rows, weight rows, K bytes a stage
 // Encodes a TMA map over int8 digit planes [batch][planes][rows][kpad] with a
-// (128 B, box_rows, planes, 1) box.
-bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows, int64_t batch = 1);
+// (box_k B, box_rows, planes, 1) box, 128-byte swizzle for box_k 128, 64-byte for box_k 64.
+bool encode_planes(void* map128, void* base, int64_t kpad, int64_t rows, int planes, int box_rows, int64_t batch = 1,
+                   int box_k = 128);
 // Encodes a TMA map over `rows` rows of row_u16 16-bit elements (no swizzle), box (box_x, box_rows).
 bool encode_rows_u16(void* map128, const void* base, int64_t row_u16, int64_t rows, int box_x, int box_rows);
 // Per-row common trailing zeros of the Q30 composites -> tz[N].
