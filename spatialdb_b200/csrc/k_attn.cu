@@ -297,8 +297,7 @@ __global__ void k_split_v(const int64_t* __restrict__ V, int64_t ldv, int T, int
 }
 
 // FixedExp(x) for the softmax's x = score - max (IntegerTranscendentals.cs FixedExp): k = -ceil(-x / ln2),
-// r = x - k ln2 in [0, ln2), e^r by the truncating Taylor recurrence term = (term * r >> 30) / n, then
-// e^r >> -k. Every term past the tenth is zero for r < ln2, and (term * r) >> 30 = umulhi(term, 4r).
+// r = x - k ln2 in [0, ln2), e^r by the truncating Taylor recurrence (exp_taylor30), then e^r >> -k.
 // x > 0 (a wrapped difference) and x near long.MinValue (where the reference's own range reduction
 // wraps) set bad.
 SLX_DEV uint32_t exp_nonpos30(int64_t x, bool& bad) {
@@ -310,14 +309,7 @@ SLX_DEV uint32_t exp_nonpos30(int64_t x, bool& bad) {
     int64_t r = c * LN2 - nx;     // c = ceil(nx / ln2) <=> 0 <= r < ln2
     if (r < 0) { c++; r += LN2; }
     else if (r >= LN2) { c--; r -= LN2; }
-    const uint32_t r4 = (uint32_t)r << 2;
-    uint32_t term = 1u << 30, sum = 1u << 30;
-#pragma unroll
-    for (int n = 1; n <= 10; n++) {
-        term = __umulhi(term, r4) / (uint32_t)n;
-        sum += term;
-    }
-    return sum >> c;  // c <= 30
+    return exp_taylor30((uint32_t)r) >> c;  // c <= 30
 }
 
 // floor(e * 2^30 / sum) for e <= 2^30 and sum in [1, 2^41): an fp64 estimate (within one) corrected

@@ -333,6 +333,83 @@ __global__ __launch_bounds__(NT) void k_layernorm(int64_t* __restrict__ X, int64
     }
 }
 
+// NormalizeRow with one warp per row and the row held in registers (n <= 32 * PER): the two Int128
+// sums reduce by shuffles, every lane takes the same mean / variance / square root, no block barrier.
+// floor(v / n) for v < 2^128 and 1 <= n < 2^32 by long division over 32-bit limbs: each step
+// divides (r << 32 | limb) < n * 2^32 with inv = floor((2^64 - 1) / n), an estimate at most two
+// below the quotient.
+SLX_DEV u128 udiv128_u32(u128 v, uint32_t n, uint64_t inv) {
+    u128 q = 0;
+    uint64_t r = 0;
+#pragma unroll
+    for (int i = 3; i >= 0; i--) {
+        const uint64_t cur = (r << 32) | (uint64_t)(uint32_t)(v >> (32 * i));
+        uint64_t qi = __umul64hi(cur, inv);
+        r = cur - qi * n;
+        while (r >= n) { qi++; r -= n; }
+        q |= (u128)qi << (32 * i);
+    }
+    return q;
+}
+
+// (long)((Int128)s / n), truncating toward zero
+SLX_DEV int64_t div_i128_n(u128 s, uint32_t n, uint64_t inv) {
+    const bool neg = (i128)s < 0;
+    const u128 q = udiv128_u32(neg ? (u128)0 - s : s, n, inv);
+    return lo64(neg ? -(i128)q : (i128)q);
+}
+
+template <int PER>
+__global__ __launch_bounds__(256) void k_layernorm_warp(int64_t* __restrict__ X, int64_t ld, int rows, int n,
+                                                         const int64_t* __restrict__ w, const int64_t* __restrict__ b) {
+    __shared__ int64_t sw[32 * PER], sb[32 * PER];  // the row's weight and bias, staged once per block
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        sw[j] = w[j];
+        sb[j] = b[j];
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const uint64_t inv = ~0ULL / (uint64_t)n;
+    for (int row = blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += gridDim.x * 8) {
+        int64_t* x = X + (int64_t)row * ld;
+        int64_t v[PER];
+        u128 s = 0;
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const int j = lane + 32 * i;
+            v[i] = j < n ? __ldcs(x + j) : 0;
+            s += (u128)(i128)v[i];
+        }
+        s = warp_sum_u128(s);
+        const int64_t mean = div_i128_n(s, (uint32_t)n, inv);
+        u128 ss = 0;
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            if (lane + 32 * i < n) {
+                v[i] = wsub(v[i], mean);
+                ss += (u128)((i128)v[i] * v[i]);
+            }
+        }
+        ss = warp_sum_u128(ss);
+        // Int128 variance = sumSq / n (a wrapped, negative sumSq gives var <= 0 as in the reference)
+        const i128 var = (i128)ss < 0 ? (i128)0 : (i128)udiv128_u32(ss, (uint32_t)n, inv);
+        if (var <= 0) {
+#pragma unroll
+            for (int i = 0; i < PER; i++)
+                if (lane + 32 * i < n) x[lane + 32 * i] = sb[lane + 32 * i];
+            continue;
+        }
+        int64_t isq = isqrt_u128((u128)var);
+        if (isq == 0) isq = 1;
+        const double rd = 1.0 / (double)isq;
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const int j = lane + 32 * i;
+            if (j < n) __stcs(x + j, wadd(div_trunc((i128)v[i] * sw[j], isq, rd), sb[j]));
+        }
+    }
+}
+
 // RmsNormRow (IntegerLayerNorm.cs:71-93); row r = segment (r % per) of line (r / per).
 __global__ __launch_bounds__(NT) void k_rmsnorm(int64_t* __restrict__ X, int64_t ld, int per, int n,
                                                 const int64_t* __restrict__ w) {
@@ -360,7 +437,12 @@ __global__ __launch_bounds__(NT) void k_rmsnorm(int64_t* __restrict__ X, int64_t
 
 int layernorm_rows(int64_t* x, int64_t ld, int rows, int n, const int64_t* w, const int64_t* b, cudaStream_t st) {
     if (rows <= 0) return 0;
-    k_layernorm<<<rows, NT, 0, st>>>(x, ld, n, w, b);
+    const unsigned wb = (unsigned)std::min((rows + 7) / 8, 148 * 4);
+    if (n <= 256) k_layernorm_warp<8><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b);
+    else if (n <= 512) k_layernorm_warp<16><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b);
+    else if (n <= 768) k_layernorm_warp<24><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b);
+    else if (n <= 1024) k_layernorm_warp<32><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b);
+    else k_layernorm<<<rows, NT, 0, st>>>(x, ld, n, w, b);
     return 1;
 }
 

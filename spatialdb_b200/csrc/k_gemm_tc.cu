@@ -32,7 +32,7 @@
 namespace slx {
 namespace tc {
 
-constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, each half of the tile's activation rows
+constexpr int EPI_WARPS = 16;  // four per TMEM lane quarter, each eight of the tile's activation rows
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
 constexpr int NACC = 2;       // TMEM accumulators (tile parity picks one)
 
@@ -122,14 +122,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int q4 = warp & 3, half = (warp - 2) >> 2;  // epilogue: TMEM lane quarter, half of the GM rows
+    const int q4 = warp & 3, sub = (warp - 2) >> 2;  // epilogue: TMEM lane quarter, eight of the GM rows
     const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
     // Every MMA accumulates (digit pairs of different j share column blocks): start from zero.
     if (warp >= 2) {
 #pragma unroll
         for (int b = 0; b < NACC; b++)
 #pragma unroll
-            for (int s = 0; s < S; s++) tmem_st16_zero(tmem + lane_base + b * ACC + s * GM + 16 * half);
+            for (int s = 0; s < S; s++) tmem_st8_zero(tmem + lane_base + b * ACC + s * GM + 8 * sub);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
     fence_before();
@@ -187,7 +187,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             }
             if (!ok) s_fail = 1;
         }
-    } else {  // epilogue: thread = weight row n (TMEM lane), half of the tile's activation rows
+    } else {  // epilogue: thread = weight row n (TMEM lane), eight of the tile's activation rows
         int lt = 0;
         for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, lt++) {
             const int b = lt & 1;
@@ -201,34 +201,40 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull0 + 8 * b, (uint32_t)(lt >> 1) & 1u));
             if (!ok) { s_fail = 1; break; }
             fence_after();
-            const uint32_t ta = tmem + lane_base + b * ACC + 16 * half;
-#pragma unroll 1
-            for (int c = 0; c < 16; c += 8) {
+            const uint32_t ta = tmem + lane_base + b * ACC + 8 * sub;
+            {
+                constexpr int c = 0;
                 uint32_t v[S][8];
 #pragma unroll
                 for (int s = 0; s < S; s++) tmem_ld8(ta + s * GM + c, v[s]);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
                 for (int s = 0; s < S; s++) tmem_st8_zero(ta + s * GM + c);
+                int64_t out[8];
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
-                    const int m = m0 + 16 * half + c + j;
                     uint64_t L = 0, H = 0;
 #pragma unroll
                     for (int s = 0; s < S && s < 4; s++) L += (uint64_t)(int64_t)(int32_t)v[s][j] << (8 * s);
 #pragma unroll
                     for (int s = 4; s < S; s++) H += (uint64_t)(int64_t)(int32_t)v[s][j] << (8 * (s - 4));
-                    uint64_t out;
+                    uint64_t o;
                     if (e <= 0) {
-                        out = (-e >= 64 ? 0 : L << -e) + (32 - e >= 64 ? 0 : H << (32 - e));
+                        o = (-e >= 64 ? 0 : L << -e) + (32 - e >= 64 ? 0 : H << (32 - e));
                     } else if (e <= 32) {
-                        out = (H << (32 - e)) + (uint64_t)((int64_t)L >> e);
+                        o = (H << (32 - e)) + (uint64_t)((int64_t)L >> e);
                     } else {
                         const int64_t q = (int64_t)H + ((int64_t)L >> 32);
-                        out = (uint64_t)(e - 32 >= 64 ? (q >> 63) : q >> (e - 32));
+                        o = (uint64_t)(e - 32 >= 64 ? (q >> 63) : q >> (e - 32));
                     }
+                    out[j] = (int64_t)o;
+                }
+                const int mb = m0 + 8 * sub + c;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int m = mb + j;
                     if (n_ok && m < p.M) {
-                        int64_t o = (int64_t)out;
+                        int64_t o = out[j];
                         if (p.R) o = wadd(o, p.R[(int64_t)m * p.ldr + n]);
                         p.C[(int64_t)m * p.ldc + n] = o;
                     }
@@ -278,6 +284,40 @@ __global__ void k_split_a(const int64_t* __restrict__ A, int64_t lda, int M, int
 #pragma unroll
     for (int i = 0; i < LA; i++)
         *(uint4*)(planes + ((int64_t)i * Mpad + row) * Kpad + k0) = make_uint4(pk[i][0], pk[i][1], pk[i][2], pk[i][3]);
+}
+
+// Same digits, four consecutive elements a thread: two 16-byte loads, one 32-bit store per plane
+// (rows of A 16-byte aligned, K a multiple of 4).
+__global__ void k_split_a4(const int64_t* __restrict__ A, int64_t lda, int M, int K, int Mpad, int Kpad,
+                           int8_t* __restrict__ planes, int* overflow) {
+    const int quads = Kpad / 4;
+    const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)Mpad * quads) return;
+    const int row = (int)(idx / quads), k0 = (int)(idx % quads) * 4;
+    int64_t x[4] = {0, 0, 0, 0};
+    if (row < M && k0 < K) {
+        const longlong2 lo = *(const longlong2*)(A + (int64_t)row * lda + k0);
+        const longlong2 hi = *(const longlong2*)(A + (int64_t)row * lda + k0 + 2);
+        x[0] = lo.x; x[1] = lo.y; x[2] = hi.x; x[3] = hi.y;
+    }
+    uint32_t pk[LA];
+#pragma unroll
+    for (int i = 0; i < LA; i++) pk[i] = 0;
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        int64_t v = x[j];
+#pragma unroll
+        for (int i = 0; i < LA; i++) {
+            const int d = (int)(((uint64_t)v + 128u) & 255u) - 128;
+            v = (v - d) >> 8;
+            pk[i] |= (uint32_t)(uint8_t)(int8_t)d << (8 * j);
+        }
+        bad |= v != 0;
+    }
+    if (bad) atomicOr(overflow, 1);
+#pragma unroll
+    for (int i = 0; i < LA; i++) *(uint32_t*)(planes + ((int64_t)i * Mpad + row) * Kpad + k0) = pk[i];
 }
 
 // Balanced digits of per-head rows: X row (b*T + t), head h, hd values at X + (b*T+t)*ld + h*hd
@@ -483,6 +523,11 @@ void split_w(const WDesc& w, int lw, int64_t npad, int64_t kpad, int8_t* planes,
 
 void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t kpad, int8_t* planes, int* overflow,
              cudaStream_t st) {
+    if (K % 4 == 0 && lda % 2 == 0 && ((uintptr_t)a & 15) == 0) {
+        const int64_t quads = mpad * (kpad / 4);
+        k_split_a4<<<(unsigned)((quads + 255) / 256), 256, 0, st>>>(a, lda, M, K, (int)mpad, (int)kpad, planes, overflow);
+        return;
+    }
     const int64_t chunks = mpad * (kpad / 16);
     k_split_a<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(a, lda, M, K, (int)mpad, (int)kpad, planes, overflow);
 }

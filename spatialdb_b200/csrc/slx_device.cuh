@@ -137,27 +137,26 @@ SLX_DEV int64_t fixed_exp30(int64_t x) {
 // Truncating num / d for d >= 1 with rd = 1.0 / d: a double estimate corrected to the exact
 // quotient by its integer remainder. Used when |num| < 2^62 and the quotient is below 2^50, where
 // the estimate is within one of the quotient; any other case divides in Int128.
+// (long)(num / d), truncating toward zero, for d >= 1 and rd ~ 1/d: a double estimate of the
+// quotient (off by at most one while |num / d| < 2^50) corrected by the remainder, which is small
+// and so exact in wrapping 64-bit arithmetic; wider quotients take the Int128 division.
 SLX_DEV int64_t div_trunc(i128 num, int64_t d, double rd) {
-    const i128 lim = (i128)1 << 62;
-    if (num > -lim && num < lim) {
-        const int64_t n = (int64_t)num;
-        const uint64_t an = n < 0 ? (uint64_t)(-n) : (uint64_t)n;
-        if ((an >> 50) < (uint64_t)d) {
-            const double qd = (double)an * rd;
-            if (qd < 1125899906842624.0) {  // 2^50
-                int64_t q = (int64_t)qd;
-                int64_t r = (int64_t)an - q * d;
-                while (r < 0) { q--; r += d; }
-                while (r >= d) { q++; r -= d; }
-                return n < 0 ? -q : q;
-            }
+    const double nd = (double)(int64_t)(num >> 64) * 18446744073709551616.0 + (double)(uint64_t)num;
+    const double qd = nd * rd;
+    if (qd > -1125899906842624.0 && qd < 1125899906842624.0) {  // |q| < 2^50
+        int64_t q = (int64_t)qd;
+        int64_t r = (int64_t)((uint64_t)num - (uint64_t)q * (uint64_t)d);
+        if (num >= 0) {
+            while (r < 0) { q--; r += d; }
+            while (r >= d) { q++; r -= d; }
+        } else {
+            while (r > 0) { q++; r -= d; }
+            while (r <= -d) { q--; r += d; }
         }
+        return q;
     }
     return lo64(num / (i128)d);
 }
-
-// C# long / long for a positive divisor d with rd = 1.0 / d: exact (double estimate corrected by
-// the integer remainder) when |x| < 2^52, cs_div64 otherwise.
 SLX_DEV int64_t div_small(int64_t x, int64_t d, double rd) {
     const uint64_t ax = x < 0 ? (uint64_t)0 - (uint64_t)x : (uint64_t)x;
     if (ax < (1ULL << 52)) {
@@ -171,20 +170,56 @@ SLX_DEV int64_t div_small(int64_t x, int64_t d, double rd) {
 }
 
 // FixedSigmoid / FixedSiLU (IntegerTranscendentals.cs:49-69), fracBits = 30.
+// e^r * 2^30 for r in [0, ln2), by FixedExp's truncating Taylor recurrence term = (term * r >> 30) / n
+// (IntegerTranscendentals.cs:13-47): every term past the tenth is zero on this range,
+// (term * r) >> 30 = umulhi(term, 4r), and each floor(x / n) equals umulhi(x, ceil(2^32 / n)) for the
+// x that step can see (n = 2, 4, 8 are shifts) -- the sum agrees with the recurrence for every r in
+// [0, ln2).
+SLX_DEV uint32_t exp_taylor30(uint32_t r) {
+    const uint32_t r4 = r << 2;
+    uint32_t t = r, sum = (1u << 30) + r;  // n = 1
+    t = __umulhi(t, r4) >> 1; sum += t;
+    t = __umulhi(__umulhi(t, r4), 1431655766u); sum += t;
+    t = __umulhi(t, r4) >> 2; sum += t;
+    t = __umulhi(__umulhi(t, r4), 858993460u); sum += t;
+    t = __umulhi(__umulhi(t, r4), 715827883u); sum += t;
+    t = __umulhi(__umulhi(t, r4), 613566757u); sum += t;
+    t = __umulhi(t, r4) >> 3; sum += t;
+    t = __umulhi(__umulhi(t, r4), 477218589u); sum += t;
+    t = __umulhi(__umulhi(t, r4), 429496730u); sum += t;
+    return sum;
+}
+
+// FixedExp for |y| <= 2^35 (FixedSigmoid's arguments lie within 20 * 2^30): the reference's range
+// reduction is k = floor(y / ln2) (truncation for y >= 0, -ceil(-y / ln2) below), r = y - k ln2 in
+// [0, ln2), so its 32-bit Taylor branch always runs (exp_taylor30). k is estimated in double
+// (|y| < 2^35 is exact) and corrected by the remainder. Same result as fixed_exp30 on this range.
+SLX_DEV int64_t fixed_exp30_bounded(int64_t y) {
+    constexpr int64_t LN2 = 744261117;
+    int64_t k = (int64_t)floor((double)y * (1.0 / (double)LN2));
+    int64_t r = y - k * LN2;
+    if (r < 0) { k--; r += LN2; }
+    else if (r >= LN2) { k++; r -= LN2; }
+    const uint32_t sum = exp_taylor30((uint32_t)r);
+    if (k >= 0) {
+        if (k >= 63 || (int64_t)sum > (INT64_MAX >> k)) return INT64_MAX;
+        return (int64_t)((uint64_t)sum << k);
+    }
+    return -k >= 31 ? 0 : (int64_t)(sum >> -k);  // sum < 2^31
+}
+
 SLX_DEV int64_t fixed_sigmoid30(int64_t x) {
     const int64_t one = 1LL << 30, thr = 20LL << 30;
     if (x > thr) return one;
     if (x < -thr) return 0;
-    int64_t den = wadd(one, fixed_exp30(wsub(0, x)));
-    if (den == 0) return one;
-    if (den > 0) {  // 2^60 / den, den in [2^30, 2^59): estimate within one, then exact correction
-        int64_t q = (int64_t)(1152921504606846976.0 * __drcp_rn((double)den));
-        int64_t r = (int64_t)((1ULL << 60) - (uint64_t)q * (uint64_t)den);
-        while (r < 0) { q--; r += den; }
-        while (r >= den) { q++; r -= den; }
-        return q;
-    }
-    return lo64((i128)(1LL << 60) / (i128)den);
+    // |x| <= 20 * 2^30: e^-x in [2^30 e^-20, 2^30 e^20], den in [2^30, 2^59]
+    const int64_t den = one + fixed_exp30_bounded(-x);
+    // 2^60 / den: estimate within one, then exact correction
+    int64_t q = (int64_t)(1152921504606846976.0 * __drcp_rn((double)den));
+    int64_t r = (int64_t)((1ULL << 60) - (uint64_t)q * (uint64_t)den);
+    while (r < 0) { q--; r += den; }
+    while (r >= den) { q++; r -= den; }
+    return q;
 }
 SLX_DEV int64_t fixed_silu30(int64_t x) { return lo64(sar128((i128)x * fixed_sigmoid30(x), 30)); }
 
