@@ -256,46 +256,8 @@ void launch_scores_kb(const CUtensorMap& tq, const CUtensorMap& tk, ScoreParams 
 }
 
 // ---------------------------------------------------------------------------------------------
-// softmax + P.V
+// softmax, then P.V
 // ---------------------------------------------------------------------------------------------
-constexpr int PR = 32;  // query rows per block
-
-template <int HD>
-struct Pv {
-    static constexpr int CPT = 4;                      // columns per thread: 2c, 2c+1, HD/2+2c, HD/2+2c+1
-    static constexpr int RPT = HD >= 64 ? 4 : HD / 16; // rows per thread
-    static constexpr int CG = HD / CPT, RG = PR / RPT;
-    static constexpr int THREADS = CG * RG;            // 128 (hd <= 64), 256 (128), 512 (256)
-    static constexpr int VT = HD >= 256 ? 8 : 16;      // keys per chunk
-    static constexpr int PUS = VT + 4;                 // p row strides (4-word bank offset per row)
-    static constexpr int PDS = VT + 2;
-    static constexpr int MINB = THREADS <= 128 ? 4 : 1;
-    // one staging buffer: v >> 30 (fp64), 4 (v mod 2^30) (uint32), p (uint32)
-    static constexpr int VH_BYTES = VT * HD * 8, VL_BYTES = VT * HD * 4, PU_BYTES = PR * PUS * 4;
-    static constexpr int BUF = VH_BYTES + VL_BYTES + PU_BYTES;
-    static constexpr size_t SMEM = 2 * (size_t)BUF + (size_t)PR * PDS * 8;
-};
-
-// V -> v >> 30 as fp64 and 4 * (v mod 2^30) as uint32, per (sequence, kv head) [T][HD]; the uint32
-// plane stores each P.V thread's four columns (2g, 2g+1, HD/2+2g, HD/2+2g+1) adjacent. |v >> 30|
-// >= 2^22 sets the flag (the fp64 sums would no longer be exact).
-template <int HD>
-__global__ void k_split_v(const int64_t* __restrict__ V, int64_t ldv, int T, int nkv, double* __restrict__ Vh,
-                          uint32_t* __restrict__ Vl, const int* __restrict__ skip, int* flag) {
-    if (*skip) return;
-    const int zk = blockIdx.y, b = zk / nkv, kvh = zk % nkv;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= T * HD) return;
-    const int s = i / HD, d = i % HD;
-    const int64_t v = V[((int64_t)b * T + s) * ldv + (int64_t)kvh * HD + d];
-    const int64_t hi = v >> 30;
-    if (hi < -(1LL << 22) || hi >= (1LL << 22)) atomicOr(flag, 1);
-    const int64_t base = (int64_t)zk * T * HD;
-    Vh[base + i] = (double)hi;
-    const int g = d < HD / 2 ? d >> 1 : (d - HD / 2) >> 1, j = d < HD / 2 ? (d & 1) : 2 + (d & 1);
-    Vl[base + (int64_t)s * HD + 4 * g + j] = (uint32_t)(v & ((1LL << 30) - 1)) << 2;
-}
-
 // FixedExp(x) for the softmax's x = score - max (IntegerTranscendentals.cs FixedExp): k = -ceil(-x / ln2),
 // r = x - k ln2 in [0, ln2), e^r by the truncating Taylor recurrence (exp_taylor30), then e^r >> -k.
 // x > 0 (a wrapped difference) and x near long.MinValue (where the reference's own range reduction
@@ -328,77 +290,134 @@ SLX_DEV void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
 SLX_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 SLX_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// One block: PR query rows of one head.
-//  1. softmax, warp per row, in place over the row's score storage (row stride SR int64): pass one
-//     writes e = FixedExp(score - max) as uint32 over the first half (each 128-key chunk is read
-//     completely before its e values are written), pass two rewrites them as p = (e << 30) / sum
-//     and zeroes p up to the next multiple of four keys;
-//  2. P.V over chunks of VT keys: p, v >> 30 and 4 (v mod 2^30) arrive by cp.async into one of two
-//     buffers while the other chunk computes; p is widened to fp64 once per chunk. Thread (rg, cg)
-//     owns rows rg*RPT .. and columns 2cg, 2cg+1, HD/2+2cg, HD/2+2cg+1.
-template <int HD>
-__global__ __launch_bounds__(Pv<HD>::THREADS, Pv<HD>::MINB) void k_softmax_pv(
-    int64_t* S, int SR, const int64_t* __restrict__ rmax, const double* __restrict__ Vh, const uint32_t* __restrict__ Vl,
-    int64_t* __restrict__ O, int64_t ldo, int T, int nh, int nkv, const int* __restrict__ skip, int* flag) {
-    using C = Pv<HD>;
-    constexpr int TH = C::THREADS, VT = C::VT, RPT = C::RPT, CG = C::CG, PUS = C::PUS, PDS = C::PDS;
-    constexpr int SU = 4;  // keys per lane per softmax chunk (loads batched, exps interleaved)
+// FixedSoftmax of score rows in place, one warp per row (row stride SR int64): pass one writes
+// e = FixedExp(score - max) as uint32 over the first half of the row's storage (each 256-key chunk is
+// read completely before its e values are written), pass two rewrites them as p = (e << 30) / sum
+// and zeroes p up to the next multiple of four keys. A row outside the fast ranges sets the flag.
+constexpr int SM_ROWS = 8;  // rows (warps) per block
+__global__ __launch_bounds__(32 * SM_ROWS) void k_softmax(int64_t* S, int SR, const int64_t* __restrict__ rmax, int T,
+                                                          int rows, const int* __restrict__ skip, int* flag) {
+    constexpr int SU = 8;  // keys per lane per chunk: loads batched, exps interleaved
     if (*skip) return;
-    extern __shared__ __align__(16) uint8_t sm[];
-    double* Pd = (double*)(sm + 2 * C::BUF);  // [PR][PDS]
-    __shared__ int s_bad;
-    const int h = blockIdx.y, b = blockIdx.z, t0 = blockIdx.x * PR;
-    const int z = b * nh + h, zk = b * nkv + h / (nh / nkv);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * SM_ROWS + (threadIdx.x >> 5);  // over z * T + t
+    if (row >= rows) return;
     const int T4 = (T + 3) & ~3;
-    if (threadIdx.x == 0) s_bad = 0;
-    __syncthreads();
-
-    // ---- 1. softmax rows
-    for (int r = warp; r < PR; r += TH / 32) {
-        const int t = t0 + r;
-        if (t >= T) continue;
-        const int64_t* srow = S + ((int64_t)z * T + t) * SR;
-        uint32_t* prow = (uint32_t*)(S + ((int64_t)z * T + t) * SR);
-        const int64_t mx = rmax[(int64_t)z * T + t];
-        uint64_t sum = 0;
-        bool bad = false;
-        for (int s0 = 0; s0 < T; s0 += 32 * SU) {
-            int64_t x[SU];
+    const int64_t* srow = S + row * SR;
+    uint32_t* prow = (uint32_t*)(S + row * SR);
+    const int64_t mx = rmax[row];
+    uint64_t sum = 0;
+    bool bad = false;
+    for (int s0 = 0; s0 < T; s0 += 32 * SU) {
+        int64_t x[SU];
 #pragma unroll
-            for (int u = 0; u < SU; u++) {
-                const int sk = s0 + 32 * u + lane;
-                x[u] = sk < T ? srow[sk] : mx;
-            }
-            __syncwarp();  // this chunk is read before its e values overwrite the first half of it
+        for (int u = 0; u < SU; u++) {
+            const int sk = s0 + 32 * u + lane;
+            x[u] = sk < T ? srow[sk] : mx;
+        }
+        __syncwarp();  // this chunk is read before its e values overwrite the first half of it
 #pragma unroll
-            for (int u = 0; u < SU; u++) {
-                const int sk = s0 + 32 * u + lane;
-                const uint32_t e = exp_nonpos30(wsub(x[u], mx), bad);
-                if (sk < T) { prow[sk] = e; sum += e; }
-            }
+        for (int u = 0; u < SU; u++) {
+            const int sk = s0 + 32 * u + lane;
+            const uint32_t e = exp_nonpos30(wsub(x[u], mx), bad);
+            if (sk < T) { prow[sk] = e; sum += e; }
         }
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, (unsigned long long)sum, o);
-        if (__any_sync(0xffffffffu, bad)) {
-            if (lane == 0) s_bad = 1;
-            continue;
-        }
-        __syncwarp();
-        if (sum == 0) {  // uniform = one / len
-            for (int s = lane; s < T; s += 32) prow[s] = (uint32_t)((1LL << 30) / T);
-        } else {
-            const double inv30 = 1073741824.0 / (double)sum;
-            for (int s = lane; s < T; s += 32) prow[s] = p_div(prow[s], sum, inv30);
-        }
-        if (lane < T4 - T) prow[T + lane] = 0;
     }
-    __syncthreads();
-    if (s_bad) {
-        if (threadIdx.x == 0) atomicOr(flag, 1);
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, (unsigned long long)sum, o);
+    if (__any_sync(0xffffffffu, bad)) {
+        if (lane == 0) atomicOr(flag, 1);
         return;
     }
+    __syncwarp();
+    if (sum == 0) {  // uniform = one / len
+        for (int s = lane; s < T; s += 32) prow[s] = (uint32_t)((1LL << 30) / T);
+    } else {
+        const double inv30 = 1073741824.0 / (double)sum;
+#pragma unroll 4
+        for (int s = lane; s < T; s += 32) prow[s] = p_div(prow[s], sum, inv30);
+    }
+    if (lane < T4 - T) prow[T + lane] = 0;
+}
 
-    // ---- 2. P.V
+// V -> v >> 30 as fp64 ([T][HD]), 4 * (v mod 2^30) as uint32 ([T][HD], each P.V thread's four columns
+// 2g, 2g+1, HD/2+2g, HD/2+2g+1 adjacent) and, for the tensor-core P.V, the two balanced base-256 digits
+// of v >> 30 as key-major int8 planes [2][HD][Tpad] (keys past T zero), per (sequence, kv head).
+// |v >> 30| >= 2^22 sets the flag (the fp64 sums would not be exact); v >> 30 outside two digits sets
+// pvsel (the fp64 P.V runs instead of the tensor-core one).
+constexpr int SV_KEYS = 64;  // keys per k_split_v block
+
+template <int HD>
+__global__ __launch_bounds__(256) void k_split_v(const int64_t* __restrict__ V, int64_t ldv, int T, int Tpad, int nkv,
+                                                 double* __restrict__ Vh, uint32_t* __restrict__ Vl,
+                                                 int8_t* __restrict__ Vd, const int* __restrict__ skip, int* flag,
+                                                 int* pvsel) {
+    __shared__ int16_t s_hi[HD][SV_KEYS + 2];  // v >> 30 of the tile's keys (two-digit values; others flagged)
+    if (*skip) return;
+    const int zk = blockIdx.y, b = zk / nkv, kvh = zk % nkv, k0 = blockIdx.x * SV_KEYS;
+    const int64_t base = (int64_t)zk * T * HD;
+    bool bad = false, wide = false;
+    for (int i = threadIdx.x; i < SV_KEYS * HD; i += 256) {  // key-major: coalesced along the head's columns
+        const int sl = i / HD, d = i % HD, s = k0 + sl;
+        int64_t hi = 0;
+        if (s < T) {
+            const int64_t v = V[((int64_t)b * T + s) * ldv + (int64_t)kvh * HD + d];
+            hi = v >> 30;
+            bad |= hi < -(1LL << 22) || hi >= (1LL << 22);
+            wide |= hi < -32640 || hi > 32639;
+            Vh[base + (int64_t)s * HD + d] = (double)hi;
+            const int g = d < HD / 2 ? d >> 1 : (d - HD / 2) >> 1, j = d < HD / 2 ? (d & 1) : 2 + (d & 1);
+            Vl[base + (int64_t)s * HD + 4 * g + j] = (uint32_t)(v & ((1LL << 30) - 1)) << 2;
+        }
+        s_hi[d][sl] = (int16_t)(hi < -32640 || hi > 32639 ? 0 : hi);
+    }
+    if (bad) atomicOr(flag, 1);
+    if (wide) atomicOr(pvsel, 1);
+    __syncthreads();
+    int8_t* vd = Vd + (int64_t)zk * 2 * HD * Tpad + k0;
+    for (int i = threadIdx.x; i < HD * SV_KEYS; i += 256) {  // column-major: each plane row's keys contiguous
+        const int d = i / SV_KEYS, sl = i % SV_KEYS;
+        const int hi = s_hi[d][sl];
+        const int d0 = ((hi + 128) & 255) - 128, d1 = (hi - d0) >> 8;
+        vd[(int64_t)d * Tpad + sl] = (int8_t)d0;
+        vd[((int64_t)HD + d) * Tpad + sl] = (int8_t)d1;
+    }
+}
+
+// ---- P.V on CUDA cores with fp64 high parts (any head size; the tensor-core kernel's fallback)
+constexpr int PR = 32;  // query rows per block
+
+template <int HD>
+struct Pv {
+    static constexpr int CPT = 4;                      // columns per thread: 2c, 2c+1, HD/2+2c, HD/2+2c+1
+    static constexpr int RPT = HD >= 64 ? 4 : HD / 16; // rows per thread
+    static constexpr int CG = HD / CPT, RG = PR / RPT;
+    static constexpr int THREADS = CG * RG;            // 128 (hd <= 64), 256 (128), 512 (256)
+    static constexpr int VT = HD >= 256 ? 8 : 16;      // keys per chunk
+    static constexpr int PUS = VT + 4;                 // p row strides (4-word bank offset per row)
+    static constexpr int PDS = VT + 2;
+    static constexpr int MINB = THREADS <= 128 ? 4 : 1;
+    // one staging buffer: v >> 30 (fp64), 4 (v mod 2^30) (uint32), p (uint32)
+    static constexpr int VH_BYTES = VT * HD * 8, VL_BYTES = VT * HD * 4, PU_BYTES = PR * PUS * 4;
+    static constexpr int BUF = VH_BYTES + VL_BYTES + PU_BYTES;
+    static constexpr size_t SMEM = 2 * (size_t)BUF + (size_t)PR * PDS * 8;
+};
+
+// PR query rows of one head over chunks of VT keys: p, v >> 30 and 4 (v mod 2^30) arrive by cp.async
+// into one of two buffers while the other chunk computes; p is widened to fp64 once per chunk.
+// Thread (rg, cg) owns rows rg*RPT .. and columns 2cg, 2cg+1, HD/2+2cg, HD/2+2cg+1. With run_if,
+// runs only when *run_if is set.
+template <int HD>
+__global__ __launch_bounds__(Pv<HD>::THREADS, Pv<HD>::MINB) void k_pv_fp64(
+    const int64_t* S, int SR, const double* __restrict__ Vh, const uint32_t* __restrict__ Vl, int64_t* __restrict__ O,
+    int64_t ldo, int T, int nh, int nkv, const int* __restrict__ skip, const int* __restrict__ run_if) {
+    using C = Pv<HD>;
+    constexpr int TH = C::THREADS, VT = C::VT, RPT = C::RPT, CG = C::CG, PUS = C::PUS, PDS = C::PDS;
+    if (*skip || (run_if && !*run_if)) return;
+    extern __shared__ __align__(16) uint8_t sm[];
+    double* Pd = (double*)(sm + 2 * C::BUF);  // [PR][PDS]
+    const int h = blockIdx.y, b = blockIdx.z, t0 = blockIdx.x * PR;
+    const int z = b * nh + h, zk = b * nkv + h / (nh / nkv);
+    const int T4 = (T + 3) & ~3;
     const int cg = threadIdx.x % CG, rg = threadIdx.x / CG;
     const int c0 = 2 * cg, c1 = HD / 2 + 2 * cg;
     const double* vh0 = Vh + (int64_t)zk * T * HD;
@@ -484,26 +503,277 @@ __global__ __launch_bounds__(Pv<HD>::THREADS, Pv<HD>::MINB) void k_softmax_pv(
     }
 }
 
+// ---- P.V with the linear part on the tensor cores (head sizes 16, 32, 64)
+//   sum_s floor(p v / 2^30) = sum_s p v_hi + sum_s floor(p v_lo / 2^30).
+// sum_s p v_hi is a GEMM: p (<= 2^30) as four balanced base-256 digits is the A operand (128 query
+// rows, built by the CUDA cores into a 64-byte-swizzled tile per 64-key chunk), v_hi as two digits
+// stacked along N (2 x HD rows, key-major planes from k_split_v) the B operand; digit pair (i, j)
+// accumulates in TMEM column block i+j (5 blocks of HD int32 columns, each below 2^31 for T < 2^16).
+// The CUDA cores add floor(p v_lo / 2^30) = umulhi(p, 4 v_lo) per term, as in k_pv_fp64.
+constexpr int PM = 128;  // query rows per block (MMA M)
+constexpr int PVT = 64;  // keys per chunk: two 32-key MMA K steps
+
+template <int HD>
+struct PvTc {
+    static constexpr int TH = 512;                       // compute threads; one more warp issues the MMAs
+    static constexpr int CG = HD / 4, RG = TH / CG, RPT = PM / RG;  // thread (rg, cg): rows rg + RG*r
+    static constexpr int NB = 2 * HD;                    // B rows: v digit j, column c at j*HD + c
+    static constexpr int NS = 5;                         // column blocks
+    static constexpr int COLS = NS * HD;
+    static constexpr int ALLOC = COLS <= 64 ? 64 : COLS <= 128 ? 128 : COLS <= 256 ? 256 : 512;
+    static constexpr int PUS = PVT + 4;                  // p row stride (uint32), rows 4 banks apart
+    static constexpr int PD_B = 4 * PM * 64;             // p digits [4][PM][64 B], 64-byte swizzle
+    static constexpr int VD_B = NB * 64;                 // v digits [NB][64 B], 64-byte swizzle
+    static constexpr int PU_B = PM * PUS * 4, VL_B = PVT * HD * 4;
+    static constexpr int BUF = (PD_B + VD_B + PU_B + VL_B + 1023) / 1024 * 1024;
+    static constexpr int FSL = HD + 1;                   // floor-sum tile row stride (uint32)
+    static constexpr int EQ = HD / 8 < 4 ? HD / 8 : 4;   // epilogue warps per TMEM lane quarter (8 columns each step)
+    static constexpr size_t SMEM = 2 * (size_t)BUF + 1024 + 64;
+    static_assert(PM * FSL * 4 <= PU_B, "floor sums reuse a p buffer");
+};
+
+SLX_DEV uint32_t sw64_off(int row, int g) { return (uint32_t)(row * 64 + ((g ^ ((row >> 1) & 3)) << 4)); }
+
+template <int HD>
+__global__ void __launch_bounds__(PvTc<HD>::TH + 32, 1)
+k_pv_tc(const int64_t* S, int SR, const int8_t* __restrict__ Vd, int Tpad, const uint32_t* __restrict__ Vl,
+        int64_t* __restrict__ O, int64_t ldo, int T, int nh, int nkv, const int* __restrict__ skip,
+        const int* __restrict__ pvsel, int* err) {
+    using C = PvTc<HD>;
+    constexpr int TH = C::TH, RPT = C::RPT, CG = C::CG, RG = C::RG, PUS = C::PUS;
+    constexpr uint32_t IDESC = idesc_i8(C::NB);
+    if (*skip || *pvsel) return;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = (uint64_t*)(sm + 2 * C::BUF);
+    const uint32_t done0 = smem_u32(bars), accd = smem_u32(bars + 2);
+    uint32_t* tmem_slot = (uint32_t*)(bars + 3);
+    __shared__ int s_fail;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.y, b = blockIdx.z, t0 = blockIdx.x * PM;
+    const int z = b * nh + h, zk = b * nkv + h / (nh / nkv);
+    const int T4 = (T + 3) & ~3;
+    const int nch = (T + PVT - 1) / PVT;
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        mbar_init(done0, 1);
+        mbar_init(done0 + 8, 1);
+        mbar_init(accd, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == TH / 32) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "n"(C::ALLOC));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (warp < TH / 32) {  // every MMA accumulates: start from zero
+        const uint32_t lb = (uint32_t)(32 * (warp & 3)) << 16;
+        for (int c = 8 * (warp >> 2); c < C::COLS; c += 8 * (TH / 128)) tmem_st8_zero(tmem + lb + c);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+
+    const uint32_t sbase = smem_u32(sm);
+    const int8_t* vd0 = Vd + (int64_t)zk * C::NB * Tpad;
+    const uint32_t* vl0 = Vl + (int64_t)zk * T * HD;
+    // chunk k0's p rows, 4 (v mod 2^30) and v digits into buffer buf (all compute threads)
+    auto issue = [&](int k0, int buf) {
+        const uint32_t dst = sbase + buf * C::BUF;
+        for (int g = threadIdx.x; g < PM * (PVT / 4); g += TH) {  // p: 16 granules a row
+            const int r = g / (PVT / 4), s = k0 + 4 * (g % (PVT / 4));
+            const int t = t0 + r;
+            const bool ok = t < T && s < T4;
+            const uint32_t* src = ok ? (const uint32_t*)(S + ((int64_t)z * T + t) * SR) + s : (const uint32_t*)S;
+            cp_async16(dst + C::PD_B + C::VD_B + (r * PUS + 4 * (g % (PVT / 4))) * 4, src, ok ? 16u : 0u);
+        }
+        const int keys = min(PVT, T - k0);
+        for (int g = threadIdx.x; g < C::VL_B / 16; g += TH) {  // 4 (v mod 2^30): HD/4 granules a key
+            const int s = g / (HD / 4);
+            cp_async16(dst + C::PD_B + C::VD_B + C::PU_B + g * 16, s < keys ? vl0 + (int64_t)k0 * HD + g * 4 : vl0,
+                       s < keys ? 16u : 0u);
+        }
+        for (int g = threadIdx.x; g < C::NB * 4; g += TH) {  // v digits: four 16-byte granules a row
+            const int r = g >> 2, q = g & 3;
+            cp_async16(dst + C::PD_B + sw64_off(r, q), vd0 + (int64_t)r * Tpad + k0 + 16 * q, 16u);
+        }
+        cp_async_commit();
+    };
+
+    const int cg = threadIdx.x % CG, rg = threadIdx.x / CG;
+    const int c0 = 2 * cg, c1 = HD / 2 + 2 * cg;
+    uint32_t al[RPT][4];
+#pragma unroll
+    for (int r = 0; r < RPT; r++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) al[r][c] = 0;
+    if (warp < TH / 32) issue(0, 0);
+    for (int c = 0; c < nch; c++) {
+        const int buf = c & 1, k0 = c * PVT;
+        uint8_t* bp = sm + buf * C::BUF;
+        const uint32_t* Pu = (const uint32_t*)(bp + C::PD_B + C::VD_B);
+        const uint32_t* Vls = (const uint32_t*)(bp + C::PD_B + C::VD_B + C::PU_B);
+        if (warp < TH / 32) cp_async_wait_all();
+        __syncthreads();  // chunk c is in; every thread finished chunk c-1's CUDA-core part
+        if (warp < TH / 32) {
+            if (c + 1 < nch) {
+                // the other buffer's digit tiles were read by chunk c-1's MMAs
+                if (c >= 1 && !mbar_wait(done0 + 8 * (buf ^ 1), (uint32_t)((c - 1) >> 1) & 1u)) s_fail = 1;
+                issue(k0 + PVT, buf ^ 1);
+            }
+            // p digits of chunk c: (row, 16-key granule) items
+            for (int it = threadIdx.x; it < PM * 4; it += TH) {
+                const int r = it >> 2, q = it & 3;
+                uint32_t pk[4][4];
+#pragma unroll
+                for (int w4 = 0; w4 < 4; w4++) {
+                    const uint4 pv = *(const uint4*)(Pu + r * PUS + 16 * q + 4 * w4);
+                    const uint32_t pp[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+                    for (int i = 0; i < 4; i++) pk[i][w4] = 0;
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        int64_t x = pp[e];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const int d = (int)(((uint64_t)x + 128u) & 255u) - 128;
+                            x = (x - d) >> 8;
+                            pk[i][w4] |= (uint32_t)(uint8_t)(int8_t)d << (8 * e);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    *(uint4*)(bp + i * (PM * 64) + sw64_off(r, q)) = make_uint4(pk[i][0], pk[i][1], pk[i][2], pk[i][3]);
+            }
+            fence_proxy_async();  // generic-proxy tile writes (and the landed copies) visible to the MMA
+        }
+        __syncthreads();  // chunk c's digit tiles complete
+        if (warp == TH / 32) {
+            if (lane == 0) {
+                fence_after();
+                const uint32_t pd = sbase + buf * C::BUF, vd = pd + C::PD_B;
+#pragma unroll
+                for (int kk = 0; kk < PVT / 32; kk++) {
+                    const uint64_t bdesc = tc::sw64_desc(vd + kk * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+                        umma_i8(tmem + i * HD, tc::sw64_desc(pd + i * (PM * 64) + kk * 32), bdesc, IDESC, 1u);
+                }
+                umma_commit(done0 + 8 * buf);
+                if (c == nch - 1) umma_commit(accd);
+            }
+        } else {
+            // floor(p v_lo / 2^30) on the CUDA cores
+#pragma unroll 2
+            for (int s = 0; s < PVT; s += 4) {
+                uint4 pu[RPT];
+#pragma unroll
+                for (int r = 0; r < RPT; r++) pu[r] = *(const uint4*)(Pu + (rg + RG * r) * PUS + s);
+#pragma unroll
+                for (int u = 0; u < 4; u += 2) {
+                    const uint4 la = *(const uint4*)(Vls + (s + u) * HD + 4 * cg);
+                    const uint4 lb = *(const uint4*)(Vls + (s + u + 1) * HD + 4 * cg);
+#pragma unroll
+                    for (int r = 0; r < RPT; r++) {
+                        const uint32_t pa = u == 0 ? pu[r].x : pu[r].z, pb = u == 0 ? pu[r].y : pu[r].w;
+                        al[r][0] += __umulhi(pa, la.x) + __umulhi(pb, lb.x);
+                        al[r][1] += __umulhi(pa, la.y) + __umulhi(pb, lb.y);
+                        al[r][2] += __umulhi(pa, la.z) + __umulhi(pb, lb.z);
+                        al[r][3] += __umulhi(pa, la.w) + __umulhi(pb, lb.w);
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();  // every chunk's CUDA-core part is done: buffer 0's p region takes the floor sums
+    uint32_t* fs = (uint32_t*)(sm + C::PD_B + C::VD_B);
+    if (warp < TH / 32) {
+#pragma unroll
+        for (int r = 0; r < RPT; r++) {
+            const int row = rg + RG * r;
+            fs[row * C::FSL + c0] = al[r][0];
+            fs[row * C::FSL + c0 + 1] = al[r][1];
+            fs[row * C::FSL + c1] = al[r][2];
+            fs[row * C::FSL + c1 + 1] = al[r][3];
+        }
+    }
+    __syncthreads();
+    if (warp < 4 * C::EQ) {
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(accd, 0));
+        if (!ok) s_fail = 1;
+        fence_after();
+        const int q4 = warp & 3, part = warp >> 2;
+        const int row = 32 * q4 + lane, t = t0 + row;
+        const uint32_t ta = tmem + ((uint32_t)(32 * q4) << 16);
+        int64_t* orow = O + ((int64_t)b * T + (t < T ? t : 0)) * ldo + (int64_t)h * HD;
+        if (ok) {
+#pragma unroll 1
+            for (int cc = 8 * part; cc < HD; cc += 8 * C::EQ) {
+                uint32_t v[C::NS][8];
+#pragma unroll
+                for (int s2 = 0; s2 < C::NS; s2++) tmem_ld8(ta + s2 * HD + cc, v[s2]);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (t < T) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        uint64_t sum = 0;  // sum_s p v_hi = sum of 2^(8 s) P_s, below 2^46 in magnitude
+#pragma unroll
+                        for (int s2 = 0; s2 < C::NS; s2++) sum += (uint64_t)(int64_t)(int32_t)v[s2][j] << (8 * s2);
+                        orow[cc + j] = (int64_t)(sum + fs[row * C::FSL + cc + j]);
+                    }
+                }
+            }
+        }
+    }
+    fence_before();
+    __syncthreads();
+    if (s_fail && threadIdx.x == 0 && err) atomicOr(err, KERR_TIMEOUT);
+    if (warp == TH / 32) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(C::ALLOC));
+    }
+}
+
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 template <int HD>
-void launch_pv(int B, int T, int nh, int nkv, int64_t* scores, int sr, const int64_t* rmax, const int64_t* v, int64_t ldv,
-               double* vh, uint32_t* vl, int64_t* out, int64_t ldo, int* flag, cudaStream_t st) {
-    const dim3 vgrid((unsigned)((T * HD + 255) / 256), (unsigned)(B * nkv));
-    k_split_v<HD><<<vgrid, 256, 0, st>>>(v, ldv, T, nkv, vh, vl, flag, flag);
+void launch_pv(int B, int T, int nh, int nkv, int64_t* scores, int sr, const int64_t* v, int64_t ldv, double* vh,
+               uint32_t* vl, int8_t* vd, int tpad, int64_t* out, int64_t ldo, int* flag, int* pvsel, int* err,
+               cudaStream_t st) {
+    const dim3 vgrid((unsigned)(tpad / SV_KEYS), (unsigned)(B * nkv));
+    k_split_v<HD><<<vgrid, 256, 0, st>>>(v, ldv, T, tpad, nkv, vh, vl, vd, flag, flag, pvsel);
+    constexpr bool tcpath = HD <= 64;
+    if constexpr (tcpath) {
+        constexpr size_t smem = PvTc<HD>::SMEM;
+        static_assert(smem <= 227 * 1024, "tensor-core P.V shared memory");
+        static bool configured = false;
+        if (!configured) {
+            cudaFuncSetAttribute(k_pv_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            configured = true;
+        }
+        dim3 grid((unsigned)((T + PM - 1) / PM), (unsigned)nh, (unsigned)B);
+        k_pv_tc<HD><<<grid, PvTc<HD>::TH + 32, smem, st>>>(scores, sr, vd, tpad, vl, out, ldo, T, nh, nkv, flag, pvsel, err);
+    }
     constexpr size_t smem = Pv<HD>::SMEM;
-    static_assert(smem <= 200 * 1024, "softmax/PV shared memory");
+    static_assert(smem <= 200 * 1024, "P.V shared memory");
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(k_softmax_pv<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_pv_fp64<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         configured = true;
     }
     dim3 grid((unsigned)((T + PR - 1) / PR), (unsigned)nh, (unsigned)B);
-    k_softmax_pv<HD><<<grid, Pv<HD>::THREADS, smem, st>>>(scores, sr, rmax, vh, vl, out, ldo, T, nh, nkv, flag, flag);
+    k_pv_fp64<HD><<<grid, Pv<HD>::THREADS, smem, st>>>(scores, sr, vh, vl, out, ldo, T, nh, nkv, flag,
+                                                      tcpath ? pvsel : nullptr);
 }
 
 struct Layout {
-    int64_t kpad, tq, tk, sr, qbytes, kbytes, sbytes, mbytes, vhbytes, vlbytes;
+    int64_t kpad, tq, tk, sr, tpad, qbytes, kbytes, sbytes, mbytes, vhbytes, vlbytes, vdbytes;
 };
 
 Layout layout(int B, int T, int nh, int nkv, int hd) {
@@ -517,14 +787,16 @@ Layout layout(int B, int T, int nh, int nkv, int hd) {
     l.sbytes = round_up((int64_t)B * nh * T * l.sr * 8, 256);
     l.mbytes = round_up((int64_t)B * nh * T * 8, 256);
     l.vhbytes = round_up((int64_t)B * nkv * T * hd * 8, 256);
-    l.vlbytes = (int64_t)B * nkv * T * hd * 4;
+    l.vlbytes = round_up((int64_t)B * nkv * T * hd * 4, 256);
+    l.tpad = round_up(T, PVT);
+    l.vdbytes = (int64_t)B * nkv * 2 * hd * l.tpad;
     return l;
 }
 }  // namespace
 
 size_t attention_tc_workspace(int B, int T, int nh, int nkv, int hd) {
     const Layout l = layout(B, T, nh, nkv, hd);
-    return (size_t)(256 + l.qbytes + l.kbytes + l.sbytes + l.mbytes + l.vhbytes + l.vlbytes);
+    return (size_t)(256 + l.qbytes + l.kbytes + l.sbytes + l.mbytes + l.vhbytes + l.vlbytes + l.vdbytes);
 }
 
 bool attention_tc_supported(int T, int nh, int nkv, int hd) {
@@ -545,11 +817,13 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     int64_t* rmax = (int64_t*)((uint8_t*)scores + l.sbytes);
     double* vh = (double*)((uint8_t*)rmax + l.mbytes);
     uint32_t* vl = (uint32_t*)((uint8_t*)vh + l.vhbytes);
+    int8_t* vd = (int8_t*)((uint8_t*)vl + l.vlbytes);
+    int* pvsel = flag + 1;  // v >> 30 beyond two digits: the fp64 P.V instead of the tensor-core one
     alignas(64) unsigned char mq[128], mk[128];
     if (!encode_planes(mq, qp, l.kpad, l.tq, LA, QM, (int64_t)B * nh) ||
         !encode_planes(mk, kp, l.kpad, l.tk, LA, NK, (int64_t)B * nkv))
         return -1;
-    cudaMemsetAsync(flag, 0, sizeof(int), st);
+    cudaMemsetAsync(flag, 0, 2 * sizeof(int), st);
     split_heads(q, ldq, B, T, nh, hd, l.tq, l.kpad, qp, flag, st);
     split_heads(k, ldk, B, T, nkv, hd, l.tk, l.kpad, kp, flag, st);
 
@@ -566,16 +840,20 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     if (l.kpad == BK) launch_scores_kb<1>(*(const CUtensorMap*)mq, *(const CUtensorMap*)mk, sp, sgrid, st);
     else launch_scores_kb<2>(*(const CUtensorMap*)mq, *(const CUtensorMap*)mk, sp, sgrid, st);
 
+    const int64_t rows = (int64_t)B * nh * T;
+    k_softmax<<<(unsigned)((rows + SM_ROWS - 1) / SM_ROWS), 32 * SM_ROWS, 0, st>>>(scores, (int)l.sr, rmax, T, (int)rows,
+                                                                                  flag, flag);
+    const int tp = (int)l.tpad, sr = (int)l.sr;
     switch (hd) {
-        case 16: launch_pv<16>(B, T, nh, nkv, scores, (int)l.sr, rmax, v, ldv, vh, vl, out, ldo, flag, st); break;
-        case 32: launch_pv<32>(B, T, nh, nkv, scores, (int)l.sr, rmax, v, ldv, vh, vl, out, ldo, flag, st); break;
-        case 64: launch_pv<64>(B, T, nh, nkv, scores, (int)l.sr, rmax, v, ldv, vh, vl, out, ldo, flag, st); break;
-        case 128: launch_pv<128>(B, T, nh, nkv, scores, (int)l.sr, rmax, v, ldv, vh, vl, out, ldo, flag, st); break;
-        default: launch_pv<256>(B, T, nh, nkv, scores, (int)l.sr, rmax, v, ldv, vh, vl, out, ldo, flag, st); break;
+        case 16: launch_pv<16>(B, T, nh, nkv, scores, sr, v, ldv, vh, vl, vd, tp, out, ldo, flag, pvsel, err, st); break;
+        case 32: launch_pv<32>(B, T, nh, nkv, scores, sr, v, ldv, vh, vl, vd, tp, out, ldo, flag, pvsel, err, st); break;
+        case 64: launch_pv<64>(B, T, nh, nkv, scores, sr, v, ldv, vh, vl, vd, tp, out, ldo, flag, pvsel, err, st); break;
+        case 128: launch_pv<128>(B, T, nh, nkv, scores, sr, v, ldv, vh, vl, vd, tp, out, ldo, flag, pvsel, err, st); break;
+        default: launch_pv<256>(B, T, nh, nkv, scores, sr, v, ldv, vh, vl, vd, tp, out, ldo, flag, pvsel, err, st); break;
     }
     // the exact kernel redoes the whole call when anything fell outside the fast ranges
     attention(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, score_shift, sqrt_hd, mode, window, st, flag);
-    return 6;
+    return hd <= 64 ? 8 : 7;
 }
 
 }  // namespace slx

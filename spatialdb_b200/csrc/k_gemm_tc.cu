@@ -48,17 +48,6 @@ struct Params {
     const int8_t* row_shift;
 };
 
-// K-major operand, 64-byte swizzle: rows of 64 bytes, 8-row groups 512 bytes apart.
-__device__ __forceinline__ uint64_t sw64_desc(uint32_t addr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((addr >> 4) & 0x3FFF);
-    d |= (uint64_t)1 << 16;
-    d |= (uint64_t)(512 >> 4) << 32;
-    d |= (uint64_t)1 << 46;
-    d |= (uint64_t)4 << 61;
-    return d;
-}
-
 // Bounded spin on an mbarrier phase without suspending (the MMA issuer's waits are short and on the
 // critical path): about two seconds of SM clock, then false.
 __device__ __forceinline__ bool mbar_spin(uint32_t bar, uint32_t parity) {

@@ -1,5 +1,5 @@
 // tc_ptx.cuh -- inline-PTX building blocks of the tcgen05 kernels (sm_100a): mbarriers with bounded
-// waits, TMA tiled loads (no multicast), shared-memory matrix descriptors (128-byte swizzle,
+// waits, TMA tiled loads (no multicast), shared-memory matrix descriptors (128- and 64-byte swizzle,
 // K-major), kind::i8 MMA issue and commit, TMEM loads and stores.
 #pragma once
 #include <cuda.h>
@@ -83,6 +83,17 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
     d |= (uint64_t)(1024 >> 4) << 32;        // stride byte offset
     d |= (uint64_t)1 << 46;                  // descriptor version (sm_100)
     d |= (uint64_t)2 << 61;                  // SWIZZLE_128B
+    return d;
+}
+
+// K-major operand, 64-byte swizzle: rows of 64 bytes, 8-row groups 512 bytes apart.
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(512 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)4 << 61;
     return d;
 }
 

@@ -45,6 +45,20 @@ def test_attention_reference_test_shapes(ctx, oracle):
         np.testing.assert_array_equal(got, ref)
 
 
+@pytest.mark.parametrize("hd", [16, 64])
+def test_attention_large_values_take_fp64_pv(ctx, oracle, hd):
+    """v >> 30 beyond two base-256 digits (|v| near 2^50): the tensor-core P.V steps aside for the fp64
+    one on the device, still exact."""
+    rng = np.random.default_rng(11 + hd)
+    seq, nh = 150, 3
+    q, k, _ = _qkv(rng, seq, nh * hd, nh * hd, 1 << 32)
+    v = rng.integers(-(1 << 50), 1 << 50, (seq, nh * hd), dtype=np.int64)
+    for mode in (0, 1):
+        got = slx.attention(q, k, v, seq, nh, nh, -30, mode, 0, ctx=ctx)
+        ref = oracle.attention(q, k, v, seq, nh * hd, nh * hd, nh, nh, -30, 30, mode, 0).reshape(seq, nh * hd)
+        np.testing.assert_array_equal(got, ref)
+
+
 @pytest.mark.parametrize("what", ["q_wide", "k_wide", "v_wide", "scores_wrap"])
 def test_attention_out_of_range_inputs_fall_back_exactly(ctx, oracle, what):
     rng = np.random.default_rng(9)
