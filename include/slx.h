@@ -174,8 +174,8 @@ slx_status slx_knn_merge_device(slx_ctx* ctx, const int64_t* d_ids, const uint64
 /* ---- measurement ---------------------------------------------------------------------------- */
 /* No reference counterpart (the reference times with Stopwatch, SparseLattice.Perf/Program.cs:817-830).
  * Per kernel class, the library's launches on ctx between begin and end, their device time from
- * CUDA events recorded on the launch stream, and the algorithmic multiply-accumulates they
- * performed. Classes: gemm, attention, norm, rope, ffn_gate, embed, pool, add, argmax, gemv, split, fallback,
+ * CUDA events recorded on the launch stream, the algorithmic multiply-accumulates they performed
+ * and, for the tensor-core projections, the int8 digit products issued. Classes: gemm, attention, norm, rope, ffn_gate, embed, pool, add, argmax, gemv, split, fallback,
  * search. */
 typedef struct slx_kernel_stat {
     char name[24];
@@ -183,6 +183,7 @@ typedef struct slx_kernel_stat {
     double ms;
     double macs;
     double bytes;
+    double tc_macs;  /* int8 multiply-accumulates issued on the tensor cores (digit products) */
 } slx_kernel_stat;
 slx_status slx_profile_begin(slx_ctx* ctx);
 slx_status slx_profile_end(slx_ctx* ctx, slx_kernel_stat* stats, int cap, int* n);

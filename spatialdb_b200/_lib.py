@@ -59,7 +59,7 @@ SIGNATURES = {
 
 class KernelStat(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 24), ("launches", ctypes.c_int64), ("ms", ctypes.c_double),
-                ("macs", ctypes.c_double), ("bytes", ctypes.c_double)]
+                ("macs", ctypes.c_double), ("bytes", ctypes.c_double), ("tc_macs", ctypes.c_double)]
 
 
 def header_symbols() -> list[str]:

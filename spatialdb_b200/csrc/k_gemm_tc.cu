@@ -37,7 +37,7 @@ constexpr int THREADS = 32 * (2 + EPI_WARPS);
 constexpr int NACC = 2;       // TMEM accumulators (tile parity picks one)
 
 struct Params {
-    int M, N, nkb, shift, tiles_m, tiles;
+    int M, N, nkb, shift, tiles_n, tiles;  // tiles: weight tiles fastest, so resident CTAs share activation tiles
     int64_t* C;
     int64_t ldc;
     const int64_t* R;
@@ -132,7 +132,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             uint32_t ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
-                const int m0 = (t % p.tiles_m) * GM, n0 = (t / p.tiles_m) * GN;
+                const int m0 = (t / p.tiles_n) * GM, n0 = (t % p.tiles_n) * GN;
                 for (int kb = 0; kb < p.nkb; kb++, g++) {
                     if (!mbar_wait(empty0 + 8 * s, ph ^ 1u) || *(volatile int*)&s_fail) {
                         s_fail = 1;
@@ -180,7 +180,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         int lt = 0;
         for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, lt++) {
             const int b = lt & 1;
-            const int m0 = (t % p.tiles_m) * GM, n0 = (t / p.tiles_m) * GN;
+            const int m0 = (t / p.tiles_n) * GM, n0 = (t % p.tiles_n) * GN;
             const int n = n0 + 32 * q4 + lane;
             const bool n_ok = n < p.N;
             // out = lo64(floor(sum * 2^rs / 2^shift)), sum = 2^32 H + L, e = shift - rs:
@@ -527,8 +527,8 @@ void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K,
     (void)K;
     Params p = base_params();
     p.M = M; p.N = N; p.nkb = (int)(kpad / GK); p.shift = shift;
-    p.tiles_m = (int)(mpad / GM);
-    p.tiles = p.tiles_m * (int)((npad + GN - 1) / GN);
+    p.tiles_n = (int)((npad + GN - 1) / GN);
+    p.tiles = (int)(mpad / GM) * p.tiles_n;
     p.C = c; p.ldc = ldc; p.R = r; p.ldr = ldr; p.skip = skip; p.err = err; p.row_shift = row_shift;
     const CUtensorMap& ta = *(const CUtensorMap*)tmap_a;
     const CUtensorMap& tw = *(const CUtensorMap*)tmap_w;

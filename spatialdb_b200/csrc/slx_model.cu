@@ -38,7 +38,7 @@ struct ProfRecord {
     int cls;
     int launches;
     cudaEvent_t a, b;
-    double macs, bytes;
+    double macs, bytes, tc_macs;
 };
 
 struct slx_ctx {
@@ -62,12 +62,12 @@ struct slx_ctx {
 // Runs one launcher (which returns how many kernels it queued), counting launches and, when
 // profiling, bracketing it with events on the launch stream.
 template <class F>
-static inline void run_k(slx_ctx* c, int cls, double macs, double bytes, cudaStream_t st, F&& f) {
+static inline void run_k(slx_ctx* c, int cls, double macs, double bytes, cudaStream_t st, F&& f, double tc_macs = 0) {
     if (!c->prof) {
         c->launches += f();
         return;
     }
-    ProfRecord r{cls, 0, c->event(), c->event(), macs, bytes};
+    ProfRecord r{cls, 0, c->event(), c->event(), macs, bytes, tc_macs};
     cudaEventRecord(r.a, st);
     r.launches = f();
     cudaEventRecord(r.b, st);
@@ -406,7 +406,11 @@ int attend(slx_model* m, const int64_t* q, int64_t ldq, const int64_t* k, int64_
 inline void project(slx_model* m, const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPlan& p, int64_t* c,
                     int64_t ldc, const int64_t* r, int64_t ldr, cudaStream_t st) {
     double macs = (double)M * (double)w.N * (double)w.K;
-    run_k(m->ctx, KC_GEMM, macs, 0, st, [&] { return gemm_run(a, lda, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st); });
+    // digit products the tensor-core path issues: 5 activation digits x the weight's digits, K padded
+    const bool tc_path = p.use_tc && !(!r && gemv_supported(w, M));
+    const double tc = tc_path ? (double)M * (double)w.N * (double)p.k_pad * tc::LA * p.wlimbs : 0.0;
+    run_k(m->ctx, KC_GEMM, macs, 0, st, [&] { return gemm_run(a, lda, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st); },
+          tc);
 }
 #define RUN(cls, macs, bytes, call) run_k(ctx, cls, macs, bytes, st, [&] { return call; })
 
@@ -922,6 +926,7 @@ slx_status slx_profile_end(slx_ctx* ctx, slx_kernel_stat* stats, int cap, int* n
         acc[r.cls].ms += ms;
         acc[r.cls].macs += r.macs;
         acc[r.cls].bytes += r.bytes;
+        acc[r.cls].tc_macs += r.tc_macs;
         ctx->event_pool.push_back(r.a);
         ctx->event_pool.push_back(r.b);
     }
