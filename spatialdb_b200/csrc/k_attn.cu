@@ -45,7 +45,8 @@ constexpr int NK = 16;                  // keys per tile
 constexpr int NSH = 2 * LA - 1;         // shift blocks of 16 columns
 constexpr int NBUF = 3;                 // TMEM accumulators
 constexpr int BUF_COLS = NSH * NK;      // 144
-constexpr int EPI = 8;                  // epilogue warps (two per TMEM lane quarter)
+constexpr int EPI = 16;                 // epilogue warps (four per TMEM lane quarter)
+constexpr int CW = NK / (EPI / 4);      // key columns of a tile per epilogue warp
 constexpr int S_THREADS = 32 * (2 + EPI);
 constexpr uint32_t QPLANE = QM * BK;    // one query digit plane, one 128-byte K block
 constexpr uint32_t KPLANE = NK * BK;
@@ -76,7 +77,7 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
     const uint32_t done0 = smem_u32(bars + 2 * nst + 1), tfree0 = smem_u32(bars + 2 * nst + 1 + NBUF);
     uint32_t* tmem_slot = (uint32_t*)(bars + 2 * nst + 1 + 2 * NBUF);
     __shared__ int s_fail;
-    __shared__ int64_t s_max[QM];
+    __shared__ int64_t s_max[EPI / 4][QM];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -100,13 +101,13 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
     __syncthreads();
     fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int q4 = warp & 3, half = (warp - 2) >> 2;           // epilogue: lane quarter, column half
+    const int q4 = warp & 3, part = (warp - 2) >> 2;           // epilogue: lane quarter, column part
     const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
     if (warp >= 2) {  // every MMA accumulates: start from zero
 #pragma unroll 1
         for (int b = 0; b < NBUF; b++)
 #pragma unroll
-            for (int s = 0; s < NSH; s++) tmem_st8_zero(tmem + lane_base + b * BUF_COLS + s * NK + 8 * half);
+            for (int s = 0; s < NSH; s++) tmem_st4_zero(tmem + lane_base + b * BUF_COLS + s * NK + CW * part);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
     fence_before();
@@ -163,7 +164,7 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
             }
             if (!ok) s_fail = 1;
         }
-    } else {  // epilogue: row = TMEM lane, 8 of each tile's 16 keys
+    } else {  // epilogue: row = TMEM lane, CW of each tile's 16 keys
         const int row = m0 + 32 * q4 + lane;
         const bool row_ok = row < p.T;
         int64_t* srow = p.S + ((int64_t)z * p.T + (row_ok ? row : 0)) * p.SR;
@@ -176,21 +177,21 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
             const bool ok = __all_sync(0xffffffffu, mbar_wait(done0 + 8 * b, (uint32_t)(t / NBUF) & 1u));
             if (!ok) { s_fail = 1; break; }
             fence_after();
-            uint32_t v[NSH][8];
-            const uint32_t ta = tmem + lane_base + b * BUF_COLS + 8 * half;
+            uint32_t v[NSH][CW];
+            const uint32_t ta = tmem + lane_base + b * BUF_COLS + CW * part;
 #pragma unroll
-            for (int s = 0; s < NSH; s++) tmem_ld8(ta + s * NK, v[s]);
+            for (int s = 0; s < NSH; s++) tmem_ld4(ta + s * NK, v[s]);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-            for (int s = 0; s < NSH; s++) tmem_st8_zero(ta + s * NK);
+            for (int s = 0; s < NSH; s++) tmem_st4_zero(ta + s * NK);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tfree0 + 8 * b);
-            const int n0 = t * NK + 8 * half;
-            int64_t o[8];
+            const int n0 = t * NK + CW * part;
+            int64_t o[CW];
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
+            for (int j = 0; j < CW; j++) {
                 const uint64_t L = (uint64_t)(int64_t)(int32_t)v[0][j] + ((uint64_t)(int64_t)(int32_t)v[1][j] << 8) +
                                    ((uint64_t)(int64_t)(int32_t)v[2][j] << 16) + ((uint64_t)(int64_t)(int32_t)v[3][j] << 24);
                 const uint64_t H = (uint64_t)(int64_t)(int32_t)v[4][j] + ((uint64_t)(int64_t)(int32_t)v[5][j] << 8) +
@@ -209,20 +210,24 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
                 if (n < p.T) mx = max(mx, x);
             }
             if (row_ok) {
-                if (n0 + 8 <= p.T) {
+                if (n0 + CW <= p.T) {
 #pragma unroll
-                    for (int j = 0; j < 8; j += 2) *(longlong2*)(srow + n0 + j) = make_longlong2(o[j], o[j + 1]);
+                    for (int j = 0; j < CW; j += 2) *(longlong2*)(srow + n0 + j) = make_longlong2(o[j], o[j + 1]);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 8; j++)
+                    for (int j = 0; j < CW; j++)
                         if (n0 + j < p.T) srow[n0 + j] = o[j];
                 }
             }
         }
-        // row maximum over both column halves
-        if (half == 1) s_max[32 * q4 + lane] = mx;
+        // row maximum over the column parts
+        s_max[part][32 * q4 + lane] = mx;
         asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI) : "memory");
-        if (half == 0 && row_ok) p.rmax[(int64_t)z * p.T + row] = max(mx, s_max[32 * q4 + lane]);
+        if (part == 0 && row_ok) {
+#pragma unroll
+            for (int i = 1; i < EPI / 4; i++) mx = max(mx, s_max[i][32 * q4 + lane]);
+            p.rmax[(int64_t)z * p.T + row] = mx;
+        }
     }
     fence_before();
     __syncthreads();
