@@ -98,6 +98,20 @@ slx_status slx_causal_next_token(slx_model* model, const int32_t* ids, int B, in
  * n_out[B] their counts. */
 slx_status slx_causal_generate(slx_model* model, const int32_t* ids, int B, int T, int max_new, int32_t* out,
                                int32_t* n_out);
+/* PredictNextToken with the VocabLattice (:149-157, Lattice/VocabLattice.cs:15-76): the rows of
+ * TokenEmbeddingsFloat ((float)Half, :51-62) and the float hidden state are quantized with
+ * ZeroThreshold 0.001 and GlobalScale 1e9; the k rows nearest by DistanceSquaredL2Fast
+ * (Math/SparseVector.cs:138-169) are scored by their sequential fp32 dot with the hidden state and
+ * the highest score wins. Ties have no defined order in the reference (unstable sorts): equal
+ * distances go by ascending row, equal scores to the nearer candidate. k <= 0 (no candidate) gives
+ * EOS; k > 8192 is SLX_EINVAL. The lattice is built on the device at the first call. */
+slx_status slx_causal_next_token_lattice(slx_model* model, const int32_t* ids, int B, int T, int k, int32_t* next);
+/* Generate(useLattice: true, latticeK: k) on token ids (:86-108), B prompts as slx_causal_generate. */
+slx_status slx_causal_generate_lattice(slx_model* model, const int32_t* ids, int B, int T, int max_new, int k,
+                                       int32_t* out, int32_t* n_out);
+/* VocabLattice.QueryTopK (Lattice/VocabLattice.cs:43-58) of a causal model's lattice for B float
+ * hidden states [B][embd]: ids[B][k] ascending by (distance, row), -1 past the vocabulary. */
+slx_status slx_vocab_lattice_query(slx_model* model, const float* hidden, int B, int k, int32_t* ids);
 
 /* ---- kernel-level ---------------------------------------------------------------------------- */
 /* IntegerMatMul.MatMul with GGUF weights (Math/IntegerMatMul.cs:37-76 for the long composite,
@@ -176,7 +190,7 @@ slx_status slx_knn_merge_device(slx_ctx* ctx, const int64_t* d_ids, const uint64
  * Per kernel class, the library's launches on ctx between begin and end, their device time from
  * CUDA events recorded on the launch stream, the algorithmic multiply-accumulates they performed
  * and, for the tensor-core projections, the int8 digit products issued. Classes: gemm, attention, norm, rope, ffn_gate, embed, pool, add, argmax, gemv, split, fallback,
- * search. */
+ * search, vocab. */
 typedef struct slx_kernel_stat {
     char name[24];
     int64_t launches;

@@ -93,6 +93,8 @@ def _sig(lib):
     f("slxo_causal_forward_last", i, VP, I32P, i, I64P)
     f("slxo_causal_next_token", i, VP, I32P, i, I32P)
     f("slxo_causal_generate", i, VP, I32P, i, i, I32P, ctypes.POINTER(i))
+    f("slxo_causal_next_token_lattice", i, VP, I32P, i, i, I32P)
+    f("slxo_causal_generate_lattice", i, VP, I32P, i, i, i, I32P, ctypes.POINTER(i))
     f("slxo_gemma_encoder_forward", i, VP, I32P, i, i, I64P)
     f("slxo_quantize_dense", None, F32P, i64, f32, i64, I64P)
     f("slxo_distance_sq_l2_fast", ctypes.c_uint64, I64P, I64P, i)
@@ -467,6 +469,25 @@ class Causal:
         st = lib().slxo_causal_generate(self._h, _p(ids, I32P), ids.size, max_new, _p(out, I32P), ctypes.byref(n))
         if st:
             raise OracleError(st, "generate")
+        return out[: n.value].copy()
+
+    def next_token_lattice(self, ids, k: int = 64) -> int:
+        """PredictNextToken with the VocabLattice (k nearest candidates, best sequential fp32 dot)."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        nx = ctypes.c_int32(0)
+        st = lib().slxo_causal_next_token_lattice(self._h, _p(ids, I32P), ids.size, k, ctypes.byref(nx))
+        if st:
+            raise OracleError(st, "next_token_lattice")
+        return nx.value
+
+    def generate_lattice(self, ids, max_new: int, k: int = 64) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty(max(max_new, 1), np.int32)
+        n = ctypes.c_int(0)
+        st = lib().slxo_causal_generate_lattice(self._h, _p(ids, I32P), ids.size, max_new, k, _p(out, I32P),
+                                                 ctypes.byref(n))
+        if st:
+            raise OracleError(st, "generate_lattice")
         return out[: n.value].copy()
 
     def encode_pooled(self, ids) -> np.ndarray:

@@ -1037,6 +1037,7 @@ struct Causal {
     std::vector<GemmaLayer> L;
     RoPE rope_local, rope_global;
     bool causal = true;  // false: IntegerGemmaSource encoder semantics
+    mutable std::vector<int64_t> vocab_q;  // the VocabLattice's quantized rows, built on first use
 };
 
 static int read_half(Gguf* g, const std::string& name, std::vector<uint16_t>& out) {
@@ -1273,6 +1274,62 @@ static void knn_l2(const int64_t* db, int64_t n, int dim, const int64_t* q, int 
     }
 }
 
+// PredictNextToken with a VocabLattice (IntegerCausalSource.cs:149-157): the lattice holds the rows of
+// TokenEmbeddingsFloat ((float)Half, :51-62) quantized by EmbeddingAdapter.Quantize with VocabLattice's
+// options (ZeroThreshold 0.001, GlobalScale 1e9; Lattice/VocabLattice.cs:15-41); QueryTopK (:43-58)
+// returns the k nearest by DistanceSquaredL2Fast; ScoreCandidates (:60-76) takes the sequential fp32
+// dot of each candidate row with the hidden state and Array.Sort orders them by descending score.
+// That sort is unstable, so equal scores have no defined order; here the first candidate (ascending
+// distance, then id) among the highest scores wins. No candidate (k = 0) gives EOS.
+static void vocab_lattice_build(const Causal& c);
+static int32_t lattice_next(const Causal& c, const float* h, int k) {
+    vocab_lattice_build(c);
+    const int64_t V = (int64_t)c.vocab_q.size() / c.embd;
+    std::vector<int64_t> hq(c.embd), ids(k > 0 ? k : 1);
+    std::vector<uint64_t> dist(k > 0 ? k : 1);
+    quantize_dense(h, c.embd, 0.001f, 1000000000LL, hq.data());
+    if (k > 0) knn_l2(c.vocab_q.data(), V, c.embd, hq.data(), 1, k, 0, ids.data(), dist.data());
+    int32_t best = c.eos;
+    float best_score = 0.0f;
+    bool have = false;
+    for (int j = 0; j < k; j++) {
+        if (ids[j] < 0) break;
+        const uint16_t* row = c.tok.data() + ids[j] * c.embd;
+        float dot = 0.0f;
+        for (int d = 0; d < c.embd; d++) {
+            float p = h[d] * half_to_float(row[d]);
+            dot = dot + p;
+        }
+        if (!have || dot > best_score || (std::isnan(best_score) && !std::isnan(dot))) {
+            best = (int32_t)ids[j];
+            best_score = dot;
+            have = true;
+        }
+    }
+    return best;
+}
+
+static void vocab_lattice_build(const Causal& c) {
+    if (!c.vocab_q.empty()) return;
+    const int64_t rows = std::min<int64_t>(c.vocab, (int64_t)c.tok.size() / c.embd);
+    std::vector<float> f((size_t)rows * c.embd);
+    for (size_t i = 0; i < f.size(); i++) f[i] = half_to_float(c.tok[i]);
+    c.vocab_q.resize(f.size());
+    quantize_dense(f.data(), (int64_t)f.size(), 0.001f, 1000000000LL, c.vocab_q.data());
+}
+
+static int causal_next_lattice(const Causal& c, const int32_t* ids, int T, int k, int32_t* next) {
+    std::vector<int64_t> x((size_t)T * c.embd);
+    int st = causal_hidden(c, ids, T, -1, true, x.data());
+    if (st) return st;
+    const int64_t* last = x.data() + (size_t)(T - 1) * c.embd;
+    std::vector<float> h(c.embd);
+    double scale = std::pow(2.0, -c.scale_bits);
+    for (int j = 0; j < c.embd; j++) h[j] = (float)((double)last[j] * scale);
+    *next = lattice_next(c, h.data(), k);
+    return SLXO_OK;
+}
+
 extern "C" {
 
 int slxo_set_threads(int n) {
@@ -1440,6 +1497,24 @@ int slxo_causal_forward_last(void* cp, const int32_t* ids, int T, int64_t* last)
 }
 int slxo_causal_next_token(void* cp, const int32_t* ids, int T, int32_t* next) {
     return causal_next(*(Causal*)cp, ids, T, next, nullptr);
+}
+int slxo_causal_next_token_lattice(void* cp, const int32_t* ids, int T, int k, int32_t* next) {
+    return causal_next_lattice(*(Causal*)cp, ids, T, k, next);
+}
+// Generate(useLattice: true, latticeK: k) on token ids (IntegerCausalSource.cs:86-108).
+int slxo_causal_generate_lattice(void* cp, const int32_t* ids, int T, int max_new, int k, int32_t* out, int* n_out) {
+    Causal* c = (Causal*)cp;
+    std::vector<int32_t> seq(ids, ids + T);
+    *n_out = 0;
+    for (int step = 0; step < max_new; step++) {
+        int32_t nx;
+        int st = causal_next_lattice(*c, seq.data(), (int)seq.size(), k, &nx);
+        if (st) return st;
+        if (nx == c->eos) break;
+        seq.push_back(nx);
+        out[(*n_out)++] = nx;
+    }
+    return SLXO_OK;
 }
 // Generate (IntegerCausalSource.cs:86-108) on token ids: full re-forward per step, greedy argmax,
 // stop at EOS (not appended). Returns the new ids in out[0..*n_out).

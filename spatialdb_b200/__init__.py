@@ -240,22 +240,46 @@ class IntegerCausalSource(_Model):
         v = self.forward_causal(ids)
         return (v.astype(np.float64) * 2.0 ** -self.scale_bits).astype(np.float32)
 
-    def next_token(self, ids) -> np.ndarray:
-        """Greedy next id for each of B sequences [B, T] (ArgmaxBruteForce head)."""
+    def next_token(self, ids, use_lattice: bool = False, lattice_k: int = 64) -> np.ndarray:
+        """Greedy next id for each of B sequences [B, T]: PredictNextToken (IntegerCausalSource.cs:149-157)
+        with the ArgmaxBruteForce head, or with the VocabLattice head and `lattice_k` candidates."""
         ids = np.ascontiguousarray(np.atleast_2d(ids), np.int32)
         B, T = ids.shape
         out = np.empty(B, np.int32)
-        self.ctx.check(self.ctx._lib.slx_causal_next_token(self._h, _p(ids, I32P), B, T, _p(out, I32P)))
+        lib = self.ctx._lib
+        if use_lattice:
+            self.ctx.check(lib.slx_causal_next_token_lattice(self._h, _p(ids, I32P), B, T, int(lattice_k), _p(out, I32P)))
+        else:
+            self.ctx.check(lib.slx_causal_next_token(self._h, _p(ids, I32P), B, T, _p(out, I32P)))
         return out
 
-    def generate(self, ids, max_new_tokens: int = 64) -> list[np.ndarray]:
-        """Generate on token ids [B, T]: greedy, full re-forward per token, stop at EOS."""
+    def generate(self, ids, max_new_tokens: int = 64, use_lattice: bool = False, lattice_k: int = 64) -> list[np.ndarray]:
+        """Generate on token ids [B, T] (IntegerCausalSource.cs:86-108): greedy, full re-forward per
+        token, stop at EOS; `use_lattice` scores only the `lattice_k` VocabLattice candidates."""
         ids = np.ascontiguousarray(np.atleast_2d(ids), np.int32)
         B, T = ids.shape
         out = np.zeros((B, max(max_new_tokens, 1)), np.int32)
         n = np.zeros(B, np.int32)
-        self.ctx.check(self.ctx._lib.slx_causal_generate(self._h, _p(ids, I32P), B, T, max_new_tokens, _p(out, I32P), _p(n, I32P)))
+        lib = self.ctx._lib
+        if use_lattice:
+            rc = lib.slx_causal_generate_lattice(self._h, _p(ids, I32P), B, T, max_new_tokens, int(lattice_k),
+                                                 _p(out, I32P), _p(n, I32P))
+        else:
+            rc = lib.slx_causal_generate(self._h, _p(ids, I32P), B, T, max_new_tokens, _p(out, I32P), _p(n, I32P))
+        self.ctx.check(rc)
         return [out[b, : n[b]].copy() for b in range(B)]
+
+    def vocab_lattice_query(self, hidden, k: int = 64) -> np.ndarray:
+        """VocabLattice.QueryTopK (Lattice/VocabLattice.cs:43-58) for float hidden states [B, embd]:
+        ids [B, k] ascending by (distance, row), -1 past the vocabulary."""
+        h = np.ascontiguousarray(np.atleast_2d(hidden), np.float32)
+        B = h.shape[0]
+        if h.shape[1] != self.embd:
+            raise ValueError(f"hidden width {h.shape[1]} != embd {self.embd}")
+        out = np.full((B, max(k, 0)), -1, np.int32)
+        if k > 0 and B > 0:
+            self.ctx.check(self.ctx._lib.slx_vocab_lattice_query(self._h, _p(h, F32P), B, int(k), _p(out, I32P)))
+        return out
 
 
 # ---- lattice k-NN search --------------------------------------------------------------------------

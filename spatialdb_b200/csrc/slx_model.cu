@@ -25,14 +25,15 @@
 #include "slx_kernels.h"
 #include "slx_gemm.h"
 #include "slx_search.h"
+#include "slx_vocab.h"
 
 using namespace slx;
 
 // Kernel classes reported by slx_profile_end.
 enum KClass { KC_GEMM, KC_ATTENTION, KC_NORM, KC_ROPE, KC_FFN_GATE, KC_EMBED, KC_POOL, KC_ADD, KC_ARGMAX, KC_GEMV,
-              KC_SPLIT, KC_FALLBACK, KC_SEARCH, KC_COUNT };
+              KC_SPLIT, KC_FALLBACK, KC_SEARCH, KC_VOCAB, KC_COUNT };
 static const char* kKClassName[KC_COUNT] = {"gemm", "attention", "norm", "rope", "ffn_gate", "embed", "pool", "add",
-                                            "argmax", "gemv", "split", "fallback", "search"};
+                                            "argmax", "gemv", "split", "fallback", "search", "vocab"};
 
 struct ProfRecord {
     int cls;
@@ -153,8 +154,11 @@ struct slx_model {
     int64_t *cos_l = nullptr, *sin_l = nullptr, *cos_g = nullptr, *sin_g = nullptr;
     std::map<std::string, DevBuf> ws;
     GemmWorkspace gws;
+    vocab::Lattice vlat;             // VocabLattice of the causal head, built on first use
+    bool vlat_ready = false;
 
     ~slx_model() {
+        vocab::release(vlat);
         for (auto& kv : ws) cudaFree(kv.second.p);
         for (void* p : allocs) cudaFree(p);
         gemm_workspace_free(gws);
@@ -706,10 +710,24 @@ slx_status slx_causal_forward_last(slx_model* m, const int32_t* ids, int T, int6
     return check_flag(ctx, st);
 }
 
-slx_status slx_causal_next_token(slx_model* m, const int32_t* ids, int B, int T, int32_t* next) {
+// Builds the VocabLattice of a causal model once (IntegerCausalSource.GetVocabLattice, :69-74).
+static int vocab_lattice_ready(slx_model* m, cudaStream_t st) {
+    if (m->vlat_ready) return SLX_OK;
+    std::string err;
+    int rc = vocab::build(m->tok, m->vocab, m->embd, m->vlat, st, err);
+    if (rc) return set_err(m->ctx, rc, "%s", err.c_str());
+    m->ctx->launches += m->vlat.V > 0 ? 1 : 0;
+    m->vlat_ready = true;
+    return SLX_OK;
+}
+
+// PredictNextToken (IntegerCausalSource.cs:149-157) for B sequences: the brute-force argmax head
+// (lattice_k < 0) or the VocabLattice head with k candidates.
+static slx_status causal_next(slx_model* m, const int32_t* ids, int B, int T, int lattice_k, int32_t* next) {
     if (!m || !ids || !next || B <= 0 || T <= 0) return m ? set_err(m->ctx, SLX_EINVAL, "bad arguments") : SLX_EINVAL;
     slx_ctx* ctx = m->ctx;
     if (m->kind != SLX_MODEL_CAUSAL) return set_err(ctx, SLX_EINVAL, "not a causal model");
+    if (lattice_k > vocab::KMAX) return set_err(ctx, SLX_EINVAL, "lattice k %d exceeds %d", lattice_k, vocab::KMAX);
     CK(cudaSetDevice(ctx->device));
     cudaStream_t st = ctx->stream;
     int32_t* d_ids = m->buf<int32_t>("ids", (size_t)B * T);
@@ -717,17 +735,29 @@ slx_status slx_causal_next_token(slx_model* m, const int32_t* ids, int B, int T,
     unsigned long long* keys = m->buf<unsigned long long>("keys", (size_t)B);
     int32_t* d_next = m->buf<int32_t>("next", (size_t)B);
     if (!d_ids || !d_last || !keys || !d_next) return set_err(ctx, SLX_EOOM, "workspace allocation failed");
+    const bool lattice = lattice_k >= 0;
+    if (lattice) {
+        if (int rc = vocab_lattice_ready(m, st)) return rc;
+        std::string err;
+        if (int rc = vocab::reserve(m->vlat, B, lattice_k, err)) return set_err(ctx, rc, "%s", err.c_str());
+    }
     CK(cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), st));
     CK(cudaMemcpyAsync(d_ids, ids, sizeof(int32_t) * B * T, cudaMemcpyHostToDevice, st));
     int rc = causal_last(m, d_ids, B, T, d_last, st);
     if (rc) return rc;
-    RUN(KC_ARGMAX, 0, 0, argmax_vocab(d_last, B, m->embd, m->tok, m->vocab, m->scale_bits, keys, d_next, st));
+    if (lattice)
+        RUN(KC_VOCAB, (double)B * m->vlat.V * m->embd, 0,
+            vocab::next_tokens(m->vlat, d_last, B, m->scale_bits, lattice_k, m->eos, d_next, st));
+    else
+        RUN(KC_ARGMAX, 0, 0, argmax_vocab(d_last, B, m->embd, m->tok, m->vocab, m->scale_bits, keys, d_next, st));
     CK(cudaMemcpyAsync(next, d_next, sizeof(int32_t) * B, cudaMemcpyDeviceToHost, st));
     return check_flag(ctx, st);
 }
 
-slx_status slx_causal_generate(slx_model* m, const int32_t* ids, int B, int T, int max_new, int32_t* out,
-                               int32_t* n_out) {
+// Generate (IntegerCausalSource.cs:86-108) on token ids for B sequences: full re-forward per step,
+// stop at EOS (not appended).
+static slx_status causal_generate(slx_model* m, const int32_t* ids, int B, int T, int max_new, int lattice_k,
+                                  int32_t* out, int32_t* n_out) {
     if (!m || !ids || !out || !n_out || B <= 0 || T <= 0 || max_new < 0)
         return m ? set_err(m->ctx, SLX_EINVAL, "bad arguments") : SLX_EINVAL;
     slx_ctx* ctx = m->ctx;
@@ -742,7 +772,7 @@ slx_status slx_causal_generate(slx_model* m, const int32_t* ids, int B, int T, i
         int alive = 0;
         for (int b = 0; b < B; b++) alive += !done[b];
         if (!alive) break;
-        int rc = slx_causal_next_token(m, seq.data(), B, cur, next.data());
+        int rc = causal_next(m, seq.data(), B, cur, lattice_k, next.data());
         if (rc) return rc;
         std::vector<int32_t> grown((size_t)B * (cur + 1));
         for (int b = 0; b < B; b++) {
@@ -755,6 +785,45 @@ slx_status slx_causal_generate(slx_model* m, const int32_t* ids, int B, int T, i
         seq.swap(grown);
         cur++;
     }
+    return SLX_OK;
+}
+
+slx_status slx_causal_next_token(slx_model* m, const int32_t* ids, int B, int T, int32_t* next) {
+    return causal_next(m, ids, B, T, -1, next);
+}
+
+slx_status slx_causal_next_token_lattice(slx_model* m, const int32_t* ids, int B, int T, int k, int32_t* next) {
+    return causal_next(m, ids, B, T, k < 0 ? 0 : k, next);
+}
+
+slx_status slx_causal_generate(slx_model* m, const int32_t* ids, int B, int T, int max_new, int32_t* out,
+                               int32_t* n_out) {
+    return causal_generate(m, ids, B, T, max_new, -1, out, n_out);
+}
+
+slx_status slx_causal_generate_lattice(slx_model* m, const int32_t* ids, int B, int T, int max_new, int k,
+                                       int32_t* out, int32_t* n_out) {
+    return causal_generate(m, ids, B, T, max_new, k < 0 ? 0 : k, out, n_out);
+}
+
+slx_status slx_vocab_lattice_query(slx_model* m, const float* hidden, int B, int k, int32_t* ids) {
+    if (!m || B < 0 || (B > 0 && k > 0 && (!hidden || !ids)))
+        return m ? set_err(m->ctx, SLX_EINVAL, "bad arguments") : SLX_EINVAL;
+    slx_ctx* ctx = m->ctx;
+    if (m->kind != SLX_MODEL_CAUSAL) return set_err(ctx, SLX_EINVAL, "not a causal model");
+    if (k > vocab::KMAX) return set_err(ctx, SLX_EINVAL, "lattice k %d exceeds %d", k, vocab::KMAX);
+    if (B == 0 || k <= 0) return SLX_OK;  // QueryKNearestL2 with k <= 0 is empty
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    if (int rc = vocab_lattice_ready(m, st)) return rc;
+    std::string err;
+    if (int rc = vocab::reserve(m->vlat, B, k, err)) return set_err(ctx, rc, "%s", err.c_str());
+    int32_t* d_ids = m->buf<int32_t>("lattice_ids", (size_t)B * k);
+    if (!d_ids) return set_err(ctx, SLX_EOOM, "workspace allocation failed");
+    CK(cudaMemcpyAsync(m->vlat.hf, hidden, sizeof(float) * (size_t)B * m->embd, cudaMemcpyHostToDevice, st));
+    RUN(KC_VOCAB, (double)B * m->vlat.V * m->embd, 0, vocab::query_topk(m->vlat, B, k, d_ids, st));
+    CK(cudaMemcpyAsync(ids, d_ids, sizeof(int32_t) * (size_t)B * k, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
     return SLX_OK;
 }
 

@@ -280,8 +280,10 @@ class CausalShape:
 
 
 def write_causal(path: str, shape: CausalShape, wtype: int = Q4_0, norm_type: int = F16, seed: int = 0,
-                 arch: str = "gemma", qk_norm: bool = True, eos: int | None = None) -> str:
+                 arch: str = "gemma", qk_norm: bool = True, eos: int | None = None,
+                 token_rows: np.ndarray | None = None) -> str:
     """Gemma-shaped causal LM: projections and token_embd as random `wtype` blocks, norms 1+N(0,0.02).
+    `token_rows` (float [vocab, embd]) replaces the random token table, stored as F16.
 
     Tensor names follow IntegerCausalSource.LoadFromReader (IntegerCausalSource.Loading.cs:74-195).
     """
@@ -317,7 +319,10 @@ def write_causal(path: str, shape: CausalShape, wtype: int = Q4_0, norm_type: in
     def norm(n):
         return 1 + rng.standard_normal(n, dtype=np.float32) * np.float32(0.02)
 
-    w.tensor_raw("token_embd.weight", (d, V), wtype, blocks(d * V))
+    if token_rows is None:
+        w.tensor_raw("token_embd.weight", (d, V), wtype, blocks(d * V))
+    else:
+        w.tensor("token_embd.weight", (d, V), F16, np.asarray(token_rows, np.float32).reshape(V * d))
     w.tensor("output_norm.weight", (d,), norm_type, norm(d))
     for i in range(shape.layers):
         p = f"blk.{i}"
