@@ -198,8 +198,70 @@ def gemma_bench(ctx, decode_b1: int = 128, decode_b16: int = 8) -> dict:
     n16 = sum(len(x) for x in g)
     res["batch16"] = {"new_tokens": int(n16), "steps": decode_b16, "s": dt, "tok_per_s": n16 / dt,
                       "note": f"first {decode_b16} of the configuration's 128 steps (context 512..{511 + decode_b16})"}
+    try:
+        res["lm_head"] = lm_head_bench(ctx, m, path, shape, p1, p16)
+    except Exception as e:  # reported, never silently dropped
+        res["lm_head"] = {"error": repr(e)}
     m.close()
     return res
+
+
+def lm_head_bench(ctx, m, path: str, shape, p1, p16, k: int = 64, reps: int = 3) -> dict:
+    """The two next-token heads of PredictNextToken on the Gemma-shaped model: the brute-force argmax
+    over all 256000 Half rows (k_argmax) and the VocabLattice head (quantized distances to every row,
+    top-k, candidate scoring; k_vocab_*), timed per call from the library's event profile around
+    `reps` next-token calls. The lattice's distance kernel streams the Half table once per eight
+    queries: its algorithmic bytes are V x d x 2 x ceil(B / 8). The CPU figure is the oracle's exact
+    k-nearest scan of one quantized hidden state over the whole quantized table (one thread)."""
+    import numpy as np
+
+    import oracle
+    from spatialdb_b200._lib import KernelStat
+
+    lib = ctx._lib
+    peaks = measured_peaks()
+
+    def classes(ids, **kw):
+        m.next_token(ids, **kw)  # warm: workspaces, the lattice table
+        lib.slx_profile_begin(ctx._h)
+        for _ in range(reps):
+            m.next_token(ids, **kw)
+        stats = (KernelStat * 16)()
+        n = ctypes_int()
+        lib.slx_profile_end(ctx._h, stats, 16, n)
+        return {s.name.decode(): s for s in stats[: n.value]}
+
+    out = {"k": k, "vocab": shape.vocab, "embd": shape.embd}
+    for name, ids in (("batch1", p1), ("batch16", p16)):
+        B = ids.shape[0]
+        a = classes(ids)["argmax"]
+        v = classes(ids, use_lattice=True, lattice_k=k)["vocab"]
+        table_bytes = shape.vocab * shape.embd * 2 * -(-B // 8)
+        ms_v = v.ms / reps
+        out[name] = {"argmax_ms": a.ms / reps, "lattice_ms": ms_v,
+                     "lattice_launches": int(v.launches // reps),
+                     "lattice_table_gbs": table_bytes / (ms_v / 1000.0) / 1e9,
+                     "lattice_table_frac_of_hbm": table_bytes / (ms_v / 1000.0) / 1e9 / peaks["hbm_gbs"]}
+    # parity at full size: QueryTopK of the prompt's last hidden state against the oracle's exact scan
+    h = m.forward_causal_float(p1[0])[None]
+    got = m.vocab_lattice_query(h, k)
+    g = oracle.Gguf(path)
+    try:
+        f = g.read_f32("token_embd.weight")
+    finally:
+        g.close()
+    table = oracle.half_to_float(oracle.float_to_half(f)).reshape(-1, shape.embd)[: shape.vocab]
+    del f
+    db = oracle.quantize_dense(table)
+    del table
+    q = oracle.quantize_dense(h)
+    t0 = time.perf_counter()
+    ids, _ = oracle.knn_l2(db, q, k)
+    cpu_s = time.perf_counter() - t0
+    out["parity_query_topk"] = bool((ids == got.astype(np.int64)).all())
+    out["cpu_baseline"] = {"value": cpu_s * 1000.0, "unit": "ms per query (k-nearest scan)", "cores": 1,
+                           "kind": "port", "sample": f"1 hidden state x {shape.vocab} quantized rows"}
+    return out
 
 
 SEARCH = dict(rows=10_000_000, dim=768, queries=10_000, k=10, centres=1024, sigma=0.1)

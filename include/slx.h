@@ -110,8 +110,9 @@ slx_status slx_causal_next_token_lattice(slx_model* model, const int32_t* ids, i
 slx_status slx_causal_generate_lattice(slx_model* model, const int32_t* ids, int B, int T, int max_new, int k,
                                        int32_t* out, int32_t* n_out);
 /* VocabLattice.QueryTopK (Lattice/VocabLattice.cs:43-58) of a causal model's lattice for B float
- * hidden states [B][embd]: ids[B][k] ascending by (distance, row), -1 past the vocabulary. */
-slx_status slx_vocab_lattice_query(slx_model* model, const float* hidden, int B, int k, int32_t* ids);
+ * hidden states [B][embd]: ids[B][k] ascending by (distance, row), -1 past the vocabulary; dist
+ * (nullable) [B][k] their DistanceSquaredL2Fast values, UINT64_MAX past the vocabulary. */
+slx_status slx_vocab_lattice_query(slx_model* model, const float* hidden, int B, int k, int32_t* ids, uint64_t* dist);
 
 /* ---- kernel-level ---------------------------------------------------------------------------- */
 /* IntegerMatMul.MatMul with GGUF weights (Math/IntegerMatMul.cs:37-76 for the long composite,

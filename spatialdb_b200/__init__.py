@@ -269,17 +269,21 @@ class IntegerCausalSource(_Model):
         self.ctx.check(rc)
         return [out[b, : n[b]].copy() for b in range(B)]
 
-    def vocab_lattice_query(self, hidden, k: int = 64) -> np.ndarray:
+    def vocab_lattice_query(self, hidden, k: int = 64, return_distances: bool = False):
         """VocabLattice.QueryTopK (Lattice/VocabLattice.cs:43-58) for float hidden states [B, embd]:
-        ids [B, k] ascending by (distance, row), -1 past the vocabulary."""
+        ids [B, k] ascending by (distance, row), -1 past the vocabulary; with return_distances also
+        their DistanceSquaredL2Fast values (uint64 [B, k], UINT64_MAX past the vocabulary)."""
         h = np.ascontiguousarray(np.atleast_2d(hidden), np.float32)
         B = h.shape[0]
         if h.shape[1] != self.embd:
             raise ValueError(f"hidden width {h.shape[1]} != embd {self.embd}")
-        out = np.full((B, max(k, 0)), -1, np.int32)
+        k = max(int(k), 0)
+        out = np.full((B, k), -1, np.int32)
+        dist = np.full((B, k), np.iinfo(np.uint64).max, np.uint64)
         if k > 0 and B > 0:
-            self.ctx.check(self.ctx._lib.slx_vocab_lattice_query(self._h, _p(h, F32P), B, int(k), _p(out, I32P)))
-        return out
+            self.ctx.check(self.ctx._lib.slx_vocab_lattice_query(self._h, _p(h, F32P), B, k, _p(out, I32P),
+                                                                 _p(dist, U64P) if return_distances else None))
+        return (out, dist) if return_distances else out
 
 
 # ---- lattice k-NN search --------------------------------------------------------------------------

@@ -42,7 +42,7 @@ SIGNATURES = {
     "slx_causal_generate": (i, [VP, I32P, i, i, i, I32P, I32P]),
     "slx_causal_next_token_lattice": (i, [VP, I32P, i, i, i, I32P]),
     "slx_causal_generate_lattice": (i, [VP, I32P, i, i, i, i, I32P, I32P]),
-    "slx_vocab_lattice_query": (i, [VP, F32P, i, i, I32P]),
+    "slx_vocab_lattice_query": (i, [VP, F32P, i, i, I32P, U64P]),
     "slx_matmul_q30": (i, [VP, I64P, i, i, i, U8P, i64, i, i, i, i, I64P]),
     "slx_matmul_q30_device": (i, [VP, VP, i, i, i, VP, i64, i, i, i, i, VP, VP]),
     "slx_matmul_q30_noalloc": (i, [VP, i, i, i, VP, i64, i, i, i, i, VP, VP]),

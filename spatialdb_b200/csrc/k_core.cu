@@ -617,35 +617,146 @@ __global__ void k_gather_last(const int64_t* __restrict__ X, int64_t ld, int T, 
 
 // VocabLattice.ArgmaxBruteForce (Lattice/VocabLattice.cs:103-126): h[j] = (float)(last[j] * 2^-s)
 // (IntegerCausalSource.ForwardCausalFloat :114-122), dot accumulated in order j = 0..d-1 with
-// separate fp32 multiply and add, strict '>' (first maximum wins, NaN never selected).
+// separate fp32 multiply and add, strict '>' (first maximum wins, NaN and -inf never selected).
+// A block owns AR vocabulary rows (one per thread) and up to AQ queries. Components stream in
+// chunks of AC: the block stages its rows' (float)(Half) values (coalesced block reads, converted
+// once for all its queries) and the queries' floats in shared memory, then every thread extends
+// its AQ independent dot chains by the chunk. Components past d are staged as zeros on both sides:
+// adding the +0 product leaves every chain unchanged (a chain that starts at +0 is never -0).
 // Candidates are combined through a 64-bit key: ordered score bits, then the inverted row id.
-constexpr int AMT = 128;
+constexpr int AR = 128, AQ = 16, AC = 64, APAD = AC + 4;
 SLX_DEV uint32_t ordered(float f) {
     uint32_t u = __float_as_uint(f);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
-__global__ __launch_bounds__(AMT) void k_argmax(const int64_t* __restrict__ last, int d, WDesc tok, int vocab,
-                                                double scale, unsigned long long* keys) {
-    extern __shared__ float hs[];
-    int b = blockIdx.y;
-    for (int j = threadIdx.x; j < d; j += AMT) hs[j] = __double2float_rn((double)last[(int64_t)b * d + j] * scale);
-    __syncthreads();
-    int v = blockIdx.x * AMT + threadIdx.x;
-    unsigned long long key = 0;
-    if (v < vocab) {
-        float dot = 0.0f;
-        int64_t base = (int64_t)v * d;
-        for (int j = 0; j < d; j++) {
-            float e = h2f(f2h(dequant_elem(tok.dtype, tok.data, base + j, tok.nblocks)));
-            dot = __fadd_rn(dot, __fmul_rn(hs[j], e));
+
+// Eight consecutive elements e0..e0+7 (e0 a multiple of 8) of a GGUF tensor as (float)(Half), with
+// the block scale read once for Q8_0 / Q4_0; elements of blocks past nblocks are 0 (dequant_elem).
+// Small integers become floats exactly by the 2^23 bias: float(2^23 + n) - (2^23 + c) = n - c.
+SLX_DEV float2 half_round2(float a, float b) { return __half22float2(__floats2half2_rn(a, b)); }
+template <int DT>
+SLX_DEV void dequant8_half(const uint8_t* __restrict__ base, int64_t e0, int64_t nblocks, float* out) {
+    if constexpr (DT == DT_Q4_0 || DT == DT_Q8_0) {
+        const int64_t b = e0 >> 5;
+        if (b >= nblocks) {
+#pragma unroll
+            for (int t = 0; t < 8; t++) out[t] = 0.0f;
+            return;
         }
-        if (dot > -INFINITY) key = ((unsigned long long)ordered(dot) << 32) | (0xFFFFFFFFu - (uint32_t)v);
+        if constexpr (DT == DT_Q4_0) {
+            const uint8_t* blk = base + b * 18;
+            const float sc = h2f(ld_u16(blk));
+            const uint16_t* q = (const uint16_t*)(blk + 2 + ((e0 & 31) >> 1));  // element 2j: low nibble of byte j
+            const uint32_t w = (uint32_t)q[0] | ((uint32_t)q[1] << 16);
+#pragma unroll
+            for (int t = 0; t < 8; t += 2) {
+                const float x0 = __fsub_rn(__uint_as_float(0x4B000000u | ((w >> (4 * t)) & 15u)), 8388616.0f);
+                const float x1 = __fsub_rn(__uint_as_float(0x4B000000u | ((w >> (4 * t + 4)) & 15u)), 8388616.0f);
+                const float2 r = half_round2(__fmul_rn(sc, x0), __fmul_rn(sc, x1));
+                out[t] = r.x;
+                out[t + 1] = r.y;
+            }
+        } else {
+            const uint8_t* blk = base + b * 34;
+            const float sc = h2f(ld_u16(blk));
+            const uint16_t* q = (const uint16_t*)(blk + 2 + (e0 & 31));
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const uint32_t pr = q[t];
+                const float x0 = __fsub_rn(__uint_as_float(0x4B000000u | ((pr & 0xFFu) ^ 0x80u)), 8388736.0f);
+                const float x1 = __fsub_rn(__uint_as_float(0x4B000000u | ((pr >> 8) ^ 0x80u)), 8388736.0f);
+                const float2 r = half_round2(__fmul_rn(sc, x0), __fmul_rn(sc, x1));
+                out[2 * t] = r.x;
+                out[2 * t + 1] = r.y;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int t = 0; t < 8; t++) out[t] = h2f(f2h(dequant_elem(DT, base, e0 + t, nblocks)));
     }
-    for (int o = 16; o > 0; o >>= 1) {
-        unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
-        key = k2 > key ? k2 : key;
+}
+
+// NQ queries per block (B rounded up to a power of two, at most AQ): every thread extends NQ
+// independent chains per component, so the adds of different queries interleave.
+template <int DT, int NQ>
+__global__ __launch_bounds__(AR) void k_argmax(const int64_t* __restrict__ last, int B, int d, WDesc tok, int vocab,
+                                               double scale, unsigned long long* keys) {
+    __shared__ __align__(16) float rows[AR][APAD];
+    __shared__ __align__(16) float hs[NQ][AC];
+    const int tid = threadIdx.x;
+    const int64_t v0 = (int64_t)blockIdx.x * AR;
+    const int q0 = blockIdx.y * NQ;
+    const int nq = min(NQ, B - q0);
+    const bool whole = (d & 7) == 0;  // 8-element groups never straddle a row
+    float acc[NQ];
+#pragma unroll
+    for (int b = 0; b < NQ; b++) acc[b] = 0.0f;
+    for (int j0 = 0; j0 < d; j0 += AC) {
+        // thread t stages 8-element groups t, t + AR, ... of the [AR][AC] tile (row g / 8, column 8 (g % 8))
+#pragma unroll 4
+        for (int g = tid; g < AR * AC / 8; g += AR) {
+            const int r = g >> 3, c = (g & 7) * 8;
+            float e[8];
+            if (v0 + r < vocab && j0 + c + 8 <= d && whole) {
+                dequant8_half<DT>(tok.data, (v0 + r) * d + j0 + c, tok.nblocks, e);
+            } else {
+#pragma unroll
+                for (int t = 0; t < 8; t++)
+                    e[t] = (v0 + r < vocab && j0 + c + t < d)
+                               ? h2f(f2h(dequant_elem(DT, tok.data, (v0 + r) * d + j0 + c + t, tok.nblocks)))
+                               : 0.0f;
+            }
+            *reinterpret_cast<float4*>(&rows[r][c]) = make_float4(e[0], e[1], e[2], e[3]);
+            *reinterpret_cast<float4*>(&rows[r][c + 4]) = make_float4(e[4], e[5], e[6], e[7]);
+        }
+        for (int idx = tid; idx < NQ * AC; idx += AR) {
+            const int b = idx / AC, c = idx % AC;
+            float h = 0.0f;
+            if (b < nq && j0 + c < d) h = __double2float_rn((double)last[(int64_t)(q0 + b) * d + j0 + c] * scale);
+            hs[b][c] = h;
+        }
+        __syncthreads();
+#pragma unroll 2
+        for (int c = 0; c < AC; c += 4) {
+            const float4 e = *reinterpret_cast<const float4*>(&rows[tid][c]);
+#pragma unroll
+            for (int b = 0; b < NQ; b++) {
+                const float4 h = *reinterpret_cast<const float4*>(&hs[b][c]);
+                float a = acc[b];
+                a = __fadd_rn(a, __fmul_rn(h.x, e.x));
+                a = __fadd_rn(a, __fmul_rn(h.y, e.y));
+                a = __fadd_rn(a, __fmul_rn(h.z, e.z));
+                a = __fadd_rn(a, __fmul_rn(h.w, e.w));
+                acc[b] = a;
+            }
+        }
+        __syncthreads();
     }
-    if ((threadIdx.x & 31) == 0 && key) atomicMax(keys + b, key);
+    const int64_t v = v0 + tid;
+#pragma unroll
+    for (int b = 0; b < NQ; b++) {
+        if (b < nq) {
+            unsigned long long key = 0;
+            if (v < vocab && acc[b] > -INFINITY)
+                key = ((unsigned long long)ordered(acc[b]) << 32) | (0xFFFFFFFFu - (uint32_t)v);
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                key = k2 > key ? k2 : key;
+            }
+            if ((tid & 31) == 0 && key) atomicMax(keys + q0 + b, key);
+        }
+    }
+}
+
+template <int DT>
+void launch_argmax(const int64_t* last, int B, int d, const WDesc& tok, int vocab, double sc, unsigned long long* keys,
+                   cudaStream_t st) {
+    const unsigned gx = (unsigned)((vocab + AR - 1) / AR);
+    if (B == 1) k_argmax<DT, 1><<<dim3(gx, 1), AR, 0, st>>>(last, B, d, tok, vocab, sc, keys);
+    else if (B == 2) k_argmax<DT, 2><<<dim3(gx, 1), AR, 0, st>>>(last, B, d, tok, vocab, sc, keys);
+    else if (B <= 4) k_argmax<DT, 4><<<dim3(gx, 1), AR, 0, st>>>(last, B, d, tok, vocab, sc, keys);
+    else if (B <= 8) k_argmax<DT, 8><<<dim3(gx, 1), AR, 0, st>>>(last, B, d, tok, vocab, sc, keys);
+    else k_argmax<DT, AQ><<<dim3(gx, (unsigned)((B + AQ - 1) / AQ)), AR, 0, st>>>(last, B, d, tok, vocab, sc, keys);
 }
 
 __global__ void k_keys_to_ids(const unsigned long long* keys, int B, int32_t* ids) {
@@ -681,20 +792,20 @@ int gather_last_rows(const int64_t* x, int64_t ld, int B, int T, int d, int64_t*
 }
 
 int argmax_vocab(const int64_t* last, int B, int d, const WDesc& tok, int vocab, int scale_bits,
-                  unsigned long long* keys, int32_t* ids, cudaStream_t st) {
+                 unsigned long long* keys, int32_t* ids, cudaStream_t st) {
     if (B <= 0) return 0;
     int64_t rows = tok.elements / d;
     if (vocab > rows) vocab = (int)rows;
     cudaMemsetAsync(keys, 0, sizeof(unsigned long long) * B, st);
-    size_t smem = (size_t)d * sizeof(float);
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-        cudaFuncSetAttribute(k_argmax, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured = smem;
-    }
     if (vocab > 0) {
-        dim3 grid((unsigned)((vocab + AMT - 1) / AMT), (unsigned)B);
-        k_argmax<<<grid, AMT, smem, st>>>(last, d, tok, vocab, ldexp(1.0, -scale_bits), keys);
+        const double sc = ldexp(1.0, -scale_bits);
+        switch (tok.dtype) {
+            case DT_Q4_0: launch_argmax<DT_Q4_0>(last, B, d, tok, vocab, sc, keys, st); break;
+            case DT_Q8_0: launch_argmax<DT_Q8_0>(last, B, d, tok, vocab, sc, keys, st); break;
+            case DT_F16: launch_argmax<DT_F16>(last, B, d, tok, vocab, sc, keys, st); break;
+            case DT_BF16: launch_argmax<DT_BF16>(last, B, d, tok, vocab, sc, keys, st); break;
+            default: launch_argmax<DT_F32>(last, B, d, tok, vocab, sc, keys, st); break;
+        }
     }
     k_keys_to_ids<<<(B + 127) / 128, 128, 0, st>>>(keys, B, ids);
     return 1 + (vocab > 0 ? 1 : 0);

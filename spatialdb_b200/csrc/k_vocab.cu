@@ -38,6 +38,22 @@ constexpr double GLOBAL_SCALE = 1e9;
 // |f| < ZeroThreshold -> 0, else (long)(f * (double)GlobalScale). The double product is exact.
 SLX_DEV int64_t quantize(float f) { return fabsf(f) < ZERO_THRESHOLD ? 0 : cs_d2l((double)f * GLOBAL_SCALE); }
 
+// The same for a Half component, in integer arithmetic. A finite Half of magnitude >= 2^-14 is
+// M * 2^(E-25) (M = 1024 + fraction, E the exponent field), so f * 1e9 = M * 1953125 * 2^(E-16)
+// exactly (1e9 = 1953125 * 2^9), and (long) truncates the magnitude: a shift of M * 1953125 (< 2^32).
+// 0x1419 is the smallest Half magnitude that is not below 0.001f; inf and NaN give long.MinValue
+// as (long) of a non-finite double does.
+constexpr uint32_t HALF_MAG_ZERO_BELOW = 0x1419u;
+SLX_DEV int64_t quantize_half(uint32_t bits) {
+    const uint32_t mag = bits & 0x7fffu;
+    if (mag < HALF_MAG_ZERO_BELOW) return 0;
+    if (mag >= 0x7c00u) return INT64_MIN;
+    const uint32_t e = mag >> 10;
+    const uint64_t p = (uint64_t)(1024u | (mag & 1023u)) * 1953125u;
+    const int64_t q = (int64_t)(e >= 16 ? p << (e - 16) : p >> (16 - e));
+    return (bits & 0x8000u) ? -q : q;
+}
+
 __global__ void k_vocab_table(WDesc tok, int64_t total, uint16_t* __restrict__ table) {
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x)
         table[e] = f2h(dequant_elem(tok.dtype, tok.data, e, tok.nblocks));
@@ -77,16 +93,25 @@ __global__ void k_vocab_norms(const int64_t* __restrict__ hq, int B, int d, uint
 }
 
 // dist[q0+i][v] for the g <= DG queries q0.. staged in shared memory: each warp takes two vocabulary
-// rows at a time, lanes stride the components (coalesced Half loads, conflict-free int64 shared reads).
+// rows at a time. With d a multiple of 8 (VEC) every lane loads eight Half components of each row
+// per step (16-byte loads) and the queries are staged component-group-major, sh[i][t][j / 8] for
+// component j = 8 (j / 8) + t, so the lanes' int64 reads stay contiguous; otherwise lanes stride
+// single components.
 constexpr int DG = 8;
-constexpr int DWARPS = 8;
+constexpr int DWARPS = 16;
 constexpr int SMEM_CAP = 200 * 1024;
+template <bool VEC>
 __global__ void __launch_bounds__(DWARPS * 32) k_vocab_dist(const uint16_t* __restrict__ table, int64_t V, int d,
                                                             const int64_t* __restrict__ hq,
                                                             const uint64_t* __restrict__ hn, int q0, int g,
                                                             uint64_t* __restrict__ dist) {
     extern __shared__ int64_t sh[];  // [g][d]
-    for (int64_t i = threadIdx.x; i < (int64_t)g * d; i += blockDim.x) sh[i] = hq[(int64_t)q0 * d + i];
+    const int d8 = d >> 3;
+    for (int64_t idx = threadIdx.x; idx < (int64_t)g * d; idx += blockDim.x) {
+        const int64_t i = idx / d;
+        const int j = (int)(idx - i * d);
+        sh[VEC ? i * d + (int64_t)(j & 7) * d8 + (j >> 3) : idx] = hq[(int64_t)q0 * d + idx];
+    }
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int64_t v0 = ((int64_t)blockIdx.x * DWARPS + warp) * 2; v0 < V; v0 += (int64_t)gridDim.x * DWARPS * 2) {
@@ -96,17 +121,42 @@ __global__ void __launch_bounds__(DWARPS * 32) k_vocab_dist(const uint16_t* __re
         uint64_t na = 0, nb = 0, a[DG], b[DG];
 #pragma unroll
         for (int i = 0; i < DG; i++) a[i] = b[i] = 0;
-        for (int j = lane; j < d; j += 32) {
-            const uint64_t ea = (uint64_t)quantize(h2f(r0[j]));
-            const uint64_t eb = (uint64_t)quantize(h2f(r1[j]));
-            na += ea * ea;
-            nb += eb * eb;
+        if constexpr (VEC) {
+            const uint4* R0 = reinterpret_cast<const uint4*>(r0);
+            const uint4* R1 = reinterpret_cast<const uint4*>(r1);
+#pragma unroll 1
+            for (int cb = lane; cb < d8; cb += 32) {
+                const uint4 x0 = __ldg(R0 + cb), x1 = __ldg(R1 + cb);
+                const uint32_t w0[4] = {x0.x, x0.y, x0.z, x0.w}, w1[4] = {x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-            for (int i = 0; i < DG; i++) {
-                if (i < g) {
-                    const uint64_t h = (uint64_t)sh[i * d + j];
-                    a[i] += h * ea;
-                    b[i] += h * eb;
+                for (int t = 0; t < 8; t++) {
+                    const uint64_t ea = (uint64_t)quantize_half((w0[t >> 1] >> (16 * (t & 1))) & 0xFFFFu);
+                    const uint64_t eb = (uint64_t)quantize_half((w1[t >> 1] >> (16 * (t & 1))) & 0xFFFFu);
+                    na += ea * ea;
+                    nb += eb * eb;
+#pragma unroll
+                    for (int i = 0; i < DG; i++) {
+                        if (i < g) {
+                            const uint64_t h = (uint64_t)sh[(int64_t)i * d + t * d8 + cb];
+                            a[i] += h * ea;
+                            b[i] += h * eb;
+                        }
+                    }
+                }
+            }
+        } else {
+            for (int j = lane; j < d; j += 32) {
+                const uint64_t ea = (uint64_t)quantize_half(r0[j]);
+                const uint64_t eb = (uint64_t)quantize_half(r1[j]);
+                na += ea * ea;
+                nb += eb * eb;
+#pragma unroll
+                for (int i = 0; i < DG; i++) {
+                    if (i < g) {
+                        const uint64_t h = (uint64_t)sh[i * d + j];
+                        a[i] += h * ea;
+                        b[i] += h * eb;
+                    }
                 }
             }
         }
@@ -130,67 +180,233 @@ __global__ void __launch_bounds__(DWARPS * 32) k_vocab_dist(const uint16_t* __re
     }
 }
 
-// The k smallest (distance, row) of dist[b][0..V) in ascending order, one block per query: an MSB-first
-// radix select over the eight distance bytes finds the k-th smallest distance D; every row below D is
-// gathered, rows equal to D are taken in ascending row order until there are k, and a bitonic sort
-// orders the pairs. Requires 1 <= k <= min(V, KMAX).
+// ---- top-k selection --------------------------------------------------------------------------
+// The k smallest (distance, row) pairs of a query, ties by ascending row: a radix select finds the
+// k-th smallest distance D, every row below D is kept, and rows equal to D are kept in ascending row
+// order until there are k. The select starts at the highest byte in which the candidates' minimum and
+// maximum differ (the bytes above are common to all of them) and each warp adds its lanes' equal bins
+// once (__match_any_sync), since distances crowd into few bins.
+//
+// Stage 1 (k_topk_slice, k <= SLICE / 4): one block per (slice of SLICE rows, query) holds the slice's
+// distances in shared memory, selects its min(k, rows) smallest and writes them in ascending row
+// order, padding its KK = min(k, SLICE) slots with (UINT64_MAX, -) marked by id INT32_MAX. Stage 2
+// (k_topk_merge) selects the k smallest of those candidates (or of all rows when k is large) and sorts
+// them; its candidates are already in ascending row order, so equal distances are taken by row.
+constexpr int SLICE = 2048, ST1 = 256;
 constexpr int TK = 1024;
-__global__ void __launch_bounds__(TK) k_vocab_topk(const uint64_t* __restrict__ dist, int64_t V, int k,
-                                                   int32_t* __restrict__ out) {
-    extern __shared__ uint64_t key_d[];  // [n2], then int32 key_i[n2]
-    __shared__ unsigned int hist[256];
-    __shared__ int warp_cnt[TK / 32];
-    __shared__ uint64_t s_prefix;
-    __shared__ int s_remaining, s_count, s_eq_taken;
-    int n2 = 1;
-    while (n2 < k) n2 <<= 1;
-    int32_t* key_i = (int32_t*)(key_d + n2);
-    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint64_t* row = dist + (int64_t)b * V;
-    if (tid == 0) {
-        s_prefix = 0;
-        s_remaining = k;
-        s_count = 0;
-        s_eq_taken = 0;
+constexpr int32_t NO_ROW = INT32_MAX;
+
+// Exclusive prefix sum over the block's threads (warp_sums holds one int per warp); returns the
+// exclusive prefix and stores the block total in *total.
+template <int NT>
+SLX_DEV int block_exclusive_scan(int v, int* warp_sums, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
     }
-    for (int pass = 7; pass >= 0; pass--) {
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    int before = 0, all = 0;
+    for (int w = 0; w < NT / 32; w++) {
+        const int c = warp_sums[w];
+        before += w < warp ? c : 0;
+        all += c;
+    }
+    __syncthreads();
+    *total = all;
+    return before + x - v;
+}
+
+// Radix select over n values (shared or global, generic addressing) with a validity predicate:
+// returns D (the k-th smallest valid value) and *need_eq (how many values equal to D belong to the k).
+template <int NT, class Get>
+SLX_DEV uint64_t radix_select(int64_t n, int k, Get get, unsigned* hist, uint64_t* wmin, uint64_t* wmax,
+                              uint64_t* s_prefix, int* s_remaining, int* s_top, int* need_eq) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint64_t mn = UINT64_MAX, mx = 0;
+    for (int64_t i = tid; i < n; i += NT) {
+        bool ok;
+        const uint64_t x = get(i, ok);
+        if (ok) {
+            mn = x < mn ? x : mn;
+            mx = x > mx ? x : mx;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t a = __shfl_xor_sync(0xffffffffu, (unsigned long long)mn, o);
+        const uint64_t c = __shfl_xor_sync(0xffffffffu, (unsigned long long)mx, o);
+        mn = a < mn ? a : mn;
+        mx = c > mx ? c : mx;
+    }
+    if (lane == 0) {
+        wmin[warp] = mn;
+        wmax[warp] = mx;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < NT / 32; w++) {
+            mn = wmin[w] < mn ? wmin[w] : mn;
+            mx = wmax[w] > mx ? wmax[w] : mx;
+        }
+        const uint64_t diff = mn ^ mx;
+        *s_top = diff ? (63 - __clzll((long long)diff)) >> 3 : -1;
+        *s_prefix = *s_top < 0 ? mn : (*s_top == 7 ? 0 : mn & (~0ull << (8 * (*s_top + 1))));
+        *s_remaining = k;
+    }
+    __syncthreads();
+    for (int pass = *s_top; pass >= 0; pass--) {
         if (tid < 256) hist[tid] = 0;
         __syncthreads();
-        const uint64_t prefix = s_prefix;
+        const uint64_t prefix = *s_prefix;
         const uint64_t hi_mask = pass == 7 ? 0 : ~0ull << (8 * (pass + 1));
-        for (int64_t v = tid; v < V; v += TK) {
-            const uint64_t x = row[v];
-            if ((x & hi_mask) == prefix) atomicAdd(&hist[(x >> (8 * pass)) & 255], 1u);
+        for (int64_t i0 = 0; i0 < n; i0 += NT) {
+            const int64_t i = i0 + tid;
+            unsigned bin = 256;
+            if (i < n) {
+                bool ok;
+                const uint64_t x = get(i, ok);
+                if (ok && (x & hi_mask) == prefix) bin = (unsigned)(x >> (8 * pass)) & 255u;
+            }
+            const unsigned same = __match_any_sync(0xffffffffu, bin);
+            if (bin < 256 && lane == __ffs(same) - 1) atomicAdd(&hist[bin], (unsigned)__popc(same));
         }
         __syncthreads();
         if (tid == 0) {
             unsigned int below = 0;
             int bin = 0;
             for (; bin < 255; bin++) {
-                if (below + hist[bin] >= (unsigned)s_remaining) break;
+                if (below + hist[bin] >= (unsigned)*s_remaining) break;
                 below += hist[bin];
             }
-            s_prefix = prefix | ((uint64_t)bin << (8 * pass));
-            s_remaining -= (int)below;
+            *s_prefix = prefix | ((uint64_t)bin << (8 * pass));
+            *s_remaining -= (int)below;
         }
         __syncthreads();
     }
-    const uint64_t D = s_prefix;  // the k-th smallest distance
-    const int need_eq = s_remaining;
-    for (int64_t v = tid; v < V; v += TK) {
-        const uint64_t x = row[v];
-        if (x < D) {
+    *need_eq = *s_remaining;
+    return *s_prefix;
+}
+
+__global__ void __launch_bounds__(ST1) k_topk_slice(const uint64_t* __restrict__ dist, int64_t V, int k, int G, int KK,
+                                                    uint64_t* __restrict__ cd, int32_t* __restrict__ ci) {
+    __shared__ uint64_t xs[SLICE];
+    __shared__ unsigned hist[256];
+    __shared__ uint64_t wmin[ST1 / 32], wmax[ST1 / 32], s_prefix;
+    __shared__ int wsum[ST1 / 32], s_remaining, s_top;
+    const int s = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int64_t r0 = (int64_t)s * SLICE;
+    const int n = (int)(V - r0 < SLICE ? V - r0 : SLICE);
+    const int kk = k < n ? k : n;
+    const uint64_t* row = dist + (int64_t)b * V + r0;
+    for (int i = tid; i < SLICE; i += ST1) xs[i] = i < n ? row[i] : UINT64_MAX;
+    __syncthreads();
+    int need_eq;
+    const uint64_t D = radix_select<ST1>(
+        n, kk, [&](int64_t i, bool& ok) { ok = true; return xs[i]; }, hist, wmin, wmax, &s_prefix, &s_remaining, &s_top,
+        &need_eq);
+    // thread t owns rows 8t .. 8t+7 of the slice: both scans keep row order
+    constexpr int PER = SLICE / ST1;
+    int eqc = 0;
+#pragma unroll
+    for (int u = 0; u < PER; u++) {
+        const int i = tid * PER + u;
+        eqc += (i < n && xs[i] == D) ? 1 : 0;
+    }
+    int tot;
+    int eq_rank = block_exclusive_scan<ST1>(eqc, wsum, &tot);
+    bool sel[PER];
+    int selc = 0;
+#pragma unroll
+    for (int u = 0; u < PER; u++) {
+        const int i = tid * PER + u;
+        const uint64_t x = xs[i];
+        bool t = false;
+        if (i < n) {
+            if (x < D) t = true;
+            else if (x == D) t = eq_rank++ < need_eq;
+        }
+        sel[u] = t;
+        selc += t;
+    }
+    int pos = block_exclusive_scan<ST1>(selc, wsum, &tot);
+    uint64_t* od = cd + ((int64_t)b * G + s) * KK;
+    int32_t* oi = ci + ((int64_t)b * G + s) * KK;
+#pragma unroll
+    for (int u = 0; u < PER; u++) {
+        if (sel[u]) {
+            const int i = tid * PER + u;
+            od[pos] = xs[i];
+            oi[pos] = (int32_t)(r0 + i);
+            pos++;
+        }
+    }
+    for (int p = kk + tid; p < KK; p += ST1) {
+        od[p] = UINT64_MAX;
+        oi[p] = NO_ROW;
+    }
+}
+
+// Stage 2: the k smallest of n candidates per query (vals[b][0..n), ids[b][0..n) or the index when
+// ids is null; id NO_ROW marks an empty slot), sorted by (distance, row). The candidates are staged
+// in shared memory when they fit. Requires 1 <= k <= valid candidates, k <= KMAX.
+__global__ void __launch_bounds__(TK) k_topk_merge(const uint64_t* __restrict__ vals, const int32_t* __restrict__ ids,
+                                                   int64_t n, int k, int staged, int32_t* __restrict__ out,
+                                                   uint64_t* __restrict__ out_d) {
+    extern __shared__ uint64_t dyn[];  // key_d[n2], key_i[n2], then (staged) sv[n], si[n]
+    __shared__ unsigned hist[256];
+    __shared__ int warp_cnt[TK / 32];
+    __shared__ uint64_t wmin[TK / 32], wmax[TK / 32], s_prefix;
+    __shared__ int s_remaining, s_count, s_eq_taken, s_top;
+    int n2 = 1;
+    while (n2 < k) n2 <<= 1;
+    uint64_t* key_d = dyn;
+    int32_t* key_i = (int32_t*)(key_d + n2);
+    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint64_t* row = vals + (int64_t)b * n;
+    const int32_t* irow = ids ? ids + (int64_t)b * n : nullptr;
+    if (staged) {
+        uint64_t* sv = (uint64_t*)(key_i + n2 + (n2 & 1));  // 8-byte aligned after key_i
+        int32_t* si = (int32_t*)(sv + n);
+        for (int64_t i = tid; i < n; i += TK) {
+            sv[i] = row[i];
+            si[i] = irow ? irow[i] : (int32_t)i;
+        }
+        row = sv;
+        irow = si;
+        __syncthreads();
+    }
+    if (tid == 0) {
+        s_count = 0;
+        s_eq_taken = 0;
+    }
+    auto get = [&](int64_t i, bool& ok) {
+        ok = !irow || irow[i] != NO_ROW;
+        return row[i];
+    };
+    int need_eq;
+    const uint64_t D = radix_select<TK>(n, k, get, hist, wmin, wmax, &s_prefix, &s_remaining, &s_top, &need_eq);
+    for (int64_t i = tid; i < n; i += TK) {
+        bool ok;
+        const uint64_t x = get(i, ok);
+        if (ok && x < D) {
             const int p = atomicAdd(&s_count, 1);
             key_d[p] = x;
-            key_i[p] = (int32_t)v;
+            key_i[p] = irow ? irow[i] : (int32_t)i;
         }
     }
     __syncthreads();
     const int base = s_count;  // = k - need_eq
-    for (int64_t v0 = 0; v0 < V; v0 += TK) {
+    for (int64_t i0 = 0; i0 < n; i0 += TK) {
         if (s_eq_taken >= need_eq) break;  // uniform: read after a barrier
-        const int64_t v = v0 + tid;
-        const bool f = v < V && row[v] == D;
+        const int64_t i = i0 + tid;
+        bool f = false;
+        if (i < n) {
+            bool ok;
+            const uint64_t x = get(i, ok);
+            f = ok && x == D;
+        }
         const unsigned m = __ballot_sync(0xffffffffu, f);
         if (lane == 0) warp_cnt[warp] = __popc(m);
         __syncthreads();
@@ -198,7 +414,7 @@ __global__ void __launch_bounds__(TK) k_vocab_topk(const uint64_t* __restrict__ 
         for (int w = 0; w < warp; w++) off += warp_cnt[w];
         if (f && off < need_eq) {
             key_d[base + off] = D;
-            key_i[base + off] = (int32_t)v;
+            key_i[base + off] = irow ? irow[i] : (int32_t)i;
         }
         __syncthreads();
         if (tid == 0) {
@@ -233,7 +449,10 @@ __global__ void __launch_bounds__(TK) k_vocab_topk(const uint64_t* __restrict__ 
             __syncthreads();
         }
     }
-    for (int i = tid; i < k; i += TK) out[(int64_t)b * k + i] = key_i[i];
+    for (int i = tid; i < k; i += TK) {
+        out[(int64_t)b * k + i] = key_i[i];
+        if (out_d) out_d[(int64_t)b * k + i] = key_d[i];
+    }
 }
 
 // ScoreCandidates (Lattice/VocabLattice.cs:60-76) and the first entry of its descending sort, one block
@@ -294,44 +513,69 @@ int sm_count() {
     return n;
 }
 
+// Stage-1 candidate slots per query: KK = k per slice of SLICE rows.
+size_t slice_slots(int64_t V, int k) {
+    if (k <= 0 || k > SLICE / 4 || V <= SLICE) return 1;
+    return (size_t)((V + SLICE - 1) / SLICE) * (size_t)k;
+}
+
 int queries_per_pass(int d) {
     int g = SMEM_CAP / (8 * d);
     return g < DG ? g : DG;
 }
 
 // Norms, distances and the radix select for the B queries quantized in L.hq; k in [1, V].
-int candidates(Lattice& L, int B, int k, cudaStream_t st) {
+int candidates(Lattice& L, int B, int k, bool want_dist, cudaStream_t st) {
     int n = 0;
     k_vocab_norms<<<(unsigned)((B + 7) / 8), 256, 0, st>>>(L.hq, B, L.d, L.hn);
     n++;
     const int gmax = queries_per_pass(L.d);
-    static int configured = 0;
+    const bool vec = (L.d & 7) == 0;
+    const void* fn = vec ? (const void*)k_vocab_dist<true> : (const void*)k_vocab_dist<false>;
+    static int configured[2] = {0, 0};
     const int smem_max = gmax * L.d * 8;
-    if (smem_max > 48 * 1024 && smem_max > configured) {
-        cudaFuncSetAttribute(k_vocab_dist, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max);
-        configured = smem_max;
+    if (smem_max > 48 * 1024 && smem_max > configured[vec]) {
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max);
+        configured[vec] = smem_max;
     }
     for (int q0 = 0; q0 < B; q0 += gmax) {
         const int g = B - q0 < gmax ? B - q0 : gmax;
         const int smem = g * L.d * 8;
         int per_sm = 1;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_vocab_dist, DWARPS * 32, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, DWARPS * 32, smem);
         if (per_sm < 1) per_sm = 1;
         const int64_t want = (L.V + DWARPS * 2 - 1) / (DWARPS * 2);
         const int64_t cap = (int64_t)sm_count() * per_sm;
-        k_vocab_dist<<<(unsigned)(want < cap ? want : cap), DWARPS * 32, smem, st>>>(L.table, L.V, L.d, L.hq, L.hn, q0,
-                                                                                    g, L.dist);
+        const unsigned grid = (unsigned)(want < cap ? want : cap);
+        if (vec)
+            k_vocab_dist<true><<<grid, DWARPS * 32, smem, st>>>(L.table, L.V, L.d, L.hq, L.hn, q0, g, L.dist);
+        else
+            k_vocab_dist<false><<<grid, DWARPS * 32, smem, st>>>(L.table, L.V, L.d, L.hq, L.hn, q0, g, L.dist);
         n++;
     }
     int n2 = 1;
     while (n2 < k) n2 <<= 1;
-    const int tsmem = n2 * 12;
-    static int tconfigured = 0;
-    if (tsmem > 48 * 1024 && tsmem > tconfigured) {
-        cudaFuncSetAttribute(k_vocab_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, tsmem);
-        tconfigured = tsmem;
+    const uint64_t* vals = L.dist;
+    const int32_t* ids = nullptr;
+    int64_t n_cand = L.V;
+    if (k <= SLICE / 4 && L.V > SLICE) {
+        const int G = (int)((L.V + SLICE - 1) / SLICE), KK = k;
+        k_topk_slice<<<dim3((unsigned)G, (unsigned)B), ST1, 0, st>>>(L.dist, L.V, k, G, KK, L.sel_d, L.sel_i);
+        n++;
+        vals = L.sel_d;
+        ids = L.sel_i;
+        n_cand = (int64_t)G * KK;
     }
-    k_vocab_topk<<<(unsigned)B, TK, tsmem, st>>>(L.dist, L.V, k, L.cand);
+    const size_t keys = (size_t)n2 * 12 + 8;
+    const size_t stage = (size_t)n_cand * 12;
+    const int staged = keys + stage <= 160 * 1024 ? 1 : 0;
+    const int tsmem = (int)(keys + (staged ? stage : 0));
+    static bool tconfigured = false;  // the largest request is 160 KiB (staged); unstaged <= KMAX * 12 + 8
+    if (tsmem > 48 * 1024 && !tconfigured) {
+        cudaFuncSetAttribute(k_topk_merge, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        tconfigured = true;
+    }
+    k_topk_merge<<<(unsigned)B, TK, tsmem, st>>>(vals, ids, n_cand, k, staged, L.cand, want_dist ? L.cdist : nullptr);
     return n + 1;
 }
 }  // namespace
@@ -366,7 +610,8 @@ int build(const WDesc& tok, int64_t vocab, int d, Lattice& L, cudaStream_t st, s
 }
 
 void release(Lattice& L) {
-    for (void* p : {(void*)L.table, (void*)L.hq, (void*)L.hf, (void*)L.hn, (void*)L.dist, (void*)L.cand})
+    for (void* p : {(void*)L.table, (void*)L.hq, (void*)L.hf, (void*)L.hn, (void*)L.dist, (void*)L.cand, (void*)L.cdist,
+                    (void*)L.sel_d, (void*)L.sel_i})
         if (p) cudaFree(p);
     L = Lattice();
 }
@@ -377,14 +622,17 @@ int reserve(Lattice& L, int B, int k, std::string& err) {
         !grow((void**)&L.hf, L.hf_bytes, sizeof(float) * (size_t)B * L.d) ||
         !grow((void**)&L.hn, L.hn_bytes, sizeof(uint64_t) * (size_t)B) ||
         !grow((void**)&L.dist, L.dist_bytes, sizeof(uint64_t) * (size_t)B * (size_t)L.V) ||
-        !grow((void**)&L.cand, L.cand_bytes, sizeof(int32_t) * (size_t)B * kc)) {
+        !grow((void**)&L.cand, L.cand_bytes, sizeof(int32_t) * (size_t)B * kc) ||
+        !grow((void**)&L.cdist, L.cdist_bytes, sizeof(uint64_t) * (size_t)B * kc) ||
+        !grow((void**)&L.sel_d, L.sel_d_bytes, sizeof(uint64_t) * (size_t)B * slice_slots(L.V, k)) ||
+        !grow((void**)&L.sel_i, L.sel_i_bytes, sizeof(int32_t) * (size_t)B * slice_slots(L.V, k))) {
         err = "vocab lattice: device allocation failed";
         return SLX_EOOM;
     }
     return SLX_OK;
 }
 
-int query_topk(Lattice& L, int B, int k, int32_t* d_ids, cudaStream_t st) {
+int query_topk(Lattice& L, int B, int k, int32_t* d_ids, uint64_t* d_dist, cudaStream_t st) {
     if (B <= 0 || k <= 0) return 0;
     const int keff = (int64_t)k > L.V ? (int)L.V : k;
     const int64_t total = (int64_t)B * L.d;
@@ -394,13 +642,20 @@ int query_topk(Lattice& L, int B, int k, int32_t* d_ids, cudaStream_t st) {
         n++;
     }
     if (keff > 0) {
-        n += candidates(L, B, keff, st);
+        n += candidates(L, B, keff, d_dist != nullptr, st);
         cudaMemcpy2DAsync(d_ids, sizeof(int32_t) * k, L.cand, sizeof(int32_t) * keff, sizeof(int32_t) * keff, B,
                           cudaMemcpyDeviceToDevice, st);
+        if (d_dist)
+            cudaMemcpy2DAsync(d_dist, sizeof(uint64_t) * k, L.cdist, sizeof(uint64_t) * keff, sizeof(uint64_t) * keff, B,
+                              cudaMemcpyDeviceToDevice, st);
     }
-    if (k > keff)  // past the vocabulary: id -1
+    if (k > keff) {  // past the vocabulary: id -1, distance UINT64_MAX
         cudaMemset2DAsync((uint8_t*)d_ids + sizeof(int32_t) * keff, sizeof(int32_t) * k, 0xFF,
                           sizeof(int32_t) * (k - keff), B, st);
+        if (d_dist)
+            cudaMemset2DAsync((uint8_t*)d_dist + sizeof(uint64_t) * keff, sizeof(uint64_t) * k, 0xFF,
+                              sizeof(uint64_t) * (k - keff), B, st);
+    }
     return n;
 }
 
@@ -415,7 +670,7 @@ int next_tokens(Lattice& L, const int64_t* d_last, int B, int scale_bits, int k,
                                                                       L.hq);
         n++;
     }
-    if (keff > 0) n += candidates(L, B, keff, st);
+    if (keff > 0) n += candidates(L, B, keff, false, st);
     const size_t smem = sizeof(float) * (size_t)L.d;
     static size_t configured = 0;
     if (smem > 48 * 1024 && smem > configured) {

@@ -806,7 +806,7 @@ slx_status slx_causal_generate_lattice(slx_model* m, const int32_t* ids, int B, 
     return causal_generate(m, ids, B, T, max_new, k < 0 ? 0 : k, out, n_out);
 }
 
-slx_status slx_vocab_lattice_query(slx_model* m, const float* hidden, int B, int k, int32_t* ids) {
+slx_status slx_vocab_lattice_query(slx_model* m, const float* hidden, int B, int k, int32_t* ids, uint64_t* dist) {
     if (!m || B < 0 || (B > 0 && k > 0 && (!hidden || !ids)))
         return m ? set_err(m->ctx, SLX_EINVAL, "bad arguments") : SLX_EINVAL;
     slx_ctx* ctx = m->ctx;
@@ -819,10 +819,12 @@ slx_status slx_vocab_lattice_query(slx_model* m, const float* hidden, int B, int
     std::string err;
     if (int rc = vocab::reserve(m->vlat, B, k, err)) return set_err(ctx, rc, "%s", err.c_str());
     int32_t* d_ids = m->buf<int32_t>("lattice_ids", (size_t)B * k);
-    if (!d_ids) return set_err(ctx, SLX_EOOM, "workspace allocation failed");
+    uint64_t* d_dist = dist ? m->buf<uint64_t>("lattice_dist", (size_t)B * k) : nullptr;
+    if (!d_ids || (dist && !d_dist)) return set_err(ctx, SLX_EOOM, "workspace allocation failed");
     CK(cudaMemcpyAsync(m->vlat.hf, hidden, sizeof(float) * (size_t)B * m->embd, cudaMemcpyHostToDevice, st));
-    RUN(KC_VOCAB, (double)B * m->vlat.V * m->embd, 0, vocab::query_topk(m->vlat, B, k, d_ids, st));
+    RUN(KC_VOCAB, (double)B * m->vlat.V * m->embd, 0, vocab::query_topk(m->vlat, B, k, d_ids, d_dist, st));
     CK(cudaMemcpyAsync(ids, d_ids, sizeof(int32_t) * (size_t)B * k, cudaMemcpyDeviceToHost, st));
+    if (dist) CK(cudaMemcpyAsync(dist, d_dist, sizeof(uint64_t) * (size_t)B * k, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
     return SLX_OK;
 }

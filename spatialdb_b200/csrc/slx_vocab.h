@@ -22,7 +22,11 @@ struct Lattice {
     uint64_t* hn = nullptr;      // [B] sum of hq^2 mod 2^64
     uint64_t* dist = nullptr;    // [B][V]
     int32_t* cand = nullptr;     // [B][k] nearest rows, ascending (distance, row)
-    size_t hq_bytes = 0, hf_bytes = 0, hn_bytes = 0, dist_bytes = 0, cand_bytes = 0;
+    uint64_t* cdist = nullptr;   // [B][k] their distances
+    uint64_t* sel_d = nullptr;   // [B][slices][k] per-slice candidates (distance)
+    int32_t* sel_i = nullptr;    // [B][slices][k] per-slice candidates (row)
+    size_t hq_bytes = 0, hf_bytes = 0, hn_bytes = 0, dist_bytes = 0, cand_bytes = 0, cdist_bytes = 0;
+    size_t sel_d_bytes = 0, sel_i_bytes = 0;
 };
 
 // Builds the lattice's table from the causal model's token tensor (once per model).
@@ -33,8 +37,9 @@ void release(Lattice& L);
 int reserve(Lattice& L, int B, int k, std::string& err);
 
 // VocabLattice.QueryTopK for the B float hidden states in L.hf: d_ids[B][k] in ascending
-// (distance, row) order, -1 past the vocabulary (k > V). Returns the kernels launched.
-int query_topk(Lattice& L, int B, int k, int32_t* d_ids, cudaStream_t st);
+// (distance, row) order, -1 past the vocabulary (k > V); d_dist (nullable) [B][k] their distances,
+// UINT64_MAX past the vocabulary. Returns the kernels launched.
+int query_topk(Lattice& L, int B, int k, int32_t* d_ids, uint64_t* d_dist, cudaStream_t st);
 
 // PredictNextToken with the lattice for B last hidden states (Q30 int64 [B][d]) -> d_next[B].
 // k <= 0 gives eos (an empty candidate list). Returns the kernels launched.

@@ -43,7 +43,20 @@ def models(tmp_path_factory):
     planted = synth.write_causal(str(d / "planted.gguf"), synth.CausalShape(layers=1, embd=dm, heads=2, kv_heads=1,
                                                                             head_dim=32, ff=96, vocab=V), seed=21,
                                  token_rows=_planted_rows(V, dm, 5))
-    return {"cau": cau, "planted": planted}
+    # 5000 rows: three 2048-row selection slices, duplicates and zero rows spread across them
+    Vw = 5000
+    rng = np.random.default_rng(8)
+    wide_rows = (rng.standard_normal((Vw, dm)) * 0.05).astype(np.float32)
+    wide_rows[4500:] = wide_rows[rng.permutation(2200)[:500]]
+    wide_rows[[5, 2047, 2048, 4095, 4096, 4999]] = 0.0
+    wide = synth.write_causal(str(d / "wide.gguf"), synth.CausalShape(layers=1, embd=dm, heads=2, kv_heads=1,
+                                                                      head_dim=32, ff=96, vocab=Vw), seed=23,
+                              token_rows=wide_rows)
+    # Q8_0 weights and a width that is not a multiple of 8 (blocks straddle token rows)
+    q8odd = synth.write_causal(str(d / "q8odd.gguf"), synth.CausalShape(layers=1, embd=100, heads=2, kv_heads=1,
+                                                                        head_dim=50, ff=64, vocab=700), synth.Q8_0,
+                               seed=24)
+    return {"cau": cau, "planted": planted, "wide": wide, "q8odd": q8odd}
 
 
 def _oracle_table(oracle, path: str, vocab: int, d: int) -> np.ndarray:
@@ -66,7 +79,7 @@ def _check_query(oracle, m, table, hidden, k):
     np.testing.assert_array_equal(got.astype(np.int64), ids, err_msg=f"k={k}")
 
 
-@pytest.mark.parametrize("name", ["cau", "planted"])
+@pytest.mark.parametrize("name", ["cau", "planted", "wide", "q8odd"])
 def test_query_topk_matches_oracle(ctx, oracle, models, name):
     path = models[name]
     m = slx.IntegerCausalSource.load(path, ctx=ctx)
@@ -82,11 +95,30 @@ def test_query_topk_matches_oracle(ctx, oracle, models, name):
     hidden[5] = table[finite[len(finite) // 2]] + 0.0004
     hidden[6] = hidden[4]                                                # duplicate queries
     hidden[7, :3] = [1e4, -2e4, 3e4]
-    for k in (0, 1, 2, 7, 64, 255, V - 1, V, V + 9):
+    for k in (0, 1, 2, 7, 64, 255, 512, 513, V - 1, V, V + 9):
         _check_query(oracle, m, table, hidden, k)
 
 
-@pytest.mark.parametrize("name", ["cau", "planted"])
+def test_query_distances_cover_every_half(ctx, oracle, tmp_path):
+    """A token table holding all 65536 Half bit patterns once (1024 rows x 64): with k = V the exact
+    distance of every row is compared, which pins the device's quantization of every Half value."""
+    V, dm = 1024, 64
+    bits = np.random.default_rng(3).permutation(65536).astype(np.uint16)
+    rows = bits.view(np.float16).astype(np.float32).reshape(V, dm)
+    path = synth.write_causal(str(tmp_path / "halves.gguf"), synth.CausalShape(layers=1, embd=dm, heads=2, kv_heads=1,
+                                                                              head_dim=32, ff=96, vocab=V), seed=22,
+                              token_rows=rows)
+    m = slx.IntegerCausalSource.load(path, ctx=ctx)
+    table = _oracle_table(oracle, path, m.vocab, m.embd)
+    hidden = (np.random.default_rng(9).standard_normal((5, dm)) * 2.0).astype(np.float32)
+    hidden[0] = 0.0
+    got_ids, got_dist = m.vocab_lattice_query(hidden, V, return_distances=True)
+    ids, dist = oracle.knn_l2(oracle.quantize_dense(table), oracle.quantize_dense(hidden), V)
+    np.testing.assert_array_equal(got_dist, dist)
+    np.testing.assert_array_equal(got_ids.astype(np.int64), ids)
+
+
+@pytest.mark.parametrize("name", ["cau", "planted", "wide", "q8odd"])
 def test_lattice_next_token_matches_oracle(ctx, oracle, models, name):
     path = models[name]
     m = slx.IntegerCausalSource.load(path, ctx=ctx)
@@ -94,6 +126,12 @@ def test_lattice_next_token_matches_oracle(ctx, oracle, models, name):
     rng = np.random.default_rng(61)
     lo = 20 if name == "planted" else 0  # prompts avoid the planted inf / NaN rows
     batch = rng.integers(lo, o.vocab // 2, (4, 9)).astype(np.int32)
+    # the brute-force head on the same models, one and several queries per block
+    expect = [o.next_token(batch[b]) for b in range(len(batch))]
+    assert list(m.next_token(batch)) == expect
+    assert list(m.next_token(batch[:1])) == expect[:1]
+    wide_batch = rng.integers(lo, o.vocab // 2, (19, 5)).astype(np.int32)
+    assert list(m.next_token(wide_batch)) == [o.next_token(wide_batch[b]) for b in range(len(wide_batch))]
     for k in (0, 1, 3, 64, 300, o.vocab, o.vocab + 5):
         nx = m.next_token(batch, use_lattice=True, lattice_k=k)
         assert list(nx) == [o.next_token_lattice(batch[b], k) for b in range(len(batch))], f"k={k}"
