@@ -92,25 +92,41 @@ __global__ void k_vocab_norms(const int64_t* __restrict__ hq, int B, int d, uint
     if (lane == 0) hn[b] = s;
 }
 
-// dist[q0+i][v] for the g <= DG queries q0.. staged in shared memory: each warp takes two vocabulary
-// rows at a time. With d a multiple of 8 (VEC) every lane loads eight Half components of each row
-// per step (16-byte loads) and the queries are staged component-group-major, sh[i][t][j / 8] for
-// component j = 8 (j / 8) + t, so the lanes' int64 reads stay contiguous; otherwise lanes stride
-// single components.
+// en[v] = sum_j q[v][j]^2 mod 2^64 of the quantized table rows, one warp per row (built once).
+__global__ void k_vocab_rownorms(const uint16_t* __restrict__ table, int64_t V, int d, uint64_t* __restrict__ en) {
+    const int lane = threadIdx.x & 31;
+    for (int64_t v = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); v < V;
+         v += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+        uint64_t s = 0;
+        for (int j = lane; j < d; j += 32) {
+            const uint64_t e = (uint64_t)quantize_half(table[v * d + j]);
+            s += e * e;
+        }
+        s = warp_sum(s);
+        if (lane == 0) en[v] = s;
+    }
+}
+
+// dist[q0+i][v] for G queries q0.. staged in shared memory (slots past the g real queries are zero
+// and their sums are dropped): each warp takes two vocabulary rows at a time. With d a multiple of 8
+// (VEC) every lane loads eight Half components of each row per step (16-byte loads) and the queries
+// are staged component-group-major, sh[i][t][j / 8] for component j = 8 (j / 8) + t, so the lanes'
+// int64 reads stay contiguous; otherwise lanes stride single components.
 constexpr int DG = 8;
 constexpr int DWARPS = 16;
 constexpr int SMEM_CAP = 200 * 1024;
-template <bool VEC>
+template <bool VEC, int G>
 __global__ void __launch_bounds__(DWARPS * 32) k_vocab_dist(const uint16_t* __restrict__ table, int64_t V, int d,
+                                                            const uint64_t* __restrict__ en,
                                                             const int64_t* __restrict__ hq,
                                                             const uint64_t* __restrict__ hn, int q0, int g,
                                                             uint64_t* __restrict__ dist) {
-    extern __shared__ int64_t sh[];  // [g][d]
+    extern __shared__ int64_t sh[];  // [G][d]
     const int d8 = d >> 3;
-    for (int64_t idx = threadIdx.x; idx < (int64_t)g * d; idx += blockDim.x) {
+    for (int64_t idx = threadIdx.x; idx < (int64_t)G * d; idx += blockDim.x) {
         const int64_t i = idx / d;
         const int j = (int)(idx - i * d);
-        sh[VEC ? i * d + (int64_t)(j & 7) * d8 + (j >> 3) : idx] = hq[(int64_t)q0 * d + idx];
+        sh[VEC ? i * d + (int64_t)(j & 7) * d8 + (j >> 3) : idx] = i < g ? hq[(int64_t)q0 * d + idx] : 0;
     }
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -118,9 +134,9 @@ __global__ void __launch_bounds__(DWARPS * 32) k_vocab_dist(const uint16_t* __re
         const bool two = v0 + 1 < V;
         const uint16_t* r0 = table + v0 * d;
         const uint16_t* r1 = two ? r0 + d : r0;
-        uint64_t na = 0, nb = 0, a[DG], b[DG];
+        uint64_t a[G], b[G];
 #pragma unroll
-        for (int i = 0; i < DG; i++) a[i] = b[i] = 0;
+        for (int i = 0; i < G; i++) a[i] = b[i] = 0;
         if constexpr (VEC) {
             const uint4* R0 = reinterpret_cast<const uint4*>(r0);
             const uint4* R1 = reinterpret_cast<const uint4*>(r1);
@@ -132,15 +148,11 @@ __global__ void __launch_bounds__(DWARPS * 32) k_vocab_dist(const uint16_t* __re
                 for (int t = 0; t < 8; t++) {
                     const uint64_t ea = (uint64_t)quantize_half((w0[t >> 1] >> (16 * (t & 1))) & 0xFFFFu);
                     const uint64_t eb = (uint64_t)quantize_half((w1[t >> 1] >> (16 * (t & 1))) & 0xFFFFu);
-                    na += ea * ea;
-                    nb += eb * eb;
 #pragma unroll
-                    for (int i = 0; i < DG; i++) {
-                        if (i < g) {
-                            const uint64_t h = (uint64_t)sh[(int64_t)i * d + t * d8 + cb];
-                            a[i] += h * ea;
-                            b[i] += h * eb;
-                        }
+                    for (int i = 0; i < G; i++) {
+                        const uint64_t h = (uint64_t)sh[(int64_t)i * d + t * d8 + cb];
+                        a[i] += h * ea;
+                        b[i] += h * eb;
                     }
                 }
             }
@@ -148,34 +160,26 @@ __global__ void __launch_bounds__(DWARPS * 32) k_vocab_dist(const uint16_t* __re
             for (int j = lane; j < d; j += 32) {
                 const uint64_t ea = (uint64_t)quantize_half(r0[j]);
                 const uint64_t eb = (uint64_t)quantize_half(r1[j]);
-                na += ea * ea;
-                nb += eb * eb;
 #pragma unroll
-                for (int i = 0; i < DG; i++) {
-                    if (i < g) {
-                        const uint64_t h = (uint64_t)sh[i * d + j];
-                        a[i] += h * ea;
-                        b[i] += h * eb;
-                    }
+                for (int i = 0; i < G; i++) {
+                    const uint64_t h = (uint64_t)sh[i * d + j];
+                    a[i] += h * ea;
+                    b[i] += h * eb;
                 }
             }
         }
-        na = warp_sum(na);
-        nb = warp_sum(nb);
         uint64_t mine = 0;
 #pragma unroll
-        for (int i = 0; i < DG; i++) {
-            if (i < g) {
-                const uint64_t sa = warp_sum(a[i]), sb = warp_sum(b[i]);
-                if (lane == i) mine = sa;
-                if (lane == 16 + i) mine = sb;
-            }
+        for (int i = 0; i < G; i++) {
+            const uint64_t sa = warp_sum(a[i]), sb = warp_sum(b[i]);
+            if (lane == i) mine = sa;
+            if (lane == 16 + i) mine = sb;
         }
         // lane i writes query q0+i of row v0, lane 16+i of row v0+1
         const int i = lane & 15;
         if (i < g && (lane < 16 || two)) {
-            const uint64_t e2 = lane < 16 ? na : nb;
-            dist[(int64_t)(q0 + i) * V + v0 + (lane >> 4)] = hn[q0 + i] + e2 - 2 * mine;
+            const int64_t v = v0 + (lane >> 4);
+            dist[(int64_t)(q0 + i) * V + v] = hn[q0 + i] + en[v] - 2 * mine;
         }
     }
 }
@@ -476,7 +480,19 @@ __global__ void __launch_bounds__(ST) k_vocab_score(const uint16_t* __restrict__
     for (int c = tid; c < k; c += ST) {
         const uint16_t* row = table + (int64_t)cand[(int64_t)b * k + c] * d;
         float dot = 0.0f;
-        for (int j = 0; j < d; j++) dot = __fadd_rn(dot, __fmul_rn(hs[j], h2f(row[j])));
+        if ((d & 7) == 0) {  // 16-byte row loads, issued ahead of the sequential chain
+            const uint4* R = reinterpret_cast<const uint4*>(row);
+#pragma unroll 4
+            for (int cb = 0; cb < (d >> 3); cb++) {
+                const uint4 x = __ldg(R + cb);
+                const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                for (int t = 0; t < 8; t++)
+                    dot = __fadd_rn(dot, __fmul_rn(hs[cb * 8 + t], h2f((uint16_t)(w[t >> 1] >> (16 * (t & 1))))));
+            }
+        } else {
+            for (int j = 0; j < d; j++) dot = __fadd_rn(dot, __fmul_rn(hs[j], h2f(row[j])));
+        }
         dot = __fadd_rn(dot, 0.0f);  // -0 -> +0: the two compare equal
         const unsigned long long kc =
             ((unsigned long long)(isnan(dot) ? 0u : ordered(dot)) << 32) | (0xFFFFFFFFu - (uint32_t)c);
@@ -519,9 +535,42 @@ size_t slice_slots(int64_t V, int k) {
     return (size_t)((V + SLICE - 1) / SLICE) * (size_t)k;
 }
 
+// Queries per distance pass: a power of two (the kernel's template slots) whose int64 rows fit SMEM_CAP.
 int queries_per_pass(int d) {
-    int g = SMEM_CAP / (8 * d);
-    return g < DG ? g : DG;
+    int g = DG;
+    while (g > 1 && g * 8 * d > SMEM_CAP) g >>= 1;
+    return g;
+}
+
+template <bool VEC, int G>
+void launch_dist_t(Lattice& L, int q0, int g, cudaStream_t st) {
+    const int smem = G * L.d * 8;
+    static int configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        cudaFuncSetAttribute(k_vocab_dist<VEC, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        configured = smem;
+    }
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_vocab_dist<VEC, G>, DWARPS * 32, smem);
+    if (per_sm < 1) per_sm = 1;
+    const int64_t want = (L.V + DWARPS * 2 - 1) / (DWARPS * 2);
+    const int64_t cap = (int64_t)sm_count() * per_sm;
+    k_vocab_dist<VEC, G><<<(unsigned)(want < cap ? want : cap), DWARPS * 32, smem, st>>>(L.table, L.V, L.d, L.en, L.hq,
+                                                                                      L.hn, q0, g, L.dist);
+}
+
+void launch_dist(Lattice& L, bool vec, int G, int q0, int g, cudaStream_t st) {
+    if (vec) {
+        if (G == 1) launch_dist_t<true, 1>(L, q0, g, st);
+        else if (G == 2) launch_dist_t<true, 2>(L, q0, g, st);
+        else if (G == 4) launch_dist_t<true, 4>(L, q0, g, st);
+        else launch_dist_t<true, 8>(L, q0, g, st);
+    } else {
+        if (G == 1) launch_dist_t<false, 1>(L, q0, g, st);
+        else if (G == 2) launch_dist_t<false, 2>(L, q0, g, st);
+        else if (G == 4) launch_dist_t<false, 4>(L, q0, g, st);
+        else launch_dist_t<false, 8>(L, q0, g, st);
+    }
 }
 
 // Norms, distances and the radix select for the B queries quantized in L.hq; k in [1, V].
@@ -530,27 +579,10 @@ int candidates(Lattice& L, int B, int k, bool want_dist, cudaStream_t st) {
     k_vocab_norms<<<(unsigned)((B + 7) / 8), 256, 0, st>>>(L.hq, B, L.d, L.hn);
     n++;
     const int gmax = queries_per_pass(L.d);
-    const bool vec = (L.d & 7) == 0;
-    const void* fn = vec ? (const void*)k_vocab_dist<true> : (const void*)k_vocab_dist<false>;
-    static int configured[2] = {0, 0};
-    const int smem_max = gmax * L.d * 8;
-    if (smem_max > 48 * 1024 && smem_max > configured[vec]) {
-        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max);
-        configured[vec] = smem_max;
-    }
     for (int q0 = 0; q0 < B; q0 += gmax) {
         const int g = B - q0 < gmax ? B - q0 : gmax;
-        const int smem = g * L.d * 8;
-        int per_sm = 1;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, DWARPS * 32, smem);
-        if (per_sm < 1) per_sm = 1;
-        const int64_t want = (L.V + DWARPS * 2 - 1) / (DWARPS * 2);
-        const int64_t cap = (int64_t)sm_count() * per_sm;
-        const unsigned grid = (unsigned)(want < cap ? want : cap);
-        if (vec)
-            k_vocab_dist<true><<<grid, DWARPS * 32, smem, st>>>(L.table, L.V, L.d, L.hq, L.hn, q0, g, L.dist);
-        else
-            k_vocab_dist<false><<<grid, DWARPS * 32, smem, st>>>(L.table, L.V, L.d, L.hq, L.hn, q0, g, L.dist);
+        const int G = g <= 1 ? 1 : g <= 2 ? 2 : g <= 4 ? 4 : 8;
+        launch_dist(L, (L.d & 7) == 0, G, q0, g, st);
         n++;
     }
     int n2 = 1;
@@ -600,7 +632,16 @@ int build(const WDesc& tok, int64_t vocab, int d, Lattice& L, cudaStream_t st, s
         err = "vocab lattice: device allocation failed";
         return SLX_EOOM;
     }
-    if (total > 0) k_vocab_table<<<(unsigned)(sm_count() * 8), 256, 0, st>>>(tok, total, L.table);
+    if (cudaMalloc(&L.en, sizeof(uint64_t) * (L.V > 0 ? L.V : 1)) != cudaSuccess) {
+        L.en = nullptr;
+        release(L);
+        err = "vocab lattice: device allocation failed";
+        return SLX_EOOM;
+    }
+    if (total > 0) {
+        k_vocab_table<<<(unsigned)(sm_count() * 8), 256, 0, st>>>(tok, total, L.table);
+        k_vocab_rownorms<<<(unsigned)(sm_count() * 4), 256, 0, st>>>(L.table, L.V, d, L.en);
+    }
     if (cudaGetLastError() != cudaSuccess) {
         release(L);
         err = "vocab lattice: table kernel failed to launch";
@@ -610,7 +651,7 @@ int build(const WDesc& tok, int64_t vocab, int d, Lattice& L, cudaStream_t st, s
 }
 
 void release(Lattice& L) {
-    for (void* p : {(void*)L.table, (void*)L.hq, (void*)L.hf, (void*)L.hn, (void*)L.dist, (void*)L.cand, (void*)L.cdist,
+    for (void* p : {(void*)L.table, (void*)L.en, (void*)L.hq, (void*)L.hf, (void*)L.hn, (void*)L.dist, (void*)L.cand, (void*)L.cdist,
                     (void*)L.sel_d, (void*)L.sel_i})
         if (p) cudaFree(p);
     L = Lattice();

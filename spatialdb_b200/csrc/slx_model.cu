@@ -716,7 +716,7 @@ static int vocab_lattice_ready(slx_model* m, cudaStream_t st) {
     std::string err;
     int rc = vocab::build(m->tok, m->vocab, m->embd, m->vlat, st, err);
     if (rc) return set_err(m->ctx, rc, "%s", err.c_str());
-    m->ctx->launches += m->vlat.V > 0 ? 1 : 0;
+    m->ctx->launches += m->vlat.V > 0 ? 2 : 0;  // table and row norms
     m->vlat_ready = true;
     return SLX_OK;
 }

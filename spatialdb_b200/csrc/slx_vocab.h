@@ -16,6 +16,7 @@ struct Lattice {
     int64_t V = 0;               // rows: min(vocab, token-table rows)
     int d = 0;
     uint16_t* table = nullptr;   // [V][d] Half bits of the token rows (TokenEmbeddingsFloat is their float)
+    uint64_t* en = nullptr;      // [V] sum of the quantized row's squares mod 2^64
     // per-query scratch, grown to the largest batch seen
     int64_t* hq = nullptr;       // [B][d] hidden states quantized with VocabLattice's options
     float* hf = nullptr;         // [B][d] hidden states as float
