@@ -652,6 +652,28 @@ def ctypes_int():
     return ctypes.c_int(0)
 
 
+def run_lm_head_only(args) -> None:
+    """The two next-token heads alone on a one-layer model of the Gemma-2B vocabulary and width
+    (256000 x 2048 Q4_0 token table): a short command for profiling the head kernels."""
+    import numpy as np
+
+    import spatialdb_b200 as slx
+    from spatialdb_b200 import synth
+
+    shape = synth.CausalShape(layers=1, embd=2048, heads=8, kv_heads=1, head_dim=256, ff=256, vocab=256000)
+    path = synth.cached("lm_head_v256000_d2048_l1_q4_0_seed5.gguf",
+                        lambda p: synth.write_causal(p, shape, synth.Q4_0, synth.F16, seed=5, eos=shape.vocab - 1))
+    ctx = slx.Context(0)
+    m = slx.IntegerCausalSource.load(path, ctx=ctx)
+    rng = np.random.default_rng(3)
+    p1 = rng.integers(0, shape.vocab - 1, (1, 32)).astype(np.int32)
+    p16 = rng.integers(0, shape.vocab - 1, (16, 32)).astype(np.int32)
+    res = lm_head_bench(ctx, m, path, shape, p1, p16, reps=args.steps)
+    res["model"] = "1 layer, Gemma-2B vocabulary and width (V 256000, d 2048, Q4_0 token table), 32-token prompts"
+    m.close()
+    print(json.dumps({"lm_head": res}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -664,10 +686,14 @@ def main():
     ap.add_argument("--skip-secondary", action="store_true",
                     help="skip the GEMV, Gemma decode and embed+search measurements")
     ap.add_argument("--skip-search", action="store_true", help="skip the embed+search measurement")
+    ap.add_argument("--lm-head-only", action="store_true",
+                    help="time only the argmax and VocabLattice next-token heads (one-layer Gemma-width model)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.lm_head_only:
+        run_lm_head_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
