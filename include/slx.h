@@ -180,6 +180,36 @@ slx_status slx_lattice_query_knn_l2(slx_lattice* lat, const float* queries, int 
                                     uint64_t* dist, int* n_exact);
 slx_status slx_lattice_query_knn_l2_device(slx_lattice* lat, const float* d_queries, int nq, int k, int flags,
                                            int64_t* d_ids, uint64_t* d_dist, int* n_exact, void* stream);
+/* KD tree over a lattice's rows: EmbeddingLatticeBuilder.Build (Lattice/EmbeddingLatticeBuilder.cs:11-127)
+ * with LatticeOptions.LeafThreshold, as the EmbeddingLattice constructor runs it (row i is occupant i).
+ * Spans of more than leaf_threshold occupants split at the median (sorted[N/2]) of their
+ * highest-variance dimension, partitioned by the reference's two-pointer swap, so leaves hold the
+ * reference's occupants in the reference's order. Equal variances take the lowest dimension (the
+ * reference's ConcurrentDictionary enumeration order is machine-dependent). Built on the device. */
+slx_status slx_lattice_build_tree(slx_lattice* lat, int leaf_threshold);
+/* SparseTreeStats (EmbeddingLattice.CollectStats, Lattice/EmbeddingLattice.cs:102-150):
+ * info = {TotalNodes, BranchNodes, LeafNodes, TotalOccupants, MaxDepth}. */
+slx_status slx_lattice_tree_info(slx_lattice* lat, int64_t* info, int n);
+/* The tree in pre-order (the serializer's order), TotalNodes entries per array (each nullable):
+ * kind 0 leaf / 1 branch, child mask (1 below, 2 above), split dimension and value, and for leaves
+ * the start and count of their occupants in perm (row index of every leaf-order position). */
+slx_status slx_lattice_tree_export(slx_lattice* lat, int32_t* kind, int32_t* mask, int32_t* dim, int64_t* val,
+                                   int64_t* start, int64_t* count, int32_t* perm);
+/* SparseLatticeSerializer.Save with Int32PayloadSerializer (Lattice/SparseLatticeSerializer.cs:27-114):
+ * the tree's SLAT bytes, payload = id_base + row (or the payloads a loaded lattice carries).
+ * SLX_EINVAL without a tree (InvalidOperationException "must be frozen"). The _mem variant writes
+ * to out (cap bytes; out may be NULL to query *size). */
+slx_status slx_lattice_save_slat(slx_lattice* lat, const char* path);
+slx_status slx_lattice_save_slat_mem(slx_lattice* lat, uint8_t* out, int64_t cap, int64_t* size);
+/* SparseLatticeSerializer.Load with Int32PayloadSerializer (:46-166): a lattice whose rows are the
+ * file's occupants in file order, with their tree; query ids are the payloads; queries are quantized
+ * with (zero_threshold, global_scale). Errors: bad magic / version / tag SLX_EFORMAT, short input
+ * SLX_EEOF, invalid occupants (SparseVector's checks) SLX_EINVAL, components beyond int32 SLX_ERANGE,
+ * occupants of different widths or wider than 16384 SLX_EUNSUPPORTED, missing file SLX_ENOTFOUND. */
+slx_status slx_lattice_load_slat(slx_ctx* ctx, const char* path, float zero_threshold, int64_t global_scale,
+                                 slx_lattice** out);
+slx_status slx_lattice_load_slat_mem(slx_ctx* ctx, const uint8_t* bytes, int64_t n, float zero_threshold,
+                                     int64_t global_scale, slx_lattice** out);
 /* k-way merge of per-shard answers: d_ids/d_dist [parts][nq][k] (each list ascending, as returned
  * above) -> [nq][k]; parts <= 64. No reference counterpart: the sharded database's top-k merge after
  * an all-gather of the shards' answers. */

@@ -99,6 +99,15 @@ def _sig(lib):
     f("slxo_quantize_dense", None, F32P, i64, f32, i64, I64P)
     f("slxo_distance_sq_l2_fast", ctypes.c_uint64, I64P, I64P, i)
     f("slxo_knn_l2", None, I64P, i64, i, I64P, i, i, i64, I64P, U64P)
+    f("slxo_tree_build", VP, I64P, i64, i, i, ctypes.POINTER(i))
+    f("slxo_tree_free", None, VP)
+    f("slxo_tree_info", None, VP, I64P)
+    f("slxo_tree_export", None, VP, I32P, I32P, I32P, I64P, I64P, I64P, I64P)
+    f("slxo_slat_save", i64, VP, I64P, i, I32P, U8P, i64)
+    f("slxo_slat_load", VP, U8P, i64, ctypes.POINTER(i), ctypes.POINTER(i64), ctypes.POINTER(i))
+    f("slxo_slat_tree", VP, VP)
+    f("slxo_slat_rows", None, VP, I64P, I32P)
+    f("slxo_slat_free", None, VP)
 
 
 def lib():
@@ -498,3 +507,77 @@ class Causal:
         if st:
             raise OracleError(st, "gemma encode")
         return out
+
+
+# ---- KD-tree lattice and SLAT ---------------------------------------------------------------------
+
+TREE_INFO_KEYS = ("nodes", "branches", "leaves", "occupants", "max_depth")
+
+
+def _tree_dict(h, n_rows: int) -> dict:
+    info = np.zeros(5, np.int64)
+    lib().slxo_tree_info(h, _p(info, I64P))
+    nn = int(info[0])
+    kind, mask, dim = (np.zeros(max(nn, 1), np.int32) for _ in range(3))
+    val, start, count = (np.zeros(max(nn, 1), np.int64) for _ in range(3))
+    perm = np.zeros(max(n_rows, 1), np.int64)
+    lib().slxo_tree_export(h, _p(kind, I32P), _p(mask, I32P), _p(dim, I32P), _p(val, I64P), _p(start, I64P),
+                           _p(count, I64P), _p(perm, I64P))
+    out = dict(zip(TREE_INFO_KEYS, (int(x) for x in info)))
+    out.update(kind=kind[:nn], mask=mask[:nn], dim=dim[:nn], val=val[:nn], start=start[:nn], count=count[:nn],
+               perm=perm[:n_rows])
+    return out
+
+
+def tree_build(rows, leaf_threshold: int = 16) -> dict:
+    """EmbeddingLatticeBuilder.Build over dense quantized rows [n, dim] (row i is occupant i).
+    Returns the tree flattened in pre-order (kind 0 leaf / 1 branch, child mask, split dimension and
+    value, leaf start and count into `perm`, the row ids in leaf order) and its statistics."""
+    rows = np.ascontiguousarray(np.atleast_2d(rows), np.int64)
+    n, dim = rows.shape
+    st = ctypes.c_int(0)
+    h = lib().slxo_tree_build(_p(rows, I64P), n, dim, leaf_threshold, ctypes.byref(st))
+    if not h:
+        raise OracleError(st.value, "tree_build")
+    try:
+        return _tree_dict(h, n)
+    finally:
+        lib().slxo_tree_free(h)
+
+
+def slat_save(rows, payload, leaf_threshold: int = 16) -> bytes:
+    """SparseLatticeSerializer.Save (Int32PayloadSerializer) of the lattice built over `rows`."""
+    rows = np.ascontiguousarray(np.atleast_2d(rows), np.int64)
+    n, dim = rows.shape
+    payload = np.ascontiguousarray(payload, np.int32)
+    st = ctypes.c_int(0)
+    h = lib().slxo_tree_build(_p(rows, I64P), n, dim, leaf_threshold, ctypes.byref(st))
+    if not h:
+        raise OracleError(st.value, "tree_build")
+    try:
+        size = lib().slxo_slat_save(h, _p(rows, I64P), dim, _p(payload, I32P), None, 0)
+        buf = np.zeros(size, np.uint8)
+        lib().slxo_slat_save(h, _p(rows, I64P), dim, _p(payload, I32P), _p(buf, U8P), size)
+        return buf.tobytes()
+    finally:
+        lib().slxo_tree_free(h)
+
+
+def slat_load(data: bytes) -> dict:
+    """SparseLatticeSerializer.Load (Int32PayloadSerializer): dense rows [n, dim] in file order,
+    payloads, and the tree as tree_build returns it (perm indexes the rows in file order)."""
+    buf = np.frombuffer(bytes(data), np.uint8).copy()
+    st, n, dim = ctypes.c_int(0), ctypes.c_int64(0), ctypes.c_int(0)
+    h = lib().slxo_slat_load(_p(buf, U8P) if buf.size else None, buf.size, ctypes.byref(st), ctypes.byref(n),
+                             ctypes.byref(dim))
+    if not h:
+        raise OracleError(st.value, "slat_load")
+    try:
+        rows = np.zeros((n.value, dim.value), np.int64)
+        payload = np.zeros(n.value, np.int32)
+        lib().slxo_slat_rows(h, _p(rows, I64P), _p(payload, I32P))
+        out = _tree_dict(lib().slxo_slat_tree(h), n.value)
+        out.update(rows=rows, payload=payload)
+        return out
+    finally:
+        lib().slxo_slat_free(h)

@@ -1330,6 +1330,254 @@ static int causal_next_lattice(const Causal& c, const int32_t* ids, int T, int k
     return SLXO_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// KD-tree lattice (EmbeddingLatticeBuilder, Lattice/EmbeddingLatticeBuilder.cs:11-127) and its
+// SLAT wire format (SparseLatticeSerializer, Lattice/SparseLatticeSerializer.cs:5-166).
+//
+// The builder splits a span of occupants at the median of its highest-variance dimension:
+// variance = sumSq * N - sum^2 over the span's N occupants (absent components are 0), among the
+// dimensions some occupant of the span populates (:47-84); median = sorted values[N / 2] (:86-97);
+// the span is partitioned in place by the two-pointer swap of :99-126 (values < median to the
+// left); a span of at most LeafThreshold occupants, or one whose split leaves a side empty, or one
+// with no populated dimension, becomes a leaf holding the span in its current order. The reference
+// accumulates in BigInteger; here components are limited to |v| < 2^31 so Int128 is exact
+// (N < 2^31). Equal variances: the reference takes the first in ConcurrentDictionary enumeration
+// order (machine-dependent); here the lowest dimension.
+struct TreeNode {
+    int kind = 0;        // 0 leaf, 1 branch
+    int mask = 0;        // branch: 1 below present, 2 above present
+    int dim = 0;
+    int64_t val = 0;
+    int below = -1, above = -1;
+    int64_t start = 0, count = 0;  // leaf: occupants perm[start .. start+count)
+};
+struct Tree {
+    std::vector<TreeNode> nodes;
+    std::vector<int64_t> perm;     // row ids in leaf order
+    int root = -1;
+};
+
+static int tree_leaf(Tree& t, int64_t start, int64_t count) {
+    TreeNode nd;
+    nd.kind = 0;
+    nd.start = start;
+    nd.count = count;
+    t.nodes.push_back(nd);
+    return (int)t.nodes.size() - 1;
+}
+
+static int tree_build_rec(Tree& t, const int64_t* rows, int dim, int64_t start, int64_t len, int leaf_threshold) {
+    int64_t* span = t.perm.data() + start;
+    if (len <= leaf_threshold) return tree_leaf(t, start, len);
+    int best_dim = -1;
+    __int128 best_var = -1;
+    for (int d = 0; d < dim; d++) {
+        __int128 sum = 0, sq = 0;
+        bool populated = false;
+        for (int64_t i = 0; i < len; i++) {
+            const int64_t v = rows[span[i] * dim + d];
+            if (v != 0) populated = true;
+            sum += v;
+            sq += (__int128)v * v;
+        }
+        if (!populated) continue;
+        const __int128 var = sq * len - sum * sum;
+        if (var > best_var) {
+            best_var = var;
+            best_dim = d;
+        }
+    }
+    if (best_dim < 0) return tree_leaf(t, start, len);
+    std::vector<int64_t> vals((size_t)len);
+    for (int64_t i = 0; i < len; i++) vals[i] = rows[span[i] * dim + best_dim];
+    std::sort(vals.begin(), vals.end());
+    const int64_t pivot = vals[(size_t)(len / 2)];
+    int64_t left = 0, right = len - 1;
+    while (left <= right) {
+        if (rows[span[left] * dim + best_dim] < pivot) { left++; continue; }
+        if (rows[span[right] * dim + best_dim] >= pivot) { right--; continue; }
+        std::swap(span[left], span[right]);
+        left++;
+        right--;
+    }
+    const int64_t boundary = left;
+    if (boundary == 0 || boundary == len) return tree_leaf(t, start, len);
+    TreeNode br;
+    br.kind = 1;
+    br.mask = 3;
+    br.dim = best_dim;
+    br.val = pivot;
+    t.nodes.push_back(br);
+    const int id = (int)t.nodes.size() - 1;
+    const int below = tree_build_rec(t, rows, dim, start, boundary, leaf_threshold);
+    const int above = tree_build_rec(t, rows, dim, start + boundary, len - boundary, leaf_threshold);
+    t.nodes[id].below = below;
+    t.nodes[id].above = above;
+    return id;
+}
+
+struct TreeStats { int64_t nodes = 0, branches = 0, leaves = 0, occupants = 0, max_depth = 0; };
+static void tree_stats(const Tree& t, int node, int64_t depth, TreeStats& s) {
+    const TreeNode& nd = t.nodes[node];
+    s.nodes++;
+    if (depth > s.max_depth) s.max_depth = depth;
+    if (nd.kind == 0) {
+        s.leaves++;
+        s.occupants += nd.count;
+        return;
+    }
+    s.branches++;
+    if (nd.below >= 0) tree_stats(t, nd.below, depth + 1, s);
+    if (nd.above >= 0) tree_stats(t, nd.above, depth + 1, s);
+}
+
+// Pre-order flattening (the order SparseLatticeSerializer.WriteNode visits, :64-95): per node its
+// kind, child mask, split dimension and value, and for leaves the offset and count of its
+// occupants in the leaf-order permutation.
+static void tree_preorder(const Tree& t, int node, std::vector<int>& order) {
+    order.push_back(node);
+    const TreeNode& nd = t.nodes[node];
+    if (nd.kind == 1) {
+        if (nd.below >= 0) tree_preorder(t, nd.below, order);
+        if (nd.above >= 0) tree_preorder(t, nd.above, order);
+    }
+}
+
+struct ByteWriter {
+    std::vector<uint8_t> b;
+    template <class T> void put(T v) {
+        const size_t o = b.size();
+        b.resize(o + sizeof(T));
+        memcpy(b.data() + o, &v, sizeof(T));
+    }
+};
+
+// WriteNode / WriteLeaf (:64-114) with Int32PayloadSerializer (:187-194): occupant records carry
+// TotalDimensions, the entry count and (ushort dimension, long value) for every nonzero component
+// in ascending dimension (EmbeddingAdapter.Quantize keeps exactly the nonzero ones), then the payload.
+static void slat_write_node(const Tree& t, int node, const int64_t* rows, int dim, const int32_t* payload,
+                            ByteWriter& w) {
+    const TreeNode& nd = t.nodes[node];
+    if (nd.kind == 0) {
+        w.put<uint8_t>(0);
+        w.put<int32_t>((int32_t)nd.count);
+        for (int64_t i = 0; i < nd.count; i++) {
+            const int64_t r = t.perm[nd.start + i];
+            const int64_t* v = rows + r * dim;
+            int32_t nnz = 0;
+            for (int d = 0; d < dim; d++) nnz += v[d] != 0;
+            w.put<int32_t>(dim);
+            w.put<int32_t>(nnz);
+            for (int d = 0; d < dim; d++)
+                if (v[d] != 0) {
+                    w.put<uint16_t>((uint16_t)d);
+                    w.put<int64_t>(v[d]);
+                }
+            w.put<int32_t>(payload[r]);
+        }
+        return;
+    }
+    w.put<uint8_t>(1);
+    w.put<uint16_t>((uint16_t)nd.dim);
+    w.put<int64_t>(nd.val);
+    w.put<uint8_t>((uint8_t)nd.mask);
+    if (nd.below >= 0) slat_write_node(t, nd.below, rows, dim, payload, w);
+    if (nd.above >= 0) slat_write_node(t, nd.above, rows, dim, payload, w);
+}
+
+// Load (:46-62, ReadNode/ReadLeaf/ReadBranch :116-166): magic and version checks
+// (InvalidDataException), unknown tags (InvalidDataException), short input (EndOfStreamException),
+// and the SparseVector constructor's checks on every occupant (Math/SparseVector.cs:21-28,303-320:
+// TotalDimensions > 0, dimensions below it, ascending without duplicates, no zero values:
+// ArgumentException). Occupants become dense rows of width `dim` (all occupants must share it).
+struct SlatReader {
+    const uint8_t* p;
+    int64_t n, pos = 0;
+    int status = SLXO_OK;
+    template <class T> bool get(T& v) {
+        if (status) return false;
+        if (pos + (int64_t)sizeof(T) > n) { status = SLXO_EEOF; return false; }
+        memcpy(&v, p + pos, sizeof(T));
+        pos += sizeof(T);
+        return true;
+    }
+};
+struct SlatLoaded {
+    Tree t;
+    std::vector<int64_t> rows;    // [n][dim]
+    std::vector<int32_t> payload; // [n]
+    int dim = -1;
+};
+static int slat_read_node(SlatReader& r, SlatLoaded& out) {
+    uint8_t tag;
+    if (!r.get(tag)) return -1;
+    if (tag == 0) {
+        int32_t count;
+        if (!r.get(count)) return -1;
+        if (count < 0) { r.status = SLXO_EFORMAT; return -1; }
+        const int64_t start = (int64_t)out.t.perm.size();
+        for (int32_t i = 0; i < count; i++) {
+            int32_t total, entries;
+            if (!r.get(total) || !r.get(entries)) return -1;
+            if (total <= 0 || entries < 0) { r.status = SLXO_EINVAL; return -1; }
+            if (out.dim < 0) out.dim = total;
+            if (total != out.dim) { r.status = SLXO_EINVAL; return -1; }
+            const int64_t row = (int64_t)out.payload.size();
+            out.rows.resize((size_t)(row + 1) * total, 0);
+            int prev = -1;
+            for (int32_t e = 0; e < entries; e++) {
+                uint16_t d;
+                int64_t v;
+                if (!r.get(d) || !r.get(v)) return -1;
+                if ((int)d >= total || v == 0 || (int)d <= prev) { r.status = SLXO_EINVAL; return -1; }
+                prev = d;
+                out.rows[(size_t)row * total + d] = v;
+            }
+            int32_t pay;
+            if (!r.get(pay)) return -1;
+            out.payload.push_back(pay);
+            out.t.perm.push_back(row);
+        }
+        return tree_leaf(out.t, start, count);
+    }
+    if (tag == 1) {
+        uint16_t d;
+        int64_t v;
+        uint8_t mask;
+        if (!r.get(d) || !r.get(v) || !r.get(mask)) return -1;
+        TreeNode br;
+        br.kind = 1;
+        br.dim = d;
+        br.val = v;
+        br.mask = mask & 3;
+        out.t.nodes.push_back(br);
+        const int id = (int)out.t.nodes.size() - 1;
+        int below = -1, above = -1;
+        if (mask & 1) { below = slat_read_node(r, out); if (below < 0) return -1; }
+        if (mask & 2) { above = slat_read_node(r, out); if (above < 0) return -1; }
+        out.t.nodes[id].below = below;
+        out.t.nodes[id].above = above;
+        return id;
+    }
+    r.status = SLXO_EFORMAT;
+    return -1;
+}
+
+static void tree_export(const Tree& t, int32_t* kind, int32_t* mask, int32_t* dim, int64_t* val, int64_t* start,
+                        int64_t* count) {
+    std::vector<int> order;
+    if (t.root >= 0) tree_preorder(t, t.root, order);
+    for (size_t i = 0; i < order.size(); i++) {
+        const TreeNode& nd = t.nodes[order[i]];
+        kind[i] = nd.kind;
+        mask[i] = nd.mask;
+        dim[i] = nd.dim;
+        val[i] = nd.val;
+        start[i] = nd.start;
+        count[i] = nd.count;
+    }
+}
+
 extern "C" {
 
 int slxo_set_threads(int n) {
@@ -1554,4 +1802,71 @@ void slxo_knn_l2(const int64_t* db, int64_t n, int dim, const int64_t* q, int nq
     knn_l2(db, n, dim, q, nq, k, id_base, ids, dist);
 }
 
+
+// ---- KD-tree lattice and SLAT (test oracle) -------------------------------------------------
+void* slxo_tree_build(const int64_t* rows, int64_t n, int dim, int leaf_threshold, int* status) {
+    *status = SLXO_OK;
+    if (n < 0 || dim <= 0 || dim > 65536 || (n > 0 && !rows)) { *status = SLXO_EINVAL; return nullptr; }
+    for (int64_t i = 0; i < n * dim; i++)
+        if (rows[i] <= -(1LL << 31) || rows[i] >= (1LL << 31)) { *status = SLXO_ERANGE; return nullptr; }
+    Tree* t = new Tree();
+    t->perm.resize((size_t)n);
+    for (int64_t i = 0; i < n; i++) t->perm[i] = i;
+    t->root = tree_build_rec(*t, rows, dim, 0, n, leaf_threshold);
+    return t;
+}
+void slxo_tree_free(void* h) { delete (Tree*)h; }
+// info: nodes, branches, leaves, occupants, max depth
+void slxo_tree_info(void* h, int64_t* info) {
+    TreeStats s;
+    Tree* t = (Tree*)h;
+    if (t->root >= 0) tree_stats(*t, t->root, 0, s);
+    info[0] = s.nodes; info[1] = s.branches; info[2] = s.leaves; info[3] = s.occupants; info[4] = s.max_depth;
+}
+void slxo_tree_export(void* h, int32_t* kind, int32_t* mask, int32_t* dim, int64_t* val, int64_t* start,
+                      int64_t* count, int64_t* perm) {
+    Tree* t = (Tree*)h;
+    tree_export(*t, kind, mask, dim, val, start, count);
+    for (size_t i = 0; i < t->perm.size(); i++) perm[i] = t->perm[i];
+}
+// SLAT bytes of a built tree over `rows` with Int32 payloads; returns the size (call with
+// out = nullptr to size the buffer).
+int64_t slxo_slat_save(void* h, const int64_t* rows, int dim, const int32_t* payload, uint8_t* out, int64_t cap) {
+    Tree* t = (Tree*)h;
+    ByteWriter w;
+    w.put<uint32_t>(0x544C4153u);
+    w.put<uint16_t>(1);
+    if (t->root >= 0) slat_write_node(*t, t->root, rows, dim, payload, w);
+    if (out && cap >= (int64_t)w.b.size()) memcpy(out, w.b.data(), w.b.size());
+    return (int64_t)w.b.size();
+}
+// Parses SLAT bytes; on success *n_out rows of *dim_out components (dim 0 when the file holds no
+// occupant) are available through slxo_slat_rows and the tree through slxo_tree_*.
+void* slxo_slat_load(const uint8_t* bytes, int64_t n, int* status, int64_t* n_out, int* dim_out) {
+    SlatReader r{bytes, n};
+    uint32_t magic;
+    uint16_t version;
+    *status = SLXO_OK;
+    if (!r.get(magic)) { *status = r.status; return nullptr; }
+    if (magic != 0x544C4153u) { *status = SLXO_EFORMAT; return nullptr; }
+    if (!r.get(version)) { *status = r.status; return nullptr; }
+    if (version != 1) { *status = SLXO_EFORMAT; return nullptr; }
+    SlatLoaded* L = new SlatLoaded();
+    L->t.root = slat_read_node(r, *L);
+    if (L->t.root < 0) {
+        *status = r.status ? r.status : SLXO_EFORMAT;
+        delete L;
+        return nullptr;
+    }
+    *n_out = (int64_t)L->payload.size();
+    *dim_out = L->dim < 0 ? 0 : L->dim;
+    return L;
+}
+void* slxo_slat_tree(void* h) { return &((SlatLoaded*)h)->t; }
+void slxo_slat_rows(void* h, int64_t* rows, int32_t* payload) {
+    SlatLoaded* L = (SlatLoaded*)h;
+    memcpy(rows, L->rows.data(), L->rows.size() * sizeof(int64_t));
+    memcpy(payload, L->payload.data(), L->payload.size() * sizeof(int32_t));
+}
+void slxo_slat_free(void* h) { delete (SlatLoaded*)h; }
 }  // extern "C"

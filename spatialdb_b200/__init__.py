@@ -364,6 +364,73 @@ class EmbeddingLattice:
         self.last_exact = ne.value
         return ne.value
 
+    # ---- KD tree (EmbeddingLatticeBuilder) and SLAT (SparseLatticeSerializer) --------------------
+
+    TREE_INFO_KEYS = ("nodes", "branches", "leaves", "occupants", "max_depth")
+
+    def freeze(self, leaf_threshold: int = 16) -> "EmbeddingLattice":
+        """Builds the KD tree over the rows (EmbeddingLatticeBuilder.Build with LatticeOptions.LeafThreshold)."""
+        self._ctx.check(self._ctx._lib.slx_lattice_build_tree(self._h, int(leaf_threshold)))
+        return self
+
+    def collect_stats(self) -> dict:
+        """SparseTreeStats: nodes, branches, leaves, occupants, max_depth."""
+        info = np.zeros(5, np.int64)
+        self._ctx.check(self._ctx._lib.slx_lattice_tree_info(self._h, _p(info, I64P), 5))
+        return dict(zip(self.TREE_INFO_KEYS, (int(x) for x in info)))
+
+    def tree(self) -> dict:
+        """The tree in pre-order: kind, mask, dim, val, start, count per node and perm (row of each
+        leaf-order position), plus the statistics."""
+        st = self.collect_stats()
+        nn = st["nodes"]
+        kind, mask, dim = (np.zeros(max(nn, 1), np.int32) for _ in range(3))
+        val, start, count = (np.zeros(max(nn, 1), np.int64) for _ in range(3))
+        perm = np.zeros(max(st["occupants"], 1), np.int32)
+        self._ctx.check(self._ctx._lib.slx_lattice_tree_export(self._h, _p(kind, I32P), _p(mask, I32P), _p(dim, I32P),
+                                                               _p(val, I64P), _p(start, I64P), _p(count, I64P),
+                                                               _p(perm, I32P)))
+        st.update(kind=kind[:nn], mask=mask[:nn], dim=dim[:nn], val=val[:nn], start=start[:nn], count=count[:nn],
+                  perm=perm[: st["occupants"]])
+        return st
+
+    def save(self, path: str | None = None) -> bytes | None:
+        """SparseLatticeSerializer.Save (Int32 payloads): to `path`, or returns the bytes."""
+        lib = self._ctx._lib
+        if path is not None:
+            self._ctx.check(lib.slx_lattice_save_slat(self._h, str(path).encode()))
+            return None
+        size = ctypes.c_int64(0)
+        self._ctx.check(lib.slx_lattice_save_slat_mem(self._h, None, 0, ctypes.byref(size)))
+        buf = np.zeros(max(size.value, 1), np.uint8)
+        self._ctx.check(lib.slx_lattice_save_slat_mem(self._h, _p(buf, U8P), buf.size, ctypes.byref(size)))
+        return buf[: size.value].tobytes()
+
+    @classmethod
+    def load(cls, source, options: QuantizationOptions = VOCAB_LATTICE_OPTIONS,
+             ctx: Context | None = None) -> "EmbeddingLattice":
+        """SparseLatticeSerializer.Load (Int32 payloads) from a path or bytes: the occupants become the
+        rows (file order) with their tree; query ids are the payloads."""
+        self = cls.__new__(cls)
+        self._ctx = ctx or Context.default()
+        self.options = options
+        h = VP()
+        lib = self._ctx._lib
+        if isinstance(source, (bytes, bytearray, memoryview)):
+            buf = np.frombuffer(bytes(source), np.uint8).copy()
+            self._ctx.check(lib.slx_lattice_load_slat_mem(self._ctx._h, _p(buf, U8P) if buf.size else None, buf.size,
+                                                          options.zero_threshold, options.global_scale,
+                                                          ctypes.byref(h)))
+        else:
+            self._ctx.check(lib.slx_lattice_load_slat(self._ctx._h, str(source).encode(), options.zero_threshold,
+                                                      options.global_scale, ctypes.byref(h)))
+        self._h = h
+        info = np.zeros(3, np.int64)
+        lib.slx_lattice_info(h, _p(info, I64P), 3)
+        self.n, self.dim, self.id_base = int(info[0]), int(info[1]), int(info[2])
+        self.last_exact = 0
+        return self
+
     def close(self):
         if getattr(self, "_h", None):
             self._ctx._lib.slx_lattice_free(self._h)

@@ -51,6 +51,13 @@ SIGNATURES = {
     "slx_lattice_build_device": (i, [VP, VP, i64, i, f32, i64, i64, VP, ctypes.POINTER(VP)]),
     "slx_lattice_free": (i, [VP]),
     "slx_lattice_info": (i, [VP, I64P, i]),
+    "slx_lattice_build_tree": (i, [VP, i]),
+    "slx_lattice_tree_info": (i, [VP, I64P, i]),
+    "slx_lattice_tree_export": (i, [VP, I32P, I32P, I32P, I64P, I64P, I64P, I32P]),
+    "slx_lattice_save_slat": (i, [VP, ctypes.c_char_p]),
+    "slx_lattice_save_slat_mem": (i, [VP, U8P, i64, I64P]),
+    "slx_lattice_load_slat": (i, [VP, ctypes.c_char_p, f32, i64, ctypes.POINTER(VP)]),
+    "slx_lattice_load_slat_mem": (i, [VP, U8P, i64, f32, i64, ctypes.POINTER(VP)]),
     "slx_lattice_query_knn_l2": (i, [VP, F32P, i, i, i, I64P, U64P, ctypes.POINTER(i)]),
     "slx_lattice_query_knn_l2_device": (i, [VP, VP, i, i, i, VP, VP, ctypes.POINTER(i), VP]),
     "slx_knn_merge_device": (i, [VP, VP, VP, i, i, i, VP, VP, VP]),

@@ -419,6 +419,7 @@ struct MergeParams {
     const SideStats* qs;
     const SideStats* ds;
     int64_t n, id_base;
+    const int32_t* payload;  // ids are payload[row] when set, else id_base + row
     int64_t* out_ids;
     uint64_t* out_dist;
     int* fb_list;
@@ -502,7 +503,8 @@ __global__ void __launch_bounds__(MT) k_search_merge(MergeParams p) {
     if (p.mode == 1) {  // exact lists: keys are distance ^ 2^63
         if (tid < p.k) {
             const bool valid = sel_id[tid] != INT32_MAX;
-            p.out_ids[(size_t)q * p.k + tid] = valid ? p.id_base + sel_id[tid] : -1;
+            p.out_ids[(size_t)q * p.k + tid] =
+                valid ? (p.payload ? (int64_t)p.payload[sel_id[tid]] : p.id_base + sel_id[tid]) : -1;
             p.out_dist[(size_t)q * p.k + tid] = valid ? ((uint64_t)sel_key[tid] ^ (1ull << 63)) : UINT64_MAX;
         }
         return;
@@ -560,7 +562,7 @@ __global__ void __launch_bounds__(MT) k_search_merge(MergeParams p) {
         if (certified) {
             for (int j = 0; j < p.k; j++) {
                 const bool valid = j < nv;
-                p.out_ids[(size_t)q * p.k + j] = valid ? p.id_base + di[j] : -1;
+                p.out_ids[(size_t)q * p.k + j] = valid ? (p.payload ? (int64_t)p.payload[di[j]] : p.id_base + di[j]) : -1;
                 p.out_dist[(size_t)q * p.k + j] = valid ? dd[j] : UINT64_MAX;
             }
         } else {
@@ -667,7 +669,54 @@ int build(const float* d_vectors, int64_t n, int dim, float zero_threshold, int6
     return SLX_OK;
 }
 
+// Max |component| of int32 rows (the quantize kernel's statistic, for rows quantized elsewhere).
+__global__ void k_maxabs(const int32_t* __restrict__ v, int64_t total, SideStats* stats) {
+    unsigned long long mx = 0;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t x = v[i];
+        const unsigned long long a = (unsigned long long)(x < 0 ? -x : x);
+        mx = a > mx ? a : mx;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long w = __shfl_xor_sync(0xffffffffu, mx, o);
+        mx = w > mx ? w : mx;
+    }
+    if ((threadIdx.x & 31) == 0 && mx) atomicMax(&stats->max_abs, mx);
+}
+
+int build_quantized(const int32_t* d_rows, int64_t n, int dim, int64_t id_base, Lattice& L, cudaStream_t st,
+                    std::string& err) {
+    if (n < 0 || dim < 1 || dim > MAX_DIM || n > INT32_MAX - 256) { err = "lattice: bad shape"; return SLX_EINVAL; }
+    cudaGetDevice(&L.device);
+    L.n = n;
+    L.dim = dim;
+    L.dpad = (int)round_up(dim, BKB);
+    L.npad = round_up(std::max<int64_t>(n, 1), DBN);
+    L.id_base = id_base;
+    const size_t vbytes = (size_t)n * dim * 4, pbytes = (size_t)2 * L.npad * L.dpad;
+    if (cudaMalloc(&L.stats, sizeof(SideStats)) != cudaSuccess || cudaMalloc(&L.counters, 256) != cudaSuccess ||
+        cudaMalloc(&L.planes, pbytes) != cudaSuccess || cudaMalloc(&L.norm2, (size_t)L.npad * 8) != cudaSuccess ||
+        (vbytes && cudaMalloc(&L.vals, vbytes) != cudaSuccess)) {
+        cudaGetLastError();
+        err = "lattice: device allocation failed";
+        return SLX_EOOM;
+    }
+    cudaMemsetAsync(L.stats, 0, sizeof(SideStats), st);
+    cudaMemsetAsync(L.planes, 0, pbytes, st);
+    if (n > 0) {
+        cudaMemcpyAsync(L.vals, d_rows, vbytes, cudaMemcpyDeviceToDevice, st);
+        k_maxabs<<<grid_for(n * dim, 256), 256, 0, st>>>(L.vals, n * dim, L.stats);
+        k_split<<<(unsigned)((n + 7) / 8), 256, 0, st>>>(L.vals, n, dim, L.npad, L.dpad, L.planes, L.norm2, nullptr,
+                                                         nullptr, L.stats);
+    }
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) { err = cudaGetErrorString(e); return SLX_ECUDA; }
+    if (!tc::encode_planes(L.tmap, L.planes, L.dpad, L.npad, 2, DBN)) { err = "lattice: tensor map"; return SLX_ECUDA; }
+    return SLX_OK;
+}
+
 void release(Lattice& L) {
+    cudaFree(L.payload);
     cudaFree(L.vals);
     cudaFree(L.planes);
     cudaFree(L.norm2);
@@ -744,6 +793,7 @@ int query(Lattice& L, const float* d_q, int nq, int k, float zero_threshold, int
         mp.nslots = nslots; mp.k = k; mp.mode = 0; mp.ckey = ckey; mp.cid = cid; mp.qlist = nullptr;
         mp.qvals = qvals; mp.dvals = L.vals; mp.dim = dim; mp.qn2 = qn2; mp.qh2 = qh2; mp.ql2 = ql2;
         mp.qs = qs; mp.ds = L.stats; mp.n = L.n; mp.id_base = L.id_base; mp.out_ids = d_ids; mp.out_dist = d_dist;
+        mp.payload = L.payload;
         mp.fb_list = fb_list; mp.fb_count = L.counters;
         k_search_merge<<<(unsigned)nq, MT, 0, st>>>(mp);
         nl += 3;
@@ -783,7 +833,7 @@ int query(Lattice& L, const float* d_q, int nq, int k, float zero_threshold, int
             L.vals, L.n, dim, qvals, ql, rows_per, xslots, xkey, xid);
         MergeParams mp{};
         mp.nslots = xslots; mp.k = k; mp.mode = 1; mp.ckey = xkey; mp.cid = xid; mp.qlist = ql;
-        mp.n = L.n; mp.id_base = L.id_base; mp.out_ids = d_ids; mp.out_dist = d_dist;
+        mp.n = L.n; mp.id_base = L.id_base; mp.out_ids = d_ids; mp.out_dist = d_dist; mp.payload = L.payload;
         k_search_merge<<<(unsigned)nfb, MT, 0, st>>>(mp);
         nl += 2;
     }

@@ -25,6 +25,7 @@
 #include "slx_kernels.h"
 #include "slx_gemm.h"
 #include "slx_search.h"
+#include "slx_tree.h"
 #include "slx_vocab.h"
 
 using namespace slx;
@@ -1022,6 +1023,8 @@ struct slx_lattice {
     search::Lattice L;
     float zero_threshold = 0.001f;
     int64_t global_scale = 1000000000;
+    tree::Tree tree;         // KD tree over the rows (built by slx_lattice_build_tree or loaded)
+    bool has_tree = false;
 };
 
 slx_status slx_lattice_build_device(slx_ctx* ctx, const float* d_vectors, int64_t n, int dim, float zero_threshold,
@@ -1066,9 +1069,203 @@ slx_status slx_lattice_free(slx_lattice* lat) {
     if (!lat) return SLX_EINVAL;
     cudaSetDevice(lat->ctx->device);
     cudaStreamSynchronize(lat->ctx->stream);
+    tree::release(lat->tree);
     search::release(lat->L);
     delete lat;
     return SLX_OK;
+}
+
+// ---- KD tree and SLAT ------------------------------------------------------------------------
+
+slx_status slx_lattice_build_tree(slx_lattice* lat, int leaf_threshold) {
+    if (!lat) return SLX_EINVAL;
+    slx_ctx* ctx = lat->ctx;
+    if (leaf_threshold < 0) return set_err(ctx, SLX_EINVAL, "LeafThreshold must be >= 0");
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    std::string err;
+    int rc = 0;
+    lat->has_tree = false;
+    run_k(ctx, KC_SEARCH, (double)lat->L.n * lat->L.dim, 0, st, [&] {
+        int64_t nl = 0;
+        rc = tree::build(lat->L.vals, lat->L.n, lat->L.dim, leaf_threshold, lat->tree, st, err, &nl);
+        return (int)nl;
+    });
+    if (rc) return set_err(ctx, rc, "%s", err.c_str());
+    lat->has_tree = true;
+    return SLX_OK;
+}
+
+slx_status slx_lattice_tree_info(slx_lattice* lat, int64_t* info, int n) {
+    if (!lat || !info || n < 0) return SLX_EINVAL;
+    if (!lat->has_tree) return set_err(lat->ctx, SLX_EINVAL, "the lattice has no tree (slx_lattice_build_tree)");
+    const tree::Stats t = tree::stats(lat->tree);
+    const int64_t v[5] = {t.nodes, t.branches, t.leaves, t.occupants, t.max_depth};
+    for (int i = 0; i < n && i < 5; i++) info[i] = v[i];
+    return SLX_OK;
+}
+
+slx_status slx_lattice_tree_export(slx_lattice* lat, int32_t* kind, int32_t* mask, int32_t* dim, int64_t* val,
+                                   int64_t* start, int64_t* count, int32_t* perm) {
+    if (!lat) return SLX_EINVAL;
+    slx_ctx* ctx = lat->ctx;
+    if (!lat->has_tree) return set_err(ctx, SLX_EINVAL, "the lattice has no tree (slx_lattice_build_tree)");
+    const std::vector<int> order = tree::preorder(lat->tree);
+    for (size_t i = 0; i < order.size(); i++) {
+        const tree::Node& nd = lat->tree.nodes[order[i]];
+        if (kind) kind[i] = nd.kind;
+        if (mask) mask[i] = nd.mask;
+        if (dim) dim[i] = nd.dim;
+        if (val) val[i] = nd.val;
+        if (start) start[i] = nd.start;
+        if (count) count[i] = nd.count;
+    }
+    if (perm && lat->tree.n > 0) {
+        CK(cudaSetDevice(ctx->device));
+        CK(cudaMemcpyAsync(perm, lat->tree.perm, sizeof(int32_t) * lat->tree.n, cudaMemcpyDeviceToHost, ctx->stream));
+        CK(cudaStreamSynchronize(ctx->stream));
+    }
+    return SLX_OK;
+}
+
+static slx_status lattice_save(slx_lattice* lat, tree::Sink& sink) {
+    slx_ctx* ctx = lat->ctx;
+    if (!lat->has_tree)
+        return set_err(ctx, SLX_EINVAL, "Lattice must be frozen before serialization (slx_lattice_build_tree).");
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    const int64_t n = lat->L.n;
+    int32_t* d_pay = lat->L.payload;
+    int32_t* tmp = nullptr;
+    if (!d_pay && n > 0) {  // Int32 payloads: the row ids
+        if (lat->L.id_base < INT32_MIN || lat->L.id_base + n - 1 > INT32_MAX)
+            return set_err(ctx, SLX_EINVAL, "row ids id_base + row do not fit the Int32 payload");
+        std::vector<int32_t> ids((size_t)n);
+        for (int64_t i = 0; i < n; i++) ids[i] = (int32_t)(lat->L.id_base + i);
+        CK(cudaMalloc(&tmp, sizeof(int32_t) * n));
+        cudaMemcpyAsync(tmp, ids.data(), sizeof(int32_t) * n, cudaMemcpyHostToDevice, st);
+        d_pay = tmp;
+    }
+    std::string err;
+    int rc = 0;
+    run_k(ctx, KC_SEARCH, 0, 0, st, [&] {
+        int64_t nl = 0;
+        rc = tree::save(lat->tree, lat->L.vals, lat->L.dim, d_pay, sink, st, err, &nl);
+        return (int)nl;
+    });
+    cudaStreamSynchronize(st);
+    cudaFree(tmp);
+    if (rc) return set_err(ctx, rc, "%s", err.c_str());
+    return SLX_OK;
+}
+
+slx_status slx_lattice_save_slat(slx_lattice* lat, const char* path) {
+    if (!lat || !path) return lat ? set_err(lat->ctx, SLX_EINVAL, "null path") : SLX_EINVAL;
+    FILE* f = fopen(path, "wb");
+    if (!f) return set_err(lat->ctx, SLX_ENOTFOUND, "cannot open %s for writing", path);
+    tree::Sink sink;
+    sink.f = f;
+    slx_status rc = lattice_save(lat, sink);
+    if (fclose(f) != 0 && rc == SLX_OK) rc = set_err(lat->ctx, SLX_EINVAL, "write to %s failed", path);
+    return rc;
+}
+
+slx_status slx_lattice_save_slat_mem(slx_lattice* lat, uint8_t* out, int64_t cap, int64_t* size) {
+    if (!lat || !size || cap < 0) return lat ? set_err(lat->ctx, SLX_EINVAL, "bad arguments") : SLX_EINVAL;
+    std::vector<uint8_t> buf;
+    tree::Sink sink;
+    sink.buf = &buf;
+    slx_status rc = lattice_save(lat, sink);
+    if (rc) return rc;
+    *size = (int64_t)buf.size();
+    if (out) {
+        if (cap < (int64_t)buf.size())
+            return set_err(lat->ctx, SLX_EINVAL, "output buffer of %lld bytes, %lld needed", (long long)cap,
+                           (long long)buf.size());
+        memcpy(out, buf.data(), buf.size());
+    }
+    return SLX_OK;
+}
+
+static slx_status lattice_load(slx_ctx* ctx, const uint8_t* bytes, int64_t n, float zero_threshold,
+                               int64_t global_scale, slx_lattice** out) {
+    tree::Loaded ld;
+    std::string err;
+    int rc = tree::parse(bytes, n, ld, err);
+    if (rc) return set_err(ctx, rc, "%s", err.c_str());
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    std::unique_ptr<slx_lattice> lat(new slx_lattice());
+    lat->ctx = ctx;
+    lat->zero_threshold = zero_threshold;
+    lat->global_scale = global_scale;
+    const int64_t rows = (int64_t)ld.payload.size();
+    const int dim = ld.dim > 0 ? ld.dim : 1;
+    int32_t* d_rows = nullptr;
+    if (rows > 0) {
+        if (cudaMalloc(&d_rows, sizeof(int32_t) * rows * dim) != cudaSuccess) {
+            cudaGetLastError();
+            return set_err(ctx, SLX_EOOM, "device allocation failed");
+        }
+        cudaMemcpyAsync(d_rows, ld.rows.data(), sizeof(int32_t) * rows * dim, cudaMemcpyHostToDevice, st);
+    }
+    rc = search::build_quantized(d_rows, rows, dim, 0, lat->L, st, err);
+    cudaFree(d_rows);
+    if (rc) {
+        search::release(lat->L);
+        return set_err(ctx, rc, "%s", err.c_str());
+    }
+    if (rows > 0) ctx->launches += 2;
+    if (rows > 0 && cudaMalloc(&lat->L.payload, sizeof(int32_t) * rows) != cudaSuccess) {
+        cudaGetLastError();
+        search::release(lat->L);
+        return set_err(ctx, SLX_EOOM, "device allocation failed");
+    }
+    if (rows > 0) cudaMemcpyAsync(lat->L.payload, ld.payload.data(), sizeof(int32_t) * rows, cudaMemcpyHostToDevice, st);
+    // the tree as read; occupants are stored in file order, so leaf order is the identity
+    lat->tree.nodes = std::move(ld.nodes);
+    lat->tree.root = ld.root;
+    lat->tree.n = rows;
+    if (cudaMalloc(&lat->tree.perm, sizeof(int32_t) * (size_t)std::max<int64_t>(rows, 1)) != cudaSuccess) {
+        cudaGetLastError();
+        search::release(lat->L);
+        return set_err(ctx, SLX_EOOM, "device allocation failed");
+    }
+    if (rows > 0) {
+        std::vector<int32_t> id((size_t)rows);
+        for (int64_t i = 0; i < rows; i++) id[i] = (int32_t)i;
+        cudaMemcpyAsync(lat->tree.perm, id.data(), sizeof(int32_t) * rows, cudaMemcpyHostToDevice, st);
+    }
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        tree::release(lat->tree);
+        search::release(lat->L);
+        return set_err(ctx, SLX_ECUDA, "%s", cudaGetErrorString(e));
+    }
+    lat->has_tree = true;
+    *out = lat.release();
+    return SLX_OK;
+}
+
+slx_status slx_lattice_load_slat_mem(slx_ctx* ctx, const uint8_t* bytes, int64_t n, float zero_threshold,
+                                     int64_t global_scale, slx_lattice** out) {
+    if (!ctx || !out || n < 0 || (n > 0 && !bytes)) return set_err(ctx, SLX_EINVAL, "bad arguments");
+    *out = nullptr;
+    return lattice_load(ctx, bytes, n, zero_threshold, global_scale, out);
+}
+
+slx_status slx_lattice_load_slat(slx_ctx* ctx, const char* path, float zero_threshold, int64_t global_scale,
+                                 slx_lattice** out) {
+    if (!ctx || !out || !path) return set_err(ctx, SLX_EINVAL, "bad arguments");
+    *out = nullptr;
+    FILE* f = fopen(path, "rb");
+    if (!f) return set_err(ctx, SLX_ENOTFOUND, "Could not find file '%s'.", path);
+    std::vector<uint8_t> bytes;
+    uint8_t chunk[1 << 16];
+    size_t got;
+    while ((got = fread(chunk, 1, sizeof chunk, f)) > 0) bytes.insert(bytes.end(), chunk, chunk + got);
+    fclose(f);
+    return lattice_load(ctx, bytes.data(), (int64_t)bytes.size(), zero_threshold, global_scale, out);
 }
 
 slx_status slx_lattice_info(slx_lattice* lat, int64_t* info, int n) {

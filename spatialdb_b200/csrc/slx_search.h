@@ -35,6 +35,7 @@ struct Lattice {
     int64_t n = 0, npad = 0, id_base = 0;
     int dim = 0, dpad = 0;
     int32_t* vals = nullptr;     // [n][dim] quantized components
+    int32_t* payload = nullptr;  // [n] ids of a lattice loaded from SLAT (query ids are payload[row])
     int8_t* planes = nullptr;    // [2][npad][dpad] balanced base-256 digits of the high parts
     uint64_t* norm2 = nullptr;   // [n] sum of squares
     SideStats* stats = nullptr;  // device
@@ -50,6 +51,9 @@ struct Lattice {
 // Builds the lattice from n float rows of dim components on the device. Returns 0 or an slx status.
 int build(const float* d_vectors, int64_t n, int dim, float zero_threshold, int64_t global_scale, int64_t id_base,
           Lattice& L, cudaStream_t st, std::string& err);
+// The same from rows already quantized to int32 (device [n][dim], copied).
+int build_quantized(const int32_t* d_rows, int64_t n, int dim, int64_t id_base, Lattice& L, cudaStream_t st,
+                    std::string& err);
 void release(Lattice& L);
 
 // k nearest rows for nq float queries: ids [nq][k] (id_base + row; -1 past the database) and
