@@ -386,6 +386,12 @@ def search_bench(ctx, torch, stream, world: int, rank: int, dist, steps: int = 3
             rq = oracle.quantize_dense(rv, 0.001, 1_000_000_000)
             ok &= all(oracle.distance_sq_l2_fast(qv, rq[j]) == int(dd_l[qi, j]) for j in range(k))
         checks["oracle_distances_of_returned_rows"] = bool(ok)
+    tree_res = None
+    if rank == 0 and world == 1:
+        try:
+            tree_res = tree_bench(ctx, torch, stream, lat, rows, cpu=cpu)
+        except Exception as e:  # reported, never silently dropped
+            tree_res = {"error": repr(e)}
     del rows
     lat.close()
     torch.cuda.empty_cache()
@@ -409,9 +415,58 @@ def search_bench(ctx, torch, stream, world: int, rank: int, dist, steps: int = 3
             "checks": checks,
             "scaling": "strong (fixed database, rows sharded over the GPUs)",
         }
+        if tree_res is not None:
+            res["kd_tree"] = tree_res
         if cpu and world == 1:
             res["cpu_baseline"] = search_cpu_baseline()
     return res
+
+
+def tree_bench(ctx, torch, stream, lat, rows, sub: int = 100_000, cpu: bool = True) -> dict:
+    """KD-tree lattice (EmbeddingLatticeBuilder, leaf threshold 16) over the whole search database on
+    the device, then over its first `sub` rows: device build and SLAT save (Int32 payloads) timed,
+    the tree checked node for node against the oracle's, and the oracle's build timed on the same
+    rows (one host thread) as the CPU baseline."""
+    import numpy as np
+
+    import oracle
+    import spatialdb_b200 as slx
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    lat.freeze(16)
+    full_s = time.perf_counter() - t0
+    out = {"rows": int(lat.n), "dim": int(lat.dim), "leaf_threshold": 16, "build_s": full_s,
+           "stats": lat.collect_stats()}
+    small = slx.EmbeddingLattice.from_device(rows[:sub].data_ptr(), sub, lat.dim, stream=stream.cuda_stream, ctx=ctx)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    small.freeze(16)
+    sub_s = time.perf_counter() - t0
+    import tempfile
+
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "subset.slat")
+        small.save(path)  # warm: pinned staging, page cache
+        t0 = time.perf_counter()
+        small.save(path)
+        save_s = time.perf_counter() - t0
+        nbytes = os.path.getsize(path)
+    out["subset"] = {"rows": sub, "build_s": sub_s, "save_s": save_s, "slat_bytes": nbytes,
+                     "save_gbs": nbytes / save_s / 1e9, "save_to": "a file (SparseLatticeSerializer.Save to a stream)"}
+    got = small.tree()
+    q = oracle.quantize_dense(rows[:sub].cpu().numpy())
+    t0 = time.perf_counter()
+    want = oracle.tree_build(q, 16)
+    cpu_s = time.perf_counter() - t0
+    same = all(bool(np.array_equal(got[k], want[k])) for k in ("kind", "mask", "dim", "val", "start", "count"))
+    same &= bool(np.array_equal(got["perm"].astype(np.int64), want["perm"]))
+    out["subset"]["parity_tree_equals_oracle"] = same
+    if cpu:
+        out["subset"]["cpu_baseline"] = {"value": cpu_s, "unit": "s per build", "cores": 1, "kind": "port",
+                                         "sample": f"the first {sub} rows x {lat.dim}"}
+    small.close()
+    return out
 
 
 def search_cpu_baseline(sample_rows: int = 200_000, sample_queries: int = 4) -> dict:

@@ -402,9 +402,11 @@ class EmbeddingLattice:
             return None
         size = ctypes.c_int64(0)
         self._ctx.check(lib.slx_lattice_save_slat_mem(self._h, None, 0, ctypes.byref(size)))
-        buf = np.zeros(max(size.value, 1), np.uint8)
-        self._ctx.check(lib.slx_lattice_save_slat_mem(self._h, _p(buf, U8P), buf.size, ctypes.byref(size)))
-        return buf[: size.value].tobytes()
+        buf = bytearray(max(size.value, 1))
+        ptr = (ctypes.c_uint8 * len(buf)).from_buffer(buf)
+        self._ctx.check(lib.slx_lattice_save_slat_mem(self._h, ctypes.cast(ptr, U8P), len(buf), ctypes.byref(size)))
+        del ptr
+        return bytes(buf) if size.value == len(buf) else bytes(buf[: size.value])
 
     @classmethod
     def load(cls, source, options: QuantizationOptions = VOCAB_LATTICE_OPTIONS,

@@ -461,11 +461,14 @@ void Sink::write(const void* p, size_t n) {
     if (!ok || n == 0) return;
     if (f) {
         ok = fwrite(p, 1, n, f) == n;
-    } else if (buf) {
-        const size_t o = buf->size();
-        buf->resize(o + n);
-        memcpy(buf->data() + o, p, n);
+    } else if (mem) {
+        if (used + n > cap) {
+            ok = false;
+            return;
+        }
+        memcpy(mem + used, p, n);
     }
+    used += n;
 }
 
 void release(Tree& t) {
@@ -658,6 +661,34 @@ Stats stats(const Tree& t) {
     return s;
 }
 
+int slat_size(const Tree& t, const int32_t* d_vals, int dim, int64_t* size, cudaStream_t st, std::string& err,
+              int64_t* launches) {
+    int64_t total = 6;
+    for (const Node& nd : t.nodes) total += nd.kind == 1 ? 12 : 5;
+    if (t.n > 0) {
+        int64_t* d_size = nullptr;
+        if (cudaMalloc(&d_size, sizeof(int64_t) * t.n) != cudaSuccess) {
+            cudaGetLastError();
+            err = "slat: device allocation failed";
+            return SLX_EOOM;
+        }
+        k_rec_sizes<<<(unsigned)std::min<int64_t>((t.n + 7) / 8, 148 * 32), 256, 0, st>>>(d_vals, dim, t.perm, 0, t.n,
+                                                                                          d_size);
+        std::vector<int64_t> h((size_t)t.n);
+        cudaMemcpyAsync(h.data(), d_size, sizeof(int64_t) * t.n, cudaMemcpyDeviceToHost, st);
+        const cudaError_t e = cudaStreamSynchronize(st);
+        cudaFree(d_size);
+        if (e != cudaSuccess) {
+            err = cudaGetErrorString(e);
+            return SLX_ECUDA;
+        }
+        for (int64_t v : h) total += v;
+        if (launches) *launches += 1;
+    }
+    *size = total;
+    return SLX_OK;
+}
+
 int save(const Tree& t, const int32_t* d_vals, int dim, const int32_t* d_payload, Sink& out, cudaStream_t st,
          std::string& err, int64_t* launches, size_t batch_bytes) {
     const int64_t n = t.n;
@@ -702,13 +733,15 @@ int save(const Tree& t, const int32_t* d_vals, int dim, const int32_t* d_payload
         max_batch = std::max(max_batch, bytes);
         max_count = std::max(max_count, bstart[b + 1] - bstart[b]);
     }
-    std::vector<uint8_t> host;
+    uint8_t* host = nullptr;  // pinned staging of one batch of records
     std::vector<int64_t> off;
     if (n > 0) {
         if (cudaMalloc(&d_buf, (size_t)std::max<int64_t>(max_batch, 1)) != cudaSuccess ||
-            cudaMalloc(&d_off, sizeof(int64_t) * (size_t)std::max<int64_t>(max_count, 1)) != cudaSuccess)
-            return fail(SLX_EOOM, "slat: device allocation failed");
-        host.resize((size_t)max_batch);
+            cudaMalloc(&d_off, sizeof(int64_t) * (size_t)std::max<int64_t>(max_count, 1)) != cudaSuccess ||
+            cudaMallocHost(&host, (size_t)std::max<int64_t>(max_batch, 1)) != cudaSuccess) {
+            cudaFreeHost(host);
+            return fail(SLX_EOOM, "slat: allocation failed");
+        }
         off.resize((size_t)max_count);
     }
     size_t cur = 0;          // batch index loaded in `host`
@@ -726,7 +759,7 @@ int save(const Tree& t, const int32_t* d_vals, int dim, const int32_t* d_payload
         k_rec_write<<<(unsigned)std::min<int64_t>((bp1 - bp0 + 7) / 8, 148 * 32), 256, 0, st>>>(
             d_vals, dim, t.perm, d_payload, bp0, bp1, d_off, d_buf);
         nl++;
-        cudaMemcpyAsync(host.data(), d_buf, (size_t)acc, cudaMemcpyDeviceToHost, st);
+        cudaMemcpyAsync(host, d_buf, (size_t)acc, cudaMemcpyDeviceToHost, st);
         if (cudaStreamSynchronize(st) != cudaSuccess) return SLX_ECUDA;
         cur = b;
         loaded = true;
@@ -759,18 +792,22 @@ int save(const Tree& t, const int32_t* d_vals, int dim, const int32_t* d_payload
             if (!loaded || p >= bp1) {
                 size_t b = loaded ? cur + 1 : 0;
                 while (bstart[b + 1] <= p) b++;
-                if (load_batch(b)) return fail(SLX_ECUDA, "slat: record kernel failed");
+                if (load_batch(b)) {
+                    cudaFreeHost(host);
+                    return fail(SLX_ECUDA, "slat: record kernel failed");
+                }
             }
             const int64_t q = std::min(end, bp1);
             const int64_t from = off[p - bp0];
             const int64_t to = q < bp1 ? off[q - bp0] : off[bp1 - 1 - bp0] + size[bp1 - 1];
-            out.write(host.data() + from, (size_t)(to - from));
+            out.write(host + from, (size_t)(to - from));
             p = q;
         }
     }
     cudaFree(d_size);
     cudaFree(d_buf);
     cudaFree(d_off);
+    cudaFreeHost(host);
     if (launches) *launches += nl;
     if (!out.ok) {
         err = "slat: write failed";

@@ -1172,19 +1172,23 @@ slx_status slx_lattice_save_slat(slx_lattice* lat, const char* path) {
 
 slx_status slx_lattice_save_slat_mem(slx_lattice* lat, uint8_t* out, int64_t cap, int64_t* size) {
     if (!lat || !size || cap < 0) return lat ? set_err(lat->ctx, SLX_EINVAL, "bad arguments") : SLX_EINVAL;
-    std::vector<uint8_t> buf;
+    slx_ctx* ctx = lat->ctx;
+    if (!lat->has_tree)
+        return set_err(ctx, SLX_EINVAL, "Lattice must be frozen before serialization (slx_lattice_build_tree).");
+    CK(cudaSetDevice(ctx->device));
+    std::string err;
+    int64_t need = 0, nl = 0;
+    int rc = tree::slat_size(lat->tree, lat->L.vals, lat->L.dim, &need, ctx->stream, err, &nl);
+    ctx->launches += nl;
+    if (rc) return set_err(ctx, rc, "%s", err.c_str());
+    *size = need;
+    if (!out) return SLX_OK;
+    if (cap < need)
+        return set_err(ctx, SLX_EINVAL, "output buffer of %lld bytes, %lld needed", (long long)cap, (long long)need);
     tree::Sink sink;
-    sink.buf = &buf;
-    slx_status rc = lattice_save(lat, sink);
-    if (rc) return rc;
-    *size = (int64_t)buf.size();
-    if (out) {
-        if (cap < (int64_t)buf.size())
-            return set_err(lat->ctx, SLX_EINVAL, "output buffer of %lld bytes, %lld needed", (long long)cap,
-                           (long long)buf.size());
-        memcpy(out, buf.data(), buf.size());
-    }
-    return SLX_OK;
+    sink.mem = out;
+    sink.cap = (size_t)cap;
+    return lattice_save(lat, sink);
 }
 
 static slx_status lattice_load(slx_ctx* ctx, const uint8_t* bytes, int64_t n, float zero_threshold,

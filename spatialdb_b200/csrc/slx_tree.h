@@ -39,13 +39,18 @@ Stats stats(const Tree& t);
 // Nodes in pre-order (the serializer's order).
 std::vector<int> preorder(const Tree& t);
 
-// Byte sink for the SLAT writer: a file or a growing buffer.
+// Byte sink for the SLAT writer: a file or a caller buffer of `cap` bytes.
 struct Sink {
     FILE* f = nullptr;
-    std::vector<uint8_t>* buf = nullptr;
+    uint8_t* mem = nullptr;
+    size_t cap = 0, used = 0;
     bool ok = true;
     void write(const void* p, size_t n);
 };
+
+// Size in bytes of the tree's SLAT serialization (record sizes counted on the device).
+int slat_size(const Tree& t, const int32_t* d_vals, int dim, int64_t* size, cudaStream_t st, std::string& err,
+              int64_t* launches);
 
 // SparseLatticeSerializer.Save with Int32 payloads: occupant records are produced on the device
 // (rows d_vals in leaf order, nonzero components ascending, payload[row]) in batches of at most
