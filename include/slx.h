@@ -37,6 +37,9 @@ typedef int slx_status;
 #define SLX_MODEL_ENCODER 0       /* IntegerTransformerSource (nomic-bert / bert) */
 #define SLX_MODEL_CAUSAL 1        /* IntegerCausalSource (gemma*) */
 #define SLX_MODEL_GEMMA_ENCODER 2 /* IntegerGemmaSource (gemma*, non-causal, mean pooled) */
+#define SLX_MODEL_FLOAT_ENCODER 3 /* TransformerEmbeddingSource (nomic-bert / bert), the fp32 twin: slx_encode
+                                     fills l2 only (pooled_q30 must be NULL); agrees with the reference to
+                                     fp32 rounding (SIMD dot order), not bit for bit */
 
 typedef struct slx_ctx slx_ctx;
 typedef struct slx_model slx_model;

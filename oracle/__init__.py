@@ -108,6 +108,9 @@ def _sig(lib):
     f("slxo_slat_tree", VP, VP)
     f("slxo_slat_rows", None, VP, I64P, I32P)
     f("slxo_slat_free", None, VP)
+    f("slxo_float_encoder_load", VP, ctypes.c_char_p, ctypes.POINTER(i))
+    f("slxo_float_encoder_free", None, VP)
+    f("slxo_float_encoder_forward", i, VP, I32P, i, F32P)
 
 
 def lib():
@@ -581,3 +584,33 @@ def slat_load(data: bytes) -> dict:
         return out
     finally:
         lib().slxo_slat_free(h)
+
+
+class FloatEncoder:
+    """TransformerEmbeddingSource (Gguf/TransformerEmbeddingSource.cs): the fp32 twin of the encoder."""
+
+    def __init__(self, path: str):
+        st = ctypes.c_int(0)
+        self._h = lib().slxo_float_encoder_load(path.encode(), ctypes.byref(st))
+        if not self._h:
+            raise OracleError(st.value, f"float encoder load {path}")
+        g = Gguf(path)
+        try:
+            self.embd = g.info()["embd"]
+        finally:
+            g.close()
+
+    def close(self):
+        if self._h:
+            lib().slxo_float_encoder_free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def forward(self, ids) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int32).reshape(-1)
+        out = np.zeros(self.embd, np.float32)
+        st = lib().slxo_float_encoder_forward(self._h, _p(ids, I32P), ids.size, _p(out, F32P))
+        if st:
+            raise OracleError(st, "float encoder forward")
+        return out

@@ -1578,6 +1578,178 @@ static void tree_export(const Tree& t, int32_t* kind, int32_t* mask, int32_t* di
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// TransformerEmbeddingSource: the float twin of the encoder (Gguf/TransformerEmbeddingSource.cs).
+// Weights are the GGUF tensors read as float (ReadTensorF32, :514-557); the forward (:124-141)
+// runs BuildEmbeddings (:144-163), LayerNorm with eps 1e-12 (:380-408; the GGUF epsilon is read
+// but unused), the blocks (:166-211: QKV, float RoPE from a 512-row cache :227-275, attention
+// :337-378 with MathF.Exp softmax :440-460, O, residual, LayerNorm, SiLU-gated FFN :461, residual,
+// LayerNorm), MeanPool over all rows (:474-491) and L2Normalize (:493-503). The reference's dots
+// are Vector<float> SIMD (lane order machine-dependent); here they are sequential fp32 with separate
+// multiply and add, so the restatement agrees with the reference to rounding, not bit for bit.
+struct FloatLayer { std::vector<float> qkv, o, anw, anb, up, gate, down, lnw, lnb; };
+struct FloatEncoder {
+    int embd = 0, heads = 0, layers = 0, ff = 0, unk = 0;
+    std::vector<float> tok, tt, enw, enb, cs, sn;
+    std::vector<FloatLayer> L;
+};
+
+static FloatEncoder* float_encoder_load(const char* path, int* status) {
+    std::unique_ptr<Gguf> g(gguf_open(path, status));
+    if (!g) return nullptr;
+    std::string al = g->arch;
+    std::transform(al.begin(), al.end(), al.begin(), ::tolower);
+    if (al != "nomic-bert" && al != "bert") { *status = SLXO_EUNSUPPORTED; return nullptr; }
+    std::unique_ptr<FloatEncoder> e(new FloatEncoder());
+    e->embd = g->embd; e->heads = g->heads; e->layers = g->layers; e->ff = g->ff;
+    const float base = meta_float(*g, g->arch + ".rope.freq_base", 10000.0f);
+    int st;
+    if ((st = gguf_read_f32(g.get(), "token_embd.weight", e->tok))) { *status = st; return nullptr; }
+    std::vector<float> tt;
+    if ((st = gguf_read_f32(g.get(), "token_types.weight", tt))) { *status = st; return nullptr; }
+    if ((int64_t)tt.size() < e->embd) { *status = SLXO_EINVAL; return nullptr; }
+    e->tt.assign(tt.begin(), tt.begin() + e->embd);
+    if ((st = gguf_read_f32(g.get(), "token_embd_norm.weight", e->enw))) { *status = st; return nullptr; }
+    if ((st = gguf_read_f32(g.get(), "token_embd_norm.bias", e->enb))) { *status = st; return nullptr; }
+    e->L.resize(e->layers);
+    for (int i = 0; i < e->layers; i++) {
+        std::string p = "blk." + std::to_string(i);
+        FloatLayer& l = e->L[i];
+        const char* names[9] = {".attn_qkv.weight", ".attn_output.weight", ".attn_output_norm.weight",
+                                ".attn_output_norm.bias", ".ffn_up.weight", ".ffn_gate.weight", ".ffn_down.weight",
+                                ".layer_output_norm.weight", ".layer_output_norm.bias"};
+        std::vector<float>* dst[9] = {&l.qkv, &l.o, &l.anw, &l.anb, &l.up, &l.gate, &l.down, &l.lnw, &l.lnb};
+        for (int j = 0; j < 9; j++)
+            if ((st = gguf_read_f32(g.get(), p + names[j], *dst[j]))) { *status = st; return nullptr; }
+    }
+    if (g->n_tokens == 0) { *status = SLXO_EINVAL; return nullptr; }
+    e->unk = g->unk;
+    // RopeCache (:227-252): theta = (float)Pow(base, -2i/hd), angle = t * theta in double.
+    const int hd = e->embd / e->heads, half = hd / 2;
+    e->cs.resize((size_t)512 * half);
+    e->sn.resize((size_t)512 * half);
+    for (int t = 0; t < 512; t++)
+        for (int i = 0; i < half; i++) {
+            const float theta = (float)std::pow((double)base, -2.0 * i / hd);
+            const double angle = t * (double)theta;
+            e->cs[(size_t)t * half + i] = (float)std::cos(angle);
+            e->sn[(size_t)t * half + i] = (float)std::sin(angle);
+        }
+    *status = SLXO_OK;
+    return e.release();
+}
+
+static float fdot(const float* a, const float* b, int n) {
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s = s + a[i] * b[i];
+    return s;
+}
+
+static void f_matmul(const float* a, int rows, int nin, const float* w, int nout, float* c) {
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; r++)
+        for (int o = 0; o < nout; o++) c[(size_t)r * nout + o] = fdot(a + (size_t)r * nin, w + (size_t)o * nin, nin);
+}
+
+static void f_layernorm(float* x, int T, int d, const float* w, const float* b) {
+    for (int t = 0; t < T; t++) {
+        float* r = x + (size_t)t * d;
+        float mean = 0.0f;
+        for (int j = 0; j < d; j++) mean += r[j];
+        mean /= d;
+        float var = 0.0f;
+        for (int j = 0; j < d; j++) {
+            const float dl = r[j] - mean;
+            var += dl * dl;
+        }
+        var /= d;
+        const float inv = 1.0f / std::sqrt(var + 1e-12f);
+        for (int j = 0; j < d; j++) r[j] = (r[j] - mean) * inv * w[j] + b[j];
+    }
+}
+
+static int float_encoder_forward(const FloatEncoder& e, const int32_t* ids, int T, float* out) {
+    const int d = e.embd, H = e.heads, hd = d / H, half = hd / 2, F = e.ff;
+    if (T > 512) return SLXO_ERANGE;  // the 512-row RoPE cache
+    std::vector<float> x((size_t)T * d);
+    for (int t = 0; t < T; t++) {
+        int64_t src = (int64_t)ids[t] * d;
+        if (ids[t] < 0 || src + d > (int64_t)e.tok.size()) src = (int64_t)e.unk * d;
+        for (int j = 0; j < d; j++) x[(size_t)t * d + j] = e.tok[src + j] + e.tt[j];
+    }
+    f_layernorm(x.data(), T, d, e.enw.data(), e.enb.data());
+    std::vector<float> qkv((size_t)T * 3 * d), q((size_t)T * d), k((size_t)T * d), v((size_t)T * d), att((size_t)T * d),
+        proj((size_t)T * d), up((size_t)T * F), gate((size_t)T * F), down((size_t)T * d), sc((size_t)T * T);
+    for (int l = 0; l < e.layers; l++) {
+        const FloatLayer& L = e.L[l];
+        f_matmul(x.data(), T, d, L.qkv.data(), 3 * d, qkv.data());
+        for (int t = 0; t < T; t++)
+            for (int j = 0; j < d; j++) {
+                q[(size_t)t * d + j] = qkv[(size_t)t * 3 * d + j];
+                k[(size_t)t * d + j] = qkv[(size_t)t * 3 * d + d + j];
+                v[(size_t)t * d + j] = qkv[(size_t)t * 3 * d + 2 * d + j];
+            }
+        for (float* m : {q.data(), k.data()})
+            for (int t = 0; t < T; t++)
+                for (int h = 0; h < H; h++)
+                    for (int i = 0; i < half; i++) {
+                        const float c = e.cs[(size_t)t * half + i], s_ = e.sn[(size_t)t * half + i];
+                        float* p = m + (size_t)t * d + h * hd;
+                        const float x0 = p[i], x1 = p[i + half];
+                        p[i] = x0 * c - x1 * s_;
+                        p[i + half] = x0 * s_ + x1 * c;
+                    }
+        const float scale = 1.0f / std::sqrt((float)hd);
+        std::fill(att.begin(), att.end(), 0.0f);
+        for (int h = 0; h < H; h++) {
+            for (int t = 0; t < T; t++)
+                for (int s2 = 0; s2 < T; s2++)
+                    sc[(size_t)t * T + s2] = fdot(&q[(size_t)t * d + h * hd], &k[(size_t)s2 * d + h * hd], hd) * scale;
+            for (int t = 0; t < T; t++) {
+                float* r = &sc[(size_t)t * T];
+                float mx = r[0];
+                for (int s2 = 1; s2 < T; s2++) mx = r[s2] > mx ? r[s2] : mx;
+                float sum = 0.0f;
+                for (int s2 = 0; s2 < T; s2++) {
+                    r[s2] = std::exp(r[s2] - mx);
+                    sum += r[s2];
+                }
+                const float inv = 1.0f / sum;
+                for (int s2 = 0; s2 < T; s2++) r[s2] *= inv;
+            }
+            for (int t = 0; t < T; t++)
+                for (int s2 = 0; s2 < T; s2++) {
+                    const float w = sc[(size_t)t * T + s2];
+                    for (int j = 0; j < hd; j++) att[(size_t)t * d + h * hd + j] += w * v[(size_t)s2 * d + h * hd + j];
+                }
+        }
+        f_matmul(att.data(), T, d, L.o.data(), d, proj.data());
+        for (size_t i = 0; i < proj.size(); i++) proj[i] += x[i];
+        f_layernorm(proj.data(), T, d, L.anw.data(), L.anb.data());
+        f_matmul(proj.data(), T, d, L.up.data(), F, up.data());
+        f_matmul(proj.data(), T, d, L.gate.data(), F, gate.data());
+        for (size_t i = 0; i < up.size(); i++) up[i] *= gate[i] / (1.0f + std::exp(-gate[i]));
+        f_matmul(up.data(), T, F, L.down.data(), d, down.data());
+        for (size_t i = 0; i < down.size(); i++) down[i] += proj[i];
+        f_layernorm(down.data(), T, d, L.lnw.data(), L.lnb.data());
+        x.swap(down);
+    }
+    std::vector<float> pooled((size_t)d, 0.0f);
+    for (int t = 0; t < T; t++)
+        for (int j = 0; j < d; j++) pooled[j] += x[(size_t)t * d + j];
+    const float inv = 1.0f / T;
+    for (int j = 0; j < d; j++) pooled[j] *= inv;
+    float norm = 0.0f;
+    for (int j = 0; j < d; j++) norm += pooled[j] * pooled[j];
+    norm = std::sqrt(norm);
+    if (norm >= 1e-10f) {
+        const float in = 1.0f / norm;
+        for (int j = 0; j < d; j++) pooled[j] *= in;
+    }
+    memcpy(out, pooled.data(), sizeof(float) * d);
+    return SLXO_OK;
+}
+
 extern "C" {
 
 int slxo_set_threads(int n) {
@@ -1869,4 +2041,11 @@ void slxo_slat_rows(void* h, int64_t* rows, int32_t* payload) {
     memcpy(payload, L->payload.data(), L->payload.size() * sizeof(int32_t));
 }
 void slxo_slat_free(void* h) { delete (SlatLoaded*)h; }
+
+// ---- float encoder twin (test oracle) ---------------------------------------------------------
+void* slxo_float_encoder_load(const char* path, int* status) { return float_encoder_load(path, status); }
+void slxo_float_encoder_free(void* h) { delete (FloatEncoder*)h; }
+int slxo_float_encoder_forward(void* h, const int32_t* ids, int T, float* out) {
+    return float_encoder_forward(*(FloatEncoder*)h, ids, T, out);
+}
 }  // extern "C"

@@ -24,7 +24,7 @@ from ._lib import I32P, I64P, F32P, U8P, U64P, VP
 
 (SLX_OK, SLX_EINVAL, SLX_EFORMAT, SLX_ENOTFOUND, SLX_EUNSUPPORTED, SLX_EEOF, SLX_ERANGE, SLX_EOOM, SLX_ECUDA, SLX_ETIMEOUT,
  SLX_ESCRATCH) = range(11)
-MODEL_ENCODER, MODEL_CAUSAL, MODEL_GEMMA_ENCODER = 0, 1, 2
+MODEL_ENCODER, MODEL_CAUSAL, MODEL_GEMMA_ENCODER, MODEL_FLOAT_ENCODER = 0, 1, 2, 3
 
 
 class SlxError(RuntimeError):
@@ -222,6 +222,21 @@ class IntegerTransformerSource(_Encoder):
 class IntegerGemmaSource(_Encoder):
     """Gemma integer encoder, non-causal GQA, mean pooled (IntegerGemmaSource)."""
     kind = MODEL_GEMMA_ENCODER
+
+
+class TransformerEmbeddingSource(_Model):
+    """nomic-bert / bert encoder in fp32 (TransformerEmbeddingSource, Gguf/TransformerEmbeddingSource.cs):
+    the float twin of IntegerTransformerSource. Agrees with the reference to fp32 rounding (its SIMD
+    dot order is machine-dependent), not bit for bit."""
+    kind = MODEL_FLOAT_ENCODER
+
+    def forward(self, ids) -> np.ndarray:
+        """Forward / EmbedBatchAsync on token ids [B, T] (or [T]): L2-normalised float embeddings [B, embd]."""
+        ids = np.ascontiguousarray(np.atleast_2d(ids), np.int32)
+        B, T = ids.shape
+        out = np.empty((B, self.embd), np.float32)
+        self.ctx.check(self.ctx._lib.slx_encode(self._h, _p(ids, I32P), B, T, None, _p(out, F32P)))
+        return out
 
 
 class IntegerCausalSource(_Model):

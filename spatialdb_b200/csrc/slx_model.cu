@@ -27,6 +27,7 @@
 #include "slx_search.h"
 #include "slx_tree.h"
 #include "slx_vocab.h"
+#include "slx_float.h"
 
 using namespace slx;
 
@@ -157,9 +158,12 @@ struct slx_model {
     GemmWorkspace gws;
     vocab::Lattice vlat;             // VocabLattice of the causal head, built on first use
     bool vlat_ready = false;
+    fenc::Model fm;                  // SLX_MODEL_FLOAT_ENCODER: fp32 weights (in allocs)
+    fenc::Workspace fws;
 
     ~slx_model() {
         vocab::release(vlat);
+        fws.release();
         for (auto& kv : ws) cudaFree(kv.second.p);
         for (void* p : allocs) cudaFree(p);
         gemm_workspace_free(gws);
@@ -249,6 +253,33 @@ struct Loader {
         return SLX_OK;
     }
 
+    // A tensor read as float (GgufReader.ReadTensorF32), dequantized on the device; at least n elements.
+    int f32(const std::string& name, int64_t n, float** out, int64_t* elements = nullptr) {
+        const GgufTensor* t = g.tensor(name);
+        if (!t) return set_err(ctx, SLX_ENOTFOUND, "Tensor '%s' not found in GGUF file", name.c_str());
+        if (t->elements < n)
+            return set_err(ctx, SLX_ERANGE, "tensor '%s' has %lld elements, the forward indexes %lld", name.c_str(),
+                           (long long)t->elements, (long long)n);
+        std::vector<uint8_t> raw;
+        std::string err;
+        int st = g.read_raw(*t, raw, err);
+        if (st) return set_err(ctx, st, "%s", err.c_str());
+        void* d = nullptr;
+        CK(cudaMalloc(&d, std::max<size_t>(raw.size(), 1)));
+        CK(cudaMemcpy(d, raw.data(), raw.size(), cudaMemcpyHostToDevice));
+        CK(cudaMalloc((void**)out, sizeof(float) * std::max<int64_t>(t->elements, 1)));
+        m->allocs.push_back(*out);
+        CK(cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), ctx->stream));
+        dequant_f32((int)t->dtype, (const uint8_t*)d, t->elements, *out, ctx->d_flag, ctx->stream);
+        int flag = 0;
+        CK(cudaMemcpyAsync(&flag, ctx->d_flag, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+        CK(cudaStreamSynchronize(ctx->stream));
+        cudaFree(d);
+        if (flag) return set_err(ctx, SLX_ERANGE, "MXFP4 nibble 15 in '%s' (index outside the 15-entry table)", name.c_str());
+        if (elements) *elements = t->elements;
+        return SLX_OK;
+    }
+
     int ones(int64_t n, int64_t** out) {  // MakeOnesWeight (IntegerCausalSource.Loading.cs:227-233)
         std::vector<int64_t> h((size_t)n, 1LL << m->scale_bits);
         return upload(h.data(), h.size() * sizeof(int64_t), (void**)out);
@@ -308,6 +339,68 @@ int load_encoder(slx_ctx* ctx, slx_model* m, GgufFile& g) {
     m->unk = g.unk; m->eos = g.eos; m->vocab = g.n_tokens;
     m->rope_rows = 512;  // s_ropeMaxSeqLen (IntegerTransformerSource.cs:27)
     return ld.rope(m->rope_rows, m->head_dim, m->rope_base, &m->cos_g, &m->sin_g);
+}
+
+// TransformerEmbeddingSource.Load / LoadFromReader (Gguf/TransformerEmbeddingSource.cs:46-57,506-557):
+// every tensor read as float; the RopeCache (:227-252) with theta = (float)Pow(base, -2i/hd) and
+// angle = t * theta in double, 512 rows.
+int load_float_encoder(slx_ctx* ctx, slx_model* m, GgufFile& g) {
+    if (!lower_eq(g.arch, "nomic-bert") && !lower_eq(g.arch, "bert"))
+        return set_err(ctx, SLX_EUNSUPPORTED, "Architecture '%s' is not supported. Only 'nomic-bert' and 'bert' are implemented.", g.arch.c_str());
+    m->embd = g.embd; m->heads = g.heads; m->kv_heads = g.heads; m->layers = g.layers; m->ff = g.ff;
+    if (m->embd <= 0 || m->heads <= 0 || m->embd % m->heads) return set_err(ctx, SLX_EINVAL, "bad encoder dimensions");
+    m->head_dim = m->embd / m->heads; m->q_dim = m->embd; m->kv_dim = m->embd;
+    m->rope_base = g.get_float(g.arch + ".rope.freq_base", 10000.0f);
+    Loader ld{ctx, m, g};
+    const int d = m->embd, F = m->ff;
+    fenc::Model& fm = m->fm;
+    fm.d = d; fm.heads = m->heads; fm.ff = F;
+    int st;
+    float* p = nullptr;
+    int64_t tok_el = 0;
+    if ((st = ld.f32("token_embd.weight", d, &p, &tok_el))) return st;
+    fm.tok = p;
+    fm.tok_rows = tok_el / d;
+    if ((st = ld.f32("token_types.weight", d, &p))) return st;
+    fm.tt = p;
+    if ((st = ld.f32("token_embd_norm.weight", d, &p))) return st;
+    fm.enw = p;
+    if ((st = ld.f32("token_embd_norm.bias", d, &p))) return st;
+    fm.enb = p;
+    fm.layers.resize(m->layers);
+    for (int i = 0; i < m->layers; i++) {
+        const std::string pre = "blk." + std::to_string(i);
+        fenc::Layer& l = fm.layers[i];
+        const struct { const char* name; int64_t n; const float** dst; } t[9] = {
+            {".attn_qkv.weight", (int64_t)3 * d * d, &l.qkv}, {".attn_output.weight", (int64_t)d * d, &l.o},
+            {".attn_output_norm.weight", d, &l.anw}, {".attn_output_norm.bias", d, &l.anb},
+            {".ffn_up.weight", (int64_t)F * d, &l.up}, {".ffn_gate.weight", (int64_t)F * d, &l.gate},
+            {".ffn_down.weight", (int64_t)d * F, &l.down}, {".layer_output_norm.weight", d, &l.lnw},
+            {".layer_output_norm.bias", d, &l.lnb}};
+        for (const auto& e : t) {
+            if ((st = ld.f32(pre + e.name, e.n, &p))) return st;
+            *e.dst = p;
+        }
+    }
+    if (g.n_tokens == 0) return set_err(ctx, SLX_EINVAL, "GGUF file contains no tokenizer vocabulary");
+    m->unk = g.unk; m->eos = g.eos; m->vocab = g.n_tokens;
+    fm.unk = g.unk;
+    m->rope_rows = 512;  // RopeMaxSeqLen (TransformerEmbeddingSource.cs:254)
+    const int hd = m->head_dim, half = hd / 2;
+    std::vector<float> cs((size_t)512 * std::max(half, 1)), sn(cs.size());
+    for (int t2 = 0; t2 < 512; t2++)
+        for (int i = 0; i < half; i++) {
+            const float theta = (float)std::pow((double)m->rope_base, -2.0 * i / hd);
+            const double angle = t2 * (double)theta;
+            cs[(size_t)t2 * half + i] = (float)std::cos(angle);
+            sn[(size_t)t2 * half + i] = (float)std::sin(angle);
+        }
+    void* dc = nullptr;
+    void* ds = nullptr;
+    if ((st = ld.upload(cs.data(), cs.size() * 4, &dc)) || (st = ld.upload(sn.data(), sn.size() * 4, &ds))) return st;
+    fm.cos = (const float*)dc;
+    fm.sin = (const float*)ds;
+    return SLX_OK;  // m->L stays empty: no integer projections to plan
 }
 
 // IntegerCausalSource.LoadFromReader (Gguf/IntegerCausalSource.Loading.cs:74-195); with
@@ -621,6 +714,8 @@ slx_status slx_model_load_gguf(slx_ctx* ctx, const char* path, int kind, int sca
         st = load_encoder(ctx, m.get(), g);
     else if (kind == SLX_MODEL_CAUSAL || kind == SLX_MODEL_GEMMA_ENCODER)
         st = load_causal(ctx, m.get(), g, kind == SLX_MODEL_GEMMA_ENCODER);
+    else if (kind == SLX_MODEL_FLOAT_ENCODER)
+        st = load_float_encoder(ctx, m.get(), g);
     else
         return set_err(ctx, SLX_EINVAL, "unknown model kind %d", kind);
     if (st) return st;
@@ -651,12 +746,48 @@ slx_status slx_model_info(slx_model* m, int32_t* info, int n) {
 slx_status slx_encode_device(slx_model* m, const int32_t* d_ids, int B, int T, int64_t* d_pooled, void* stream) {
     if (!m || (B > 0 && T > 0 && (!d_ids || !d_pooled))) return m ? set_err(m->ctx, SLX_EINVAL, "null argument") : SLX_EINVAL;
     if (m->kind == SLX_MODEL_CAUSAL) return set_err(m->ctx, SLX_EINVAL, "slx_encode on a causal model");
+    if (m->kind == SLX_MODEL_FLOAT_ENCODER) return set_err(m->ctx, SLX_EINVAL, "the float encoder has no Q30 output");
     return encode_device(m, d_ids, B, T, d_pooled, pick(m->ctx, stream));
+}
+
+// TransformerEmbeddingSource.Forward / EmbedBatchAsync (Gguf/TransformerEmbeddingSource.cs:106-141) for B
+// sequences of T ids: L2-normalised float embeddings.
+static slx_status encode_float(slx_model* m, const int32_t* ids, int B, int T, float* out) {
+    slx_ctx* ctx = m->ctx;
+    if (T > m->rope_rows)
+        return set_err(ctx, SLX_ERANGE, "sequence length %d exceeds the RoPE table (%d rows)", T, m->rope_rows);
+    if (B == 0) return SLX_OK;
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    int32_t* d_ids = m->buf<int32_t>("ids", (size_t)std::max(1, B * T));
+    float* d_out = m->buf<float>("fout", (size_t)B * m->embd);
+    if (!d_ids || !d_out) return set_err(ctx, SLX_EOOM, "workspace allocation failed");
+    if (T == 0) {  // MeanPool of no rows is the zero vector, which L2Normalize leaves unchanged
+        std::fill(out, out + (size_t)B * m->embd, 0.0f);
+        return SLX_OK;
+    }
+    CK(cudaMemcpyAsync(d_ids, ids, sizeof(int32_t) * B * T, cudaMemcpyHostToDevice, st));
+    int rc = 0;
+    run_k(ctx, KC_GEMM, (double)B * T * (3.0 * m->embd * m->embd + m->embd * m->embd + 3.0 * m->embd * m->ff) * m->fm.layers.size(),
+          0, st, [&] {
+              const int n = fenc::forward(m->fm, d_ids, B, T, d_out, m->fws, st, nullptr);
+              if (n < 0) rc = SLX_EOOM;
+              return n < 0 ? 0 : n;
+          });
+    if (rc) return set_err(ctx, rc, "workspace allocation failed");
+    CK(cudaMemcpyAsync(out, d_out, sizeof(float) * B * m->embd, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    return SLX_OK;
 }
 
 slx_status slx_encode(slx_model* m, const int32_t* ids, int B, int T, int64_t* pooled, float* l2) {
     if (!m) return SLX_EINVAL;
     slx_ctx* ctx = m->ctx;
+    if (m->kind == SLX_MODEL_FLOAT_ENCODER) {
+        if (B < 0 || T < 0 || (B > 0 && T > 0 && !ids) || (B > 0 && !l2) || pooled)
+            return set_err(ctx, SLX_EINVAL, "bad arguments (the float encoder fills l2 only)");
+        return encode_float(m, ids, B, T, l2);
+    }
     if (B < 0 || T < 0 || (B > 0 && T > 0 && !ids) || (B > 0 && !pooled)) return set_err(ctx, SLX_EINVAL, "bad arguments");
     if (m->kind == SLX_MODEL_CAUSAL) return set_err(ctx, SLX_EINVAL, "slx_encode on a causal model");
     if (B == 0) return SLX_OK;
@@ -679,6 +810,7 @@ slx_status slx_encode(slx_model* m, const int32_t* ids, int B, int T, int64_t* p
 slx_status slx_trace_hidden(slx_model* m, const int32_t* ids, int T, int n_layers, int final_norm, int64_t* x_q30) {
     if (!m || !ids || !x_q30 || T <= 0) return m ? set_err(m->ctx, SLX_EINVAL, "bad arguments") : SLX_EINVAL;
     slx_ctx* ctx = m->ctx;
+    if (m->kind == SLX_MODEL_FLOAT_ENCODER) return set_err(ctx, SLX_EINVAL, "the float encoder has no Q30 trace");
     CK(cudaSetDevice(ctx->device));
     cudaStream_t st = ctx->stream;
     int32_t* d_ids = m->buf<int32_t>("ids", (size_t)T);
