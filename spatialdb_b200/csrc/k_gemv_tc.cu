@@ -567,6 +567,237 @@ void launch_m(int M, const WDesc& w, const int64_t* a, int64_t lda, int64_t* c, 
 #undef SLX_GT
 }
 
+// ---- M = 1: digit products on the CUDA cores (dp4a) --------------------------------------------
+// For one activation row a tensor-core tile is mostly padding and every quant block needs
+// its own trip through TMEM (its scale differs), so these shapes run on the CUDA cores: each lane
+// holds one block's activation digits (5 digits x 8 words per row) in registers and reuses them for
+// R weight rows; per (row, block) the weights are 8 words of int8x4 (Q4_0 nibbles 0..15, Q8_0
+// bytes), P_i = sum dp4a(weights, digit i) is exact in int32, S = sum_i 256^i P_i, and S * D is
+// added in Int128 exactly as the tensor-core kernel's epilogue does. Lanes stride the blocks of a
+// row (32 consecutive blocks per warp load, coalesced) and reduce their Int128 sums at the end.
+
+// dig[m][digit][word][b] (consecutive blocks adjacent, so a warp's lanes read one coalesced line per
+// word) in the weight words' element order (as block_words unpacks them), asum[m][b] = sum of the
+// block's activations, and the overflow tag when a value needs a sixth digit.
+template <bool Q4>
+__global__ void k_gemv_digits_lin(const int64_t* __restrict__ A, int64_t lda, int M, int nb,
+                                  uint32_t* __restrict__ dig, int64_t* __restrict__ asum, int* overflow, int tag) {
+    // four threads per block, thread q of a block taking elements 8q .. 8q+7 (payload words 2q, 2q+1
+    // in both formats); the block sum is reduced over the four lanes
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool live = t < M * nb * 4;
+    const int blk = t >> 2, q = t & 3;
+    const int m = live ? blk / nb : 0, b = live ? blk % nb : 0;
+    uint32_t w[ND][2];
+#pragma unroll
+    for (int i = 0; i < ND; i++) w[i][0] = w[i][1] = 0;
+    int64_t sum = 0;
+    bool bad = false;
+    if (live) {
+        const int64_t* a = A + (int64_t)m * lda + (int64_t)b * 32 + 8 * q;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            int64_t x = a[e];
+            sum = wadd(sum, x);
+            bad |= x > DIG5_MAX || x < DIG5_MIN;
+            const int word = Q4 ? (e & 1) : e >> 2;  // of the thread's two words
+            const int byte = Q4 ? e >> 1 : e & 3;
+#pragma unroll
+            for (int i = 0; i < ND; i++) {
+                const int d = (int)(((uint64_t)x + 128u) & 255u) - 128;
+                x = (x - d) >> 8;
+                w[i][word] |= (uint32_t)(uint8_t)(int8_t)d << (8 * byte);
+            }
+        }
+    }
+    sum = wadd(sum, (int64_t)__shfl_xor_sync(0xffffffffu, (long long)sum, 1));
+    sum = wadd(sum, (int64_t)__shfl_xor_sync(0xffffffffu, (long long)sum, 2));
+    if (!live) return;
+#pragma unroll
+    for (int i = 0; i < ND; i++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) dig[((size_t)(m * ND + i) * 8 + 2 * q + j) * nb + b] = w[i][j];
+    if (q == 0) asum[(size_t)m * nb + b] = sum;
+    if (bad) atomicExch(overflow, tag);
+}
+
+SLX_DEV int dp4a_s32(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+SLX_DEV void add128(uint64_t& lo, int64_t& hi, uint64_t l2, int64_t h2) {
+    const uint64_t s = lo + l2;
+    hi = (int64_t)((uint64_t)hi + (uint64_t)h2 + (s < lo ? 1u : 0u));
+    lo = s;
+}
+
+struct DpParams {
+    int N, K;
+    const uint8_t* W;
+    const int64_t* A;
+    int64_t lda;
+    const uint32_t* dig;
+    const int64_t* asum;
+    const int* overflow;
+    int tag;
+    double scale;
+    int shift;
+    int64_t* C;
+    int64_t ldc;
+};
+
+constexpr int DPW = 4;  // warps per CTA
+
+// Raw words of the block at byte offset o: NW + 1 words from o rounded down to 4 bytes (an odd block
+// starts 2 bytes early, inside the previous block), and their unpacking into scale and payload.
+template <bool Q4>
+SLX_DEV void load_raw(const uint8_t* __restrict__ W, int64_t o, uint32_t (&v)[(Q4 ? 4 : 8) + 1]) {
+    constexpr int NW = Q4 ? 4 : 8;
+    const uint32_t* r = (const uint32_t*)(W + (o & ~(int64_t)3));
+#pragma unroll
+    for (int j = 0; j <= NW; j++) v[j] = __ldg(r + j);
+}
+template <bool Q4>
+SLX_DEV uint16_t unpack_raw(int64_t o, const uint32_t (&v)[(Q4 ? 4 : 8) + 1], uint32_t (&w)[8]) {
+    constexpr int NW = Q4 ? 4 : 8;
+    uint32_t x[8];
+    uint16_t scale;
+    if ((o & 3) == 0) {
+        scale = (uint16_t)(v[0] & 0xFFFFu);
+#pragma unroll
+        for (int j = 0; j < NW; j++) x[j] = __funnelshift_r(v[j], v[j + 1], 16);
+    } else {
+        scale = (uint16_t)(v[0] >> 16);
+#pragma unroll
+        for (int j = 0; j < NW; j++) x[j] = v[j + 1];
+    }
+    if (Q4) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            w[2 * j] = x[j] & 0x0F0F0F0Fu;
+            w[2 * j + 1] = (x[j] >> 4) & 0x0F0F0F0Fu;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) w[j] = x[j];
+    }
+    return scale;
+}
+
+template <bool Q4, int MM, int R>
+__global__ void __launch_bounds__(DPW * 32) k_gemv_dp4a(DpParams p) {
+    constexpr int BB = Q4 ? 18 : 34;
+    constexpr int NV = (Q4 ? 4 : 8) + 1;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = p.K / 32;
+    const int n0 = (blockIdx.x * DPW + warp) * R;
+    if (n0 >= p.N) return;
+    const bool wide = *(volatile const int*)p.overflow == p.tag;  // an activation needs a sixth digit
+    uint64_t lo[R][MM];
+    int64_t hi[R][MM];
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int m = 0; m < MM; m++) lo[r][m] = 0, hi[r][m] = 0;
+    for (int b = lane; b < nb; b += 32) {
+        uint32_t cur[R][NV];
+#pragma unroll
+        for (int r = 0; r < R; r++)
+            if (n0 + r < p.N) load_raw<Q4>(p.W, ((int64_t)(n0 + r) * nb + b) * BB, cur[r]);
+        uint32_t dq[MM][ND][8];
+        int64_t as[MM];
+        if (!wide) {
+#pragma unroll
+            for (int m = 0; m < MM; m++) {
+#pragma unroll
+                for (int i = 0; i < ND; i++)
+#pragma unroll
+                    for (int j = 0; j < 8; j++) dq[m][i][j] = __ldg(p.dig + ((size_t)(m * ND + i) * 8 + j) * nb + b);
+                as[m] = __ldg(p.asum + (size_t)m * nb + b);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const int n = n0 + r;
+            if (n >= p.N) break;
+            uint32_t wq[8];
+            const int64_t o = ((int64_t)n * nb + b) * BB;
+            const float d = h2f(unpack_raw<Q4>(o, cur[r], wq));
+            // D = d * 2^s (an integer below 2^63 for a finite d); long.MinValue marks a non-finite scale
+            const int64_t D = isfinite(d) ? (int64_t)((double)d * p.scale) : INT64_MIN;
+            if (!wide) {
+#pragma unroll
+                for (int m = 0; m < MM; m++) {
+                    int P[ND];
+#pragma unroll
+                    for (int i = 0; i < ND; i++) {
+                        int acc = 0;
+#pragma unroll
+                        for (int j = 0; j < 8; j++) acc = dp4a_s32(wq[j], dq[m][i][j], acc);
+                        P[i] = acc;
+                    }
+                    const int t01 = P[1] * 256 + P[0], t23 = P[3] * 256 + P[2];  // |P_i| < 2^20
+                    int64_t S = (int64_t)t01 + (int64_t)t23 * 65536 + ((int64_t)P[4] << 32);
+                    if (Q4) S -= 8 * as[m];
+                    if (D == INT64_MIN) S = as[m];  // every composite of the block is long.MinValue
+                    add128(lo[r][m], hi[r][m], (uint64_t)S * (uint64_t)D, __mul64hi(S, D));
+                }
+            } else {
+                // Int128 multiply-adds of the composites w = D * q (long.MinValue for a non-finite scale)
+                for (int e = 0; e < 32; e++) {
+                    const int word = Q4 ? 2 * (e >> 3) + (e & 1) : e >> 2;
+                    const int byte = Q4 ? (e & 7) >> 1 : e & 3;
+                    const int q = Q4 ? (int)((wq[word] >> (8 * byte)) & 15u) - 8
+                                     : (int)(int8_t)(uint8_t)(wq[word] >> (8 * byte));
+                    const int64_t wc = D == INT64_MIN ? INT64_MIN : D * q;
+#pragma unroll
+                    for (int m = 0; m < MM; m++) {
+                        const int64_t x = p.A[(int64_t)m * p.lda + (int64_t)b * 32 + e];
+                        add128(lo[r][m], hi[r][m], (uint64_t)x * (uint64_t)wc, __mul64hi(x, wc));
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int m = 0; m < MM; m++) {
+            uint64_t l = lo[r][m];
+            int64_t h = hi[r][m];
+            for (int o = 16; o > 0; o >>= 1) {
+                const uint64_t l2 = __shfl_xor_sync(0xffffffffu, (unsigned long long)l, o);
+                const int64_t h2 = __shfl_xor_sync(0xffffffffu, (long long)h, o);
+                add128(l, h, l2, h2);
+            }
+            const int n = n0 + r;
+            if (lane == 0 && n < p.N) {
+                const i128 v = (i128)(((u128)(uint64_t)h << 64) | l);
+                p.C[(int64_t)m * p.ldc + n] = p.shift > 0 ? lo64(sar128(v, p.shift)) : lo64(v);
+            }
+        }
+}
+
+template <bool Q4, int MM>
+void launch_dp4a(const WDesc& w, const int64_t* a, int64_t lda, int64_t* c, int64_t ldc, int shift, GemmWorkspace& ws,
+                 cudaStream_t st) {
+    const int N = (int)w.N, K = (int)w.K, nb = K / 32;
+    uint8_t* base = (uint8_t*)ws.p;
+    int* flag = (int*)base + FLAG_WORD;
+    uint8_t* dig = base + 256 + counters_bytes(N) + partial_bytes(MM, N, K);  // the digit-tile region
+    int64_t* asum = (int64_t*)(dig + digit_bytes(MM, K));
+    ws.tag = ws.tag >= 0x3fffffffu ? 1u : ws.tag + 1u;
+    k_gemv_digits_lin<Q4><<<(MM * nb * 4 + 127) / 128, 128, 0, st>>>(a, lda, MM, nb, (uint32_t*)dig, asum, flag,
+                                                                    (int)ws.tag);
+    DpParams p;
+    p.N = N; p.K = K; p.W = w.data; p.A = a; p.lda = lda; p.dig = (const uint32_t*)dig; p.asum = asum;
+    p.overflow = flag; p.tag = (int)ws.tag; p.scale = w.scale; p.shift = shift; p.C = c; p.ldc = ldc;
+    constexpr int R = 4;  // rows per warp
+    k_gemv_dp4a<Q4, MM, R><<<(unsigned)((N + DPW * R - 1) / (DPW * R)), DPW * 32, 0, st>>>(p);
+}
+
 }  // namespace
 
 bool gemv_supported(const WDesc& w, int M) {
@@ -596,6 +827,11 @@ bool gemv_reserve(GemmWorkspace& ws, int M, int N, int K, cudaStream_t st) {
 
 int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift,
                GemmWorkspace& ws, cudaStream_t st) {
+    if (M == 1) {
+        if (w.dtype == DT_Q4_0) launch_dp4a<true, 1>(w, a, lda, c, ldc, shift, ws, st);
+        else launch_dp4a<false, 1>(w, a, lda, c, ldc, shift, ws, st);
+        return 2;
+    }
     if (w.dtype == DT_Q4_0)
         launch_m<true>(M, w, a, lda, c, ldc, shift, ws, st);
     else
