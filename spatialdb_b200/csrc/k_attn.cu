@@ -546,7 +546,7 @@ k_pv_tc(const int64_t* S, int SR, const int8_t* __restrict__ Vd, int Tpad, const
         const int* __restrict__ pvsel, int* err) {
     using C = PvTc<HD>;
     constexpr int TH = C::TH, RPT = C::RPT, CG = C::CG, RG = C::RG, PUS = C::PUS;
-    constexpr uint32_t IDESC = idesc_i8(C::NB);
+    constexpr uint32_t IDESC = idesc_u8s8(C::NB);  // p's digits are its bytes (0 <= p <= 2^30)
     if (*skip || *pvsel) return;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -631,26 +631,21 @@ k_pv_tc(const int64_t* S, int SR, const int8_t* __restrict__ Vd, int Tpad, const
                 if (c >= 1 && !mbar_wait(done0 + 8 * (buf ^ 1), (uint32_t)((c - 1) >> 1) & 1u)) s_fail = 1;
                 issue(k0 + PVT, buf ^ 1);
             }
-            // p digits of chunk c: (row, 16-key granule) items
+            // p digits of chunk c: (row, 16-key granule) items. 0 <= p <= 2^30, so its unsigned
+            // base-256 digits are its four bytes (the MMA reads A as u8); a 4 x 4 byte transpose per
+            // 4 keys puts byte i of keys k..k+3 into plane i
             for (int it = threadIdx.x; it < PM * 4; it += TH) {
                 const int r = it >> 2, q = it & 3;
                 uint32_t pk[4][4];
 #pragma unroll
                 for (int w4 = 0; w4 < 4; w4++) {
                     const uint4 pv = *(const uint4*)(Pu + r * PUS + 16 * q + 4 * w4);
-                    const uint32_t pp[4] = {pv.x, pv.y, pv.z, pv.w};
-#pragma unroll
-                    for (int i = 0; i < 4; i++) pk[i][w4] = 0;
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        int64_t x = pp[e];
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            const int d = (int)(((uint64_t)x + 128u) & 255u) - 128;
-                            x = (x - d) >> 8;
-                            pk[i][w4] |= (uint32_t)(uint8_t)(int8_t)d << (8 * e);
-                        }
-                    }
+                    const uint32_t ab_lo = __byte_perm(pv.x, pv.y, 0x5140), ab_hi = __byte_perm(pv.x, pv.y, 0x7362);
+                    const uint32_t cd_lo = __byte_perm(pv.z, pv.w, 0x5140), cd_hi = __byte_perm(pv.z, pv.w, 0x7362);
+                    pk[0][w4] = __byte_perm(ab_lo, cd_lo, 0x5410);
+                    pk[1][w4] = __byte_perm(ab_lo, cd_lo, 0x7632);
+                    pk[2][w4] = __byte_perm(ab_hi, cd_hi, 0x5410);
+                    pk[3][w4] = __byte_perm(ab_hi, cd_hi, 0x7632);
                 }
 #pragma unroll
                 for (int i = 0; i < 4; i++)
@@ -755,6 +750,12 @@ void launch_pv(int B, int T, int nh, int nkv, int64_t* scores, int sr, const int
     k_split_v<HD><<<vgrid, 256, 0, st>>>(v, ldv, T, tpad, nkv, vh, vl, vd, flag, flag, pvsel);
     constexpr bool tcpath = HD <= 64;
     if constexpr (tcpath) {
+        // a TMEM column block sums at most two (p byte, v digit) products of 255 * 128 per key:
+        // int32 holds them for T < 32896; longer rows take the fp64 P.V
+        if (T > 32768) {
+            cudaMemsetAsync(pvsel, 1, sizeof(int), st);
+            goto fp64;
+        }
         constexpr size_t smem = PvTc<HD>::SMEM;
         static_assert(smem <= 227 * 1024, "tensor-core P.V shared memory");
         static bool configured = false;
@@ -765,6 +766,7 @@ void launch_pv(int B, int T, int nh, int nkv, int64_t* scores, int sr, const int
         dim3 grid((unsigned)((T + PM - 1) / PM), (unsigned)nh, (unsigned)B);
         k_pv_tc<HD><<<grid, PvTc<HD>::TH + 32, smem, st>>>(scores, sr, vd, tpad, vl, out, ldo, T, nh, nkv, flag, pvsel, err);
     }
+fp64:
     constexpr size_t smem = Pv<HD>::SMEM;
     static_assert(smem <= 200 * 1024, "P.V shared memory");
     static bool configured = false;

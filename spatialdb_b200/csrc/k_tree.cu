@@ -510,6 +510,27 @@ int build(const int32_t* d_vals, int64_t n, int dim, int leaf_threshold, Tree& t
     std::vector<Span> active;
     if (n > leaf_threshold) active.push_back(Span{0, n, t.root});
     Scratch sc;
+    // Upper bounds of every level's scratch, allocated once: active spans are disjoint and hold more
+    // than leaf_threshold occupants each; work items number at most n / CH plus one per span, and
+    // the items of multi-item spans at most 2 n / CH.
+    if (!active.empty()) {
+        const size_t smax = (size_t)(n / (leaf_threshold + 1) + 1);
+        const size_t imax = (size_t)(n / CH) + smax + 1, pmax = (size_t)(2 * n / CH) + 2;
+        if (!grow(sc.seg_start, sc.c_seg, smax) || !grow(sc.seg_len, sc.c_seg2, smax) ||
+            !grow(sc.seg_nitems, sc.c_seg3, smax) || !grow(sc.seg_item0, sc.c_seg4, smax) ||
+            !grow(sc.item_seg, sc.c_item, imax) || !grow(sc.item_begin, sc.c_item2, imax) ||
+            !grow(sc.item_len, sc.c_item3, imax) || !grow(sc.item_pidx, sc.c_item4, imax) ||
+            !grow(sc.best_dim, sc.c_bd, smax) || !grow(sc.pivot, sc.c_pv, smax) || !grow(sc.boundary, sc.c_bn, smax) ||
+            !grow(sc.krem, sc.c_kr, smax) || !grow(sc.prefix, sc.c_pre, smax) || !grow(sc.hist, sc.c_hist, smax * 256) ||
+            !grow(sc.item_cnt, sc.c_cnt, imax) || !grow(sc.item_off, sc.c_off, imax) || !grow(sc.mseg, sc.c_ms, smax) ||
+            !grow(sc.mitem0, sc.c_mi, smax) || !grow(sc.psum, sc.c_psum, pmax * dim) ||
+            !grow(sc.psq, sc.c_psq, pmax * dim * 2) || !grow(sc.ppop, sc.c_ppop, pmax * dim) ||
+            !grow(sc.pv, sc.c_pvv, (size_t)n) || !grow(sc.F, sc.c_F, (size_t)n) || !grow(sc.lpos, sc.c_l, (size_t)n) ||
+            !grow(sc.rpos, sc.c_r, (size_t)n) || !grow(sc.tmp, sc.c_t, (size_t)n)) {
+            err = "lattice tree: device allocation failed";
+            return SLX_EOOM;
+        }
+    }
     std::vector<int32_t> h_ss, h_sl, h_sn, h_si, h_is, h_ib, h_il, h_ip, h_ms, h_mi, h_bd, h_pv, h_bn;
     while (!active.empty()) {
         const int S = (int)active.size();
