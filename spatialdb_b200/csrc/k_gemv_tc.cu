@@ -574,7 +574,8 @@ void launch_m(int M, const WDesc& w, const int64_t* a, int64_t lda, int64_t* c, 
 // R weight rows; per (row, block) the weights are 8 words of int8x4 (Q4_0 nibbles 0..15, Q8_0
 // bytes), P_i = sum dp4a(weights, digit i) is exact in int32, S = sum_i 256^i P_i, and S * D is
 // added in Int128 exactly as the tensor-core kernel's epilogue does. Lanes stride the blocks of a
-// row (32 consecutive blocks per warp load, coalesced) and reduce their Int128 sums at the end.
+// row and reduce their Int128 sums at the end. (An fp64 variant, S = sum a_k q_k by DFMA, exact for
+// these ranges, measured slower on this part: 25.5 / 29.8 us against 18.4 / 20.3 us.)
 
 // dig[m][digit][word][b] (consecutive blocks adjacent, so a warp's lanes read one coalesced line per
 // word) in the weight words' element order (as block_words unpacks them), asum[m][b] = sum of the
@@ -686,80 +687,119 @@ SLX_DEV uint16_t unpack_raw(int64_t o, const uint32_t (&v)[(Q4 ? 4 : 8) + 1], ui
     return scale;
 }
 
+SLX_DEV void gv_cp16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+SLX_DEV void gv_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+SLX_DEV void gv_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// A warp streams its R rows through shared memory: each step copies the rows' next 32 quant blocks
+// (32 * BB bytes a row, 16-byte aligned since K % 256 == 0) with 16-byte cp.async, one step ahead of
+// the arithmetic; each lane then reads its own block's words from shared memory.
 template <bool Q4, int MM, int R>
 __global__ void __launch_bounds__(DPW * 32) k_gemv_dp4a(DpParams p) {
     constexpr int BB = Q4 ? 18 : 34;
     constexpr int NV = (Q4 ? 4 : 8) + 1;
+    constexpr int SEG = 32 * BB;  // bytes of one row's 32 blocks
+    __shared__ __align__(16) uint8_t seg[DPW][2][R * SEG];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nb = p.K / 32;
     const int n0 = (blockIdx.x * DPW + warp) * R;
     if (n0 >= p.N) return;
     const bool wide = *(volatile const int*)p.overflow == p.tag;  // an activation needs a sixth digit
+    const int steps = (nb + 31) / 32;
+    auto issue = [&](int it, int buf) {
+        const int blocks = min(32, nb - 32 * it);  // a multiple of 8: whole 16-byte chunks
+        const int chunks = blocks * BB / 16;
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(seg[warp][buf]);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            if (n0 + r >= p.N) break;
+            const uint8_t* src = p.W + ((int64_t)(n0 + r) * nb + 32 * it) * BB;
+            for (int c = lane; c < chunks; c += 32) gv_cp16(dst + r * SEG + c * 16, src + c * 16);
+        }
+        gv_commit();
+    };
     uint64_t lo[R][MM];
     int64_t hi[R][MM];
 #pragma unroll
     for (int r = 0; r < R; r++)
 #pragma unroll
         for (int m = 0; m < MM; m++) lo[r][m] = 0, hi[r][m] = 0;
-    for (int b = lane; b < nb; b += 32) {
-        uint32_t cur[R][NV];
-#pragma unroll
-        for (int r = 0; r < R; r++)
-            if (n0 + r < p.N) load_raw<Q4>(p.W, ((int64_t)(n0 + r) * nb + b) * BB, cur[r]);
-        uint32_t dq[MM][ND][8];
-        int64_t as[MM];
-        if (!wide) {
-#pragma unroll
-            for (int m = 0; m < MM; m++) {
-#pragma unroll
-                for (int i = 0; i < ND; i++)
-#pragma unroll
-                    for (int j = 0; j < 8; j++) dq[m][i][j] = __ldg(p.dig + ((size_t)(m * ND + i) * 8 + j) * nb + b);
-                as[m] = __ldg(p.asum + (size_t)m * nb + b);
-            }
+    issue(0, 0);
+    for (int it = 0; it < steps; it++) {
+        if (it + 1 < steps) {
+            issue(it + 1, (it + 1) & 1);
+            gv_wait<1>();
+        } else {
+            gv_wait<0>();
         }
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-            const int n = n0 + r;
-            if (n >= p.N) break;
-            uint32_t wq[8];
-            const int64_t o = ((int64_t)n * nb + b) * BB;
-            const float d = h2f(unpack_raw<Q4>(o, cur[r], wq));
-            // D = d * 2^s (an integer below 2^63 for a finite d); long.MinValue marks a non-finite scale
-            const int64_t D = isfinite(d) ? (int64_t)((double)d * p.scale) : INT64_MIN;
+        __syncwarp();
+        const int b = 32 * it + lane;
+        const uint8_t* sb = seg[warp][it & 1];
+        if (b < nb) {
+            uint32_t dq[MM][ND][8];
+            int64_t as[MM];
             if (!wide) {
 #pragma unroll
                 for (int m = 0; m < MM; m++) {
-                    int P[ND];
 #pragma unroll
-                    for (int i = 0; i < ND; i++) {
-                        int acc = 0;
+                    for (int i = 0; i < ND; i++)
 #pragma unroll
-                        for (int j = 0; j < 8; j++) acc = dp4a_s32(wq[j], dq[m][i][j], acc);
-                        P[i] = acc;
-                    }
-                    const int t01 = P[1] * 256 + P[0], t23 = P[3] * 256 + P[2];  // |P_i| < 2^20
-                    int64_t S = (int64_t)t01 + (int64_t)t23 * 65536 + ((int64_t)P[4] << 32);
-                    if (Q4) S -= 8 * as[m];
-                    if (D == INT64_MIN) S = as[m];  // every composite of the block is long.MinValue
-                    add128(lo[r][m], hi[r][m], (uint64_t)S * (uint64_t)D, __mul64hi(S, D));
+                        for (int j = 0; j < 8; j++)
+                            dq[m][i][j] = __ldg(p.dig + ((size_t)(m * ND + i) * 8 + j) * nb + b);
+                    as[m] = __ldg(p.asum + (size_t)m * nb + b);
                 }
-            } else {
-                // Int128 multiply-adds of the composites w = D * q (long.MinValue for a non-finite scale)
-                for (int e = 0; e < 32; e++) {
-                    const int word = Q4 ? 2 * (e >> 3) + (e & 1) : e >> 2;
-                    const int byte = Q4 ? (e & 7) >> 1 : e & 3;
-                    const int q = Q4 ? (int)((wq[word] >> (8 * byte)) & 15u) - 8
-                                     : (int)(int8_t)(uint8_t)(wq[word] >> (8 * byte));
-                    const int64_t wc = D == INT64_MIN ? INT64_MIN : D * q;
+            }
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int n = n0 + r;
+                if (n >= p.N) break;
+                const int64_t o = (int64_t)lane * BB;  // the block's offset in its segment (same parity as in W)
+                uint32_t v[NV];
+                const uint32_t* wsrc = (const uint32_t*)(sb + r * SEG + (o & ~(int64_t)3));
+#pragma unroll
+                for (int j = 0; j < NV; j++) v[j] = wsrc[j];
+                uint32_t wq[8];
+                const float d = h2f(unpack_raw<Q4>(o, v, wq));
+                // D = d * 2^s (an integer below 2^63 for a finite d); long.MinValue marks a non-finite scale
+                const int64_t D = isfinite(d) ? (int64_t)((double)d * p.scale) : INT64_MIN;
+                if (!wide) {
 #pragma unroll
                     for (int m = 0; m < MM; m++) {
-                        const int64_t x = p.A[(int64_t)m * p.lda + (int64_t)b * 32 + e];
-                        add128(lo[r][m], hi[r][m], (uint64_t)x * (uint64_t)wc, __mul64hi(x, wc));
+                        int P[ND];
+#pragma unroll
+                        for (int i = 0; i < ND; i++) {
+                            int acc = 0;
+#pragma unroll
+                            for (int j = 0; j < 8; j++) acc = dp4a_s32(wq[j], dq[m][i][j], acc);
+                            P[i] = acc;
+                        }
+                        const int t01 = P[1] * 256 + P[0], t23 = P[3] * 256 + P[2];  // |P_i| < 2^20
+                        int64_t S = (int64_t)t01 + (int64_t)t23 * 65536 + ((int64_t)P[4] << 32);
+                        if (Q4) S -= 8 * as[m];
+                        if (D == INT64_MIN) S = as[m];  // every composite of the block is long.MinValue
+                        add128(lo[r][m], hi[r][m], (uint64_t)S * (uint64_t)D, __mul64hi(S, D));
+                    }
+                } else {
+                    // Int128 multiply-adds of the composites w = D * q (long.MinValue for a non-finite scale)
+                    for (int e = 0; e < 32; e++) {
+                        const int word = Q4 ? 2 * (e >> 3) + (e & 1) : e >> 2;
+                        const int byte = Q4 ? (e & 7) >> 1 : e & 3;
+                        const int q = Q4 ? (int)((wq[word] >> (8 * byte)) & 15u) - 8
+                                         : (int)(int8_t)(uint8_t)(wq[word] >> (8 * byte));
+                        const int64_t wc = D == INT64_MIN ? INT64_MIN : D * q;
+#pragma unroll
+                        for (int m = 0; m < MM; m++) {
+                            const int64_t x = p.A[(int64_t)m * p.lda + (int64_t)b * 32 + e];
+                            add128(lo[r][m], hi[r][m], (uint64_t)x * (uint64_t)wc, __mul64hi(x, wc));
+                        }
                     }
                 }
             }
         }
+        __syncwarp();  // every lane is done with this buffer before it is refilled
     }
 #pragma unroll
     for (int r = 0; r < R; r++)
