@@ -1,4 +1,4 @@
-// k_attn.cu -- exact integer attention: tcgen05 scores, fixed-point softmax and per-term P.V.
+// k_attn.cu -- exact integer attention: tcgen05 scores, fixed-point softmax and a directed-rounding fp64 P.V.
 //
 // Reference semantics (Math/IntegerAttention.cs:60-109, 165-202, 246-289, 333-377), per head:
 //   score[t][s] = (long)((sum_d q[t][d]*k[s][d]) >> shift) / ISqrt64(hd)   (masked slots: -2^29)
@@ -16,15 +16,14 @@
 // 64-bit arithmetic -- the reference's (long)(Int128 >> shift) without 128-bit work. The epilogue
 // also keeps each row's maximum for the softmax.
 //
-// k_softmax_pv: e = FixedExp(score - max) (the reference's Taylor recurrence, ten terms suffice
-// for 0 <= r < ln 2), p = (e << 30) / sum. With v = v_hi 2^30 + v_lo (0 <= v_lo < 2^30) and
-// 0 <= p <= 2^30,
-//   floor(p v / 2^30) = p v_hi + floor(p v_lo / 2^30),
-// the first part summed in fp64 (exact: sum_s p_s <= 2^30 and |v_hi| < 2^22 keep every partial
-// sum an integer below 2^52) and the second as one mad.hi.u32 per term (the sum stays below
-// sum_s p_s <= 2^30, so 32 bits hold it). Any row outside these fast ranges (q/k wider than five
-// digits, a score difference that wraps, |v_hi| >= 2^22) raises the call's flag, and the exact
-// kernel redoes the call.
+// k_softmax: e = FixedExp(score - max) (the reference's Taylor recurrence, ten terms suffice for
+// 0 <= r < ln 2), p = (e << 30) / sum, so 0 <= p <= 2^30 and sum_s p_s <= 2^30.
+//
+// k_pv: floor(p v / 2^30) per term, summed, as one fp64 FMA rounded toward minus infinity into an
+// accumulator kept in [2^52, 2^53) (the window where the doubles are the integers): exact for
+// |v| < 2^50, which keeps every partial sum inside the window. Any row outside the fast ranges (q/k
+// wider than five digits, a score difference that wraps, |v| >= 2^50) raises the call's flag, and
+// the exact kernel redoes the call.
 #include <cuda.h>
 
 #include "slx_device.cuh"
@@ -344,443 +343,144 @@ __global__ __launch_bounds__(32 * SM_ROWS) void k_softmax(int64_t* S, int SR, co
     if (lane < T4 - T) prow[T + lane] = 0;
 }
 
-// V -> v >> 30 as fp64 ([T][HD]), 4 * (v mod 2^30) as uint32 ([T][HD], each P.V thread's four columns
-// 2g, 2g+1, HD/2+2g, HD/2+2g+1 adjacent) and, for the tensor-core P.V, the two balanced base-256 digits
-// of v >> 30 as key-major int8 planes [2][HD][Tpad] (keys past T zero), per (sequence, kv head).
-// |v >> 30| >= 2^22 sets the flag (the fp64 sums would not be exact); v >> 30 outside two digits sets
-// pvsel (the fp64 P.V runs instead of the tensor-core one).
-constexpr int SV_KEYS = 64;  // keys per k_split_v block
-
-template <int HD>
-__global__ __launch_bounds__(256) void k_split_v(const int64_t* __restrict__ V, int64_t ldv, int T, int Tpad, int nkv,
-                                                 double* __restrict__ Vh, uint32_t* __restrict__ Vl,
-                                                 int8_t* __restrict__ Vd, const int* __restrict__ skip, int* flag,
-                                                 int* pvsel) {
-    __shared__ int16_t s_hi[HD][SV_KEYS + 2];  // v >> 30 of the tile's keys (two-digit values; others flagged)
-    if (*skip) return;
-    const int zk = blockIdx.y, b = zk / nkv, kvh = zk % nkv, k0 = blockIdx.x * SV_KEYS;
-    const int64_t base = (int64_t)zk * T * HD;
-    bool bad = false, wide = false;
-    for (int i = threadIdx.x; i < SV_KEYS * HD; i += 256) {  // key-major: coalesced along the head's columns
-        const int sl = i / HD, d = i % HD, s = k0 + sl;
-        int64_t hi = 0;
-        if (s < T) {
-            const int64_t v = V[((int64_t)b * T + s) * ldv + (int64_t)kvh * HD + d];
-            hi = v >> 30;
-            bad |= hi < -(1LL << 22) || hi >= (1LL << 22);
-            wide |= hi < -32640 || hi > 32639;
-            Vh[base + (int64_t)s * HD + d] = (double)hi;
-            const int g = d < HD / 2 ? d >> 1 : (d - HD / 2) >> 1, j = d < HD / 2 ? (d & 1) : 2 + (d & 1);
-            Vl[base + (int64_t)s * HD + 4 * g + j] = (uint32_t)(v & ((1LL << 30) - 1)) << 2;
-        }
-        s_hi[d][sl] = (int16_t)(hi < -32640 || hi > 32639 ? 0 : hi);
-    }
-    if (bad) atomicOr(flag, 1);
-    if (wide) atomicOr(pvsel, 1);
-    __syncthreads();
-    int8_t* vd = Vd + (int64_t)zk * 2 * HD * Tpad + k0;
-    for (int i = threadIdx.x; i < HD * SV_KEYS; i += 256) {  // column-major: each plane row's keys contiguous
-        const int d = i / SV_KEYS, sl = i % SV_KEYS;
-        const int hi = s_hi[d][sl];
-        const int d0 = ((hi + 128) & 255) - 128, d1 = (hi - d0) >> 8;
-        vd[(int64_t)d * Tpad + sl] = (int8_t)d0;
-        vd[((int64_t)HD + d) * Tpad + sl] = (int8_t)d1;
-    }
-}
-
-// ---- P.V on CUDA cores with fp64 high parts (any head size; the tensor-core kernel's fallback)
-constexpr int PR = 32;  // query rows per block
+// ---- P.V: one fp64 FMA rounded toward minus infinity per term (any head size)
+//   out[t][d] = sum_s floor(p[t][s] v[s][d] / 2^30),   0 <= p <= 2^30,  |v| < 2^50.
+// The accumulator starts at 1.5 * 2^52 and holds 1.5 * 2^52 + S with S an integer, |S| < 2^51, so
+// every exact value acc + p v / 2^30 lies in [2^52, 2^53), where the doubles are exactly the
+// integers: fma_rd(p, v * 2^-30, acc) rounds that value down, which adds floor(p v / 2^30) exactly
+// (p and v * 2^-30 are exact doubles and the FMA rounds once). S stays inside the window because
+// FixedSoftmax floors every share, so sum_s p_s <= 2^30 and |S| <= max |v| + T. A value with
+// |v| >= 2^50 raises the call's flag and the exact kernel redoes the call.
+constexpr int PV_TH = 256;
+constexpr double PV_BASE = 6755399441055744.0;  // 1.5 * 2^52
 
 template <int HD>
 struct Pv {
-    static constexpr int CPT = 4;                      // columns per thread: 2c, 2c+1, HD/2+2c, HD/2+2c+1
-    static constexpr int RPT = HD >= 64 ? 4 : HD / 16; // rows per thread
-    static constexpr int CG = HD / CPT, RG = PR / RPT;
-    static constexpr int THREADS = CG * RG;            // 128 (hd <= 64), 256 (128), 512 (256)
-    static constexpr int VT = HD >= 256 ? 8 : 16;      // keys per chunk
-    static constexpr int PUS = VT + 4;                 // p row strides (4-word bank offset per row)
-    static constexpr int PDS = VT + 2;
-    static constexpr int MINB = THREADS <= 128 ? 4 : 1;
-    // one staging buffer: v >> 30 (fp64), 4 (v mod 2^30) (uint32), p (uint32)
-    static constexpr int VH_BYTES = VT * HD * 8, VL_BYTES = VT * HD * 4, PU_BYTES = PR * PUS * 4;
-    static constexpr int BUF = VH_BYTES + VL_BYTES + PU_BYTES;
+    static constexpr int CG = HD / 4;                    // thread columns 2c, 2c+1, HD/2+2c, HD/2+2c+1
+    static constexpr int RG = PV_TH / CG;                // row groups
+    static constexpr int RPT = RG >= 16 ? 128 / RG : 8;  // rows per thread (rows rg + RG*r)
+    static constexpr int PR = RG * RPT;                  // query rows per block: 128 (hd <= 64), 64, 32
+    static constexpr int VT = HD >= 128 ? 16 : 32;       // keys per chunk
+    static constexpr int PUS = VT + 4;                   // p row stride (uint32), rows 4 banks apart
+    static constexpr int PDS = VT + 2;                   // fp64 p row stride, rows 16 bytes apart mod 128
+    static constexpr int V_BYTES = VT * HD * 8, PU_BYTES = PR * PUS * 4;
+    static constexpr int BUF = V_BYTES + PU_BYTES;
     static constexpr size_t SMEM = 2 * (size_t)BUF + (size_t)PR * PDS * 8;
+    static_assert(BUF % 16 == 0, "16-byte copies");
 };
 
-// PR query rows of one head over chunks of VT keys: p, v >> 30 and 4 (v mod 2^30) arrive by cp.async
-// into one of two buffers while the other chunk computes; p is widened to fp64 once per chunk.
-// Thread (rg, cg) owns rows rg*RPT .. and columns 2cg, 2cg+1, HD/2+2cg, HD/2+2cg+1. With run_if,
-// runs only when *run_if is set.
+// PR query rows of one head over chunks of VT keys: the chunk's v rows (int64, straight from the
+// QKV buffer) and p rows (uint32) arrive by cp.async into one of two buffers while the other chunk
+// computes; v becomes v * 2^-30 in place and p is widened into Pd once per chunk.
 template <int HD>
-__global__ __launch_bounds__(Pv<HD>::THREADS, Pv<HD>::MINB) void k_pv_fp64(
-    const int64_t* S, int SR, const double* __restrict__ Vh, const uint32_t* __restrict__ Vl, int64_t* __restrict__ O,
-    int64_t ldo, int T, int nh, int nkv, const int* __restrict__ skip, const int* __restrict__ run_if) {
+__global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const int64_t* __restrict__ V,
+                                                  int64_t ldv, int64_t* __restrict__ O, int64_t ldo, int T, int nh,
+                                                  int nkv, int* flag) {
     using C = Pv<HD>;
-    constexpr int TH = C::THREADS, VT = C::VT, RPT = C::RPT, CG = C::CG, PUS = C::PUS, PDS = C::PDS;
-    if (*skip || (run_if && !*run_if)) return;
+    constexpr int VT = C::VT, RPT = C::RPT, CG = C::CG, RG = C::RG, PUS = C::PUS, PDS = C::PDS, PR = C::PR;
+    if (*flag) return;
     extern __shared__ __align__(16) uint8_t sm[];
     double* Pd = (double*)(sm + 2 * C::BUF);  // [PR][PDS]
     const int h = blockIdx.y, b = blockIdx.z, t0 = blockIdx.x * PR;
-    const int z = b * nh + h, zk = b * nkv + h / (nh / nkv);
+    const int z = b * nh + h, kvh = h / (nh / nkv);
     const int T4 = (T + 3) & ~3;
     const int cg = threadIdx.x % CG, rg = threadIdx.x / CG;
     const int c0 = 2 * cg, c1 = HD / 2 + 2 * cg;
-    const double* vh0 = Vh + (int64_t)zk * T * HD;
-    const uint32_t* vl0 = Vl + (int64_t)zk * T * HD;
+    const int64_t* v0 = V + (int64_t)b * T * ldv + (int64_t)kvh * HD;  // key s: v0 + s * ldv
     const uint32_t sbase = tc::smem_u32(sm);
     auto issue = [&](int k0, int buf) {
         const uint32_t dst = sbase + buf * C::BUF;
         const int keys = min(VT, T - k0);
-        for (int g = threadIdx.x; g < C::VH_BYTES / 16; g += TH) {  // v >> 30: HD/2 granules a key
-            const int s = g / (HD / 2);
-            cp_async16(dst + g * 16, s < keys ? vh0 + (int64_t)k0 * HD + g * 2 : vh0, s < keys ? 16u : 0u);
+        for (int g = threadIdx.x; g < C::V_BYTES / 16; g += PV_TH) {  // v: HD/2 granules a key
+            const int s = g / (HD / 2), j = g % (HD / 2);
+            cp_async16(dst + g * 16, s < keys ? v0 + (int64_t)(k0 + s) * ldv + 2 * j : v0, s < keys ? 16u : 0u);
         }
-        for (int g = threadIdx.x; g < C::VL_BYTES / 16; g += TH) {  // 4 (v mod 2^30): HD/4 granules a key
-            const int s = g / (HD / 4);
-            cp_async16(dst + C::VH_BYTES + g * 16, s < keys ? vl0 + (int64_t)k0 * HD + g * 4 : vl0, s < keys ? 16u : 0u);
-        }
-        for (int g = threadIdx.x; g < PR * (VT / 4); g += TH) {  // p: VT/4 granules a row
+        for (int g = threadIdx.x; g < PR * (VT / 4); g += PV_TH) {  // p: VT/4 granules a row
             const int r = g / (VT / 4), s = k0 + 4 * (g % (VT / 4));
             const int t = t0 + r;
             const bool ok = t < T && s < T4;
             const uint32_t* src = ok ? (const uint32_t*)(S + ((int64_t)z * T + t) * SR) + s : (const uint32_t*)S;
-            cp_async16(dst + C::VH_BYTES + C::VL_BYTES + (r * PUS + 4 * (g % (VT / 4))) * 4, src, ok ? 16u : 0u);
+            cp_async16(dst + C::V_BYTES + (r * PUS + 4 * (g % (VT / 4))) * 4, src, ok ? 16u : 0u);
         }
         cp_async_commit();
     };
-    double ah[RPT][4];
-    uint32_t al[RPT][4];
+    double acc[RPT][4];
 #pragma unroll
     for (int r = 0; r < RPT; r++)
 #pragma unroll
-        for (int c = 0; c < 4; c++) { ah[r][c] = 0.0; al[r][c] = 0; }
+        for (int c = 0; c < 4; c++) acc[r][c] = PV_BASE;
+    bool wide = false;
     issue(0, 0);
     for (int k0 = 0, buf = 0; k0 < T; k0 += VT, buf ^= 1) {
         cp_async_wait_all();
         __syncthreads();  // chunk k0 is in for every thread; the other buffer and Pd are free
         if (k0 + VT < T) issue(k0 + VT, buf ^ 1);
-        const double* Vhs = (const double*)(sm + buf * C::BUF);
-        const uint32_t* Vls = (const uint32_t*)(sm + buf * C::BUF + C::VH_BYTES);
-        const uint32_t* Pu = (const uint32_t*)(sm + buf * C::BUF + C::VH_BYTES + C::VL_BYTES);
-        for (int i = threadIdx.x; i < PR * VT; i += TH) {
+        double* Vs = (double*)(sm + buf * C::BUF);
+        const uint32_t* Pu = (const uint32_t*)(sm + buf * C::BUF + C::V_BYTES);
+        for (int i = threadIdx.x; i < VT * HD; i += PV_TH) {  // exact for |v| < 2^53
+            const int64_t x = ((const int64_t*)Vs)[i];
+            wide |= (x >> 30) < -(1LL << 20) || (x >> 30) >= (1LL << 20);
+            Vs[i] = (double)x * 0x1p-30;
+        }
+        for (int i = threadIdx.x; i < PR * VT; i += PV_TH) {
             const int r = i / VT, s = i % VT;
             Pd[r * PDS + s] = (double)Pu[r * PUS + s];
         }
         __syncthreads();
 #pragma unroll 2
-        for (int s = 0; s < VT; s += 4) {
-            uint4 pu[RPT];
+        for (int s = 0; s < VT; s += 2) {
+            const double2 a0 = *(const double2*)(Vs + s * HD + c0);
+            const double2 a1 = *(const double2*)(Vs + s * HD + c1);
+            const double2 b0 = *(const double2*)(Vs + (s + 1) * HD + c0);
+            const double2 b1 = *(const double2*)(Vs + (s + 1) * HD + c1);
 #pragma unroll
-            for (int r = 0; r < RPT; r++) pu[r] = *(const uint4*)(Pu + (rg * RPT + r) * PUS + s);
-#pragma unroll
-            for (int u = 0; u < 4; u += 2) {
-                const double2 ha0 = *(const double2*)(Vhs + (s + u) * HD + c0);
-                const double2 ha1 = *(const double2*)(Vhs + (s + u) * HD + c1);
-                const double2 hb0 = *(const double2*)(Vhs + (s + u + 1) * HD + c0);
-                const double2 hb1 = *(const double2*)(Vhs + (s + u + 1) * HD + c1);
-                const uint4 la = *(const uint4*)(Vls + (s + u) * HD + 4 * cg);
-                const uint4 lb = *(const uint4*)(Vls + (s + u + 1) * HD + 4 * cg);
-#pragma unroll
-                for (int r = 0; r < RPT; r++) {
-                    const double2 pd = *(const double2*)(Pd + (rg * RPT + r) * PDS + s + u);
-                    const uint32_t pa = u == 0 ? pu[r].x : pu[r].z, pb = u == 0 ? pu[r].y : pu[r].w;
-                    ah[r][0] = fma(pd.y, hb0.x, fma(pd.x, ha0.x, ah[r][0]));
-                    ah[r][1] = fma(pd.y, hb0.y, fma(pd.x, ha0.y, ah[r][1]));
-                    ah[r][2] = fma(pd.y, hb1.x, fma(pd.x, ha1.x, ah[r][2]));
-                    ah[r][3] = fma(pd.y, hb1.y, fma(pd.x, ha1.y, ah[r][3]));
-                    al[r][0] += __umulhi(pa, la.x) + __umulhi(pb, lb.x);
-                    al[r][1] += __umulhi(pa, la.y) + __umulhi(pb, lb.y);
-                    al[r][2] += __umulhi(pa, la.z) + __umulhi(pb, lb.z);
-                    al[r][3] += __umulhi(pa, la.w) + __umulhi(pb, lb.w);
-                }
+            for (int r = 0; r < RPT; r++) {
+                const double2 pd = *(const double2*)(Pd + (rg + RG * r) * PDS + s);
+                acc[r][0] = __fma_rd(pd.y, b0.x, __fma_rd(pd.x, a0.x, acc[r][0]));
+                acc[r][1] = __fma_rd(pd.y, b0.y, __fma_rd(pd.x, a0.y, acc[r][1]));
+                acc[r][2] = __fma_rd(pd.y, b1.x, __fma_rd(pd.x, a1.x, acc[r][2]));
+                acc[r][3] = __fma_rd(pd.y, b1.y, __fma_rd(pd.x, a1.y, acc[r][3]));
             }
         }
+    }
+    if (__syncthreads_or(wide)) {
+        if (threadIdx.x == 0) atomicOr(flag, 1);
+        return;
     }
 #pragma unroll
     for (int r = 0; r < RPT; r++) {
-        const int t = t0 + rg * RPT + r;
+        const int t = t0 + rg + RG * r;
         if (t >= T) continue;
         int64_t* orow = O + ((int64_t)b * T + t) * ldo + (int64_t)h * HD;
-        orow[c0] = __double2ll_rz(ah[r][0]) + (int64_t)al[r][0];
-        orow[c0 + 1] = __double2ll_rz(ah[r][1]) + (int64_t)al[r][1];
-        orow[c1] = __double2ll_rz(ah[r][2]) + (int64_t)al[r][2];
-        orow[c1 + 1] = __double2ll_rz(ah[r][3]) + (int64_t)al[r][3];
-    }
-}
-
-// ---- P.V with the linear part on the tensor cores (head sizes 16, 32, 64)
-//   sum_s floor(p v / 2^30) = sum_s p v_hi + sum_s floor(p v_lo / 2^30).
-// sum_s p v_hi is a GEMM: p (<= 2^30) as four balanced base-256 digits is the A operand (128 query
-// rows, built by the CUDA cores into a 64-byte-swizzled tile per 64-key chunk), v_hi as two digits
-// stacked along N (2 x HD rows, key-major planes from k_split_v) the B operand; digit pair (i, j)
-// accumulates in TMEM column block i+j (5 blocks of HD int32 columns, each below 2^31 for T < 2^16).
-// The CUDA cores add floor(p v_lo / 2^30) = umulhi(p, 4 v_lo) per term, as in k_pv_fp64.
-constexpr int PM = 128;  // query rows per block (MMA M)
-constexpr int PVT = 64;  // keys per chunk: two 32-key MMA K steps
-
-template <int HD>
-struct PvTc {
-    static constexpr int TH = 512;                       // compute threads; one more warp issues the MMAs
-    static constexpr int CG = HD / 4, RG = TH / CG, RPT = PM / RG;  // thread (rg, cg): rows rg + RG*r
-    static constexpr int NB = 2 * HD;                    // B rows: v digit j, column c at j*HD + c
-    static constexpr int NS = 5;                         // column blocks
-    static constexpr int COLS = NS * HD;
-    static constexpr int ALLOC = COLS <= 64 ? 64 : COLS <= 128 ? 128 : COLS <= 256 ? 256 : 512;
-    static constexpr int PUS = PVT + 4;                  // p row stride (uint32), rows 4 banks apart
-    static constexpr int PD_B = 4 * PM * 64;             // p digits [4][PM][64 B], 64-byte swizzle
-    static constexpr int VD_B = NB * 64;                 // v digits [NB][64 B], 64-byte swizzle
-    static constexpr int PU_B = PM * PUS * 4, VL_B = PVT * HD * 4;
-    static constexpr int BUF = (PD_B + VD_B + PU_B + VL_B + 1023) / 1024 * 1024;
-    static constexpr int FSL = HD + 1;                   // floor-sum tile row stride (uint32)
-    static constexpr int EQ = HD / 8 < 4 ? HD / 8 : 4;   // epilogue warps per TMEM lane quarter (8 columns each step)
-    static constexpr size_t SMEM = 2 * (size_t)BUF + 1024 + 64;
-    static_assert(PM * FSL * 4 <= PU_B, "floor sums reuse a p buffer");
-};
-
-SLX_DEV uint32_t sw64_off(int row, int g) { return (uint32_t)(row * 64 + ((g ^ ((row >> 1) & 3)) << 4)); }
-
-template <int HD>
-__global__ void __launch_bounds__(PvTc<HD>::TH + 32, 1)
-k_pv_tc(const int64_t* S, int SR, const int8_t* __restrict__ Vd, int Tpad, const uint32_t* __restrict__ Vl,
-        int64_t* __restrict__ O, int64_t ldo, int T, int nh, int nkv, const int* __restrict__ skip,
-        const int* __restrict__ pvsel, int* err) {
-    using C = PvTc<HD>;
-    constexpr int TH = C::TH, RPT = C::RPT, CG = C::CG, RG = C::RG, PUS = C::PUS;
-    constexpr uint32_t IDESC = idesc_u8s8(C::NB);  // p's digits are its bytes (0 <= p <= 2^30)
-    if (*skip || *pvsel) return;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = (uint64_t*)(sm + 2 * C::BUF);
-    const uint32_t done0 = smem_u32(bars), accd = smem_u32(bars + 2);
-    uint32_t* tmem_slot = (uint32_t*)(bars + 3);
-    __shared__ int s_fail;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.y, b = blockIdx.z, t0 = blockIdx.x * PM;
-    const int z = b * nh + h, zk = b * nkv + h / (nh / nkv);
-    const int T4 = (T + 3) & ~3;
-    const int nch = (T + PVT - 1) / PVT;
-    if (threadIdx.x == 0) {
-        s_fail = 0;
-        mbar_init(done0, 1);
-        mbar_init(done0 + 8, 1);
-        mbar_init(accd, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    if (warp == TH / 32) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "n"(C::ALLOC));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
-    fence_before();
-    __syncthreads();
-    fence_after();
-    const uint32_t tmem = *tmem_slot;
-    if (warp < TH / 32) {  // every MMA accumulates: start from zero
-        const uint32_t lb = (uint32_t)(32 * (warp & 3)) << 16;
-        for (int c = 8 * (warp >> 2); c < C::COLS; c += 8 * (TH / 128)) tmem_st8_zero(tmem + lb + c);
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-    }
-    fence_before();
-    __syncthreads();
-    fence_after();
-
-    const uint32_t sbase = smem_u32(sm);
-    const int8_t* vd0 = Vd + (int64_t)zk * C::NB * Tpad;
-    const uint32_t* vl0 = Vl + (int64_t)zk * T * HD;
-    // chunk k0's p rows, 4 (v mod 2^30) and v digits into buffer buf (all compute threads)
-    auto issue = [&](int k0, int buf) {
-        const uint32_t dst = sbase + buf * C::BUF;
-        for (int g = threadIdx.x; g < PM * (PVT / 4); g += TH) {  // p: 16 granules a row
-            const int r = g / (PVT / 4), s = k0 + 4 * (g % (PVT / 4));
-            const int t = t0 + r;
-            const bool ok = t < T && s < T4;
-            const uint32_t* src = ok ? (const uint32_t*)(S + ((int64_t)z * T + t) * SR) + s : (const uint32_t*)S;
-            cp_async16(dst + C::PD_B + C::VD_B + (r * PUS + 4 * (g % (PVT / 4))) * 4, src, ok ? 16u : 0u);
-        }
-        const int keys = min(PVT, T - k0);
-        for (int g = threadIdx.x; g < C::VL_B / 16; g += TH) {  // 4 (v mod 2^30): HD/4 granules a key
-            const int s = g / (HD / 4);
-            cp_async16(dst + C::PD_B + C::VD_B + C::PU_B + g * 16, s < keys ? vl0 + (int64_t)k0 * HD + g * 4 : vl0,
-                       s < keys ? 16u : 0u);
-        }
-        for (int g = threadIdx.x; g < C::NB * 4; g += TH) {  // v digits: four 16-byte granules a row
-            const int r = g >> 2, q = g & 3;
-            cp_async16(dst + C::PD_B + sw64_off(r, q), vd0 + (int64_t)r * Tpad + k0 + 16 * q, 16u);
-        }
-        cp_async_commit();
-    };
-
-    const int cg = threadIdx.x % CG, rg = threadIdx.x / CG;
-    const int c0 = 2 * cg, c1 = HD / 2 + 2 * cg;
-    uint32_t al[RPT][4];
-#pragma unroll
-    for (int r = 0; r < RPT; r++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) al[r][c] = 0;
-    if (warp < TH / 32) issue(0, 0);
-    for (int c = 0; c < nch; c++) {
-        const int buf = c & 1, k0 = c * PVT;
-        uint8_t* bp = sm + buf * C::BUF;
-        const uint32_t* Pu = (const uint32_t*)(bp + C::PD_B + C::VD_B);
-        const uint32_t* Vls = (const uint32_t*)(bp + C::PD_B + C::VD_B + C::PU_B);
-        if (warp < TH / 32) cp_async_wait_all();
-        __syncthreads();  // chunk c is in; every thread finished chunk c-1's CUDA-core part
-        if (warp < TH / 32) {
-            if (c + 1 < nch) {
-                // the other buffer's digit tiles were read by chunk c-1's MMAs
-                if (c >= 1 && !mbar_wait(done0 + 8 * (buf ^ 1), (uint32_t)((c - 1) >> 1) & 1u)) s_fail = 1;
-                issue(k0 + PVT, buf ^ 1);
-            }
-            // p digits of chunk c: (row, 16-key granule) items. 0 <= p <= 2^30, so its unsigned
-            // base-256 digits are its four bytes (the MMA reads A as u8); a 4 x 4 byte transpose per
-            // 4 keys puts byte i of keys k..k+3 into plane i
-            for (int it = threadIdx.x; it < PM * 4; it += TH) {
-                const int r = it >> 2, q = it & 3;
-                uint32_t pk[4][4];
-#pragma unroll
-                for (int w4 = 0; w4 < 4; w4++) {
-                    const uint4 pv = *(const uint4*)(Pu + r * PUS + 16 * q + 4 * w4);
-                    const uint32_t ab_lo = __byte_perm(pv.x, pv.y, 0x5140), ab_hi = __byte_perm(pv.x, pv.y, 0x7362);
-                    const uint32_t cd_lo = __byte_perm(pv.z, pv.w, 0x5140), cd_hi = __byte_perm(pv.z, pv.w, 0x7362);
-                    pk[0][w4] = __byte_perm(ab_lo, cd_lo, 0x5410);
-                    pk[1][w4] = __byte_perm(ab_lo, cd_lo, 0x7632);
-                    pk[2][w4] = __byte_perm(ab_hi, cd_hi, 0x5410);
-                    pk[3][w4] = __byte_perm(ab_hi, cd_hi, 0x7632);
-                }
-#pragma unroll
-                for (int i = 0; i < 4; i++)
-                    *(uint4*)(bp + i * (PM * 64) + sw64_off(r, q)) = make_uint4(pk[i][0], pk[i][1], pk[i][2], pk[i][3]);
-            }
-            fence_proxy_async();  // generic-proxy tile writes (and the landed copies) visible to the MMA
-        }
-        __syncthreads();  // chunk c's digit tiles complete
-        if (warp == TH / 32) {
-            if (lane == 0) {
-                fence_after();
-                const uint32_t pd = sbase + buf * C::BUF, vd = pd + C::PD_B;
-#pragma unroll
-                for (int kk = 0; kk < PVT / 32; kk++) {
-                    const uint64_t bdesc = tc::sw64_desc(vd + kk * 32);
-#pragma unroll
-                    for (int i = 0; i < 4; i++)
-                        umma_i8(tmem + i * HD, tc::sw64_desc(pd + i * (PM * 64) + kk * 32), bdesc, IDESC, 1u);
-                }
-                umma_commit(done0 + 8 * buf);
-                if (c == nch - 1) umma_commit(accd);
-            }
-        } else {
-            // floor(p v_lo / 2^30) on the CUDA cores
-#pragma unroll 2
-            for (int s = 0; s < PVT; s += 4) {
-                uint4 pu[RPT];
-#pragma unroll
-                for (int r = 0; r < RPT; r++) pu[r] = *(const uint4*)(Pu + (rg + RG * r) * PUS + s);
-#pragma unroll
-                for (int u = 0; u < 4; u += 2) {
-                    const uint4 la = *(const uint4*)(Vls + (s + u) * HD + 4 * cg);
-                    const uint4 lb = *(const uint4*)(Vls + (s + u + 1) * HD + 4 * cg);
-#pragma unroll
-                    for (int r = 0; r < RPT; r++) {
-                        const uint32_t pa = u == 0 ? pu[r].x : pu[r].z, pb = u == 0 ? pu[r].y : pu[r].w;
-                        al[r][0] += __umulhi(pa, la.x) + __umulhi(pb, lb.x);
-                        al[r][1] += __umulhi(pa, la.y) + __umulhi(pb, lb.y);
-                        al[r][2] += __umulhi(pa, la.z) + __umulhi(pb, lb.z);
-                        al[r][3] += __umulhi(pa, la.w) + __umulhi(pb, lb.w);
-                    }
-                }
-            }
-        }
-    }
-    __syncthreads();  // every chunk's CUDA-core part is done: buffer 0's p region takes the floor sums
-    uint32_t* fs = (uint32_t*)(sm + C::PD_B + C::VD_B);
-    if (warp < TH / 32) {
-#pragma unroll
-        for (int r = 0; r < RPT; r++) {
-            const int row = rg + RG * r;
-            fs[row * C::FSL + c0] = al[r][0];
-            fs[row * C::FSL + c0 + 1] = al[r][1];
-            fs[row * C::FSL + c1] = al[r][2];
-            fs[row * C::FSL + c1 + 1] = al[r][3];
-        }
-    }
-    __syncthreads();
-    if (warp < 4 * C::EQ) {
-        const bool ok = __all_sync(0xffffffffu, mbar_wait(accd, 0));
-        if (!ok) s_fail = 1;
-        fence_after();
-        const int q4 = warp & 3, part = warp >> 2;
-        const int row = 32 * q4 + lane, t = t0 + row;
-        const uint32_t ta = tmem + ((uint32_t)(32 * q4) << 16);
-        int64_t* orow = O + ((int64_t)b * T + (t < T ? t : 0)) * ldo + (int64_t)h * HD;
-        if (ok) {
-#pragma unroll 1
-            for (int cc = 8 * part; cc < HD; cc += 8 * C::EQ) {
-                uint32_t v[C::NS][8];
-#pragma unroll
-                for (int s2 = 0; s2 < C::NS; s2++) tmem_ld8(ta + s2 * HD + cc, v[s2]);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (t < T) {
-#pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        uint64_t sum = 0;  // sum_s p v_hi = sum of 2^(8 s) P_s, below 2^46 in magnitude
-#pragma unroll
-                        for (int s2 = 0; s2 < C::NS; s2++) sum += (uint64_t)(int64_t)(int32_t)v[s2][j] << (8 * s2);
-                        orow[cc + j] = (int64_t)(sum + fs[row * C::FSL + cc + j]);
-                    }
-                }
-            }
-        }
-    }
-    fence_before();
-    __syncthreads();
-    if (s_fail && threadIdx.x == 0 && err) atomicOr(err, KERR_TIMEOUT);
-    if (warp == TH / 32) {
-        fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(C::ALLOC));
+        orow[c0] = (int64_t)(acc[r][0] - PV_BASE);
+        orow[c0 + 1] = (int64_t)(acc[r][1] - PV_BASE);
+        orow[c1] = (int64_t)(acc[r][2] - PV_BASE);
+        orow[c1 + 1] = (int64_t)(acc[r][3] - PV_BASE);
     }
 }
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 template <int HD>
-void launch_pv(int B, int T, int nh, int nkv, int64_t* scores, int sr, const int64_t* v, int64_t ldv, double* vh,
-               uint32_t* vl, int8_t* vd, int tpad, int64_t* out, int64_t ldo, int* flag, int* pvsel, int* err,
-               cudaStream_t st) {
-    const dim3 vgrid((unsigned)(tpad / SV_KEYS), (unsigned)(B * nkv));
-    k_split_v<HD><<<vgrid, 256, 0, st>>>(v, ldv, T, tpad, nkv, vh, vl, vd, flag, flag, pvsel);
-    constexpr bool tcpath = HD <= 64;
-    if constexpr (tcpath) {
-        // a TMEM column block sums at most two (p byte, v digit) products of 255 * 128 per key:
-        // int32 holds them for T < 32896; longer rows take the fp64 P.V
-        if (T > 32768) {
-            cudaMemsetAsync(pvsel, 1, sizeof(int), st);
-            goto fp64;
-        }
-        constexpr size_t smem = PvTc<HD>::SMEM;
-        static_assert(smem <= 227 * 1024, "tensor-core P.V shared memory");
-        static bool configured = false;
-        if (!configured) {
-            cudaFuncSetAttribute(k_pv_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            configured = true;
-        }
-        dim3 grid((unsigned)((T + PM - 1) / PM), (unsigned)nh, (unsigned)B);
-        k_pv_tc<HD><<<grid, PvTc<HD>::TH + 32, smem, st>>>(scores, sr, vd, tpad, vl, out, ldo, T, nh, nkv, flag, pvsel, err);
+void launch_pv(int B, int T, int nh, int nkv, const int64_t* scores, int sr, const int64_t* v, int64_t ldv,
+               int64_t* out, int64_t ldo, int* flag, cudaStream_t st) {
+    using C = Pv<HD>;
+    static_assert(C::SMEM <= 112 * 1024, "two P.V blocks per SM");
+    if (((uintptr_t)v & 15) != 0 || (ldv & 1) != 0) {  // rows the 16-byte copies cannot read: the exact kernel
+        cudaMemsetAsync(flag, 1, sizeof(int), st);
+        return;
     }
-fp64:
-    constexpr size_t smem = Pv<HD>::SMEM;
-    static_assert(smem <= 200 * 1024, "P.V shared memory");
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(k_pv_fp64<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_pv<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
         configured = true;
     }
-    dim3 grid((unsigned)((T + PR - 1) / PR), (unsigned)nh, (unsigned)B);
-    k_pv_fp64<HD><<<grid, Pv<HD>::THREADS, smem, st>>>(scores, sr, vh, vl, out, ldo, T, nh, nkv, flag,
-                                                      tcpath ? pvsel : nullptr);
+    const dim3 grid((unsigned)((T + C::PR - 1) / C::PR), (unsigned)nh, (unsigned)B);
+    k_pv<HD><<<grid, PV_TH, C::SMEM, st>>>(scores, sr, v, ldv, out, ldo, T, nh, nkv, flag);
 }
 
 struct Layout {
-    int64_t kpad, tq, tk, sr, tpad, qbytes, kbytes, sbytes, mbytes, vhbytes, vlbytes, vdbytes;
+    int64_t kpad, tq, tk, sr, qbytes, kbytes, sbytes, mbytes;
 };
 
 Layout layout(int B, int T, int nh, int nkv, int hd) {
@@ -793,17 +493,13 @@ Layout layout(int B, int T, int nh, int nkv, int hd) {
     l.sr = round_up(T, 2);
     l.sbytes = round_up((int64_t)B * nh * T * l.sr * 8, 256);
     l.mbytes = round_up((int64_t)B * nh * T * 8, 256);
-    l.vhbytes = round_up((int64_t)B * nkv * T * hd * 8, 256);
-    l.vlbytes = round_up((int64_t)B * nkv * T * hd * 4, 256);
-    l.tpad = round_up(T, PVT);
-    l.vdbytes = (int64_t)B * nkv * 2 * hd * l.tpad;
     return l;
 }
 }  // namespace
 
 size_t attention_tc_workspace(int B, int T, int nh, int nkv, int hd) {
     const Layout l = layout(B, T, nh, nkv, hd);
-    return (size_t)(256 + l.qbytes + l.kbytes + l.sbytes + l.mbytes + l.vhbytes + l.vlbytes + l.vdbytes);
+    return (size_t)(256 + l.qbytes + l.kbytes + l.sbytes + l.mbytes);
 }
 
 bool attention_tc_supported(int T, int nh, int nkv, int hd) {
@@ -822,15 +518,11 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     int8_t* kp = qp + l.qbytes;
     int64_t* scores = (int64_t*)(kp + l.kbytes);
     int64_t* rmax = (int64_t*)((uint8_t*)scores + l.sbytes);
-    double* vh = (double*)((uint8_t*)rmax + l.mbytes);
-    uint32_t* vl = (uint32_t*)((uint8_t*)vh + l.vhbytes);
-    int8_t* vd = (int8_t*)((uint8_t*)vl + l.vlbytes);
-    int* pvsel = flag + 1;  // v >> 30 beyond two digits: the fp64 P.V instead of the tensor-core one
     alignas(64) unsigned char mq[128], mk[128];
     if (!encode_planes(mq, qp, l.kpad, l.tq, LA, QM, (int64_t)B * nh) ||
         !encode_planes(mk, kp, l.kpad, l.tk, LA, NK, (int64_t)B * nkv))
         return -1;
-    cudaMemsetAsync(flag, 0, 2 * sizeof(int), st);
+    cudaMemsetAsync(flag, 0, sizeof(int), st);
     split_heads(q, ldq, B, T, nh, hd, l.tq, l.kpad, qp, flag, st);
     split_heads(k, ldk, B, T, nkv, hd, l.tk, l.kpad, kp, flag, st);
 
@@ -850,17 +542,17 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     const int64_t rows = (int64_t)B * nh * T;
     k_softmax<<<(unsigned)((rows + SM_ROWS - 1) / SM_ROWS), 32 * SM_ROWS, 0, st>>>(scores, (int)l.sr, rmax, T, (int)rows,
                                                                                   flag, flag);
-    const int tp = (int)l.tpad, sr = (int)l.sr;
+    const int sr = (int)l.sr;
     switch (hd) {
-        case 16: launch_pv<16>(B, T, nh, nkv, scores, sr, v, ldv, vh, vl, vd, tp, out, ldo, flag, pvsel, err, st); break;
-        case 32: launch_pv<32>(B, T, nh, nkv, scores, sr, v, ldv, vh, vl, vd, tp, out, ldo, flag, pvsel, err, st); break;
-        case 64: launch_pv<64>(B, T, nh, nkv, scores, sr, v, ldv, vh, vl, vd, tp, out, ldo, flag, pvsel, err, st); break;
-        case 128: launch_pv<128>(B, T, nh, nkv, scores, sr, v, ldv, vh, vl, vd, tp, out, ldo, flag, pvsel, err, st); break;
-        default: launch_pv<256>(B, T, nh, nkv, scores, sr, v, ldv, vh, vl, vd, tp, out, ldo, flag, pvsel, err, st); break;
+        case 16: launch_pv<16>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, flag, st); break;
+        case 32: launch_pv<32>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, flag, st); break;
+        case 64: launch_pv<64>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, flag, st); break;
+        case 128: launch_pv<128>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, flag, st); break;
+        default: launch_pv<256>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, flag, st); break;
     }
     // the exact kernel redoes the whole call when anything fell outside the fast ranges
     attention(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, score_shift, sqrt_hd, mode, window, st, flag);
-    return hd <= 64 ? 8 : 7;
+    return 6;
 }
 
 }  // namespace slx

@@ -45,18 +45,40 @@ def test_attention_reference_test_shapes(ctx, oracle):
         np.testing.assert_array_equal(got, ref)
 
 
-@pytest.mark.parametrize("hd", [16, 64])
-def test_attention_large_values_take_fp64_pv(ctx, oracle, hd):
-    """v >> 30 beyond two base-256 digits (|v| near 2^50): the tensor-core P.V steps aside for the fp64
-    one on the device, still exact."""
+@pytest.mark.parametrize("hd", [16, 64, 256])
+def test_attention_values_at_the_fp64_window_edge(ctx, oracle, hd):
+    """|v| up to the P.V's bound 2^50 (the accumulator window [2^52, 2^53) holds every partial sum),
+    with rows at both ends of the range; one value at 2^50 sends the call to the exact kernel."""
     rng = np.random.default_rng(11 + hd)
     seq, nh = 150, 3
     q, k, _ = _qkv(rng, seq, nh * hd, nh * hd, 1 << 32)
     v = rng.integers(-(1 << 50), 1 << 50, (seq, nh * hd), dtype=np.int64)
+    v[0, :] = (1 << 50) - 1
+    v[1, :] = -(1 << 50)
+    v[2, ::2] = (1 << 50) - 1
     for mode in (0, 1):
         got = slx.attention(q, k, v, seq, nh, nh, -30, mode, 0, ctx=ctx)
         ref = oracle.attention(q, k, v, seq, nh * hd, nh * hd, nh, nh, -30, 30, mode, 0).reshape(seq, nh * hd)
         np.testing.assert_array_equal(got, ref)
+    v[7, 5] = 1 << 50
+    got = slx.attention(q, k, v, seq, nh, nh, -30, 0, 0, ctx=ctx)
+    ref = oracle.attention(q, k, v, seq, nh * hd, nh * hd, nh, nh, -30, 30, 0, 0).reshape(seq, nh * hd)
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_attention_one_hot_softmax(ctx, oracle):
+    """One key dominates every row: p = 2^30 for it and 0 elsewhere, so each product p v / 2^30 is an
+    exact integer (the directed rounding must not move it)."""
+    rng = np.random.default_rng(5)
+    seq, nh, hd = 70, 2, 64
+    q = np.full((seq, nh * hd), 1 << 33, np.int64)
+    k = rng.integers(-(1 << 10), 1 << 10, (seq, nh * hd), dtype=np.int64)
+    k[3, :] = 1 << 33
+    v = rng.integers(-(1 << 45), 1 << 45, (seq, nh * hd), dtype=np.int64)
+    got = slx.attention(q, k, v, seq, nh, nh, -30, 0, 0, ctx=ctx)
+    ref = oracle.attention(q, k, v, seq, nh * hd, nh * hd, nh, nh, -30, 30, 0, 0).reshape(seq, nh * hd)
+    np.testing.assert_array_equal(got, ref)
+    np.testing.assert_array_equal(ref, np.broadcast_to(v[3], ref.shape))
 
 
 @pytest.mark.parametrize("what", ["q_wide", "k_wide", "v_wide", "scores_wrap"])
