@@ -263,25 +263,22 @@ void launch_scores_kb(const CUtensorMap& tq, const CUtensorMap& tk, ScoreParams 
 // softmax, then P.V
 // ---------------------------------------------------------------------------------------------
 // FixedExp(x) for the softmax's x = score - max (IntegerTranscendentals.cs FixedExp): k = -ceil(-x / ln2),
-// r = x - k ln2 in [0, ln2), e^r by the truncating Taylor recurrence (exp_taylor30), then e^r >> -k.
-// x > 0 (a wrapped difference) and x near long.MinValue (where the reference's own range reduction
-// wraps) set bad.
+// r = x - k ln2 in [0, ln2) (ln2_reduce, on the fp64 pipe), e^r by the truncating Taylor recurrence
+// (exp_taylor30_fp), then e^r >> -k. x > 0 (a wrapped difference) and x near long.MinValue (where the
+// reference's own range reduction wraps) set bad.
 SLX_DEV uint32_t exp_nonpos30(int64_t x, bool& bad) {
     constexpr int64_t LN2 = 744261117;  // (long)(0.6931471805599453 * 2^30)
     if (x > 0 || x < -(1LL << 62)) { bad = true; return 0; }
     if (x < -30 * LN2) return 0;  // a shift of 31 or more clears e^r < 2^31
-    const int64_t nx = -x;        // < 2^35, exact in double
-    int64_t c = (int64_t)((double)nx * (1.0 / (double)LN2));
-    int64_t r = c * LN2 - nx;     // c = ceil(nx / ln2) <=> 0 <= r < ln2
-    if (r < 0) { c++; r += LN2; }
-    else if (r >= LN2) { c--; r -= LN2; }
-    return exp_taylor30((uint32_t)r) >> c;  // c <= 30
+    double r;
+    const int k = ln2_reduce(d_i64(x), r);  // -30 <= k <= 0
+    return exp_taylor30_fp((uint32_t)rd_i32(r + RD_BASE), r) >> -k;
 }
 
 // floor(e * 2^30 / sum) for e <= 2^30 and sum in [1, 2^41): an fp64 estimate (within one) corrected
 // by the exact remainder.
 SLX_DEV uint32_t p_div(uint32_t e, uint64_t sum, double inv30) {
-    int64_t q = (int64_t)((double)e * inv30);
+    int64_t q = rd_i32(rd_floor(d_u32(e), inv30));
     int64_t r = (int64_t)(((uint64_t)e << 30) - (uint64_t)q * sum);
     if (r < 0) q--;
     else if (r >= (int64_t)sum) q++;
@@ -427,19 +424,17 @@ __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const
             Pd[r * PDS + s] = (double)Pu[r * PUS + s];
         }
         __syncthreads();
-#pragma unroll 2
-        for (int s = 0; s < VT; s += 2) {
+#pragma unroll 4
+        for (int s = 0; s < VT; s++) {  // one key at a time: every accumulator once per key
             const double2 a0 = *(const double2*)(Vs + s * HD + c0);
             const double2 a1 = *(const double2*)(Vs + s * HD + c1);
-            const double2 b0 = *(const double2*)(Vs + (s + 1) * HD + c0);
-            const double2 b1 = *(const double2*)(Vs + (s + 1) * HD + c1);
 #pragma unroll
             for (int r = 0; r < RPT; r++) {
-                const double2 pd = *(const double2*)(Pd + (rg + RG * r) * PDS + s);
-                acc[r][0] = __fma_rd(pd.y, b0.x, __fma_rd(pd.x, a0.x, acc[r][0]));
-                acc[r][1] = __fma_rd(pd.y, b0.y, __fma_rd(pd.x, a0.y, acc[r][1]));
-                acc[r][2] = __fma_rd(pd.y, b1.x, __fma_rd(pd.x, a1.x, acc[r][2]));
-                acc[r][3] = __fma_rd(pd.y, b1.y, __fma_rd(pd.x, a1.y, acc[r][3]));
+                const double p = Pd[(rg + RG * r) * PDS + s];
+                acc[r][0] = __fma_rd(p, a0.x, acc[r][0]);
+                acc[r][1] = __fma_rd(p, a0.y, acc[r][1]);
+                acc[r][2] = __fma_rd(p, a1.x, acc[r][2]);
+                acc[r][3] = __fma_rd(p, a1.y, acc[r][3]);
             }
         }
     }

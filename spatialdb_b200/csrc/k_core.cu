@@ -584,13 +584,13 @@ int attention(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, cons
 namespace {
 // IntegerFFN.Apply: up[i] = (long)((Int128)FixedSiLU(gate[i]) * up[i] >> 30) (IntegerFFN.cs:84-89)
 __global__ void k_silu_gate(const int64_t* __restrict__ G, int64_t ldg, int64_t* __restrict__ U, int64_t ldu, int F,
-                            int64_t total) {
-    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= total) return;
-    int64_t m = i / F, f = i % F;
-    int64_t g = G[m * ldg + f];
-    int64_t* u = U + m * ldu + f;
-    *u = lo64(sar128((i128)fixed_silu30(g) * *u, 30));
+                            int rows) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    if (f >= F) return;
+    for (int m = blockIdx.y; m < rows; m += gridDim.y) {
+        int64_t* u = U + (int64_t)m * ldu + f;
+        *u = silu_gate30(G[(int64_t)m * ldg + f], *u);
+    }
 }
 
 __global__ void k_add(int64_t* __restrict__ D, int64_t ldd, const int64_t* __restrict__ S, int64_t lds, int n,
@@ -766,9 +766,9 @@ __global__ void k_keys_to_ids(const unsigned long long* keys, int B, int32_t* id
 }  // namespace
 
 int silu_gate(const int64_t* gate, int64_t ldg, int64_t* up, int64_t ldu, int M, int F, cudaStream_t st) {
-    int64_t total = (int64_t)M * F;
-    if (total <= 0) return 0;
-    k_silu_gate<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(gate, ldg, up, ldu, F, total);
+    if (M <= 0 || F <= 0) return 0;
+    const dim3 grid((unsigned)((F + 255) / 256), (unsigned)(M < 65535 ? M : 65535));
+    k_silu_gate<<<grid, 256, 0, st>>>(gate, ldg, up, ldu, F, M);
     return 1;
 }
 

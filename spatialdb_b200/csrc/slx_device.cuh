@@ -190,38 +190,93 @@ SLX_DEV uint32_t exp_taylor30(uint32_t r) {
     return sum;
 }
 
-// FixedExp for |y| <= 2^35 (FixedSigmoid's arguments lie within 20 * 2^30): the reference's range
-// reduction is k = floor(y / ln2) (truncation for y >= 0, -ceil(-y / ln2) below), r = y - k ln2 in
-// [0, ln2), so its 32-bit Taylor branch always runs (exp_taylor30). k is estimated in double
-// (|y| < 2^35 is exact) and corrected by the remainder. Same result as fixed_exp30 on this range.
-SLX_DEV int64_t fixed_exp30_bounded(int64_t y) {
-    constexpr int64_t LN2 = 744261117;
-    int64_t k = (int64_t)floor((double)y * (1.0 / (double)LN2));
-    int64_t r = y - k * LN2;
-    if (r < 0) { k--; r += LN2; }
-    else if (r >= LN2) { k++; r -= LN2; }
-    const uint32_t sum = exp_taylor30((uint32_t)r);
-    if (k >= 0) {
-        if (k >= 63 || (int64_t)sum > (INT64_MAX >> k)) return INT64_MAX;
-        return (int64_t)((uint64_t)sum << k);
-    }
-    return -k >= 31 ? 0 : (int64_t)(sum >> -k);  // sum < 2^31
+// ---- exact fixed-point steps on the fp64 pipe
+// The doubles in [2^52, 2^53) are exactly the integers there. For doubles a, b holding exact values
+// and |floor(a b)| < 2^51, fma_rd(a, b, 1.5 * 2^52) rounds the exact a b + 1.5 * 2^52 toward minus
+// infinity, which is 1.5 * 2^52 + floor(a b): one instruction for a floored fixed-point product.
+// The integer is the bit pattern minus that of 1.5 * 2^52 (its low word when it fits in 32 bits),
+// and an integer below 2^51 in magnitude becomes an exact double the same way backwards.
+constexpr double RD_BASE = 6755399441055744.0;  // 1.5 * 2^52
+constexpr int64_t RD_BASE_BITS = 0x4338000000000000LL;
+SLX_DEV double rd_floor(double a, double b) { return __fma_rd(a, b, RD_BASE); }
+SLX_DEV int32_t rd_i32(double y) { return __double2loint(y); }
+SLX_DEV int64_t rd_i64(double y) { return __double_as_longlong(y) - RD_BASE_BITS; }
+SLX_DEV double d_u32(uint32_t x) { return __hiloint2double(0x43380000, (int)x) - RD_BASE; }
+SLX_DEV double d_i64(int64_t x) { return __longlong_as_double(RD_BASE_BITS + x) - RD_BASE; }  // |x| < 2^51
+SLX_DEV double pow2d(int k) { return __hiloint2double((1023 + k) << 20, 0); }                  // |k| < 1023
+
+// exp_taylor30 with its work split between the fp64 and integer pipes; every term is the same
+// integer. floor(t r / 2^30) is one fp64 FMA rounded down (so are the whole terms n = 2, 4, 8, whose
+// divisions are powers of two folded into r), the other divisions by n are exp_taylor30's
+// multiply-high constants, and the terms n = 3 and 7 stay entirely on the integer pipe. rd = r.
+SLX_DEV uint32_t exp_taylor30_fp(uint32_t r, double rd) {
+    const uint32_t r4 = r << 2;
+    const double r30 = rd * 0x1p-30;
+    uint32_t sum = (1u << 30) + r, t;                                                          // n = 1
+    double y = rd_floor(rd, rd * 0x1p-31);
+    t = (uint32_t)rd_i32(y); sum += t;                                                         // n = 2
+    t = __umulhi(__umulhi(t, r4), 1431655766u); sum += t;                                      // n = 3
+    y = rd_floor(d_u32(t), rd * 0x1p-32);
+    t = (uint32_t)rd_i32(y); sum += t;                                                         // n = 4
+    y = rd_floor(y - RD_BASE, r30);
+    t = __umulhi((uint32_t)rd_i32(y), 858993460u); sum += t;                                   // n = 5
+    y = rd_floor(d_u32(t), r30);
+    t = __umulhi((uint32_t)rd_i32(y), 715827883u); sum += t;                                   // n = 6
+    t = __umulhi(__umulhi(t, r4), 613566757u); sum += t;                                       // n = 7
+    y = rd_floor(d_u32(t), rd * 0x1p-33);
+    t = (uint32_t)rd_i32(y); sum += t;                                                         // n = 8
+    y = rd_floor(y - RD_BASE, r30);
+    t = __umulhi((uint32_t)rd_i32(y), 477218589u); sum += t;                                   // n = 9
+    y = rd_floor(d_u32(t), r30);
+    t = __umulhi((uint32_t)rd_i32(y), 429496730u); sum += t;                                   // n = 10
+    return sum;
 }
 
-SLX_DEV int64_t fixed_sigmoid30(int64_t x) {
-    const int64_t one = 1LL << 30, thr = 20LL << 30;
-    if (x > thr) return one;
-    if (x < -thr) return 0;
-    // |x| <= 20 * 2^30: e^-x in [2^30 e^-20, 2^30 e^20], den in [2^30, 2^59]
-    const int64_t den = one + fixed_exp30_bounded(-x);
-    // 2^60 / den: estimate within one, then exact correction
-    int64_t q = (int64_t)(1152921504606846976.0 * __drcp_rn((double)den));
-    int64_t r = (int64_t)((1ULL << 60) - (uint64_t)q * (uint64_t)den);
-    while (r < 0) { q--; r += den; }
-    while (r >= den) { q++; r -= den; }
-    return q;
+// floor(y / ln2) and y - floor(y / ln2) ln2 in [0, ln2) for |y| < 2^50, ln2 = 744261117 (2^30 ln 2
+// truncated): the fp64 estimate is within one, the exact remainder (an integer below 2^51) picks it.
+SLX_DEV int ln2_reduce(double yd, double& rem) {
+    constexpr double LN2D = 744261117.0;
+    const double ky = rd_floor(yd, 1.0 / LN2D);
+    int k = rd_i32(ky);
+    double r = __fma_rn(-(ky - RD_BASE), LN2D, yd);
+    if (r < 0.0) { k--; r += LN2D; }
+    else if (r >= LN2D) { k++; r -= LN2D; }
+    rem = r;
+    return k;
 }
-SLX_DEV int64_t fixed_silu30(int64_t x) { return lo64(sar128((i128)x * fixed_sigmoid30(x), 30)); }
+
+// FixedSigmoid / FixedSiLU (IntegerTranscendentals.cs:49-69), fracBits = 30, and the gated product
+// (long)((Int128)FixedSiLU(g) * u >> 30) of IntegerFFN (Math/IntegerFFN.cs:70-100).
+// FixedExp(-g) for |g| <= 20 * 2^30: the reference's k = floor(y / ln2) (truncation for y >= 0,
+// -ceil(-y / ln2) below), r = y - k ln2, so its 32-bit Taylor branch always runs; k <= 28, so
+// e = sum << k never overflows, and k >= -29. den = 2^30 + e < 2^60 is an exact double (at most 32
+// significant bits). 2^60 / den: the fp64 estimate floor(2^60 rcp(den)) corrected by the exact
+// remainder. FixedSiLU = floor(g sig / 2^30) is one rounded-down FMA (|result| <= 20 * 2^30). The
+// gated product takes the same FMA when |s|, |u| < 2^51 and |s u| < 2^80, else Int128.
+SLX_DEV int64_t silu_gate30(int64_t g, int64_t u) {
+    constexpr int64_t one = 1LL << 30, thr = 20LL << 30;
+    int64_t s;
+    if (g > thr) s = g;
+    else if (g < -thr) s = 0;
+    else {
+        double rem;
+        const int k = ln2_reduce(d_i64(-g), rem);
+        const uint32_t sum = exp_taylor30_fp((uint32_t)rd_i32(rem + RD_BASE), rem);
+        const int64_t den = one + (k >= 0 ? (int64_t)sum << k : (int64_t)(sum >> -k));
+        const double den_d = k >= 0 ? __fma_rn(d_u32(sum), pow2d(k), 1073741824.0) : d_i64(den);
+        int64_t q = rd_i32(rd_floor(1152921504606846976.0, __drcp_rn(den_d)));
+        int64_t r = (int64_t)((1ULL << 60) - (uint64_t)q * (uint64_t)den);
+        while (r < 0) { q--; r += den; }
+        while (r >= den) { q++; r -= den; }
+        s = rd_i64(rd_floor(d_i64(g), d_u32((uint32_t)q) * 0x1p-30));
+    }
+    const int64_t lim = 1LL << 51;
+    if (s > -lim && s < lim && u > -lim && u < lim) {
+        const double sd = d_i64(s), ud = d_i64(u);
+        if (fabs(sd * ud) < 0x1p80) return rd_i64(rd_floor(sd, ud * 0x1p-30));
+    }
+    return lo64(sar128((i128)s * u, 30));
+}
 
 // 128-bit warp reductions (wrap-around sums).
 SLX_DEV u128 warp_sum_u128(u128 v) {
