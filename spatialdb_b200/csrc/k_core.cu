@@ -328,8 +328,8 @@ __global__ __launch_bounds__(NT) void k_layernorm(int64_t* __restrict__ X, int64
     const int64_t isq = s_isq;
     const double rd = 1.0 / (double)isq;
     for (int j = threadIdx.x; j < n; j += NT) {
-        int64_t dl = wsub(x[j], mean);
-        x[j] = wadd(div_trunc((i128)dl * w[j], isq, rd), b[j]);
+        const int64_t dl = wsub(x[j], mean), wj = w[j];
+        x[j] = wadd(muldiv_trunc(dl, wj, d_i64(wj), isq, rd), b[j]);
     }
 }
 
@@ -363,9 +363,11 @@ template <int PER>
 __global__ __launch_bounds__(256) void k_layernorm_warp(int64_t* __restrict__ X, int64_t ld, int rows, int n,
                                                          const int64_t* __restrict__ w, const int64_t* __restrict__ b) {
     __shared__ int64_t sw[32 * PER], sb[32 * PER];  // the row's weight and bias, staged once per block
+    __shared__ double swd[32 * PER];                 // the weight as a double (exact below 2^51)
     for (int j = threadIdx.x; j < n; j += blockDim.x) {
         sw[j] = w[j];
         sb[j] = b[j];
+        swd[j] = d_i64(w[j]);
     }
     __syncthreads();
     const int lane = threadIdx.x & 31;
@@ -405,7 +407,7 @@ __global__ __launch_bounds__(256) void k_layernorm_warp(int64_t* __restrict__ X,
 #pragma unroll
         for (int i = 0; i < PER; i++) {
             const int j = lane + 32 * i;
-            if (j < n) __stcs(x + j, wadd(div_trunc((i128)v[i] * sw[j], isq, rd), sb[j]));
+            if (j < n) __stcs(x + j, wadd(muldiv_trunc(v[i], sw[j], swd[j], isq, rd), sb[j]));
         }
     }
 }
@@ -431,7 +433,10 @@ __global__ __launch_bounds__(NT) void k_rmsnorm(int64_t* __restrict__ X, int64_t
     if (s_skip) return;
     const int64_t rms = s_rms;
     const double rd = 1.0 / (double)rms;
-    for (int j = threadIdx.x; j < n; j += NT) x[j] = div_trunc((i128)x[j] * w[j], rms, rd);
+    for (int j = threadIdx.x; j < n; j += NT) {
+        const int64_t wj = w[j];
+        x[j] = muldiv_trunc(x[j], wj, d_i64(wj), rms, rd);
+    }
 }
 }  // namespace
 

@@ -134,29 +134,8 @@ SLX_DEV int64_t fixed_exp30(int64_t x) {
     return sum >> sh;
 }
 
-// Truncating num / d for d >= 1 with rd = 1.0 / d: a double estimate corrected to the exact
-// quotient by its integer remainder. Used when |num| < 2^62 and the quotient is below 2^50, where
-// the estimate is within one of the quotient; any other case divides in Int128.
-// (long)(num / d), truncating toward zero, for d >= 1 and rd ~ 1/d: a double estimate of the
-// quotient (off by at most one while |num / d| < 2^50) corrected by the remainder, which is small
-// and so exact in wrapping 64-bit arithmetic; wider quotients take the Int128 division.
-SLX_DEV int64_t div_trunc(i128 num, int64_t d, double rd) {
-    const double nd = (double)(int64_t)(num >> 64) * 18446744073709551616.0 + (double)(uint64_t)num;
-    const double qd = nd * rd;
-    if (qd > -1125899906842624.0 && qd < 1125899906842624.0) {  // |q| < 2^50
-        int64_t q = (int64_t)qd;
-        int64_t r = (int64_t)((uint64_t)num - (uint64_t)q * (uint64_t)d);
-        if (num >= 0) {
-            while (r < 0) { q--; r += d; }
-            while (r >= d) { q++; r -= d; }
-        } else {
-            while (r > 0) { q++; r -= d; }
-            while (r <= -d) { q--; r += d; }
-        }
-        return q;
-    }
-    return lo64(num / (i128)d);
-}
+// (long)(x / d), truncating toward zero, for d >= 1 and rd ~ 1 / d: a double estimate of |x| / d
+// (off by at most one below 2^52) corrected by the remainder; wider values take the 64-bit division.
 SLX_DEV int64_t div_small(int64_t x, int64_t d, double rd) {
     const uint64_t ax = x < 0 ? (uint64_t)0 - (uint64_t)x : (uint64_t)x;
     if (ax < (1ULL << 52)) {
@@ -169,7 +148,7 @@ SLX_DEV int64_t div_small(int64_t x, int64_t d, double rd) {
     return cs_div64(x, d);
 }
 
-// FixedSigmoid / FixedSiLU (IntegerTranscendentals.cs:49-69), fracBits = 30.
+// FixedExp's Taylor branch (IntegerTranscendentals.cs:13-47), fracBits = 30.
 // e^r * 2^30 for r in [0, ln2), by FixedExp's truncating Taylor recurrence term = (term * r >> 30) / n
 // (IntegerTranscendentals.cs:13-47): every term past the tenth is zero on this range,
 // (term * r) >> 30 = umulhi(term, 4r), and each floor(x / n) equals umulhi(x, ceil(2^32 / n)) for the
@@ -204,6 +183,27 @@ SLX_DEV int64_t rd_i64(double y) { return __double_as_longlong(y) - RD_BASE_BITS
 SLX_DEV double d_u32(uint32_t x) { return __hiloint2double(0x43380000, (int)x) - RD_BASE; }
 SLX_DEV double d_i64(int64_t x) { return __longlong_as_double(RD_BASE_BITS + x) - RD_BASE; }  // |x| < 2^51
 SLX_DEV double pow2d(int k) { return __hiloint2double((1023 + k) << 20, 0); }                  // |k| < 1023
+
+// trunc(a w / d) for d >= 1 (the reference's Int128 division, truncating toward zero) with wd = w as
+// a double and rd ~ 1 / d. When |a|, |w| < 2^51, d < 2^60 and the quotient is below 2^49 in magnitude,
+// floor(|a w| rd) from one product and one rounded-down FMA is within one of floor(|a w| / d) (and
+// almost always equal), and the remainder |a w| - q d, exact in wrapping 64-bit arithmetic because
+// |r| < 2 d, fixes it; anything else takes the Int128 division.
+SLX_DEV int64_t muldiv_trunc(int64_t a, int64_t w, double wd, int64_t d, double rd) {
+    constexpr int64_t lim = 1LL << 51;
+    if (a > -lim && a < lim && w > -lim && w < lim && d < (1LL << 60)) {
+        int64_t q = rd_i64(rd_floor(fabs(d_i64(a) * wd), rd));
+        if (q < (1LL << 49)) {
+            const uint64_t ua = a < 0 ? (uint64_t)0 - (uint64_t)a : (uint64_t)a;
+            const uint64_t uw = w < 0 ? (uint64_t)0 - (uint64_t)w : (uint64_t)w;
+            int64_t r = (int64_t)(ua * uw - (uint64_t)q * (uint64_t)d);
+            while (r < 0) { q--; r += d; }
+            while (r >= d) { q++; r -= d; }
+            return (a < 0) != (w < 0) ? -q : q;
+        }
+    }
+    return lo64(((i128)a * w) / (i128)d);
+}
 
 // exp_taylor30 with its work split between the fp64 and integer pipes; every term is the same
 // integer. floor(t r / 2^30) is one fp64 FMA rounded down (so are the whole terms n = 2, 4, 8, whose
