@@ -360,7 +360,7 @@ SLX_DEV int64_t div_i128_n(u128 s, uint32_t n, uint64_t inv) {
 }
 
 template <int PER>
-__global__ __launch_bounds__(256) void k_layernorm_warp(int64_t* __restrict__ X, int64_t ld, int rows, int n,
+__global__ __launch_bounds__(256, 4) void k_layernorm_warp(int64_t* __restrict__ X, int64_t ld, int rows, int n,
                                                          const int64_t* __restrict__ w, const int64_t* __restrict__ b) {
     __shared__ int64_t sw[32 * PER], sb[32 * PER];  // the row's weight and bias, staged once per block
     __shared__ double swd[32 * PER];                 // the weight as a double (exact below 2^51)
@@ -442,7 +442,7 @@ __global__ __launch_bounds__(NT) void k_rmsnorm(int64_t* __restrict__ X, int64_t
 
 int layernorm_rows(int64_t* x, int64_t ld, int rows, int n, const int64_t* w, const int64_t* b, cudaStream_t st) {
     if (rows <= 0) return 0;
-    const unsigned wb = (unsigned)std::min((rows + 7) / 8, 148 * 4);
+    const unsigned wb = (unsigned)std::min((rows + 7) / 8, 148 * 4);  // four blocks per SM
     if (n <= 256) k_layernorm_warp<8><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b);
     else if (n <= 512) k_layernorm_warp<16><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b);
     else if (n <= 768) k_layernorm_warp<24><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b);
