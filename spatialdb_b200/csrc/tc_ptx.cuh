@@ -101,8 +101,6 @@ __device__ __forceinline__ uint64_t sw64_desc(uint32_t addr) {
 __host__ __device__ constexpr uint32_t idesc_i8(int n) {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
-// The same with an unsigned 8-bit A operand (A format 0 = u8, 1 = s8; B stays s8).
-__host__ __device__ constexpr uint32_t idesc_u8s8(int n) { return idesc_i8(n) & ~(1u << 7); }
 
 __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
