@@ -148,27 +148,6 @@ SLX_DEV int64_t div_small(int64_t x, int64_t d, double rd) {
     return cs_div64(x, d);
 }
 
-// FixedExp's Taylor branch (IntegerTranscendentals.cs:13-47), fracBits = 30.
-// e^r * 2^30 for r in [0, ln2), by FixedExp's truncating Taylor recurrence term = (term * r >> 30) / n
-// (IntegerTranscendentals.cs:13-47): every term past the tenth is zero on this range,
-// (term * r) >> 30 = umulhi(term, 4r), and each floor(x / n) equals umulhi(x, ceil(2^32 / n)) for the
-// x that step can see (n = 2, 4, 8 are shifts) -- the sum agrees with the recurrence for every r in
-// [0, ln2).
-SLX_DEV uint32_t exp_taylor30(uint32_t r) {
-    const uint32_t r4 = r << 2;
-    uint32_t t = r, sum = (1u << 30) + r;  // n = 1
-    t = __umulhi(t, r4) >> 1; sum += t;
-    t = __umulhi(__umulhi(t, r4), 1431655766u); sum += t;
-    t = __umulhi(t, r4) >> 2; sum += t;
-    t = __umulhi(__umulhi(t, r4), 858993460u); sum += t;
-    t = __umulhi(__umulhi(t, r4), 715827883u); sum += t;
-    t = __umulhi(__umulhi(t, r4), 613566757u); sum += t;
-    t = __umulhi(t, r4) >> 3; sum += t;
-    t = __umulhi(__umulhi(t, r4), 477218589u); sum += t;
-    t = __umulhi(__umulhi(t, r4), 429496730u); sum += t;
-    return sum;
-}
-
 // ---- exact fixed-point steps on the fp64 pipe
 // The doubles in [2^52, 2^53) are exactly the integers there. For doubles a, b holding exact values
 // and |floor(a b)| < 2^51, fma_rd(a, b, 1.5 * 2^52) rounds the exact a b + 1.5 * 2^52 toward minus
@@ -205,10 +184,14 @@ SLX_DEV int64_t muldiv_trunc(int64_t a, int64_t w, double wd, int64_t d, double 
     return lo64(((i128)a * w) / (i128)d);
 }
 
-// exp_taylor30 with its work split between the fp64 and integer pipes; every term is the same
-// integer. floor(t r / 2^30) is one fp64 FMA rounded down (so are the whole terms n = 2, 4, 8, whose
-// divisions are powers of two folded into r), the other divisions by n are exp_taylor30's
-// multiply-high constants, and the terms n = 3 and 7 stay entirely on the integer pipe. rd = r.
+// FixedExp's Taylor branch (IntegerTranscendentals.cs:13-47), fracBits = 30: e^r * 2^30 for r in
+// [0, ln2) by the truncating recurrence term_n = (term * r >> 30) / n. Every term past the tenth is
+// zero on this range, and each floor(x / n) equals umulhi(x, ceil(2^32 / n)) for the x that step can
+// see, so the sum agrees with the recurrence for every r in [0, ln2). The work is split between the
+// fp64 and integer pipes: floor(t r / 2^30) is one fp64 FMA rounded down (so are the whole terms
+// n = 2, 4, 8, whose divisions are powers of two folded into r), the other divisions by n are those
+// multiply-high constants, and the terms n = 3 and 7 are umulhi(umulhi(t, 4r), c) on the integer
+// pipe. rd = r.
 SLX_DEV uint32_t exp_taylor30_fp(uint32_t r, double rd) {
     const uint32_t r4 = r << 2;
     const double r30 = rd * 0x1p-30;
