@@ -62,21 +62,54 @@ def recorded_traffic(kernel: str) -> float | None:
 
 
 class Clocks:
-    """nvidia-smi samples of one GPU's clocks during the timed region."""
+    """nvidia-smi samples (every 50 ms, timestamped) of one GPU's clocks; started before the warm-up
+    so the sampler is running when the timed loops begin, and reduced to the samples inside them."""
 
-    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+    Q = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, index: int):
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "50"],
                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.p = None
 
-    def stop(self) -> dict | None:
+    @classmethod
+    def summarize(cls, lines, t0: float | None = None, t1: float | None = None) -> dict | None:
+        """Median SM clock, max clock and active throttle reasons of the samples whose timestamps
+        (local time) fall in [t0, t1] (host epoch seconds, 50 ms of slack each side); all samples when
+        no window is given or none falls inside it."""
+        import datetime
+
+        rows = []
+        for line in lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm, mx = float(f[1]), float(f[2])
+            except ValueError:
+                continue
+            try:
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                ts = None
+            rows.append((ts, sm, mx, [n for n, v in zip(cls.NAMES, f[5:9]) if v.lower().startswith("active")]))
+        if not rows:
+            return None
+        inside = rows
+        if t0 is not None and t1 is not None:
+            sel = [r for r in rows if r[0] is not None and t0 - 0.05 <= r[0] <= t1 + 0.05]
+            inside = sel or rows
+        reasons = sorted({n for r in inside for n in r[3]})
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": inside[-1][2], "reasons": reasons,
+                "samples": len(inside), "window": "timed loops" if inside is not rows else "whole run"}
+
+    def stop(self, t0: float | None = None, t1: float | None = None) -> dict | None:
         if self.p is None:
             return None
         self.p.terminate()
@@ -85,23 +118,7 @@ class Clocks:
         except subprocess.TimeoutExpired:
             self.p.kill()
             out, _ = self.p.communicate()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 8:
-                continue
-            try:
-                sm.append(float(f[0]))
-                mx = float(f[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[4:8]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return self.summarize(out.splitlines(), t0, t1)
 
 
 def gemv_bench(ctx, torch, stream, iters: int = 200) -> dict:
@@ -579,6 +596,7 @@ def run_ours(args) -> None:
     def step(i):
         model.encode_device(ids_dev[i].data_ptr(), B, SEQ, pooled.data_ptr(), stream.cuda_stream)
 
+    clocks = Clocks(local) if rank == 0 else None  # sampling from before the warm-up to after the e2e loop
     for i in range(W):
         flush.zero_()
         step(i)
@@ -591,7 +609,7 @@ def run_ours(args) -> None:
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = Clocks(local) if rank == 0 else None
+    tw0 = time.time()
     for i in range(K):
         flush.zero_()
         ev[i][0].record(stream)
@@ -600,7 +618,6 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    clk = clocks.stop() if clocks else None
     step_ms = [a.elapsed_time(b) for a, b in ev]
     stats = (KernelStat * 16)()
     nstat = ctypes_int()
@@ -624,6 +641,7 @@ def run_ours(args) -> None:
     for i in range(K):
         out_host[:] = model.forward(ids_pinned[W + i])
     e2e_s = time.perf_counter() - t0
+    clk = clocks.stop(tw0, time.time()) if clocks else None  # samples inside the device-timed and e2e loops
     te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
