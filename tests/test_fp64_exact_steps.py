@@ -173,6 +173,10 @@ def test_softmax_division(oracle):
             continue
         for e in es[:20]:
             assert p_div(e, total) == (e << 30) // total
+    # extremes: one key takes everything, a sum of one, sums near the 2^41 bound
+    for e, total in [(1 << 30, 1 << 30), (1, 1), (0, 1), ((1 << 30) - 1, (1 << 41) - 1), (1 << 30, (1 << 41) - 1),
+                     (12345, 12346), ((1 << 30), (1 << 30) + 1)]:
+        assert p_div(e, total) == (e << 30) // total, (e, total)
 
 
 def test_norm_division_matches_int128():
