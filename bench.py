@@ -40,9 +40,39 @@ def workload_name(batch: int) -> str:
 def model_path() -> str:
     from spatialdb_b200 import synth
 
-    shape = synth.EncoderShape(**ARCH)
-    return synth.cached("encoder_nomic_L12_d768_q4_0_seed3.gguf",
-                        lambda p: synth.write_encoder(p, shape, synth.Q4_0, seed=3))
+    assert synth.EncoderShape() == synth.EncoderShape(**ARCH)
+    return synth.encoder_q4_0_model()
+
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def golden(name: str) -> dict:
+    """A committed fixture of the oracle's outputs at a configuration's full size."""
+    import numpy as np
+
+    return dict(np.load(os.path.join(GOLDEN, name)))
+
+
+def class_roofline(cls: dict, name: str, peak_tops: float, peak_source: str) -> dict | None:
+    """Roofline of one kernel class from the library's event profile: the algorithmic int64
+    multiply-accumulate rate against the int8 tensor peak (frac), and the int8 digit products the
+    exact path issues for it (frac_digit; 5 activation x the weight's digits per multiply-accumulate)."""
+    g = cls.get(name)
+    if g is None or g.ms <= 0:
+        return None
+    sec = g.ms / 1000.0
+    alg = 2.0 * g.macs / sec / 1e12
+    dig = 2.0 * g.tc_macs / sec / 1e12
+    per_mac = g.tc_macs / g.macs if g.macs else 0.0
+    return {"bound": "tensor", "achieved": alg, "peak": peak_tops, "unit": "TOPS", "frac": alg / peak_tops,
+            "ops": "algorithmic: 2 x int64 multiply-accumulates (rows x N x K)",
+            "peak_source": peak_source,
+            "achieved_digit": dig, "frac_digit": dig / peak_tops,
+            "digit_products_per_mac": per_mac,
+            "exact_ceiling_tops": peak_tops / per_mac if per_mac else None,
+            "exact_ceiling_frac": (alg / (peak_tops / per_mac)) if per_mac else None,
+            "launches": int(g.launches), "avg_launch_ms": g.ms / max(1, g.launches)}
 
 
 def measured_peaks() -> dict:
@@ -183,7 +213,185 @@ def gemv_bench(ctx, torch, stream, iters: int = 200) -> dict:
     return out
 
 
-def gemma_bench(ctx, decode_b1: int = 128, decode_b16: int = 8) -> dict:
+def gemm_bench(ctx, torch, stream, reps: int = 10, check_rows: int = 4) -> dict:
+    """Prefill-shaped dequant+matmul microbench (the kernel microbench configuration at M = 128 and
+    512): Q8_0 / Q4_0 weights of K 4096 x N 4096 and 4096 x 11008 prepared once
+    (slx_weight_prepare: the tensor-core digit planes), Q30 activations from fp32 N(0, 1)
+    (QuantizeFromFloat). Per call: L2 flushed, then CUDA events around slx_matmul_q30_prepared
+    (activation digit split + tcgen05 GEMM). The first rows of every product are checked against the
+    oracle's IntegerMatMul."""
+    import numpy as np
+
+    import oracle
+    import spatialdb_b200 as slx
+    from spatialdb_b200 import synth
+    from spatialdb_b200._lib import KernelStat
+
+    lib = ctx._lib
+    peaks = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    rng = np.random.default_rng(12)
+    out = {"l2": "flushed (256 MiB write) before every call, outside its events",
+           "activations": "Q30 of fp32 N(0,1) (QuantizeFromFloat)", "peak_tops": int8_peak,
+           "peak_source": f"2 x {peaks['source']} bf16 dense ({peaks['bf16_tflops']} TF/s)"}
+    parity = True
+    for K, N in ((4096, 4096), (4096, 11008)):
+        for name, dtype in (("q8_0", synth.Q8_0), ("q4_0", synth.Q4_0)):
+            raw = synth.random_q4_0(rng, N * K) if dtype == synth.Q4_0 else synth.random_q8_0(rng, N * K)
+            d_w = torch.from_numpy(raw).cuda()
+            w = slx.PreparedWeight(d_w.data_ptr(), raw.size, dtype, N, K, ctx=ctx)
+            wq = None
+            for M in (128, 512):
+                x = torch.randn(M, K, dtype=torch.float32, generator=torch.Generator().manual_seed(100 + M))
+                a = torch.trunc(x.double() * 2.0 ** 30).long().cuda()
+                c = torch.empty((M, N), dtype=torch.int64, device="cuda")
+                for _ in range(2):
+                    w.matmul_device(a.data_ptr(), M, c.data_ptr(), stream=stream.cuda_stream)
+                torch.cuda.synchronize()
+                ctx.status(stream.cuda_stream)
+                if wq is None:
+                    wq = oracle.quantize_from_float(oracle.dequantize(dtype, raw, N * K))
+                a_host = a.cpu().numpy()
+                want = oracle.matmul_long(a_host[:check_rows], check_rows, K, wq, N, 30).reshape(check_rows, N)
+                ok = bool(np.array_equal(c[:check_rows].cpu().numpy(), want))
+                parity = parity and ok
+                lib.slx_profile_begin(ctx._h)
+                ev = []
+                for _ in range(reps):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    w.matmul_device(a.data_ptr(), M, c.data_ptr(), stream=stream.cuda_stream)
+                    e1.record(stream)
+                    ev.append((e0, e1))
+                torch.cuda.synchronize()
+                stats = (KernelStat * 16)()
+                nst = ctypes_int()
+                lib.slx_profile_end(ctx._h, stats, 16, nst)
+                ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / reps
+                g = {s.name.decode(): s for s in stats[: nst.value]}.get("gemm")
+                alg = 2.0 * M * N * K / (ms / 1000.0) / 1e12
+                dig = 2.0 * g.tc_macs / reps / (ms / 1000.0) / 1e12 if g is not None else None
+                out[f"{name}_k{K}_n{N}_m{M}"] = {
+                    "us_per_call": 1000 * ms, "tops": alg, "frac_of_int8_peak": alg / int8_peak,
+                    "digit_tops": dig, "frac_digit": dig / int8_peak if dig is not None else None,
+                    "weight_digits": w.digits, "parity_rows_vs_oracle": ok}
+            w.close()
+            del d_w
+    out["parity_vs_oracle"] = parity
+    return out
+
+
+def encoder_q8_0_bench(ctx, torch, stream, steps: int, warmup: int, cpu: bool = True) -> dict:
+    """The CPU-runnable encoder configuration: nomic-bert 12L d768 H12 F3072 V30522 with Q8_0
+    weights, a batch of 32 sequences of 128 ids. Device time per step from CUDA events (L2 flushed
+    before each step, outside its events); e2e through the host-buffer entry point (pinned ids in,
+    pooled int64 out, per step, L2 flushed before each). The batch's first 4 sequences are the
+    oracle fixture's ids and must reproduce its pooled vectors bit for bit."""
+    import numpy as np
+
+    import spatialdb_b200 as slx
+    from spatialdb_b200 import synth
+    from spatialdb_b200._lib import KernelStat
+
+    lib = ctx._lib
+    B, T = 32, 128
+    path = synth.encoder_q8_0_model()
+    m = slx.IntegerTransformerSource.load(path, ctx=ctx)
+    ids = np.random.default_rng(0).integers(0, ARCH["vocab"], (B, T)).astype(np.int32)
+    d_ids = torch.from_numpy(ids).cuda()
+    pooled = torch.empty((B, ARCH["embd"]), dtype=torch.int64, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def step():
+        m.encode_device(d_ids.data_ptr(), B, T, pooled.data_ptr(), stream.cuda_stream)
+
+    for _ in range(warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    ctx.status(stream.cuda_stream)
+    gold = golden("encoder_q8_0_b4_t128.npz")
+    parity = bool(np.array_equal(gold["ids"], ids[:4]) and np.array_equal(pooled[:4].cpu().numpy(), gold["pooled"]))
+    lib.slx_profile_begin(ctx._h)
+    ev = []
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        ev.append((e0, e1))
+    torch.cuda.synchronize()
+    stats = (KernelStat * 16)()
+    nst = ctypes_int()
+    lib.slx_profile_end(ctx._h, stats, 16, nst)
+    ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    pinned = torch.from_numpy(ids).pin_memory().numpy()
+    e2e = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        m.forward(pinned)
+        e2e += time.perf_counter() - t0
+    peaks = measured_peaks()
+    res = {"workload": f"encoder nomic-bert 12L d768 H12 SiLU-FFN 3072 V30522, Q8_0 weights, {B} x {T} ids",
+           "embeddings_per_s": B / (ms / 1000.0), "ms_per_step": ms, "steps": steps,
+           "e2e_embeddings_per_s": B * steps / e2e,
+           "parity_vs_oracle": parity,
+           "oracle": "fixture tests/golden/encoder_q8_0_b4_t128.npz (the batch's first 4 sequences)",
+           "roofline_gemm": class_roofline({s.name.decode(): s for s in stats[: nst.value]}, "gemm",
+                                           2.0 * peaks["bf16_tflops"], f"2 x {peaks['source']} bf16 dense"),
+           "kernels": {s.name.decode(): {"ms_per_step": s.ms / steps, "launches_per_step": s.launches / steps}
+                       for s in stats[: nst.value]}}
+    if cpu:
+        import oracle
+
+        cores = oracle.set_threads(os.cpu_count() or 1)
+        t0 = time.perf_counter()
+        oracle.Encoder(path).forward(ids[:2])
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": 2 / dt, "unit": UNIT, "cores": cores, "kind": "port",
+                               "sample": f"2 sequences x {T} tokens of the same batch, {dt:.1f} s"}
+    m.close()
+    return res
+
+
+def full_batch_bench(model, torch, stream, world: int, rank: int, dist, batch: int, total: int = 8192) -> dict:
+    """One pass over the whole batched-encoder input: `total` sequences of 512 ids split evenly over
+    the ranks (strong scaling: the total is fixed), each rank encoding its share in batches of
+    `batch` sequences on the device. Device time from CUDA events around the pass, max over ranks;
+    the inputs (16 MB of ids per 8192 sequences) are resident before the pass starts."""
+    import numpy as np
+
+    per = total // world
+    ids = np.random.default_rng(5000 + rank).integers(0, ARCH["vocab"], (per, SEQ)).astype(np.int32)
+    d_ids = torch.from_numpy(ids).cuda()
+    pooled = torch.empty((per, ARCH["embd"]), dtype=torch.int64, device="cuda")
+    model.encode_device(d_ids.data_ptr(), batch, SEQ, pooled.data_ptr(), stream.cuda_stream)  # warm-up
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for b0 in range(0, per, batch):
+        nb = min(batch, per - b0)
+        model.encode_device(d_ids[b0].data_ptr(), nb, SEQ, pooled[b0].data_ptr(), stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    model.ctx.status(stream.cuda_stream)
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    s = float(t.item()) / 1000.0
+    return {"workload": f"batched encoder, all {total} sequences x {SEQ} ids, Q4_0", "sequences": total,
+            "per_gpu": per, "gpus": world, "batch": batch, "s": s, "embeddings_per_s": total / s,
+            "scaling": "strong (fixed total, sequences split over the GPUs)"}
+
+
+def gemma_bench(ctx, decode_b1: int = 128, decode_b16: int = 128) -> dict:
     """Gemma-2B-shaped causal LM (18 layers, d 2048, 8 query / 1 KV head of 256, GeGLU-width
     SiLU FFN 16384, vocab 256000, Q4_0 projections and embeddings, F16 norms): a 512-token prompt,
     then greedy tokens with a full re-forward per token exactly as the reference's Generate does
@@ -194,27 +402,35 @@ def gemma_bench(ctx, decode_b1: int = 128, decode_b16: int = 8) -> dict:
     from spatialdb_b200 import synth
 
     shape = synth.CausalShape()
-    path = synth.cached("gemma2b_shape_q4_0_f16norm_seed5.gguf",
-                        lambda p: synth.write_causal(p, shape, synth.Q4_0, synth.F16, seed=5, eos=shape.vocab - 1))
+    path = synth.gemma_model()
     t0 = time.perf_counter()
     m = slx.IntegerCausalSource.load(path, ctx=ctx)
     load_s = time.perf_counter() - t0
-    rng = np.random.default_rng(21)
+    prompts = synth.gemma_prompts(17)  # row 0: the batch-1 prompt (the oracle fixture's), rows 1..16: batch 16
     res = {"model": "gemma 18L d2048 8q/1kv hd256 F16384 V256000 Q4_0", "prompt": 512, "load_s": load_s}
-    p1 = rng.integers(0, shape.vocab - 1, (1, 512)).astype(np.int32)
+    p1 = prompts[:1]
     m.generate(p1, 1)  # warm-up: workspaces at full size
     t0 = time.perf_counter()
     g = m.generate(p1, decode_b1)
     dt = time.perf_counter() - t0
     res["batch1"] = {"new_tokens": int(len(g[0])), "s": dt, "tok_per_s": len(g[0]) / dt}
-    p16 = rng.integers(0, shape.vocab - 1, (16, 512)).astype(np.int32)
+    # parity with the oracle's outputs for this prompt (committed fixture: ForwardCausal's last hidden
+    # state and Generate's first two greedy tokens)
+    gold = golden("gemma_q4_0_t512_greedy2.npz")
+    same_prompt = bool(np.array_equal(gold["prompt"], p1[0]))
+    res["parity_vs_oracle"] = {
+        "prompt_is_fixture_prompt": same_prompt,
+        "last_hidden": same_prompt and bool(np.array_equal(m.forward_causal(p1[0]), gold["last"])),
+        "first_2_tokens": same_prompt and bool(np.array_equal(g[0][:2], gold["tokens"])),
+        "oracle": "fixture tests/golden/gemma_q4_0_t512_greedy2.npz (oracle prefill of 512 + 2 greedy steps)"}
+    p16 = prompts[1:]
     m.generate(p16, 1)
     t0 = time.perf_counter()
     g = m.generate(p16, decode_b16)
     dt = time.perf_counter() - t0
     n16 = sum(len(x) for x in g)
     res["batch16"] = {"new_tokens": int(n16), "steps": decode_b16, "s": dt, "tok_per_s": n16 / dt,
-                      "note": f"first {decode_b16} of the configuration's 128 steps (context 512..{511 + decode_b16})"}
+                      "context": f"512..{511 + decode_b16} tokens re-forwarded per step"}
     try:
         res["lm_head"] = lm_head_bench(ctx, m, path, shape, p1, p16)
     except Exception as e:  # reported, never silently dropped
@@ -506,20 +722,21 @@ def search_cpu_baseline(sample_rows: int = 200_000, sample_queries: int = 4) -> 
             "sample": f"{sample_queries} queries x {sample_rows} rows ({dt:.1f} s), scaled to {SEARCH['rows']} rows"}
 
 
-def cpu_baseline(path: str, sample_seqs: int, seed: int = 99) -> dict:
+def cpu_baseline(path: str, ids) -> tuple[dict, "np.ndarray"]:
     """The oracle (C++ restatement of the reference CPU path, OpenMP over output columns as the
-    reference's Parallel.For) on a bounded sample of the workload, all host threads."""
-    import numpy as np
+    reference's Parallel.For) on a bounded sample of the workload -- the given sequences, which are
+    the first of a timed GPU batch -- on all host threads. Returns the baseline and the oracle's
+    pooled outputs, which the caller compares with the GPU's for the same sequences."""
     import oracle
 
     cores = oracle.set_threads(os.cpu_count() or 1)
     enc = oracle.Encoder(path)
-    ids = np.random.default_rng(seed).integers(0, ARCH["vocab"], (sample_seqs, SEQ)).astype(np.int32)
     t0 = time.perf_counter()
-    enc.forward(ids)
+    out = enc.forward(ids)
     dt = time.perf_counter() - t0
-    return {"value": sample_seqs / dt, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{sample_seqs} sequence(s) x {SEQ} tokens of the same workload, {dt:.1f} s"}
+    n = ids.shape[0]
+    return ({"value": n / dt, "unit": UNIT, "cores": cores, "kind": "port",
+             "sample": f"the first {n} sequence(s) x {SEQ} tokens of the first timed batch, {dt:.1f} s"}, out)
 
 
 def run_reference(args) -> None:
@@ -573,11 +790,9 @@ def run_ours(args) -> None:
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
-    if rank == 0:
-        path = model_path()
+    path = model_path()  # every rank writes its own temporary and renames it into place: no torn reads
     if dist:
         dist.barrier()
-    path = model_path()
 
     B, K, W = args.batch, args.steps, args.warmup
     ctx = slx.Context(local)
@@ -591,16 +806,18 @@ def run_ours(args) -> None:
     ids_host = rng.integers(0, ARCH["vocab"], (W + K, B, SEQ)).astype(np.int32)
     ids_dev = torch.from_numpy(ids_host).cuda()
     pooled = torch.empty((B, ARCH["embd"]), dtype=torch.int64, device="cuda")
+    first = torch.empty((B, ARCH["embd"]), dtype=torch.int64, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
 
-    def step(i):
-        model.encode_device(ids_dev[i].data_ptr(), B, SEQ, pooled.data_ptr(), stream.cuda_stream)
+    def step(i, out=pooled):
+        model.encode_device(ids_dev[i].data_ptr(), B, SEQ, out.data_ptr(), stream.cuda_stream)
 
     clocks = Clocks(local) if rank == 0 else None  # sampling from before the warm-up to after the e2e loop
     for i in range(W):
         flush.zero_()
         step(i)
     torch.cuda.synchronize()
+    ctx.status(stream.cuda_stream)
 
     launches0 = ctypes_i64()
     lib.slx_launch_count(ctx._h, launches0)
@@ -613,11 +830,12 @@ def run_ours(args) -> None:
     for i in range(K):
         flush.zero_()
         ev[i][0].record(stream)
-        step(W + i)
+        step(W + i, first if i == 0 else pooled)
         ev[i][1].record(stream)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
+    ctx.status(stream.cuda_stream)  # device-side errors of the timed steps (none expected)
     step_ms = [a.elapsed_time(b) for a, b in ev]
     stats = (KernelStat * 16)()
     nstat = ctypes_int()
@@ -626,31 +844,42 @@ def run_ours(args) -> None:
     lib.slx_launch_count(ctx._h, launches1)
     total_ms = sum(step_ms)
     t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
+    rank_ms = [total_ms / K]
     if dist:
+        gathered = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(gathered, t)
+        rank_ms = [float(x.item()) / K for x in gathered]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     max_ms = float(t.item())
     value = world * B * K / (max_ms / 1000.0)
 
-    # end to end through the public host-buffer API (pinned host ids in, pooled int64 out)
+    # end to end through the public host-buffer API (pinned host ids in, pooled int64 out); each step
+    # timed on the host around the call, with L2 flushed before it outside the timing
     ids_pinned = torch.from_numpy(ids_host).pin_memory().numpy()
     out_host = np.empty((B, ARCH["embd"]), np.int64)
     model.forward(ids_pinned[0])
     if dist:
         dist.barrier()
-    t0 = time.perf_counter()
+    e2e_s = 0.0
     for i in range(K):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
         out_host[:] = model.forward(ids_pinned[W + i])
-    e2e_s = time.perf_counter() - t0
+        e2e_s += time.perf_counter() - t0
     clk = clocks.stop(tw0, time.time()) if clocks else None  # samples inside the device-timed and e2e loops
     te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = world * B * K / float(te.item())
+    device_equals_host = bool((pooled.cpu().numpy() == out_host).all())  # the last timed batch, both entry points
 
-    # parity spot check of the timed outputs against the host path (same library)
-    last = pooled.cpu().numpy()
-    chk = model.forward(ids_host[W + K - 1])
-    parity_ok = bool((last == chk).all())
+    full_res = None
+    if not args.skip_full_batch:
+        try:
+            full_res = full_batch_bench(model, torch, stream, world, rank, dist, B)
+        except Exception as e:  # reported, never silently dropped
+            full_res = {"error": repr(e)}
 
     search_res = None
     if not args.skip_secondary and not args.skip_search:
@@ -663,20 +892,11 @@ def run_ours(args) -> None:
         peaks = measured_peaks()
         cls = {s.name.decode(): s for s in stats[: nstat.value]}
         int8_peak = 2.0 * peaks["bf16_tflops"]
-        roof = None
-        g = cls.get("gemm")
-        if g is not None and g.ms > 0:
-            # the projection GEMM (k_gemm_tc) is the largest single kernel of the step; its exact int64
-            # products run as int8 digit products on the tensor cores (5 activation x 3-4 weight digits)
-            achieved = 2.0 * g.tc_macs / (g.ms / 1000.0) / 1e12
-            roof = {"bound": "tensor", "kernel": "gemm (k_gemm_tc + activation digit split)", "achieved": achieved,
-                    "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak,
-                    "peak_source": f"2 x {peaks['source']} bf16 dense ({peaks['bf16_tflops']} TF/s): B200 int8:bf16 dense rate",
-                    "ops": "2 x int8 digit-product multiply-accumulates the exact int64 GEMM needs "
-                           "(rows x N x K_pad x 5 x weight digits)",
-                    "algorithmic_int64_tops": 2.0 * g.macs / (g.ms / 1000.0) / 1e12,
-                    "launches": int(g.launches), "avg_launch_ms": g.ms / max(1, g.launches),
-                    "traffic": recorded_traffic("k_gemm_tc")}
+        roof = class_roofline(cls, "gemm", int8_peak,
+                              f"2 x {peaks['source']} bf16 dense ({peaks['bf16_tflops']} TF/s): B200 int8:bf16 dense rate")
+        if roof is not None:
+            roof["kernel"] = "gemm (k_gemm_tc + activation digit split), the largest kernel class of the step"
+            roof["traffic"] = recorded_traffic("k_gemm_tc")
         breakdown = {s.name.decode(): {"ms_per_step": s.ms / K, "launches_per_step": s.launches / K}
                      for s in stats[: nstat.value]}
         line = {
@@ -685,27 +905,37 @@ def run_ours(args) -> None:
             "dtype": "int64", "data": "synthetic",
             "config": {"workload": workload_name(B), "seq_len": SEQ, "batch_per_gpu": B, "weights": "Q4_0",
                        "parallelism": f"dp{world} (independent sequences)",
-                       "l2": "flushed (256 MiB write) before every timed step, outside the step's events"},
+                       "l2": "flushed (256 MiB write) before every timed step, outside the step's events "
+                             "(device loop) and outside the host timing (e2e loop)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(B * SEQ * 4),
                     "d2h_bytes_per_step": int(B * ARCH["embd"] * 8)},
             "gpu_launches": int(launches1.value - launches0.value),
             "roofline": roof,
             "kernels": breakdown,
-            "parity_spot_check": parity_ok,
+            "rank_ms_per_step": rank_ms,
+            "device_equals_host_entry_point": device_equals_host,
             "clocks": clk,
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(path, args.cpu_sample)
+            n = max(1, min(args.cpu_sample, B))
+            base, want = cpu_baseline(path, ids_host[W][:n])
+            line["cpu_baseline"] = base
+            line["parity_vs_oracle"] = bool((first[:n].cpu().numpy() == want).all())
+            line["parity"] = {"oracle_sequences": n, "of_timed_batch": 0,
+                              "fixture_checks": "secondary.encoder_q8_0, secondary.gemma_decode, secondary.gemm"}
+        if full_res is not None:
+            line.setdefault("secondary", {})["batched_encoder_full"] = full_res
         if world == 1 and not args.skip_secondary:
             sec = line.setdefault("secondary", {})
-            try:
-                sec["gemv"] = gemv_bench(ctx, torch, stream)
-            except Exception as e:  # reported, never silently dropped
-                sec["gemv"] = {"error": repr(e)}
-            try:
-                sec["gemma_decode"] = gemma_bench(ctx)
-            except Exception as e:
-                sec["gemma_decode"] = {"error": repr(e)}
+            for key, fn in (("encoder_q8_0", lambda: encoder_q8_0_bench(ctx, torch, stream, K, W,
+                                                                         cpu=not args.no_cpu_baseline)),
+                            ("gemv", lambda: gemv_bench(ctx, torch, stream)),
+                            ("gemm", lambda: gemm_bench(ctx, torch, stream)),
+                            ("gemma_decode", lambda: gemma_bench(ctx))):
+                try:
+                    sec[key] = fn()
+                except Exception as e:  # reported, never silently dropped
+                    sec[key] = {"error": repr(e)}
         if search_res is not None:
             line.setdefault("secondary", {})["search"] = search_res
         print(json.dumps(line), flush=True)
@@ -754,11 +984,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=16, help="sequences per GPU per step")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-sample", type=int, default=2, help="sequences in the CPU-baseline sample")
+    ap.add_argument("--cpu-sample", type=int, default=2,
+                    help="sequences of the first timed batch in the CPU-baseline sample (checked against the GPU's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-secondary", action="store_true",
                     help="skip the GEMV, Gemma decode and embed+search measurements")
     ap.add_argument("--skip-search", action="store_true", help="skip the embed+search measurement")
+    ap.add_argument("--skip-full-batch", action="store_true",
+                    help="skip the pass over all 8192 sequences of the batched-encoder configuration")
     ap.add_argument("--lm-head-only", action="store_true",
                     help="time only the argmax and VocabLattice next-token heads (one-layer Gemma-width model)")
     args = ap.parse_args()

@@ -53,6 +53,22 @@ slx_status slx_destroy(slx_ctx* ctx);
 const char* slx_last_error(slx_ctx* ctx);
 /* Library version string. */
 const char* slx_version(void);
+/* No reference counterpart (the reference's errors are exceptions thrown on the calling thread).
+ * Device-side errors of work queued on ctx through the _device entry points -- a token id whose UNK
+ * row is outside the table (SLX_ERANGE), a tensor-core GEMM that gave up on a bounded wait
+ * (SLX_ETIMEOUT) -- are recorded in the context's error word, which stays set until it is read:
+ * slx_ctx_status waits for `stream` (NULL = the context's stream), returns the recorded status and
+ * clears it. The host-buffer entry points check the word themselves and clear it when they start. */
+slx_status slx_ctx_status(slx_ctx* ctx, void* stream);
+/* Context options (no reference counterpart). SLX_OPT_WAIT_LIMIT_CYCLES: SM clock cycles after
+ * which a wait inside the tensor-core projection GEMM gives up (0 = the default, about two seconds);
+ * the kernel then lets its copies and MMAs in flight finish, frees its tensor memory, returns and
+ * reports SLX_ETIMEOUT, leaving the context usable. SLX_OPT_TEST_STALL_MMA (testing only): nonzero
+ * makes that GEMM's MMA warp issue nothing, so its pipeline waits run out and the timeout path runs
+ * without any fault; results of such calls are undefined. */
+#define SLX_OPT_WAIT_LIMIT_CYCLES 1
+#define SLX_OPT_TEST_STALL_MMA 2
+slx_status slx_ctx_set_option(slx_ctx* ctx, int option, int64_t value);
 
 /* ---- GGUF ---------------------------------------------------------------------------------- */
 /* GgufReader.ReadTensorF32 (Gguf/GgufReader.cs:141-145, 172-201) for one tensor of a file:
@@ -81,7 +97,8 @@ slx_status slx_model_info(slx_model* model, int32_t* info, int n);
  * L2-normalised float vectors (:52-62, .Forward.cs:89-99). Also serves SLX_MODEL_GEMMA_ENCODER
  * (IntegerGemmaSource.Forward, Gguf/IntegerGemmaSource.cs:66-80). */
 slx_status slx_encode(slx_model* model, const int32_t* ids, int B, int T, int64_t* pooled_q30, float* l2);
-/* Same on device buffers: d_ids[B*T] int32, d_pooled[B*embd] int64, queued on `stream`. */
+/* Same on device buffers: d_ids[B*T] int32, d_pooled[B*embd] int64, queued on `stream`. Errors the
+ * device raises while it runs (SLX_ERANGE, SLX_ETIMEOUT) are read with slx_ctx_status. */
 slx_status slx_encode_device(slx_model* model, const int32_t* d_ids, int B, int T, int64_t* d_pooled, void* stream);
 
 /* Hidden states after the first n_layers blocks (n_layers < 0: all), x_q30[T][embd], for one
@@ -132,6 +149,21 @@ slx_status slx_matmul_q30(slx_ctx* ctx, const int64_t* a, int M, int K, int dtyp
 slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K, int dtype, const uint8_t* d_w,
                                  int64_t w_bytes, int N, int half_composite, int scale_bits, int shift, int64_t* d_c,
                                  void* stream);
+
+/* IntegerMatMul.MatMul with a weight prepared once (Math/IntegerMatMul.cs:37-76 / :166-205), the way
+ * the model sources use their weights: the reference converts every weight at load
+ * (Gguf/IntegerTransformerSource.Loading.cs:105-119 to Q30 long[], Gguf/IntegerCausalSource.Loading.cs:218-225
+ * to Half[]) and multiplies many activations by it. slx_weight_prepare builds the tensor-core digit
+ * planes of the composites of the GGUF blocks at d_w (device memory the caller keeps alive while the
+ * handle lives) and waits for them; slx_matmul_q30_prepared queues c[M][N] = MatMul(d_a[M][K], w) >>
+ * shift on `stream` (M <= 8 with Q4_0 / Q8_0 and the long composite streams the packed blocks
+ * instead). info: N, K, tensor-core path (1) or exact kernel (0), weight digits. */
+typedef struct slx_weight slx_weight;
+slx_status slx_weight_prepare(slx_ctx* ctx, const uint8_t* d_w, int64_t w_bytes, int dtype, int N, int K,
+                              int half_composite, int scale_bits, slx_weight** out);
+slx_status slx_weight_free(slx_weight* w);
+slx_status slx_weight_info(slx_weight* w, int32_t* info, int n);
+slx_status slx_matmul_q30_prepared(slx_weight* w, const int64_t* d_a, int M, int shift, int64_t* d_c, void* stream);
 
 /* No counterpart in the reference: slx_matmul_q30_device for callers that must not allocate device
  * memory -- services whose GPU memory is owned by another allocator (a framework's caching

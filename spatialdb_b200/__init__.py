@@ -24,6 +24,7 @@ from ._lib import I32P, I64P, F32P, U8P, U64P, VP
 
 (SLX_OK, SLX_EINVAL, SLX_EFORMAT, SLX_ENOTFOUND, SLX_EUNSUPPORTED, SLX_EEOF, SLX_ERANGE, SLX_EOOM, SLX_ECUDA, SLX_ETIMEOUT,
  SLX_ESCRATCH) = range(11)
+OPT_WAIT_LIMIT_CYCLES, OPT_TEST_STALL_MMA = 1, 2
 MODEL_ENCODER, MODEL_CAUSAL, MODEL_GEMMA_ENCODER, MODEL_FLOAT_ENCODER = 0, 1, 2, 3
 
 
@@ -88,6 +89,15 @@ class Context:
             msg = self._lib.slx_last_error(self._h).decode(errors="replace")
             raise _EXC.get(st, SlxError)(st, msg)
 
+    def status(self, stream: int = 0):
+        """slx_ctx_status: wait for `stream` (cudaStream_t as int, 0 = the context's stream), raise the
+        device-side error recorded by work queued through the _device entry points, and clear it."""
+        self.check(self._lib.slx_ctx_status(self._h, VP(stream or None)))
+
+    def set_option(self, option: int, value: int):
+        """slx_ctx_set_option (OPT_WAIT_LIMIT_CYCLES, OPT_TEST_STALL_MMA)."""
+        self.check(self._lib.slx_ctx_set_option(self._h, option, int(value)))
+
     def close(self):
         if getattr(self, "_h", None):
             self._lib.slx_destroy(self._h)
@@ -128,6 +138,39 @@ def matmul_q30(a: np.ndarray, dtype: int, w_raw, N: int, half_composite: bool = 
     ctx.check(ctx._lib.slx_matmul_q30(ctx._h, _p(a, I64P), M, K, int(dtype), _p(w, U8P), w.size, N, int(half_composite),
                                       scale_bits, shift, _p(c, I64P)))
     return c
+
+
+class PreparedWeight:
+    """A GGUF weight in device memory prepared once for repeated IntegerMatMul products
+    (slx_weight_prepare): the tensor-core digit planes of its Q30 composites. `d_w` is a device
+    pointer to the raw blocks, which must stay alive while this object does."""
+
+    def __init__(self, d_w: int, w_bytes: int, dtype: int, N: int, K: int, half_composite: bool = False,
+                 scale_bits: int = 30, ctx: Context | None = None):
+        self.ctx = ctx or Context.default()
+        h = VP()
+        self.ctx.check(self.ctx._lib.slx_weight_prepare(self.ctx._h, VP(d_w), int(w_bytes), int(dtype), int(N), int(K),
+                                                        int(half_composite), int(scale_bits), ctypes.byref(h)))
+        self._h = h
+        info = (ctypes.c_int32 * 4)()
+        self.ctx._lib.slx_weight_info(h, info, 4)
+        self.N, self.K, self.tensor_cores, self.digits = list(info)
+
+    def matmul_device(self, d_a: int, M: int, d_c: int, shift: int = 30, stream: int = 0):
+        """Queue c[M][N] = MatMul(a[M][K], w) >> shift on device buffers (raw pointers)."""
+        self.ctx.check(self.ctx._lib.slx_matmul_q30_prepared(self._h, VP(d_a), int(M), int(shift), VP(d_c),
+                                                             VP(stream or None)))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.ctx._lib.slx_weight_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def attention(q, k, v, seq: int, n_heads: int, n_kv_heads: int, scale_exp: int = -30, mode: int = 0,

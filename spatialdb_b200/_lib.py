@@ -29,6 +29,8 @@ SIGNATURES = {
     "slx_destroy": (i, [VP]),
     "slx_last_error": (ctypes.c_char_p, [VP]),
     "slx_version": (ctypes.c_char_p, []),
+    "slx_ctx_status": (i, [VP, VP]),
+    "slx_ctx_set_option": (i, [VP, i, i64]),
     "slx_gguf_read_f32": (i, [VP, ctypes.c_char_p, ctypes.c_char_p, F32P, i64]),
     "slx_dequantize": (i, [VP, i, U8P, i64, F32P, i64]),
     "slx_model_load_gguf": (i, [VP, ctypes.c_char_p, i, i, ctypes.POINTER(VP)]),
@@ -45,6 +47,10 @@ SIGNATURES = {
     "slx_vocab_lattice_query": (i, [VP, F32P, i, i, I32P, U64P]),
     "slx_matmul_q30": (i, [VP, I64P, i, i, i, U8P, i64, i, i, i, i, I64P]),
     "slx_matmul_q30_device": (i, [VP, VP, i, i, i, VP, i64, i, i, i, i, VP, VP]),
+    "slx_weight_prepare": (i, [VP, VP, i64, i, i, i, i, i, ctypes.POINTER(VP)]),
+    "slx_weight_free": (i, [VP]),
+    "slx_weight_info": (i, [VP, I32P, i]),
+    "slx_matmul_q30_prepared": (i, [VP, VP, i, i, VP, VP]),
     "slx_matmul_q30_noalloc": (i, [VP, i, i, i, VP, i64, i, i, i, i, VP, VP]),
     "slx_attention": (i, [VP, I64P, I64P, I64P, i, i, i, i, i, i, i, i, I64P]),
     "slx_lattice_build": (i, [VP, F32P, i64, i, f32, i64, i64, ctypes.POINTER(VP)]),

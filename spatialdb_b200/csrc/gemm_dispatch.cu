@@ -78,7 +78,7 @@ int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPla
     cudaMemsetAsync(flag, 0, sizeof(int), st);
     tc::split_a(a, lda, M, (int)w.K, mpad, plan.k_pad, planes, flag, st);
     tc::launch(tmap_a, plan.tmap_w, plan.wlimbs, M, (int)w.N, (int)w.K, mpad, plan.n_pad, plan.k_pad, shift, c, ldc, r,
-               ldr, flag, ws.err, st, plan.row_shift);
+               ldr, flag, ws.err, st, plan.row_shift, ws.wait);
     gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st, flag);  // runs only if the split overflowed
     return 3;
 }

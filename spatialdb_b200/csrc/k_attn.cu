@@ -26,6 +26,7 @@
 // the exact kernel redoes the call.
 #include <cuda.h>
 
+#include "slx_attr.h"
 #include "slx_device.cuh"
 #include "slx_gemm.h"
 #include "slx_kernels.h"
@@ -251,11 +252,7 @@ void launch_scores_kb(const CUtensorMap& tq, const CUtensorMap& tk, ScoreParams 
     p.stages = score_stages<KB>();
     constexpr size_t smem = score_smem<KB>();
     static_assert(smem <= 227 * 1024, "score kernel shared memory");
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(k_scores<KB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured = true;
-    }
+    slx::ensure_smem((const void*)k_scores<KB>, smem);
     k_scores<KB><<<grid, S_THREADS, smem, st>>>(tq, tk, p);
 }
 
@@ -465,11 +462,7 @@ void launch_pv(int B, int T, int nh, int nkv, const int64_t* scores, int sr, con
         cudaMemsetAsync(flag, 1, sizeof(int), st);
         return;
     }
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(k_pv<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
-        configured = true;
-    }
+    slx::ensure_smem((const void*)k_pv<HD>, C::SMEM);
     const dim3 grid((unsigned)((T + C::PR - 1) / C::PR), (unsigned)nh, (unsigned)B);
     k_pv<HD><<<grid, PV_TH, C::SMEM, st>>>(scores, sr, v, ldv, out, ldo, T, nh, nkv, flag);
 }

@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cstdio>
 
+#include "slx_attr.h"
 #include "slx_device.cuh"
 #include "slx_kernels.h"
 
@@ -571,11 +572,7 @@ int attention(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, cons
                int mode, int window, cudaStream_t st, const int* only_if) {
     if (B * T <= 0) return 0;
     size_t smem = (size_t)AW * (T + hd) * sizeof(int64_t);
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-        cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured = smem;
-    }
+    slx::ensure_smem((const void*)k_attention, smem);
     const int64_t nblocks = (int64_t)((T + AW - 1) / AW) * nh * B;
     const int64_t grid = only_if ? std::min<int64_t>(nblocks, 4 * 148) : nblocks;
     k_attention<<<(unsigned)grid, AW * 32, smem, st>>>(q, ldq, k, ldk, v, ldv, out, ldo, T, nh, nkv, hd, score_shift,

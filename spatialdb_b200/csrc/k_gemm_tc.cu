@@ -24,6 +24,7 @@
 
 #include <cstring>
 
+#include "slx_attr.h"
 #include "slx_device.cuh"
 #include "slx_gemm.h"
 #include "slx_kernels.h"
@@ -46,18 +47,20 @@ struct Params {
     int* err;         // set on a bounded-wait timeout
     // the weight row n was stored as w >> row_shift[n] (its common trailing zeros)
     const int8_t* row_shift;
+    long long wait_limit;  // SM clock cycles before a wait on the pipeline gives up
+    int stall_mma;         // test hook: the MMA warp issues nothing (the pipeline's waits then run out)
 };
 
 // Bounded spin on an mbarrier phase without suspending (the MMA issuer's waits are short and on the
-// critical path): about two seconds of SM clock, then false.
-__device__ __forceinline__ bool mbar_spin(uint32_t bar, uint32_t parity) {
+// critical path): `limit` SM clock cycles, then false.
+__device__ __forceinline__ bool mbar_spin(uint32_t bar, uint32_t parity, long long limit) {
     if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     for (;;) {
 #pragma unroll 1
         for (int i = 0; i < 64; i++)
             if (mbar_try(bar, parity)) return true;
-        if (clock64() - t0 > 4000000000LL) return false;
+        if (clock64() - t0 > limit) return false;
     }
 }
 
@@ -87,7 +90,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     uint64_t* bars = (uint64_t*)(smem + (size_t)nst * STAGE);
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + nst);
     const uint32_t tfull0 = smem_u32(bars + 2 * nst), tfree0 = smem_u32(bars + 2 * nst + NACC);
-    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * nst + 2 * NACC);
+    const uint32_t drain = smem_u32(bars + 2 * nst + 2 * NACC);  // MMAs retired, after a failed wait
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * nst + 2 * NACC + 1);
+    const long long lim = p.wait_limit > 0 ? p.wait_limit : kWaitCycles;
     __shared__ int s_fail;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -101,6 +106,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             mbar_init(tfull0 + 8 * b, 1);
             mbar_init(tfree0 + 8 * b, EPI_WARPS);
         }
+        mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -134,7 +140,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
                 const int m0 = (t / p.tiles_n) * GM, n0 = (t % p.tiles_n) * GN;
                 for (int kb = 0; kb < p.nkb; kb++, g++) {
-                    if (!mbar_wait(empty0 + 8 * s, ph ^ 1u) || *(volatile int*)&s_fail) {
+                    if (!mbar_wait(empty0 + 8 * s, ph ^ 1u, lim) || *(volatile int*)&s_fail) {
                         s_fail = 1;
                         ok = false;
                         break;
@@ -145,21 +151,21 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                     if (++s == nst) { s = 0; ph ^= 1u; }
                 }
             }
-            if (!ok)  // let copies still in flight land before the CTA exits
+            if (!ok)  // let copies still in flight land before the CTA exits (they always complete)
                 for (int j = g - nst < 0 ? 0 : g - nst; j < g; j++) mbar_wait(full0 + 8 * (j % nst), (uint32_t)(j / nst) & 1u);
         }
     } else if (warp == 1) {
-        if (lane == 0) {  // MMA issuer
+        if (lane == 0 && !p.stall_mma) {  // MMA issuer
             int lt = 0, s = 0;
             uint32_t ph = 0;
-            bool ok = true;
+            bool ok = true, issued = false;
             for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, lt++) {
                 const int b = lt & 1;
-                if (!mbar_spin(tfree0 + 8 * b, ((uint32_t)(lt >> 1) & 1u) ^ 1u)) { ok = false; break; }
+                if (!mbar_spin(tfree0 + 8 * b, ((uint32_t)(lt >> 1) & 1u) ^ 1u, lim)) { ok = false; break; }
                 fence_after();
                 const uint32_t d = tmem + b * ACC;
                 for (int kb = 0; kb < p.nkb; kb++) {
-                    if (!mbar_spin(full0 + 8 * s, ph)) { ok = false; break; }
+                    if (!mbar_spin(full0 + 8 * s, ph, lim)) { ok = false; break; }
                     fence_after();
                     const uint32_t w = sbase + s * STAGE, a = w + W_ST;
 #pragma unroll
@@ -169,12 +175,19 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                         for (int j = 0; j < LW; j++) umma_i8(d + j * GM, kdesc(w + j * (GN * GK) + kk * 32), bdesc, IDESC, 1u);
                     }
                     umma_commit(empty0 + 8 * s);
+                    issued = true;
                     if (++s == nst) { s = 0; ph ^= 1u; }
                 }
                 if (!ok) break;
                 umma_commit(tfull0 + 8 * b);
             }
-            if (!ok) s_fail = 1;
+            if (!ok) {
+                s_fail = 1;
+                if (issued) {  // MMAs still in flight write TMEM: let them retire before it is freed
+                    umma_commit(drain);
+                    mbar_wait(drain, 0u);
+                }
+            }
         }
     } else {  // epilogue: thread = weight row n (TMEM lane), eight of the tile's activation rows
         int lt = 0;
@@ -187,7 +200,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             //   e <= 0: (H << 32-e) + (L << -e);  0 < e <= 32: (H << 32-e) + (L >> e);
             //   e > 32: (H + (L >> 32)) >> (e - 32).
             const int e = p.shift - ((p.row_shift && n_ok) ? p.row_shift[n] : 0);
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull0 + 8 * b, (uint32_t)(lt >> 1) & 1u));
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull0 + 8 * b, (uint32_t)(lt >> 1) & 1u, lim));
             if (!ok) { s_fail = 1; break; }
             fence_after();
             const uint32_t ta = tmem + lane_base + b * ACC + 8 * sub;
@@ -408,16 +421,15 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
+    // The driver entry point is the same for every device; looked up once (thread-safe static init).
+    static const EncodeTiledFn fn = [] {
         void* p = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)p;
-    }
+            return (EncodeTiledFn)p;
+        return (EncodeTiledFn) nullptr;
+    }();
     return fn;
 }
 
@@ -425,26 +437,13 @@ template <int LW>
 constexpr size_t stage_bytes() { return (size_t)LW * GN * GK + (size_t)LA * GM * GK; }
 
 
-int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
+int sm_count() { return slx::device_sm_count(); }
 
 template <int LW>
 void launch_lw(const CUtensorMap& ta, const CUtensorMap& tw, Params p, cudaStream_t st) {
     constexpr int nst = gemm_stages<LW>();
-    const size_t smem = nst * stage_bytes<LW>() + 1024 + (2 * nst + 2 * NACC + 1) * 8;
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(k_gemm_tc<LW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured = true;
-    }
+    const size_t smem = nst * stage_bytes<LW>() + 1024 + (2 * nst + 2 * NACC + 2) * 8;
+    slx::ensure_smem((const void*)k_gemm_tc<LW>, smem);
     const int grid = p.tiles < sm_count() ? p.tiles : sm_count();
     k_gemm_tc<LW><<<grid, THREADS, smem, st>>>(ta, tw, p);
 }
@@ -523,13 +522,14 @@ void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t 
 
 void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K, int64_t mpad, int64_t npad, int64_t kpad,
             int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st,
-            const int8_t* row_shift) {
+            const int8_t* row_shift, const WaitOptions* wait) {
     (void)K;
     Params p = base_params();
     p.M = M; p.N = N; p.nkb = (int)(kpad / GK); p.shift = shift;
     p.tiles_n = (int)((npad + GN - 1) / GN);
     p.tiles = (int)(mpad / GM) * p.tiles_n;
     p.C = c; p.ldc = ldc; p.R = r; p.ldr = ldr; p.skip = skip; p.err = err; p.row_shift = row_shift;
+    if (wait) { p.wait_limit = wait->limit_cycles; p.stall_mma = wait->stall_mma; }
     const CUtensorMap& ta = *(const CUtensorMap*)tmap_a;
     const CUtensorMap& tw = *(const CUtensorMap*)tmap_w;
     switch (lw) {

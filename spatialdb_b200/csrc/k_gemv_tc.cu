@@ -30,6 +30,7 @@
 #include <cmath>
 #include <cstring>
 
+#include "slx_attr.h"
 #include "slx_device.cuh"
 #include "slx_gemm.h"
 #include "slx_kernels.h"
@@ -481,16 +482,7 @@ __global__ void __launch_bounds__(threads_of(MM), 1) k_gemv_tc(const __grid_cons
 
 // ---- host ----
 
-int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
+int sm_count() { return slx::device_sm_count(); }
 
 // K split (one CTA per SM): minimizes (waves) x (a CTA's chunks x a per-chunk time that grows with M,
 // plus a fixed start-up and drain of about 2.5 us).
@@ -518,11 +510,7 @@ void launch_tc(const WDesc& w, const int64_t* a, int64_t lda, int64_t* c, int64_
                cudaStream_t st) {
     const int N = (int)w.N, K = (int)w.K;
     constexpr size_t smem = smem_bytes(Q4, MM);
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(k_gemv_tc<Q4, MM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured = true;
-    }
+    slx::ensure_smem((const void*)k_gemv_tc<Q4, MM>, smem);
     uint8_t* base = (uint8_t*)ws.p;
     int* flag = (int*)base + FLAG_WORD;
     int* counters = (int*)(base + 256);

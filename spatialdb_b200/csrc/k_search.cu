@@ -29,6 +29,7 @@
 #include <cmath>
 #include <cstring>
 
+#include "slx_attr.h"
 #include "slx_device.cuh"
 #include "slx_gemm.h"
 #include "slx_kernels.h"
@@ -776,11 +777,7 @@ int query(Lattice& L, const float* d_q, int nq, int k, float zero_threshold, int
         k_split<<<(unsigned)((nq + 7) / 8), 256, 0, st>>>(qvals, nq, dim, qpad, dpad, qplanes, qn2, qh2, ql2, qs);
         alignas(64) unsigned char tmq[128];
         if (!tc::encode_planes(tmq, qplanes, dpad, qpad, 2, QBM)) { err = "lattice query: tensor map"; return SLX_ECUDA; }
-        static bool configured = false;
-        if (!configured) {
-            cudaFuncSetAttribute(k_search_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
-            configured = true;
-        }
+        slx::ensure_smem((const void*)k_search_tc, SMEM);
         TcParams tp;
         tp.nq = nq; tp.nkb = dpad / BKB; tp.tiles_per_chunk = per; tp.ntiles = ntiles; tp.nslots = nslots;
         tp.n = L.n; tp.dn = L.norm2; tp.qs = qs; tp.ds = L.stats; tp.ckey = ckey; tp.cid = cid;
@@ -826,9 +823,7 @@ int query(Lattice& L, const float* d_q, int nq, int k, float zero_threshold, int
         int32_t* xid = carve<int32_t>(xc, (size_t)nfb * xslots * T);
         const int* ql = exact_only ? nullptr : fb_list;
         const size_t xsmem = (size_t)dim * 4;
-        if (xsmem > 48 * 1024) {
-            cudaFuncSetAttribute(k_search_exact, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xsmem);
-        }
+        slx::ensure_smem((const void*)k_search_exact, xsmem);
         k_search_exact<<<dim3((unsigned)xchunks, (unsigned)nfb), EXACT_THREADS, xsmem, st>>>(
             L.vals, L.n, dim, qvals, ql, rows_per, xslots, xkey, xid);
         MergeParams mp{};

@@ -22,6 +22,7 @@
 
 #include <cuda_runtime.h>
 
+#include "slx_attr.h"
 #include "slx_device.cuh"
 #include "slx_kernels.h"
 #include "slx_status.h"
@@ -518,16 +519,7 @@ bool grow(void** p, size_t& cap, size_t need) {
     return true;
 }
 
-int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
+int sm_count() { return slx::device_sm_count(); }
 
 // Stage-1 candidate slots per query: KK = k per slice of SLICE rows.
 size_t slice_slots(int64_t V, int k) {
@@ -545,11 +537,7 @@ int queries_per_pass(int d) {
 template <bool VEC, int G>
 void launch_dist_t(Lattice& L, int q0, int g, cudaStream_t st) {
     const int smem = G * L.d * 8;
-    static int configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-        cudaFuncSetAttribute(k_vocab_dist<VEC, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        configured = smem;
-    }
+    slx::ensure_smem((const void*)k_vocab_dist<VEC, G>, (size_t)smem);
     int per_sm = 1;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_vocab_dist<VEC, G>, DWARPS * 32, smem);
     if (per_sm < 1) per_sm = 1;
@@ -602,11 +590,8 @@ int candidates(Lattice& L, int B, int k, bool want_dist, cudaStream_t st) {
     const size_t stage = (size_t)n_cand * 12;
     const int staged = keys + stage <= 160 * 1024 ? 1 : 0;
     const int tsmem = (int)(keys + (staged ? stage : 0));
-    static bool tconfigured = false;  // the largest request is 160 KiB (staged); unstaged <= KMAX * 12 + 8
-    if (tsmem > 48 * 1024 && !tconfigured) {
-        cudaFuncSetAttribute(k_topk_merge, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        tconfigured = true;
-    }
+    // the largest request is 160 KiB (staged); unstaged <= KMAX * 12 + 8
+    if (tsmem > 48 * 1024) slx::ensure_smem((const void*)k_topk_merge, 160 * 1024);
     k_topk_merge<<<(unsigned)B, TK, tsmem, st>>>(vals, ids, n_cand, k, staged, L.cand, want_dist ? L.cdist : nullptr);
     return n + 1;
 }
@@ -713,11 +698,7 @@ int next_tokens(Lattice& L, const int64_t* d_last, int B, int scale_bits, int k,
     }
     if (keff > 0) n += candidates(L, B, keff, false, st);
     const size_t smem = sizeof(float) * (size_t)L.d;
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-        cudaFuncSetAttribute(k_vocab_score, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured = smem;
-    }
+    slx::ensure_smem((const void*)k_vocab_score, smem);
     k_vocab_score<<<(unsigned)B, ST, smem, st>>>(L.table, L.d, L.hf, L.cand, keff, eos, d_next);
     return n + 1;
 }

@@ -21,12 +21,19 @@ struct GemmPlan {
     int8_t* row_shift = nullptr;              // device [N]: trailing zeros factored out of each row
 };
 
+// Bounded-wait settings of the tensor-core projection GEMM, per context.
+struct WaitOptions {
+    long long limit_cycles = 0;  // SM clock cycles before an mbarrier wait gives up (0: about two seconds)
+    int stall_mma = 0;           // test hook: the MMA warp issues nothing, so the other warps' waits run out
+};
+
 // Per-model scratch shared by the projections.
 struct GemmWorkspace {
     void* p = nullptr;
     size_t bytes = 0;
     int* err = nullptr;  // device error word (bounded-wait timeouts)
     unsigned tag = 0;    // last GEMV call's tag (the GEMV's overflow word is compared with it)
+    const WaitOptions* wait = nullptr;  // the owning context's settings (nullptr: defaults)
 };
 
 // Tensor-core kernel launchers (k_gemm_tc.cu).
@@ -49,7 +56,7 @@ void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t 
              cudaStream_t st);
 void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K, int64_t mpad, int64_t npad, int64_t kpad,
             int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st,
-            const int8_t* row_shift = nullptr);
+            const int8_t* row_shift = nullptr, const WaitOptions* wait = nullptr);
 // Per-head digit planes of rows at x + (b*T+t)*ld + h*hd -> [(b*nh+h)][LA][tpad][kpad].
 void split_heads(const int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad, int8_t* planes,
                  int* overflow, cudaStream_t st);

@@ -53,6 +53,7 @@ struct slx_ctx {
     bool prof = false;
     std::vector<ProfRecord> records;
     GemmWorkspace kws;               // scratch of the kernel-level matmul entry points
+    WaitOptions wait;                // bounded-wait settings of the tensor-core GEMMs (slx_ctx_set_option)
     std::vector<cudaEvent_t> event_pool;
     cudaEvent_t event() {
         if (!event_pool.empty()) { cudaEvent_t e = event_pool.back(); event_pool.pop_back(); return e; }
@@ -678,6 +679,7 @@ slx_status slx_init(int device, slx_ctx** out) {
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     CK(cudaMalloc(&c->d_flag, sizeof(int)));
     CK(cudaMemset(c->d_flag, 0, sizeof(int)));
+    c->kws.wait = &c->wait;
     *out = c.release();
     return SLX_OK;
 }
@@ -696,6 +698,31 @@ slx_status slx_destroy(slx_ctx* ctx) {
 }
 
 const char* slx_last_error(slx_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+slx_status slx_ctx_status(slx_ctx* ctx, void* stream) {
+    if (!ctx) return SLX_EINVAL;
+    CK(cudaSetDevice(ctx->device));
+    cudaStream_t st = pick(ctx, stream);
+    int rc = check_flag(ctx, st);
+    CK(cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), st));
+    CK(cudaStreamSynchronize(st));
+    return rc;
+}
+
+slx_status slx_ctx_set_option(slx_ctx* ctx, int option, int64_t value) {
+    if (!ctx) return SLX_EINVAL;
+    switch (option) {
+        case SLX_OPT_WAIT_LIMIT_CYCLES:
+            if (value < 0) return set_err(ctx, SLX_EINVAL, "wait limit %lld < 0", (long long)value);
+            ctx->wait.limit_cycles = value;
+            return SLX_OK;
+        case SLX_OPT_TEST_STALL_MMA:
+            ctx->wait.stall_mma = value ? 1 : 0;
+            return SLX_OK;
+        default:
+            return set_err(ctx, SLX_EINVAL, "unknown option %d", option);
+    }
+}
 
 slx_status slx_model_load_gguf(slx_ctx* ctx, const char* path, int kind, int scale_bits, slx_model** out) {
     if (!ctx || !path || !out) return set_err(ctx, SLX_EINVAL, "null argument");
@@ -720,6 +747,7 @@ slx_status slx_model_load_gguf(slx_ctx* ctx, const char* path, int kind, int sca
         return set_err(ctx, SLX_EINVAL, "unknown model kind %d", kind);
     if (st) return st;
     m->gws.err = ctx->d_flag;
+    m->gws.wait = &ctx->wait;
     if ((st = prepare_gemms(ctx, m.get()))) return st;
     CK(cudaStreamSynchronize(ctx->stream));
     CK(cudaGetLastError());
@@ -1029,12 +1057,90 @@ slx_status slx_matmul_q30_device(slx_ctx* ctx, const int64_t* d_a, int M, int K,
     if (rc) return set_err(ctx, rc, "%s", err.c_str());
     GemmWorkspace ws;
     ws.err = ctx->d_flag;
+    ws.wait = &ctx->wait;
     RUN(KC_GEMM, (double)M * N * K, 0, gemm_run(d_a, K, M, w, plan, d_c, N, shift, nullptr, 0, ws, st));
     cudaError_t e = cudaStreamSynchronize(st);
     if (plan.limbs) cudaFree(plan.limbs);
     if (plan.row_shift) cudaFree(plan.row_shift);
     gemm_workspace_free(ws);
     if (e != cudaSuccess) return set_err(ctx, SLX_ECUDA, "%s", cudaGetErrorString(e));
+    CK(cudaGetLastError());
+    return SLX_OK;
+}
+
+// A weight prepared once for repeated products: the load-time half of the reference's weight
+// handling (IntegerTransformerSource.Loading.cs:105-119 re-quantizes every weight to Q30 long[] at
+// load), here the tensor-core digit planes of the composites, built beside the caller's blocks.
+struct slx_weight {
+    slx_ctx* ctx = nullptr;
+    WDesc w;
+    GemmPlan plan;
+    GemmWorkspace ws;
+    ~slx_weight() {
+        if (plan.limbs) cudaFree(plan.limbs);
+        if (plan.row_shift) cudaFree(plan.row_shift);
+        gemm_workspace_free(ws);
+    }
+};
+
+slx_status slx_weight_prepare(slx_ctx* ctx, const uint8_t* d_w, int64_t w_bytes, int dtype, int N, int K,
+                              int half_composite, int scale_bits, slx_weight** out) {
+    if (!ctx || !d_w || !out || N <= 0 || K <= 0 || scale_bits < 1 || scale_bits > 62)
+        return set_err(ctx, SLX_EINVAL, "bad arguments");
+    *out = nullptr;
+    if (dtype != GG_F32 && dtype != GG_F16 && dtype != GG_BF16 && dtype != GG_Q8_0 && dtype != GG_Q4_0)
+        return set_err(ctx, SLX_EUNSUPPORTED, "matmul weight dtype %d (expand other formats with slx_dequantize)", dtype);
+    const int64_t elems = (int64_t)N * K;
+    if (w_bytes < gguf_byte_count((uint32_t)dtype, elems)) return set_err(ctx, SLX_EEOF, "weight buffer too small");
+    CK(cudaSetDevice(ctx->device));
+    std::unique_ptr<slx_weight> h(new slx_weight());
+    h->ctx = ctx;
+    WDesc& w = h->w;
+    w.dtype = dtype; w.data = d_w; w.nblocks = elems / 32; w.elements = elems; w.N = N; w.K = K;
+    w.mode = half_composite ? 1 : 0;
+    w.scale = std::ldexp(1.0, scale_bits);
+    h->ws.err = ctx->d_flag;
+    h->ws.wait = &ctx->wait;
+    std::string err;
+    int rc = gemm_prepare(w, h->plan, ctx->stream, err);
+    if (rc) return set_err(ctx, rc, "%s", err.c_str());
+    CK(cudaStreamSynchronize(ctx->stream));
+    *out = h.release();
+    return SLX_OK;
+}
+
+slx_status slx_weight_free(slx_weight* w) {
+    if (!w) return SLX_EINVAL;
+    cudaSetDevice(w->ctx->device);
+    cudaStreamSynchronize(w->ctx->stream);
+    delete w;
+    return SLX_OK;
+}
+
+slx_status slx_weight_info(slx_weight* w, int32_t* info, int n) {
+    if (!w || !info) return SLX_EINVAL;
+    int32_t v[4] = {(int32_t)w->w.N, (int32_t)w->w.K, w->plan.use_tc, w->plan.wlimbs};
+    for (int i = 0; i < n && i < 4; i++) info[i] = v[i];
+    return SLX_OK;
+}
+
+slx_status slx_matmul_q30_prepared(slx_weight* h, const int64_t* d_a, int M, int shift, int64_t* d_c, void* stream) {
+    if (!h) return SLX_EINVAL;
+    slx_ctx* ctx = h->ctx;
+    if (M < 0 || (M > 0 && (!d_a || !d_c))) return set_err(ctx, SLX_EINVAL, "bad arguments");
+    if (M == 0) return SLX_OK;
+    cudaStream_t st = pick(ctx, stream);
+    const WDesc& w = h->w;
+    const double macs = (double)M * (double)w.N * (double)w.K;
+    if (gemv_supported(w, M)) {
+        if (!gemv_reserve(h->ws, M, (int)w.N, (int)w.K, st)) return set_err(ctx, SLX_EOOM, "GEMV workspace");
+        RUN(KC_GEMV, macs, (double)gguf_byte_count((uint32_t)w.dtype, w.elements) + (double)M * (w.K + w.N) * 8,
+            gemv_exact(d_a, w.K, M, w, d_c, w.N, shift, h->ws, st));
+    } else {
+        const double tc = h->plan.use_tc ? (double)M * (double)w.N * (double)h->plan.k_pad * tc::LA * h->plan.wlimbs : 0.0;
+        run_k(ctx, KC_GEMM, macs, 0, st,
+              [&] { return gemm_run(d_a, w.K, M, w, h->plan, d_c, w.N, shift, nullptr, 0, h->ws, st); }, tc);
+    }
     CK(cudaGetLastError());
     return SLX_OK;
 }

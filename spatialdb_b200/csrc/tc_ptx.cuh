@@ -40,12 +40,13 @@ __device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: about two seconds of SM clock, then false.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait: `limit` SM clock cycles (default about two seconds), then false.
+constexpr long long kWaitCycles = 4000000000LL;
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long long limit = kWaitCycles) {
     if (mbar_try(bar, parity)) return true;
     long long t0 = clock64();
     while (!mbar_try_sleep(bar, parity)) {
-        if (clock64() - t0 > 4000000000LL) return false;
+        if (clock64() - t0 > limit) return false;
     }
     return true;
 }

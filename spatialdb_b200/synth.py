@@ -223,7 +223,7 @@ class EncoderShape:
 
 
 def write_encoder(path: str, shape: EncoderShape, wtype: int = Q8_0, seed: int = 0, arch: str = "nomic-bert",
-                  rope_base: float = 10000.0) -> str:
+                  rope_base: float = 10000.0, unk: int | None = None) -> str:
     """nomic-bert style encoder with N(0, 0.02) weights quantized to `wtype` (norms and token types F32).
 
     Tensor names and shapes are those IntegerTransformerSource.LoadFromReader reads
@@ -243,7 +243,7 @@ def write_encoder(path: str, shape: EncoderShape, wtype: int = Q8_0, seed: int =
     w.kv("tokenizer.ggml.tokens", T_ARRAY, (T_STRING, [f"t{i}" for i in range(V)]))
     w.kv("tokenizer.ggml.bos_token_id", T_UINT32, min(101, V - 1))
     w.kv("tokenizer.ggml.eos_token_id", T_UINT32, min(102, V - 1))
-    w.kv("tokenizer.ggml.unknown_token_id", T_UINT32, min(100, V - 1))
+    w.kv("tokenizer.ggml.unknown_token_id", T_UINT32, min(100, V - 1) if unk is None else unk)
 
     def normal(n):
         return rng.standard_normal(n, dtype=np.float32) * np.float32(0.02)
@@ -351,11 +351,43 @@ def model_dir() -> str:
 
 
 def cached(name: str, make) -> str:
-    """Path of a generated model, written once by make(path)."""
+    """Path of a generated model, written once by make(path). The file is written under a name of
+    this process's own and renamed into place, so ranks that generate it at the same time never
+    read a half-written file."""
     path = os.path.join(model_dir(), name)
     if not os.path.exists(path):
-        make(path)
+        tmp = f"{path}.tmp{os.getpid()}"
+        make(tmp)
+        os.replace(tmp, path)
     return path
+
+
+# ----------------------------------------------------------------------------------------------
+# the benchmark configurations' models (seeded; identical bytes on every machine)
+# ----------------------------------------------------------------------------------------------
+def encoder_q8_0_model() -> str:
+    """CPU-runnable encoder configuration: nomic-bert 12L d768 H12 F3072 V30522, Q8_0 weights."""
+    return cached("encoder_nomic_L12_d768_q8_0_seed1.gguf",
+                  lambda p: write_encoder(p, EncoderShape(), Q8_0, seed=1))
+
+
+def encoder_q4_0_model() -> str:
+    """Batched-encoder configuration: the same architecture with Q4_0 weights."""
+    return cached("encoder_nomic_L12_d768_q4_0_seed3.gguf",
+                  lambda p: write_encoder(p, EncoderShape(), Q4_0, seed=3))
+
+
+def gemma_model() -> str:
+    """Gemma-2B-shaped causal LM: 18L d2048 8q/1kv hd256 F16384 V256000, Q4_0 projections and
+    embeddings, F16 norms, EOS the last token (so greedy runs are not cut short by a random EOS)."""
+    shape = CausalShape()
+    return cached("gemma2b_shape_q4_0_f16norm_seed5.gguf",
+                  lambda p: write_causal(p, shape, Q4_0, F16, seed=5, eos=shape.vocab - 1))
+
+
+def gemma_prompts(batch: int, seq: int = 512, seed: int = 21) -> "np.ndarray":
+    """Seeded prompt ids [batch, seq] drawn uniformly from [0, vocab - 1) (EOS excluded)."""
+    return np.random.default_rng(seed).integers(0, CausalShape().vocab - 1, (batch, seq)).astype(np.int32)
 
 
 def gaussian_mixture(rng: np.random.Generator, n: int, dim: int = 768, centres: int = 1024, sigma: float = 0.1,

@@ -133,3 +133,27 @@ def test_gemv_large_scale_bits_take_general_path(ctx, oracle):
     want = oracle.matmul_long(a, 2, K, w, N, 30).reshape(2, N)
     got = slx.matmul_q30(a, synth.Q8_0, raw, N, scale_bits=45, shift=30, ctx=ctx)
     np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("M", [1, 8, 128, 200])
+@pytest.mark.parametrize("dtype,half", [(synth.Q8_0, False), (synth.Q4_0, False), (synth.Q4_0, True)])
+def test_prepared_weight_matches_oracle(ctx, oracle, M, dtype, half):
+    """slx_weight_prepare + slx_matmul_q30_prepared: digit planes built once, several products."""
+    import torch
+
+    rng = np.random.default_rng(31 * M + dtype)
+    K, N = 512, 384
+    raw = _raw(dtype, rng, N * K)
+    d_w = torch.from_numpy(raw).cuda()
+    w = slx.PreparedWeight(d_w.data_ptr(), raw.size, dtype, N, K, half_composite=half, ctx=ctx)
+    assert (w.N, w.K) == (N, K) and w.tensor_cores == 1
+    stream = torch.cuda.Stream()
+    for rep in range(2):
+        a = rng.integers(-(1 << 37), 1 << 37, (M, K), dtype=np.int64)
+        d_a = torch.from_numpy(a).cuda()
+        d_c = torch.empty((M, N), dtype=torch.int64, device="cuda")
+        torch.cuda.synchronize()
+        w.matmul_device(d_a.data_ptr(), M, d_c.data_ptr(), stream=stream.cuda_stream)
+        ctx.status(stream.cuda_stream)
+        np.testing.assert_array_equal(d_c.cpu().numpy(), _ref(oracle, a, dtype, raw, N, half, 30), err_msg=f"rep {rep}")
+    w.close()
