@@ -58,7 +58,8 @@ const char* slx_version(void);
  * row is outside the table (SLX_ERANGE), a tensor-core GEMM that gave up on a bounded wait
  * (SLX_ETIMEOUT) -- are recorded in the context's error word, which stays set until it is read:
  * slx_ctx_status waits for `stream` (NULL = the context's stream), returns the recorded status and
- * clears it. The host-buffer entry points check the word themselves and clear it when they start. */
+ * clears it. The host-buffer entry points clear the word when they start and check it (reporting
+ * and clearing what they find) before they return. */
 slx_status slx_ctx_status(slx_ctx* ctx, void* stream);
 /* Context options (no reference counterpart). SLX_OPT_WAIT_LIMIT_CYCLES: SM clock cycles after
  * which a wait inside the tensor-core projection GEMM gives up (0 = the default, about two seconds);

@@ -16,6 +16,7 @@ All work runs in the CUDA library; nothing here computes on the CPU.
 from __future__ import annotations
 
 import ctypes
+import weakref
 
 import numpy as np
 
@@ -77,6 +78,7 @@ class Context:
             raise SlxError(st, f"slx_init(device={device}) failed")
         self._h = h
         self.device = device
+        self._children = weakref.WeakSet()
 
     @classmethod
     def default(cls) -> "Context":
@@ -98,8 +100,19 @@ class Context:
         """slx_ctx_set_option (OPT_WAIT_LIMIT_CYCLES, OPT_TEST_STALL_MMA)."""
         self.check(self._lib.slx_ctx_set_option(self._h, option, int(value)))
 
+    def _adopt(self, child):
+        """Registers a handle created on this context (model, weight, lattice): closing the context
+        closes them first, so a garbage collection that finalizes the context before them (objects in
+        a reference cycle are finalized in no fixed order) never frees a handle after its context."""
+        self._children.add(child)
+
     def close(self):
         if getattr(self, "_h", None):
+            for c in list(getattr(self, "_children", ())):
+                try:
+                    c.close()
+                except Exception:
+                    pass
             self._lib.slx_destroy(self._h)
             self._h = None
 
@@ -152,6 +165,7 @@ class PreparedWeight:
         self.ctx.check(self.ctx._lib.slx_weight_prepare(self.ctx._h, VP(d_w), int(w_bytes), int(dtype), int(N), int(K),
                                                         int(half_composite), int(scale_bits), ctypes.byref(h)))
         self._h = h
+        self.ctx._adopt(self)
         info = (ctypes.c_int32 * 4)()
         self.ctx._lib.slx_weight_info(h, info, 4)
         self.N, self.K, self.tensor_cores, self.digits = list(info)
@@ -194,6 +208,7 @@ class _Model:
         h = VP()
         self.ctx.check(self.ctx._lib.slx_model_load_gguf(self.ctx._h, path.encode(), self.kind, scale_bits, ctypes.byref(h)))
         self._h = h
+        self.ctx._adopt(self)
         info = np.zeros(12, np.int32)
         self.ctx._lib.slx_model_info(self._h, _p(info, I32P), 12)
         (_, self.embd, self.heads, self.kv_heads, self.head_dim, self.ff, self.layers, self.vocab, self.eos, self.unk,
@@ -380,6 +395,7 @@ class EmbeddingLattice:
                                                          options.zero_threshold, options.global_scale, int(id_base),
                                                          ctypes.byref(h)))
         self._h = h
+        self._ctx._adopt(self)
         self.n, self.dim, self.id_base = v.shape[0], v.shape[1], int(id_base)
         self.last_exact = 0
 
@@ -394,6 +410,7 @@ class EmbeddingLattice:
                                                                 options.zero_threshold, options.global_scale,
                                                                 int(id_base), VP(stream), ctypes.byref(h)))
         self._h = h
+        self._ctx._adopt(self)
         self.n, self.dim, self.id_base = int(n), int(dim), int(id_base)
         self.last_exact = 0
         return self
@@ -485,6 +502,7 @@ class EmbeddingLattice:
             self._ctx.check(lib.slx_lattice_load_slat(self._ctx._h, str(source).encode(), options.zero_threshold,
                                                       options.global_scale, ctypes.byref(h)))
         self._h = h
+        self._ctx._adopt(self)
         info = np.zeros(3, np.int64)
         lib.slx_lattice_info(h, _p(info, I64P), 3)
         self.n, self.dim, self.id_base = int(info[0]), int(info[1]), int(info[2])

@@ -345,41 +345,43 @@ __global__ __launch_bounds__(32 * SM_ROWS) void k_softmax(int64_t* S, int SR, co
 // (p and v * 2^-30 are exact doubles and the FMA rounds once). S stays inside the window because
 // FixedSoftmax floors every share, so sum_s p_s <= 2^30 and |S| <= max |v| + T. A value with
 // |v| >= 2^50 raises the call's flag and the exact kernel redoes the call.
-constexpr int PV_TH = 256;
+constexpr int PV_TH = 128;  // four warps
 constexpr double PV_BASE = 6755399441055744.0;  // 1.5 * 2^52
 
+// Register tile of a thread: 8 query rows x 8 columns (64 fp64 accumulators). Per key a thread
+// loads its 8 columns of v and its 8 rows of p as four 16-byte shared loads each and issues 64
+// DFMAs. Columns of a thread: 2cg, 2cg+1 + 2 CG j (j < 4), so the eight lanes of a quarter warp
+// read 128 contiguous bytes of a v row; rows: 8 consecutive, contiguous in the key-major p tile.
 template <int HD>
 struct Pv {
-    static constexpr int CG = HD / 4;                    // thread columns 2c, 2c+1, HD/2+2c, HD/2+2c+1
-    static constexpr int RG = PV_TH / CG;                // row groups
-    static constexpr int RPT = RG >= 16 ? 128 / RG : 8;  // rows per thread (rows rg + RG*r)
-    static constexpr int PR = RG * RPT;                  // query rows per block: 128 (hd <= 64), 64, 32
-    static constexpr int VT = HD >= 128 ? 16 : 32;       // keys per chunk
-    static constexpr int PUS = VT + 4;                   // p row stride (uint32), rows 4 banks apart
-    static constexpr int PDS = VT + 2;                   // fp64 p row stride, rows 16 bytes apart mod 128
-    static constexpr int V_BYTES = VT * HD * 8, PU_BYTES = PR * PUS * 4;
+    static constexpr int CG = HD / 8;                    // column groups (lanes per row group)
+    static constexpr int RGW = 32 / CG;                  // row groups per warp
+    static constexpr int PR = (PV_TH / 32) * RGW * 8;    // query rows per block: 8192 / HD
+    static constexpr int VT = HD == 256 ? 16 : (HD / 2 < 32 ? HD / 2 : 32);  // keys per chunk
+    static constexpr int V_BYTES = VT * HD * 8;          // int64 v rows, converted in place to v * 2^-30
+    static constexpr int PU_BYTES = PR * VT * 4;         // uint32 p as 16-byte granules [VT/4][PR]
     static constexpr int BUF = V_BYTES + PU_BYTES;
-    static constexpr size_t SMEM = 2 * (size_t)BUF + (size_t)PR * PDS * 8;
-    static_assert(BUF % 16 == 0, "16-byte copies");
+    static constexpr size_t SMEM = 2 * (size_t)BUF + (size_t)PR * VT * 8;  // + fp64 p, key-major [VT][PR]
+    static_assert(CG >= 2 && CG <= 32 && BUF % 16 == 0 && VT % 4 == 0, "P.V tiling");
 };
 
 // PR query rows of one head over chunks of VT keys: the chunk's v rows (int64, straight from the
 // QKV buffer) and p rows (uint32) arrive by cp.async into one of two buffers while the other chunk
-// computes; v becomes v * 2^-30 in place and p is widened into Pd once per chunk.
+// computes; v becomes v * 2^-30 in place and p is widened and transposed into Pd once per chunk.
 template <int HD>
 __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const int64_t* __restrict__ V,
                                                   int64_t ldv, int64_t* __restrict__ O, int64_t ldo, int T, int nh,
                                                   int nkv, int* flag) {
     using C = Pv<HD>;
-    constexpr int VT = C::VT, RPT = C::RPT, CG = C::CG, RG = C::RG, PUS = C::PUS, PDS = C::PDS, PR = C::PR;
+    constexpr int VT = C::VT, CG = C::CG, RGW = C::RGW, PR = C::PR;
     if (*flag) return;
     extern __shared__ __align__(16) uint8_t sm[];
-    double* Pd = (double*)(sm + 2 * C::BUF);  // [PR][PDS]
+    double* Pd = (double*)(sm + 2 * C::BUF);  // [VT][PR]
     const int h = blockIdx.y, b = blockIdx.z, t0 = blockIdx.x * PR;
     const int z = b * nh + h, kvh = h / (nh / nkv);
     const int T4 = (T + 3) & ~3;
-    const int cg = threadIdx.x % CG, rg = threadIdx.x / CG;
-    const int c0 = 2 * cg, c1 = HD / 2 + 2 * cg;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cg = lane % CG, r0 = 8 * (warp * RGW + lane / CG);  // first of the thread's 8 rows
     const int64_t* v0 = V + (int64_t)b * T * ldv + (int64_t)kvh * HD;  // key s: v0 + s * ldv
     const uint32_t sbase = tc::smem_u32(sm);
     auto issue = [&](int k0, int buf) {
@@ -389,20 +391,20 @@ __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const
             const int s = g / (HD / 2), j = g % (HD / 2);
             cp_async16(dst + g * 16, s < keys ? v0 + (int64_t)(k0 + s) * ldv + 2 * j : v0, s < keys ? 16u : 0u);
         }
-        for (int g = threadIdx.x; g < PR * (VT / 4); g += PV_TH) {  // p: VT/4 granules a row
-            const int r = g / (VT / 4), s = k0 + 4 * (g % (VT / 4));
+        for (int g = threadIdx.x; g < PR * (VT / 4); g += PV_TH) {  // p: granule (row r, keys 4q..4q+3) at [q][r]
+            const int r = g % PR, q = g / PR, s = k0 + 4 * q;
             const int t = t0 + r;
             const bool ok = t < T && s < T4;
             const uint32_t* src = ok ? (const uint32_t*)(S + ((int64_t)z * T + t) * SR) + s : (const uint32_t*)S;
-            cp_async16(dst + C::V_BYTES + (r * PUS + 4 * (g % (VT / 4))) * 4, src, ok ? 16u : 0u);
+            cp_async16(dst + C::V_BYTES + g * 16, src, ok ? 16u : 0u);
         }
         cp_async_commit();
     };
-    double acc[RPT][4];
+    double acc[8][8];
 #pragma unroll
-    for (int r = 0; r < RPT; r++)
+    for (int r = 0; r < 8; r++)
 #pragma unroll
-        for (int c = 0; c < 4; c++) acc[r][c] = PV_BASE;
+        for (int c = 0; c < 8; c++) acc[r][c] = PV_BASE;
     bool wide = false;
     issue(0, 0);
     for (int k0 = 0, buf = 0; k0 < T; k0 += VT, buf ^= 1) {
@@ -410,29 +412,37 @@ __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const
         __syncthreads();  // chunk k0 is in for every thread; the other buffer and Pd are free
         if (k0 + VT < T) issue(k0 + VT, buf ^ 1);
         double* Vs = (double*)(sm + buf * C::BUF);
-        const uint32_t* Pu = (const uint32_t*)(sm + buf * C::BUF + C::V_BYTES);
+        const uint4* Pu = (const uint4*)(sm + buf * C::BUF + C::V_BYTES);
         for (int i = threadIdx.x; i < VT * HD; i += PV_TH) {  // exact for |v| < 2^53
             const int64_t x = ((const int64_t*)Vs)[i];
             wide |= (x >> 30) < -(1LL << 20) || (x >> 30) >= (1LL << 20);
             Vs[i] = (double)x * 0x1p-30;
         }
-        for (int i = threadIdx.x; i < PR * VT; i += PV_TH) {
-            const int r = i / VT, s = i % VT;
-            Pd[r * PDS + s] = (double)Pu[r * PUS + s];
+        for (int g = threadIdx.x; g < PR * (VT / 4); g += PV_TH) {
+            const uint4 u = Pu[g];
+            const int r = g % PR, q = g / PR;
+            Pd[(4 * q + 0) * PR + r] = (double)u.x;
+            Pd[(4 * q + 1) * PR + r] = (double)u.y;
+            Pd[(4 * q + 2) * PR + r] = (double)u.z;
+            Pd[(4 * q + 3) * PR + r] = (double)u.w;
         }
         __syncthreads();
-#pragma unroll 4
+#pragma unroll 2
         for (int s = 0; s < VT; s++) {  // one key at a time: every accumulator once per key
-            const double2 a0 = *(const double2*)(Vs + s * HD + c0);
-            const double2 a1 = *(const double2*)(Vs + s * HD + c1);
+            double2 v[4], p[4];
 #pragma unroll
-            for (int r = 0; r < RPT; r++) {
-                const double p = Pd[(rg + RG * r) * PDS + s];
-                acc[r][0] = __fma_rd(p, a0.x, acc[r][0]);
-                acc[r][1] = __fma_rd(p, a0.y, acc[r][1]);
-                acc[r][2] = __fma_rd(p, a1.x, acc[r][2]);
-                acc[r][3] = __fma_rd(p, a1.y, acc[r][3]);
-            }
+            for (int j = 0; j < 4; j++) v[j] = *(const double2*)(Vs + s * HD + 2 * cg + 2 * CG * j);
+#pragma unroll
+            for (int i = 0; i < 4; i++) p[i] = *(const double2*)(Pd + s * PR + r0 + 2 * i);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    acc[2 * i][2 * j] = __fma_rd(p[i].x, v[j].x, acc[2 * i][2 * j]);
+                    acc[2 * i][2 * j + 1] = __fma_rd(p[i].x, v[j].y, acc[2 * i][2 * j + 1]);
+                    acc[2 * i + 1][2 * j] = __fma_rd(p[i].y, v[j].x, acc[2 * i + 1][2 * j]);
+                    acc[2 * i + 1][2 * j + 1] = __fma_rd(p[i].y, v[j].y, acc[2 * i + 1][2 * j + 1]);
+                }
         }
     }
     if (__syncthreads_or(wide)) {
@@ -440,14 +450,14 @@ __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const
         return;
     }
 #pragma unroll
-    for (int r = 0; r < RPT; r++) {
-        const int t = t0 + rg + RG * r;
+    for (int r = 0; r < 8; r++) {
+        const int t = t0 + r0 + r;
         if (t >= T) continue;
         int64_t* orow = O + ((int64_t)b * T + t) * ldo + (int64_t)h * HD;
-        orow[c0] = (int64_t)(acc[r][0] - PV_BASE);
-        orow[c0 + 1] = (int64_t)(acc[r][1] - PV_BASE);
-        orow[c1] = (int64_t)(acc[r][2] - PV_BASE);
-        orow[c1 + 1] = (int64_t)(acc[r][3] - PV_BASE);
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            *(longlong2*)(orow + 2 * cg + 2 * CG * j) =
+                make_longlong2((int64_t)(acc[r][2 * j] - PV_BASE), (int64_t)(acc[r][2 * j + 1] - PV_BASE));
     }
 }
 
@@ -458,7 +468,8 @@ void launch_pv(int B, int T, int nh, int nkv, const int64_t* scores, int sr, con
                int64_t* out, int64_t ldo, int* flag, cudaStream_t st) {
     using C = Pv<HD>;
     static_assert(C::SMEM <= 112 * 1024, "two P.V blocks per SM");
-    if (((uintptr_t)v & 15) != 0 || (ldv & 1) != 0) {  // rows the 16-byte copies cannot read: the exact kernel
+    if (((uintptr_t)v & 15) != 0 || (ldv & 1) != 0 || ((uintptr_t)out & 15) != 0 || (ldo & 1) != 0) {
+        // rows the 16-byte copies and stores cannot address: the exact kernel
         cudaMemsetAsync(flag, 1, sizeof(int), st);
         return;
     }

@@ -9,6 +9,7 @@
 //             ApplyGemmaBlock (Gguf/IntegerGemmaSource.Forward.cs:32-75).
 // B independent sequences of T tokens run as one batch: every projection is one GEMM over B*T
 // rows, attention and pooling stay per sequence.
+#include <atomic>
 #include <algorithm>
 #include <cmath>
 #include <cstdarg>
@@ -54,6 +55,7 @@ struct slx_ctx {
     std::vector<ProfRecord> records;
     GemmWorkspace kws;               // scratch of the kernel-level matmul entry points
     WaitOptions wait;                // bounded-wait settings of the tensor-core GEMMs (slx_ctx_set_option)
+    std::atomic<int> refs{1};        // slx_destroy's reference plus one per live model, weight and lattice
     std::vector<cudaEvent_t> event_pool;
     cudaEvent_t event() {
         if (!event_pool.empty()) { cudaEvent_t e = event_pool.back(); event_pool.pop_back(); return e; }
@@ -601,9 +603,12 @@ int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, 
     return SLX_OK;
 }
 
+// Reads the context's device error word after the work queued on st, clears it (each error is
+// reported once) and maps it to a status.
 int check_flag(slx_ctx* ctx, cudaStream_t st) {
     int flag = 0;
     CK(cudaMemcpyAsync(&flag, ctx->d_flag, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CK(cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), st));
     CK(cudaStreamSynchronize(st));
     if (flag & KERR_RANGE) return set_err(ctx, SLX_ERANGE, "index out of range (token id and UNK row outside the table)");
     if (flag & KERR_TIMEOUT) return set_err(ctx, SLX_ETIMEOUT, "a tensor-core GEMM gave up on a bounded wait");
@@ -684,8 +689,11 @@ slx_status slx_init(int device, slx_ctx** out) {
     return SLX_OK;
 }
 
-slx_status slx_destroy(slx_ctx* ctx) {
-    if (!ctx) return SLX_EINVAL;
+// Drops one reference; the last one frees the context. Models, weights and lattices hold one each,
+// so the context (its device, stream and error word) outlives every object created on it, whatever
+// order the host frees them in (a garbage-collected host may finalize the context first).
+static void ctx_release(slx_ctx* ctx) {
+    if (ctx->refs.fetch_sub(1) != 1) return;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->d_flag);
@@ -694,6 +702,11 @@ slx_status slx_destroy(slx_ctx* ctx) {
     gemm_workspace_free(ctx->kws);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
+}
+
+slx_status slx_destroy(slx_ctx* ctx) {
+    if (!ctx) return SLX_EINVAL;
+    ctx_release(ctx);
     return SLX_OK;
 }
 
@@ -702,11 +715,7 @@ const char* slx_last_error(slx_ctx* ctx) { return ctx ? ctx->err.c_str() : "null
 slx_status slx_ctx_status(slx_ctx* ctx, void* stream) {
     if (!ctx) return SLX_EINVAL;
     CK(cudaSetDevice(ctx->device));
-    cudaStream_t st = pick(ctx, stream);
-    int rc = check_flag(ctx, st);
-    CK(cudaMemsetAsync(ctx->d_flag, 0, sizeof(int), st));
-    CK(cudaStreamSynchronize(st));
-    return rc;
+    return check_flag(ctx, pick(ctx, stream));
 }
 
 slx_status slx_ctx_set_option(slx_ctx* ctx, int option, int64_t value) {
@@ -751,15 +760,18 @@ slx_status slx_model_load_gguf(slx_ctx* ctx, const char* path, int kind, int sca
     if ((st = prepare_gemms(ctx, m.get()))) return st;
     CK(cudaStreamSynchronize(ctx->stream));
     CK(cudaGetLastError());
+    ctx->refs.fetch_add(1);
     *out = m.release();
     return SLX_OK;
 }
 
 slx_status slx_model_free(slx_model* m) {
     if (!m) return SLX_EINVAL;
-    cudaSetDevice(m->ctx->device);
-    cudaStreamSynchronize(m->ctx->stream);
+    slx_ctx* ctx = m->ctx;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
     delete m;
+    ctx_release(ctx);
     return SLX_OK;
 }
 
@@ -1105,15 +1117,18 @@ slx_status slx_weight_prepare(slx_ctx* ctx, const uint8_t* d_w, int64_t w_bytes,
     int rc = gemm_prepare(w, h->plan, ctx->stream, err);
     if (rc) return set_err(ctx, rc, "%s", err.c_str());
     CK(cudaStreamSynchronize(ctx->stream));
+    ctx->refs.fetch_add(1);
     *out = h.release();
     return SLX_OK;
 }
 
 slx_status slx_weight_free(slx_weight* w) {
     if (!w) return SLX_EINVAL;
-    cudaSetDevice(w->ctx->device);
-    cudaStreamSynchronize(w->ctx->stream);
+    slx_ctx* ctx = w->ctx;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
     delete w;
+    ctx_release(ctx);
     return SLX_OK;
 }
 
@@ -1282,6 +1297,7 @@ slx_status slx_lattice_build_device(slx_ctx* ctx, const float* d_vectors, int64_
         search::release(lat->L);
         return set_err(ctx, rc, "%s", err.c_str());
     }
+    ctx->refs.fetch_add(1);
     *out = lat.release();
     return SLX_OK;
 }
@@ -1305,11 +1321,13 @@ slx_status slx_lattice_build(slx_ctx* ctx, const float* vectors, int64_t n, int 
 
 slx_status slx_lattice_free(slx_lattice* lat) {
     if (!lat) return SLX_EINVAL;
-    cudaSetDevice(lat->ctx->device);
-    cudaStreamSynchronize(lat->ctx->stream);
+    slx_ctx* ctx = lat->ctx;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
     tree::release(lat->tree);
     search::release(lat->L);
     delete lat;
+    ctx_release(ctx);
     return SLX_OK;
 }
 
@@ -1485,6 +1503,7 @@ static slx_status lattice_load(slx_ctx* ctx, const uint8_t* bytes, int64_t n, fl
         return set_err(ctx, SLX_ECUDA, "%s", cudaGetErrorString(e));
     }
     lat->has_tree = true;
+    ctx->refs.fetch_add(1);
     *out = lat.release();
     return SLX_OK;
 }
