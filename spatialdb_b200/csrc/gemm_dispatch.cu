@@ -83,6 +83,50 @@ int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPla
     return 3;
 }
 
+int gemm_run_multi(const int64_t* a, int64_t lda, int M, int n, const WDesc* const* w, const GemmPlan* const* plan,
+                   int64_t* const* c, const int64_t* ldc, int shift, GemmWorkspace& ws, cudaStream_t st) {
+    if (M <= 0 || n <= 0) return 0;
+    bool shared = true;
+    for (int i = 0; i < n; i++)
+        shared = shared && plan[i]->use_tc && plan[i]->k_pad == plan[0]->k_pad && w[i]->K == w[0]->K &&
+                 !gemv_supported(*w[i], M);
+    if (!shared) {
+        int q = 0;
+        for (int i = 0; i < n; i++) q += gemm_run(a, lda, M, *w[i], *plan[i], c[i], ldc[i], shift, nullptr, 0, ws, st);
+        return q;
+    }
+    const int64_t mpad = round_up(M, tc::BM), kpad = plan[0]->k_pad;
+    const size_t need = (size_t)tc::LA * mpad * kpad + 256;
+    if (need > ws.bytes) {
+        if (ws.p) cudaFree(ws.p);
+        ws.p = nullptr;
+        ws.bytes = 0;
+        if (cudaMalloc(&ws.p, need) != cudaSuccess) {
+            int q = 0;
+            for (int i = 0; i < n; i++) q += gemm_exact(a, lda, M, (int)w[i]->K, *w[i], c[i], ldc[i], shift, nullptr, 0, st);
+            return q;
+        }
+        ws.bytes = need;
+        cudaMemsetAsync(ws.p, 0, need, st);  // flag words, and the GEMV's row-tile counters start at zero
+    }
+    int* flag = (int*)ws.p;
+    int8_t* planes = (int8_t*)ws.p + 256;
+    alignas(64) unsigned char tmap_a[128];
+    if (!tc::encode_planes(tmap_a, planes, kpad, mpad, tc::LA, tc::GM, 1, tc::GK)) {
+        int q = 0;
+        for (int i = 0; i < n; i++) q += gemm_exact(a, lda, M, (int)w[i]->K, *w[i], c[i], ldc[i], shift, nullptr, 0, st);
+        return q;
+    }
+    cudaMemsetAsync(flag, 0, sizeof(int), st);
+    tc::split_a(a, lda, M, (int)w[0]->K, mpad, kpad, planes, flag, st);
+    for (int i = 0; i < n; i++) {
+        tc::launch(tmap_a, plan[i]->tmap_w, plan[i]->wlimbs, M, (int)w[i]->N, (int)w[i]->K, mpad, plan[i]->n_pad, kpad,
+                   shift, c[i], ldc[i], nullptr, 0, flag, ws.err, st, plan[i]->row_shift, ws.wait);
+        gemm_exact(a, lda, M, (int)w[i]->K, *w[i], c[i], ldc[i], shift, nullptr, 0, st, flag);  // only if the split overflowed
+    }
+    return 1 + 2 * n;
+}
+
 void gemm_workspace_free(GemmWorkspace& ws) {
     if (ws.p) cudaFree(ws.p);
     ws.p = nullptr;

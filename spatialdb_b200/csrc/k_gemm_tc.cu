@@ -302,21 +302,10 @@ __global__ void k_split_a4(const int64_t* __restrict__ A, int64_t lda, int M, in
         const longlong2 hi = *(const longlong2*)(A + (int64_t)row * lda + k0 + 2);
         x[0] = lo.x; x[1] = lo.y; x[2] = hi.x; x[3] = hi.y;
     }
+    static_assert(LA == 5, "digit_words4 forms five digits");
     uint32_t pk[LA];
-#pragma unroll
-    for (int i = 0; i < LA; i++) pk[i] = 0;
     bool bad = false;
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        int64_t v = x[j];
-#pragma unroll
-        for (int i = 0; i < LA; i++) {
-            const int d = (int)(((uint64_t)v + 128u) & 255u) - 128;
-            v = (v - d) >> 8;
-            pk[i] |= (uint32_t)(uint8_t)(int8_t)d << (8 * j);
-        }
-        bad |= v != 0;
-    }
+    digit_words4(x[0], x[1], x[2], x[3], pk, bad);
     if (bad) atomicOr(overflow, 1);
 #pragma unroll
     for (int i = 0; i < LA; i++) *(uint32_t*)(planes + ((int64_t)i * Mpad + row) * Kpad + k0) = pk[i];
@@ -337,21 +326,16 @@ __global__ void k_split_heads(const int64_t* __restrict__ X, int64_t ld, int T, 
     const int h = (int)(bh % nh);
     const int64_t b = bh / nh;
     uint32_t pk[LA][4];
-#pragma unroll
-    for (int i = 0; i < LA; i++)
-#pragma unroll
-        for (int q = 0; q < 4; q++) pk[i][q] = 0;
     bool bad = false;
+    int64_t x[16];
 #pragma unroll
-    for (int j = 0; j < 16; j++) {
-        int64_t x = (t < T && k0 + j < hd) ? X[(b * T + t) * ld + (int64_t)h * hd + k0 + j] : 0;
+    for (int j = 0; j < 16; j++) x[j] = (t < T && k0 + j < hd) ? X[(b * T + t) * ld + (int64_t)h * hd + k0 + j] : 0;
 #pragma unroll
-        for (int i = 0; i < LA; i++) {
-            int d = (int)(((uint64_t)x + 128u) & 255u) - 128;
-            x = (x - d) >> 8;
-            pk[i][j >> 2] |= (uint32_t)(uint8_t)(int8_t)d << (8 * (j & 3));
-        }
-        bad |= x != 0;
+    for (int q = 0; q < 4; q++) {
+        uint32_t w[LA];
+        digit_words4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3], w, bad);
+#pragma unroll
+        for (int i = 0; i < LA; i++) pk[i][q] = w[i];
     }
     if (bad) atomicOr(overflow, 1);
 #pragma unroll

@@ -856,6 +856,7 @@ bool gemv_reserve(GemmWorkspace& ws, int M, int N, int K, cudaStream_t st) {
 int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift,
                GemmWorkspace& ws, cudaStream_t st) {
     if (M == 1) {
+        if (gemv1(w, a, c, shift, ws.err, st)) return 1;
         if (w.dtype == DT_Q4_0) launch_dp4a<true, 1>(w, a, lda, c, ldc, shift, ws, st);
         else launch_dp4a<false, 1>(w, a, lda, c, ldc, shift, ws, st);
         return 2;

@@ -261,6 +261,25 @@ SLX_DEV int64_t silu_gate30(int64_t g, int64_t u) {
     return lo64(sar128((i128)s * u, 30));
 }
 
+// Five balanced base-256 digits (each in [-128, 127]) of four values x0..x3: w[i] holds digit i of
+// x_j in byte j. For x in [-0x8080808080, 0x7F7F7F7F7F] the digits are the low five bytes of
+// (x + 0x8080808080) ^ 0x8080808080 (adding 128 at every byte position leaves bytes d_i + 128 with no
+// carries); bad is set when a value lies outside that range (it would need a sixth digit).
+SLX_DEV void digit_words4(int64_t x0, int64_t x1, int64_t x2, int64_t x3, uint32_t (&w)[5], bool& bad) {
+    constexpr uint64_t OFF = 0x8080808080ull;
+    const uint64_t y0 = (uint64_t)x0 + OFF, y1 = (uint64_t)x1 + OFF, y2 = (uint64_t)x2 + OFF, y3 = (uint64_t)x3 + OFF;
+    bad |= ((y0 | y1 | y2 | y3) >> 40) != 0;
+    const uint64_t z0 = y0 ^ OFF, z1 = y1 ^ OFF, z2 = y2 ^ OFF, z3 = y3 ^ OFF;
+    const uint32_t l0 = (uint32_t)z0, l1 = (uint32_t)z1, l2 = (uint32_t)z2, l3 = (uint32_t)z3;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint32_t sel = (uint32_t)i | ((uint32_t)(4 + i) << 4);
+        w[i] = __byte_perm(__byte_perm(l0, l1, sel), __byte_perm(l2, l3, sel), 0x5410);
+    }
+    w[4] = __byte_perm(__byte_perm((uint32_t)(z0 >> 32), (uint32_t)(z1 >> 32), 0x40),
+                       __byte_perm((uint32_t)(z2 >> 32), (uint32_t)(z3 >> 32), 0x40), 0x5410);
+}
+
 // 128-bit warp reductions (wrap-around sums).
 SLX_DEV u128 warp_sum_u128(u128 v) {
     for (int o = 16; o > 0; o >>= 1) {

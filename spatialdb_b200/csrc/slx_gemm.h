@@ -67,6 +67,11 @@ int gemm_prepare(const WDesc& w, GemmPlan& plan, cudaStream_t st, std::string& e
 int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPlan& plan, int64_t* c, int64_t ldc,
               int shift, const int64_t* r, int64_t ldr, GemmWorkspace& ws, cudaStream_t st);
 void gemm_workspace_free(GemmWorkspace& ws);
+// Several projections of the same activations (Q/K/V, gate/up): c_i = (a . w_i^T) >> shift. The
+// activation digits are formed once for all of them when every weight takes the tensor-core path
+// with the same K padding; otherwise each runs as gemm_run. Returns the kernels queued.
+int gemm_run_multi(const int64_t* a, int64_t lda, int M, int n, const WDesc* const* w, const GemmPlan* const* plan,
+                   int64_t* const* c, const int64_t* ldc, int shift, GemmWorkspace& ws, cudaStream_t st);
 
 // Decode-shaped exact GEMV (M <= 8) straight from packed Q4_0 / Q8_0 blocks with the long
 // composite, digit products on the tensor cores (k_gemv_tc.cu).
@@ -74,6 +79,10 @@ bool gemv_supported(const WDesc& w, int M);
 size_t gemv_workspace(int M, int N, int K);
 // Grows ws for an M x N x K GEMV (zeroing it when it allocates); false when out of memory.
 bool gemv_reserve(GemmWorkspace& ws, int M, int N, int K, cudaStream_t st);
+// Single-row GEMV (k_gemv1.cu): one launch of persistent CTAs streaming the packed Q4_0 / Q8_0 rows
+// by bulk copies, activation digits formed in-kernel. false (nothing queued) when the shape is not
+// covered (K / 32 a multiple of 8 and at most 256, composite scale 2^24 .. 2^39, 16-byte aligned).
+bool gemv1(const WDesc& w, const int64_t* a, int64_t* c, int shift, int* err, cudaStream_t st);
 // One launch; bounded-wait timeouts set KERR_TIMEOUT in *ws.err when it is set.
 int gemv_exact(const int64_t* a, int64_t lda, int M, const WDesc& w, int64_t* c, int64_t ldc, int shift,
                GemmWorkspace& ws, cudaStream_t st);

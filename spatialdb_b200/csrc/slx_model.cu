@@ -179,9 +179,16 @@ struct slx_model {
         if (need > b.bytes) {
             if (b.p) cudaFree(b.p);
             b.p = nullptr;
+            // A generate loop asks for one more token row every step: grow by at least a quarter, so
+            // the buffers (and cudaFree's device synchronisation) are not renewed at every step.
+            const size_t grown = b.bytes ? std::max(need, b.bytes + b.bytes / 4) : need;
             b.bytes = 0;
-            if (cudaMalloc(&b.p, need) != cudaSuccess) return nullptr;
-            b.bytes = need;
+            if (cudaMalloc(&b.p, grown) != cudaSuccess) {
+                if (grown == need || cudaMalloc(&b.p, need) != cudaSuccess) return nullptr;
+                b.bytes = need;
+            } else {
+                b.bytes = grown;
+            }
         }
         return (T*)b.p;
     }
@@ -513,6 +520,18 @@ inline void project(slx_model* m, const int64_t* a, int64_t lda, int M, const WD
     run_k(m->ctx, KC_GEMM, macs, 0, st, [&] { return gemm_run(a, lda, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st); },
           tc);
 }
+// Projections of the same activations (Q/K/V, gate/up), the activation digits formed once.
+inline void project_multi(slx_model* m, const int64_t* a, int64_t lda, int M, int n, const WDesc* const* w,
+                          const GemmPlan* const* p, int64_t* const* c, const int64_t* ldc, cudaStream_t st) {
+    double macs = 0, tc = 0;
+    for (int i = 0; i < n; i++) {
+        macs += (double)M * (double)w[i]->N * (double)w[i]->K;
+        if (p[i]->use_tc && !gemv_supported(*w[i], M))
+            tc += (double)M * (double)w[i]->N * (double)p[i]->k_pad * tc::LA * p[i]->wlimbs;
+    }
+    run_k(m->ctx, KC_GEMM, macs, 0, st,
+          [&] { return gemm_run_multi(a, lda, M, n, w, p, c, ldc, m->scale_bits, m->gws, st); }, tc);
+}
 #define RUN(cls, macs, bytes, call) run_k(ctx, cls, macs, bytes, st, [&] { return call; })
 
 // Encoder forward to the last block's output, x[B*T][d] (layer limit for tracing).
@@ -540,8 +559,13 @@ int encoder_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers,
         RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0, attend(m, qkv, 3 * d, qkv + d, 3 * d, qkv + 2 * d, 3 * d, att, d, B, T, m->heads, m->heads, hd, sshift, sq, 0, 0, st));
         project(m, att, d, M, l.o, l.p_o, h, d, x, d, st);  // O-projection + residual (AddInPlace)
         RUN(KC_NORM, 0, 0, layernorm_rows(h, d, M, d, l.anw, l.anb, st));
-        project(m, h, d, M, l.gate, l.p_gate, gate, F, nullptr, 0, st);
-        project(m, h, d, M, l.up, l.p_up, up, F, nullptr, 0, st);
+        {  // gate and up read the same normalised rows: one digit split for both
+            const WDesc* ws2[2] = {&l.gate, &l.up};
+            const GemmPlan* ps2[2] = {&l.p_gate, &l.p_up};
+            int64_t* cs2[2] = {gate, up};
+            const int64_t ld2[2] = {F, F};
+            project_multi(m, h, d, M, 2, ws2, ps2, cs2, ld2, st);
+        }
         RUN(KC_FFN_GATE, 0, 0, silu_gate(gate, F, up, F, M, F, st));
         project(m, up, F, M, l.down, l.p_down, x, d, h, d, st);  // down-projection + residual
         RUN(KC_NORM, 0, 0, layernorm_rows(x, d, M, d, l.lnw, l.lnb, st));
@@ -576,9 +600,13 @@ int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, 
         bool global = !causal || m->global_interval <= 0 || ((i + 1) % m->global_interval) == 0;  // IsGlobalLayer
         cudaMemcpyAsync(xn, x, sizeof(int64_t) * M * d, cudaMemcpyDeviceToDevice, st);
         RUN(KC_NORM, 0, 0, rmsnorm_rows(xn, d, M, 1, d, l.attn_norm, st));
-        project(m, xn, d, M, l.q, l.p_q, q, qd, nullptr, 0, st);
-        project(m, xn, d, M, l.k, l.p_k, k, kvd, nullptr, 0, st);
-        project(m, xn, d, M, l.v, l.p_v, v, kvd, nullptr, 0, st);
+        {  // Q, K and V read the same normalised rows: one digit split for all three
+            const WDesc* ws3[3] = {&l.q, &l.k, &l.v};
+            const GemmPlan* ps3[3] = {&l.p_q, &l.p_k, &l.p_v};
+            int64_t* cs3[3] = {q, k, v};
+            const int64_t ld3[3] = {qd, kvd, kvd};
+            project_multi(m, xn, d, M, 3, ws3, ps3, cs3, ld3, st);
+        }
         RUN(KC_NORM, 0, 0, rmsnorm_rows(q, qd, M * m->heads, m->heads, hd, l.qn, st));
         RUN(KC_NORM, 0, 0, rmsnorm_rows(k, kvd, M * m->kv_heads, m->kv_heads, hd, l.kn, st));
         const int64_t* cs = global ? m->cos_g : m->cos_l;
@@ -592,8 +620,13 @@ int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, 
         RUN(KC_ADD, 0, 0, add_rows(p, d, x, d, M, d, st));  // projected += residual; p is the FFN residual
         cudaMemcpyAsync(xn, p, sizeof(int64_t) * M * d, cudaMemcpyDeviceToDevice, st);
         RUN(KC_NORM, 0, 0, rmsnorm_rows(xn, d, M, 1, d, l.ffn_norm, st));
-        project(m, xn, d, M, l.gate, l.p_gate, gate, F, nullptr, 0, st);
-        project(m, xn, d, M, l.up, l.p_up, up, F, nullptr, 0, st);
+        {
+            const WDesc* ws2[2] = {&l.gate, &l.up};
+            const GemmPlan* ps2[2] = {&l.p_gate, &l.p_up};
+            int64_t* cs2[2] = {gate, up};
+            const int64_t ld2[2] = {F, F};
+            project_multi(m, xn, d, M, 2, ws2, ps2, cs2, ld2, st);
+        }
         RUN(KC_FFN_GATE, 0, 0, silu_gate(gate, F, up, F, M, F, st));
         project(m, up, F, M, l.down, l.p_down, x, d, nullptr, 0, st);
         RUN(KC_NORM, 0, 0, rmsnorm_rows(x, d, M, 1, d, l.post_ffw, st));

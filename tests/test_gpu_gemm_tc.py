@@ -92,9 +92,10 @@ def test_gemv_matches_oracle(ctx, oracle, M, dtype, K, N):
     np.testing.assert_array_equal(got, _ref(oracle, a, dtype, raw, N, False, 30))
 
 
-def test_gemv_non_finite_scales_and_overflow(ctx, oracle):
+@pytest.mark.parametrize("M", [1, 2])
+def test_gemv_non_finite_scales_and_overflow(ctx, oracle, M):
     rng = np.random.default_rng(77)
-    M, K, N = 2, 256, 40
+    K, N = 256, 40
     raw = synth.random_q4_0(rng, N * K).reshape(-1, 18)
     raw[3, 0:2] = np.frombuffer(np.float16(np.inf).tobytes(), np.uint8)
     raw[9, 0:2] = np.frombuffer(np.float16(np.nan).tobytes(), np.uint8)
@@ -102,8 +103,23 @@ def test_gemv_non_finite_scales_and_overflow(ctx, oracle):
     raw = raw.reshape(-1)
     a = rng.integers(-(1 << 30), 1 << 30, (M, K), dtype=np.int64)
     np.testing.assert_array_equal(slx.matmul_q30(a, synth.Q4_0, raw, N, ctx=ctx), _ref(oracle, a, synth.Q4_0, raw, N, False, 30))
-    a[1, 5] = 1 << 44  # beyond 5 digits: exact fallback
+    a[M - 1, 5] = 1 << 44  # beyond 5 digits: exact fallback
     np.testing.assert_array_equal(slx.matmul_q30(a, synth.Q4_0, raw, N, ctx=ctx), _ref(oracle, a, synth.Q4_0, raw, N, False, 30))
+
+
+@pytest.mark.parametrize("K,N", [(8192, 70), (2048, 1001), (256, 5)])
+@pytest.mark.parametrize("dtype", [synth.Q4_0, synth.Q8_0])
+def test_gemv_single_row_widths(ctx, oracle, K, N, dtype):
+    """M = 1 at the single-row kernel's limits: 256 quant blocks a row (one row group per CTA), row
+    counts that leave a partial last stage, rows narrower than a warp of blocks, and activations at
+    the five-digit limits."""
+    rng = np.random.default_rng(K + N + dtype)
+    raw = _raw(dtype, rng, N * K)
+    a = rng.integers(-(1 << 38), 1 << 38, (1, K), dtype=np.int64)
+    a[0, :3] = [0x7F7F7F7F7F, -0x8080808080, 0]
+    for shift in (30, 0):
+        got = slx.matmul_q30(a, dtype, raw, N, shift=shift, ctx=ctx)
+        np.testing.assert_array_equal(got, _ref(oracle, a, dtype, raw, N, False, shift))
 
 
 @pytest.mark.parametrize("M", [1, 3, 8])
