@@ -508,7 +508,8 @@ bool attention_tc_supported(int T, int nh, int nkv, int hd) {
 
 int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
                  int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int score_shift, int64_t sqrt_hd,
-                 int mode, int window, void* ws, int* err, cudaStream_t st) {
+                 int mode, int window, void* ws, int* err, cudaStream_t st, const int64_t* rope_cs,
+                 const int64_t* rope_sn) {
     if (score_shift < 0 || score_shift > 32 || sqrt_hd < 1) return -1;
     const Layout l = layout(B, T, nh, nkv, hd);
     uint8_t* base = (uint8_t*)ws;
@@ -522,8 +523,13 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
         !encode_planes(mk, kp, l.kpad, l.tk, LA, NK, (int64_t)B * nkv))
         return -1;
     cudaMemsetAsync(flag, 0, sizeof(int), st);
-    split_heads(q, ldq, B, T, nh, hd, l.tq, l.kpad, qp, flag, st);
-    split_heads(k, ldk, B, T, nkv, hd, l.tk, l.kpad, kp, flag, st);
+    if (rope_cs) {  // ApplyRoPE on q and k in place, fused with their digit split
+        rope_split_heads(const_cast<int64_t*>(q), ldq, B, T, nh, hd, l.tq, l.kpad, rope_cs, rope_sn, qp, flag, st);
+        rope_split_heads(const_cast<int64_t*>(k), ldk, B, T, nkv, hd, l.tk, l.kpad, rope_cs, rope_sn, kp, flag, st);
+    } else {
+        split_heads(q, ldq, B, T, nh, hd, l.tq, l.kpad, qp, flag, st);
+        split_heads(k, ldk, B, T, nkv, hd, l.tk, l.kpad, kp, flag, st);
+    }
 
     ScoreParams sp;
     sp.T = T; sp.SR = (int)l.sr; sp.nh = nh; sp.zgroup = nh / nkv; sp.nkv = nkv;

@@ -343,6 +343,59 @@ __global__ void k_split_heads(const int64_t* __restrict__ X, int64_t ld, int T, 
         *(uint4*)(planes + ((bh * LA + i) * tpad + t) * kpad + k0) = make_uint4(pk[i][0], pk[i][1], pk[i][2], pk[i][3]);
 }
 
+// ApplyRoPE (Math/IntegerAttention.cs:35-58) fused with the head digit split: X row (b*T + t), head h,
+// values rotated in place as the reference does (pairs p, p + hd/2 at position t, Int128 products
+// >> 30), and their balanced digits written to planes[(b*nh + h)][i][t][k] as k_split_heads does
+// (t < tpad, k < kpad, zero padded). A thread owns four pairs of a head row (positions 4q..4q+3 and
+// their partners half + 4q..): it rewrites them, writes both digit quads, and zeroes its share of
+// the row's padding columns hd..kpad. Rows t >= T get zero digits. hd is a power of two >= 16.
+__global__ void k_rope_split_heads(int64_t* __restrict__ X, int64_t ld, int T, int nh, int hd, int tpad, int kpad,
+                                   const int64_t* __restrict__ cs, const int64_t* __restrict__ sn,
+                                   int8_t* __restrict__ planes, int* overflow, int64_t total) {
+    const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (idx >= total) return;
+    const int half = hd / 2, qpr = half / 4;  // threads per head row
+    const int q = (int)(idx % qpr);
+    const int64_t r = idx / qpr;  // over (b*nh + h) * tpad + t
+    const int t = (int)(r % tpad);
+    const int64_t bh = r / tpad;
+    const int h = (int)(bh % nh);
+    const int64_t b = bh / nh;
+    const int p0 = 4 * q;
+    int64_t ya[4] = {0, 0, 0, 0}, yb[4] = {0, 0, 0, 0};  // rotated values at p0.. and half + p0..
+    bool bad = false;
+    if (t < T) {
+        int64_t* row = X + (b * T + t) * ld + (int64_t)h * hd;
+        const longlong2 a0 = *(const longlong2*)(row + p0), a1 = *(const longlong2*)(row + p0 + 2);
+        const longlong2 b0 = *(const longlong2*)(row + half + p0), b1 = *(const longlong2*)(row + half + p0 + 2);
+        const int64_t xa[4] = {a0.x, a0.y, a1.x, a1.y}, xb[4] = {b0.x, b0.y, b1.x, b1.y};
+        const int64_t* crow = cs + (int64_t)t * half + p0;
+        const int64_t* srow = sn + (int64_t)t * half + p0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int64_t c = crow[j], s = srow[j];
+            ya[j] = lo64(sar128((i128)((u128)((i128)xa[j] * c) - (u128)((i128)xb[j] * s)), 30));
+            yb[j] = lo64(sar128((i128)((u128)((i128)xa[j] * s) + (u128)((i128)xb[j] * c)), 30));
+        }
+        *(longlong2*)(row + p0) = make_longlong2(ya[0], ya[1]);
+        *(longlong2*)(row + p0 + 2) = make_longlong2(ya[2], ya[3]);
+        *(longlong2*)(row + half + p0) = make_longlong2(yb[0], yb[1]);
+        *(longlong2*)(row + half + p0 + 2) = make_longlong2(yb[2], yb[3]);
+    }
+    uint32_t wa[LA], wb[LA];
+    digit_words4(ya[0], ya[1], ya[2], ya[3], wa, bad);
+    digit_words4(yb[0], yb[1], yb[2], yb[3], wb, bad);
+    const int pad = (kpad - hd) / qpr;  // padding bytes of this thread per plane row (a multiple of 8)
+#pragma unroll
+    for (int i = 0; i < LA; i++) {
+        int8_t* prow = planes + ((bh * LA + i) * tpad + t) * kpad;
+        *(uint32_t*)(prow + p0) = wa[i];
+        *(uint32_t*)(prow + half + p0) = wb[i];
+        for (int z = 0; z < pad; z += 8) *(uint64_t*)(prow + hd + q * pad + z) = 0;
+    }
+    if (bad) atomicOr(overflow, 1);
+}
+
 // Common trailing zero bits of each weight row's Q30 composites (0 for an all-zero row).
 // Q4_0 / Q8_0 composites are d_int * q with d_int an f16 mantissa times a power of two, so a row
 // typically shares ten or more low zero bits; storing w >> tz[n] saves one or two digits.
@@ -522,6 +575,14 @@ void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K,
         case 3: launch_lw<3>(ta, tw, p, st); break;
         default: launch_lw<4>(ta, tw, p, st); break;
     }
+}
+
+void rope_split_heads(int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad,
+                      const int64_t* cs, const int64_t* sn, int8_t* planes, int* overflow, cudaStream_t st) {
+    const int64_t total = (int64_t)B * nh * tpad * (hd / 8);
+    if (total <= 0) return;
+    k_rope_split_heads<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(x, ld, T, nh, hd, (int)tpad, (int)kpad, cs, sn,
+                                                                       planes, overflow, total);
 }
 
 void split_heads(const int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad, int8_t* planes,

@@ -11,10 +11,11 @@
 // blocks are one contiguous byte range of the weight:
 //   * a producer warp streams that range in stages of SR rows with 1D bulk copies (cp.async.bulk,
 //     no multicast) into a ring of NS shared-memory slots, each slot an mbarrier with a byte count;
-//   * every consumer thread owns one block column b of the row (K / 32 columns, in RG row groups
-//     that take alternate stages) and forms that column's 40 activation digit words itself, once,
-//     in registers; per stage it reads its block of each of the SR rows from shared memory (5 or 9
-//     words), runs the 40 dp4a and the Int128 multiply-add;
+//   * the consumers stage the activation row in shared memory with coalesced loads; every consumer
+//     thread then owns one block column b of the row (K / 32 columns, in RG row groups that take
+//     alternate stages) and forms that column's 40 activation digit words, once, in registers; per
+//     stage it reads its block of each of the SR rows from shared memory (5 or 9 words), runs the
+//     40 dp4a and the Int128 multiply-add;
 //   * the SR per-row partial sums of a warp are reduced by a butterfly (SR Int128 values shrink to
 //     one per lane), the group's warps leave theirs in shared memory, and the last warp of the group
 //     to arrive (an atomic count, no barrier) adds them and writes lo64(sum >> shift) for the rows.
@@ -173,6 +174,9 @@ __global__ void __launch_bounds__(G1_THREADS, 2) k_gemv1(G1Params p) {
     uint64_t* red_lo = (uint64_t*)(bars + 2 * p.ns);
     int64_t* red_hi = (int64_t*)(red_lo + (size_t)p.ns * 8 * G1_SR);
     int* red_cnt = (int*)(red_hi + (size_t)p.ns * 8 * G1_SR);
+    // the activation row, staged by coalesced loads: block b's 32 values at b * 34 (16-byte aligned rows,
+    // four banks apart, so each quarter warp's 16-byte reads of 8 consecutive blocks are conflict-free)
+    int64_t* as = (int64_t*)(((uintptr_t)(red_cnt + p.ns) + 15) & ~(uintptr_t)15);
     __shared__ int s_fail, s_wide;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -234,12 +238,16 @@ __global__ void __launch_bounds__(G1_THREADS, 2) k_gemv1(G1Params p) {
     for (int j = 0; j < 8; j++)
 #pragma unroll
         for (int i = 0; i < G1_ND; i++) dq[j][i] = 0;
+    for (int i = tid; i < p.NB * 16; i += G1_CONS) {  // 16-byte granules of the row, coalesced
+        const longlong2 v = __ldg((const longlong2*)p.A + i);
+        *(longlong2*)(as + (i >> 4) * 34 + 2 * (i & 15)) = v;
+    }
+    asm volatile("bar.sync 9, %0;" ::"n"(G1_CONS) : "memory");
     if (col) {
-        const longlong2* a2 = (const longlong2*)(p.A + (int64_t)b * 32);
         int64_t x[32];
 #pragma unroll
         for (int e = 0; e < 16; e++) {
-            const longlong2 v = __ldg(a2 + e);
+            const longlong2 v = *(const longlong2*)(as + b * 34 + 2 * e);
             x[2 * e] = v.x;
             x[2 * e + 1] = v.y;
         }
@@ -277,7 +285,7 @@ __global__ void __launch_bounds__(G1_THREADS, 2) k_gemv1(G1Params p) {
         if (col && ok) {
 #pragma unroll
             for (int r = 0; r < G1_SR; r++) {
-                if (n0 + r >= p.N) break;
+                // rows past N (a partial last stage) compute on stale bytes of the slot; never written out
                 const int o = r * row_bytes + b * BB;
                 uint32_t wq[8];
                 const int64_t D = g1_scale(g1_block<Q4>(sl, o, wq), p.sbits);
@@ -352,11 +360,12 @@ bool launch_gemv1(const WDesc& w, const int64_t* a, int64_t* c, int shift, int* 
     p.nbp = (NB + 31) / 32 * 32;
     p.rg = std::min(8, G1_CONS / p.nbp);
     const int slot = G1_SR * NB * BB;  // a multiple of 16 bytes (NB % 8 == 0)
-    p.ns = std::max(2, std::min(8, (96 * 1024 - 4096) / slot));
+    const size_t astage = (size_t)NB * 34 * 8 + 16;  // the staged activation row
+    p.ns = (int)std::max<int64_t>(2, std::min<int64_t>(8, ((int64_t)110 * 1024 - 4096 - (int64_t)astage) / slot));
     p.W = w.data; p.A = a; p.sbits = e - 1; p.shift = shift; p.C = c; p.err = err;
     // the ring, then per slot two mbarriers, 8 warps x SR Int128 partials and a counter
-    const size_t smem = (size_t)p.ns * slot + (size_t)p.ns * (16 + 8 * G1_SR * 16 + 4);
-    if (smem > 200 * 1024) return false;
+    const size_t smem = (size_t)p.ns * slot + (size_t)p.ns * (16 + 8 * G1_SR * 16 + 4) + astage;
+    if (smem > 112 * 1024) return false;  // two CTAs per SM
     if (slx::ensure_smem((const void*)k_gemv1<Q4>, smem) != cudaSuccess) return false;
     const int grid = std::min(2 * slx::device_sm_count(), p.stages);
     k_gemv1<Q4><<<grid, G1_THREADS, smem, st>>>(p);

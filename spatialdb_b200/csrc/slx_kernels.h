@@ -60,7 +60,8 @@ int attention(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, cons
 
 
 
-// Same attention with tensor-core scores (k_attn.cu): digit split of q/k, tcgen05 score GEMM,
+// Same attention with tensor-core scores (k_attn.cu): digit split of q/k (with rope_cs / rope_sn
+// given, ApplyRoPE is applied to q and k in place by the same pass), tcgen05 score GEMM,
 // CUDA-core softmax and per-term PV, and the exact kernel gated behind them for out-of-range
 // inputs. ws must hold attention_tc_workspace() bytes. Returns the kernels queued, -1 if the
 // tensor maps could not be encoded (nothing queued).
@@ -68,7 +69,8 @@ size_t attention_tc_workspace(int B, int T, int nh, int nkv, int hd);
 bool attention_tc_supported(int T, int nh, int nkv, int hd);
 int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
                  int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int score_shift, int64_t sqrt_hd,
-                 int mode, int window, void* ws, int* err, cudaStream_t st);
+                 int mode, int window, void* ws, int* err, cudaStream_t st, const int64_t* rope_cs = nullptr,
+                 const int64_t* rope_sn = nullptr);
 
 // up[i] = (FixedSiLU(gate[i]) * up[i]) >> 30 over M rows of F (IntegerFFN)
 int silu_gate(const int64_t* gate, int64_t ldg, int64_t* up, int64_t ldu, int M, int F, cudaStream_t st);

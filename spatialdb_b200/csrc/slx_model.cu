@@ -495,19 +495,23 @@ int prepare_gemms(slx_ctx* ctx, slx_model* m) {
 }
 
 // Attention for one layer: tensor-core scores when the shape allows (exact kernel gated behind).
-int attend(slx_model* m, const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
+// q and k are rotated in place first (ApplyRoPE with the cos / sin tables): by the tensor-core path's
+// digit split itself, or by k_rope before the exact kernel.
+int attend(slx_model* m, int64_t* q, int64_t ldq, int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
            int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int sshift, int64_t sq, int mode, int window,
-           cudaStream_t st) {
+           const int64_t* cs, const int64_t* sn, cudaStream_t st) {
     if (tc_enabled() && attention_tc_supported(T, nh, nkv, hd)) {
         size_t need = attention_tc_workspace(B, T, nh, nkv, hd);
         void* ws = m->buf<uint8_t>("attn_ws", need);
         if (ws) {
             int n = attention_tc(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, sshift, sq, mode, window, ws,
-                                 m->ctx->d_flag, st);
+                                 m->ctx->d_flag, st, cs, sn);
             if (n >= 0) return n;
         }
     }
-    return attention(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, sshift, sq, mode, window, st);
+    int n = rope_rows(q, ldq, B, T, nh, hd, cs, sn, st);
+    n += rope_rows(k, ldk, B, T, nkv, hd, cs, sn, st);
+    return n + attention(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, sshift, sq, mode, window, st);
 }
 
 // One projection: c = (a . w^T) >> shift (+ r).
@@ -554,9 +558,9 @@ int encoder_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers,
     for (int i = 0; i < nl; i++) {
         auto& l = m->L[i];
         project(m, x, d, M, l.qkv, l.p_qkv, qkv, 3 * d, nullptr, 0, st);
-        RUN(KC_ROPE, 0, 0, rope_rows(qkv, 3 * d, B, T, m->heads, hd, m->cos_g, m->sin_g, st));
-        RUN(KC_ROPE, 0, 0, rope_rows(qkv + d, 3 * d, B, T, m->heads, hd, m->cos_g, m->sin_g, st));
-        RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0, attend(m, qkv, 3 * d, qkv + d, 3 * d, qkv + 2 * d, 3 * d, att, d, B, T, m->heads, m->heads, hd, sshift, sq, 0, 0, st));
+        RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0,
+            attend(m, qkv, 3 * d, qkv + d, 3 * d, qkv + 2 * d, 3 * d, att, d, B, T, m->heads, m->heads, hd, sshift, sq, 0, 0,
+                   m->cos_g, m->sin_g, st));
         project(m, att, d, M, l.o, l.p_o, h, d, x, d, st);  // O-projection + residual (AddInPlace)
         RUN(KC_NORM, 0, 0, layernorm_rows(h, d, M, d, l.anw, l.anb, st));
         {  // gate and up read the same normalised rows: one digit split for both
@@ -611,10 +615,9 @@ int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, 
         RUN(KC_NORM, 0, 0, rmsnorm_rows(k, kvd, M * m->kv_heads, m->kv_heads, hd, l.kn, st));
         const int64_t* cs = global ? m->cos_g : m->cos_l;
         const int64_t* sn = global ? m->sin_g : m->sin_l;
-        RUN(KC_ROPE, 0, 0, rope_rows(q, qd, B, T, m->heads, hd, cs, sn, st));
-        RUN(KC_ROPE, 0, 0, rope_rows(k, kvd, B, T, m->kv_heads, hd, cs, sn, st));
         int mode = !causal ? 0 : ((global || m->sliding <= 0) ? 1 : 2);
-        RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0, attend(m, q, qd, k, kvd, v, kvd, att, qd, B, T, m->heads, m->kv_heads, hd, sshift, sq, mode, m->sliding, st));
+        RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0,
+            attend(m, q, qd, k, kvd, v, kvd, att, qd, B, T, m->heads, m->kv_heads, hd, sshift, sq, mode, m->sliding, cs, sn, st));
         project(m, att, qd, M, l.o, l.p_o, p, d, nullptr, 0, st);
         RUN(KC_NORM, 0, 0, rmsnorm_rows(p, d, M, 1, d, l.post_attn, st));
         RUN(KC_ADD, 0, 0, add_rows(p, d, x, d, M, d, st));  // projected += residual; p is the FFN residual
