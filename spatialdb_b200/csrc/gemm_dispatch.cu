@@ -127,6 +127,19 @@ int gemm_run_multi(const int64_t* a, int64_t lda, int M, int n, const WDesc* con
     return 1 + 2 * n;
 }
 
+bool gemm_run_planes(const int8_t* planes, const int* flag, const int64_t* a, int64_t lda, int M, const WDesc& w,
+                     const GemmPlan& plan, int64_t* c, int64_t ldc, int shift, const int64_t* r, int64_t ldr,
+                     GemmWorkspace& ws, cudaStream_t st) {
+    if (M <= 0 || !plan.use_tc || (!r && gemv_supported(w, M))) return false;
+    const int64_t mpad = round_up(M, tc::BM);
+    alignas(64) unsigned char tmap_a[128];
+    if (!tc::encode_planes(tmap_a, const_cast<int8_t*>(planes), plan.k_pad, mpad, tc::LA, tc::GM, 1, tc::GK)) return false;
+    tc::launch(tmap_a, plan.tmap_w, plan.wlimbs, M, (int)w.N, (int)w.K, mpad, plan.n_pad, plan.k_pad, shift, c, ldc, r,
+               ldr, flag, ws.err, st, plan.row_shift, ws.wait);
+    gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st, flag);  // runs only if a value overflowed its digits
+    return true;
+}
+
 void gemm_workspace_free(GemmWorkspace& ws) {
     if (ws.p) cudaFree(ws.p);
     ws.p = nullptr;

@@ -413,6 +413,86 @@ __global__ __launch_bounds__(256, 4) void k_layernorm_warp(int64_t* __restrict__
     }
 }
 
+// NormalizeRow again, for rows whose length n is a multiple of 4, with each lane taking four
+// consecutive values at a time (columns 128 q + 4 lane + 0..3): the row is read three times (sum,
+// sum of squares, output; the rereads come from cache) instead of being held in registers, so the
+// kernel needs few registers and keeps many rows in flight. With planes given it also writes the
+// outputs' five balanced digit planes ([5][Mpad][Kpad] int8, the next projection's activation
+// operand; columns n..Kpad zero) and raises *overflow for a value beyond five digits.
+template <int NQ>
+__global__ __launch_bounds__(256) void k_layernorm_q(int64_t* __restrict__ X, int64_t ld, int rows, int n,
+                                                     const int64_t* __restrict__ w, const int64_t* __restrict__ b,
+                                                     int Mpad, int Kpad, int8_t* __restrict__ planes, int* overflow) {
+    __shared__ __align__(16) int64_t sw[128 * NQ], sb[128 * NQ];
+    __shared__ __align__(16) double swd[128 * NQ];
+    for (int j = threadIdx.x; j < 128 * NQ; j += blockDim.x) {
+        const bool in = j < n;
+        sw[j] = in ? w[j] : 0;
+        sb[j] = in ? b[j] : 0;
+        swd[j] = in ? d_i64(w[j]) : 0.0;
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const uint64_t inv = ~0ULL / (uint64_t)n;
+    bool bad = false;
+    for (int row = blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += gridDim.x * 8) {
+        int64_t* x = X + (int64_t)row * ld;
+        u128 s = 0;
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            const int j = 128 * q + 4 * lane;
+            if (j < n) {
+                const longlong2 a = __ldg((const longlong2*)(x + j)), c = __ldg((const longlong2*)(x + j + 2));
+                s += (u128)(i128)a.x + (u128)(i128)a.y + (u128)(i128)c.x + (u128)(i128)c.y;
+            }
+        }
+        s = warp_sum_u128(s);
+        const int64_t mean = div_i128_n(s, (uint32_t)n, inv);
+        u128 ss = 0;
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            const int j = 128 * q + 4 * lane;
+            if (j < n) {
+                const longlong2 a = __ldg((const longlong2*)(x + j)), c = __ldg((const longlong2*)(x + j + 2));
+                const int64_t d0 = wsub(a.x, mean), d1 = wsub(a.y, mean), d2 = wsub(c.x, mean), d3 = wsub(c.y, mean);
+                ss += (u128)((i128)d0 * d0) + (u128)((i128)d1 * d1) + (u128)((i128)d2 * d2) + (u128)((i128)d3 * d3);
+            }
+        }
+        ss = warp_sum_u128(ss);
+        // Int128 variance = sumSq / n (a wrapped, negative sumSq gives var <= 0 as in the reference)
+        const i128 var = (i128)ss < 0 ? (i128)0 : (i128)udiv128_u32(ss, (uint32_t)n, inv);
+        int64_t isq = var > 0 ? isqrt_u128((u128)var) : 1;
+        if (isq == 0) isq = 1;
+        const double rd = 1.0 / (double)isq;
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            const int j = 128 * q + 4 * lane;
+            int64_t y[4] = {0, 0, 0, 0};
+            if (j < n) {
+                if (var <= 0) {  // x = bias (IntegerLayerNorm.cs:39-44)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) y[e] = sb[j + e];
+                } else {
+                    const longlong2 a = __ldg((const longlong2*)(x + j)), c = __ldg((const longlong2*)(x + j + 2));
+                    const int64_t v[4] = {a.x, a.y, c.x, c.y};
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                        y[e] = wadd(muldiv_trunc(wsub(v[e], mean), sw[j + e], swd[j + e], isq, rd), sb[j + e]);
+                }
+                *(longlong2*)(x + j) = make_longlong2(y[0], y[1]);
+                *(longlong2*)(x + j + 2) = make_longlong2(y[2], y[3]);
+            }
+            if (planes && j < Kpad) {
+                uint32_t wd[5];
+                digit_words4(y[0], y[1], y[2], y[3], wd, bad);
+#pragma unroll
+                for (int i = 0; i < 5; i++) *(uint32_t*)(planes + ((int64_t)i * Mpad + row) * Kpad + j) = wd[i];
+            }
+        }
+    }
+    if (bad) atomicOr(overflow, 1);
+}
+
 // RmsNormRow (IntegerLayerNorm.cs:71-93); row r = segment (r % per) of line (r / per).
 __global__ __launch_bounds__(NT) void k_rmsnorm(int64_t* __restrict__ X, int64_t ld, int per, int n,
                                                 const int64_t* __restrict__ w) {
@@ -450,6 +530,25 @@ int layernorm_rows(int64_t* x, int64_t ld, int rows, int n, const int64_t* w, co
     else if (n <= 1024) k_layernorm_warp<32><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b);
     else k_layernorm<<<rows, NT, 0, st>>>(x, ld, n, w, b);
     return 1;
+}
+
+int layernorm_rows_digits(int64_t* x, int64_t ld, int rows, int n, const int64_t* w, const int64_t* b, int64_t Mpad,
+                          int64_t Kpad, int8_t* planes, int* overflow, cudaStream_t st) {
+    if (rows <= 0) return 0;
+    const int nq = (int)((Kpad + 127) / 128);
+    if (n % 4 != 0 || (ld & 1) != 0 || ((uintptr_t)x & 15) != 0 || nq > 8 || Kpad % 128 != 0 || Kpad < n) return -1;
+    int k = 0;
+    if (planes && Mpad > rows)  // padding rows of every plane: zero digits
+        for (int i = 0; i < 5; i++, k++)
+            cudaMemsetAsync(planes + ((int64_t)i * Mpad + rows) * Kpad, 0, (size_t)(Mpad - rows) * Kpad, st);
+    const unsigned wb = (unsigned)std::min((rows + 7) / 8, 148 * 8);
+    switch (nq) {
+        case 1: k_layernorm_q<1><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b, (int)Mpad, (int)Kpad, planes, overflow); break;
+        case 2: k_layernorm_q<2><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b, (int)Mpad, (int)Kpad, planes, overflow); break;
+        case 3: case 4: k_layernorm_q<4><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b, (int)Mpad, (int)Kpad, planes, overflow); break;
+        default: k_layernorm_q<8><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b, (int)Mpad, (int)Kpad, planes, overflow); break;
+    }
+    return k + 1;
 }
 
 int rmsnorm_rows(int64_t* x, int64_t ld, int rows, int per, int n, const int64_t* w, cudaStream_t st) {
@@ -593,6 +692,37 @@ __global__ void k_silu_gate(const int64_t* __restrict__ G, int64_t ldg, int64_t*
         int64_t* u = U + (int64_t)m * ldu + f;
         *u = silu_gate30(G[(int64_t)m * ldg + f], *u);
     }
+}
+
+// The same gate for four consecutive columns a thread, which also writes the five balanced digit
+// planes of the gated values ([5][Mpad][Kpad] int8, the next projection's activation operand) and sets
+// *overflow when a value needs a sixth digit. Columns F..Kpad get zero digits; rows M..Mpad are left
+// to the caller. F % 4 == 0 and 16-byte aligned rows.
+__global__ void k_silu_gate_digits(const int64_t* __restrict__ G, int64_t ldg, int64_t* __restrict__ U, int64_t ldu,
+                                   int F, int rows, int Mpad, int Kpad, int8_t* __restrict__ planes, int* overflow) {
+    const int f = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (f >= Kpad) return;
+    bool bad = false;
+    for (int m = blockIdx.y; m < rows; m += gridDim.y) {
+        int64_t y[4] = {0, 0, 0, 0};
+        if (f < F) {
+            const int64_t* g = G + (int64_t)m * ldg + f;
+            int64_t* u = U + (int64_t)m * ldu + f;
+            const longlong2 g0 = *(const longlong2*)g, g1 = *(const longlong2*)(g + 2);
+            const longlong2 u0 = *(const longlong2*)u, u1 = *(const longlong2*)(u + 2);
+            y[0] = silu_gate30(g0.x, u0.x);
+            y[1] = silu_gate30(g0.y, u0.y);
+            y[2] = silu_gate30(g1.x, u1.x);
+            y[3] = silu_gate30(g1.y, u1.y);
+            *(longlong2*)u = make_longlong2(y[0], y[1]);
+            *(longlong2*)(u + 2) = make_longlong2(y[2], y[3]);
+        }
+        uint32_t w[5];
+        digit_words4(y[0], y[1], y[2], y[3], w, bad);
+#pragma unroll
+        for (int i = 0; i < 5; i++) *(uint32_t*)(planes + ((int64_t)i * Mpad + m) * Kpad + f) = w[i];
+    }
+    if (bad) atomicOr(overflow, 1);
 }
 
 __global__ void k_add(int64_t* __restrict__ D, int64_t ldd, const int64_t* __restrict__ S, int64_t lds, int n,
@@ -772,6 +902,18 @@ int silu_gate(const int64_t* gate, int64_t ldg, int64_t* up, int64_t ldu, int M,
     const dim3 grid((unsigned)((F + 255) / 256), (unsigned)(M < 65535 ? M : 65535));
     k_silu_gate<<<grid, 256, 0, st>>>(gate, ldg, up, ldu, F, M);
     return 1;
+}
+
+int silu_gate_digits(const int64_t* gate, int64_t ldg, int64_t* up, int64_t ldu, int M, int F, int64_t Mpad, int64_t Kpad,
+                     int8_t* planes, int* overflow, cudaStream_t st) {
+    if (M <= 0 || F <= 0) return 0;
+    int n = 0;
+    if (Mpad > M)  // padding rows of every plane: zero digits
+        for (int i = 0; i < 5; i++, n++)
+            cudaMemsetAsync(planes + ((int64_t)i * Mpad + M) * Kpad, 0, (size_t)(Mpad - M) * Kpad, st);
+    const dim3 grid((unsigned)((Kpad / 4 + 255) / 256), (unsigned)(M < 65535 ? M : 65535));
+    k_silu_gate_digits<<<grid, 256, 0, st>>>(gate, ldg, up, ldu, F, M, (int)Mpad, (int)Kpad, planes, overflow);
+    return n + 1;
 }
 
 int add_rows(int64_t* dst, int64_t ldd, const int64_t* src, int64_t lds, int M, int n, cudaStream_t st) {

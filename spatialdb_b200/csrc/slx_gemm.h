@@ -70,6 +70,12 @@ int gemm_prepare(const WDesc& w, GemmPlan& plan, cudaStream_t st, std::string& e
 int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPlan& plan, int64_t* c, int64_t ldc,
               int shift, const int64_t* r, int64_t ldr, GemmWorkspace& ws, cudaStream_t st);
 void gemm_workspace_free(GemmWorkspace& ws);
+// gemm_run with the activations' digit planes already written by their producer: planes
+// [5][round_up(M, 128)][plan.k_pad] int8 and its overflow word *flag (nonzero: the exact kernel
+// computes the call). false (nothing queued) when the weight does not take the tensor-core path.
+bool gemm_run_planes(const int8_t* planes, const int* flag, const int64_t* a, int64_t lda, int M, const WDesc& w,
+                     const GemmPlan& plan, int64_t* c, int64_t ldc, int shift, const int64_t* r, int64_t ldr,
+                     GemmWorkspace& ws, cudaStream_t st);
 // Several projections of the same activations (Q/K/V, gate/up): c_i = (a . w_i^T) >> shift. The
 // activation digits are formed once for all of them when every weight takes the tensor-core path
 // with the same K padding; otherwise each runs as gemm_run. Returns the kernels queued.

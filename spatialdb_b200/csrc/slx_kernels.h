@@ -43,6 +43,12 @@ int embed_scaled(const int32_t* ids, int B, int T, const WDesc& tok, int unk, in
 
 // LayerNorm rows (IntegerLayerNorm.NormalizeRow): rows of length n at x + r*ld.
 int layernorm_rows(int64_t* x, int64_t ld, int rows, int n, const int64_t* w, const int64_t* b, cudaStream_t st);
+// The same LayerNorm (n % 4 == 0, 16-byte aligned rows) with, when planes is not null, the outputs'
+// digit planes [5][Mpad][Kpad] written alongside (the next projection's operand, zero padded) and
+// *overflow raised for a value beyond five digits. Returns -1 (nothing queued) for shapes it does
+// not cover.
+int layernorm_rows_digits(int64_t* x, int64_t ld, int rows, int n, const int64_t* w, const int64_t* b, int64_t Mpad,
+                          int64_t Kpad, int8_t* planes, int* overflow, cudaStream_t st);
 // RmsNorm rows (IntegerLayerNorm.RmsNormRow): row r is segment (r % per) of line (r / per),
 // x + (r/per)*ld + (r%per)*n, length n; per > 1 gives RmsNormPerHead.
 int rmsnorm_rows(int64_t* x, int64_t ld, int rows, int per, int n, const int64_t* w, cudaStream_t st);
@@ -74,6 +80,11 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
 
 // up[i] = (FixedSiLU(gate[i]) * up[i]) >> 30 over M rows of F (IntegerFFN)
 int silu_gate(const int64_t* gate, int64_t ldg, int64_t* up, int64_t ldu, int M, int F, cudaStream_t st);
+// The same gate, also writing the gated values' digit planes [5][Mpad][Kpad] (the next projection's
+// operand, zero padded) and raising *overflow for a value beyond five digits. F % 4 == 0, rows 16-byte
+// aligned (ldg, ldu even).
+int silu_gate_digits(const int64_t* gate, int64_t ldg, int64_t* up, int64_t ldu, int M, int F, int64_t Mpad, int64_t Kpad,
+                     int8_t* planes, int* overflow, cudaStream_t st);
 // dst = dst + src (unchecked long adds) over M rows of n
 int add_rows(int64_t* dst, int64_t ldd, const int64_t* src, int64_t lds, int M, int n, cudaStream_t st);
 // pooled[b][j] = (long)(sum_t x[b*T+t][j] / T)  (MeanPool)

@@ -536,6 +536,71 @@ inline void project_multi(slx_model* m, const int64_t* a, int64_t lda, int M, in
     run_k(m->ctx, KC_GEMM, macs, 0, st,
           [&] { return gemm_run_multi(a, lda, M, n, w, p, c, ldc, m->scale_bits, m->gws, st); }, tc);
 }
+// FixedSiLU gate then the down projection (IntegerFFN.Apply, Math/IntegerFFN.cs:70-100): the gate
+// kernel writes the down projection's activation digit planes as it writes the gated values, so
+// the projection skips its own digit split; shapes it does not cover take the separate kernels.
+inline void gate_down(slx_model* m, const int64_t* gate, int64_t* up, int F, int M, const WDesc& w, const GemmPlan& p,
+                      int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, cudaStream_t st) {
+    slx_ctx* ctx = m->ctx;
+    const int64_t mpad = (M + tc::BM - 1) / tc::BM * tc::BM;
+    const bool fused = F % 4 == 0 && p.use_tc && !(!r && gemv_supported(w, M)) && p.k_pad == (F + tc::BK - 1) / tc::BK * tc::BK;
+    uint8_t* buf = fused ? m->buf<uint8_t>("down_planes", 256 + (size_t)tc::LA * mpad * p.k_pad) : nullptr;
+    if (!buf) {
+        run_k(ctx, KC_FFN_GATE, 0, 0, st, [&] { return silu_gate(gate, F, up, F, M, F, st); });
+        project(m, up, F, M, w, p, c, ldc, r, ldr, st);
+        return;
+    }
+    int* flag = (int*)buf;
+    int8_t* planes = (int8_t*)buf + 256;
+    cudaMemsetAsync(flag, 0, sizeof(int), st);
+    run_k(ctx, KC_FFN_GATE, 0, 0, st,
+          [&] { return silu_gate_digits(gate, F, up, F, M, F, mpad, p.k_pad, planes, flag, st); });
+    const double macs = (double)M * (double)w.N * (double)w.K;
+    const double tc = (double)M * (double)w.N * (double)p.k_pad * tc::LA * p.wlimbs;
+    run_k(ctx, KC_GEMM, macs, 0, st, [&] {
+        if (gemm_run_planes(planes, flag, up, F, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st)) return 2;
+        return gemm_run(up, F, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st);
+    }, tc);
+}
+// LayerNorm of M rows of d (IntegerLayerNorm.NormalizeRow) that also writes the rows' activation
+// digit planes for the projection(s) reading them next. Returns the planes buffer (overflow word at
+// byte 0, planes [5][M_pad][K_pad] from byte 256), or nullptr when the plain kernel ran instead.
+inline uint8_t* norm_digits(slx_model* m, int64_t* x, int M, int d, const int64_t* w, const int64_t* b, cudaStream_t st) {
+    slx_ctx* ctx = m->ctx;
+    const int64_t mpad = (M + tc::BM - 1) / tc::BM * tc::BM, kpad = (d + tc::BK - 1) / tc::BK * tc::BK;
+    uint8_t* buf = tc_enabled() ? m->buf<uint8_t>("ln_planes", 256 + (size_t)tc::LA * mpad * kpad) : nullptr;
+    int n = -1;
+    if (buf) {
+        cudaMemsetAsync(buf, 0, sizeof(int), st);
+        run_k(ctx, KC_NORM, 0, 0, st, [&] {
+            n = layernorm_rows_digits(x, d, M, d, w, b, mpad, kpad, (int8_t*)buf + 256, (int*)buf, st);
+            return n < 0 ? 0 : n;
+        });
+    }
+    if (n >= 0) return buf;
+    run_k(ctx, KC_NORM, 0, 0, st, [&] { return layernorm_rows(x, d, M, d, w, b, st); });
+    return nullptr;
+}
+
+// A projection of rows whose digit planes a producer wrote (norm_digits); the split runs itself when
+// there are none or the weight does not take the tensor-core path.
+inline void project_from(slx_model* m, const uint8_t* planes, const int64_t* a, int64_t lda, int M, const WDesc& w,
+                         const GemmPlan& p, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, cudaStream_t st) {
+    const int64_t kpad = (w.K + tc::BK - 1) / tc::BK * tc::BK;
+    if (!planes || p.k_pad != kpad) {
+        project(m, a, lda, M, w, p, c, ldc, r, ldr, st);
+        return;
+    }
+    const double macs = (double)M * (double)w.N * (double)w.K;
+    const bool tcp = p.use_tc && !(!r && gemv_supported(w, M));
+    const double tc = tcp ? (double)M * (double)w.N * (double)p.k_pad * tc::LA * p.wlimbs : 0.0;
+    run_k(m->ctx, KC_GEMM, macs, 0, st, [&] {
+        if (gemm_run_planes((const int8_t*)planes + 256, (const int*)planes, a, lda, M, w, p, c, ldc, m->scale_bits, r, ldr,
+                            m->gws, st))
+            return 2;
+        return gemm_run(a, lda, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st);
+    }, tc);
+}
 #define RUN(cls, macs, bytes, call) run_k(ctx, cls, macs, bytes, st, [&] { return call; })
 
 // Encoder forward to the last block's output, x[B*T][d] (layer limit for tracing).
@@ -551,28 +616,30 @@ int encoder_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers,
     int64_t* up = m->buf<int64_t>("up", (size_t)M * F);
     if (!x || !qkv || !att || !h || !gate || !up) return set_err(ctx, SLX_EOOM, "workspace allocation failed (M=%d)", M);
     RUN(KC_EMBED, 0, 0, embed_encoder(ids, B, T, m->tok, m->tt, m->unk, x, ctx->d_flag, st));
-    RUN(KC_NORM, 0, 0, layernorm_rows(x, d, M, d, m->enw, m->enb, st));
+    const uint8_t* xpl = norm_digits(m, x, M, d, m->enw, m->enb, st);  // digit planes of x for the QKV projection
     const int sshift = 2 * m->scale_bits - 30;
     const int64_t sq = std::max<int64_t>(1, isqrt64_host(hd));
     int nl = n_layers < 0 ? m->layers : std::min(n_layers, m->layers);
     for (int i = 0; i < nl; i++) {
         auto& l = m->L[i];
-        project(m, x, d, M, l.qkv, l.p_qkv, qkv, 3 * d, nullptr, 0, st);
+        project_from(m, xpl, x, d, M, l.qkv, l.p_qkv, qkv, 3 * d, nullptr, 0, st);
         RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0,
             attend(m, qkv, 3 * d, qkv + d, 3 * d, qkv + 2 * d, 3 * d, att, d, B, T, m->heads, m->heads, hd, sshift, sq, 0, 0,
                    m->cos_g, m->sin_g, st));
         project(m, att, d, M, l.o, l.p_o, h, d, x, d, st);  // O-projection + residual (AddInPlace)
-        RUN(KC_NORM, 0, 0, layernorm_rows(h, d, M, d, l.anw, l.anb, st));
-        {  // gate and up read the same normalised rows: one digit split for both
+        const uint8_t* hpl = norm_digits(m, h, M, d, l.anw, l.anb, st);
+        if (hpl) {  // gate and up read the normalised rows' digit planes the norm wrote
+            project_from(m, hpl, h, d, M, l.gate, l.p_gate, gate, F, nullptr, 0, st);
+            project_from(m, hpl, h, d, M, l.up, l.p_up, up, F, nullptr, 0, st);
+        } else {  // one digit split for both
             const WDesc* ws2[2] = {&l.gate, &l.up};
             const GemmPlan* ps2[2] = {&l.p_gate, &l.p_up};
             int64_t* cs2[2] = {gate, up};
             const int64_t ld2[2] = {F, F};
             project_multi(m, h, d, M, 2, ws2, ps2, cs2, ld2, st);
         }
-        RUN(KC_FFN_GATE, 0, 0, silu_gate(gate, F, up, F, M, F, st));
-        project(m, up, F, M, l.down, l.p_down, x, d, h, d, st);  // down-projection + residual
-        RUN(KC_NORM, 0, 0, layernorm_rows(x, d, M, d, l.lnw, l.lnb, st));
+        gate_down(m, gate, up, F, M, l.down, l.p_down, x, d, h, d, st);  // SiLU gate, down-projection + residual
+        xpl = norm_digits(m, x, M, d, l.lnw, l.lnb, st);
     }
     x_out = x;
     return SLX_OK;
@@ -630,8 +697,7 @@ int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, 
             const int64_t ld2[2] = {F, F};
             project_multi(m, xn, d, M, 2, ws2, ps2, cs2, ld2, st);
         }
-        RUN(KC_FFN_GATE, 0, 0, silu_gate(gate, F, up, F, M, F, st));
-        project(m, up, F, M, l.down, l.p_down, x, d, nullptr, 0, st);
+        gate_down(m, gate, up, F, M, l.down, l.p_down, x, d, nullptr, 0, st);
         RUN(KC_NORM, 0, 0, rmsnorm_rows(x, d, M, 1, d, l.post_ffw, st));
         RUN(KC_ADD, 0, 0, add_rows(x, d, p, d, M, d, st));
     }
