@@ -423,15 +423,6 @@ template <int NQ>
 __global__ __launch_bounds__(256) void k_layernorm_q(int64_t* __restrict__ X, int64_t ld, int rows, int n,
                                                      const int64_t* __restrict__ w, const int64_t* __restrict__ b,
                                                      int Mpad, int Kpad, int8_t* __restrict__ planes, int* overflow) {
-    __shared__ __align__(16) int64_t sw[128 * NQ], sb[128 * NQ];
-    __shared__ __align__(16) double swd[128 * NQ];
-    for (int j = threadIdx.x; j < 128 * NQ; j += blockDim.x) {
-        const bool in = j < n;
-        sw[j] = in ? w[j] : 0;
-        sb[j] = in ? b[j] : 0;
-        swd[j] = in ? d_i64(w[j]) : 0.0;
-    }
-    __syncthreads();
     const int lane = threadIdx.x & 31;
     const uint64_t inv = ~0ULL / (uint64_t)n;
     bool bad = false;
@@ -464,20 +455,24 @@ __global__ __launch_bounds__(256) void k_layernorm_q(int64_t* __restrict__ X, in
         int64_t isq = var > 0 ? isqrt_u128((u128)var) : 1;
         if (isq == 0) isq = 1;
         const double rd = 1.0 / (double)isq;
-#pragma unroll
-        for (int q = 0; q < NQ; q++) {
+#pragma unroll 1
+        for (int q = 0; q < NQ; q++) {  // not unrolled: the per-value division code stays in the instruction cache
             const int j = 128 * q + 4 * lane;
             int64_t y[4] = {0, 0, 0, 0};
             if (j < n) {
+                // the weight and bias (the same for every row: cached reads)
+                const longlong2 b0 = __ldg((const longlong2*)(b + j)), b1 = __ldg((const longlong2*)(b + j + 2));
+                const int64_t bb[4] = {b0.x, b0.y, b1.x, b1.y};
                 if (var <= 0) {  // x = bias (IntegerLayerNorm.cs:39-44)
 #pragma unroll
-                    for (int e = 0; e < 4; e++) y[e] = sb[j + e];
+                    for (int e = 0; e < 4; e++) y[e] = bb[e];
                 } else {
                     const longlong2 a = __ldg((const longlong2*)(x + j)), c = __ldg((const longlong2*)(x + j + 2));
-                    const int64_t v[4] = {a.x, a.y, c.x, c.y};
+                    const longlong2 w0 = __ldg((const longlong2*)(w + j)), w1 = __ldg((const longlong2*)(w + j + 2));
+                    const int64_t v[4] = {a.x, a.y, c.x, c.y}, ww[4] = {w0.x, w0.y, w1.x, w1.y};
 #pragma unroll
                     for (int e = 0; e < 4; e++)
-                        y[e] = wadd(muldiv_trunc(wsub(v[e], mean), sw[j + e], swd[j + e], isq, rd), sb[j + e]);
+                        y[e] = wadd(muldiv_trunc(wsub(v[e], mean), ww[e], d_i64(ww[e]), isq, rd), bb[e]);
                 }
                 *(longlong2*)(x + j) = make_longlong2(y[0], y[1]);
                 *(longlong2*)(x + j + 2) = make_longlong2(y[2], y[3]);
@@ -536,7 +531,9 @@ int layernorm_rows_digits(int64_t* x, int64_t ld, int rows, int n, const int64_t
                           int64_t Kpad, int8_t* planes, int* overflow, cudaStream_t st) {
     if (rows <= 0) return 0;
     const int nq = (int)((Kpad + 127) / 128);
-    if (n % 4 != 0 || (ld & 1) != 0 || ((uintptr_t)x & 15) != 0 || nq > 8 || Kpad % 128 != 0 || Kpad < n) return -1;
+    if (n % 4 != 0 || (ld & 1) != 0 || ((uintptr_t)x & 15) != 0 || ((uintptr_t)w & 15) != 0 || ((uintptr_t)b & 15) != 0 ||
+        nq > 8 || Kpad % 128 != 0 || Kpad < n)
+        return -1;
     int k = 0;
     if (planes && Mpad > rows)  // padding rows of every plane: zero digits
         for (int i = 0; i < 5; i++, k++)
@@ -546,6 +543,7 @@ int layernorm_rows_digits(int64_t* x, int64_t ld, int rows, int n, const int64_t
         case 1: k_layernorm_q<1><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b, (int)Mpad, (int)Kpad, planes, overflow); break;
         case 2: k_layernorm_q<2><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b, (int)Mpad, (int)Kpad, planes, overflow); break;
         case 3: case 4: k_layernorm_q<4><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b, (int)Mpad, (int)Kpad, planes, overflow); break;
+        case 5: case 6: k_layernorm_q<6><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b, (int)Mpad, (int)Kpad, planes, overflow); break;
         default: k_layernorm_q<8><<<wb, 256, 0, st>>>(x, ld, rows, n, w, b, (int)Mpad, (int)Kpad, planes, overflow); break;
     }
     return k + 1;

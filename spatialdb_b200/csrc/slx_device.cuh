@@ -69,7 +69,8 @@ SLX_DEV int64_t composite(float f, int mode, double scale) {
 
 // Exact floor square root of a non-negative 128-bit value (ISqrt64 / ISqrt128,
 // IntegerLayerNorm.cs:99-149). Returned as the low 64 bits, like the reference's (long)x.
-SLX_DEV int64_t isqrt_u128(u128 v) {
+// Out of line: one call per row, and its Newton steps divide in 128 bits.
+static __device__ __noinline__ int64_t isqrt_u128(u128 v) {
     if (v == 0) return 0;
     u128 x = (u128)sqrt((double)v);
     if (x == 0) x = 1;
@@ -168,6 +169,10 @@ SLX_DEV double pow2d(int k) { return __hiloint2double((1023 + k) << 20, 0); }   
 // floor(|a w| rd) from one product and one rounded-down FMA is within one of floor(|a w| / d) (and
 // almost always equal), and the remainder |a w| - q d, exact in wrapping 64-bit arithmetic because
 // |r| < 2 d, fixes it; anything else takes the Int128 division.
+// The Int128 division (rare: outside the fast path's ranges), kept out of line so the callers' code
+// stays small.
+static __device__ __noinline__ int64_t muldiv_trunc_slow(int64_t a, int64_t w, int64_t d) { return lo64(((i128)a * w) / (i128)d); }
+
 SLX_DEV int64_t muldiv_trunc(int64_t a, int64_t w, double wd, int64_t d, double rd) {
     constexpr int64_t lim = 1LL << 51;
     if (a > -lim && a < lim && w > -lim && w < lim && d < (1LL << 60)) {
@@ -181,7 +186,7 @@ SLX_DEV int64_t muldiv_trunc(int64_t a, int64_t w, double wd, int64_t d, double 
             return (a < 0) != (w < 0) ? -q : q;
         }
     }
-    return lo64(((i128)a * w) / (i128)d);
+    return muldiv_trunc_slow(a, w, d);
 }
 
 // FixedExp's Taylor branch (IntegerTranscendentals.cs:13-47), fracBits = 30: e^r * 2^30 for r in
