@@ -63,7 +63,9 @@ struct ScoreParams {
     int* err;
 };
 
-template <int KB>
+// FAST: shift 30, a power-of-two divisor and no mask (the encoders' attention): constant shifts and
+// no per-score mask tests.
+template <int KB, bool FAST>
 __global__ void __launch_bounds__(S_THREADS, 1)
 k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, ScoreParams p) {
     constexpr uint32_t QBYTES = KB * LA * QPLANE;
@@ -192,13 +194,21 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
             int64_t o[CW];
 #pragma unroll
             for (int j = 0; j < CW; j++) {
-                const uint64_t L = (uint64_t)(int64_t)(int32_t)v[0][j] + ((uint64_t)(int64_t)(int32_t)v[1][j] << 8) +
-                                   ((uint64_t)(int64_t)(int32_t)v[2][j] << 16) + ((uint64_t)(int64_t)(int32_t)v[3][j] << 24);
-                const uint64_t H = (uint64_t)(int64_t)(int32_t)v[4][j] + ((uint64_t)(int64_t)(int32_t)v[5][j] << 8) +
-                                   ((uint64_t)(int64_t)(int32_t)v[6][j] << 16) + ((uint64_t)(int64_t)(int32_t)v[7][j] << 24) +
-                                   ((uint64_t)(int64_t)(int32_t)v[8][j] << 32);
-                int64_t x = (int64_t)((H << (32 - p.shift)) + (uint64_t)((int64_t)L >> p.shift));
+                // L and H as sums of int32 x constant products (wide multiply-adds), in wrapping 64 bits
+                const int64_t L = (int64_t)(int32_t)v[0][j] + (int64_t)(int32_t)v[1][j] * 256 +
+                                  (int64_t)(int32_t)v[2][j] * 65536 + (int64_t)(int32_t)v[3][j] * 16777216;
+                const uint64_t H = (uint64_t)((int64_t)(int32_t)v[4][j] + (int64_t)(int32_t)v[5][j] * 256 +
+                                              (int64_t)(int32_t)v[6][j] * 65536 + (int64_t)(int32_t)v[7][j] * 16777216) +
+                                   ((uint64_t)v[8][j] << 32);
                 const int n = n0 + j;
+                if (FAST) {
+                    int64_t x = (int64_t)((H << 2) + (uint64_t)(L >> 30));
+                    x = (int64_t)((uint64_t)x + ((uint64_t)(x >> 63) & (uint64_t)(p.div - 1))) >> p.dshift;  // truncating
+                    o[j] = x;
+                    if (n < p.T) mx = max(mx, x);
+                    continue;
+                }
+                int64_t x = (int64_t)((H << (32 - p.shift)) + (uint64_t)(L >> p.shift));
                 if ((p.mask_mode >= 1 && n > row) || (p.mask_mode == 2 && n < ws)) {
                     x = -(1LL << 29);  // maskValue (IntegerAttention.cs:222)
                 } else if (p.dshift >= 0) {  // C# long division truncates toward zero
@@ -252,8 +262,13 @@ void launch_scores_kb(const CUtensorMap& tq, const CUtensorMap& tk, ScoreParams 
     p.stages = score_stages<KB>();
     constexpr size_t smem = score_smem<KB>();
     static_assert(smem <= 227 * 1024, "score kernel shared memory");
-    slx::ensure_smem((const void*)k_scores<KB>, smem);
-    k_scores<KB><<<grid, S_THREADS, smem, st>>>(tq, tk, p);
+    if (p.shift == 30 && p.dshift >= 0 && p.mask_mode == 0) {
+        slx::ensure_smem((const void*)k_scores<KB, true>, smem);
+        k_scores<KB, true><<<grid, S_THREADS, smem, st>>>(tq, tk, p);
+    } else {
+        slx::ensure_smem((const void*)k_scores<KB, false>, smem);
+        k_scores<KB, false><<<grid, S_THREADS, smem, st>>>(tq, tk, p);
+    }
 }
 
 // ---------------------------------------------------------------------------------------------
