@@ -37,7 +37,10 @@ namespace slx {
 namespace {
 
 constexpr int G1_ND = 5;      // activation digits
-constexpr int G1_SR = 4;      // weight rows per stage
+// weight rows per stage: 8 for Q4_0 (more rows share each stage's reduction), 4 for Q8_0 (twice the
+// bytes per row; measured faster with the shorter stages)
+template <bool Q4>
+__host__ __device__ constexpr int g1_sr() { return Q4 ? 8 : 4; }
 constexpr int G1_CONS = 256;  // consumer threads
 constexpr int G1_THREADS = G1_CONS + 32;
 
@@ -77,25 +80,20 @@ __device__ __forceinline__ void g1_bulk(uint32_t dst, const void* src, uint32_t 
 
 // The block at byte offset o of a stage slot: scale bits and the 8 payload words in the element
 // order of the digit words (Q4_0: word 2j = low nibbles of payload bytes 4j..4j+3, word 2j+1 their high
-// nibbles; Q8_0: the payload bytes in order). o is even; an odd block starts 2 bytes into a word.
+// nibbles; Q8_0: the payload bytes in order). o is even, so the payload (byte o + 2) starts on a word
+// boundary or halfway into one: one funnel shift by 0 or 16 bits per word, the same code for every lane.
 template <bool Q4>
 __device__ __forceinline__ uint32_t g1_block(const uint8_t* slot, int o, uint32_t (&w)[8]) {
     constexpr int NW = Q4 ? 4 : 8;
-    const uint32_t* r = (const uint32_t*)(slot + (o & ~3));
+    const uint32_t* r = (const uint32_t*)(slot + ((o + 2) & ~3));
+    const uint32_t sh = (uint32_t)((o + 2) & 3) * 8u;
     uint32_t v[NW + 1];
 #pragma unroll
     for (int j = 0; j <= NW; j++) v[j] = r[j];
+    const uint32_t scale = *(const uint16_t*)(slot + o);
     uint32_t x[NW];
-    uint32_t scale;
-    if ((o & 3) == 0) {
-        scale = v[0] & 0xFFFFu;
 #pragma unroll
-        for (int j = 0; j < NW; j++) x[j] = __funnelshift_r(v[j], v[j + 1], 16);
-    } else {
-        scale = v[0] >> 16;
-#pragma unroll
-        for (int j = 0; j < NW; j++) x[j] = v[j + 1];
-    }
+    for (int j = 0; j < NW; j++) x[j] = __funnelshift_r(v[j], v[j + 1], sh);
     if (Q4) {
 #pragma unroll
         for (int j = 0; j < 4; j++) {
@@ -117,6 +115,17 @@ __device__ __forceinline__ int64_t g1_scale(uint32_t h, int sbits) {
     const int64_t m = ex ? (int64_t)(mant | 1024u) : (int64_t)mant;
     const int64_t D = m << (ex ? (int)ex - 25 + sbits : sbits - 24);
     return (h & 0x8000u) ? -D : D;
+}
+
+// S * D in Int128 for a finite scale, from D = +-m 2^e (m the 11-bit significand, 0 <= e <= 44):
+// the 64-bit product S m (|S m| < 2^63 for the block sums here) shifted left by e.
+__device__ __forceinline__ void g1_mul_scale(int64_t S, uint32_t h, int sbits, uint64_t& lo, int64_t& hi) {
+    const uint32_t ex = (h >> 10) & 31u, mant = h & 1023u;
+    const int64_t m = ex ? (int64_t)(mant | 1024u) : (int64_t)mant;
+    const int e = ex ? (int)ex - 25 + sbits : sbits - 24;
+    const int64_t p = (h & 0x8000u) ? -(S * m) : S * m;
+    lo = (uint64_t)p << e;
+    hi = (p >> 1) >> (63 - e);  // the bits shifted out of the low word, sign-extended
 }
 
 // One block of one row by Int128 multiply-adds of the composites w = D * q (long.MinValue for a
@@ -165,6 +174,7 @@ __device__ __forceinline__ void g1_fly(uint64_t (&lo)[N], int64_t (&hi)[N], int 
 template <bool Q4>
 __global__ void __launch_bounds__(G1_THREADS, 2) k_gemv1(G1Params p) {
     constexpr int BB = g1_bb<Q4>();
+    constexpr int G1_SR = g1_sr<Q4>();
     extern __shared__ __align__(128) uint8_t g1_smem[];
     const int row_bytes = p.NB * BB;
     const int slot_bytes = G1_SR * row_bytes;
@@ -288,7 +298,8 @@ __global__ void __launch_bounds__(G1_THREADS, 2) k_gemv1(G1Params p) {
                 // rows past N (a partial last stage) compute on stale bytes of the slot; never written out
                 const int o = r * row_bytes + b * BB;
                 uint32_t wq[8];
-                const int64_t D = g1_scale(g1_block<Q4>(sl, o, wq), p.sbits);
+                const uint32_t hs = g1_block<Q4>(sl, o, wq);
+                const bool finite = ((hs >> 10) & 31u) != 31u;
                 if (!wide) {
                     int P[G1_ND];
 #pragma unroll
@@ -301,11 +312,14 @@ __global__ void __launch_bounds__(G1_THREADS, 2) k_gemv1(G1Params p) {
                     const int t01 = P[1] * 256 + P[0], t23 = P[3] * 256 + P[2];  // |P_i| < 2^20
                     int64_t S = (int64_t)t01 + (int64_t)t23 * 65536 + ((int64_t)P[4] << 32);
                     if (Q4) S -= 8 * asum;
-                    if (D == INT64_MIN) S = asum;  // every composite of the block is long.MinValue
-                    lo[r] = (uint64_t)S * (uint64_t)D;
-                    hi[r] = __mul64hi(S, D);
+                    if (finite) {
+                        g1_mul_scale(S, hs, p.sbits, lo[r], hi[r]);
+                    } else {  // every composite of the block is long.MinValue: sum_k a_k * long.MinValue
+                        lo[r] = (uint64_t)asum << 63;
+                        hi[r] = __mul64hi(asum, INT64_MIN);
+                    }
                 } else {
-                    g1_block_wide<Q4>(sl + o, D, p.A + (int64_t)b * 32, lo[r], hi[r]);
+                    g1_block_wide<Q4>(sl + o, g1_scale(hs, p.sbits), p.A + (int64_t)b * 32, lo[r], hi[r]);
                 }
             }
         }
@@ -348,6 +362,7 @@ __global__ void __launch_bounds__(G1_THREADS, 2) k_gemv1(G1Params p) {
 template <bool Q4>
 bool launch_gemv1(const WDesc& w, const int64_t* a, int64_t* c, int shift, int* err, cudaStream_t st) {
     constexpr int BB = g1_bb<Q4>();
+    constexpr int G1_SR = g1_sr<Q4>();
     const int NB = (int)(w.K / 32);
     if (NB % 8 != 0 || NB > G1_CONS || w.N <= 0 || ((uintptr_t)w.data & 15) != 0 || ((uintptr_t)a & 15) != 0)
         return false;
