@@ -26,6 +26,8 @@
 // the exact kernel redoes the call.
 #include <cuda.h>
 
+#include <algorithm>
+
 #include "slx_attr.h"
 #include "slx_device.cuh"
 #include "slx_gemm.h"
@@ -302,6 +304,7 @@ SLX_DEV void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
 }
 SLX_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 SLX_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+SLX_DEV void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // FixedSoftmax of score rows in place, one warp per row (row stride SR int64): pass one writes
 // e = FixedExp(score - max) as uint32 over the first half of the row's storage (each 256-key chunk is
@@ -363,86 +366,171 @@ __global__ __launch_bounds__(32 * SM_ROWS) void k_softmax(int64_t* S, int SR, co
 constexpr int PV_TH = 128;  // four warps
 constexpr double PV_BASE = 6755399441055744.0;  // 1.5 * 2^52
 
+constexpr int pv_keys_per_chunk(int hd) { return (hd == 256 || hd == 16) ? 8 : 16; }
+constexpr int PV_MAX_SPLIT = 1024;  // tail tiles that may be split (counters in the workspace header)
+
+// Work of one P.V launch: tiles of PR query rows of one head, numbered u = (b * nh + h) * ntr + rt.
+// The first `whole` tiles run one block each over all keys; when the tiles do not fill the last
+// wave of resident blocks (two per SM), the remaining tiles are split into S key ranges each, so
+// the tail is S times shorter. A split part writes its exact int64 partial sums to the workspace
+// and the last part of a tile to finish (an atomic count per tile) adds them up and writes the
+// rows: partial sums of floored terms are integers, so the split changes no bit of the result.
+struct PvPlan {
+    int ntr = 0, tiles = 0, whole = 0, rem = 0, S = 1;
+    int blocks() const { return whole + rem * S; }
+    size_t partial_bytes() const { return S > 1 ? (size_t)rem * S * 8192 * 8 : 0; }  // PR * HD = 8192
+};
+
+PvPlan pv_plan(int hd, int B, int T, int nh) {
+    PvPlan pl;
+    const int pr = 8192 / hd, vt = pv_keys_per_chunk(hd);
+    const int slots = 2 * device_sm_count();
+    const int nch = (T + vt - 1) / vt;
+    pl.ntr = (T + pr - 1) / pr;
+    pl.tiles = pl.ntr * nh * B;
+    pl.rem = pl.tiles % slots;
+    pl.whole = pl.tiles - pl.rem;
+    if (pl.rem == 0 || pl.rem > PV_MAX_SPLIT || nch < 2) {
+        pl.whole = pl.tiles;
+        pl.rem = 0;
+        return pl;
+    }
+    // tail length in whole-tile times: ceil(rem * S / slots) / S, plus ~3 % for the partials
+    double best = 1.0;
+    const int smax = std::min(std::min(nch, 16), std::max(1, 3 * slots / pl.rem));
+    for (int sp = 2; sp <= smax; sp++) {
+        const double tail = (double)((pl.rem * sp + slots - 1) / slots) / sp * 1.03;
+        if (tail < 0.95 * best) best = tail, pl.S = sp;
+    }
+    if (pl.S == 1) pl.whole = pl.tiles, pl.rem = 0;
+    return pl;
+}
+
 // Register tile of a thread: 8 query rows x 8 columns (64 fp64 accumulators). Per key a thread
 // loads its 8 columns of v and its 8 rows of p as four 16-byte shared loads each and issues 64
 // DFMAs. Columns of a thread: 2cg, 2cg+1 + 2 CG j (j < 4), so the eight lanes of a quarter warp
 // read 128 contiguous bytes of a v row; rows: 8 consecutive, contiguous in the key-major p tile.
+//
+// Chunks of VT keys move through two raw buffers (int64 v rows and uint32 p granules, filled by
+// cp.async) and two converted buffers (v * 2^-30 and p as doubles, p transposed key-major). While
+// a block multiplies chunk c out of one converted buffer, its threads convert chunk c + 1 into the
+// other, a few values after each key's DFMAs, so the conversions issue beside the fp64 pipe's work
+// instead of in a phase of their own; chunk c + 2 is in flight meanwhile.
 template <int HD>
 struct Pv {
     static constexpr int CG = HD / 8;                    // column groups (lanes per row group)
     static constexpr int RGW = 32 / CG;                  // row groups per warp
     static constexpr int PR = (PV_TH / 32) * RGW * 8;    // query rows per block: 8192 / HD
-    static constexpr int VT = HD == 256 ? 16 : (HD / 2 < 32 ? HD / 2 : 32);  // keys per chunk
-    static constexpr int V_BYTES = VT * HD * 8;          // int64 v rows, converted in place to v * 2^-30
-    static constexpr int PU_BYTES = PR * VT * 4;         // uint32 p as 16-byte granules [VT/4][PR]
-    static constexpr int BUF = V_BYTES + PU_BYTES;
-    static constexpr size_t SMEM = 2 * (size_t)BUF + (size_t)PR * VT * 8;  // + fp64 p, key-major [VT][PR]
-    static_assert(CG >= 2 && CG <= 32 && BUF % 16 == 0 && VT % 4 == 0, "P.V tiling");
+    static constexpr int VT = pv_keys_per_chunk(HD);     // keys per chunk
+    static constexpr int RV = VT * HD * 8;               // raw v: int64 [VT][HD]
+    static constexpr int RP = PR * VT * 4;               // raw p: 16-byte granules [VT/4][PR]
+    static constexpr int RAW = RV + RP;
+    static constexpr int CV = VT * HD * 8;               // converted v: double [VT][HD]
+    static constexpr int CONV = CV + VT * PR * 8;        // + converted p: double [VT][PR]
+    static constexpr size_t SMEM = 2 * (size_t)RAW + 2 * (size_t)CONV;
+    static constexpr int NV = VT * HD / PV_TH;           // v values a thread converts per chunk
+    static constexpr int NPG = PR * VT / 4;              // p granules per chunk
+    static constexpr int NP = (NPG + PV_TH - 1) / PV_TH; // p granules a thread converts per chunk
+    static constexpr int NW = NV + NP;                   // conversion items a thread has per chunk
+    static_assert(CG >= 2 && CG <= 32 && RAW % 16 == 0 && CONV % 16 == 0 && VT % 4 == 0, "P.V tiling");
+    static_assert(VT * HD % PV_TH == 0, "v conversion");
 };
 
-// PR query rows of one head over chunks of VT keys: the chunk's v rows (int64, straight from the
-// QKV buffer) and p rows (uint32) arrive by cp.async into one of two buffers while the other chunk
-// computes; v becomes v * 2^-30 in place and p is widened and transposed into Pd once per chunk.
+// PR query rows of one head, VT keys at a time (see Pv).
+// flag: bit 0 set by the earlier stages (the block returns at once), bit 1 set here when a value
+// of v is out of range; either makes the exact kernel redo the call.
 template <int HD>
 __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const int64_t* __restrict__ V,
                                                   int64_t ldv, int64_t* __restrict__ O, int64_t ldo, int T, int nh,
-                                                  int nkv, int* flag) {
+                                                  int nkv, PvPlan pl, int* flag, int* cnt, int64_t* part) {
     using C = Pv<HD>;
     constexpr int VT = C::VT, CG = C::CG, RGW = C::RGW, PR = C::PR;
-    if (*flag) return;
+    if (*flag & 1) return;
     extern __shared__ __align__(16) uint8_t sm[];
-    double* Pd = (double*)(sm + 2 * C::BUF);  // [VT][PR]
-    const int h = blockIdx.y, b = blockIdx.z, t0 = blockIdx.x * PR;
+    __shared__ int s_last;
+    uint8_t* raw_base = sm;                   // raw chunk buffers: [2][RAW]
+    uint8_t* conv_base = sm + 2 * C::RAW;     // converted chunk buffers: [2][CONV]
+    const int nchunks = (T + VT - 1) / VT;
+    const int item = blockIdx.x;
+    int u = item, pid = 0, c_lo = 0, c_hi = nchunks;
+    if (item >= pl.whole) {  // part pid of split tile (item - whole) / S: chunks [c_lo, c_hi)
+        const int j = (item - pl.whole) / pl.S;
+        pid = (item - pl.whole) % pl.S;
+        u = pl.whole + j;
+        c_lo = pid * nchunks / pl.S;
+        c_hi = (pid + 1) * nchunks / pl.S;
+    }
+    const int h = (u / pl.ntr) % nh, b = u / (pl.ntr * nh), t0 = (u % pl.ntr) * PR;
     const int z = b * nh + h, kvh = h / (nh / nkv);
     const int T4 = (T + 3) & ~3;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cg = lane % CG, r0 = 8 * (warp * RGW + lane / CG);  // first of the thread's 8 rows
     const int64_t* v0 = V + (int64_t)b * T * ldv + (int64_t)kvh * HD;  // key s: v0 + s * ldv
     const uint32_t sbase = tc::smem_u32(sm);
-    auto issue = [&](int k0, int buf) {
-        const uint32_t dst = sbase + buf * C::BUF;
+    auto issue = [&](int c, int buf) {
+        const int k0 = c * VT;
+        const uint32_t dst = sbase + buf * C::RAW;
         const int keys = min(VT, T - k0);
-        for (int g = threadIdx.x; g < C::V_BYTES / 16; g += PV_TH) {  // v: HD/2 granules a key
+        for (int g = threadIdx.x; g < C::RV / 16; g += PV_TH) {  // v: HD/2 granules a key
             const int s = g / (HD / 2), j = g % (HD / 2);
             cp_async16(dst + g * 16, s < keys ? v0 + (int64_t)(k0 + s) * ldv + 2 * j : v0, s < keys ? 16u : 0u);
         }
-        for (int g = threadIdx.x; g < PR * (VT / 4); g += PV_TH) {  // p: granule (row r, keys 4q..4q+3) at [q][r]
+        for (int g = threadIdx.x; g < C::NPG; g += PV_TH) {  // p: granule (row r, keys 4q..4q+3) at [q][r]
             const int r = g % PR, q = g / PR, s = k0 + 4 * q;
             const int t = t0 + r;
             const bool ok = t < T && s < T4;
             const uint32_t* src = ok ? (const uint32_t*)(S + ((int64_t)z * T + t) * SR) + s : (const uint32_t*)S;
-            cp_async16(dst + C::V_BYTES + g * 16, src, ok ? 16u : 0u);
+            cp_async16(dst + C::RV + g * 16, src, ok ? 16u : 0u);
         }
-        cp_async_commit();
+    };
+    bool wide = false;
+    // item w of a thread's share of converting raw buffer rb into converted buffer cb
+    auto convert = [&](int w, int rb, int cb, bool live) {
+        const uint8_t* rw = raw_base + rb * C::RAW;
+        uint8_t* cv = conv_base + cb * C::CONV;
+        if (w < C::NV) {
+            const int i = threadIdx.x + w * PV_TH;  // exact for |v| < 2^53
+            const int64_t x = ((const int64_t*)rw)[i];
+            wide |= live && ((x >> 30) < -(1LL << 20) || (x >> 30) >= (1LL << 20));
+            ((double*)cv)[i] = (double)x * 0x1p-30;
+        } else {
+            const int g = threadIdx.x + (w - C::NV) * PV_TH;
+            if (C::NPG % PV_TH == 0 || g < C::NPG) {
+                const uint4 u = ((const uint4*)(rw + C::RV))[g];
+                const int r = g % PR, q = g / PR;
+                double* Pd = (double*)(cv + C::CV);
+                Pd[(4 * q + 0) * PR + r] = (double)u.x;
+                Pd[(4 * q + 1) * PR + r] = (double)u.y;
+                Pd[(4 * q + 2) * PR + r] = (double)u.z;
+                Pd[(4 * q + 3) * PR + r] = (double)u.w;
+            }
+        }
     };
     double acc[8][8];
 #pragma unroll
     for (int r = 0; r < 8; r++)
 #pragma unroll
         for (int c = 0; c < 8; c++) acc[r][c] = PV_BASE;
-    bool wide = false;
-    issue(0, 0);
-    for (int k0 = 0, buf = 0; k0 < T; k0 += VT, buf ^= 1) {
+    issue(c_lo, 0);
+    cp_async_commit();
+    if (c_lo + 1 < c_hi) issue(c_lo + 1, 1);
+    cp_async_commit();
+    cp_async_wait_1();
+    __syncthreads();  // the first chunk's raw rows are in for every thread
+#pragma unroll
+    for (int w = 0; w < C::NW; w++) convert(w, 0, 0, true);
+    for (int c = c_lo; c < c_hi; c++) {
+        const int cur = (c - c_lo) & 1;
         cp_async_wait_all();
-        __syncthreads();  // chunk k0 is in for every thread; the other buffer and Pd are free
-        if (k0 + VT < T) issue(k0 + VT, buf ^ 1);
-        double* Vs = (double*)(sm + buf * C::BUF);
-        const uint4* Pu = (const uint4*)(sm + buf * C::BUF + C::V_BYTES);
-        for (int i = threadIdx.x; i < VT * HD; i += PV_TH) {  // exact for |v| < 2^53
-            const int64_t x = ((const int64_t*)Vs)[i];
-            wide |= (x >> 30) < -(1LL << 20) || (x >> 30) >= (1LL << 20);
-            Vs[i] = (double)x * 0x1p-30;
-        }
-        for (int g = threadIdx.x; g < PR * (VT / 4); g += PV_TH) {
-            const uint4 u = Pu[g];
-            const int r = g % PR, q = g / PR;
-            Pd[(4 * q + 0) * PR + r] = (double)u.x;
-            Pd[(4 * q + 1) * PR + r] = (double)u.y;
-            Pd[(4 * q + 2) * PR + r] = (double)u.z;
-            Pd[(4 * q + 3) * PR + r] = (double)u.w;
-        }
+        // chunk c + 1's raw rows and chunk c's converted values are in for every thread; raw
+        // buffer cur (chunk c, converted) and converted buffer cur ^ 1 (chunk c - 1) are free
         __syncthreads();
-#pragma unroll 2
+        if (c + 2 < c_hi) issue(c + 2, cur);
+        cp_async_commit();
+        const double* Vs = (const double*)(conv_base + cur * C::CONV);
+        const double* Pd = (const double*)(conv_base + cur * C::CONV + C::CV);
+        const bool live = c + 1 < c_hi;  // raw buffer cur ^ 1 holds a real chunk
+#pragma unroll
         for (int s = 0; s < VT; s++) {  // one key at a time: every accumulator once per key
             double2 v[4], p[4];
 #pragma unroll
@@ -458,11 +546,44 @@ __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const
                     acc[2 * i + 1][2 * j] = __fma_rd(p[i].y, v[j].x, acc[2 * i + 1][2 * j]);
                     acc[2 * i + 1][2 * j + 1] = __fma_rd(p[i].y, v[j].y, acc[2 * i + 1][2 * j + 1]);
                 }
+#pragma unroll
+            for (int w = s * C::NW / VT; w < (s + 1) * C::NW / VT; w++) convert(w, cur ^ 1, cur ^ 1, live);
         }
     }
-    if (__syncthreads_or(wide)) {
-        if (threadIdx.x == 0) atomicOr(flag, 1);
-        return;
+    // a wide v leaves the rows to the exact kernel; the split parts still count in below, so the
+    // per-tile counts stay whole
+    if (__syncthreads_or(wide) && threadIdx.x == 0) atomicOr(flag, 2);
+    int64_t sum[8][8];
+#pragma unroll
+    for (int r = 0; r < 8; r++)
+#pragma unroll
+        for (int c = 0; c < 8; c++) sum[r][c] = (int64_t)(acc[r][c] - PV_BASE);
+    if (item >= pl.whole) {
+        const int j = (item - pl.whole) / pl.S;
+        int64_t* mine = part + (int64_t)(item - pl.whole) * PR * HD;  // [PR][HD]
+#pragma unroll
+        for (int r = 0; r < 8; r++)
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                *(longlong2*)(mine + (r0 + r) * HD + 2 * cg + 2 * CG * q) = make_longlong2(sum[r][2 * q], sum[r][2 * q + 1]);
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = atomicAdd(cnt + j, 1) == pl.S - 1;
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        for (int o = 0; o < pl.S; o++) {
+            if (o == pid) continue;
+            const int64_t* other = part + ((int64_t)j * pl.S + o) * PR * HD;
+#pragma unroll
+            for (int r = 0; r < 8; r++)
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const longlong2 x = __ldcg((const longlong2*)(other + (r0 + r) * HD + 2 * cg + 2 * CG * q));
+                    sum[r][2 * q] += x.x;
+                    sum[r][2 * q + 1] += x.y;
+                }
+        }
     }
 #pragma unroll
     for (int r = 0; r < 8; r++) {
@@ -470,9 +591,8 @@ __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const
         if (t >= T) continue;
         int64_t* orow = O + ((int64_t)b * T + t) * ldo + (int64_t)h * HD;
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-            *(longlong2*)(orow + 2 * cg + 2 * CG * j) =
-                make_longlong2((int64_t)(acc[r][2 * j] - PV_BASE), (int64_t)(acc[r][2 * j + 1] - PV_BASE));
+        for (int q = 0; q < 4; q++)
+            *(longlong2*)(orow + 2 * cg + 2 * CG * q) = make_longlong2(sum[r][2 * q], sum[r][2 * q + 1]);
     }
 }
 
@@ -480,21 +600,25 @@ int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 template <int HD>
 void launch_pv(int B, int T, int nh, int nkv, const int64_t* scores, int sr, const int64_t* v, int64_t ldv,
-               int64_t* out, int64_t ldo, int* flag, cudaStream_t st) {
+               int64_t* out, int64_t ldo, const PvPlan& pl, int* flag, int* cnt, int64_t* part, cudaStream_t st) {
     using C = Pv<HD>;
     static_assert(C::SMEM <= 112 * 1024, "two P.V blocks per SM");
+    static_assert(C::VT == pv_keys_per_chunk(HD) && C::PR * HD == 8192, "plan and kernel agree");
     if (((uintptr_t)v & 15) != 0 || (ldv & 1) != 0 || ((uintptr_t)out & 15) != 0 || (ldo & 1) != 0) {
         // rows the 16-byte copies and stores cannot address: the exact kernel
         cudaMemsetAsync(flag, 1, sizeof(int), st);
         return;
     }
     slx::ensure_smem((const void*)k_pv<HD>, C::SMEM);
-    const dim3 grid((unsigned)((T + C::PR - 1) / C::PR), (unsigned)nh, (unsigned)B);
-    k_pv<HD><<<grid, PV_TH, C::SMEM, st>>>(scores, sr, v, ldv, out, ldo, T, nh, nkv, flag);
+    k_pv<HD><<<(unsigned)pl.blocks(), PV_TH, C::SMEM, st>>>(scores, sr, v, ldv, out, ldo, T, nh, nkv, pl, flag, cnt,
+                                                            part);
 }
 
+// Workspace: [0, 256) the call's flag; [256, HDR) the split tiles' counters; then the q and k
+// digit planes, the scores, the row maxima and the split parts' partial sums.
+constexpr int64_t WS_HDR = 256 + 4 * PV_MAX_SPLIT;
 struct Layout {
-    int64_t kpad, tq, tk, sr, qbytes, kbytes, sbytes, mbytes;
+    int64_t kpad, tq, tk, sr, qbytes, kbytes, sbytes, mbytes, pbytes;
 };
 
 Layout layout(int B, int T, int nh, int nkv, int hd) {
@@ -507,13 +631,14 @@ Layout layout(int B, int T, int nh, int nkv, int hd) {
     l.sr = round_up(T, 2);
     l.sbytes = round_up((int64_t)B * nh * T * l.sr * 8, 256);
     l.mbytes = round_up((int64_t)B * nh * T * 8, 256);
+    l.pbytes = (int64_t)pv_plan(hd, B, T, nh).partial_bytes();
     return l;
 }
 }  // namespace
 
 size_t attention_tc_workspace(int B, int T, int nh, int nkv, int hd) {
     const Layout l = layout(B, T, nh, nkv, hd);
-    return (size_t)(256 + l.qbytes + l.kbytes + l.sbytes + l.mbytes);
+    return (size_t)(WS_HDR + l.qbytes + l.kbytes + l.sbytes + l.mbytes + l.pbytes);
 }
 
 bool attention_tc_supported(int T, int nh, int nkv, int hd) {
@@ -529,15 +654,18 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     const Layout l = layout(B, T, nh, nkv, hd);
     uint8_t* base = (uint8_t*)ws;
     int* flag = (int*)base;
-    int8_t* qp = (int8_t*)(base + 256);
+    int* cnt = (int*)(base + 256);
+    int8_t* qp = (int8_t*)(base + WS_HDR);
     int8_t* kp = qp + l.qbytes;
     int64_t* scores = (int64_t*)(kp + l.kbytes);
     int64_t* rmax = (int64_t*)((uint8_t*)scores + l.sbytes);
+    int64_t* part = (int64_t*)((uint8_t*)rmax + l.mbytes);
+    const PvPlan pl = pv_plan(hd, B, T, nh);
     alignas(64) unsigned char mq[128], mk[128];
     if (!encode_planes(mq, qp, l.kpad, l.tq, LA, QM, (int64_t)B * nh) ||
         !encode_planes(mk, kp, l.kpad, l.tk, LA, NK, (int64_t)B * nkv))
         return -1;
-    cudaMemsetAsync(flag, 0, sizeof(int), st);
+    cudaMemsetAsync(flag, 0, 256 + 4 * (size_t)pl.rem, st);  // the flag and the split tiles' counters
     if (rope_cs) {  // ApplyRoPE on q and k in place, fused with their digit split
         rope_split_heads(const_cast<int64_t*>(q), ldq, B, T, nh, hd, l.tq, l.kpad, rope_cs, rope_sn, qp, flag, st);
         rope_split_heads(const_cast<int64_t*>(k), ldk, B, T, nkv, hd, l.tk, l.kpad, rope_cs, rope_sn, kp, flag, st);
@@ -564,11 +692,11 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
                                                                                   flag, flag);
     const int sr = (int)l.sr;
     switch (hd) {
-        case 16: launch_pv<16>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, flag, st); break;
-        case 32: launch_pv<32>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, flag, st); break;
-        case 64: launch_pv<64>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, flag, st); break;
-        case 128: launch_pv<128>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, flag, st); break;
-        default: launch_pv<256>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, flag, st); break;
+        case 16: launch_pv<16>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, pl, flag, cnt, part, st); break;
+        case 32: launch_pv<32>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, pl, flag, cnt, part, st); break;
+        case 64: launch_pv<64>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, pl, flag, cnt, part, st); break;
+        case 128: launch_pv<128>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, pl, flag, cnt, part, st); break;
+        default: launch_pv<256>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, pl, flag, cnt, part, st); break;
     }
     // the exact kernel redoes the whole call when anything fell outside the fast ranges
     attention(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, score_shift, sqrt_hd, mode, window, st, flag);
