@@ -45,7 +45,12 @@ using namespace tc;
 constexpr int QM = 128;                 // query rows per CTA (TMEM lanes)
 constexpr int NK = 16;                  // keys per tile
 constexpr int NSH = 2 * LA - 1;         // shift blocks of 16 columns
-constexpr int NBUF = 3;                 // TMEM accumulators
+// TMEM accumulators per CTA: with a query tile of one 128-byte K block (hd <= 128) two CTAs share
+// an SM, each with one accumulator in 256 columns, and one CTA's epilogue overlaps the other's MMAs
+// (measured faster than one CTA with three accumulators); wider heads keep one CTA with three.
+template <int KB> __host__ __device__ constexpr int nbuf() { return KB == 1 ? 1 : 3; }
+template <int KB> __host__ __device__ constexpr int score_ctas() { return KB == 1 ? 2 : 1; }
+constexpr int NBUF_MAX = 3;
 constexpr int BUF_COLS = NSH * NK;      // 144
 constexpr int EPI = 16;                 // epilogue warps (four per TMEM lane quarter)
 constexpr int CW = NK / (EPI / 4);      // key columns of a tile per epilogue warp
@@ -53,7 +58,7 @@ constexpr int S_THREADS = 32 * (2 + EPI);
 constexpr uint32_t QPLANE = QM * BK;    // one query digit plane, one 128-byte K block
 constexpr uint32_t KPLANE = NK * BK;
 constexpr uint32_t IDESC_S = idesc_i8(LA * NK);
-static_assert(NBUF * BUF_COLS <= 512, "TMEM holds 512 columns");
+static_assert(NBUF_MAX * BUF_COLS <= 512 && BUF_COLS <= 256, "TMEM holds 512 columns");
 
 struct ScoreParams {
     int T, SR, nh, zgroup, nkv, ksteps, shift, mask_mode, window, ntiles, stages;  // SR: score row stride (even)
@@ -68,10 +73,12 @@ struct ScoreParams {
 // FAST: shift 30, a power-of-two divisor and no mask (the encoders' attention): constant shifts and
 // no per-score mask tests.
 template <int KB, bool FAST>
-__global__ void __launch_bounds__(S_THREADS, 1)
+__global__ void __launch_bounds__(S_THREADS, score_ctas<KB>())
 k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, ScoreParams p) {
     constexpr uint32_t QBYTES = KB * LA * QPLANE;
     constexpr uint32_t KSTAGE = KB * LA * KPLANE;
+    constexpr int NBUF = nbuf<KB>();
+    constexpr uint32_t TCOLS = score_ctas<KB>() == 2 ? 256 : 512;
     if (*p.skip) return;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -98,7 +105,7 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "n"(TCOLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     fence_before();
@@ -246,17 +253,17 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
     if (s_fail && threadIdx.x == 0 && p.err) atomicOr(p.err, KERR_TIMEOUT);
     if (warp == 1) {
         fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(TCOLS));
     }
 }
 
 template <int KB>
-constexpr int score_stages() { return KB == 1 ? 6 : 2; }
+constexpr int score_stages() { return 2; }
 
 template <int KB>
 constexpr size_t score_smem() {
     return (size_t)KB * LA * QPLANE + (size_t)score_stages<KB>() * KB * LA * KPLANE + 1024 +
-           (2 * score_stages<KB>() + 1 + 2 * NBUF + 1) * 8;
+           (2 * score_stages<KB>() + 1 + 2 * nbuf<KB>() + 1) * 8;
 }
 
 template <int KB>
@@ -264,6 +271,8 @@ void launch_scores_kb(const CUtensorMap& tq, const CUtensorMap& tk, ScoreParams 
     p.stages = score_stages<KB>();
     constexpr size_t smem = score_smem<KB>();
     static_assert(smem <= 227 * 1024, "score kernel shared memory");
+    static_assert(score_ctas<KB>() == 1 || smem + sizeof(int64_t) * (EPI / 4) * QM + 64 <= 113 * 1024,
+                  "two score CTAs per SM");
     if (p.shift == 30 && p.dshift >= 0 && p.mask_mode == 0) {
         slx::ensure_smem((const void*)k_scores<KB, true>, smem);
         k_scores<KB, true><<<grid, S_THREADS, smem, st>>>(tq, tk, p);
