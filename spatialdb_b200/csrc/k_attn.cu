@@ -386,6 +386,11 @@ constexpr int PV_MAX_SPLIT = 1024;  // tail tiles that may be split (counters in
 // rows: partial sums of floored terms are integers, so the split changes no bit of the result.
 struct PvPlan {
     int ntr = 0, tiles = 0, whole = 0, rem = 0, S = 1;
+    // optional: the next projection's activation digit planes ([5][mpad][kpad] int8, row b * T + t,
+    // column h * HD + d), written beside the int64 rows; a value needing a sixth digit sets bit 2 of
+    // the flag
+    int8_t* planes = nullptr;
+    int64_t mpad = 0, kpad = 0;
     int blocks() const { return whole + rem * S; }
     size_t partial_bytes() const { return S > 1 ? (size_t)rem * S * 8192 * 8 : 0; }  // PR * HD = 8192
 };
@@ -594,6 +599,7 @@ __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const
                 }
         }
     }
+    bool over = false;
 #pragma unroll
     for (int r = 0; r < 8; r++) {
         const int t = t0 + r0 + r;
@@ -602,7 +608,22 @@ __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const
 #pragma unroll
         for (int q = 0; q < 4; q++)
             *(longlong2*)(orow + 2 * cg + 2 * CG * q) = make_longlong2(sum[r][2 * q], sum[r][2 * q + 1]);
+        if (pl.planes) {  // digits of column pairs q and q + 1: the low and high halves of each word
+            int8_t* prow = pl.planes + ((int64_t)b * T + t) * pl.kpad + (int64_t)h * HD + 2 * cg;
+#pragma unroll
+            for (int q = 0; q < 4; q += 2) {
+                uint32_t wd[5];
+                digit_words4(sum[r][2 * q], sum[r][2 * q + 1], sum[r][2 * q + 2], sum[r][2 * q + 3], wd, over);
+#pragma unroll
+                for (int i = 0; i < 5; i++) {
+                    int8_t* d = prow + (int64_t)i * pl.mpad * pl.kpad + 2 * CG * q;
+                    *(uint16_t*)d = (uint16_t)wd[i];
+                    *(uint16_t*)(d + 2 * CG) = (uint16_t)(wd[i] >> 16);
+                }
+            }
+        }
     }
+    if (over) atomicOr(flag, 4);
 }
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
@@ -658,7 +679,7 @@ bool attention_tc_supported(int T, int nh, int nkv, int hd) {
 int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
                  int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int score_shift, int64_t sqrt_hd,
                  int mode, int window, void* ws, int* err, cudaStream_t st, const int64_t* rope_cs,
-                 const int64_t* rope_sn) {
+                 const int64_t* rope_sn, int8_t* planes, int64_t mpad, int64_t kpad) {
     if (score_shift < 0 || score_shift > 32 || sqrt_hd < 1) return -1;
     const Layout l = layout(B, T, nh, nkv, hd);
     uint8_t* base = (uint8_t*)ws;
@@ -669,7 +690,12 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     int64_t* scores = (int64_t*)(kp + l.kbytes);
     int64_t* rmax = (int64_t*)((uint8_t*)scores + l.sbytes);
     int64_t* part = (int64_t*)((uint8_t*)rmax + l.mbytes);
-    const PvPlan pl = pv_plan(hd, B, T, nh);
+    PvPlan pl = pv_plan(hd, B, T, nh);
+    if (planes && kpad == (int64_t)nh * hd && mpad >= (int64_t)B * T) {
+        pl.planes = planes;
+        pl.mpad = mpad;
+        pl.kpad = kpad;
+    }
     alignas(64) unsigned char mq[128], mk[128];
     if (!encode_planes(mq, qp, l.kpad, l.tq, LA, QM, (int64_t)B * nh) ||
         !encode_planes(mk, kp, l.kpad, l.tk, LA, NK, (int64_t)B * nkv))

@@ -70,13 +70,18 @@ int attention(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, cons
 // given, ApplyRoPE is applied to q and k in place by the same pass), tcgen05 score GEMM,
 // CUDA-core softmax and per-term PV, and the exact kernel gated behind them for out-of-range
 // inputs. ws must hold attention_tc_workspace() bytes. Returns the kernels queued, -1 if the
-// tensor maps could not be encoded (nothing queued).
+// tensor maps could not be encoded (nothing queued). With planes (and kpad == nh * hd, mpad >= B * T)
+// the P.V also writes the output rows' five activation digit planes [5][mpad][kpad] for the next
+// projection; they are valid only while the int word at ws (attention_tc_flag) stays zero, which
+// the caller passes to the projection as its fallback flag. Rows B*T..mpad are the caller's.
 size_t attention_tc_workspace(int B, int T, int nh, int nkv, int hd);
 bool attention_tc_supported(int T, int nh, int nkv, int hd);
 int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
                  int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int score_shift, int64_t sqrt_hd,
                  int mode, int window, void* ws, int* err, cudaStream_t st, const int64_t* rope_cs = nullptr,
-                 const int64_t* rope_sn = nullptr);
+                 const int64_t* rope_sn = nullptr, int8_t* planes = nullptr, int64_t mpad = 0, int64_t kpad = 0);
+// The call's fallback flag inside ws: nonzero when the exact kernel produced the output.
+inline const int* attention_tc_flag(const void* ws) { return (const int*)ws; }
 
 // up[i] = (FixedSiLU(gate[i]) * up[i]) >> 30 over M rows of F (IntegerFFN)
 int silu_gate(const int64_t* gate, int64_t ldg, int64_t* up, int64_t ldu, int M, int F, cudaStream_t st);

@@ -497,16 +497,25 @@ int prepare_gemms(slx_ctx* ctx, slx_model* m) {
 // Attention for one layer: tensor-core scores when the shape allows (exact kernel gated behind).
 // q and k are rotated in place first (ApplyRoPE with the cos / sin tables): by the tensor-core path's
 // digit split itself, or by k_rope before the exact kernel.
+// With planes ([5][mpad][kpad], kpad == nh * hd) the tensor-core path also writes the output rows'
+// activation digit planes for the next projection and sets *planes_flag to the word that must stay
+// zero for them to be used; otherwise *planes_flag is left null.
 int attend(slx_model* m, int64_t* q, int64_t ldq, int64_t* k, int64_t ldk, const int64_t* v, int64_t ldv,
            int64_t* out, int64_t ldo, int B, int T, int nh, int nkv, int hd, int sshift, int64_t sq, int mode, int window,
-           const int64_t* cs, const int64_t* sn, cudaStream_t st) {
+           const int64_t* cs, const int64_t* sn, cudaStream_t st, int8_t* planes = nullptr, int64_t mpad = 0,
+           int64_t kpad = 0, const int** planes_flag = nullptr) {
+    if (planes_flag) *planes_flag = nullptr;
     if (tc_enabled() && attention_tc_supported(T, nh, nkv, hd)) {
         size_t need = attention_tc_workspace(B, T, nh, nkv, hd);
         void* ws = m->buf<uint8_t>("attn_ws", need);
         if (ws) {
+            const bool pl = planes && planes_flag && kpad == (int64_t)nh * hd && mpad >= (int64_t)B * T;
             int n = attention_tc(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, sshift, sq, mode, window, ws,
-                                 m->ctx->d_flag, st, cs, sn);
-            if (n >= 0) return n;
+                                 m->ctx->d_flag, st, cs, sn, pl ? planes : nullptr, mpad, kpad);
+            if (n >= 0) {
+                if (pl) *planes_flag = attention_tc_flag(ws);
+                return n;
+            }
         }
     }
     int n = rope_rows(q, ldq, B, T, nh, hd, cs, sn, st);
@@ -582,10 +591,12 @@ inline uint8_t* norm_digits(slx_model* m, int64_t* x, int M, int d, const int64_
     return nullptr;
 }
 
-// A projection of rows whose digit planes a producer wrote (norm_digits); the split runs itself when
-// there are none or the weight does not take the tensor-core path.
-inline void project_from(slx_model* m, const uint8_t* planes, const int64_t* a, int64_t lda, int M, const WDesc& w,
-                         const GemmPlan& p, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, cudaStream_t st) {
+// A projection of rows whose digit planes a producer wrote (norm_digits, the attention's P.V): the
+// planes are used while *flag is zero, the int64 rows by the exact kernel otherwise; the split runs
+// itself when there are none or the weight does not take the tensor-core path.
+inline void project_from(slx_model* m, const int8_t* planes, const int* flag, const int64_t* a, int64_t lda, int M,
+                         const WDesc& w, const GemmPlan& p, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr,
+                         cudaStream_t st) {
     const int64_t kpad = (w.K + tc::BK - 1) / tc::BK * tc::BK;
     if (!planes || p.k_pad != kpad) {
         project(m, a, lda, M, w, p, c, ldc, r, ldr, st);
@@ -595,11 +606,25 @@ inline void project_from(slx_model* m, const uint8_t* planes, const int64_t* a, 
     const bool tcp = p.use_tc && !(!r && gemv_supported(w, M));
     const double tc = tcp ? (double)M * (double)w.N * (double)p.k_pad * tc::LA * p.wlimbs : 0.0;
     run_k(m->ctx, KC_GEMM, macs, 0, st, [&] {
-        if (gemm_run_planes((const int8_t*)planes + 256, (const int*)planes, a, lda, M, w, p, c, ldc, m->scale_bits, r, ldr,
-                            m->gws, st))
+        if (gemm_run_planes(planes, flag, a, lda, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st))
             return 2;
         return gemm_run(a, lda, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st);
     }, tc);
+}
+inline void project_from(slx_model* m, const uint8_t* norm_buf, const int64_t* a, int64_t lda, int M, const WDesc& w,
+                         const GemmPlan& p, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, cudaStream_t st) {
+    project_from(m, norm_buf ? (const int8_t*)norm_buf + 256 : nullptr, (const int*)norm_buf, a, lda, M, w, p, c, ldc, r,
+                 ldr, st);
+}
+// Digit planes for the attention output (the O projection's activations), padding rows zeroed; null
+// when the tensor-core path is off or the width is not a whole number of 128-byte K blocks.
+inline int8_t* attention_planes(slx_model* m, int M, int width, int64_t& mpad, cudaStream_t st) {
+    mpad = (M + tc::BM - 1) / tc::BM * tc::BM;
+    if (!tc_enabled() || width % tc::BK != 0) return nullptr;
+    int8_t* pl = m->buf<int8_t>("att_planes", (size_t)tc::LA * mpad * width);
+    if (pl && mpad > M)
+        for (int i = 0; i < tc::LA; i++) cudaMemsetAsync(pl + ((int64_t)i * mpad + M) * width, 0, (size_t)(mpad - M) * width, st);
+    return pl;
 }
 #define RUN(cls, macs, bytes, call) run_k(ctx, cls, macs, bytes, st, [&] { return call; })
 
@@ -617,16 +642,19 @@ int encoder_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers,
     if (!x || !qkv || !att || !h || !gate || !up) return set_err(ctx, SLX_EOOM, "workspace allocation failed (M=%d)", M);
     RUN(KC_EMBED, 0, 0, embed_encoder(ids, B, T, m->tok, m->tt, m->unk, x, ctx->d_flag, st));
     const uint8_t* xpl = norm_digits(m, x, M, d, m->enw, m->enb, st);  // digit planes of x for the QKV projection
+    int64_t apad = 0;
+    int8_t* apl = attention_planes(m, M, d, apad, st);  // the P.V writes the O projection's digit planes
     const int sshift = 2 * m->scale_bits - 30;
     const int64_t sq = std::max<int64_t>(1, isqrt64_host(hd));
     int nl = n_layers < 0 ? m->layers : std::min(n_layers, m->layers);
     for (int i = 0; i < nl; i++) {
         auto& l = m->L[i];
         project_from(m, xpl, x, d, M, l.qkv, l.p_qkv, qkv, 3 * d, nullptr, 0, st);
+        const int* aflag = nullptr;
         RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0,
             attend(m, qkv, 3 * d, qkv + d, 3 * d, qkv + 2 * d, 3 * d, att, d, B, T, m->heads, m->heads, hd, sshift, sq, 0, 0,
-                   m->cos_g, m->sin_g, st));
-        project(m, att, d, M, l.o, l.p_o, h, d, x, d, st);  // O-projection + residual (AddInPlace)
+                   m->cos_g, m->sin_g, st, apl, apad, d, &aflag));
+        project_from(m, aflag ? apl : nullptr, aflag, att, d, M, l.o, l.p_o, h, d, x, d, st);  // O-projection + residual
         const uint8_t* hpl = norm_digits(m, h, M, d, l.anw, l.anb, st);
         if (hpl) {  // gate and up read the normalised rows' digit planes the norm wrote
             project_from(m, hpl, h, d, M, l.gate, l.p_gate, gate, F, nullptr, 0, st);
@@ -663,6 +691,8 @@ int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, 
         return set_err(ctx, SLX_EOOM, "workspace allocation failed (M=%d)", M);
     const bool causal = m->kind == SLX_MODEL_CAUSAL;
     RUN(KC_EMBED, 0, 0, embed_scaled(ids, B, T, m->tok, m->unk, isqrt64_host(d), x, ctx->d_flag, st));
+    int64_t apad = 0;
+    int8_t* apl = attention_planes(m, M, qd, apad, st);  // the P.V writes the O projection's digit planes
     const int sshift = 2 * m->scale_bits - 30;
     const int64_t sq = std::max<int64_t>(1, isqrt64_host(hd));
     int nl = n_layers < 0 ? m->layers : std::min(n_layers, m->layers);
@@ -683,9 +713,11 @@ int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, 
         const int64_t* cs = global ? m->cos_g : m->cos_l;
         const int64_t* sn = global ? m->sin_g : m->sin_l;
         int mode = !causal ? 0 : ((global || m->sliding <= 0) ? 1 : 2);
+        const int* aflag = nullptr;
         RUN(KC_ATTENTION, 2.0 * B * m->heads * (double)T * T * hd, 0,
-            attend(m, q, qd, k, kvd, v, kvd, att, qd, B, T, m->heads, m->kv_heads, hd, sshift, sq, mode, m->sliding, cs, sn, st));
-        project(m, att, qd, M, l.o, l.p_o, p, d, nullptr, 0, st);
+            attend(m, q, qd, k, kvd, v, kvd, att, qd, B, T, m->heads, m->kv_heads, hd, sshift, sq, mode, m->sliding, cs, sn, st,
+                   apl, apad, qd, &aflag));
+        project_from(m, aflag ? apl : nullptr, aflag, att, qd, M, l.o, l.p_o, p, d, nullptr, 0, st);
         RUN(KC_NORM, 0, 0, rmsnorm_rows(p, d, M, 1, d, l.post_attn, st));
         RUN(KC_ADD, 0, 0, add_rows(p, d, x, d, M, d, st));  // projected += residual; p is the FFN residual
         cudaMemcpyAsync(xn, p, sizeof(int64_t) * M * d, cudaMemcpyDeviceToDevice, st);
