@@ -60,8 +60,21 @@ constexpr uint32_t KPLANE = NK * BK;
 constexpr uint32_t IDESC_S = idesc_i8(LA * NK);
 static_assert(NBUF_MAX * BUF_COLS <= 512 && BUF_COLS <= 256, "TMEM holds 512 columns");
 
+// Work split of a score launch: units (query tile rt, head z) numbered u = z * ntr + rt; the first
+// `whole` run over every key tile; when the units do not fill the last wave of resident CTAs, each of
+// the remaining ones is split into S key ranges, whose parts write their own scores and a partial row
+// maximum, and the last part of a unit to finish (an atomic count) writes the unit's row maxima.
+struct ScorePlan {
+    int ntr = 0, units = 0, whole = 0, rem = 0, S = 1;
+    int blocks() const { return whole + rem * S; }
+    size_t partial_bytes() const { return S > 1 ? (size_t)rem * S * QM * 8 : 0; }
+};
+
 struct ScoreParams {
     int T, SR, nh, zgroup, nkv, ksteps, shift, mask_mode, window, ntiles, stages;  // SR: score row stride (even)
+    ScorePlan plan;
+    int* cnt;        // per split unit, zeroed before the launch
+    int64_t* pmax;   // [rem][S][QM] partial row maxima
     int64_t div;
     int dshift;  // log2(div) when div is a power of two, else -1
     int64_t* S;
@@ -87,7 +100,7 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + nst), qfull = smem_u32(bars + 2 * nst);
     const uint32_t done0 = smem_u32(bars + 2 * nst + 1), tfree0 = smem_u32(bars + 2 * nst + 1 + NBUF);
     uint32_t* tmem_slot = (uint32_t*)(bars + 2 * nst + 1 + 2 * NBUF);
-    __shared__ int s_fail;
+    __shared__ int s_fail, s_last;
     __shared__ int64_t s_max[EPI / 4][QM];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -125,7 +138,16 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
     __syncthreads();
     fence_after();
 
-    const int m0 = blockIdx.x * QM, z = blockIdx.y;
+    const int item = blockIdx.x;
+    int u = item, pid = 0, t_lo = 0, t_hi = p.ntiles;
+    if (item >= p.plan.whole) {  // part pid of split unit (item - whole) / S: key tiles [t_lo, t_hi)
+        pid = (item - p.plan.whole) % p.plan.S;
+        u = p.plan.whole + (item - p.plan.whole) / p.plan.S;
+        t_lo = pid * p.ntiles / p.plan.S;
+        t_hi = (pid + 1) * p.ntiles / p.plan.S;
+    }
+    const int nloc = t_hi - t_lo;
+    const int m0 = (u % p.plan.ntr) * QM, z = u / p.plan.ntr;
     const int zb = (z / p.nh) * p.nkv + (z % p.nh) / p.zgroup;
     const uint32_t sq = smem_u32(smem), sk = sq + QBYTES;
 
@@ -135,14 +157,14 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
 #pragma unroll
             for (int kb = 0; kb < KB; kb++) tma_load_4d(sq + kb * LA * QPLANE, &tmQ, kb * BK, m0, 0, z, qfull);
             int issued = 0;
-            for (int t = 0; t < p.ntiles; t++) {
+            for (int t = 0; t < nloc; t++) {  // t: the CTA's own tile count, t_lo + t the key tile
                 const int s = t % nst;
                 if (!mbar_wait(empty0 + 8 * s, ((uint32_t)(t / nst) & 1u) ^ 1u)) { s_fail = 1; break; }
                 if (*(volatile int*)&s_fail) break;
                 mbar_expect_tx(full0 + 8 * s, KSTAGE);
 #pragma unroll
                 for (int kb = 0; kb < KB; kb++)
-                    tma_load_4d(sk + s * KSTAGE + kb * LA * KPLANE, &tmK, kb * BK, t * NK, 0, zb, full0 + 8 * s);
+                    tma_load_4d(sk + s * KSTAGE + kb * LA * KPLANE, &tmK, kb * BK, (t_lo + t) * NK, 0, zb, full0 + 8 * s);
                 issued = t + 1;
             }
             if (*(volatile int*)&s_fail) {  // let copies still in flight land before the CTA exits
@@ -154,7 +176,7 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
             bool ok = mbar_wait(qfull, 0);
-            for (int t = 0; ok && t < p.ntiles; t++) {
+            for (int t = 0; ok && t < nloc; t++) {
                 const int s = t % nst, b = t % NBUF;
                 if (!mbar_wait(full0 + 8 * s, (uint32_t)(t / nst) & 1u) ||
                     !mbar_wait(tfree0 + 8 * b, ((uint32_t)(t / NBUF) & 1u) ^ 1u)) {
@@ -183,7 +205,7 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
         const double rdiv = 1.0 / (double)p.div;
         int64_t mx = INT64_MIN;
 #pragma unroll 1
-        for (int t = 0; t < p.ntiles; t++) {
+        for (int t = 0; t < nloc; t++) {
             const int b = t % NBUF;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(done0 + 8 * b, (uint32_t)(t / NBUF) & 1u));
             if (!ok) { s_fail = 1; break; }
@@ -199,7 +221,7 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tfree0 + 8 * b);
-            const int n0 = t * NK + CW * part;
+            const int n0 = (t_lo + t) * NK + CW * part;
             int64_t o[CW];
 #pragma unroll
             for (int j = 0; j < CW; j++) {
@@ -242,14 +264,31 @@ k_scores(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
         // row maximum over the column parts
         s_max[part][32 * q4 + lane] = mx;
         asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI) : "memory");
-        if (part == 0 && row_ok) {
+        if (part == 0) {
 #pragma unroll
             for (int i = 1; i < EPI / 4; i++) mx = max(mx, s_max[i][32 * q4 + lane]);
-            p.rmax[(int64_t)z * p.T + row] = mx;
+            if (item < p.plan.whole) {
+                if (row_ok) p.rmax[(int64_t)z * p.T + row] = mx;
+            } else {
+                p.pmax[(int64_t)(item - p.plan.whole) * QM + 32 * q4 + lane] = mx;
+                __threadfence();
+            }
         }
     }
     fence_before();
     __syncthreads();
+    if (item >= p.plan.whole) {  // the last part of a split unit writes its row maxima
+        const int j = (item - p.plan.whole) / p.plan.S;
+        if (threadIdx.x == 0) s_last = atomicAdd(p.cnt + j, 1) == p.plan.S - 1;
+        __syncthreads();
+        if (s_last && threadIdx.x < QM && m0 + (int)threadIdx.x < p.T) {
+            __threadfence();
+            int64_t mx = INT64_MIN;
+            for (int o = 0; o < p.plan.S; o++)
+                mx = max(mx, (int64_t)__ldcg((const long long*)p.pmax + ((int64_t)j * p.plan.S + o) * QM + threadIdx.x));
+            p.rmax[(int64_t)z * p.T + m0 + threadIdx.x] = mx;
+        }
+    }
     if (s_fail && threadIdx.x == 0 && p.err) atomicOr(p.err, KERR_TIMEOUT);
     if (warp == 1) {
         fence_after();
@@ -646,10 +685,35 @@ void launch_pv(int B, int T, int nh, int nkv, const int64_t* scores, int sr, con
 
 // Workspace: [0, 256) the call's flag; [256, HDR) the split tiles' counters; then the q and k
 // digit planes, the scores, the row maxima and the split parts' partial sums.
-constexpr int64_t WS_HDR = 256 + 4 * PV_MAX_SPLIT;
+constexpr int SC_MAX_SPLIT = 1024;  // score units that may be split (their counters follow the P.V's)
+constexpr int64_t WS_HDR = 256 + 4 * PV_MAX_SPLIT + 4 * SC_MAX_SPLIT;
 struct Layout {
-    int64_t kpad, tq, tk, sr, qbytes, kbytes, sbytes, mbytes, pbytes;
+    int64_t kpad, tq, tk, sr, qbytes, kbytes, sbytes, mbytes, pbytes, xbytes;
 };
+
+ScorePlan score_plan(int hd, int B, int T, int nh) {
+    ScorePlan pl;
+    const int slots = (hd <= BK ? score_ctas<1>() : score_ctas<2>()) * device_sm_count();
+    const int nt = (int)(round_up(T, NK) / NK);
+    pl.ntr = (int)(round_up(T, QM) / QM);
+    pl.units = pl.ntr * nh * B;
+    pl.rem = pl.units % slots;
+    pl.whole = pl.units - pl.rem;
+    if (pl.rem == 0 || pl.rem > SC_MAX_SPLIT || nt < 2) {
+        pl.whole = pl.units;
+        pl.rem = 0;
+        return pl;
+    }
+    // tail length in whole-unit times: ceil(rem * S / slots) / S, plus ~3 % for the partial maxima
+    double best = 1.0;
+    const int smax = std::min(std::min(nt, 16), std::max(1, 3 * slots / pl.rem));
+    for (int sp = 2; sp <= smax; sp++) {
+        const double tail = (double)((pl.rem * sp + slots - 1) / slots) / sp * 1.03;
+        if (tail < 0.95 * best) best = tail, pl.S = sp;
+    }
+    if (pl.S == 1) pl.whole = pl.units, pl.rem = 0;
+    return pl;
+}
 
 Layout layout(int B, int T, int nh, int nkv, int hd) {
     Layout l;
@@ -661,14 +725,15 @@ Layout layout(int B, int T, int nh, int nkv, int hd) {
     l.sr = round_up(T, 2);
     l.sbytes = round_up((int64_t)B * nh * T * l.sr * 8, 256);
     l.mbytes = round_up((int64_t)B * nh * T * 8, 256);
-    l.pbytes = (int64_t)pv_plan(hd, B, T, nh).partial_bytes();
+    l.pbytes = round_up((int64_t)pv_plan(hd, B, T, nh).partial_bytes(), 256);
+    l.xbytes = (int64_t)score_plan(hd, B, T, nh).partial_bytes();
     return l;
 }
 }  // namespace
 
 size_t attention_tc_workspace(int B, int T, int nh, int nkv, int hd) {
     const Layout l = layout(B, T, nh, nkv, hd);
-    return (size_t)(WS_HDR + l.qbytes + l.kbytes + l.sbytes + l.mbytes + l.pbytes);
+    return (size_t)(WS_HDR + l.qbytes + l.kbytes + l.sbytes + l.mbytes + l.pbytes + l.xbytes);
 }
 
 bool attention_tc_supported(int T, int nh, int nkv, int hd) {
@@ -690,6 +755,9 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     int64_t* scores = (int64_t*)(kp + l.kbytes);
     int64_t* rmax = (int64_t*)((uint8_t*)scores + l.sbytes);
     int64_t* part = (int64_t*)((uint8_t*)rmax + l.mbytes);
+    int64_t* pmax = (int64_t*)((uint8_t*)part + l.pbytes);
+    int* scnt = cnt + PV_MAX_SPLIT;
+    const ScorePlan spl = score_plan(hd, B, T, nh);
     PvPlan pl = pv_plan(hd, B, T, nh);
     if (planes && kpad == (int64_t)nh * hd && mpad >= (int64_t)B * T) {
         pl.planes = planes;
@@ -700,7 +768,8 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     if (!encode_planes(mq, qp, l.kpad, l.tq, LA, QM, (int64_t)B * nh) ||
         !encode_planes(mk, kp, l.kpad, l.tk, LA, NK, (int64_t)B * nkv))
         return -1;
-    cudaMemsetAsync(flag, 0, 256 + 4 * (size_t)pl.rem, st);  // the flag and the split tiles' counters
+    // the flag and the split units' counters (P.V's, then the score kernel's)
+    cudaMemsetAsync(flag, 0, 256 + 4 * (size_t)PV_MAX_SPLIT + 4 * (size_t)spl.rem, st);
     if (rope_cs) {  // ApplyRoPE on q and k in place, fused with their digit split
         rope_split_heads(const_cast<int64_t*>(q), ldq, B, T, nh, hd, l.tq, l.kpad, rope_cs, rope_sn, qp, flag, st);
         rope_split_heads(const_cast<int64_t*>(k), ldk, B, T, nkv, hd, l.tk, l.kpad, rope_cs, rope_sn, kp, flag, st);
@@ -718,7 +787,10 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     sp.div = sqrt_hd;
     sp.dshift = (sqrt_hd & (sqrt_hd - 1)) == 0 ? __builtin_ctzll((unsigned long long)sqrt_hd) : -1;
     sp.S = scores; sp.rmax = rmax; sp.skip = flag; sp.err = err;
-    const dim3 sgrid((unsigned)(l.tq / QM), (unsigned)(B * nh));
+    sp.plan = spl;
+    sp.cnt = scnt;
+    sp.pmax = pmax;
+    const dim3 sgrid((unsigned)spl.blocks());
     if (l.kpad == BK) launch_scores_kb<1>(*(const CUtensorMap*)mq, *(const CUtensorMap*)mk, sp, sgrid, st);
     else launch_scores_kb<2>(*(const CUtensorMap*)mq, *(const CUtensorMap*)mk, sp, sgrid, st);
 

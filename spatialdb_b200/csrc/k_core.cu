@@ -732,12 +732,23 @@ __global__ void k_add(int64_t* __restrict__ D, int64_t ldd, const int64_t* __res
 }
 
 // MeanPool (IntegerTransformerSource.Forward.cs:69-87)
-__global__ void k_mean_pool(const int64_t* __restrict__ X, int64_t ld, int T, int d, int64_t* __restrict__ P) {
-    int j = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
-    if (j >= d) return;
+// A block owns 32 columns of one sequence; its eight warps sum interleaved rows (a warp reads 256
+// contiguous bytes of a row) and the Int128 partials are added in shared memory.
+constexpr int MP_COLS = 32, MP_GROUPS = 8;
+__global__ __launch_bounds__(MP_COLS * MP_GROUPS) void k_mean_pool(const int64_t* __restrict__ X, int64_t ld, int T,
+                                                                   int d, int64_t* __restrict__ P) {
+    __shared__ u128 part[MP_GROUPS][MP_COLS];
+    const int c = threadIdx.x % MP_COLS, g = threadIdx.x / MP_COLS;
+    const int j = blockIdx.x * MP_COLS + c, b = blockIdx.y;
     u128 s = 0;
-    for (int t = 0; t < T; t++) s += (u128)(i128)X[((int64_t)b * T + t) * ld + j];
-    P[(int64_t)b * d + j] = T > 0 ? lo64((i128)s / (i128)T) : 0;
+    if (j < d)
+        for (int t = g; t < T; t += MP_GROUPS) s += (u128)(i128)X[((int64_t)b * T + t) * ld + j];
+    part[g][c] = s;
+    __syncthreads();
+    if (g == 0 && j < d) {
+        for (int i = 1; i < MP_GROUPS; i++) s += part[i][c];
+        P[(int64_t)b * d + j] = T > 0 ? lo64((i128)s / (i128)T) : 0;
+    }
 }
 
 __global__ void k_gather_last(const int64_t* __restrict__ X, int64_t ld, int T, int d, int64_t* __restrict__ D) {
@@ -923,7 +934,8 @@ int add_rows(int64_t* dst, int64_t ldd, const int64_t* src, int64_t lds, int M, 
 
 int mean_pool(const int64_t* x, int64_t ld, int B, int T, int d, int64_t* pooled, cudaStream_t st) {
     if (B <= 0) return 0;
-    k_mean_pool<<<dim3((unsigned)((d + 127) / 128), (unsigned)B), 128, 0, st>>>(x, ld, T, d, pooled);
+    k_mean_pool<<<dim3((unsigned)((d + MP_COLS - 1) / MP_COLS), (unsigned)B), MP_COLS * MP_GROUPS, 0, st>>>(x, ld, T, d,
+                                                                                                     pooled);
     return 1;
 }
 
