@@ -7,9 +7,10 @@
 // are Vector<float> SIMD sums whose lane order depends on the machine, so this twin is held to a
 // tolerance (maximum absolute error and cosine), not to bits.
 //
-// Every matrix product here, the projections and both attention contractions, is one fp32 GEMM
-// kernel with FFMA accumulation (the products keep fp32 precision; tensor-core tf32 would round the
-// operands to 10 mantissa bits): 128 x 128 output tiles, 8 x 8 per thread, K staged through shared
+// The projections run on the tensor cores (k_fgemm_tc.cu: operands split into high and low tf32
+// parts, three products per pair, fp32 accumulation), which keeps fp32-level precision. The two
+// attention contractions, and the projections when the tensor-core path is off, use one fp32 GEMM
+// kernel with FFMA accumulation: 128 x 128 output tiles, 8 x 8 per thread, K staged through shared
 // memory in steps of 8, arbitrary strides on both operands and a two-level batch (sequence, head).
 #include <algorithm>
 #include <cmath>
@@ -100,13 +101,21 @@ void sgemm(const GemmF& p, int batch, cudaStream_t st) {
 }
 
 // c[rows][nout] = a[rows][nin] . w[nout][nin]^T (GGUF weights are [out][in] row-major)
-void project(const float* a, int rows, int nin, const float* w, int nout, float* c, cudaStream_t st) {
+void project_ffma(const float* a, int rows, int nin, const float* w, int nout, float* c, cudaStream_t st) {
     GemmF p{};
     p.A = a; p.a_m = nin; p.a_k = 1;
     p.B = w; p.b_n = nin; p.b_k = 1;
     p.C = c; p.c_m = nout;
     p.M = rows; p.N = nout; p.K = nin; p.zdiv = 1; p.alpha = 1.0f;
     sgemm(p, 1, st);
+}
+
+// The same product on the tensor cores when the weight's split planes exist (the FFMA kernel
+// otherwise, or when the tensor maps cannot be encoded).
+void project(const float* a, int rows, int nin, const float* w, const float* w_t, int nout, float* c, Workspace& ws,
+             cudaStream_t st) {
+    if (w_t && ws.planes && tc_project(a, rows, nin, w_t, nout, c, ws.planes, ws.err, st)) return;
+    project_ffma(a, rows, nin, w, nout, c, st);
 }
 
 __global__ void k_embed(const int32_t* __restrict__ ids, int64_t total, int d, const float* __restrict__ tok,
@@ -235,8 +244,10 @@ bool grow(T*& p, size_t& cap, size_t count) {
 }  // namespace
 
 void Workspace::release() {
-    for (float* p : {x, qkv, att, h, up, gate, sc}) cudaFree(p);
+    for (float* p : {x, qkv, att, h, up, gate, sc, planes}) cudaFree(p);
+    int* e = err;
     *this = Workspace();
+    err = e;
 }
 
 int forward(const Model& m, const int32_t* d_ids, int B, int T, float* d_out, Workspace& ws, cudaStream_t st,
@@ -247,13 +258,15 @@ int forward(const Model& m, const int32_t* d_ids, int B, int T, float* d_out, Wo
         !grow(ws.h, ws.ch, M * d) || !grow(ws.up, ws.cup, M * F) || !grow(ws.gate, ws.cgate, M * F) ||
         !grow(ws.sc, ws.csc, (size_t)B * H * T * T))
         return -1;
+    const bool tc = !m.layers.empty() && m.layers[0].qkv_t;
+    if (tc && !grow(ws.planes, ws.cplanes, tc_act_bytes((int)M, std::max(d, F)) / sizeof(float))) return -1;
     int64_t nl = 0;
     k_embed<<<blocks(M * d, 256), 256, 0, st>>>(d_ids, M * d, d, m.tok, m.tok_rows, m.tt, m.unk, ws.x);
     k_layernorm<<<blocks(M, 8), 256, 0, st>>>(ws.x, (int)M, d, m.enw, m.enb);
     nl += 2;
     const float scale = 1.0f / sqrtf((float)hd);
     for (const Layer& L : m.layers) {
-        project(ws.x, (int)M, d, L.qkv, 3 * d, ws.qkv, st);
+        project(ws.x, (int)M, d, L.qkv, L.qkv_t, 3 * d, ws.qkv, ws, st);
         k_rope<<<(unsigned)std::min<int64_t>(blocks(M * d, 256), 148 * 32), 256, 0, st>>>(ws.qkv, M, T, d, H, hd, m.cos,
                                                                                           m.sin);
         // scores[b][h][t][s] = scale * q_t . k_s
@@ -271,16 +284,16 @@ int forward(const Model& m, const int32_t* d_ids, int B, int T, float* d_out, Wo
         pv.C = ws.att; pv.c_m = d; pv.c_z1 = (int64_t)T * d; pv.c_z2 = hd;
         pv.M = T; pv.N = hd; pv.K = T; pv.zdiv = H; pv.alpha = 1.0f;
         sgemm(pv, B * H, st);
-        project(ws.att, (int)M, d, L.o, d, ws.h, st);
+        project(ws.att, (int)M, d, L.o, L.o_t, d, ws.h, ws, st);
         k_add<<<blocks(M * d, 256), 256, 0, st>>>(ws.h, ws.x, M * d);
         k_layernorm<<<blocks(M, 8), 256, 0, st>>>(ws.h, (int)M, d, L.anw, L.anb);
-        project(ws.h, (int)M, d, L.up, F, ws.up, st);
-        project(ws.h, (int)M, d, L.gate, F, ws.gate, st);
+        project(ws.h, (int)M, d, L.up, L.up_t, F, ws.up, ws, st);
+        project(ws.h, (int)M, d, L.gate, L.gate_t, F, ws.gate, ws, st);
         k_silu_mul<<<blocks(M * F, 256), 256, 0, st>>>(ws.up, ws.gate, M * F);
-        project(ws.up, (int)M, F, L.down, d, ws.x, st);
+        project(ws.up, (int)M, F, L.down, L.down_t, d, ws.x, ws, st);
         k_add<<<blocks(M * d, 256), 256, 0, st>>>(ws.x, ws.h, M * d);
         k_layernorm<<<blocks(M, 8), 256, 0, st>>>(ws.x, (int)M, d, L.lnw, L.lnb);
-        nl += 14;
+        nl += tc ? 19 : 14;
     }
     k_pool_l2<<<(unsigned)B, 256, sizeof(float) * d, st>>>(ws.x, T, d, d_out);
     nl++;

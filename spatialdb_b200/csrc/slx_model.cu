@@ -410,6 +410,22 @@ int load_float_encoder(slx_ctx* ctx, slx_model* m, GgufFile& g) {
     if ((st = ld.upload(cs.data(), cs.size() * 4, &dc)) || (st = ld.upload(sn.data(), sn.size() * 4, &ds))) return st;
     fm.cos = (const float*)dc;
     fm.sin = (const float*)ds;
+    m->fws.err = ctx->d_flag;
+    if (tc_enabled()) {  // the projections' weights split once for the tensor-core path
+        for (fenc::Layer& l : fm.layers) {
+            const struct { const float* w; int N, K; const float** dst; } t[5] = {
+                {l.qkv, 3 * d, d, &l.qkv_t}, {l.o, d, d, &l.o_t}, {l.up, F, d, &l.up_t}, {l.gate, F, d, &l.gate_t},
+                {l.down, d, F, &l.down_t}};
+            for (const auto& e : t) {
+                void* pl = nullptr;
+                CK(cudaMalloc(&pl, fenc::tc_weight_bytes(e.N, e.K)));
+                m->allocs.push_back(pl);
+                if (!fenc::tc_prepare_weight(e.w, e.N, e.K, (float*)pl, 0)) return set_err(ctx, SLX_ECUDA, "weight split failed");
+                *e.dst = (const float*)pl;
+            }
+        }
+        CK(cudaDeviceSynchronize());
+    }
     return SLX_OK;  // m->L stays empty: no integer projections to plan
 }
 
