@@ -223,11 +223,13 @@ class EncoderShape:
 
 
 def write_encoder(path: str, shape: EncoderShape, wtype: int = Q8_0, seed: int = 0, arch: str = "nomic-bert",
-                  rope_base: float = 10000.0, unk: int | None = None) -> str:
+                  rope_base: float = 10000.0, unk: int | None = None, ffn_norm_scale: float = 1.0) -> str:
     """nomic-bert style encoder with N(0, 0.02) weights quantized to `wtype` (norms and token types F32).
 
     Tensor names and shapes are those IntegerTransformerSource.LoadFromReader reads
     (Gguf/IntegerTransformerSource.Loading.cs:72-151); GGUF ne0 is the inner (K) dimension.
+    ffn_norm_scale multiplies the weight of the norm in front of the FFN (attn_output_norm): large
+    values make the FFN's activations exceed the tensor-core digit range.
     """
     rng = np.random.default_rng(seed)
     d, F, V = shape.embd, shape.ff, shape.vocab
@@ -256,7 +258,7 @@ def write_encoder(path: str, shape: EncoderShape, wtype: int = Q8_0, seed: int =
         p = f"blk.{i}"
         w.tensor(f"{p}.attn_qkv.weight", (d, 3 * d), wtype, normal(3 * d * d))
         w.tensor(f"{p}.attn_output.weight", (d, d), wtype, normal(d * d))
-        w.tensor(f"{p}.attn_output_norm.weight", (d,), F32, 1 + normal(d))
+        w.tensor(f"{p}.attn_output_norm.weight", (d,), F32, (1 + normal(d)) * np.float32(ffn_norm_scale))
         w.tensor(f"{p}.attn_output_norm.bias", (d,), F32, normal(d))
         w.tensor(f"{p}.ffn_up.weight", (d, F), wtype, normal(d * F))
         w.tensor(f"{p}.ffn_gate.weight", (d, F), wtype, normal(d * F))

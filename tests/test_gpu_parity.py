@@ -31,7 +31,10 @@ def models(tmp_path_factory):
     cau_sw = synth.write_causal(str(d / "cau_sw.gguf"), synth.CausalShape(layers=7, embd=64, heads=2, kv_heads=1, head_dim=32,
                                                                           ff=96, vocab=300, sliding_window=5), seed=14,
                                 qk_norm=False)
-    return {"enc": enc, "enc4": enc4, "cau": cau, "cau_sw": cau_sw}
+    # FFN activations beyond five digits: the gate/up and down projections take their exact kernels
+    big = synth.write_encoder(str(d / "big.gguf"), synth.EncoderShape(layers=2, embd=64, heads=4, ff=128, vocab=300, ctx=512),
+                              synth.Q8_0, seed=15, ffn_norm_scale=1000.0)
+    return {"enc": enc, "enc4": enc4, "cau": cau, "cau_sw": cau_sw, "big": big}
 
 
 # ------------------------------------------------------------------ dequant
@@ -120,6 +123,18 @@ def test_encoder_layers_and_pool(ctx, oracle, models, name):
     for b in range(B):
         ref = oracle.to_float_l2(o.forward(batch[b:b + 1])[0])
         np.testing.assert_array_equal(l2[b].view(np.uint32), ref.view(np.uint32))
+
+
+def test_encoder_ffn_beyond_digit_range(ctx, oracle, models):
+    """The FFN's activations exceed the five-digit range: the gate/up projections and the down
+    projection (reading the SiLU gate's planes) fall back to their exact kernels."""
+    path = models["big"]
+    m = slx.IntegerTransformerSource.load(path, ctx=ctx)
+    o = oracle.Encoder(path)
+    batch = np.random.default_rng(5).integers(0, o.vocab, (2, 24)).astype(np.int32)
+    for nl in range(o.layers + 1):
+        np.testing.assert_array_equal(m.trace_hidden(batch[0], nl), o.hidden(batch[0], nl), err_msg=f"layer {nl}")
+    np.testing.assert_array_equal(m.forward(batch), o.forward(batch))
 
 
 def test_encoder_edge_shapes(ctx, oracle, models):
