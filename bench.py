@@ -314,7 +314,6 @@ def encoder_q8_0_bench(ctx, torch, stream, steps: int, warmup: int, cpu: bool = 
     ctx.status(stream.cuda_stream)
     gold = golden("encoder_q8_0_b4_t128.npz")
     parity = bool(np.array_equal(gold["ids"], ids[:4]) and np.array_equal(pooled[:4].cpu().numpy(), gold["pooled"]))
-    lib.slx_profile_begin(ctx._h)
     ev = []
     for _ in range(steps):
         flush.zero_()
@@ -324,11 +323,18 @@ def encoder_q8_0_bench(ctx, torch, stream, steps: int, warmup: int, cpu: bool = 
         e1.record(stream)
         ev.append((e0, e1))
     torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    lib.slx_profile_begin(ctx._h)  # per-class times: a separate, eager pass under the event profile
+    for _ in range(steps):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
     stats = (KernelStat * 16)()
     nst = ctypes_int()
     lib.slx_profile_end(ctx._h, stats, 16, nst)
-    ms = sum(a.elapsed_time(b) for a, b in ev) / steps
     pinned = torch.from_numpy(ids).pin_memory().numpy()
+    for _ in range(3):  # warm the host entry point's buffers and its graph
+        m.forward(pinned)
     e2e = 0.0
     for _ in range(steps):
         flush.zero_()
@@ -821,7 +827,6 @@ def run_ours(args) -> None:
 
     launches0 = ctypes_i64()
     lib.slx_launch_count(ctx._h, launches0)
-    lib.slx_profile_begin(ctx._h)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     if dist:
         dist.barrier()
@@ -837,11 +842,20 @@ def run_ours(args) -> None:
         dist.barrier()
     ctx.status(stream.cuda_stream)  # device-side errors of the timed steps (none expected)
     step_ms = [a.elapsed_time(b) for a, b in ev]
+    launches1 = ctypes_i64()
+    lib.slx_launch_count(ctx._h, launches1)
+    # Per-class device time for the breakdown and the roofline: the same K steps again under the
+    # library's event profile (which brackets each kernel class with events, so these steps run the
+    # forward eagerly rather than from its CUDA graph), L2 flushed before each.
+    lib.slx_profile_begin(ctx._h)
+    for i in range(K):
+        flush.zero_()
+        step(W + i)
+    torch.cuda.synchronize()
     stats = (KernelStat * 16)()
     nstat = ctypes_int()
     lib.slx_profile_end(ctx._h, stats, 16, nstat)
-    launches1 = ctypes_i64()
-    lib.slx_launch_count(ctx._h, launches1)
+    ctx.status(stream.cuda_stream)
     total_ms = sum(step_ms)
     t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
     rank_ms = [total_ms / K]
@@ -857,7 +871,8 @@ def run_ours(args) -> None:
     # timed on the host around the call, with L2 flushed before it outside the timing
     ids_pinned = torch.from_numpy(ids_host).pin_memory().numpy()
     out_host = np.empty((B, ARCH["embd"]), np.int64)
-    model.forward(ids_pinned[0])
+    for i in range(3):  # warm: the entry point's own buffers, then the graph of this shape
+        model.forward(ids_pinned[i])
     if dist:
         dist.barrier()
     e2e_s = 0.0
@@ -905,6 +920,9 @@ def run_ours(args) -> None:
             "dtype": "int64", "data": "synthetic",
             "config": {"workload": workload_name(B), "seq_len": SEQ, "batch_per_gpu": B, "weights": "Q4_0",
                        "parallelism": f"dp{world} (independent sequences)",
+                       "launch": "the library replays each shape's encoder forward from a CUDA graph it captured "
+                                 "(value and e2e loops); the per-class breakdown and the roofline come from a "
+                                 "separate profiled pass of the same steps, run eagerly",
                        "l2": "flushed (256 MiB write) before every timed step, outside the step's events "
                              "(device loop) and outside the host timing (e2e loop)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(B * SEQ * 4),

@@ -66,6 +66,7 @@ int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPla
         if (ws.p) cudaFree(ws.p);
         ws.p = nullptr;
         ws.bytes = 0;
+        ws.gen++;
         if (cudaMalloc(&ws.p, need) != cudaSuccess) return gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st);
         ws.bytes = need;
         cudaMemsetAsync(ws.p, 0, need, st);  // flag words, and the GEMV's row-tile counters start at zero
@@ -101,6 +102,7 @@ int gemm_run_multi(const int64_t* a, int64_t lda, int M, int n, const WDesc* con
         if (ws.p) cudaFree(ws.p);
         ws.p = nullptr;
         ws.bytes = 0;
+        ws.gen++;
         if (cudaMalloc(&ws.p, need) != cudaSuccess) {
             int q = 0;
             for (int i = 0; i < n; i++) q += gemm_exact(a, lda, M, (int)w[i]->K, *w[i], c[i], ldc[i], shift, nullptr, 0, st);

@@ -847,6 +847,7 @@ bool gemv_reserve(GemmWorkspace& ws, int M, int N, int K, cudaStream_t st) {
     ws.p = nullptr;
     ws.bytes = 0;
     ws.tag = 0;
+    ws.gen++;
     if (cudaMalloc(&ws.p, need) != cudaSuccess) return false;
     ws.bytes = need;
     cudaMemsetAsync(ws.p, 0, need, st);  // the overflow word starts below every tag

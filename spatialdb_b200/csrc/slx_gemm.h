@@ -34,6 +34,7 @@ struct GemmWorkspace {
     int* err = nullptr;  // device error word (bounded-wait timeouts)
     unsigned tag = 0;    // last GEMV call's tag (the GEMV's overflow word is compared with it)
     const WaitOptions* wait = nullptr;  // the owning context's settings (nullptr: defaults)
+    uint64_t gen = 0;    // bumped whenever p is reallocated (a captured CUDA graph holds p)
 };
 
 // Tensor-core kernel launchers (k_gemm_tc.cu).

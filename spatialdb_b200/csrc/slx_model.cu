@@ -163,8 +163,24 @@ struct slx_model {
     bool vlat_ready = false;
     fenc::Model fm;                  // SLX_MODEL_FLOAT_ENCODER: fp32 weights (in allocs)
     fenc::Workspace fws;
+    uint64_t buf_gen = 0;            // bumped whenever buf() reallocates
+    // The encoder forward of one (B, T) captured as a CUDA graph (encode_device): replayed while no
+    // buffer it reads or writes has been reallocated since the capture.
+    struct EncoderGraph {
+        cudaGraphExec_t exec = nullptr;
+        int B = -1, T = -1;
+        uint64_t gen = 0;
+        long long wait_limit = 0;
+        int stall = 0;
+        int64_t launches = 0;
+        int seen_B = -1, seen_T = -1;  // the last eager forward, and the generation after it
+        uint64_t seen_gen = ~0ull;
+        bool disabled = false;
+    } eg;
+    uint64_t gen() const { return buf_gen + gws.gen; }
 
     ~slx_model() {
+        if (eg.exec) cudaGraphExecDestroy(eg.exec);
         vocab::release(vlat);
         fws.release();
         for (auto& kv : ws) cudaFree(kv.second.p);
@@ -179,6 +195,7 @@ struct slx_model {
         if (need > b.bytes) {
             if (b.p) cudaFree(b.p);
             b.p = nullptr;
+            buf_gen++;
             // A generate loop asks for one more token row every step: grow by at least a quarter, so
             // the buffers (and cudaFree's device synchronisation) are not renewed at every step.
             const size_t grown = b.bytes ? std::max(need, b.bytes + b.bytes / 4) : need;
@@ -767,6 +784,74 @@ int check_flag(slx_ctx* ctx, cudaStream_t st) {
 
 cudaStream_t pick(slx_ctx* ctx, void* s) { return s ? (cudaStream_t)s : ctx->stream; }
 
+int encode_eager(slx_model* m, const int32_t* d_ids, int B, int T, int64_t* d_pooled, cudaStream_t st);
+
+// The integer encoder's forward replayed from a CUDA graph: the ids are copied into the graph's own
+// input buffer and the pooled rows out of its output buffer, so one capture serves every call of
+// the same shape. A shape is captured on its second call, after an eager call of that shape that
+// allocated nothing further (every buffer at its size); the graph is replayed only while no buffer
+// has been reallocated since (the generation count), with the same bounded-wait settings, outside
+// profiling (which brackets kernel classes with events) and on a stream other than the legacy one.
+// Any failure to capture or instantiate turns graphs off for the model; the eager path computes the
+// same result. Sets served when the graph ran the call; returns a status.
+int encode_graph(slx_model* m, const int32_t* d_ids, int B, int T, int64_t* d_pooled, cudaStream_t st, bool& served) {
+    slx_ctx* ctx = m->ctx;
+    auto& g = m->eg;
+    served = false;
+    if (g.disabled || ctx->prof || !st || m->kind != SLX_MODEL_ENCODER || !tc_enabled() || (int64_t)B * T < 64)
+        return SLX_OK;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return SLX_OK;
+    }
+    int32_t* gids = m->buf<int32_t>("graph_ids", (size_t)B * T);
+    int64_t* gout = m->buf<int64_t>("graph_pooled", (size_t)B * m->embd);
+    if (!gids || !gout) return SLX_OK;
+    const uint64_t gen = m->gen();
+    const bool same_wait = g.wait_limit == ctx->wait.limit_cycles && g.stall == ctx->wait.stall_mma;
+    if (!(g.exec && g.B == B && g.T == T && g.gen == gen && same_wait)) {
+        if (!(g.seen_B == B && g.seen_T == T && g.seen_gen == gen)) return SLX_OK;  // warm this shape eagerly first
+        if (g.exec) cudaGraphExecDestroy(g.exec);
+        g.exec = nullptr;
+        g.B = g.T = -1;
+        const int64_t l0 = ctx->launches;
+        cudaGraph_t graph = nullptr;
+        if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            cudaGetLastError();
+            g.disabled = true;
+            return SLX_OK;
+        }
+        const int rc = encode_eager(m, gids, B, T, gout, st);
+        const cudaError_t e = cudaStreamEndCapture(st, &graph);
+        const int64_t n = ctx->launches - l0;
+        ctx->launches = l0;  // nothing ran during the capture
+        cudaGraphExec_t exec = nullptr;
+        if (rc != SLX_OK || e != cudaSuccess || !graph || m->gen() != gen ||
+            cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            cudaGetLastError();
+            ctx->err.clear();
+            g.disabled = true;
+            return SLX_OK;
+        }
+        cudaGraphDestroy(graph);
+        g.exec = exec;
+        g.B = B;
+        g.T = T;
+        g.gen = gen;
+        g.wait_limit = ctx->wait.limit_cycles;
+        g.stall = ctx->wait.stall_mma;
+        g.launches = n;
+    }
+    CK(cudaMemcpyAsync(gids, d_ids, sizeof(int32_t) * B * T, cudaMemcpyDeviceToDevice, st));
+    CK(cudaGraphLaunch(g.exec, st));
+    CK(cudaMemcpyAsync(d_pooled, gout, sizeof(int64_t) * B * m->embd, cudaMemcpyDeviceToDevice, st));
+    ctx->launches += g.launches;
+    served = true;
+    return SLX_OK;
+}
+
 int encode_device(slx_model* m, const int32_t* d_ids, int B, int T, int64_t* d_pooled, cudaStream_t st) {
     slx_ctx* ctx = m->ctx;
     if (B < 0 || T < 0) return set_err(ctx, SLX_EINVAL, "bad batch shape B=%d T=%d", B, T);
@@ -775,6 +860,20 @@ int encode_device(slx_model* m, const int32_t* d_ids, int B, int T, int64_t* d_p
         CK(cudaMemsetAsync(d_pooled, 0, sizeof(int64_t) * B * m->embd, st));
         return SLX_OK;
     }
+    bool served = false;
+    const int gr = encode_graph(m, d_ids, B, T, d_pooled, st, served);
+    if (gr != SLX_OK || served) return gr;
+    const int rc = encode_eager(m, d_ids, B, T, d_pooled, st);
+    if (rc == SLX_OK) {  // the shape is warm once this call has allocated what it needs
+        m->eg.seen_B = B;
+        m->eg.seen_T = T;
+        m->eg.seen_gen = m->gen();
+    }
+    return rc;
+}
+
+int encode_eager(slx_model* m, const int32_t* d_ids, int B, int T, int64_t* d_pooled, cudaStream_t st) {
+    slx_ctx* ctx = m->ctx;
     int64_t* x = nullptr;
     int rc;
     if (m->kind == SLX_MODEL_ENCODER) {

@@ -137,6 +137,18 @@ def test_encoder_ffn_beyond_digit_range(ctx, oracle, models):
     np.testing.assert_array_equal(m.forward(batch), o.forward(batch))
 
 
+def test_encoder_graph_replay_across_shapes(ctx, oracle, models):
+    """Repeated calls of one shape replay the forward from the library's CUDA graph (captured on the
+    second call); a larger shape reallocates the workspaces, after which the first shape runs eagerly
+    and is captured again. Every call equals the oracle."""
+    m = slx.IntegerTransformerSource.load(models["enc"], ctx=ctx)
+    o = oracle.Encoder(models["enc"])
+    rng = np.random.default_rng(9)
+    for B, T in [(2, 40)] * 4 + [(4, 64)] * 2 + [(2, 40)] * 3:
+        batch = rng.integers(0, o.vocab, (B, T)).astype(np.int32)
+        np.testing.assert_array_equal(m.forward(batch), o.forward(batch), err_msg=f"{B} x {T}")
+
+
 def test_encoder_edge_shapes(ctx, oracle, models):
     m = slx.IntegerTransformerSource.load(models["enc"], ctx=ctx)
     o = oracle.Encoder(models["enc"])
