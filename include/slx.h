@@ -99,7 +99,12 @@ slx_status slx_model_info(slx_model* model, int32_t* info, int n);
  * (IntegerGemmaSource.Forward, Gguf/IntegerGemmaSource.cs:66-80). */
 slx_status slx_encode(slx_model* model, const int32_t* ids, int B, int T, int64_t* pooled_q30, float* l2);
 /* Same on device buffers: d_ids[B*T] int32, d_pooled[B*embd] int64, queued on `stream`. Errors the
- * device raises while it runs (SLX_ERANGE, SLX_ETIMEOUT) are read with slx_ctx_status. */
+ * device raises while it runs (SLX_ERANGE, SLX_ETIMEOUT) are read with slx_ctx_status. From the
+ * second call of a (B, T) on, the integer encoder's forward is replayed from a CUDA graph the model
+ * captured (same results; the graph's input and output live in the model's workspace, so d_ids and
+ * d_pooled may change between calls). The replay is skipped, and the forward queued kernel by
+ * kernel, while profiling, on the legacy default stream, while `stream` is itself being captured,
+ * and for fewer than 64 rows. */
 slx_status slx_encode_device(slx_model* model, const int32_t* d_ids, int B, int T, int64_t* d_pooled, void* stream);
 
 /* Hidden states after the first n_layers blocks (n_layers < 0: all), x_q30[T][embd], for one
