@@ -428,28 +428,43 @@ __global__ __launch_bounds__(256) void k_layernorm_q(int64_t* __restrict__ X, in
     bool bad = false;
     for (int row = blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += gridDim.x * 8) {
         int64_t* x = X + (int64_t)row * ld;
-        u128 s = 0;
+        // one pass for the sum and the sum of squares; with every |x| < 2^62 no x - mean wraps, and
+        // then sum (x - mean)^2 = Q - 2 mean S + n mean^2 holds exactly in wrapping 128-bit arithmetic
+        u128 s = 0, sq = 0;
+        bool wide = false;
 #pragma unroll
         for (int q = 0; q < NQ; q++) {
             const int j = 128 * q + 4 * lane;
             if (j < n) {
                 const longlong2 a = __ldg((const longlong2*)(x + j)), c = __ldg((const longlong2*)(x + j + 2));
                 s += (u128)(i128)a.x + (u128)(i128)a.y + (u128)(i128)c.x + (u128)(i128)c.y;
+                sq += (u128)((i128)a.x * a.x) + (u128)((i128)a.y * a.y) + (u128)((i128)c.x * c.x) + (u128)((i128)c.y * c.y);
+                wide |= (((uint64_t)a.x + (1ULL << 62)) | ((uint64_t)a.y + (1ULL << 62)) | ((uint64_t)c.x + (1ULL << 62)) |
+                         ((uint64_t)c.y + (1ULL << 62))) >> 63;
             }
         }
         s = warp_sum_u128(s);
+        sq = warp_sum_u128(sq);
         const int64_t mean = div_i128_n(s, (uint32_t)n, inv);
-        u128 ss = 0;
+        u128 ss;
+        if (!__any_sync(0xffffffffu, wide)) {
+            const uint64_t s_lo = (uint64_t)s, s_hi = (uint64_t)(s >> 64);
+            const u128 ms = (u128)((i128)mean * (int64_t)s_lo) + ((u128)(s_lo >> 63) * (u128)(uint64_t)mean << 64) +
+                            ((u128)((uint64_t)mean * s_hi) << 64);  // mean * S mod 2^128
+            ss = sq - 2 * ms + (u128)n * (u128)((i128)mean * mean);
+        } else {  // values near the int64 limits: the reference's wrapping differences, a second pass
+            ss = 0;
 #pragma unroll
-        for (int q = 0; q < NQ; q++) {
-            const int j = 128 * q + 4 * lane;
-            if (j < n) {
-                const longlong2 a = __ldg((const longlong2*)(x + j)), c = __ldg((const longlong2*)(x + j + 2));
-                const int64_t d0 = wsub(a.x, mean), d1 = wsub(a.y, mean), d2 = wsub(c.x, mean), d3 = wsub(c.y, mean);
-                ss += (u128)((i128)d0 * d0) + (u128)((i128)d1 * d1) + (u128)((i128)d2 * d2) + (u128)((i128)d3 * d3);
+            for (int q = 0; q < NQ; q++) {
+                const int j = 128 * q + 4 * lane;
+                if (j < n) {
+                    const longlong2 a = __ldg((const longlong2*)(x + j)), c = __ldg((const longlong2*)(x + j + 2));
+                    const int64_t d0 = wsub(a.x, mean), d1 = wsub(a.y, mean), d2 = wsub(c.x, mean), d3 = wsub(c.y, mean);
+                    ss += (u128)((i128)d0 * d0) + (u128)((i128)d1 * d1) + (u128)((i128)d2 * d2) + (u128)((i128)d3 * d3);
+                }
             }
+            ss = warp_sum_u128(ss);
         }
-        ss = warp_sum_u128(ss);
         // Int128 variance = sumSq / n (a wrapped, negative sumSq gives var <= 0 as in the reference)
         const i128 var = (i128)ss < 0 ? (i128)0 : (i128)udiv128_u32(ss, (uint32_t)n, inv);
         int64_t isq = var > 0 ? isqrt_u128((u128)var) : 1;
