@@ -564,7 +564,9 @@ void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K,
     Params p = base_params();
     p.M = M; p.N = N; p.nkb = (int)(kpad / GK); p.shift = shift;
     p.tiles_n = (int)((npad + GN - 1) / GN);
-    p.tiles = (int)(mpad / GM) * p.tiles_n;
+    // activation tiles up to M only: the digit planes' padding rows (up to the 128-row multiple)
+    // hold zeros whose outputs are never stored
+    p.tiles = (int)std::min<int64_t>(mpad / GM, (M + GM - 1) / GM) * p.tiles_n;
     p.C = c; p.ldc = ldc; p.R = r; p.ldr = ldr; p.skip = skip; p.err = err; p.row_shift = row_shift;
     if (wait) { p.wait_limit = wait->limit_cycles; p.stall_mma = wait->stall_mma; }
     const CUtensorMap& ta = *(const CUtensorMap*)tmap_a;
