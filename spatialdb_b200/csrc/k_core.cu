@@ -529,6 +529,130 @@ __global__ __launch_bounds__(NT) void k_rmsnorm(int64_t* __restrict__ X, int64_t
         x[j] = muldiv_trunc(x[j], wj, d_i64(wj), rms, rd);
     }
 }
+
+// RmsNormRow for short rows (n <= 32 * PL, e.g. RmsNormPerHead's head segments): one warp per row,
+// the lane's values in registers, the Int128 sum reduced by shuffles, every lane taking the same
+// square root; row r is segment (r % per) of line (r / per).
+template <int PL>
+__global__ __launch_bounds__(256) void k_rmsnorm_warp(int64_t* __restrict__ X, int64_t ld, int per, int n, int rows,
+                                                      const int64_t* __restrict__ w) {
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    int64_t* x = X + (int64_t)(r / per) * ld + (int64_t)(r % per) * n;
+    int64_t v[PL];
+    u128 ss = 0;
+#pragma unroll
+    for (int e = 0; e < PL; e++) {
+        const int j = lane + 32 * e;
+        v[e] = j < n ? x[j] : 0;
+        ss += (u128)((i128)v[e] * v[e]);
+    }
+    ss = warp_sum_u128(ss);
+    if ((i128)ss < (i128)n) return;  // ms = sumSq / n <= 0: the row is left as it is
+    int64_t rms = isqrt_u128(udiv128_u32(ss, (uint32_t)n, ~0ULL / (uint32_t)n));
+    if (rms == 0) rms = 1;
+    const double rd = 1.0 / (double)rms;
+#pragma unroll
+    for (int e = 0; e < PL; e++) {
+        const int j = lane + 32 * e;
+        if (j < n) {
+            const int64_t wj = w[j];
+            x[j] = muldiv_trunc(v[e], wj, d_i64(wj), rms, rd);
+        }
+    }
+}
+
+// The causal block's norms around a residual add, one block per row of n = 256 * EPT (EPT
+// consecutive values a thread, kept in registers between the steps):
+//   with w1:  y <- RmsNormRow(y; w1) + r   (the post-attention / post-FFN norm and the residual add)
+//   with w2:  z <- RmsNormRow(y; w2)       (the next pre-norm), with, when planes is given, z's five
+//             balanced digit planes [5][Mpad][Kpad] for the projections that read it (*overflow raised
+//             for a value beyond five digits).
+// RmsNormRow (IntegerLayerNorm.cs:71-93): ms = (Int128 sum x^2) / n; a row with ms <= 0 is left as it
+// is; otherwise x = (long)((Int128)x * w / max(ISqrt(ms), 1)).
+SLX_DEV int64_t rms_of_block(u128 ss, int n, u128* sh, bool& skip) {
+    ss = warp_sum_u128(ss);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    u128 t = 0;
+#pragma unroll
+    for (int i = 0; i < NT / 32; i++) t += sh[i];  // every thread forms the same total
+    // ms = (Int128)t / n is at most 0 exactly when t (signed) < n; otherwise t > 0 and the unsigned
+    // division by the 32-bit n is the same quotient
+    skip = (i128)t < (i128)n;
+    const int64_t r = skip ? 0 : isqrt_u128(udiv128_u32(t, (uint32_t)n, ~0ULL / (uint32_t)n));
+    return r == 0 ? 1 : r;
+}
+
+template <int EPT>
+__global__ __launch_bounds__(NT) void k_rms_pair(int64_t* __restrict__ Y, const int64_t* __restrict__ R,
+                                                 int64_t* __restrict__ Z, int n, const int64_t* __restrict__ w1,
+                                                 const int64_t* __restrict__ w2, int Mpad, int Kpad,
+                                                 int8_t* __restrict__ planes, int* overflow) {
+    __shared__ u128 sh1[NT / 32], sh2[NT / 32];
+    const int64_t row = blockIdx.x;
+    const int j0 = threadIdx.x * EPT;
+    const bool in = j0 < n;
+    int64_t v[EPT];
+#pragma unroll
+    for (int e = 0; e < EPT; e += 2) {
+        const longlong2 a = in ? *(const longlong2*)(Y + row * n + j0 + e) : make_longlong2(0, 0);
+        v[e] = a.x;
+        v[e + 1] = a.y;
+    }
+    if (w1) {
+        u128 ss = 0;
+#pragma unroll
+        for (int e = 0; e < EPT; e++) ss += (u128)((i128)v[e] * v[e]);
+        bool skip;
+        const int64_t rms = rms_of_block(ss, n, sh1, skip);
+        const double rd = 1.0 / (double)rms;
+        if (in) {
+#pragma unroll
+            for (int e = 0; e < EPT; e += 2) {
+                const longlong2 r = *(const longlong2*)(R + row * n + j0 + e);
+                if (!skip) {
+                    const longlong2 w = *(const longlong2*)(w1 + j0 + e);
+                    v[e] = muldiv_trunc(v[e], w.x, d_i64(w.x), rms, rd);
+                    v[e + 1] = muldiv_trunc(v[e + 1], w.y, d_i64(w.y), rms, rd);
+                }
+                v[e] = wadd(v[e], r.x);
+                v[e + 1] = wadd(v[e + 1], r.y);
+                *(longlong2*)(Y + row * n + j0 + e) = make_longlong2(v[e], v[e + 1]);
+            }
+        }
+    }
+    if (!w2) return;
+    u128 ss = 0;
+#pragma unroll
+    for (int e = 0; e < EPT; e++) ss += (u128)((i128)v[e] * v[e]);
+    bool skip;
+    const int64_t rms = rms_of_block(ss, n, sh2, skip);
+    const double rd = 1.0 / (double)rms;
+    if (!in) return;
+    bool bad = false;
+#pragma unroll
+    for (int e = 0; e < EPT; e += 4) {
+        int64_t z[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            z[u] = v[e + u];
+            if (!skip) {
+                const int64_t w = w2[j0 + e + u];
+                z[u] = muldiv_trunc(z[u], w, d_i64(w), rms, rd);
+            }
+        }
+        *(longlong2*)(Z + row * n + j0 + e) = make_longlong2(z[0], z[1]);
+        *(longlong2*)(Z + row * n + j0 + e + 2) = make_longlong2(z[2], z[3]);
+        if (planes) {
+            uint32_t wd[5];
+            digit_words4(z[0], z[1], z[2], z[3], wd, bad);
+#pragma unroll
+            for (int i = 0; i < 5; i++) *(uint32_t*)(planes + ((int64_t)i * Mpad + row) * Kpad + j0 + e) = wd[i];
+        }
+    }
+    if (bad) atomicOr(overflow, 1);
+}
 }  // namespace
 
 int layernorm_rows(int64_t* x, int64_t ld, int rows, int n, const int64_t* w, const int64_t* b, cudaStream_t st) {
@@ -566,8 +690,33 @@ int layernorm_rows_digits(int64_t* x, int64_t ld, int rows, int n, const int64_t
 
 int rmsnorm_rows(int64_t* x, int64_t ld, int rows, int per, int n, const int64_t* w, cudaStream_t st) {
     if (rows <= 0) return 0;
-    k_rmsnorm<<<rows, NT, 0, st>>>(x, ld, per, n, w);
+    const unsigned wb = (unsigned)((rows + 7) / 8);
+    if (n <= 32) k_rmsnorm_warp<1><<<wb, 256, 0, st>>>(x, ld, per, n, rows, w);
+    else if (n <= 64) k_rmsnorm_warp<2><<<wb, 256, 0, st>>>(x, ld, per, n, rows, w);
+    else if (n <= 128) k_rmsnorm_warp<4><<<wb, 256, 0, st>>>(x, ld, per, n, rows, w);
+    else if (n <= 256) k_rmsnorm_warp<8><<<wb, 256, 0, st>>>(x, ld, per, n, rows, w);
+    else if (n <= 512) k_rmsnorm_warp<16><<<wb, 256, 0, st>>>(x, ld, per, n, rows, w);
+    else k_rmsnorm<<<rows, NT, 0, st>>>(x, ld, per, n, w);
     return 1;
+}
+
+int rms_pair_rows(int64_t* y, const int64_t* r, int64_t* z, int rows, int n, const int64_t* w1, const int64_t* w2,
+                  int64_t Mpad, int64_t Kpad, int8_t* planes, int* overflow, cudaStream_t st) {
+    if (rows <= 0) return 0;
+    if (n % (4 * NT) != 0 || n > 16 * NT || ((uintptr_t)y & 15) || (r && ((uintptr_t)r & 15)) || ((uintptr_t)z & 15) ||
+        (w1 && ((uintptr_t)w1 & 15)) || (planes && (Kpad != n || Mpad < rows)))
+        return -1;
+    int k = 0;
+    if (planes && Mpad > rows)  // padding rows of every plane: zero digits
+        for (int i = 0; i < 5; i++, k++)
+            cudaMemsetAsync(planes + ((int64_t)i * Mpad + rows) * Kpad, 0, (size_t)(Mpad - rows) * Kpad, st);
+    switch (n / NT) {
+        case 4: k_rms_pair<4><<<rows, NT, 0, st>>>(y, r, z, n, w1, w2, (int)Mpad, (int)Kpad, planes, overflow); break;
+        case 8: k_rms_pair<8><<<rows, NT, 0, st>>>(y, r, z, n, w1, w2, (int)Mpad, (int)Kpad, planes, overflow); break;
+        case 12: k_rms_pair<12><<<rows, NT, 0, st>>>(y, r, z, n, w1, w2, (int)Mpad, (int)Kpad, planes, overflow); break;
+        default: k_rms_pair<16><<<rows, NT, 0, st>>>(y, r, z, n, w1, w2, (int)Mpad, (int)Kpad, planes, overflow); break;
+    }
+    return k + 1;
 }
 
 // ------------------------------------------------------------------------------------------

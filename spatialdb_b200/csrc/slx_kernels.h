@@ -52,6 +52,12 @@ int layernorm_rows_digits(int64_t* x, int64_t ld, int rows, int n, const int64_t
 // RmsNorm rows (IntegerLayerNorm.RmsNormRow): row r is segment (r % per) of line (r / per),
 // x + (r/per)*ld + (r%per)*n, length n; per > 1 gives RmsNormPerHead.
 int rmsnorm_rows(int64_t* x, int64_t ld, int rows, int per, int n, const int64_t* w, cudaStream_t st);
+// The causal block's norm pair over rows of n (contiguous, n a multiple of 1024, at most 4096):
+// with w1, y = RmsNormRow(y; w1) + r; with w2, z = RmsNormRow(y; w2), plus z's five digit planes
+// [5][Mpad][Kpad = n] when planes is given (*overflow raised beyond five digits). Returns -1
+// (nothing queued) for shapes it does not cover.
+int rms_pair_rows(int64_t* y, const int64_t* r, int64_t* z, int rows, int n, const int64_t* w1, const int64_t* w2,
+                  int64_t Mpad, int64_t Kpad, int8_t* planes, int* overflow, cudaStream_t st);
 
 // ApplyRoPE on rows m of B*T (position m % T), nh heads of hd at x + m*ld + h*hd.
 int rope_rows(int64_t* x, int64_t ld, int B, int T, int nh, int hd, const int64_t* cos, const int64_t* sin,

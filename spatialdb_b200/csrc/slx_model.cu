@@ -729,12 +729,37 @@ int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, 
     const int sshift = 2 * m->scale_bits - 30;
     const int64_t sq = std::max<int64_t>(1, isqrt64_host(hd));
     int nl = n_layers < 0 ? m->layers : std::min(n_layers, m->layers);
+    // The norms around each residual add run as one kernel per pair (rms_pair_rows), which also
+    // writes the normalised rows' digit planes for the projections that read them (overflow word
+    // at byte 0, planes from byte 256); without it, the separate norm, add and copy launches.
+    const int64_t npad = (M + tc::BM - 1) / tc::BM * tc::BM;
+    uint8_t* nbuf = tc_enabled() ? m->buf<uint8_t>("rms_planes", 256 + (size_t)tc::LA * npad * d) : nullptr;
+    int8_t* npl = nbuf ? (int8_t*)nbuf + 256 : nullptr;
+    int* nflag = (int*)nbuf;
+    auto rms_pair = [&](int64_t* y, const int64_t* r, int64_t* z, const int64_t* w1, const int64_t* w2) -> bool {
+        int n = -1;
+        if (nbuf && w2) cudaMemsetAsync(nflag, 0, sizeof(int), st);
+        RUN(KC_NORM, 0, 0, (n = rms_pair_rows(y, r, z, M, d, w1, w2, npad, d, w2 ? npl : nullptr, nflag, st)) < 0 ? 0 : n);
+        return n >= 0;
+    };
+    bool xn_ready = false;  // xn (and its planes) already hold this layer's pre-attention norm
     for (int i = 0; i < nl; i++) {
         auto& l = m->L[i];
         bool global = !causal || m->global_interval <= 0 || ((i + 1) % m->global_interval) == 0;  // IsGlobalLayer
-        cudaMemcpyAsync(xn, x, sizeof(int64_t) * M * d, cudaMemcpyDeviceToDevice, st);
-        RUN(KC_NORM, 0, 0, rmsnorm_rows(xn, d, M, 1, d, l.attn_norm, st));
-        {  // Q, K and V read the same normalised rows: one digit split for all three
+        bool planes = xn_ready;
+        if (!xn_ready) {
+            planes = nbuf && rms_pair(x, nullptr, xn, nullptr, l.attn_norm);
+            if (!planes) {
+                cudaMemcpyAsync(xn, x, sizeof(int64_t) * M * d, cudaMemcpyDeviceToDevice, st);
+                RUN(KC_NORM, 0, 0, rmsnorm_rows(xn, d, M, 1, d, l.attn_norm, st));
+            }
+        }
+        xn_ready = false;
+        if (planes) {  // Q, K and V read the norm's digit planes
+            project_from(m, npl, nflag, xn, d, M, l.q, l.p_q, q, qd, nullptr, 0, st);
+            project_from(m, npl, nflag, xn, d, M, l.k, l.p_k, k, kvd, nullptr, 0, st);
+            project_from(m, npl, nflag, xn, d, M, l.v, l.p_v, v, kvd, nullptr, 0, st);
+        } else {  // Q, K and V read the same normalised rows: one digit split for all three
             const WDesc* ws3[3] = {&l.q, &l.k, &l.v};
             const GemmPlan* ps3[3] = {&l.p_q, &l.p_k, &l.p_v};
             int64_t* cs3[3] = {q, k, v};
@@ -751,11 +776,15 @@ int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, 
             attend(m, q, qd, k, kvd, v, kvd, att, qd, B, T, m->heads, m->kv_heads, hd, sshift, sq, mode, m->sliding, cs, sn, st,
                    apl, apad, qd, &aflag));
         project_from(m, aflag ? apl : nullptr, aflag, att, qd, M, l.o, l.p_o, p, d, nullptr, 0, st);
-        RUN(KC_NORM, 0, 0, rmsnorm_rows(p, d, M, 1, d, l.post_attn, st));
-        RUN(KC_ADD, 0, 0, add_rows(p, d, x, d, M, d, st));  // projected += residual; p is the FFN residual
-        cudaMemcpyAsync(xn, p, sizeof(int64_t) * M * d, cudaMemcpyDeviceToDevice, st);
-        RUN(KC_NORM, 0, 0, rmsnorm_rows(xn, d, M, 1, d, l.ffn_norm, st));
-        {
+        // p = post-attention norm(p) + x (p is the FFN's residual), xn = ffn_norm(p)
+        if (nbuf && rms_pair(p, x, xn, l.post_attn, l.ffn_norm)) {
+            project_from(m, npl, nflag, xn, d, M, l.gate, l.p_gate, gate, F, nullptr, 0, st);
+            project_from(m, npl, nflag, xn, d, M, l.up, l.p_up, up, F, nullptr, 0, st);
+        } else {
+            RUN(KC_NORM, 0, 0, rmsnorm_rows(p, d, M, 1, d, l.post_attn, st));
+            RUN(KC_ADD, 0, 0, add_rows(p, d, x, d, M, d, st));  // projected += residual; p is the FFN residual
+            cudaMemcpyAsync(xn, p, sizeof(int64_t) * M * d, cudaMemcpyDeviceToDevice, st);
+            RUN(KC_NORM, 0, 0, rmsnorm_rows(xn, d, M, 1, d, l.ffn_norm, st));
             const WDesc* ws2[2] = {&l.gate, &l.up};
             const GemmPlan* ps2[2] = {&l.p_gate, &l.p_up};
             int64_t* cs2[2] = {gate, up};
@@ -763,8 +792,14 @@ int causal_hidden(slx_model* m, const int32_t* ids, int B, int T, int n_layers, 
             project_multi(m, xn, d, M, 2, ws2, ps2, cs2, ld2, st);
         }
         gate_down(m, gate, up, F, M, l.down, l.p_down, x, d, nullptr, 0, st);
-        RUN(KC_NORM, 0, 0, rmsnorm_rows(x, d, M, 1, d, l.post_ffw, st));
-        RUN(KC_ADD, 0, 0, add_rows(x, d, p, d, M, d, st));
+        // x = post-FFN norm(x) + p, and the next layer's pre-attention norm xn = attn_norm(x)
+        const int64_t* next_norm = i + 1 < nl ? m->L[i + 1].attn_norm : nullptr;
+        if (nbuf && rms_pair(x, p, xn, l.post_ffw, next_norm)) {
+            xn_ready = next_norm != nullptr;
+        } else {
+            RUN(KC_NORM, 0, 0, rmsnorm_rows(x, d, M, 1, d, l.post_ffw, st));
+            RUN(KC_ADD, 0, 0, add_rows(x, d, p, d, M, d, st));
+        }
     }
     x_out = x;
     return SLX_OK;
