@@ -78,10 +78,10 @@ int gemm_run(const int64_t* a, int64_t lda, int M, const WDesc& w, const GemmPla
         return gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st);
     cudaMemsetAsync(flag, 0, sizeof(int), st);
     tc::split_a(a, lda, M, (int)w.K, mpad, plan.k_pad, planes, flag, st);
+    // (the exact product runs in the same launch if the split overflowed)
     tc::launch(tmap_a, plan.tmap_w, plan.wlimbs, M, (int)w.N, (int)w.K, mpad, plan.n_pad, plan.k_pad, shift, c, ldc, r,
-               ldr, flag, ws.err, st, plan.row_shift, ws.wait);
-    gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st, flag);  // runs only if the split overflowed
-    return 3;
+               ldr, flag, ws.err, st, plan.row_shift, ws.wait, a, lda, &w);
+    return 2;
 }
 
 int gemm_run_multi(const int64_t* a, int64_t lda, int M, int n, const WDesc* const* w, const GemmPlan* const* plan,
@@ -123,10 +123,9 @@ int gemm_run_multi(const int64_t* a, int64_t lda, int M, int n, const WDesc* con
     tc::split_a(a, lda, M, (int)w[0]->K, mpad, kpad, planes, flag, st);
     for (int i = 0; i < n; i++) {
         tc::launch(tmap_a, plan[i]->tmap_w, plan[i]->wlimbs, M, (int)w[i]->N, (int)w[i]->K, mpad, plan[i]->n_pad, kpad,
-                   shift, c[i], ldc[i], nullptr, 0, flag, ws.err, st, plan[i]->row_shift, ws.wait);
-        gemm_exact(a, lda, M, (int)w[i]->K, *w[i], c[i], ldc[i], shift, nullptr, 0, st, flag);  // only if the split overflowed
+                   shift, c[i], ldc[i], nullptr, 0, flag, ws.err, st, plan[i]->row_shift, ws.wait, a, lda, w[i]);
     }
-    return 1 + 2 * n;
+    return 1 + n;
 }
 
 bool gemm_run_planes(const int8_t* planes, const int* flag, const int64_t* a, int64_t lda, int M, const WDesc& w,
@@ -136,9 +135,9 @@ bool gemm_run_planes(const int8_t* planes, const int* flag, const int64_t* a, in
     const int64_t mpad = round_up(M, tc::BM);
     alignas(64) unsigned char tmap_a[128];
     if (!tc::encode_planes(tmap_a, const_cast<int8_t*>(planes), plan.k_pad, mpad, tc::LA, tc::GM, 1, tc::GK)) return false;
+    // (the exact product runs in the same launch if a value overflowed its digits)
     tc::launch(tmap_a, plan.tmap_w, plan.wlimbs, M, (int)w.N, (int)w.K, mpad, plan.n_pad, plan.k_pad, shift, c, ldc, r,
-               ldr, flag, ws.err, st, plan.row_shift, ws.wait);
-    gemm_exact(a, lda, M, (int)w.K, w, c, ldc, shift, r, ldr, st, flag);  // runs only if a value overflowed its digits
+               ldr, flag, ws.err, st, plan.row_shift, ws.wait, a, lda, &w);
     return true;
 }
 

@@ -118,8 +118,9 @@ extern "C" slx_status slx_matmul_q30_noalloc(const int64_t* d_a, int M, int K, i
     const int64_t tot = npad * kpad;
     k_split_w_checked<<<(unsigned)((tot + 255) / 256), 256, 0, st>>>(w, (int)npad, (int)kpad, w_dig, overflow);
     tc::split_a(d_a, K, M, K, mpad, kpad, a_planes, overflow, st);
-    tc::launch(map_a, map_w, kWeightDigits, M, N, K, mpad, npad, kpad, shift, d_c, N, nullptr, 0, overflow, err, st);
-    gemm_exact(d_a, K, M, K, w, d_c, N, shift, nullptr, 0, st, overflow);  // only if a value overflowed its digits
+    // (the exact product runs in the same launch if a value overflowed its digits)
+    tc::launch(map_a, map_w, kWeightDigits, M, N, K, mpad, npad, kpad, shift, d_c, N, nullptr, 0, overflow, err, st, nullptr,
+               nullptr, d_a, K, &w);
     if (cudaGetLastError() != cudaSuccess) return SLX_ECUDA;
     int host_err = 0;
     if (cudaMemcpyAsync(&host_err, err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) return SLX_ECUDA;

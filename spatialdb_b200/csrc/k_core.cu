@@ -9,6 +9,7 @@
 
 #include "slx_attr.h"
 #include "slx_device.cuh"
+#include "slx_exact.cuh"
 #include "slx_kernels.h"
 
 namespace slx {
@@ -19,72 +20,14 @@ namespace slx {
 // 64x64 output tile, K in steps of one 32-element quant block, 4x4 Int128 accumulators per thread.
 // ------------------------------------------------------------------------------------------
 namespace {
-constexpr int GBM = 64, GBN = 64, GBK = 32;
-
-__global__ __launch_bounds__(256) void k_gemm_exact(const int64_t* __restrict__ A, int64_t lda, int M, int K,
-                                                    WDesc W, int64_t* __restrict__ C, int64_t ldc, int shift,
+__global__ __launch_bounds__(XTH) void k_gemm_exact(const int64_t* __restrict__ A, int64_t lda, int M, int K, WDesc W,
+                                                    int64_t* __restrict__ C, int64_t ldc, int shift,
                                                     const int64_t* __restrict__ R, int64_t ldr,
                                                     const int* __restrict__ only_if) {
     if (only_if && *only_if == 0) return;
-    __shared__ int64_t As[GBK][GBM + 1];
-    __shared__ int64_t Ws[GBK][GBN + 1];
-    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const int N = (int)W.N;
-    const int ntn = (N + GBN - 1) / GBN, ntiles = ntn * ((M + GBM - 1) / GBM);
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int m0 = (tile / ntn) * GBM, n0 = (tile % ntn) * GBN;
-    u128 acc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0;
-
-    for (int k0 = 0; k0 < K; k0 += GBK) {
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            int idx = tid + 256 * i, r = idx >> 5, c = idx & 31;
-            int gm = m0 + r, gk = k0 + c;
-            As[c][r] = (gm < M && gk < K) ? A[(int64_t)gm * lda + gk] : 0;
-        }
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            int idx = tid + 256 * i, r = idx >> 5, c = idx & 31;
-            int gn = n0 + r, gk = k0 + c;
-            int64_t w = 0;
-            if (gn < N && gk < K)
-                w = composite(dequant_elem(W.dtype, W.data, (int64_t)gn * K + gk, W.nblocks), W.mode, W.scale);
-            Ws[c][r] = w;
-        }
-        __syncthreads();
-#pragma unroll 4
-        for (int kk = 0; kk < GBK; kk++) {
-            int64_t a[4], w[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) a[i] = As[kk][ty + 16 * i];
-#pragma unroll
-            for (int j = 0; j < 4; j++) w[j] = Ws[kk][tx + 16 * j];
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) acc[i][j] += (u128)((i128)a[i] * (i128)w[j]);
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        int m = m0 + ty + 16 * i;
-        if (m >= M) continue;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            int n = n0 + tx + 16 * j;
-            if (n >= N) continue;
-            int64_t v = shift > 0 ? lo64(sar128((i128)acc[i][j], shift)) : lo64((i128)acc[i][j]);
-            if (R) v = wadd(v, R[(int64_t)m * ldr + n]);
-            C[(int64_t)m * ldc + n] = v;
-        }
-    }
-    __syncthreads();  // the next tile reuses As / Ws
-    }
+    __shared__ int64_t As[XBK][XBM + 1];
+    __shared__ int64_t Ws[XBK][XBN + 1];
+    exact_gemm_tiles(A, lda, M, K, W, C, ldc, shift, R, ldr, As, Ws, blockIdx.x, gridDim.x);
 }
 
 __global__ void k_weight_q30(WDesc W, int64_t n, int64_t* out) {
@@ -96,10 +39,10 @@ __global__ void k_weight_q30(WDesc W, int64_t n, int64_t* out) {
 int gemm_exact(const int64_t* a, int64_t lda, int M, int K, const WDesc& w, int64_t* c, int64_t ldc, int shift,
                 const int64_t* r, int64_t ldr, cudaStream_t st, const int* only_if) {
     if (M <= 0 || w.N <= 0) return 0;
-    const int64_t ntiles = ((w.N + GBN - 1) / GBN) * (int64_t)((M + GBM - 1) / GBM);
+    const int64_t ntiles = ((w.N + XBN - 1) / XBN) * (int64_t)((M + XBM - 1) / XBM);
     // Gated behind a faster path it usually does nothing, so a small grid walks the tiles.
     const int64_t grid = only_if ? std::min<int64_t>(ntiles, 2 * 148) : ntiles;
-    k_gemm_exact<<<(unsigned)grid, 256, 0, st>>>(a, lda, M, K, w, c, ldc, shift, r, ldr, only_if);
+    k_gemm_exact<<<(unsigned)grid, XTH, 0, st>>>(a, lda, M, K, w, c, ldc, shift, r, ldr, only_if);
     return 1;
 }
 

@@ -26,6 +26,7 @@
 
 #include "slx_attr.h"
 #include "slx_device.cuh"
+#include "slx_exact.cuh"
 #include "slx_gemm.h"
 #include "slx_kernels.h"
 #include "tc_ptx.cuh"
@@ -49,6 +50,11 @@ struct Params {
     const int8_t* row_shift;
     long long wait_limit;  // SM clock cycles before a wait on the pipeline gives up
     int stall_mma;         // test hook: the MMA warp issues nothing (the pipeline's waits then run out)
+    // the exact CUDA-core product the CTAs compute instead when *skip is set (A null: nothing)
+    const int64_t* A;
+    int64_t lda;
+    int K;
+    WDesc W;
 };
 
 // Bounded spin on an mbarrier phase without suspending (the MMA issuer's waits are short and on the
@@ -62,6 +68,12 @@ __device__ __forceinline__ bool mbar_spin(uint32_t bar, uint32_t parity, long lo
             if (mbar_try(bar, parity)) return true;
         if (clock64() - t0 > limit) return false;
     }
+}
+
+// The exact fallback out of line, so its Int128 accumulators do not weigh on the register
+// allocation of the tensor-core path (the kernel runs one or the other).
+__device__ __noinline__ void exact_fallback(const Params& p, int64_t (*xs)[XBM + 1]) {
+    exact_gemm_tiles(p.A, p.lda, p.M, p.K, p.W, p.C, p.ldc, p.shift, p.R, p.ldr, xs, xs + XBK, blockIdx.x, gridDim.x);
 }
 
 template <int LW>
@@ -83,9 +95,12 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     constexpr int W_ST = LW * GN * GK, A_ST = LA * GM * GK, STAGE = W_ST + A_ST;
     constexpr int nst = gemm_stages<LW>();
     constexpr uint32_t IDESC = idesc_i8(LA * GM);
-    if (p.skip && *p.skip) return;
-
     extern __shared__ uint8_t smem_raw[];
+    if (p.skip && *p.skip) {  // an operand did not fit its digits: the exact product, on CUDA cores
+        if (p.A) exact_fallback(p, (int64_t(*)[XBM + 1])smem_raw);
+        return;
+    }
+
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = (uint64_t*)(smem + (size_t)nst * STAGE);
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + nst);
@@ -559,9 +574,11 @@ void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t 
 
 void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K, int64_t mpad, int64_t npad, int64_t kpad,
             int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st,
-            const int8_t* row_shift, const WaitOptions* wait) {
-    (void)K;
+            const int8_t* row_shift, const WaitOptions* wait, const int64_t* a, int64_t lda, const WDesc* w) {
     Params p = base_params();
+    if (a && w) {
+        p.A = a; p.lda = lda; p.K = K; p.W = *w;
+    }
     p.M = M; p.N = N; p.nkb = (int)(kpad / GK); p.shift = shift;
     p.tiles_n = (int)((npad + GN - 1) / GN);
     // activation tiles up to M only: the digit planes' padding rows (up to the 128-row multiple)

@@ -55,9 +55,12 @@ void split_w(const WDesc& w, int lw, int64_t npad, int64_t kpad, int8_t* planes,
              const int8_t* tz = nullptr);
 void split_a(const int64_t* a, int64_t lda, int M, int K, int64_t mpad, int64_t kpad, int8_t* planes, int* overflow,
              cudaStream_t st);
+// With a and w, a set *skip makes the kernel compute the exact product of a (int64 rows, lda) and
+// w's composites on its CUDA cores instead (no separate fallback launch); without them it does nothing.
 void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K, int64_t mpad, int64_t npad, int64_t kpad,
             int shift, int64_t* c, int64_t ldc, const int64_t* r, int64_t ldr, const int* skip, int* err, cudaStream_t st,
-            const int8_t* row_shift = nullptr, const WaitOptions* wait = nullptr);
+            const int8_t* row_shift = nullptr, const WaitOptions* wait = nullptr, const int64_t* a = nullptr,
+            int64_t lda = 0, const WDesc* w = nullptr);
 // Per-head digit planes of rows at x + (b*T+t)*ld + h*hd -> [(b*nh+h)][LA][tpad][kpad].
 // ApplyRoPE in place on the same head rows (cos / sin tables [T][hd/2], Q30), fused with their split.
 void rope_split_heads(int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad,

@@ -600,7 +600,7 @@ inline void gate_down(slx_model* m, const int64_t* gate, int64_t* up, int F, int
     const double macs = (double)M * (double)w.N * (double)w.K;
     const double tc = (double)M * (double)w.N * (double)p.k_pad * tc::LA * p.wlimbs;
     run_k(ctx, KC_GEMM, macs, 0, st, [&] {
-        if (gemm_run_planes(planes, flag, up, F, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st)) return 2;
+        if (gemm_run_planes(planes, flag, up, F, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st)) return 1;
         return gemm_run(up, F, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st);
     }, tc);
 }
@@ -640,7 +640,7 @@ inline void project_from(slx_model* m, const int8_t* planes, const int* flag, co
     const double tc = tcp ? (double)M * (double)w.N * (double)p.k_pad * tc::LA * p.wlimbs : 0.0;
     run_k(m->ctx, KC_GEMM, macs, 0, st, [&] {
         if (gemm_run_planes(planes, flag, a, lda, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st))
-            return 2;
+            return 1;
         return gemm_run(a, lda, M, w, p, c, ldc, m->scale_bits, r, ldr, m->gws, st);
     }, tc);
 }
