@@ -181,10 +181,10 @@ slx_status slx_matmul_q30_prepared(slx_weight* w, const int64_t* d_a, int M, int
  * Limit: 256 + 5*ceil(M/128)*128*ceil(K/128)*128 + 4*ceil(N/64)*64*ceil(K/128)*128 bytes must fit
  * the scratch and K < 32768, else SLX_ESCRATCH. The first call on a device looks up the scratch
  * address there (cudaGetSymbolAddress) and keeps it for the life of the process, so the entry point
- * must not be used on a device after a cudaDeviceReset (or primary-context reset) there; make that
- * first call before any stream capture. The call waits for its work on `stream` to finish before it
- * returns (it reads the call's error word back). All calls share the scratch: calls whose GPU
- * work overlaps (other streams or threads on the same device) race and must be serialised. */
+ * must not be used on a device after a cudaDeviceReset (or primary-context reset) there. The call is
+ * synchronous: it reads the call's error word back and waits for its work on `stream` to finish
+ * before it returns, so it cannot be captured into a CUDA graph. All calls share the scratch: calls
+ * whose GPU work overlaps (other streams or threads on the same device) race and must be serialised. */
 #define SLX_NOALLOC_SCRATCH_BYTES (32u << 20)
 slx_status slx_matmul_q30_noalloc(const int64_t* d_a, int M, int K, int dtype, const uint8_t* d_w, int64_t w_bytes,
                                   int N, int half_composite, int scale_bits, int shift, int64_t* d_c, void* stream);
