@@ -770,9 +770,9 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
         return -1;
     // the flag and the split units' counters (P.V's, then the score kernel's)
     cudaMemsetAsync(flag, 0, 256 + 4 * (size_t)PV_MAX_SPLIT + 4 * (size_t)spl.rem, st);
-    if (rope_cs) {  // ApplyRoPE on q and k in place, fused with their digit split
-        rope_split_heads(const_cast<int64_t*>(q), ldq, B, T, nh, hd, l.tq, l.kpad, rope_cs, rope_sn, qp, flag, st);
-        rope_split_heads(const_cast<int64_t*>(k), ldk, B, T, nkv, hd, l.tk, l.kpad, rope_cs, rope_sn, kp, flag, st);
+    if (rope_cs) {  // ApplyRoPE on q and k, fused with their digit split (the planes get the rotated values)
+        rope_split_heads(const_cast<int64_t*>(q), ldq, B, T, nh, hd, l.tq, l.kpad, rope_cs, rope_sn, qp, flag, st, false);
+        rope_split_heads(const_cast<int64_t*>(k), ldk, B, T, nkv, hd, l.tk, l.kpad, rope_cs, rope_sn, kp, flag, st, false);
     } else {
         split_heads(q, ldq, B, T, nh, hd, l.tq, l.kpad, qp, flag, st);
         split_heads(k, ldk, B, T, nkv, hd, l.tk, l.kpad, kp, flag, st);
@@ -805,9 +805,15 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
         case 128: launch_pv<128>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, pl, flag, cnt, part, st); break;
         default: launch_pv<256>(B, T, nh, nkv, scores, sr, v, ldv, out, ldo, pl, flag, cnt, part, st); break;
     }
-    // the exact kernel redoes the whole call when anything fell outside the fast ranges
+    // the exact kernel redoes the whole call when anything fell outside the fast ranges, on q and k
+    // rotated in place first (the fast path rotated only their digit planes)
+    int n = 6;
+    if (rope_cs) {
+        n += rope_rows(const_cast<int64_t*>(q), ldq, B, T, nh, hd, rope_cs, rope_sn, st, flag);
+        n += rope_rows(const_cast<int64_t*>(k), ldk, B, T, nkv, hd, rope_cs, rope_sn, st, flag);
+    }
     attention(q, ldq, k, ldk, v, ldv, out, ldo, B, T, nh, nkv, hd, score_shift, sqrt_hd, mode, window, st, flag);
-    return 6;
+    return n;
 }
 
 }  // namespace slx

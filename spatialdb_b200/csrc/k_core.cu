@@ -666,10 +666,12 @@ int rms_pair_rows(int64_t* y, const int64_t* r, int64_t* z, int rows, int n, con
 // RoPE (IntegerAttention.ApplyRoPE, IntegerAttention.cs:35-58)
 // ------------------------------------------------------------------------------------------
 namespace {
+// With only_if, nothing is done unless *only_if is nonzero (the rotation is then needed by the exact
+// attention kernel, the tensor-core path having rotated only its digit planes).
 __global__ void k_rope(int64_t* __restrict__ X, int64_t ld, int T, int nh, int hd, const int64_t* __restrict__ cs,
-                       const int64_t* __restrict__ sn, int64_t total) {
-    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= total) return;
+                       const int64_t* __restrict__ sn, int64_t total, const int* __restrict__ only_if) {
+    if (only_if && *only_if == 0) return;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     int half = hd / 2;
     int p = (int)(i % half);
     int64_t mh = i / half;
@@ -681,14 +683,17 @@ __global__ void k_rope(int64_t* __restrict__ X, int64_t ld, int T, int nh, int h
     int64_t x0 = hb[p], x1 = hb[p + half];
     hb[p] = lo64(sar128((i128)((u128)((i128)x0 * c) - (u128)((i128)x1 * s)), 30));
     hb[p + half] = lo64(sar128((i128)((u128)((i128)x0 * s) + (u128)((i128)x1 * c)), 30));
+    }
 }
 }  // namespace
 
 int rope_rows(int64_t* x, int64_t ld, int B, int T, int nh, int hd, const int64_t* cos, const int64_t* sin,
-               cudaStream_t st) {
+               cudaStream_t st, const int* only_if) {
     int64_t total = (int64_t)B * T * nh * (hd / 2);
     if (total <= 0) return 0;
-    k_rope<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(x, ld, T, nh, hd, cos, sin, total);
+    // gated: it usually does nothing, so a small grid strides over the pairs
+    const int64_t grid = only_if ? std::min<int64_t>((total + 255) / 256, 148 * 2) : (total + 255) / 256;
+    k_rope<<<(unsigned)grid, 256, 0, st>>>(x, ld, T, nh, hd, cos, sin, total, only_if);
     return 1;
 }
 

@@ -364,6 +364,9 @@ __global__ void k_split_heads(const int64_t* __restrict__ X, int64_t ld, int T, 
 // (t < tpad, k < kpad, zero padded). A thread owns four pairs of a head row (positions 4q..4q+3 and
 // their partners half + 4q..): it rewrites them, writes both digit quads, and zeroes its share of
 // the row's padding columns hd..kpad. Rows t >= T get zero digits. hd is a power of two >= 16.
+// Without WB the rotated values go to the digit planes only (the int64 rows keep their unrotated
+// values; the exact attention, when it runs, rotates them itself first).
+template <bool WB>
 __global__ void k_rope_split_heads(int64_t* __restrict__ X, int64_t ld, int T, int nh, int hd, int tpad, int kpad,
                                    const int64_t* __restrict__ cs, const int64_t* __restrict__ sn,
                                    int8_t* __restrict__ planes, int* overflow, int64_t total) {
@@ -392,10 +395,12 @@ __global__ void k_rope_split_heads(int64_t* __restrict__ X, int64_t ld, int T, i
             ya[j] = lo64(sar128((i128)((u128)((i128)xa[j] * c) - (u128)((i128)xb[j] * s)), 30));
             yb[j] = lo64(sar128((i128)((u128)((i128)xa[j] * s) + (u128)((i128)xb[j] * c)), 30));
         }
-        *(longlong2*)(row + p0) = make_longlong2(ya[0], ya[1]);
-        *(longlong2*)(row + p0 + 2) = make_longlong2(ya[2], ya[3]);
-        *(longlong2*)(row + half + p0) = make_longlong2(yb[0], yb[1]);
-        *(longlong2*)(row + half + p0 + 2) = make_longlong2(yb[2], yb[3]);
+        if (WB) {
+            *(longlong2*)(row + p0) = make_longlong2(ya[0], ya[1]);
+            *(longlong2*)(row + p0 + 2) = make_longlong2(ya[2], ya[3]);
+            *(longlong2*)(row + half + p0) = make_longlong2(yb[0], yb[1]);
+            *(longlong2*)(row + half + p0 + 2) = make_longlong2(yb[2], yb[3]);
+        }
     }
     uint32_t wa[LA], wb[LA];
     digit_words4(ya[0], ya[1], ya[2], ya[3], wa, bad);
@@ -597,11 +602,15 @@ void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K,
 }
 
 void rope_split_heads(int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad,
-                      const int64_t* cs, const int64_t* sn, int8_t* planes, int* overflow, cudaStream_t st) {
+                      const int64_t* cs, const int64_t* sn, int8_t* planes, int* overflow, cudaStream_t st,
+                      bool write_back) {
     const int64_t total = (int64_t)B * nh * tpad * (hd / 8);
     if (total <= 0) return;
-    k_rope_split_heads<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(x, ld, T, nh, hd, (int)tpad, (int)kpad, cs, sn,
-                                                                       planes, overflow, total);
+    const unsigned grid = (unsigned)((total + 255) / 256);
+    if (write_back)
+        k_rope_split_heads<true><<<grid, 256, 0, st>>>(x, ld, T, nh, hd, (int)tpad, (int)kpad, cs, sn, planes, overflow, total);
+    else
+        k_rope_split_heads<false><<<grid, 256, 0, st>>>(x, ld, T, nh, hd, (int)tpad, (int)kpad, cs, sn, planes, overflow, total);
 }
 
 void split_heads(const int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad, int8_t* planes,

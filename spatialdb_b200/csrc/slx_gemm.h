@@ -64,7 +64,8 @@ void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K,
 // Per-head digit planes of rows at x + (b*T+t)*ld + h*hd -> [(b*nh+h)][LA][tpad][kpad].
 // ApplyRoPE in place on the same head rows (cos / sin tables [T][hd/2], Q30), fused with their split.
 void rope_split_heads(int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad,
-                      const int64_t* cs, const int64_t* sn, int8_t* planes, int* overflow, cudaStream_t st);
+                      const int64_t* cs, const int64_t* sn, int8_t* planes, int* overflow, cudaStream_t st,
+                      bool write_back = true);
 void split_heads(const int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad, int8_t* planes,
                  int* overflow, cudaStream_t st);
 }  // namespace tc

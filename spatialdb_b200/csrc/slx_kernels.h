@@ -61,7 +61,7 @@ int rms_pair_rows(int64_t* y, const int64_t* r, int64_t* z, int rows, int n, con
 
 // ApplyRoPE on rows m of B*T (position m % T), nh heads of hd at x + m*ld + h*hd.
 int rope_rows(int64_t* x, int64_t ld, int B, int T, int nh, int hd, const int64_t* cos, const int64_t* sin,
-               cudaStream_t st);
+              cudaStream_t st, const int* only_if = nullptr);
 
 // Attention for B sequences of T: q (ldq, nh heads of hd), k/v (ldk/ldv, nkv heads), out (ldo).
 // mode 0 non-causal, 1 causal with the -2^(frac-1) mask, 2 sliding window.
@@ -73,7 +73,9 @@ int attention(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, cons
 
 
 // Same attention with tensor-core scores (k_attn.cu): digit split of q/k (with rope_cs / rope_sn
-// given, ApplyRoPE is applied to q and k in place by the same pass), tcgen05 score GEMM,
+// given, ApplyRoPE is applied by the same pass to the values it splits; q and k themselves are
+// rotated in place only when the exact kernel has to run, so afterwards they hold unspecified
+// rotated or unrotated values), tcgen05 score GEMM,
 // CUDA-core softmax and per-term PV, and the exact kernel gated behind them for out-of-range
 // inputs. ws must hold attention_tc_workspace() bytes. Returns the kernels queued, -1 if the
 // tensor maps could not be encoded (nothing queued). With planes (and kpad == nh * hd, mpad >= B * T)

@@ -223,13 +223,15 @@ class EncoderShape:
 
 
 def write_encoder(path: str, shape: EncoderShape, wtype: int = Q8_0, seed: int = 0, arch: str = "nomic-bert",
-                  rope_base: float = 10000.0, unk: int | None = None, ffn_norm_scale: float = 1.0) -> str:
+                  rope_base: float = 10000.0, unk: int | None = None, ffn_norm_scale: float = 1.0,
+                  embd_norm_scale: float = 1.0) -> str:
     """nomic-bert style encoder with N(0, 0.02) weights quantized to `wtype` (norms and token types F32).
 
     Tensor names and shapes are those IntegerTransformerSource.LoadFromReader reads
     (Gguf/IntegerTransformerSource.Loading.cs:72-151); GGUF ne0 is the inner (K) dimension.
     ffn_norm_scale multiplies the weight of the norm in front of the FFN (attn_output_norm): large
-    values make the FFN's activations exceed the tensor-core digit range.
+    values make the FFN's activations exceed the tensor-core digit range. embd_norm_scale does the
+    same for the embeddings' norm, so the first block's projections and attention inputs exceed it.
     """
     rng = np.random.default_rng(seed)
     d, F, V = shape.embd, shape.ff, shape.vocab
@@ -252,7 +254,7 @@ def write_encoder(path: str, shape: EncoderShape, wtype: int = Q8_0, seed: int =
 
     w.tensor("token_embd.weight", (d, V), wtype, normal(d * V))
     w.tensor("token_types.weight", (d, 2), F32, normal(2 * d))
-    w.tensor("token_embd_norm.weight", (d,), F32, 1 + normal(d))
+    w.tensor("token_embd_norm.weight", (d,), F32, (1 + normal(d)) * np.float32(embd_norm_scale))
     w.tensor("token_embd_norm.bias", (d,), F32, normal(d))
     for i in range(shape.layers):
         p = f"blk.{i}"

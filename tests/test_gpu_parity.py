@@ -34,7 +34,10 @@ def models(tmp_path_factory):
     # FFN activations beyond five digits: the gate/up and down projections take their exact kernels
     big = synth.write_encoder(str(d / "big.gguf"), synth.EncoderShape(layers=2, embd=64, heads=4, ff=128, vocab=300, ctx=512),
                               synth.Q8_0, seed=15, ffn_norm_scale=1000.0)
-    return {"enc": enc, "enc4": enc4, "cau": cau, "cau_sw": cau_sw, "big": big}
+    # the first block's q and k beyond five digits: the attention's exact fallback (q and k rotated first)
+    bigq = synth.write_encoder(str(d / "bigq.gguf"), synth.EncoderShape(layers=2, embd=64, heads=4, ff=128, vocab=300,
+                                                                        ctx=512), synth.Q8_0, seed=16, embd_norm_scale=3000.0)
+    return {"enc": enc, "enc4": enc4, "cau": cau, "cau_sw": cau_sw, "big": big, "bigq": bigq}
 
 
 # ------------------------------------------------------------------ dequant
@@ -132,6 +135,18 @@ def test_encoder_ffn_beyond_digit_range(ctx, oracle, models):
     m = slx.IntegerTransformerSource.load(path, ctx=ctx)
     o = oracle.Encoder(path)
     batch = np.random.default_rng(5).integers(0, o.vocab, (2, 24)).astype(np.int32)
+    for nl in range(o.layers + 1):
+        np.testing.assert_array_equal(m.trace_hidden(batch[0], nl), o.hidden(batch[0], nl), err_msg=f"layer {nl}")
+    np.testing.assert_array_equal(m.forward(batch), o.forward(batch))
+
+
+def test_encoder_attention_beyond_digit_range(ctx, oracle, models):
+    """q and k of the first block exceed the five-digit range after RoPE: the attention's exact kernel
+    runs on q and k that are rotated in place first (the fast path rotates only their digit planes)."""
+    path = models["bigq"]
+    m = slx.IntegerTransformerSource.load(path, ctx=ctx)
+    o = oracle.Encoder(path)
+    batch = np.random.default_rng(6).integers(0, o.vocab, (2, 20)).astype(np.int32)
     for nl in range(o.layers + 1):
         np.testing.assert_array_equal(m.trace_hidden(batch[0], nl), o.hidden(batch[0], nl), err_msg=f"layer {nl}")
     np.testing.assert_array_equal(m.forward(batch), o.forward(batch))
