@@ -638,7 +638,6 @@ __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const
                 }
         }
     }
-    bool over = false;
 #pragma unroll
     for (int r = 0; r < 8; r++) {
         const int t = t0 + r0 + r;
@@ -647,20 +646,30 @@ __global__ __launch_bounds__(PV_TH, 2) void k_pv(const int64_t* S, int SR, const
 #pragma unroll
         for (int q = 0; q < 4; q++)
             *(longlong2*)(orow + 2 * cg + 2 * CG * q) = make_longlong2(sum[r][2 * q], sum[r][2 * q + 1]);
-        if (pl.planes) {  // digits of column pairs q and q + 1: the low and high halves of each word
-            int8_t* prow = pl.planes + ((int64_t)b * T + t) * pl.kpad + (int64_t)h * HD + 2 * cg;
+    }
+    if (!pl.planes) return;
+    // The digit planes through shared memory: the block's [PR][HD] tile (64 KB, the chunk buffers'
+    // space, free once every thread is past the key loop), then four consecutive columns a thread, so
+    // a warp writes 128 contiguous bytes of a plane row.
+    int64_t* tile = (int64_t*)sm;
+    __syncthreads();
 #pragma unroll
-            for (int q = 0; q < 4; q += 2) {
-                uint32_t wd[5];
-                digit_words4(sum[r][2 * q], sum[r][2 * q + 1], sum[r][2 * q + 2], sum[r][2 * q + 3], wd, over);
+    for (int r = 0; r < 8; r++)
 #pragma unroll
-                for (int i = 0; i < 5; i++) {
-                    int8_t* d = prow + (int64_t)i * pl.mpad * pl.kpad + 2 * CG * q;
-                    *(uint16_t*)d = (uint16_t)wd[i];
-                    *(uint16_t*)(d + 2 * CG) = (uint16_t)(wd[i] >> 16);
-                }
-            }
-        }
+        for (int q = 0; q < 4; q++)
+            *(longlong2*)(tile + (r0 + r) * HD + 2 * cg + 2 * CG * q) = make_longlong2(sum[r][2 * q], sum[r][2 * q + 1]);
+    __syncthreads();
+    bool over = false;
+    for (int g = threadIdx.x; g < PR * (HD / 4); g += PV_TH) {
+        const int r = g / (HD / 4), c = 4 * (g % (HD / 4));
+        const int t = t0 + r;
+        if (t >= T) continue;
+        const longlong2 x01 = *(const longlong2*)(tile + r * HD + c), x23 = *(const longlong2*)(tile + r * HD + c + 2);
+        uint32_t wd[5];
+        digit_words4(x01.x, x01.y, x23.x, x23.y, wd, over);
+        int8_t* prow = pl.planes + ((int64_t)b * T + t) * pl.kpad + (int64_t)h * HD + c;
+#pragma unroll
+        for (int i = 0; i < 5; i++) *(uint32_t*)(prow + (int64_t)i * pl.mpad * pl.kpad) = wd[i];
     }
     if (over) atomicOr(flag, 4);
 }
@@ -672,6 +681,7 @@ void launch_pv(int B, int T, int nh, int nkv, const int64_t* scores, int sr, con
                int64_t* out, int64_t ldo, const PvPlan& pl, int* flag, int* cnt, int64_t* part, cudaStream_t st) {
     using C = Pv<HD>;
     static_assert(C::SMEM <= 112 * 1024, "two P.V blocks per SM");
+    static_assert(C::SMEM >= (size_t)C::PR * HD * sizeof(int64_t), "the output tile fits the chunk buffers");
     static_assert(C::VT == pv_keys_per_chunk(HD) && C::PR * HD == 8192, "plan and kernel agree");
     if (((uintptr_t)v & 15) != 0 || (ldv & 1) != 0 || ((uintptr_t)out & 15) != 0 || (ldo & 1) != 0) {
         // rows the 16-byte copies and stores cannot address: the exact kernel
