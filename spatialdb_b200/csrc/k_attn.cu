@@ -337,13 +337,20 @@ SLX_DEV uint32_t exp_nonpos30(int64_t x, bool& bad) {
     return exp_taylor30_fp((uint32_t)rd_i32(r + RD_BASE), r) >> -k;
 }
 
-// floor(e * 2^30 / sum) for e <= 2^30 and sum in [1, 2^41): an fp64 estimate (within one) corrected
-// by the exact remainder.
+// floor(e * 2^30 / sum) for e <= 2^30 and sum in [2^30, 2^41) (the softmax's sum includes the
+// maximum's own e = 2^30): the fp64 product e * inv30, inv30 = 2^30 / sum rounded to nearest, is
+// within 2^-23 of the exact quotient (at most 2^30), so its floor is exact unless the product lies
+// within 2^-22 of an integer; only there the exact 64-bit remainder decides.
 SLX_DEV uint32_t p_div(uint32_t e, uint64_t sum, double inv30) {
-    int64_t q = rd_i32(rd_floor(d_u32(e), inv30));
-    int64_t r = (int64_t)(((uint64_t)e << 30) - (uint64_t)q * sum);
-    if (r < 0) q--;
-    else if (r >= (int64_t)sum) q++;
+    const double ed = d_u32(e);
+    const double y = rd_floor(ed, inv30);  // 1.5 * 2^52 + floor(e * inv30)
+    int64_t q = rd_i32(y);
+    const double frac = __fma_rn(ed, inv30, -(y - RD_BASE));  // e * inv30 - floor(e * inv30)
+    if (frac < 0x1p-22 || frac > 1.0 - 0x1p-22) {
+        const int64_t r = (int64_t)(((uint64_t)e << 30) - (uint64_t)q * sum);
+        if (r < 0) q--;
+        else if (r >= (int64_t)sum) q++;
+    }
     return (uint32_t)q;
 }
 
