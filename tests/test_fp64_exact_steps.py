@@ -94,13 +94,17 @@ def exp_nonpos30(x: int) -> int:
 
 
 def p_div(e: int, total: int) -> int:
+    """k_attn.cu p_div: the floor of the fp64 product, checked by the exact remainder only when the
+    product lies within 2^-22 of an integer."""
     inv30 = 1073741824.0 / float(total)
     q = rd_floor(float(e), inv30)
-    rem = (e << 30) - q * total
-    if rem < 0:
-        q -= 1
-    elif rem >= total:
-        q += 1
+    frac = float(Fraction(e) * Fraction(inv30) - q)  # fma_rn(e, inv30, -q)
+    if frac < 2.0 ** -22 or frac > 1.0 - 2.0 ** -22:
+        rem = (e << 30) - q * total
+        if rem < 0:
+            q -= 1
+        elif rem >= total:
+            q += 1
     return q
 
 
@@ -177,6 +181,13 @@ def test_softmax_division(oracle):
     for e, total in [(1 << 30, 1 << 30), (1, 1), (0, 1), ((1 << 30) - 1, (1 << 41) - 1), (1 << 30, (1 << 41) - 1),
                      (12345, 12346), ((1 << 30), (1 << 30) + 1)]:
         assert p_div(e, total) == (e << 30) // total, (e, total)
+    # quotients just above and just below an integer, where the fp64 product alone can round across it
+    for _ in range(20000):
+        total = rng.randrange(1 << 30, 1 << 41)
+        k = rng.randrange(1, 1 << 30)
+        for e in ((k * total) >> 30, ((k * total) >> 30) + 1, max(0, ((k * total) >> 30) - 1)):
+            if e <= min(total, 1 << 30):
+                assert p_div(e, total) == (e << 30) // total, (e, total)
 
 
 def test_norm_division_matches_int128():
