@@ -181,13 +181,21 @@ def test_softmax_division(oracle):
     for e, total in [(1 << 30, 1 << 30), (1, 1), (0, 1), ((1 << 30) - 1, (1 << 41) - 1), (1 << 30, (1 << 41) - 1),
                      (12345, 12346), ((1 << 30), (1 << 30) + 1)]:
         assert p_div(e, total) == (e << 30) // total, (e, total)
-    # quotients just above and just below an integer, where the fp64 product alone can round across it
-    for _ in range(20000):
-        total = rng.randrange(1 << 30, 1 << 41)
-        k = rng.randrange(1, 1 << 30)
-        for e in ((k * total) >> 30, ((k * total) >> 30) + 1, max(0, ((k * total) >> 30) - 1)):
-            if e <= min(total, 1 << 30):
-                assert p_div(e, total) == (e << 30) // total, (e, total)
+    # quotients within 2^-22 of an integer k (total = e 2^30 / k rounded, +-1), where the fp64 product
+    # alone can round across k: every one takes the remainder check, and some need its correction
+    wrong = 0
+    for _ in range(6000):
+        m = rng.randrange(1 << 6, 1 << 11)
+        k = rng.randrange(1, m << 6)
+        e = k * m + rng.randrange(0, k)
+        base = (e << 30) // k
+        for total in (base - 1, base, base + 1):
+            if e > (1 << 30) or total < e or total >= (1 << 41):
+                continue
+            inv30 = 1073741824.0 / float(total)
+            wrong += rd_floor(float(e), inv30) != (e << 30) // total
+            assert p_div(e, total) == (e << 30) // total, (e, total)
+    assert wrong > 0  # the fast product alone is not enough there
 
 
 def test_norm_division_matches_int128():
