@@ -238,8 +238,8 @@ SLX_DEV int ln2_reduce(double yd, double& rem) {
 // FixedExp(-g) for |g| <= 20 * 2^30: the reference's k = floor(y / ln2) (truncation for y >= 0,
 // -ceil(-y / ln2) below), r = y - k ln2, so its 32-bit Taylor branch always runs; k <= 28, so
 // e = sum << k never overflows, and k >= -29. den = 2^30 + e < 2^60 is an exact double (at most 32
-// significant bits). 2^60 / den: the fp64 estimate floor(2^60 rcp(den)) corrected by the exact
-// remainder. FixedSiLU = floor(g sig / 2^30) is one rounded-down FMA (|result| <= 20 * 2^30). The
+// significant bits). 2^60 / den: the fp64 estimate floor(2^60 rcp(den)), corrected by the exact
+// remainder where it lies near an integer. FixedSiLU = floor(g sig / 2^30) is one rounded-down FMA (|result| <= 20 * 2^30). The
 // gated product takes the same FMA when |s|, |u| < 2^51 and |s u| < 2^80, else Int128.
 SLX_DEV int64_t silu_gate30(int64_t g, int64_t u) {
     constexpr int64_t one = 1LL << 30, thr = 20LL << 30;
@@ -252,10 +252,17 @@ SLX_DEV int64_t silu_gate30(int64_t g, int64_t u) {
         const uint32_t sum = exp_taylor30_fp((uint32_t)rd_i32(rem + RD_BASE), rem);
         const int64_t den = one + (k >= 0 ? (int64_t)sum << k : (int64_t)(sum >> -k));
         const double den_d = k >= 0 ? __fma_rn(d_u32(sum), pow2d(k), 1073741824.0) : d_i64(den);
-        int64_t q = rd_i32(rd_floor(1152921504606846976.0, __drcp_rn(den_d)));
-        int64_t r = (int64_t)((1ULL << 60) - (uint64_t)q * (uint64_t)den);
-        while (r < 0) { q--; r += den; }
-        while (r >= den) { q++; r -= den; }
+        // 2^60 * rcp(den) is within 2^-23 of 2^60 / den (at most 2^30): its floor is exact unless it
+        // lies within 2^-22 of an integer, where the exact remainder decides
+        const double rcp = __drcp_rn(den_d);
+        const double y = rd_floor(1152921504606846976.0, rcp);
+        int64_t q = rd_i32(y);
+        const double frac = __fma_rn(1152921504606846976.0, rcp, -(y - RD_BASE));
+        if (frac < 0x1p-22 || frac > 1.0 - 0x1p-22) {
+            int64_t r = (int64_t)((1ULL << 60) - (uint64_t)q * (uint64_t)den);
+            while (r < 0) { q--; r += den; }
+            while (r >= den) { q++; r -= den; }
+        }
         s = rd_i64(rd_floor(d_i64(g), d_u32((uint32_t)q) * 0x1p-30));
     }
     const int64_t lim = 1LL << 51;

@@ -138,12 +138,15 @@ def silu_gate30(g: int, u: int) -> int:
         den = one + e
         den_d = fma_rn_exact(float(total), 2.0 ** k, 1073741824.0) if k >= 0 else float(den)
         assert Fraction(den_d) == den
-        q = rd_floor(2.0 ** 60, 1.0 / den_d)
-        rem = (1 << 60) - q * den
-        while rem < 0:
-            q -= 1; rem += den
-        while rem >= den:
-            q += 1; rem -= den
+        rcp = 1.0 / den_d
+        q = rd_floor(2.0 ** 60, rcp)
+        frac = float(Fraction(2 ** 60) * Fraction(rcp) - q)  # fma_rn(2^60, rcp, -q)
+        if frac < 2.0 ** -22 or frac > 1.0 - 2.0 ** -22:
+            rem = (1 << 60) - q * den
+            while rem < 0:
+                q -= 1; rem += den
+            while rem >= den:
+                q += 1; rem -= den
         s = rd_floor(float(g), float(q) * 2.0 ** -30)
     lim = 1 << 51
     if -lim < s < lim and -lim < u < lim and abs(float(s) * float(u)) < 2.0 ** 80:
