@@ -788,8 +788,8 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     // the flag and the split units' counters (P.V's, then the score kernel's)
     cudaMemsetAsync(flag, 0, 256 + 4 * (size_t)PV_MAX_SPLIT + 4 * (size_t)spl.rem, st);
     if (rope_cs) {  // ApplyRoPE on q and k, fused with their digit split (the planes get the rotated values)
-        rope_split_heads(const_cast<int64_t*>(q), ldq, B, T, nh, hd, l.tq, l.kpad, rope_cs, rope_sn, qp, flag, st, false);
-        rope_split_heads(const_cast<int64_t*>(k), ldk, B, T, nkv, hd, l.tk, l.kpad, rope_cs, rope_sn, kp, flag, st, false);
+        rope_split_heads(const_cast<int64_t*>(q), ldq, nh, l.tq, qp, const_cast<int64_t*>(k), ldk, nkv, l.tk, kp, B, T, hd,
+                         l.kpad, rope_cs, rope_sn, flag, st, false);
     } else {
         split_heads(q, ldq, B, T, nh, hd, l.tq, l.kpad, qp, flag, st);
         split_heads(k, ldk, B, T, nkv, hd, l.tk, l.kpad, kp, flag, st);
@@ -824,7 +824,7 @@ int attention_tc(const int64_t* q, int64_t ldq, const int64_t* k, int64_t ldk, c
     }
     // the exact kernel redoes the whole call when anything fell outside the fast ranges, on q and k
     // rotated in place first (the fast path rotated only their digit planes)
-    int n = 6;
+    int n = rope_cs ? 5 : 6;  // the q and k digit splits (one launch with RoPE), scores, softmax, P.V, exact
     if (rope_cs) {
         n += rope_rows(const_cast<int64_t*>(q), ldq, B, T, nh, hd, rope_cs, rope_sn, st, flag);
         n += rope_rows(const_cast<int64_t*>(k), ldk, B, T, nkv, hd, rope_cs, rope_sn, st, flag);

@@ -366,12 +366,26 @@ __global__ void k_split_heads(const int64_t* __restrict__ X, int64_t ld, int T, 
 // the row's padding columns hd..kpad. Rows t >= T get zero digits. hd is a power of two >= 16.
 // Without WB the rotated values go to the digit planes only (the int64 rows keep their unrotated
 // values; the exact attention, when it runs, rotates them itself first).
+// One launch serves q and k: threads [0, a.total) take the head rows of a, the rest those of b.
+struct RopeHeads {
+    int64_t* X;
+    int64_t ld;
+    int nh, tpad;
+    int8_t* planes;
+    int64_t total;  // threads: B * nh * tpad * hd / 8
+};
 template <bool WB>
-__global__ void k_rope_split_heads(int64_t* __restrict__ X, int64_t ld, int T, int nh, int hd, int tpad, int kpad,
-                                   const int64_t* __restrict__ cs, const int64_t* __restrict__ sn,
-                                   int8_t* __restrict__ planes, int* overflow, int64_t total) {
-    const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (idx >= total) return;
+__global__ void __launch_bounds__(256, 6) k_rope_split_heads(RopeHeads ja, RopeHeads jb, int T, int hd, int kpad,
+                                                             const int64_t* __restrict__ cs,
+                                                             const int64_t* __restrict__ sn, int* overflow) {
+    int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const bool second = idx >= ja.total;
+    if (second) idx -= ja.total;
+    if (idx >= (second ? jb.total : ja.total)) return;
+    int64_t* const X = second ? jb.X : ja.X;
+    const int64_t ld = second ? jb.ld : ja.ld;
+    const int nh = second ? jb.nh : ja.nh, tpad = second ? jb.tpad : ja.tpad;
+    int8_t* const planes = second ? jb.planes : ja.planes;
     const int half = hd / 2, qpr = half / 4;  // threads per head row
     const int q = (int)(idx % qpr);
     const int64_t r = idx / qpr;  // over (b*nh + h) * tpad + t
@@ -601,16 +615,18 @@ void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K,
     }
 }
 
-void rope_split_heads(int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad,
-                      const int64_t* cs, const int64_t* sn, int8_t* planes, int* overflow, cudaStream_t st,
-                      bool write_back) {
-    const int64_t total = (int64_t)B * nh * tpad * (hd / 8);
+void rope_split_heads(int64_t* q, int64_t ldq, int nh, int64_t tq, int8_t* qplanes, int64_t* k, int64_t ldk, int nkv,
+                      int64_t tk, int8_t* kplanes, int B, int T, int hd, int64_t kpad, const int64_t* cs,
+                      const int64_t* sn, int* overflow, cudaStream_t st, bool write_back) {
+    const RopeHeads ja{q, ldq, nh, (int)tq, qplanes, (int64_t)B * nh * tq * (hd / 8)};
+    const RopeHeads jb{k, ldk, nkv, (int)tk, kplanes, (int64_t)B * nkv * tk * (hd / 8)};
+    const int64_t total = ja.total + jb.total;
     if (total <= 0) return;
     const unsigned grid = (unsigned)((total + 255) / 256);
     if (write_back)
-        k_rope_split_heads<true><<<grid, 256, 0, st>>>(x, ld, T, nh, hd, (int)tpad, (int)kpad, cs, sn, planes, overflow, total);
+        k_rope_split_heads<true><<<grid, 256, 0, st>>>(ja, jb, T, hd, (int)kpad, cs, sn, overflow);
     else
-        k_rope_split_heads<false><<<grid, 256, 0, st>>>(x, ld, T, nh, hd, (int)tpad, (int)kpad, cs, sn, planes, overflow, total);
+        k_rope_split_heads<false><<<grid, 256, 0, st>>>(ja, jb, T, hd, (int)kpad, cs, sn, overflow);
 }
 
 void split_heads(const int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad, int8_t* planes,

@@ -165,10 +165,13 @@ SLX_DEV double d_i64(int64_t x) { return __longlong_as_double(RD_BASE_BITS + x) 
 SLX_DEV double pow2d(int k) { return __hiloint2double((1023 + k) << 20, 0); }                  // |k| < 1023
 
 // trunc(a w / d) for d >= 1 (the reference's Int128 division, truncating toward zero) with wd = w as
-// a double and rd ~ 1 / d. When |a|, |w| < 2^51, d < 2^60 and the quotient is below 2^49 in magnitude,
-// floor(|a w| rd) from one product and one rounded-down FMA is within one of floor(|a w| / d) (and
-// almost always equal), and the remainder |a w| - q d, exact in wrapping 64-bit arithmetic because
-// |r| < 2 d, fixes it; anything else takes the Int128 division.
+// a double and rd = 1 / (double)d rounded to nearest. When |a|, |w| < 2^51, d < 2^60 and the quotient
+// is below 2^49 in magnitude, P rd, with P = |a w| rounded to a double, is within Q 2^-51 of the exact
+// quotient Q = |a w| / d (three roundings of relative size 2^-53 at most: the product, d as a double
+// and its reciprocal). One rounded-down FMA gives q = floor(P rd); a second FMA gives P rd - q. Where
+// that fraction lies at least (q + 1) 2^-50 away from both integers, no integer lies between P rd and
+// Q, so q = floor(Q); only nearer to an integer does the remainder |a w| - q d, exact in wrapping
+// 64-bit arithmetic because |r| < 2 d, decide. Anything else takes the Int128 division.
 // The Int128 division (rare: outside the fast path's ranges), kept out of line so the callers' code
 // stays small.
 static __device__ __noinline__ int64_t muldiv_trunc_slow(int64_t a, int64_t w, int64_t d) { return lo64(((i128)a * w) / (i128)d); }
@@ -176,13 +179,20 @@ static __device__ __noinline__ int64_t muldiv_trunc_slow(int64_t a, int64_t w, i
 SLX_DEV int64_t muldiv_trunc(int64_t a, int64_t w, double wd, int64_t d, double rd) {
     constexpr int64_t lim = 1LL << 51;
     if (a > -lim && a < lim && w > -lim && w < lim && d < (1LL << 60)) {
-        int64_t q = rd_i64(rd_floor(fabs(d_i64(a) * wd), rd));
+        const double P = fabs(d_i64(a) * wd);
+        const double y = rd_floor(P, rd);  // 1.5 * 2^52 + floor(P rd)
+        int64_t q = rd_i64(y);
         if (q < (1LL << 49)) {
-            const uint64_t ua = a < 0 ? (uint64_t)0 - (uint64_t)a : (uint64_t)a;
-            const uint64_t uw = w < 0 ? (uint64_t)0 - (uint64_t)w : (uint64_t)w;
-            int64_t r = (int64_t)(ua * uw - (uint64_t)q * (uint64_t)d);
-            while (r < 0) { q--; r += d; }
-            while (r >= d) { q++; r -= d; }
+            const double fl = y - RD_BASE;
+            const double frac = __fma_rn(P, rd, -fl);  // P rd - q
+            const double tol = (fl + 1.0) * 0x1p-50;
+            if (frac < tol || frac > 1.0 - tol) {
+                const uint64_t ua = a < 0 ? (uint64_t)0 - (uint64_t)a : (uint64_t)a;
+                const uint64_t uw = w < 0 ? (uint64_t)0 - (uint64_t)w : (uint64_t)w;
+                int64_t r = (int64_t)(ua * uw - (uint64_t)q * (uint64_t)d);
+                while (r < 0) { q--; r += d; }
+                while (r >= d) { q++; r -= d; }
+            }
             return (a < 0) != (w < 0) ? -q : q;
         }
     }

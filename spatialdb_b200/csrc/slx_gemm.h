@@ -62,10 +62,11 @@ void launch(const void* tmap_a, const void* tmap_w, int lw, int M, int N, int K,
             const int8_t* row_shift = nullptr, const WaitOptions* wait = nullptr, const int64_t* a = nullptr,
             int64_t lda = 0, const WDesc* w = nullptr);
 // Per-head digit planes of rows at x + (b*T+t)*ld + h*hd -> [(b*nh+h)][LA][tpad][kpad].
-// ApplyRoPE in place on the same head rows (cos / sin tables [T][hd/2], Q30), fused with their split.
-void rope_split_heads(int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad,
-                      const int64_t* cs, const int64_t* sn, int8_t* planes, int* overflow, cudaStream_t st,
-                      bool write_back = true);
+// ApplyRoPE in place on the same head rows (cos / sin tables [T][hd/2], Q30), fused with their split;
+// one launch for q (nh heads, tq padded rows) and k (nkv heads, tk padded rows).
+void rope_split_heads(int64_t* q, int64_t ldq, int nh, int64_t tq, int8_t* qplanes, int64_t* k, int64_t ldk, int nkv,
+                      int64_t tk, int8_t* kplanes, int B, int T, int hd, int64_t kpad, const int64_t* cs,
+                      const int64_t* sn, int* overflow, cudaStream_t st, bool write_back = true);
 void split_heads(const int64_t* x, int64_t ld, int B, int T, int nh, int hd, int64_t tpad, int64_t kpad, int8_t* planes,
                  int* overflow, cudaStream_t st);
 }  // namespace tc

@@ -109,17 +109,23 @@ def p_div(e: int, total: int) -> int:
 
 
 def muldiv_trunc(a: int, w: int, d: int) -> int:
+    """slx_device.cuh muldiv_trunc: the floor of the fp64 quotient, checked by the exact remainder
+    only when the quotient lies within (q + 1) 2^-50 of an integer."""
     lim = 1 << 51
     if -lim < a < lim and -lim < w < lim and d < (1 << 60):
         rd = 1.0 / float(d)
-        q = rd_floor(abs(float(a) * float(w)), rd) if abs(float(a) * float(w)) * rd < 2.0 ** 50 else None
+        P = abs(float(a) * float(w))
+        q = rd_floor(P, rd) if P * rd < 2.0 ** 50 else None
         if q is not None and q < (1 << 49):
-            rem = abs(a) * abs(w) - q * d  # the kernel's wrapping 64-bit value, exact since |rem| < 2 d
-            assert abs(rem) < 2 * d
-            while rem < 0:
-                q -= 1; rem += d
-            while rem >= d:
-                q += 1; rem -= d
+            frac = float(Fraction(P) * Fraction(rd) - q)  # fma_rn(P, rd, -q)
+            tol = (q + 1) * 2.0 ** -50
+            if frac < tol or frac > 1.0 - tol:
+                rem = abs(a) * abs(w) - q * d  # the kernel's wrapping 64-bit value, exact since |rem| < 2 d
+                assert abs(rem) < 2 * d
+                while rem < 0:
+                    q -= 1; rem += d
+                while rem >= d:
+                    q += 1; rem -= d
             return -q if (a < 0) != (w < 0) else q
     p = a * w
     return -(abs(p) // d) if p < 0 else p // d
@@ -214,6 +220,30 @@ def test_norm_division_matches_int128():
         p = a * w
         want = -(abs(p) // d) if p < 0 else p // d
         assert muldiv_trunc(a, w, d) == want, (a, w, d)
+
+
+def test_norm_division_near_integers():
+    """Quotients a w / d just around an integer k (d = floor(a w / k) + {-1, 0, 1}), from k = 1 to
+    2^48: every one takes the remainder check, and at the large ones the fp64 quotient alone rounds
+    across k."""
+    rng = random.Random(14)
+    wrong = checked = 0
+    for _ in range(12000):
+        a = rng.randrange(1, 1 << rng.randrange(1, 51))
+        w = rng.randrange(1, 1 << rng.randrange(1, 51))
+        k = rng.randrange(1, 1 << rng.randrange(1, 49))
+        p = a * w
+        for d in (p // k - 1, p // k, p // k + 1):
+            if not 1 <= d < (1 << 60) or p // d >= (1 << 49):
+                continue
+            for sa, sw in ((1, 1), (-1, 1), (1, -1)):
+                pp = sa * a * sw * w
+                want = -(abs(pp) // d) if pp < 0 else pp // d
+                assert muldiv_trunc(sa * a, sw * w, d) == want, (sa * a, sw * w, d)
+            checked += 1
+            wrong += rd_floor(abs(float(a) * float(w)), 1.0 / float(d)) != p // d
+    assert checked > 10000
+    assert wrong > 0  # the fast quotient alone is not enough there
 
 
 def test_silu_gate_matches_fixed_silu(oracle):
